@@ -1,0 +1,118 @@
+"""Pins the CPU oracle against golden vectors written by the reference's own eager functions."""
+
+import torch
+
+import oracle
+
+
+def rel(a, b):
+    return ((a.double() - b.double()).norm() / b.double().norm()).item()
+
+
+def test_chunk_config0_matches_reference(golden):
+    c = golden("chunk_cfg0")
+    o, S = oracle.chunk_gated_delta_rule(c["q"], c["k"], c["v"], c["g"], c["beta"], output_final_state=True)
+    assert (o - c["o"]).abs().max().item() < 1e-6
+    assert rel(S, c["S"]) < 1e-6
+
+
+def test_chunk_ragged_bf16_matches_reference(golden):
+    c = golden("chunk_bf16_ragged")
+    o, S = oracle.chunk_gated_delta_rule(c["q"], c["k"], c["v"], c["g"], c["beta"], initial_state=c["h0"],
+                                         output_final_state=True)
+    assert o.dtype == torch.bfloat16
+    assert (o.float() - c["o"].float()).abs().max().item() <= 2 ** -8 * c["o"].float().abs().max().item()
+    assert rel(S, c["S"]) < 1e-6
+
+
+def test_recurrent_matches_reference(golden):
+    c = golden("recurrent_bf16")
+    o, S = oracle.recurrent_gated_delta_rule(c["q"], c["k"], c["v"], c["g"], c["beta"], initial_state=c["h0"],
+                                             output_final_state=True)
+    assert torch.equal(o, c["o"]) or (o.float() - c["o"].float()).abs().max().item() < 1e-2
+    assert rel(S, c["S"]) < 1e-6
+
+
+def test_chunk_and_recurrent_forms_agree(golden):
+    c = golden("chunk_cfg0")
+    o1, S1 = oracle.chunk_gated_delta_rule(c["q"], c["k"], c["v"], c["g"], c["beta"], output_final_state=True)
+    o2, S2 = oracle.recurrent_gated_delta_rule(c["q"], c["k"], c["v"], c["g"], c["beta"], output_final_state=True)
+    assert (o1 - o2).abs().max().item() < 1e-5
+    assert rel(S1, S2) < 1e-5
+
+
+def test_advance_matches_reference(golden):
+    c = golden("advance")
+    S = oracle.advance_gated_delta_rule(c["k"], c["v"], c["g"], c["beta"], c["h0"], c["steps"])
+    assert rel(S, c["S"]) < 1e-6
+    # steps <= 0 leave the state bit for bit unchanged
+    for b, s in enumerate(c["steps"].tolist()):
+        if s <= 0:
+            assert torch.equal(S[b], c["h0"][b])
+
+
+def test_varlen_equals_per_sequence(golden):
+    c = golden("chunk_bf16_ragged")
+    q = torch.cat([c["q"][0:1], c["q"][1:2, :60]], dim=1)
+    k = torch.cat([c["k"][0:1], c["k"][1:2, :60]], dim=1)
+    v = torch.cat([c["v"][0:1], c["v"][1:2, :60]], dim=1)
+    g = torch.cat([c["g"][0:1], c["g"][1:2, :60]], dim=1)
+    beta = torch.cat([c["beta"][0:1], c["beta"][1:2, :60]], dim=1)
+    cu = torch.tensor([0, 100, 160])
+    o, S = oracle.chunk_gated_delta_rule_varlen(q, k, v, g, beta, cu, initial_state=c["h0"], output_final_state=True)
+    o0, S0 = oracle.chunk_gated_delta_rule(c["q"][0:1], c["k"][0:1], c["v"][0:1], c["g"][0:1], c["beta"][0:1],
+                                           initial_state=c["h0"][0:1], output_final_state=True)
+    assert torch.equal(o[:, :100], o0) and torch.equal(S[0:1], S0)
+
+
+def test_snapshots_are_the_advanced_states(golden):
+    c = golden("recurrent_bf16")
+    o, snaps = oracle.verify_with_snapshots(c["q"], c["k"], c["v"], c["g"], c["beta"], c["h0"])
+    assert snaps.shape == (2, 5, 4, 128, 128)
+    assert rel(snaps[:, -1], c["S"]) < 1e-6
+    ke = c["k"].repeat_interleave(2, dim=2)
+    for j in range(1, 6):
+        S = oracle.advance_gated_delta_rule(ke, c["v"], c["g"], c["beta"], c["h0"], torch.tensor([j, j]))
+        assert rel(snaps[:, j - 1], S) < 1e-6
+
+
+def test_float64_recurrence_close(golden):
+    c = golden("chunk_cfg0")
+    o, S = oracle.exact_recurrence_f64(c["q"], c["k"], c["v"], c["g"], c["beta"])
+    assert (o.float() - c["o"]).abs().max().item() < 1e-5
+    assert rel(S, c["S"]) < 1e-5
+
+
+def test_conv1d_matches_reference(golden):
+    c = golden("conv1d")
+    assert torch.equal(oracle.causal_conv1d(c["x"], c["w"]), c["y"])
+
+
+def test_conv1d_step_matches_reference(golden):
+    c = golden("conv1d_step")
+    st = c["state"].clone()
+    y = oracle.causal_conv1d_step(c["x"], st, c["w"])
+    assert torch.equal(y, c["y"]) and torch.equal(st, c["state_after"])
+
+
+def test_conv_step_matches_reference(golden):
+    c = golden("conv_step")
+    ext, q, k, v = oracle.conv_step(c["state"], c["qkv"], c["w"], c["key_dim"], c["value_dim"], c["head_dim"], c["head_dim"])
+    for a, b in zip((ext, q, k, v), (c["ext"], c["q"], c["k"], c["v"])):
+        assert torch.equal(a, b)
+
+
+def test_gated_norm_matches_reference(golden):
+    c = golden("gated_norm")
+    y = oracle.gated_rms_norm(c["x"], c["z"], c["w"])
+    diff = (y.float() - c["y"].float()).abs()
+    # silu(z) in fp32 may differ from the CPU's vectorised silu in the last fp32 bit,
+    # which can move a bf16 rounding by one ulp.
+    assert (diff > c["y"].float().abs() * 2 ** -7).sum().item() == 0
+    assert (y != c["y"]).float().mean().item() < 0.01
+
+
+def test_delta_gates_match_reference(golden):
+    c = golden("delta_gates")
+    beta, g = oracle.delta_gates(c["b"], c["a"], c["dt_bias"], c["rate"], c["valid"])
+    assert torch.equal(beta, c["beta"]) and torch.equal(g, c["g"])
