@@ -1,0 +1,494 @@
+"""Benchmark of the gated-delta hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload prefill|varlen|decode|verify]
+
+Workloads (synthetic inputs with the benchmark configs' shapes and distributions; no
+dataset or checkpoint is involved):
+
+* ``prefill`` (headline, config 1): one gated-delta layer of the 9B shape, B=1, T=4096,
+  16 key / 32 value heads, bf16 with an fp32 state: causal conv1d (k=4) + SiLU over the
+  8192 qkv channels, chunked gated delta rule with the final state, output-gated RMSNorm.
+  A step is one such layer pass; the metric unit is tokens/s.
+* ``varlen`` (config 2): 32 packed sequences (lengths U{128..2048}, seed 2) with random
+  fp32 initial states and final states.
+* ``decode`` (config 3): 24 stacked layers (no projections between them), 256 sequences
+  with fp32 state [32, 128, 128] and conv state [8192, 3]; a step is one new token
+  through the fused decode layer of all 24 layers.
+* ``verify`` (config 4): 128 sequences score 5 tokens through 24 layers writing the 5
+  per-token fp32 states, then roll back to an accepted length U{1..5}.
+
+Multi-GPU (torchrun, one process per GPU): every rank runs its own shard with no
+collective on the data path (prefill: an independent replica per GPU; decode/verify:
+sequences split across ranks); the step time is the max over ranks.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import platform
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+L2_BYTES = 126 * 2 ** 20
+MiB = 2 ** 20
+D = 128
+H, HV = 16, 32
+C_QKV = 2 * H * D + HV * D  # 8192 conv channels
+METRIC = "gated-delta prefill tok/s & decode tok/s per GPU, 1–8 B200, % of roofline"
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as fh:
+            p = json.load(fh)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def profiled_traffic():
+    """Per-launch DRAM bytes of the dominant kernels from the committed ncu summaries."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(path) as fh:
+            return json.load(fh)
+    except Exception:
+        return {}
+
+
+# ------------------------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ------------------------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.idx = device_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        busy = [s for s in sm if s > 0.5 * max(sm)] or sm
+        return {"sm_mhz": statistics.median(busy), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------------------
+# workloads
+# ------------------------------------------------------------------------------------------
+def make_prefill_inputs(seed=1, T=4096, device="cpu", pin=False):
+    gen = torch.Generator().manual_seed(seed)
+    qkv = torch.randn(1, T, C_QKV, generator=gen).to(torch.bfloat16)
+    w = (torch.randn(C_QKV, 4, generator=gen) * 0.5).to(torch.bfloat16)
+    g = -torch.exp(torch.randn(1, T, HV, generator=gen) * 0.5 - 3.0)
+    beta = torch.sigmoid(torch.randn(1, T, HV, generator=gen)).to(torch.bfloat16)
+    z = torch.randn(1, T, HV, D, generator=gen).to(torch.bfloat16)
+    nw = (torch.rand(D, generator=gen) + 0.5).to(torch.bfloat16)
+    out = dict(qkv=qkv, w=w, g=g, beta=beta, z=z, nw=nw)
+    if pin:
+        out = {k: v.pin_memory() for k, v in out.items()}
+    if device != "cpu":
+        out = {k: v.to(device) for k, v in out.items()}
+    return out
+
+
+def prefill_layer(gdn, x):
+    """conv1d + SiLU -> chunked gated delta rule (final state) -> gated RMSNorm."""
+    T = x["qkv"].shape[1]
+    y = gdn.causal_conv1d(x["qkv"], x["w"])
+    q = y[..., :H * D].view(1, T, H, D)
+    k = y[..., H * D:2 * H * D].view(1, T, H, D)
+    v = y[..., 2 * H * D:].view(1, T, HV, D)
+    o, final = gdn.gated_delta_rule_chunk(q, k, v, x["g"], x["beta"], output_final_state=True)
+    out = gdn.gated_rms_norm(o.view(-1, D), x["z"].view(-1, D), x["nw"])
+    return out, final, (q, k, v)
+
+
+def prefill_core_bytes(T, n_seq=1, with_h0=False):
+    """Algorithmic bytes of the chunk kernel: q, k at H key heads, v, o, g, beta once; states."""
+    per_token = 2 * H * D * 2 + HV * D * 2 + HV * D * 2 + HV * (4 + 2)
+    state = HV * D * D * 4
+    return T * per_token + n_seq * state * (2 if with_h0 else 1)
+
+
+def prefill_flops(T):
+    return T * HV * 180_224
+
+
+def varlen_lengths(seed=2, n=32):
+    gen = torch.Generator().manual_seed(seed)
+    return torch.randint(128, 2049, (n,), generator=gen).tolist()
+
+
+# ------------------------------------------------------------------------------------------
+def timed(fn, steps, warmup, rank_sync, stream=None, inner_events=None):
+    for _ in range(warmup):
+        fn(0)
+    torch.cuda.synchronize()
+    rank_sync()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record()
+    for i in range(steps):
+        fn(i)
+    stop.record()
+    torch.cuda.synchronize()
+    rank_sync()
+    return start.elapsed_time(stop)
+
+
+def run_ours(args, rank, world, device, rank_sync, reduce_max):
+    import jeeves_b200 as gdn
+
+    gdn.load_library()
+    hbm_peak, tc_peak, peak_kind = peaks()
+    traffic = profiled_traffic()
+    result = {}
+
+    # ---------------- prefill (config 1), the headline ----------------
+    T = 4096
+    host = make_prefill_inputs(seed=1, T=T, pin=True)
+    set_bytes = sum(v.numel() * v.element_size() for v in host.values()) + T * HV * D * 2 * 3
+    n_sets = max(2, -(-2 * L2_BYTES // set_bytes))
+    sets = [make_prefill_inputs(seed=1 + i, T=T, device=device) for i in range(n_sets)]
+    kernel_ms = []
+    ev_pairs = []
+
+    def prefill_step(i):
+        x = sets[i % n_sets]
+        y = gdn.causal_conv1d(x["qkv"], x["w"])
+        q = y[..., :H * D].view(1, T, H, D)
+        k = y[..., H * D:2 * H * D].view(1, T, H, D)
+        v = y[..., 2 * H * D:].view(1, T, HV, D)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        o, final = gdn.gated_delta_rule_chunk(q, k, v, x["g"], x["beta"], output_final_state=True)
+        b.record()
+        ev_pairs.append((a, b))
+        gdn.gated_rms_norm(o.view(-1, D), x["z"].view(-1, D), x["nw"])
+
+    with ClockSampler(device.index) as clocks:
+        ms = timed(prefill_step, args.steps, args.warmup, rank_sync)
+    torch.cuda.synchronize()
+    kernel_ms = [a.elapsed_time(b) for a, b in ev_pairs[args.warmup:]]
+    ms = reduce_max(ms)
+    ms_step = ms / args.steps
+    value = world * T * args.steps / (ms / 1e3)
+    k_ms = statistics.mean(kernel_ms)
+    core_bytes = prefill_core_bytes(T)
+    achieved = core_bytes / (k_ms / 1e3) / 1e9
+    launches_per_step = 3
+
+    # e2e: host buffers in, result out, through the public API
+    dev_in = make_prefill_inputs(seed=1, T=T, device=device)
+    out_host = torch.empty(T * HV, D, dtype=torch.bfloat16).pin_memory()
+    state_host = torch.empty(1, HV, D, D, dtype=torch.float32).pin_memory()
+
+    def e2e_step(i):
+        for key in ("qkv", "g", "beta", "z"):
+            dev_in[key].copy_(host[key], non_blocking=True)
+        out, final, _ = prefill_layer(gdn, dev_in)
+        out_host.copy_(out, non_blocking=True)
+        state_host.copy_(final, non_blocking=True)
+
+    e2e_ms = reduce_max(timed(e2e_step, args.steps, args.warmup, rank_sync))
+    h2d = sum(host[k].numel() * host[k].element_size() for k in ("qkv", "g", "beta", "z"))
+    d2h = out_host.numel() * 2 + state_host.numel() * 4
+
+    result.update({
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) qkv/z, g=-exp(N(-3,0.5)), beta=sigmoid(N(0,1)); no dataset)",
+        "config": {"workload": "config 1: 9B-shaped prefill layer, B=1, T=4096, 16/32 heads, d=128, conv1d k=4 + SiLU, "
+                               "chunked gated delta rule (final state), gated RMSNorm",
+                   "tokens_per_gpu_step": T, "parallelism": f"replicas x{world} (no collective)",
+                   "l2": f"inputs rotate over {n_sets} sets of {set_bytes / MiB:.0f} MiB (> L2)"},
+        "e2e": {"value": round(world * T * args.steps / (e2e_ms / 1e3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches_per_step * args.steps,
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                     "frac": round(achieved / hbm_peak, 4), "peak_kind": peak_kind,
+                     "kernel": "gated_delta_rule_chunk", "kernel_ms": round(k_ms, 4),
+                     "algorithmic_bytes": core_bytes,
+                     "traffic": traffic.get("prefill", {}).get("dram_bytes_per_launch"),
+                     "tensor_frac": round(prefill_flops(T) / (k_ms / 1e3) / 1e12 / tc_peak, 4)},
+        "clocks": clocks.summary(),
+    })
+
+    # ---------------- extras: varlen, decode, verify ----------------
+    if args.extras:
+        extra = {}
+        extra["varlen"] = bench_varlen(gdn, args, device, rank_sync, reduce_max, world, hbm_peak)
+        extra["decode"] = bench_decode(gdn, args, device, rank, world, rank_sync, reduce_max, hbm_peak)
+        extra["verify"] = bench_verify(gdn, args, device, rank, world, rank_sync, reduce_max, hbm_peak)
+        result["extra"] = extra
+        result["gpu_launches"] += sum(e.get("gpu_launches", 0) for e in extra.values())
+    return result
+
+
+def bench_varlen(gdn, args, device, rank_sync, reduce_max, world, hbm_peak):
+    lens = varlen_lengths()
+    N = len(lens)
+    Ttot = sum(lens)
+    gen = torch.Generator().manual_seed(2)
+    q = torch.randn(1, Ttot, H, D, generator=gen)
+    q = (q * torch.rsqrt((q * q).sum(-1, keepdim=True) + 1e-6)).to(torch.bfloat16).to(device)
+    k = torch.randn(1, Ttot, H, D, generator=gen)
+    k = (k * torch.rsqrt((k * k).sum(-1, keepdim=True) + 1e-6)).to(torch.bfloat16).to(device)
+    v = torch.randn(1, Ttot, HV, D, generator=gen).to(torch.bfloat16).to(device)
+    g = (-torch.exp(torch.randn(1, Ttot, HV, generator=gen) * 0.5 - 3.0)).to(device)
+    beta = torch.sigmoid(torch.randn(1, Ttot, HV, generator=gen)).to(torch.bfloat16).to(device)
+    h0 = (torch.randn(N, HV, D, D, generator=gen) * 0.02).to(device)
+    cu = torch.tensor([0] + torch.tensor(lens).cumsum(0).tolist(), dtype=torch.int32, device=device)
+
+    def step(i):
+        gdn.gated_delta_rule_chunk(q, k, v, g, beta, initial_state=h0, output_final_state=True, cu_seqlens=cu)
+
+    steps = max(3, args.steps // 2)
+    ms = reduce_max(timed(step, steps, args.warmup, rank_sync)) / steps
+    bytes_ = prefill_core_bytes(Ttot, n_seq=N, with_h0=True)
+    ach = bytes_ / (ms / 1e3) / 1e9
+    return {"workload": "config 2: 32 packed sequences U{128..2048} (seed 2), cu_seqlens, initial+final state",
+            "tokens": Ttot, "value": round(world * Ttot / (ms / 1e3), 1), "unit": "tokens/s", "ms_per_step": round(ms, 4),
+            "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(ach / hbm_peak, 4), "algorithmic_bytes": bytes_},
+            "gpu_launches": steps}
+
+
+def shard(n, rank, world):
+    per = n // world
+    return per, rank * per
+
+
+def bench_decode(gdn, args, device, rank, world, rank_sync, reduce_max, hbm_peak, layers=24, B_total=256, taps=3):
+    B, _ = shard(B_total, rank, world)
+    gen = torch.Generator().manual_seed(3)
+    states = [torch.zeros(B, HV, D, D, device=device) for _ in range(layers)]
+    for s in states:
+        s.normal_(0, 0.02)
+    conv_states = [torch.randn(B, C_QKV, taps, device=device).to(torch.bfloat16) for _ in range(layers)]
+    w = [(torch.randn(C_QKV, 4, generator=gen) * 0.5).to(torch.bfloat16).to(device) for _ in range(layers)]
+    nw = (torch.rand(D, generator=gen) + 0.5).to(torch.bfloat16).to(device)
+    qkv = [torch.randn(B, C_QKV, device=device).to(torch.bfloat16) for _ in range(layers)]
+    g = [(-torch.exp(torch.randn(B, HV, device=device) * 0.5 - 3.0)) for _ in range(layers)]
+    beta = [torch.sigmoid(torch.randn(B, HV, device=device)).to(torch.bfloat16) for _ in range(layers)]
+    z = [torch.randn(B, HV, D, device=device).to(torch.bfloat16) for _ in range(layers)]
+
+    def step(i):
+        for l in range(layers):
+            gdn.decode_layer_step(qkv[l], conv_states[l], w[l], g[l], beta[l], states[l], z[l], nw, H)
+
+    ms = reduce_max(timed(step, args.steps, args.warmup, rank_sync)) / args.steps
+    unit_bytes = 2 * HV * D * D * 4 + 2 * C_QKV * taps * 2 + C_QKV * 2 + HV * 6 + 2 * HV * D * 2
+    total = unit_bytes * B * layers
+    ach = total / (ms / 1e3) / 1e9
+    return {"workload": f"config 3: 24 layers, {B_total} sequences (state [32,128,128] fp32, conv state [8192,3]), "
+                        f"one token per step, fused conv+L2+GDN+gated norm; {B} sequences per GPU",
+            "value": round(world * B / (ms / 1e3), 1), "unit": "tokens/s (sequences x steps)", "ms_per_step": round(ms, 4),
+            "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(ach / hbm_peak, 4), "algorithmic_bytes_per_unit": unit_bytes},
+            "gpu_launches": 2 * layers * args.steps}
+
+
+def bench_verify(gdn, args, device, rank, world, rank_sync, reduce_max, hbm_peak, layers=24, B_total=128, T=5):
+    B, _ = shard(B_total, rank, world)
+    gen = torch.Generator().manual_seed(4)
+    states = [torch.zeros(B, HV, D, D, device=device).normal_(0, 0.02) for _ in range(layers)]
+    snaps = torch.empty(B, T, HV, D, D, device=device)  # reused per layer (rollback runs right after)
+    q = [torch.randn(B, T, H, D, device=device).to(torch.bfloat16) for _ in range(layers)]
+    k = [torch.randn(B, T, H, D, device=device).to(torch.bfloat16) for _ in range(layers)]
+    v = [torch.randn(B, T, HV, D, device=device).to(torch.bfloat16) for _ in range(layers)]
+    g = [(-torch.exp(torch.randn(B, T, HV, device=device) * 0.5 - 3.0)) for _ in range(layers)]
+    beta = [torch.sigmoid(torch.randn(B, T, HV, device=device)).to(torch.bfloat16) for _ in range(layers)]
+    accepted = torch.randint(1, T + 1, (B,), generator=gen).to(device)
+
+    def step(i):
+        for l in range(layers):
+            gdn.gated_delta_rule_verify(q[l], k[l], v[l], g[l], beta[l], states[l], snapshots=snaps)
+            gdn.gated_delta_rule_rollback(states[l], snaps, accepted)
+
+    ms = reduce_max(timed(step, args.steps, args.warmup, rank_sync)) / args.steps
+    unit_bytes = (HV * D * D * 4 * (1 + T) + T * (2 * H * D * 2 + HV * D * 2 + HV * 6 + HV * D * 2)
+                  + 2 * HV * D * D * 4)  # verify read + T snapshots + inputs/outputs, then the rollback copy
+    total = unit_bytes * B * layers
+    ach = total / (ms / 1e3) / 1e9
+    return {"workload": f"config 4: 24 layers, {B_total} sequences x 5 tokens, 5 fp32 snapshots, rollback by snapshot "
+                        f"copy to accepted U{{1..5}}; {B} sequences per GPU",
+            "value": round(world * B * T / (ms / 1e3), 1), "unit": "scored tokens/s", "ms_per_step": round(ms, 4),
+            "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(ach / hbm_peak, 4), "algorithmic_bytes_per_unit": unit_bytes},
+            "gpu_launches": 2 * layers * args.steps}
+
+
+# ------------------------------------------------------------------------------------------
+# CPU baseline: the oracle (a restatement of the reference's eager path) on host cores
+# ------------------------------------------------------------------------------------------
+def cpu_prefill_once(x, T):
+    import oracle
+
+    y = oracle.causal_conv1d(x["qkv"], x["w"])
+    q = y[..., :H * D].reshape(1, T, H, D)
+    k = y[..., H * D:2 * H * D].reshape(1, T, H, D)
+    v = y[..., 2 * H * D:].reshape(1, T, HV, D)
+    o, S = oracle.chunk_gated_delta_rule(q, k, v, x["g"], x["beta"], output_final_state=True)
+    return oracle.gated_rms_norm(o.reshape(-1, D), x["z"].reshape(-1, D), x["nw"])
+
+
+def cpu_baseline(T=4096, reps=2):
+    torch.set_num_threads(os.cpu_count() or 1)
+    x = make_prefill_inputs(seed=1, T=T)
+    cpu_prefill_once(x, T)
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        cpu_prefill_once(x, T)
+    dt = (time.perf_counter() - t0) / reps
+    return {"value": round(T / dt, 1), "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"config 1 prefill layer (conv + chunk GDN + gated norm), full T={T}, 1 warm-up + {reps} timed, "
+                      f"oracle/ fp32 PyTorch on {platform.processor() or platform.machine()}"}
+
+
+def run_reference(args, rank, world):
+    """The reference's CPU implementation of the path (oracle port), on this box's host cores."""
+    if rank != 0:
+        return None
+    torch.set_num_threads(os.cpu_count() or 1)
+    T = 4096
+    x = make_prefill_inputs(seed=1, T=T)
+    for _ in range(args.warmup):
+        cpu_prefill_once(x, T)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_prefill_once(x, T)
+    dt = time.perf_counter() - t0
+    value = T * args.steps / dt
+    return {"impl": "reference", "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (same generator as the GPU arm)",
+            "config": {"workload": "config 1: 9B-shaped prefill layer, B=1, T=4096, 16/32 heads (CPU, rank 0 only)"},
+            "cpu_baseline": {"value": round(value, 1), "unit": "tokens/s", "cores": torch.get_num_threads(),
+                             "kind": "port",
+                             "sample": f"full config-1 layer per step: oracle/ (fp32 PyTorch restatement of "
+                                       f"model/model.py eager path) conv + chunk GDN + gated norm, T={T}"},
+            "e2e": {"value": round(value, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--no-extras", dest="extras", action="store_false")
+    ap.add_argument("--no-cpu-baseline", dest="cpu", action="store_false")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        out = run_reference(args, rank, world)
+        if out is not None:
+            print(json.dumps(out), flush=True)
+        return
+
+    if not torch.cuda.is_available():
+        print(json.dumps({"error": "no CUDA device"}))
+        sys.exit(1)
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+
+        def rank_sync():
+            dist.barrier()
+
+        def reduce_max(x):
+            t = torch.tensor([x], dtype=torch.float64, device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return t.item()
+    else:
+        def rank_sync():
+            pass
+
+        def reduce_max(x):
+            return x
+
+    result = run_ours(args, rank, world, device, rank_sync, reduce_max)
+    if rank == 0 and world == 1 and args.cpu:
+        result["cpu_baseline"] = cpu_baseline()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,166 @@
+/*
+ * gdn_b200.h — C ABI of the B200 (sm_100a) gated-delta-rule library.
+ *
+ * Every entry point takes raw device pointers, element counts and element strides,
+ * launches on the given CUDA stream (passed as void*, a cudaStream_t; NULL is the
+ * legacy default stream), never allocates device memory, never synchronises the
+ * host, and returns a status code (GDN_OK on success). Calls are therefore safe to
+ * record into CUDA graphs. Element strides count elements, not bytes; the innermost
+ * (head) dimension is always contiguous.
+ *
+ * Each declaration names the reference interface it replaces (PostHog/jeeves,
+ * file:line). Shapes use B batch rows, T tokens, H key heads, HV value heads
+ * (HV a multiple of H; value head hv reads key head hv / (HV / H), i.e.
+ * repeat_interleave semantics as in model/model.py:487-490), Dk = Dv = 128.
+ */
+#ifndef GDN_B200_H
+#define GDN_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define GDN_API __attribute__((visibility("default")))
+#else
+#define GDN_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. Input errors (1-4, 7) are raised before any launch; 5-6 report the device. */
+enum {
+    GDN_OK = 0,
+    GDN_ERR_SHAPE = 1,        /* a size, a head count or a stride is not accepted */
+    GDN_ERR_DTYPE = 2,        /* an unsupported element type code */
+    GDN_ERR_ALIGN = 3,        /* a pointer or stride breaks the 16-byte alignment rule */
+    GDN_ERR_NULL = 4,         /* a required pointer is NULL */
+    GDN_ERR_LAUNCH = 5,       /* the CUDA launch failed (cudaGetLastError) */
+    GDN_ERR_DEVICE_TIMEOUT = 6, /* a bounded device-side wait gave up (see gdn_device_error) */
+    GDN_ERR_UNSUPPORTED = 7   /* a valid but unimplemented configuration (e.g. head dim != 128) */
+};
+
+/* Element type codes. */
+enum { GDN_F32 = 0, GDN_BF16 = 1 };
+
+/* Text for a status code. */
+GDN_API const char* gdn_status_string(int status);
+
+/* ABI version of this header (bumped on any signature change). */
+GDN_API int gdn_abi_version(void);
+
+/* Device-side error word of the current device, written by bounded waits inside kernels
+ * (0 = none). Reading it synchronises the stream; it is meant for tests and debugging.
+ * Passing reset != 0 clears it afterwards. */
+GDN_API int gdn_device_error(void* stream, int reset);
+
+/*
+ * Gated delta rule, recurrent form, on CUDA cores in fp32. One launch covers:
+ *   - the decode step with the state updated in place (state_out == state_in):
+ *       replaces model/fla_inplace.py:17-26 (gated_delta_rule_step_inplace) and the
+ *       StaticCache decode branch at model/model.py:496-499;
+ *   - the T-token recurrent call with or without a final state:
+ *       replaces gated_delta_rule_step, model/model.py:297-302 (fla fused_recurrent /
+ *       torch_recurrent_gated_delta_rule :221-239), e.g. the verify outputs of
+ *       inference/engine.py:250-252;
+ *   - block-K verify with per-token state snapshots (snapshots != NULL, layout
+ *       [B, T, HV, Dk, Dv]); the rollback point after j accepted tokens is snapshot j-1;
+ *   - the rollback/commit advance (steps != NULL): row b advances by clamp(steps[b], 0, T)
+ *       tokens and writes no outputs; replaces gated_delta_rule_advance_inplace,
+ *       model/model.py:305-311 and model/fla_inplace.py:29-74.
+ *   - with cu_seqlens (int32, [batch + 1], a packed batch of 1), sequence n is tokens
+ *       cu_seqlens[n] .. cu_seqlens[n+1]; state rows are per sequence.
+ * q, k: [B, T, H, Dk]; v: [B, T, HV, Dv] (strides in elements for the b, t, h dims);
+ * g: [B, T, HV] fp32 log decay, contiguous; beta: [B, T, HV] contiguous (bf16 or fp32);
+ * state_in: [B, HV, Dk, Dv] fp32 or NULL for a zero state; state_out: same or NULL;
+ * o: [B, T, HV, Dv] contiguous in qkv_dtype, or NULL (no outputs).
+ * q is normalised and scaled by `scale` (Dk^-0.5 in the reference); q and k are
+ * L2-normalised with eps 1e-6 inside the kernel (model/model.py:217-218, :253).
+ */
+GDN_API int gdn_recurrent(const void* q, const void* k, const void* v, int qkv_dtype,
+                  const float* g, const void* beta, int beta_dtype,
+                  const float* state_in, float* state_out, float* snapshots, void* o,
+                  const int64_t* steps, const int32_t* cu_seqlens,
+                  int64_t batch, int64_t seqlen, int64_t key_heads, int64_t value_heads,
+                  int64_t head_dim_k, int64_t head_dim_v,
+                  int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h,
+                  int64_t k_stride_b, int64_t k_stride_t, int64_t k_stride_h,
+                  int64_t v_stride_b, int64_t v_stride_t, int64_t v_stride_h,
+                  float scale, void* stream);
+
+/*
+ * Rollback by snapshot: for each row b with accepted[b] >= 1, copy snapshot
+ * accepted[b]-1 (clamped to T) into state[b]; rows with accepted[b] <= 0 keep their state.
+ * snapshots: [B, T, HV, Dk, Dv] fp32 from gdn_recurrent; state: [B, HV, Dk, Dv] fp32.
+ * Same result as gated_delta_rule_advance_inplace (model/model.py:305-311) after the
+ * verify of inference/engine.py:471-472, without recomputing the accepted tokens.
+ */
+GDN_API int gdn_snapshot_commit(float* state, const float* snapshots, const int64_t* accepted,
+                        int64_t batch, int64_t seqlen, int64_t value_heads,
+                        int64_t head_dim_k, int64_t head_dim_v, void* stream);
+
+/*
+ * Causal depthwise conv1d + SiLU over a prefill (replaces causal_conv1d,
+ * model/model.py:199-204). x: [B, T, C] bf16 (strides x_stride_b, x_stride_t; channels
+ * contiguous); w: [C, K] bf16; y: [B, T, C] bf16 contiguous. With cu_seqlens (int32,
+ * [batch+1]) x is one packed row of `seqlen` tokens holding `batch` sequences, and every
+ * sequence restarts from zeros. Rounds like the eager path:
+ * fp32 sum in tap order -> bf16 -> silu in fp32 -> bf16.
+ */
+GDN_API int gdn_conv1d_silu(const void* x, int64_t x_stride_b, int64_t x_stride_t, const void* w, void* y,
+                    const int32_t* cu_seqlens, int64_t batch, int64_t seqlen, int64_t channels,
+                    int64_t kernel_size, void* stream);
+
+/*
+ * One decode token of the conv (replaces causal_conv1d_step, model/model.py:207-214).
+ * x: [B, C] bf16 (row stride x_stride_b); state: [B, C, taps] bf16 updated in place to
+ * the last `taps` inputs; w: [C, K] bf16 with K <= taps + 1; y: [B, C] bf16.
+ * Rounds like the eager path: bf16 products, fp32 sum, bf16, silu, bf16.
+ */
+GDN_API int gdn_conv1d_silu_step(const void* x, int64_t x_stride_b, void* state, const void* w, void* y,
+                         int64_t batch, int64_t channels, int64_t taps, int64_t kernel_size,
+                         void* stream);
+
+/*
+ * Verify-step conv (replaces conv_step / eager_conv_step, model/model.py:324-339 and the
+ * Triton _conv_step, model/triton_kernels.py:265-325). state: [B, C, taps] bf16; qkv:
+ * [B, T, C] bf16 (strides qkv_stride_b, qkv_stride_t); w: [C, K] bf16 (K <= taps + 1).
+ * Writes ext [B, C, taps + T] = state ++ qkv^T, and q, k [B, T, HV, Dk] (repeat-
+ * interleaved from the key heads), v [B, T, HV, Dv], all bf16 contiguous.
+ */
+GDN_API int gdn_conv_step(const void* state, const void* qkv, int64_t qkv_stride_b, int64_t qkv_stride_t,
+                  const void* w, void* ext, void* q, void* k, void* v,
+                  int64_t batch, int64_t seqlen, int64_t taps, int64_t kernel_size,
+                  int64_t key_dim, int64_t value_dim, int64_t head_dim_k, int64_t head_dim_v,
+                  void* stream);
+
+/*
+ * Output-gated RMSNorm (replaces GatedRMSNorm.forward, model/model.py:150-158):
+ * y = bf16(bf16(w * bf16(x * rsqrt(mean(x^2) + eps))) * silu(z)). x, z, y: [rows, dim]
+ * bf16 contiguous, w: [dim] bf16.
+ */
+GDN_API int gdn_gated_rmsnorm(const void* x, const void* z, const void* w, void* y,
+                      int64_t rows, int64_t dim, float eps, void* stream);
+
+/*
+ * Fused decode layer for one new token per row: conv step (+SiLU) over the pre-conv
+ * qkv, q/k L2 norm, gated delta rule step with the state updated in place, and the
+ * output-gated RMSNorm. Replaces the StaticCache decode branch of
+ * GatedDeltaNet.forward (model/model.py:465-467, :496-499, :516).
+ * qkv: [B, C] bf16 (row stride qkv_stride_b) with C = 2*H*Dk + HV*Dv laid out q | k | v;
+ * conv_state: [B, C, taps] bf16 (in place); conv_w: [C, K] bf16; g: [B, HV] fp32;
+ * beta: [B, HV] bf16; state: [B, HV, Dk, Dv] fp32 (in place); z: [B, HV, Dv] bf16;
+ * norm_w: [Dv] bf16; out: [B, HV, Dv] bf16.
+ */
+GDN_API int gdn_decode_layer(const void* qkv, int64_t qkv_stride_b, void* conv_state, const void* conv_w,
+                     const float* g, const void* beta, float* state, const void* z,
+                     const void* norm_w, void* out,
+                     int64_t batch, int64_t key_heads, int64_t value_heads,
+                     int64_t head_dim_k, int64_t head_dim_v, int64_t taps, int64_t kernel_size,
+                     float scale, float eps, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GDN_B200_H */

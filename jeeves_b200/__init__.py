@@ -1,0 +1,22 @@
+"""B200 (sm_100a) gated-delta-rule library for the linear-attention layers of a Qwen3.5-style hybrid model.
+
+Drop-in replacements for the gated-delta hot path of PostHog/jeeves: the chunked
+prefill, the recurrent decode and block-K verify steps with snapshot rollback, the
+causal conv1d + SiLU and the output-gated RMSNorm around them. All compute runs in
+hand-written CUDA kernels of ``_lib/libgdn_b200.so`` through its C ABI
+(``include/gdn_b200.h``); ``install`` routes the reference's dispatchers to them.
+"""
+
+from .gated_delta import (  # noqa: F401
+    gated_delta_rule_advance_inplace,
+    gated_delta_rule_chunk,
+    gated_delta_rule_rollback,
+    gated_delta_rule_step,
+    gated_delta_rule_verify,
+)
+from .conv import causal_conv1d, causal_conv1d_step, conv_step, eager_conv_step  # noqa: F401
+from .norm import GatedRMSNorm, gated_rms_norm  # noqa: F401
+from .layer import decode_layer_step  # noqa: F401
+from . import fla_inplace  # noqa: F401
+from ._lib import load as load_library  # noqa: F401
+from .integration import install  # noqa: F401

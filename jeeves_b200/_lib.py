@@ -1,0 +1,79 @@
+"""ctypes binding of ``libgdn_b200.so`` (the C ABI declared in ``include/gdn_b200.h``).
+
+The library is loaded once, from this package's ``_lib`` folder. There is no fallback:
+if the library is missing or cannot be loaded, every operation raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "_lib", "libgdn_b200.so")
+
+OK, ERR_SHAPE, ERR_DTYPE, ERR_ALIGN, ERR_NULL, ERR_LAUNCH, ERR_DEVICE_TIMEOUT, ERR_UNSUPPORTED = range(8)
+F32, BF16 = 0, 1
+
+_p = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_i32 = ctypes.c_int
+_f32 = ctypes.c_float
+
+# name -> argument types, in declaration order of include/gdn_b200.h
+SIGNATURES: dict[str, list] = {
+    "gdn_status_string": [_i32],
+    "gdn_abi_version": [],
+    "gdn_device_error": [_p, _i32],
+    "gdn_recurrent": [_p, _p, _p, _i32, _p, _p, _i32, _p, _p, _p, _p, _p, _p,
+                      _i64, _i64, _i64, _i64, _i64, _i64,
+                      _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _p],
+    "gdn_snapshot_commit": [_p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p],
+    "gdn_conv1d_silu": [_p, _i64, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _p],
+    "gdn_conv1d_silu_step": [_p, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _p],
+    "gdn_conv_step": [_p, _p, _i64, _i64, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p],
+    "gdn_gated_rmsnorm": [_p, _p, _p, _p, _i64, _i64, _f32, _p],
+    "gdn_decode_layer": [_p, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
+                         _f32, _f32, _p],
+}
+
+_lock = threading.Lock()
+_lib = None
+
+
+class LibraryError(RuntimeError):
+    pass
+
+
+def load() -> ctypes.CDLL:
+    """Load the library (once). Raises if it is missing: there is no other implementation."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(LIB_PATH):
+            raise LibraryError(f"{LIB_PATH} is missing; build it with `python -m jeeves_b200.build`")
+        lib = ctypes.CDLL(LIB_PATH)
+        for name, args in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.argtypes = args
+            fn.restype = ctypes.c_char_p if name == "gdn_status_string" else ctypes.c_int
+        _lib = lib
+        return lib
+
+
+def status_text(status: int) -> str:
+    return load().gdn_status_string(status).decode()
+
+
+def check(status: int, what: str) -> None:
+    """Map a C status to the reference's error convention: ValueError for bad input, RuntimeError otherwise."""
+    if status == OK:
+        return
+    text = f"{what}: {status_text(status)} (status {status})"
+    if status in (ERR_SHAPE, ERR_DTYPE, ERR_ALIGN, ERR_NULL, ERR_UNSUPPORTED):
+        raise ValueError(text)
+    raise RuntimeError(text)

@@ -1,0 +1,185 @@
+// C ABI: argument checks and dispatch. Declarations and contracts are in include/gdn_b200.h.
+
+#include "common.cuh"
+#include "launch.h"
+
+using namespace gdn;
+
+namespace {
+
+constexpr int kAbiVersion = 1;
+
+inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+inline int elem_size(int dtype) { return dtype == GDN_BF16 ? 2 : 4; }
+
+inline bool known_dtype(int dtype) { return dtype == GDN_BF16 || dtype == GDN_F32; }
+
+// Vector loads need 16-byte alignment of every row start: base pointer aligned and every
+// stride a multiple of 16 bytes (the head dim, 128, always is).
+inline bool rows_aligned(const void* p, int esize, int64_t s0, int64_t s1, int64_t s2) {
+    return aligned16(p) && (s0 * esize) % 16 == 0 && (s1 * esize) % 16 == 0 && (s2 * esize) % 16 == 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* gdn_status_string(int status) {
+    switch (status) {
+        case GDN_OK: return "ok";
+        case GDN_ERR_SHAPE: return "invalid shape, head count or stride";
+        case GDN_ERR_DTYPE: return "unsupported element type";
+        case GDN_ERR_ALIGN: return "pointer or stride not 16-byte aligned";
+        case GDN_ERR_NULL: return "required pointer is NULL";
+        case GDN_ERR_LAUNCH: return "CUDA kernel launch failed";
+        case GDN_ERR_DEVICE_TIMEOUT: return "a bounded device-side wait timed out";
+        case GDN_ERR_UNSUPPORTED: return "unsupported configuration";
+        default: return "unknown status";
+    }
+}
+
+int gdn_abi_version(void) { return kAbiVersion; }
+
+int gdn_device_error(void* stream, int reset) {
+    int value = 0;
+    if (cudaMemcpyFromSymbolAsync(&value, g_device_error, sizeof(int), 0, cudaMemcpyDeviceToHost, as_stream(stream)) !=
+        cudaSuccess)
+        return -1;
+    if (cudaStreamSynchronize(as_stream(stream)) != cudaSuccess) return -1;
+    if (reset) {
+        const int zero = 0;
+        if (cudaMemcpyToSymbolAsync(g_device_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, as_stream(stream)) !=
+            cudaSuccess)
+            return -1;
+        if (cudaStreamSynchronize(as_stream(stream)) != cudaSuccess) return -1;
+    }
+    return value;
+}
+
+int gdn_recurrent(const void* q, const void* k, const void* v, int qkv_dtype, const float* g, const void* beta,
+                  int beta_dtype, const float* state_in, float* state_out, float* snapshots, void* o,
+                  const int64_t* steps, const int32_t* cu_seqlens, int64_t batch, int64_t seqlen, int64_t key_heads,
+                  int64_t value_heads, int64_t head_dim_k, int64_t head_dim_v, int64_t q_stride_b, int64_t q_stride_t,
+                  int64_t q_stride_h, int64_t k_stride_b, int64_t k_stride_t, int64_t k_stride_h, int64_t v_stride_b,
+                  int64_t v_stride_t, int64_t v_stride_h, float scale, void* stream) {
+    if (!known_dtype(qkv_dtype) || !known_dtype(beta_dtype)) return GDN_ERR_DTYPE;
+    if (batch < 0 || seqlen < 0 || key_heads <= 0 || value_heads <= 0 || value_heads % key_heads) return GDN_ERR_SHAPE;
+    if (batch > 65535 || value_heads > 65535) return GDN_ERR_SHAPE;
+    if (head_dim_k != kHeadDim || head_dim_v != kHeadDim) return GDN_ERR_UNSUPPORTED;
+    if (batch == 0 || seqlen == 0) {
+        // nothing to run; a zero-length call still copies the state through
+        if (batch > 0 && state_out && state_out != state_in && !steps) {
+            const size_t bytes = (size_t)batch * value_heads * kHeadDim * kHeadDim * sizeof(float);
+            cudaError_t e = state_in ? cudaMemcpyAsync(state_out, state_in, bytes, cudaMemcpyDeviceToDevice, as_stream(stream))
+                                     : cudaMemsetAsync(state_out, 0, bytes, as_stream(stream));
+            return e == cudaSuccess ? GDN_OK : GDN_ERR_LAUNCH;
+        }
+        return GDN_OK;
+    }
+    if (!k || !v || !g || !beta) return GDN_ERR_NULL;
+    if (o && !q) return GDN_ERR_NULL;
+    if (steps && (o || snapshots)) return GDN_ERR_SHAPE;  // an advance writes only the state
+    const int es = elem_size(qkv_dtype);
+    if (!rows_aligned(k, es, k_stride_b, k_stride_t, k_stride_h) || !rows_aligned(v, es, v_stride_b, v_stride_t, v_stride_h))
+        return GDN_ERR_ALIGN;
+    if (q && !rows_aligned(q, es, q_stride_b, q_stride_t, q_stride_h)) return GDN_ERR_ALIGN;
+    if ((state_in && !aligned16(state_in)) || (state_out && !aligned16(state_out)) ||
+        (snapshots && !aligned16(snapshots)) || (o && !aligned16(o)))
+        return GDN_ERR_ALIGN;
+    RecurrentArgs a;
+    a.q = q; a.k = k; a.v = v; a.qkv_dtype = qkv_dtype;
+    a.g = g; a.beta = beta; a.beta_dtype = beta_dtype;
+    a.state_in = state_in; a.state_out = state_out; a.snapshots = snapshots; a.o = o;
+    a.steps = steps; a.cu_seqlens = cu_seqlens;
+    a.rows = batch; a.T = seqlen; a.H = (int)key_heads; a.HV = (int)value_heads;
+    a.qsb = q_stride_b; a.qst = q_stride_t; a.qsh = q_stride_h;
+    a.ksb = k_stride_b; a.kst = k_stride_t; a.ksh = k_stride_h;
+    a.vsb = v_stride_b; a.vst = v_stride_t; a.vsh = v_stride_h;
+    a.scale = scale;
+    return launch_recurrent(a, as_stream(stream));
+}
+
+int gdn_snapshot_commit(float* state, const float* snapshots, const int64_t* accepted, int64_t batch, int64_t seqlen,
+                        int64_t value_heads, int64_t head_dim_k, int64_t head_dim_v, void* stream) {
+    if (batch < 0 || seqlen <= 0 || value_heads <= 0 || batch > 65535 || value_heads > 65535) return GDN_ERR_SHAPE;
+    if (head_dim_k != kHeadDim || head_dim_v != kHeadDim) return GDN_ERR_UNSUPPORTED;
+    if (batch == 0) return GDN_OK;
+    if (!state || !snapshots || !accepted) return GDN_ERR_NULL;
+    if (!aligned16(state) || !aligned16(snapshots)) return GDN_ERR_ALIGN;
+    return launch_snapshot_commit(state, snapshots, accepted, batch, seqlen, value_heads, as_stream(stream));
+}
+
+int gdn_conv1d_silu(const void* x, int64_t x_stride_b, int64_t x_stride_t, const void* w, void* y,
+                    const int32_t* cu_seqlens, int64_t batch, int64_t seqlen, int64_t channels, int64_t kernel_size,
+                    void* stream) {
+    if (batch < 0 || seqlen < 0 || channels <= 0 || channels % 8) return GDN_ERR_SHAPE;
+    if (kernel_size < 2 || kernel_size > 4) return GDN_ERR_UNSUPPORTED;
+    if (batch == 0 || seqlen == 0) return GDN_OK;
+    if (!x || !w || !y) return GDN_ERR_NULL;
+    if (!rows_aligned(x, 2, x_stride_b, x_stride_t, 0) || !aligned16(y)) return GDN_ERR_ALIGN;
+    if (cu_seqlens && batch > 65535) return GDN_ERR_SHAPE;
+    if (!cu_seqlens && batch > 65535) return GDN_ERR_SHAPE;
+    return launch_conv1d_silu(x, x_stride_b, x_stride_t, w, y, cu_seqlens, batch, seqlen, channels, (int)kernel_size,
+                              as_stream(stream));
+}
+
+int gdn_conv1d_silu_step(const void* x, int64_t x_stride_b, void* state, const void* w, void* y, int64_t batch,
+                         int64_t channels, int64_t taps, int64_t kernel_size, void* stream) {
+    if (batch < 0 || channels <= 0 || taps < 1 || taps > 8 || kernel_size < 1 || kernel_size > taps + 1)
+        return GDN_ERR_SHAPE;
+    if (batch == 0) return GDN_OK;
+    if (!x || !state || !w || !y) return GDN_ERR_NULL;
+    return launch_conv1d_silu_step(x, x_stride_b, state, w, y, batch, channels, (int)taps, (int)kernel_size,
+                                   as_stream(stream));
+}
+
+int gdn_conv_step(const void* state, const void* qkv, int64_t qkv_stride_b, int64_t qkv_stride_t, const void* w,
+                  void* ext, void* q, void* k, void* v, int64_t batch, int64_t seqlen, int64_t taps, int64_t kernel_size,
+                  int64_t key_dim, int64_t value_dim, int64_t head_dim_k, int64_t head_dim_v, void* stream) {
+    if (batch < 0 || seqlen < 0 || taps < 1 || taps > 8 || kernel_size < 1 || kernel_size > taps + 1) return GDN_ERR_SHAPE;
+    if (head_dim_k <= 0 || head_dim_v <= 0 || key_dim <= 0 || value_dim <= 0) return GDN_ERR_SHAPE;
+    if (key_dim % head_dim_k || value_dim % head_dim_v) return GDN_ERR_SHAPE;
+    const int64_t kh = key_dim / head_dim_k, vh = value_dim / head_dim_v;
+    if (vh % kh) return GDN_ERR_SHAPE;
+    if (batch > 65535) return GDN_ERR_SHAPE;
+    if (batch == 0 || seqlen == 0) {
+        if (batch == 0) return GDN_OK;
+    }
+    if (!state || !qkv || !w || !ext || !q || !k || !v) return GDN_ERR_NULL;
+    return launch_conv_step(state, qkv, qkv_stride_b, qkv_stride_t, w, ext, q, k, v, batch, seqlen, (int)taps,
+                            (int)kernel_size, key_dim, value_dim, (int)head_dim_k, (int)head_dim_v, as_stream(stream));
+}
+
+int gdn_gated_rmsnorm(const void* x, const void* z, const void* w, void* y, int64_t rows, int64_t dim, float eps,
+                      void* stream) {
+    if (rows < 0 || dim <= 0) return GDN_ERR_SHAPE;
+    if (dim != kHeadDim) return GDN_ERR_UNSUPPORTED;
+    if (rows == 0) return GDN_OK;
+    if (!x || !z || !w || !y) return GDN_ERR_NULL;
+    if (!aligned16(x) || !aligned16(z) || !aligned16(y) || (reinterpret_cast<uintptr_t>(w) & 7u)) return GDN_ERR_ALIGN;
+    if (rows > (int64_t)65535 * 65535) return GDN_ERR_SHAPE;
+    return launch_gated_rmsnorm(x, z, w, y, rows, (int)dim, eps, as_stream(stream));
+}
+
+int gdn_decode_layer(const void* qkv, int64_t qkv_stride_b, void* conv_state, const void* conv_w, const float* g,
+                     const void* beta, float* state, const void* z, const void* norm_w, void* out, int64_t batch,
+                     int64_t key_heads, int64_t value_heads, int64_t head_dim_k, int64_t head_dim_v, int64_t taps,
+                     int64_t kernel_size, float scale, float eps, void* stream) {
+    if (batch < 0 || key_heads <= 0 || value_heads <= 0 || value_heads % key_heads) return GDN_ERR_SHAPE;
+    if (taps < 1 || taps > 8 || kernel_size < 1 || kernel_size > taps + 1) return GDN_ERR_SHAPE;
+    if (head_dim_k != kHeadDim || head_dim_v != kHeadDim) return GDN_ERR_UNSUPPORTED;
+    if (batch > 65535 || value_heads > 65535) return GDN_ERR_SHAPE;
+    if (batch == 0) return GDN_OK;
+    if (!qkv || !conv_state || !conv_w || !g || !beta || !state || !z || !norm_w || !out) return GDN_ERR_NULL;
+    if (!aligned16(state) || !aligned16(z) || !aligned16(out) || (reinterpret_cast<uintptr_t>(norm_w) & 7u))
+        return GDN_ERR_ALIGN;
+    DecodeLayerArgs a;
+    a.qkv = qkv; a.qkv_sb = qkv_stride_b; a.conv_state = conv_state; a.conv_w = conv_w;
+    a.g = g; a.beta = beta; a.state = state; a.z = z; a.norm_w = norm_w; a.out = out;
+    a.B = batch; a.H = (int)key_heads; a.HV = (int)value_heads; a.taps = (int)taps; a.K = (int)kernel_size;
+    a.scale = scale; a.eps = eps;
+    return launch_decode_layer(a, as_stream(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,220 @@
+// Causal depthwise conv1d + SiLU kernels around the gated delta rule.
+//
+// Rounding follows the reference's eager path: the prefill conv and the verify conv use
+// F.conv1d (an fp32 sum of fp32 products in tap order, without fused multiply-add,
+// rounded once to bf16;
+// model/model.py:199-204, :324-332) and the decode step multiplies in bf16 before an
+// fp32 sum (model/model.py:207-214). SiLU is x / (1 + exp(-x)) in fp32 on the bf16 value.
+
+#include "common.cuh"
+#include "launch.h"
+
+namespace gdn {
+
+constexpr int kMaxTaps = 8;
+
+// Prefill: each thread owns 8 channels and walks a run of tokens with the last K-1
+// inputs in registers, so every input is read from memory once.
+constexpr int kConvTokens = 32;
+
+__device__ __forceinline__ void load8(const bf16* p, float* out) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(p);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(h[i]);
+        out[2 * i] = f.x;
+        out[2 * i + 1] = f.y;
+    }
+}
+
+__device__ __forceinline__ void store8(bf16* p, const float* v) {
+    uint4 raw;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+    *reinterpret_cast<uint4*>(p) = raw;
+}
+
+template <int K>
+__global__ void conv1d_silu_kernel(const bf16* __restrict__ x, int64_t sxb, int64_t sxt, const bf16* __restrict__ w,
+                                   bf16* __restrict__ y, const int32_t* __restrict__ cu, int nseq, int64_t T, int64_t C) {
+    const int64_t c8 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8;
+    if (c8 >= C) return;
+    const int64_t b = blockIdx.z;
+    const int64_t t0 = (int64_t)blockIdx.y * kConvTokens;
+    if (t0 >= T) return;
+    const int64_t t1 = t0 + kConvTokens < T ? t0 + kConvTokens : T;
+
+    float wt[8][K];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+        for (int i = 0; i < K; ++i) wt[j][i] = to_f32(w[(c8 + j) * K + i]);
+
+    // sequence boundaries: a window never reaches back past the start of its sequence
+    int64_t seq_start = 0, seq_end = T;
+    int s = 0;
+    if (cu) {
+        while (s + 1 < nseq && cu[s + 1] <= t0) ++s;
+        seq_start = cu[s];
+        seq_end = cu[s + 1];
+    }
+    float win[K][8];  // win[K-1] is the current token; win[0] the oldest
+#pragma unroll
+    for (int i = 0; i < K - 1; ++i) {
+        const int64_t t = t0 - (K - 1) + i;
+        if (t >= seq_start) load8(x + b * sxb + t * sxt + c8, win[i]);
+        else
+#pragma unroll
+            for (int j = 0; j < 8; ++j) win[i][j] = 0.f;
+    }
+    for (int64_t t = t0; t < t1; ++t) {
+        if (cu && t >= seq_end) {  // next sequence starts here: clear the window
+            while (s + 1 < nseq && cu[s + 1] <= t) ++s;
+            seq_start = cu[s];
+            seq_end = cu[s + 1];
+#pragma unroll
+            for (int i = 0; i < K - 1; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) win[i][j] = 0.f;
+        }
+        load8(x + b * sxb + t * sxt + c8, win[K - 1]);
+        float out[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            float acc = 0.f;
+#pragma unroll
+            for (int i = 0; i < K; ++i) acc = __fadd_rn(acc, __fmul_rn(wt[j][i], win[i][j]));
+            out[j] = silu_f32(round_bf16(acc));
+        }
+        store8(y + (b * T + t) * C + c8, out);
+#pragma unroll
+        for (int i = 0; i < K - 1; ++i)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) win[i][j] = win[i + 1][j];
+    }
+}
+
+int launch_conv1d_silu(const void* x, int64_t sxb, int64_t sxt, const void* w, void* y, const int32_t* cu, int64_t B,
+                       int64_t T, int64_t C, int K, cudaStream_t s) {
+    if (B == 0 || T == 0) return GDN_OK;
+    constexpr int threads = 128;
+    dim3 grid((unsigned)((C / 8 + threads - 1) / threads), (unsigned)((T + kConvTokens - 1) / kConvTokens), (unsigned)B);
+    const int nseq = cu ? (int)B : 0;  // with cu_seqlens the caller passes the sequence count as B
+    if (cu) grid.z = 1;
+    auto xp = static_cast<const bf16*>(x);
+    auto wp = static_cast<const bf16*>(w);
+    auto yp = static_cast<bf16*>(y);
+    switch (K) {
+        case 2: conv1d_silu_kernel<2><<<grid, threads, 0, s>>>(xp, sxb, sxt, wp, yp, cu, nseq, T, C); break;
+        case 3: conv1d_silu_kernel<3><<<grid, threads, 0, s>>>(xp, sxb, sxt, wp, yp, cu, nseq, T, C); break;
+        case 4: conv1d_silu_kernel<4><<<grid, threads, 0, s>>>(xp, sxb, sxt, wp, yp, cu, nseq, T, C); break;
+        default: return GDN_ERR_UNSUPPORTED;
+    }
+    return launch_status();
+}
+
+// Decode step: y = silu(bf16(sum_i bf16(w_i * window_i))); the state keeps the last `taps` inputs.
+__global__ void conv1d_silu_step_kernel(const bf16* __restrict__ x, int64_t sxb, bf16* __restrict__ state,
+                                        const bf16* __restrict__ w, bf16* __restrict__ y, int64_t B, int64_t C,
+                                        int taps, int K) {
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= B * C) return;
+    const int64_t b = idx / C, c = idx % C;
+    bf16* st = state + idx * taps;
+    float buf[kMaxTaps + 1];
+    for (int i = 0; i < taps; ++i) buf[i] = to_f32(st[i]);
+    buf[taps] = to_f32(x[b * sxb + c]);
+    float acc = 0.f;
+    for (int i = 0; i < K; ++i) acc = __fadd_rn(acc, round_bf16(__fmul_rn(to_f32(w[c * K + i]), buf[taps + 1 - K + i])));
+    y[b * C + c] = __float2bfloat16_rn(silu_f32(round_bf16(acc)));
+    for (int i = 0; i < taps; ++i) st[i] = __float2bfloat16_rn(buf[i + 1]);
+}
+
+int launch_conv1d_silu_step(const void* x, int64_t sxb, void* state, const void* w, void* y, int64_t B, int64_t C,
+                            int taps, int K, cudaStream_t s) {
+    if (B * C == 0) return GDN_OK;
+    constexpr int threads = 256;
+    const int64_t blocks = (B * C + threads - 1) / threads;
+    conv1d_silu_step_kernel<<<(unsigned)blocks, threads, 0, s>>>(static_cast<const bf16*>(x), sxb,
+                                                                 static_cast<bf16*>(state), static_cast<const bf16*>(w),
+                                                                 static_cast<bf16*>(y), B, C, taps, K);
+    return launch_status();
+}
+
+// Rolls the conv state forward by one token (used after the fused decode layer).
+__global__ void conv_state_shift_kernel(const bf16* __restrict__ x, int64_t sxb, bf16* __restrict__ state, int64_t B,
+                                        int64_t C, int taps) {
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= B * C) return;
+    const int64_t b = idx / C, c = idx % C;
+    bf16* st = state + idx * taps;
+    bf16 vals[kMaxTaps];
+    for (int i = 1; i < taps; ++i) vals[i - 1] = st[i];
+    vals[taps - 1] = x[b * sxb + c];
+    for (int i = 0; i < taps; ++i) st[i] = vals[i];
+}
+
+int launch_conv_state_shift(const void* x, int64_t sxb, void* state, int64_t B, int64_t C, int taps, cudaStream_t s) {
+    if (B * C == 0) return GDN_OK;
+    constexpr int threads = 256;
+    const int64_t blocks = (B * C + threads - 1) / threads;
+    conv_state_shift_kernel<<<(unsigned)blocks, threads, 0, s>>>(static_cast<const bf16*>(x), sxb,
+                                                                 static_cast<bf16*>(state), B, C, taps);
+    return launch_status();
+}
+
+// Verify conv: ext = state ++ qkv^T; output t = silu(bf16(sum_i w_i ext[t + taps - K + 1 + i]))
+// split into q, k (repeat-interleaved over the value heads) and v. One thread per channel.
+__global__ void conv_step_kernel(const bf16* __restrict__ state, const bf16* __restrict__ qkv, int64_t sqb, int64_t sqt,
+                                 const bf16* __restrict__ w, bf16* __restrict__ ext, bf16* __restrict__ q,
+                                 bf16* __restrict__ k, bf16* __restrict__ v, int64_t T, int taps, int K, int64_t C,
+                                 int64_t key_dim, int64_t value_dim, int dk, int dv, int rep) {
+    const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= C) return;
+    const int64_t b = blockIdx.y;
+    const int64_t L = taps + T;
+    bf16* e = ext + (b * C + c) * L;
+    const bf16* st = state + (b * C + c) * taps;
+    for (int i = 0; i < taps; ++i) e[i] = st[i];
+    for (int64_t t = 0; t < T; ++t) e[taps + t] = qkv[b * sqb + t * sqt + c];
+    float wt[kMaxTaps];
+    for (int i = 0; i < K; ++i) wt[i] = to_f32(w[c * K + i]);
+    const int64_t k_heads = key_dim / dk, v_heads = value_dim / dv;
+    for (int64_t t = 0; t < T; ++t) {
+        float acc = 0.f;
+        for (int i = 0; i < K; ++i) {
+            const int64_t col = t + taps - K + 1 + i;
+            const float xv = col < taps ? to_f32(st[col]) : to_f32(qkv[b * sqb + (col - taps) * sqt + c]);
+            acc = __fadd_rn(acc, __fmul_rn(wt[i], xv));
+        }
+        const bf16 yv = __float2bfloat16_rn(silu_f32(round_bf16(acc)));
+        if (c < 2 * key_dim) {
+            const int64_t kc = c < key_dim ? c : c - key_dim;
+            const int64_t head = kc / dk, d = kc % dk;
+            bf16* dst = c < key_dim ? q : k;
+            for (int r = 0; r < rep; ++r) dst[((b * T + t) * v_heads + head * rep + r) * dk + d] = yv;
+        } else {
+            v[(b * T + t) * value_dim + (c - 2 * key_dim)] = yv;
+        }
+    }
+    (void)k_heads;
+}
+
+int launch_conv_step(const void* state, const void* qkv, int64_t sqb, int64_t sqt, const void* w, void* ext, void* q,
+                     void* k, void* v, int64_t B, int64_t T, int taps, int K, int64_t key_dim, int64_t value_dim, int dk,
+                     int dv, cudaStream_t s) {
+    const int64_t C = 2 * key_dim + value_dim;
+    if (B == 0 || C == 0) return GDN_OK;
+    const int rep = (int)((value_dim / dv) / (key_dim / dk));
+    constexpr int threads = 128;
+    dim3 grid((unsigned)((C + threads - 1) / threads), (unsigned)B);
+    conv_step_kernel<<<grid, threads, 0, s>>>(static_cast<const bf16*>(state), static_cast<const bf16*>(qkv), sqb, sqt,
+                                              static_cast<const bf16*>(w), static_cast<bf16*>(ext),
+                                              static_cast<bf16*>(q), static_cast<bf16*>(k), static_cast<bf16*>(v), T,
+                                              taps, K, C, key_dim, value_dim, dk, dv, rep);
+    return launch_status();
+}
+
+}  // namespace gdn

@@ -1,0 +1,62 @@
+// Internal launcher declarations shared by the kernel files and the C ABI layer.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace gdn {
+
+struct RecurrentArgs {
+    const void* q;
+    const void* k;
+    const void* v;
+    int qkv_dtype;
+    const float* g;
+    const void* beta;
+    int beta_dtype;
+    const float* state_in;
+    float* state_out;
+    float* snapshots;
+    void* o;
+    const int64_t* steps;
+    const int32_t* cu_seqlens;
+    int64_t rows;    // batch rows, or sequences when cu_seqlens is set
+    int64_t T;       // token extent of the [B, T, ...] tensors (total tokens when packed)
+    int H, HV;
+    int64_t qsb, qst, qsh, ksb, kst, ksh, vsb, vst, vsh;
+    float scale;
+};
+int launch_recurrent(const RecurrentArgs& a, cudaStream_t s);
+
+int launch_snapshot_commit(float* state, const float* snapshots, const int64_t* accepted, int64_t B, int64_t T,
+                           int64_t HV, cudaStream_t s);
+
+struct DecodeLayerArgs {
+    const void* qkv;
+    int64_t qkv_sb;
+    void* conv_state;
+    const void* conv_w;
+    const float* g;
+    const void* beta;
+    float* state;
+    const void* z;
+    const void* norm_w;
+    void* out;
+    int64_t B;
+    int H, HV, taps, K;
+    float scale, eps;
+};
+int launch_decode_layer(const DecodeLayerArgs& a, cudaStream_t s);
+
+int launch_conv1d_silu(const void* x, int64_t sxb, int64_t sxt, const void* w, void* y, const int32_t* cu, int64_t B,
+                       int64_t T, int64_t C, int K, cudaStream_t s);
+int launch_conv1d_silu_step(const void* x, int64_t sxb, void* state, const void* w, void* y, int64_t B, int64_t C,
+                            int taps, int K, cudaStream_t s);
+int launch_conv_state_shift(const void* x, int64_t sxb, void* state, int64_t B, int64_t C, int taps, cudaStream_t s);
+int launch_conv_step(const void* state, const void* qkv, int64_t sqb, int64_t sqt, const void* w, void* ext, void* q,
+                     void* k, void* v, int64_t B, int64_t T, int taps, int K, int64_t key_dim, int64_t value_dim, int dk,
+                     int dv, cudaStream_t s);
+int launch_gated_rmsnorm(const void* x, const void* z, const void* w, void* y, int64_t rows, int dim, float eps,
+                         cudaStream_t s);
+
+}  // namespace gdn

@@ -1,0 +1,6 @@
+// Single translation unit of libgdn_b200.so: the device error word and every kernel
+// live in one module, so no relocatable device code or device link step is needed.
+#include "capi.cu"
+#include "recurrent.cu"
+#include "conv.cu"
+#include "norm.cu"

@@ -1,0 +1,200 @@
+"""Gated delta rule operators with the reference's call signatures.
+
+Each function mirrors one dispatcher of ``model/model.py`` (PostHog/jeeves) and runs on
+the CUDA kernels of ``libgdn_b200.so``. Inputs must be CUDA tensors: there is no CPU or
+eager fallback, and a missing library raises. Shapes: q, k ``[B, T, H, 128]`` (H key
+heads; H may be smaller than HV, value head hv then reads key head hv // (HV // H), the
+repeat-interleave mapping of ``model/model.py:487-490``), v ``[B, T, HV, 128]``, g
+``[B, T, HV]`` (log decay), beta ``[B, T, HV]``, states ``[B, HV, 128, 128]`` fp32.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+HEAD_DIM = 128
+_DTYPES = {torch.bfloat16: _lib.BF16, torch.float32: _lib.F32}
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _require_cuda(what: str, *tensors: torch.Tensor | None) -> None:
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise ValueError(f"{what}: expected CUDA tensors, got a tensor on {t.device}")
+
+
+def _heads_last_contiguous(x: torch.Tensor) -> torch.Tensor:
+    return x if x.stride(-1) == 1 else x.contiguous()
+
+
+def _check_qkv(what: str, q, k, v):
+    if k.dim() != 4 or v.dim() != 4:
+        raise ValueError(f"{what}: expected k [B, T, H, D] and v [B, T, HV, D], got {tuple(k.shape)} and {tuple(v.shape)}")
+    B, T, H, Dk = k.shape
+    HV, Dv = v.shape[2], v.shape[3]
+    if v.shape[:2] != (B, T) or (q is not None and q.shape != k.shape):
+        raise ValueError(f"{what}: q {None if q is None else tuple(q.shape)}, k {tuple(k.shape)} and v {tuple(v.shape)} "
+                         f"do not agree")
+    if HV % H:
+        raise ValueError(f"{what}: {HV} value heads are not a multiple of {H} key heads")
+    if Dk != HEAD_DIM or Dv != HEAD_DIM:
+        raise ValueError(f"{what}: head dims must be {HEAD_DIM}, got {Dk} and {Dv}")
+    dtypes = {t.dtype for t in (q, k, v) if t is not None}
+    if len(dtypes) != 1 or next(iter(dtypes)) not in _DTYPES:
+        raise ValueError(f"{what}: q, k, v must all be bfloat16 or all float32, got {sorted(map(str, dtypes))}")
+    return B, T, H, HV
+
+
+def _gates(what: str, g, beta, B, T, HV):
+    if g.shape != (B, T, HV) or beta.shape != (B, T, HV):
+        raise ValueError(f"{what}: g and beta must be {(B, T, HV)}, got {tuple(g.shape)} and {tuple(beta.shape)}")
+    g = g.to(torch.float32).contiguous()
+    if beta.dtype not in _DTYPES:
+        beta = beta.to(torch.float32)
+    return g, beta.contiguous()
+
+
+def _state_arg(what: str, state, rows, HV, *, name="initial_state"):
+    if state is None:
+        return None
+    if state.shape != (rows, HV, HEAD_DIM, HEAD_DIM):
+        raise ValueError(f"{what}: {name} must be {(rows, HV, HEAD_DIM, HEAD_DIM)}, got {tuple(state.shape)}")
+    return state.to(torch.float32).contiguous()
+
+
+def _recurrent(what, q, k, v, g, beta, *, state_in=None, state_out=None, snapshots=None, o=None, steps=None,
+               cu_seqlens=None, rows=None, scale=None):
+    B, T = k.shape[:2]
+    H, HV = k.shape[2], v.shape[2]
+    q = None if q is None else _heads_last_contiguous(q)
+    k, v = _heads_last_contiguous(k), _heads_last_contiguous(v)
+    if scale is None:
+        scale = HEAD_DIM ** -0.5
+    qs = (0, 0, 0) if q is None else (q.stride(0), q.stride(1), q.stride(2))
+    status = _lib.load().gdn_recurrent(
+        _ptr(q), _ptr(k), _ptr(v), _DTYPES[k.dtype], _ptr(g), _ptr(beta), _DTYPES[beta.dtype],
+        _ptr(state_in), _ptr(state_out), _ptr(snapshots), _ptr(o), _ptr(steps), _ptr(cu_seqlens),
+        B if rows is None else rows, T, H, HV, HEAD_DIM, HEAD_DIM,
+        *qs, k.stride(0), k.stride(1), k.stride(2), v.stride(0), v.stride(1), v.stride(2),
+        float(scale), _stream())
+    _lib.check(status, what)
+
+
+def _cu_seqlens_arg(what, cu_seqlens, B):
+    if cu_seqlens is None:
+        return None, B
+    if B != 1:
+        raise ValueError(f"{what}: with cu_seqlens the inputs are packed into a batch of 1, got batch {B}")
+    if cu_seqlens.dim() != 1 or cu_seqlens.numel() < 1 or cu_seqlens.dtype not in (torch.int32, torch.int64):
+        raise ValueError(f"{what}: cu_seqlens must be a 1-D int32/int64 tensor, got {cu_seqlens.dtype} {tuple(cu_seqlens.shape)}")
+    return cu_seqlens.to(device="cuda", dtype=torch.int32).contiguous(), cu_seqlens.numel() - 1
+
+
+def gated_delta_rule_step(q, k, v, g, beta, initial_state=None, output_final_state=True, scale=None, cu_seqlens=None):
+    """Recurrent gated delta rule over T tokens; returns ``(o, final_state or None)``.
+
+    Replaces ``gated_delta_rule_step`` (``model/model.py:297-302``): the verify outputs of
+    ``inference/engine.py:250-252`` and the decode step of the non-static cache path.
+    """
+    what = "gated_delta_rule_step"
+    _require_cuda(what, q, k, v, g, beta, initial_state, cu_seqlens)
+    B, T, H, HV = _check_qkv(what, q, k, v)
+    g, beta = _gates(what, g, beta, B, T, HV)
+    cu, rows = _cu_seqlens_arg(what, cu_seqlens, B)
+    h0 = _state_arg(what, initial_state, rows, HV)
+    o = torch.empty(B, T, HV, HEAD_DIM, dtype=q.dtype, device=q.device)
+    final = torch.empty(rows, HV, HEAD_DIM, HEAD_DIM, dtype=torch.float32, device=q.device) if output_final_state else None
+    _recurrent(what, q, k, v, g, beta, state_in=h0, state_out=final, o=o, cu_seqlens=cu, rows=rows, scale=scale)
+    return o, final
+
+
+def gated_delta_rule_chunk(q, k, v, g, beta, initial_state=None, output_final_state=False, scale=None, cu_seqlens=None):
+    """Chunked prefill; returns ``(o, final_state or None)``.
+
+    Replaces ``gated_delta_rule_chunk`` (``model/model.py:289-294``). ``cu_seqlens`` (int32 or
+    int64, ``[N + 1]``) packs N sequences into a batch of 1, as fla 0.5.x's
+    ``chunk_gated_delta_rule(..., cu_seqlens=...)``; ``initial_state`` and the final state
+    then have N rows.
+    """
+    what = "gated_delta_rule_chunk"
+    _require_cuda(what, q, k, v, g, beta, initial_state, cu_seqlens)
+    B, T, H, HV = _check_qkv(what, q, k, v)
+    g, beta = _gates(what, g, beta, B, T, HV)
+    cu, rows = _cu_seqlens_arg(what, cu_seqlens, B)
+    h0 = _state_arg(what, initial_state, rows, HV)
+    o = torch.empty(B, T, HV, HEAD_DIM, dtype=q.dtype, device=q.device)
+    final = torch.empty(rows, HV, HEAD_DIM, HEAD_DIM, dtype=torch.float32, device=q.device) if output_final_state else None
+    _recurrent(what, q, k, v, g, beta, state_in=h0, state_out=final, o=o, cu_seqlens=cu, rows=rows, scale=scale)
+    return o, final
+
+
+def _check_state_inplace(what, state, B, HV):
+    if state.dtype != torch.float32 or not state.is_contiguous() or state.shape != (B, HV, HEAD_DIM, HEAD_DIM):
+        raise ValueError(f"state: expected a contiguous float32 tensor of shape {(B, HV, HEAD_DIM, HEAD_DIM)}, "
+                         f"got {state.dtype} {tuple(state.shape)}")
+
+
+def gated_delta_rule_advance_inplace(k, v, g, beta, state, steps) -> None:
+    """Advance ``state[b]`` by ``clamp(steps[b], 0, T)`` tokens in place, without outputs.
+
+    Replaces ``gated_delta_rule_advance_inplace`` (``model/model.py:305-311``,
+    ``model/fla_inplace.py:63-74``); same errors (ValueError) for a bad state or steps.
+    """
+    what = "gated_delta_rule_advance_inplace"
+    _require_cuda(what, k, v, g, beta, state, steps)
+    B, T, H, HV = _check_qkv(what, None, k, v)
+    _check_state_inplace(what, state, B, HV)
+    if steps.shape != (B,) or steps.dtype not in (torch.int32, torch.int64):
+        raise ValueError(f"steps: expected {B} integers, got {steps.dtype} {tuple(steps.shape)}")
+    g, beta = _gates(what, g, beta, B, T, HV)
+    _recurrent(what, None, k, v, g, beta, state_in=state, state_out=state, steps=steps.to(torch.int64).contiguous())
+
+
+def gated_delta_rule_verify(q, k, v, g, beta, state, snapshots=None, scale=None):
+    """Score T drafted tokens; returns ``(o, snapshots)`` with ``snapshots[b, t]`` the state after token t.
+
+    ``state`` is read, not written. After acceptance, ``gated_delta_rule_rollback`` makes
+    ``snapshots[b, accepted[b] - 1]`` the live state (the rollback of
+    ``inference/engine.py:471-472`` without recomputing the accepted tokens).
+    """
+    what = "gated_delta_rule_verify"
+    _require_cuda(what, q, k, v, g, beta, state, snapshots)
+    B, T, H, HV = _check_qkv(what, q, k, v)
+    g, beta = _gates(what, g, beta, B, T, HV)
+    h0 = _state_arg(what, state, B, HV, name="state")
+    shape = (B, T, HV, HEAD_DIM, HEAD_DIM)
+    if snapshots is None:
+        snapshots = torch.empty(shape, dtype=torch.float32, device=q.device)
+    elif snapshots.shape != shape or snapshots.dtype != torch.float32 or not snapshots.is_contiguous():
+        raise ValueError(f"snapshots: expected a contiguous float32 tensor of shape {shape}, got {snapshots.dtype} "
+                         f"{tuple(snapshots.shape)}")
+    o = torch.empty(B, T, HV, HEAD_DIM, dtype=q.dtype, device=q.device)
+    _recurrent(what, q, k, v, g, beta, state_in=h0, snapshots=snapshots, o=o, scale=scale)
+    return o, snapshots
+
+
+def gated_delta_rule_rollback(state, snapshots, accepted) -> None:
+    """``state[b] <- snapshots[b, accepted[b] - 1]`` for rows with ``accepted[b] >= 1`` (clamped to T)."""
+    what = "gated_delta_rule_rollback"
+    _require_cuda(what, state, snapshots, accepted)
+    if snapshots.dim() != 5:
+        raise ValueError(f"snapshots: expected [B, T, HV, 128, 128], got {tuple(snapshots.shape)}")
+    B, T, HV = snapshots.shape[:3]
+    _check_state_inplace(what, state, B, HV)
+    if snapshots.dtype != torch.float32 or not snapshots.is_contiguous():
+        raise ValueError("snapshots: expected a contiguous float32 tensor")
+    if accepted.shape != (B,) or accepted.dtype not in (torch.int32, torch.int64):
+        raise ValueError(f"accepted: expected {B} integers, got {accepted.dtype} {tuple(accepted.shape)}")
+    status = _lib.load().gdn_snapshot_commit(state.data_ptr(), snapshots.data_ptr(),
+                                             accepted.to(torch.int64).contiguous().data_ptr(), B, T, HV, HEAD_DIM,
+                                             HEAD_DIM, _stream())
+    _lib.check(status, what)

@@ -1,0 +1,47 @@
+"""Fused decode step of one gated-delta layer (CUDA only).
+
+``decode_layer_step`` does, for one new token per row, what the StaticCache decode branch
+of ``GatedDeltaNet.forward`` (``model/model.py:465-467``, ``:496-499``, ``:516``) does
+between the input projections and ``out_proj``: conv step + SiLU, q/k L2 norm, gated
+delta rule step on the state in place, and the output-gated RMSNorm.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from .gated_delta import HEAD_DIM, _require_cuda, _stream
+
+
+def decode_layer_step(qkv, conv_state, conv_weight, g, beta, state, z, norm_weight, key_heads: int,
+                      eps: float = 1e-6, scale: float | None = None) -> torch.Tensor:
+    """qkv ``[B, C]`` pre-conv bf16 (q | k | v channels); conv_state ``[B, C, taps]`` and state
+    ``[B, HV, 128, 128]`` are updated in place; g ``[B, HV]`` fp32, beta ``[B, HV]`` bf16, z
+    ``[B, HV, 128]``; returns the normed output ``[B, HV, 128]`` bf16."""
+    what = "decode_layer_step"
+    _require_cuda(what, qkv, conv_state, conv_weight, g, beta, state, z, norm_weight)
+    B, C = qkv.shape
+    HV = state.shape[1]
+    if C != 2 * key_heads * HEAD_DIM + HV * HEAD_DIM:
+        raise ValueError(f"qkv: expected {2 * key_heads * HEAD_DIM + HV * HEAD_DIM} channels, got {C}")
+    taps = conv_state.shape[-1]
+    w = conv_weight.reshape(C, -1).contiguous()
+    if conv_state.shape != (B, C, taps) or not conv_state.is_contiguous() or conv_state.dtype != torch.bfloat16:
+        raise ValueError(f"conv_state: expected a contiguous bfloat16 tensor of shape {(B, C, taps)}, got "
+                         f"{conv_state.dtype} {tuple(conv_state.shape)}")
+    if state.dtype != torch.float32 or not state.is_contiguous() or state.shape != (B, HV, HEAD_DIM, HEAD_DIM):
+        raise ValueError(f"state: expected a contiguous float32 tensor of shape {(B, HV, HEAD_DIM, HEAD_DIM)}, got "
+                         f"{state.dtype} {tuple(state.shape)}")
+    if qkv.stride(-1) != 1:
+        qkv = qkv.contiguous()
+    g = g.reshape(B, HV).to(torch.float32).contiguous()
+    beta = beta.reshape(B, HV).to(torch.bfloat16).contiguous()
+    z = z.reshape(B, HV, HEAD_DIM).contiguous()
+    out = torch.empty(B, HV, HEAD_DIM, dtype=torch.bfloat16, device=qkv.device)
+    status = _lib.load().gdn_decode_layer(
+        qkv.data_ptr(), qkv.stride(0), conv_state.data_ptr(), w.data_ptr(), g.data_ptr(), beta.data_ptr(),
+        state.data_ptr(), z.data_ptr(), norm_weight.contiguous().data_ptr(), out.data_ptr(), B, key_heads, HV,
+        HEAD_DIM, HEAD_DIM, taps, w.shape[1], float(HEAD_DIM ** -0.5 if scale is None else scale), float(eps), _stream())
+    _lib.check(status, what)
+    return out

@@ -1,0 +1,77 @@
+"""CPU checks of the C ABI: the library loads, exports every declared entry point, and
+rejects bad arguments before touching a GPU."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from jeeves_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "gdn_b200.h")
+
+
+def declared():
+    text = open(HEADER).read()
+    return re.findall(r"GDN_API\s+[\w\s\*]+?\b(gdn_\w+)\s*\(", text)
+
+
+def test_header_declares_entry_points():
+    names = declared()
+    assert "gdn_recurrent" in names and "gdn_conv_step" in names
+    assert len(names) == len(set(names))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    for name in declared():
+        assert hasattr(lib, name), name
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+
+
+def test_binding_covers_exactly_the_header():
+    assert set(_lib.SIGNATURES) == set(declared())
+
+
+def test_status_strings_and_version():
+    assert _lib.status_text(0) == "ok"
+    assert "aligned" in _lib.status_text(_lib.ERR_ALIGN)
+    assert _lib.load().gdn_abi_version() >= 1
+
+
+def _recurrent(lib, **over):
+    args = dict(q=None, k=16, v=16, qkv_dtype=_lib.BF16, g=16, beta=16, beta_dtype=_lib.BF16, state_in=None,
+                state_out=None, snapshots=None, o=None, steps=None, cu=None, B=1, T=1, H=1, HV=1, Dk=128, Dv=128,
+                strides=(128, 128, 128) * 3, scale=0.0884, stream=None)
+    args.update(over)
+    return lib.gdn_recurrent(args["q"], args["k"], args["v"], args["qkv_dtype"], args["g"], args["beta"],
+                             args["beta_dtype"], args["state_in"], args["state_out"], args["snapshots"], args["o"],
+                             args["steps"], args["cu"], args["B"], args["T"], args["H"], args["HV"], args["Dk"],
+                             args["Dv"], *args["strides"], args["scale"], args["stream"])
+
+
+def test_argument_checks_run_before_any_launch():
+    lib = _lib.load()
+    assert _recurrent(lib, qkv_dtype=7) == _lib.ERR_DTYPE
+    assert _recurrent(lib, HV=3, H=2) == _lib.ERR_SHAPE
+    assert _recurrent(lib, Dk=64) == _lib.ERR_UNSUPPORTED
+    assert _recurrent(lib, k=None) == _lib.ERR_NULL
+    assert _recurrent(lib, k=18) == _lib.ERR_ALIGN
+    assert _recurrent(lib, strides=(128,) * 3 + (128, 129, 128) + (128,) * 3) == _lib.ERR_ALIGN
+    assert _recurrent(lib, o=16, q=None) == _lib.ERR_NULL
+    assert _recurrent(lib, steps=16, o=16, q=16) == _lib.ERR_SHAPE
+    assert _recurrent(lib, B=0) == _lib.OK  # empty batch: nothing to launch
+    assert lib.gdn_gated_rmsnorm(16, 16, 16, 16, 4, 64, 1e-6, None) == _lib.ERR_UNSUPPORTED
+    assert lib.gdn_conv1d_silu(16, 0, 0, 16, 16, None, 1, 4, 12, 4, None) == _lib.ERR_SHAPE
+    assert lib.gdn_conv_step(16, 16, 0, 0, 16, 16, 16, 16, 16, 1, 1, 4, 4, 33, 64, 16, 16, None) == _lib.ERR_SHAPE
+    assert lib.gdn_snapshot_commit(16, 16, None, 2, 5, 4, 128, 128, None) == _lib.ERR_NULL
+
+
+def test_status_mapping_to_exceptions():
+    with pytest.raises(ValueError):
+        _lib.check(_lib.ERR_SHAPE, "x")
+    with pytest.raises(RuntimeError):
+        _lib.check(_lib.ERR_LAUNCH, "x")
+    _lib.check(_lib.OK, "x")

@@ -1,0 +1,155 @@
+"""GPU parity of the recurrent-form kernel (decode, verify + snapshots, rollback, fp32 mode)
+against the CPU oracle and the reference's golden vectors."""
+
+import pytest
+import torch
+
+import jeeves_b200 as gdn
+import oracle
+from tests.helpers import cuda, gdn_inputs, maxabs, rel, same_bits
+
+pytestmark = pytest.mark.gpu
+
+# Tolerances: outputs in bf16 within the north-star max-abs 2e-2; the state is fp32 math on
+# CUDA cores, so it must match the fp32 oracle to 1e-5 relative (the fp32-mode bound).
+O_TOL, S_TOL = 2e-2, 1e-5
+
+
+def test_golden_recurrent_bf16(golden):
+    c = golden("recurrent_bf16")
+    q, k, v, g, beta, h0 = cuda(c["q"], c["k"], c["v"], c["g"], c["beta"], c["h0"])
+    o, S = gdn.gated_delta_rule_step(q, k, v, g, beta, initial_state=h0, output_final_state=True)
+    assert maxabs(o, c["o"]) < O_TOL and rel(S, c["S"]) < S_TOL
+    # bf16 outputs: nearly all elements round identically to the fp32 reference
+    assert (o.cpu() != c["o"]).float().mean().item() < 0.02
+
+
+def test_golden_config0_fp32_mode(golden):
+    c = golden("chunk_cfg0")
+    q, k, v, g, beta = cuda(c["q"], c["k"], c["v"], c["g"], c["beta"])
+    o, S = gdn.gated_delta_rule_chunk(q, k, v, g, beta, output_final_state=True)
+    assert o.dtype == torch.float32
+    assert maxabs(o, c["o"]) < 1e-5 and rel(S, c["S"]) < 1e-5
+
+
+@pytest.mark.parametrize("B,T,H,HV", [(1, 1, 2, 4), (4, 1, 16, 32), (3, 5, 4, 8), (2, 7, 2, 2), (64, 1, 16, 32)])
+def test_step_matches_oracle(B, T, H, HV):
+    q, k, v, g, beta, h0 = gdn_inputs(B * 100 + T, B, T, H, HV, normalise=False)
+    o_ref, S_ref = oracle.recurrent_gated_delta_rule(q, k, v, g, beta, initial_state=h0, output_final_state=True)
+    o, S = gdn.gated_delta_rule_step(*cuda(q, k, v, g, beta), initial_state=h0.cuda(), output_final_state=True)
+    assert maxabs(o, o_ref) < O_TOL and rel(S, S_ref) < S_TOL
+
+
+def test_step_inplace_matches_oracle():
+    q, k, v, g, beta, h0 = gdn_inputs(7, 8, 1, 16, 32, normalise=False)
+    o_ref, S_ref = oracle.recurrent_gated_delta_rule(q, k, v, g, beta, initial_state=h0, output_final_state=True)
+    state = h0.cuda()
+    o = gdn.fla_inplace.gated_delta_rule_step_inplace(*cuda(q, k, v, g, beta), state)
+    assert maxabs(o, o_ref) < O_TOL and rel(state, S_ref) < S_TOL
+
+
+def test_fp32_inputs_and_beta_dtypes():
+    q, k, v, g, beta, h0 = gdn_inputs(8, 2, 9, 2, 4, dtype=torch.float32)
+    o_ref, S_ref = oracle.recurrent_gated_delta_rule(q, k, v, g, beta, initial_state=h0, output_final_state=True)
+    o, S = gdn.gated_delta_rule_step(*cuda(q, k, v, g, beta), initial_state=h0.cuda())
+    assert maxabs(o, o_ref) < 1e-5 and rel(S, S_ref) < 1e-5
+
+
+def test_strided_inputs():
+    q, k, v, g, beta, h0 = gdn_inputs(9, 2, 6, 4, 8, normalise=False)
+    packed = torch.cat([q, k], dim=2).cuda()  # [B, T, 2H, D]: q and k are strided views
+    qv, kv = packed[:, :, :4], packed[:, :, 4:]
+    assert not qv.is_contiguous()
+    o_ref, S_ref = oracle.recurrent_gated_delta_rule(q, k, v, g, beta, initial_state=h0, output_final_state=True)
+    o, S = gdn.gated_delta_rule_step(qv, kv, *cuda(v, g, beta), initial_state=h0.cuda())
+    assert maxabs(o, o_ref) < O_TOL and rel(S, S_ref) < S_TOL
+
+
+def test_golden_advance(golden):
+    c = golden("advance")
+    k, v, g, beta, h0, steps = cuda(c["k"], c["v"], c["g"], c["beta"], c["h0"], c["steps"])
+    state = h0.clone()
+    gdn.gated_delta_rule_advance_inplace(k, v, g, beta, state, steps)
+    assert rel(state, c["S"]) < S_TOL
+    for b, s in enumerate(c["steps"].tolist()):
+        if s <= 0:
+            assert same_bits(state[b], h0[b])
+
+
+def test_advance_clamps_and_equals_prefix_run():
+    B, T = 4, 5
+    _, k, v, g, beta, h0 = gdn_inputs(10, B, T, 16, 32, normalise=False)
+    k, v, g, beta, h0 = cuda(k, v, g, beta, h0)
+    clamped, exact = h0.clone(), h0.clone()
+    gdn.gated_delta_rule_advance_inplace(k, v, g, beta, clamped, torch.tensor([-5, T + 9, 0, 3], device="cuda"))
+    gdn.gated_delta_rule_advance_inplace(k, v, g, beta, exact, torch.tensor([0, T, 0, 3], device="cuda", dtype=torch.int32))
+    assert same_bits(clamped, exact)
+    assert same_bits(clamped[0], h0[0]) and same_bits(clamped[2], h0[2])
+    # advancing j tokens equals running the first j tokens (same kernel, same arithmetic)
+    prefix, _ = None, None
+    _, S3 = gdn.gated_delta_rule_step(torch.zeros_like(k[3:4, :3]), k[3:4, :3], v[3:4, :3], g[3:4, :3], beta[3:4, :3],
+                                       initial_state=h0[3:4])
+    assert rel(clamped[3:4], S3) < 1e-6
+
+
+def test_advance_g_beta_zero_is_identity():
+    _, k, v, g, beta, h0 = gdn_inputs(11, 3, 7, 2, 4, normalise=False)
+    k, v, h0 = cuda(k, v, h0)
+    state = h0.clone()
+    gdn.gated_delta_rule_advance_inplace(k, v, torch.zeros(3, 7, 4, device="cuda"),
+                                         torch.zeros(3, 7, 4, device="cuda", dtype=torch.bfloat16), state,
+                                         torch.full((3,), 7, device="cuda"))
+    assert same_bits(state, h0)
+
+
+def test_verify_snapshots_and_rollback():
+    B, T, H, HV = 6, 5, 16, 32
+    q, k, v, g, beta, h0 = gdn_inputs(12, B, T, H, HV, normalise=False)
+    o_ref, snaps_ref = oracle.verify_with_snapshots(q, k, v, g, beta, h0)
+    qc, kc, vc, gc, bc, hc = cuda(q, k, v, g, beta, h0)
+    o, snaps = gdn.gated_delta_rule_verify(qc, kc, vc, gc, bc, hc)
+    assert maxabs(o, o_ref) < O_TOL and rel(snaps, snaps_ref) < S_TOL
+    assert same_bits(hc, h0.cuda())  # verify reads the state, never writes it
+    accepted = torch.tensor([1, 2, 3, 4, 5, 0], device="cuda")
+    rolled, advanced = hc.clone(), hc.clone()
+    gdn.gated_delta_rule_rollback(rolled, snaps, accepted)
+    gdn.gated_delta_rule_advance_inplace(kc, vc, gc, bc, advanced, accepted)
+    assert same_bits(rolled, advanced)
+    # verify outputs equal the plain recurrent outputs
+    o2, _ = gdn.gated_delta_rule_step(qc, kc, vc, gc, bc, initial_state=hc, output_final_state=False)
+    assert same_bits(o, o2)
+
+
+def test_resumed_equals_uninterrupted():
+    B, T = 2, 9
+    q, k, v, g, beta, h0 = cuda(*gdn_inputs(13, B, T, 2, 4, normalise=False))
+    o_full, S_full = gdn.gated_delta_rule_step(q, k, v, g, beta, initial_state=h0)
+    o_a, S_a = gdn.gated_delta_rule_step(q[:, :4], k[:, :4], v[:, :4], g[:, :4], beta[:, :4], initial_state=h0)
+    o_b, S_b = gdn.gated_delta_rule_step(q[:, 4:], k[:, 4:], v[:, 4:], g[:, 4:], beta[:, 4:], initial_state=S_a)
+    assert same_bits(torch.cat([o_a, o_b], 1), o_full) and same_bits(S_b, S_full)
+
+
+def test_varlen_recurrent_equals_per_sequence():
+    lens = [3, 0, 11, 6]
+    T = sum(lens)
+    q, k, v, g, beta, _ = gdn_inputs(14, 1, T, 2, 4, normalise=False)
+    h0 = torch.randn(len(lens), 4, 128, 128) * 0.02
+    cu = torch.tensor([0, 3, 3, 14, 20], dtype=torch.int32)
+    o, S = gdn.gated_delta_rule_step(*cuda(q, k, v, g, beta), initial_state=h0.cuda(), cu_seqlens=cu.cuda())
+    for i in range(len(lens)):
+        s, e = int(cu[i]), int(cu[i + 1])
+        o_r, S_r = oracle.recurrent_gated_delta_rule(q[:, s:e], k[:, s:e], v[:, s:e], g[:, s:e], beta[:, s:e],
+                                                     initial_state=h0[i:i + 1], output_final_state=True)
+        if e > s:
+            assert maxabs(o[:, s:e], o_r) < O_TOL
+        assert rel(S[i:i + 1], S_r) < S_TOL
+
+
+def test_errors_follow_reference_convention():
+    q, k, v, g, beta, h0 = cuda(*gdn_inputs(15, 2, 3, 2, 4))
+    with pytest.raises(ValueError):
+        gdn.gated_delta_rule_step(q.half(), k.half(), v.half(), g, beta)
+    with pytest.raises(ValueError, match="state"):
+        gdn.gated_delta_rule_advance_inplace(k, v, g, beta, h0.transpose(2, 3), torch.ones(2, device="cuda"))
+    with pytest.raises(ValueError, match="steps"):
+        gdn.gated_delta_rule_advance_inplace(k, v, g, beta, h0.clone(), torch.ones(2, device="cuda"))
