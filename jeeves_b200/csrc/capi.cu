@@ -137,7 +137,8 @@ int gdn_conv1d_silu_step(const void* x, int64_t x_stride_b, void* state, const v
 int gdn_conv_step(const void* state, const void* qkv, int64_t qkv_stride_b, int64_t qkv_stride_t, const void* w,
                   void* ext, void* q, void* k, void* v, int64_t batch, int64_t seqlen, int64_t taps, int64_t kernel_size,
                   int64_t key_dim, int64_t value_dim, int64_t head_dim_k, int64_t head_dim_v, void* stream) {
-    if (batch < 0 || seqlen < 0 || taps < 1 || taps > 8 || kernel_size < 1 || kernel_size > taps + 1) return GDN_ERR_SHAPE;
+    if (batch < 0 || seqlen < 0 || taps < 1 || taps > 8 || kernel_size < 1 || kernel_size > taps + 1 || kernel_size > 8)
+        return GDN_ERR_SHAPE;
     if (head_dim_k <= 0 || head_dim_v <= 0 || key_dim <= 0 || value_dim <= 0) return GDN_ERR_SHAPE;
     if (key_dim % head_dim_k || value_dim % head_dim_v) return GDN_ERR_SHAPE;
     const int64_t kh = key_dim / head_dim_k, vh = value_dim / head_dim_v;

@@ -89,14 +89,20 @@ def _recurrent(what, q, k, v, g, beta, *, state_in=None, state_out=None, snapsho
     _lib.check(status, what)
 
 
-def _cu_seqlens_arg(what, cu_seqlens, B):
+def _cu_seqlens_arg(what, cu_seqlens, B, T):
     if cu_seqlens is None:
         return None, B
     if B != 1:
         raise ValueError(f"{what}: with cu_seqlens the inputs are packed into a batch of 1, got batch {B}")
     if cu_seqlens.dim() != 1 or cu_seqlens.numel() < 1 or cu_seqlens.dtype not in (torch.int32, torch.int64):
         raise ValueError(f"{what}: cu_seqlens must be a 1-D int32/int64 tensor, got {cu_seqlens.dtype} {tuple(cu_seqlens.shape)}")
-    return cu_seqlens.to(device="cuda", dtype=torch.int32).contiguous(), cu_seqlens.numel() - 1
+    if not cu_seqlens.is_cuda:
+        # A host copy can be checked without a device sync: offsets must rise from 0 to T.
+        steps = cu_seqlens[1:] - cu_seqlens[:-1]
+        if int(cu_seqlens[0]) != 0 or bool((steps < 0).any()) or int(cu_seqlens[-1]) > T:
+            raise ValueError(f"{what}: cu_seqlens must rise from 0 to at most {T}, got {cu_seqlens.tolist()}")
+        return cu_seqlens.to(dtype=torch.int32).pin_memory().to("cuda", non_blocking=True), cu_seqlens.numel() - 1
+    return cu_seqlens.to(dtype=torch.int32).contiguous(), cu_seqlens.numel() - 1
 
 
 def gated_delta_rule_step(q, k, v, g, beta, initial_state=None, output_final_state=True, scale=None, cu_seqlens=None):
@@ -109,7 +115,7 @@ def gated_delta_rule_step(q, k, v, g, beta, initial_state=None, output_final_sta
     _require_cuda(what, q, k, v, g, beta, initial_state, cu_seqlens)
     B, T, H, HV = _check_qkv(what, q, k, v)
     g, beta = _gates(what, g, beta, B, T, HV)
-    cu, rows = _cu_seqlens_arg(what, cu_seqlens, B)
+    cu, rows = _cu_seqlens_arg(what, cu_seqlens, B, T)
     h0 = _state_arg(what, initial_state, rows, HV)
     o = torch.empty(B, T, HV, HEAD_DIM, dtype=q.dtype, device=q.device)
     final = torch.empty(rows, HV, HEAD_DIM, HEAD_DIM, dtype=torch.float32, device=q.device) if output_final_state else None
@@ -129,7 +135,7 @@ def gated_delta_rule_chunk(q, k, v, g, beta, initial_state=None, output_final_st
     _require_cuda(what, q, k, v, g, beta, initial_state, cu_seqlens)
     B, T, H, HV = _check_qkv(what, q, k, v)
     g, beta = _gates(what, g, beta, B, T, HV)
-    cu, rows = _cu_seqlens_arg(what, cu_seqlens, B)
+    cu, rows = _cu_seqlens_arg(what, cu_seqlens, B, T)
     h0 = _state_arg(what, initial_state, rows, HV)
     o = torch.empty(B, T, HV, HEAD_DIM, dtype=q.dtype, device=q.device)
     final = torch.empty(rows, HV, HEAD_DIM, HEAD_DIM, dtype=torch.float32, device=q.device) if output_final_state else None
