@@ -112,7 +112,7 @@ def gated_delta_rule_step(q, k, v, g, beta, initial_state=None, output_final_sta
     ``inference/engine.py:250-252`` and the decode step of the non-static cache path.
     """
     what = "gated_delta_rule_step"
-    _require_cuda(what, q, k, v, g, beta, initial_state, cu_seqlens)
+    _require_cuda(what, q, k, v, g, beta, initial_state)
     B, T, H, HV = _check_qkv(what, q, k, v)
     g, beta = _gates(what, g, beta, B, T, HV)
     cu, rows = _cu_seqlens_arg(what, cu_seqlens, B, T)
@@ -132,7 +132,7 @@ def gated_delta_rule_chunk(q, k, v, g, beta, initial_state=None, output_final_st
     then have N rows.
     """
     what = "gated_delta_rule_chunk"
-    _require_cuda(what, q, k, v, g, beta, initial_state, cu_seqlens)
+    _require_cuda(what, q, k, v, g, beta, initial_state)
     B, T, H, HV = _check_qkv(what, q, k, v)
     g, beta = _gates(what, g, beta, B, T, HV)
     cu, rows = _cu_seqlens_arg(what, cu_seqlens, B, T)
