@@ -55,6 +55,9 @@ __device__ __forceinline__ float warp_sum(float x) {
 // SiLU as the eager path evaluates it on bf16: x / (1 + exp(-x)) in fp32, IEEE division.
 __device__ __forceinline__ float silu_f32(float x) { return __fdiv_rn(x, 1.0f + expf(-x)); }
 
+// 1 / sqrt(x) with an IEEE square root and an IEEE division, as the CPU evaluates rsqrt.
+__device__ __forceinline__ float inv_sqrt_rn(float x) { return __fdiv_rn(1.0f, __fsqrt_rn(x)); }
+
 // Device-side error word written by bounded waits (one per device image of the library;
 // the library is built as a single translation unit, library.cu).
 __device__ int g_device_error = 0;

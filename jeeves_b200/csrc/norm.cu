@@ -19,7 +19,7 @@ __global__ void gated_rmsnorm_kernel(const bf16* __restrict__ x, const bf16* __r
     const float4 zv = load4(z + off);
     const float4 wv = load4(w + 4 * lane);
     const float sq = warp_sum(xv.x * xv.x + xv.y * xv.y + xv.z * xv.z + xv.w * xv.w);
-    const float inv = rsqrtf(sq * (1.0f / kHeadDim) + eps);
+    const float inv = inv_sqrt_rn(sq * (1.0f / kHeadDim) + eps);
     const float xs[4] = {xv.x, xv.y, xv.z, xv.w}, zs[4] = {zv.x, zv.y, zv.z, zv.w}, ws[4] = {wv.x, wv.y, wv.z, wv.w};
     float4 out;
     float* o = &out.x;

@@ -364,7 +364,7 @@ __global__ void __launch_bounds__(NT) decode_layer_kernel(const DecodeParams p) 
             o[i] = round_bf16(o[i]);
             sq += o[i] * o[i];
         }
-        const float inv = rsqrtf(warp_sum(sq) * (1.0f / kHeadDim) + p.eps);
+        const float inv = inv_sqrt_rn(warp_sum(sq) * (1.0f / kHeadDim) + p.eps);
         const float4 zz = load4(p.z + gi * kHeadDim + col);
         const float4 ww = load4(p.norm_w + col);
         const float zv[4] = {zz.x, zz.y, zz.z, zz.w}, wv[4] = {ww.x, ww.y, ww.z, ww.w};

@@ -39,3 +39,24 @@ def same_bits(x, y):
     if not torch.equal(nan, y.isnan()):
         return False
     return torch.equal(x.view(view)[~nan], y.view(view)[~nan])
+
+
+def bf16_ulps(x, y):
+    """Number of differing bf16 elements and the largest distance in units of the last place."""
+    x, y = x.detach().cpu().contiguous(), y.detach().cpu().contiguous()
+    assert x.dtype == y.dtype == torch.bfloat16 and x.shape == y.shape
+    a = x.view(torch.int16).to(torch.int32)
+    b = y.view(torch.int16).to(torch.int32)
+    # map sign-magnitude bit patterns to a monotonic integer line
+    a = torch.where(a < 0, -(a & 0x7FFF), a)
+    b = torch.where(b < 0, -(b & 0x7FFF), b)
+    d = (a - b).abs()
+    return int((d > 0).sum()), int(d.max()) if d.numel() else 0
+
+
+def assert_bf16_matches_cpu(gpu, cpu, max_frac=1e-6):
+    """GPU output against the CPU oracle: bitwise, except that SiLU's exp may differ in the
+    last fp32 bit between the CPU's vectorised exp and CUDA's expf, which can move a bf16
+    rounding by one ulp on rare elements."""
+    n, ulp = bf16_ulps(gpu, cpu)
+    assert ulp <= 1 and n <= max(1, int(max_frac * cpu.numel())), (n, ulp, cpu.numel())
