@@ -89,6 +89,26 @@ GDN_API int gdn_recurrent(const void* q, const void* k, const void* v, int qkv_d
                   float scale, void* stream);
 
 /*
+ * Chunked prefill on tcgen05 tensor cores (chunk 64, WY/UT form) with an fp32 state in
+ * TMEM. Replaces gated_delta_rule_chunk, model/model.py:289-294 (fla chunk_gated_delta_rule
+ * on CUDA; fp32 eager torch_chunk_gated_delta_rule :242-286). bf16 q, k: [B, T, H, Dk],
+ * v: [B, T, HV, Dv] with element strides for the b, t, h dims; g: [B, T, HV] fp32
+ * contiguous; beta: [B, T, HV] contiguous, bf16 or fp32; o: [B, T, HV, Dv] bf16 contiguous.
+ * initial_state / final_state: [N, HV, Dk, Dv] fp32 or NULL (zero start / not written).
+ * With cu_seqlens (int32, [batch + 1]) the tensors hold one packed row of `seqlen` tokens
+ * and `batch` is the number of sequences N (fla 0.5.x varlen convention); otherwise N =
+ * batch. q is L2-normalised and scaled by `scale`, k L2-normalised, in the kernel.
+ */
+GDN_API int gdn_chunk_prefill(const void* q, const void* k, const void* v, const float* g, const void* beta,
+                              int beta_dtype, const float* initial_state, float* final_state, void* o,
+                              const int32_t* cu_seqlens, int64_t batch, int64_t seqlen, int64_t key_heads,
+                              int64_t value_heads, int64_t head_dim_k, int64_t head_dim_v,
+                              int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h,
+                              int64_t k_stride_b, int64_t k_stride_t, int64_t k_stride_h,
+                              int64_t v_stride_b, int64_t v_stride_t, int64_t v_stride_h,
+                              float scale, void* stream);
+
+/*
  * Rollback by snapshot: for each row b with accepted[b] >= 1, copy snapshot
  * accepted[b]-1 (clamped to T) into state[b]; rows with accepted[b] <= 0 keep their state.
  * snapshots: [B, T, HV, Dk, Dv] fp32 from gdn_recurrent; state: [B, HV, Dk, Dv] fp32.

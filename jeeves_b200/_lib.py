@@ -29,6 +29,8 @@ SIGNATURES: dict[str, list] = {
     "gdn_recurrent": [_p, _p, _p, _i32, _p, _p, _i32, _p, _p, _p, _p, _p, _p,
                       _i64, _i64, _i64, _i64, _i64, _i64,
                       _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _p],
+    "gdn_chunk_prefill": [_p, _p, _p, _p, _p, _i32, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64,
+                          _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _p],
     "gdn_snapshot_commit": [_p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p],
     "gdn_conv1d_silu": [_p, _i64, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _p],
     "gdn_conv1d_silu_step": [_p, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _p],

@@ -100,6 +100,36 @@ int gdn_recurrent(const void* q, const void* k, const void* v, int qkv_dtype, co
     return launch_recurrent(a, as_stream(stream));
 }
 
+int gdn_chunk_prefill(const void* q, const void* k, const void* v, const float* g, const void* beta, int beta_dtype,
+                      const float* initial_state, float* final_state, void* o, const int32_t* cu_seqlens,
+                      int64_t batch, int64_t seqlen, int64_t key_heads, int64_t value_heads, int64_t head_dim_k,
+                      int64_t head_dim_v, int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h,
+                      int64_t k_stride_b, int64_t k_stride_t, int64_t k_stride_h, int64_t v_stride_b,
+                      int64_t v_stride_t, int64_t v_stride_h, float scale, void* stream) {
+    if (!known_dtype(beta_dtype)) return GDN_ERR_DTYPE;
+    if (batch < 0 || seqlen < 0 || key_heads <= 0 || value_heads <= 0 || value_heads % key_heads) return GDN_ERR_SHAPE;
+    if (batch > 65535 || value_heads > 512) return GDN_ERR_SHAPE;
+    if (seqlen > INT32_MAX - 64) return GDN_ERR_SHAPE;  // TMA coordinates are 32-bit
+    if (head_dim_k != kHeadDim || head_dim_v != kHeadDim) return GDN_ERR_UNSUPPORTED;
+    if (batch == 0) return GDN_OK;
+    if (!q || !k || !v || !g || !beta || !o) return GDN_ERR_NULL;
+    if (cu_seqlens == nullptr && seqlen == 0) return GDN_OK;
+    if (!rows_aligned(q, 2, q_stride_b, q_stride_t, q_stride_h) || !rows_aligned(k, 2, k_stride_b, k_stride_t, k_stride_h) ||
+        !rows_aligned(v, 2, v_stride_b, v_stride_t, v_stride_h) || !aligned16(o))
+        return GDN_ERR_ALIGN;
+    if ((initial_state && !aligned16(initial_state)) || (final_state && !aligned16(final_state))) return GDN_ERR_ALIGN;
+    ChunkArgs a;
+    a.q = q; a.k = k; a.v = v; a.g = g; a.beta = beta; a.beta_dtype = beta_dtype;
+    a.h0 = initial_state; a.ht = final_state; a.o = o; a.cu_seqlens = cu_seqlens;
+    a.B = cu_seqlens ? 1 : batch; a.T = seqlen; a.nseq = batch;
+    a.H = (int)key_heads; a.HV = (int)value_heads;
+    a.qsb = q_stride_b; a.qst = q_stride_t; a.qsh = q_stride_h;
+    a.ksb = k_stride_b; a.kst = k_stride_t; a.ksh = k_stride_h;
+    a.vsb = v_stride_b; a.vst = v_stride_t; a.vsh = v_stride_h;
+    a.scale = scale;
+    return launch_chunk(a, as_stream(stream));
+}
+
 int gdn_snapshot_commit(float* state, const float* snapshots, const int64_t* accepted, int64_t batch, int64_t seqlen,
                         int64_t value_heads, int64_t head_dim_k, int64_t head_dim_v, void* stream) {
     if (batch < 0 || seqlen <= 0 || value_heads <= 0 || batch > 65535 || value_heads > 65535) return GDN_ERR_SHAPE;

@@ -28,6 +28,24 @@ struct RecurrentArgs {
 };
 int launch_recurrent(const RecurrentArgs& a, cudaStream_t s);
 
+struct ChunkArgs {
+    const void* q;
+    const void* k;
+    const void* v;
+    const float* g;
+    const void* beta;
+    int beta_dtype;
+    const float* h0;
+    float* ht;
+    void* o;
+    const int32_t* cu_seqlens;
+    int64_t B, T, nseq;
+    int H, HV;
+    int64_t qsb, qst, qsh, ksb, kst, ksh, vsb, vst, vsh;
+    float scale;
+};
+int launch_chunk(const ChunkArgs& a, cudaStream_t s);
+
 int launch_snapshot_commit(float* state, const float* snapshots, const int64_t* accepted, int64_t B, int64_t T,
                            int64_t HV, cudaStream_t s);
 

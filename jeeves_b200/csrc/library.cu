@@ -4,3 +4,4 @@
 #include "recurrent.cu"
 #include "conv.cu"
 #include "norm.cu"
+#include "chunk.cu"

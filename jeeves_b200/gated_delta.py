@@ -129,7 +129,8 @@ def gated_delta_rule_chunk(q, k, v, g, beta, initial_state=None, output_final_st
     Replaces ``gated_delta_rule_chunk`` (``model/model.py:289-294``). ``cu_seqlens`` (int32 or
     int64, ``[N + 1]``) packs N sequences into a batch of 1, as fla 0.5.x's
     ``chunk_gated_delta_rule(..., cu_seqlens=...)``; ``initial_state`` and the final state
-    then have N rows.
+    then have N rows. bf16 inputs run the tcgen05 chunk kernel; fp32 inputs (the fp32 mode
+    of the parity bound) run the fp32 recurrent kernel on CUDA cores.
     """
     what = "gated_delta_rule_chunk"
     _require_cuda(what, q, k, v, g, beta, initial_state)
@@ -139,7 +140,20 @@ def gated_delta_rule_chunk(q, k, v, g, beta, initial_state=None, output_final_st
     h0 = _state_arg(what, initial_state, rows, HV)
     o = torch.empty(B, T, HV, HEAD_DIM, dtype=q.dtype, device=q.device)
     final = torch.empty(rows, HV, HEAD_DIM, HEAD_DIM, dtype=torch.float32, device=q.device) if output_final_state else None
-    _recurrent(what, q, k, v, g, beta, state_in=h0, state_out=final, o=o, cu_seqlens=cu, rows=rows, scale=scale)
+    if q.dtype == torch.float32:
+        _recurrent(what, q, k, v, g, beta, state_in=h0, state_out=final, o=o, cu_seqlens=cu, rows=rows, scale=scale)
+        return o, final
+    if T == 0:
+        if final is not None:
+            final.copy_(h0) if h0 is not None else final.zero_()
+        return o, final
+    q, k, v = (_heads_last_contiguous(t) for t in (q, k, v))
+    status = _lib.load().gdn_chunk_prefill(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(), beta.data_ptr(), _DTYPES[beta.dtype], _ptr(h0),
+        _ptr(final), o.data_ptr(), _ptr(cu), rows, T, H, HV, HEAD_DIM, HEAD_DIM,
+        q.stride(0), q.stride(1), q.stride(2), k.stride(0), k.stride(1), k.stride(2), v.stride(0), v.stride(1),
+        v.stride(2), float(HEAD_DIM ** -0.5 if scale is None else scale), _stream())
+    _lib.check(status, what)
     return o, final
 
 
