@@ -332,10 +332,12 @@ def bench_decode(gdn, args, device, rank, world, rank_sync, reduce_max, hbm_peak
     g = [(-torch.exp(torch.randn(B, HV, device=device) * 0.5 - 3.0)) for _ in range(layers)]
     beta = [torch.sigmoid(torch.randn(B, HV, device=device)).to(torch.bfloat16) for _ in range(layers)]
     z = [torch.randn(B, HV, D, device=device).to(torch.bfloat16) for _ in range(layers)]
+    workspace = torch.empty(B, C_QKV, dtype=torch.bfloat16, device=device)
 
     def step(i):
         for l in range(layers):
-            gdn.decode_layer_step(qkv[l], conv_states[l], w[l], g[l], beta[l], states[l], z[l], nw, H)
+            gdn.decode_layer_step(qkv[l], conv_states[l], w[l], g[l], beta[l], states[l], z[l], nw, H,
+                                  workspace=workspace)
 
     ms = reduce_max(timed(step, args.steps, args.warmup, rank_sync)) / args.steps
     unit_bytes = 2 * HV * D * D * 4 + 2 * C_QKV * taps * 2 + C_QKV * 2 + HV * 6 + 2 * HV * D * 2
@@ -346,7 +348,7 @@ def bench_decode(gdn, args, device, rank, world, rank_sync, reduce_max, hbm_peak
             "value": round(world * B / (ms / 1e3), 1), "unit": "tokens/s (sequences x steps)", "ms_per_step": round(ms, 4),
             "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(ach / hbm_peak, 4), "algorithmic_bytes_per_unit": unit_bytes},
-            "gpu_launches": 2 * layers * args.steps}
+            "gpu_launches": 3 * layers * args.steps}
 
 
 def bench_verify(gdn, args, device, rank, world, rank_sync, reduce_max, hbm_peak, layers=24, B_total=128, T=5):

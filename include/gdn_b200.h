@@ -133,8 +133,9 @@ GDN_API int gdn_conv1d_silu(const void* x, int64_t x_stride_b, int64_t x_stride_
 
 /*
  * One decode token of the conv (replaces causal_conv1d_step, model/model.py:207-214).
- * x: [B, C] bf16 (row stride x_stride_b); state: [B, C, taps] bf16 updated in place to
- * the last `taps` inputs; w: [C, K] bf16 with K <= taps + 1; y: [B, C] bf16.
+ * x: [B, C] bf16 (row stride x_stride_b), C a multiple of 8; state: [B, C, taps] bf16,
+ * 2 <= taps <= 4, updated in place to the last `taps` inputs; w: [C, K] bf16 with
+ * K <= taps + 1; y: [B, C] bf16.
  * Rounds like the eager path: bf16 products, fp32 sum, bf16, silu, bf16.
  */
 GDN_API int gdn_conv1d_silu_step(const void* x, int64_t x_stride_b, void* state, const void* w, void* y,
@@ -163,18 +164,21 @@ GDN_API int gdn_gated_rmsnorm(const void* x, const void* z, const void* w, void*
                       int64_t rows, int64_t dim, float eps, void* stream);
 
 /*
- * Fused decode layer for one new token per row: conv step (+SiLU) over the pre-conv
- * qkv, q/k L2 norm, gated delta rule step with the state updated in place, and the
- * output-gated RMSNorm. Replaces the StaticCache decode branch of
- * GatedDeltaNet.forward (model/model.py:465-467, :496-499, :516).
+ * Decode layer for one new token per row: conv step (+SiLU) over the pre-conv qkv, q/k L2
+ * norm, gated delta rule step with the state updated in place, and the output-gated
+ * RMSNorm. Replaces the StaticCache decode branch of GatedDeltaNet.forward
+ * (model/model.py:465-467, :496-499, :516). Three launches on `stream`: the conv over every
+ * channel once (writing the post-conv activations to `workspace` and rolling conv_state
+ * forward), the recurrent step on 32-column state slices, the gated norm in place on `out`.
  * qkv: [B, C] bf16 (row stride qkv_stride_b) with C = 2*H*Dk + HV*Dv laid out q | k | v;
- * conv_state: [B, C, taps] bf16 (in place); conv_w: [C, K] bf16; g: [B, HV] fp32;
- * beta: [B, HV] bf16; state: [B, HV, Dk, Dv] fp32 (in place); z: [B, HV, Dv] bf16;
- * norm_w: [Dv] bf16; out: [B, HV, Dv] bf16.
+ * conv_state: [B, C, taps] bf16, 2 <= taps <= 4 (in place); conv_w: [C, K] bf16, K <= taps+1;
+ * g: [B, HV] fp32; beta: [B, HV] bf16; state: [B, HV, Dk, Dv] fp32 (in place);
+ * z: [B, HV, Dv] bf16; norm_w: [Dv] bf16; out: [B, HV, Dv] bf16;
+ * workspace: [B, C] bf16 scratch owned by the caller (the library never allocates).
  */
 GDN_API int gdn_decode_layer(const void* qkv, int64_t qkv_stride_b, void* conv_state, const void* conv_w,
                      const float* g, const void* beta, float* state, const void* z,
-                     const void* norm_w, void* out,
+                     const void* norm_w, void* out, void* workspace,
                      int64_t batch, int64_t key_heads, int64_t value_heads,
                      int64_t head_dim_k, int64_t head_dim_v, int64_t taps, int64_t kernel_size,
                      float scale, float eps, void* stream);

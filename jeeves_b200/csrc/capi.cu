@@ -156,10 +156,12 @@ int gdn_conv1d_silu(const void* x, int64_t x_stride_b, int64_t x_stride_t, const
 
 int gdn_conv1d_silu_step(const void* x, int64_t x_stride_b, void* state, const void* w, void* y, int64_t batch,
                          int64_t channels, int64_t taps, int64_t kernel_size, void* stream) {
-    if (batch < 0 || channels <= 0 || taps < 1 || taps > 8 || kernel_size < 1 || kernel_size > taps + 1)
+    if (batch < 0 || channels <= 0 || channels % 8 || taps < 1 || kernel_size < 1 || kernel_size > taps + 1)
         return GDN_ERR_SHAPE;
+    if (taps < 2 || taps > 4 || kernel_size < 2) return GDN_ERR_UNSUPPORTED;
     if (batch == 0) return GDN_OK;
     if (!x || !state || !w || !y) return GDN_ERR_NULL;
+    if (!rows_aligned(x, 2, x_stride_b, 0, 0) || !aligned16(state) || !aligned16(y) || !aligned16(w)) return GDN_ERR_ALIGN;
     return launch_conv1d_silu_step(x, x_stride_b, state, w, y, batch, channels, (int)taps, (int)kernel_size,
                                    as_stream(stream));
 }
@@ -194,20 +196,24 @@ int gdn_gated_rmsnorm(const void* x, const void* z, const void* w, void* y, int6
 }
 
 int gdn_decode_layer(const void* qkv, int64_t qkv_stride_b, void* conv_state, const void* conv_w, const float* g,
-                     const void* beta, float* state, const void* z, const void* norm_w, void* out, int64_t batch,
-                     int64_t key_heads, int64_t value_heads, int64_t head_dim_k, int64_t head_dim_v, int64_t taps,
-                     int64_t kernel_size, float scale, float eps, void* stream) {
+                     const void* beta, float* state, const void* z, const void* norm_w, void* out, void* workspace,
+                     int64_t batch, int64_t key_heads, int64_t value_heads, int64_t head_dim_k, int64_t head_dim_v,
+                     int64_t taps, int64_t kernel_size, float scale, float eps, void* stream) {
     if (batch < 0 || key_heads <= 0 || value_heads <= 0 || value_heads % key_heads) return GDN_ERR_SHAPE;
-    if (taps < 1 || taps > 8 || kernel_size < 1 || kernel_size > taps + 1) return GDN_ERR_SHAPE;
+    if (taps < 1 || kernel_size < 1 || kernel_size > taps + 1) return GDN_ERR_SHAPE;
+    if (taps < 2 || taps > 4 || kernel_size < 2) return GDN_ERR_UNSUPPORTED;
     if (head_dim_k != kHeadDim || head_dim_v != kHeadDim) return GDN_ERR_UNSUPPORTED;
     if (batch > 65535 || value_heads > 65535) return GDN_ERR_SHAPE;
     if (batch == 0) return GDN_OK;
-    if (!qkv || !conv_state || !conv_w || !g || !beta || !state || !z || !norm_w || !out) return GDN_ERR_NULL;
-    if (!aligned16(state) || !aligned16(z) || !aligned16(out) || (reinterpret_cast<uintptr_t>(norm_w) & 7u))
+    if (!qkv || !conv_state || !conv_w || !g || !beta || !state || !z || !norm_w || !out || !workspace)
+        return GDN_ERR_NULL;
+    if (!rows_aligned(qkv, 2, qkv_stride_b, 0, 0) || !aligned16(conv_state) || !aligned16(state) || !aligned16(z) ||
+        !aligned16(conv_w) ||
+        !aligned16(out) || !aligned16(workspace) || (reinterpret_cast<uintptr_t>(norm_w) & 7u))
         return GDN_ERR_ALIGN;
     DecodeLayerArgs a;
     a.qkv = qkv; a.qkv_sb = qkv_stride_b; a.conv_state = conv_state; a.conv_w = conv_w;
-    a.g = g; a.beta = beta; a.state = state; a.z = z; a.norm_w = norm_w; a.out = out;
+    a.g = g; a.beta = beta; a.state = state; a.z = z; a.norm_w = norm_w; a.out = out; a.workspace = workspace;
     a.B = batch; a.H = (int)key_heads; a.HV = (int)value_heads; a.taps = (int)taps; a.K = (int)kernel_size;
     a.scale = scale; a.eps = eps;
     return launch_decode_layer(a, as_stream(stream));

@@ -115,54 +115,85 @@ int launch_conv1d_silu(const void* x, int64_t sxb, int64_t sxt, const void* w, v
     return launch_status();
 }
 
-// Decode step: y = silu(bf16(sum_i bf16(w_i * window_i))); the state keeps the last `taps` inputs.
+// Decode step: y = silu(bf16(sum_i bf16(w_i * window_i))); the state keeps the last `taps`
+// inputs. One thread owns 8 consecutive channels, so every access is a 16-byte vector: the
+// channels' conv states are 8 * taps contiguous bf16 values, and x, y are 8 contiguous bf16.
+template <int TAPS, int K>
 __global__ void conv1d_silu_step_kernel(const bf16* __restrict__ x, int64_t sxb, bf16* __restrict__ state,
-                                        const bf16* __restrict__ w, bf16* __restrict__ y, int64_t B, int64_t C,
-                                        int taps, int K) {
-    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (idx >= B * C) return;
-    const int64_t b = idx / C, c = idx % C;
-    bf16* st = state + idx * taps;
-    float buf[kMaxTaps + 1];
-    for (int i = 0; i < taps; ++i) buf[i] = to_f32(st[i]);
-    buf[taps] = to_f32(x[b * sxb + c]);
-    float acc = 0.f;
-    for (int i = 0; i < K; ++i) acc = __fadd_rn(acc, round_bf16(__fmul_rn(to_f32(w[c * K + i]), buf[taps + 1 - K + i])));
-    y[b * C + c] = __float2bfloat16_rn(silu_f32(round_bf16(acc)));
-    for (int i = 0; i < taps; ++i) st[i] = __float2bfloat16_rn(buf[i + 1]);
+                                        const bf16* __restrict__ w, bf16* __restrict__ y, int64_t B, int64_t C) {
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // group of 8 channels
+    const int64_t groups = C / 8;
+    if (idx >= B * groups) return;
+    const int64_t b = idx / groups, c8 = (idx % groups) * 8;
+    constexpr int N = 8 * TAPS;  // bf16 state values of 8 channels
+    constexpr int NW = 8 * K;    // bf16 weights of 8 channels
+    bf16 st[N], wt[NW];
+    {
+        uint4* st_vec = reinterpret_cast<uint4*>(st);
+        const uint4* src = reinterpret_cast<const uint4*>(state + (b * C + c8) * TAPS);
+#pragma unroll
+        for (int i = 0; i < N / 8; ++i) st_vec[i] = src[i];
+        uint4* w_vec = reinterpret_cast<uint4*>(wt);
+        const uint4* wsrc = reinterpret_cast<const uint4*>(w + c8 * K);
+#pragma unroll
+        for (int i = 0; i < NW / 8; ++i) w_vec[i] = __ldg(wsrc + i);
+    }
+    float xv[8];
+    load8(x + b * sxb + c8, xv);
+    float out[8];
+    bf16 nst[N];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        float win[TAPS + 1];
+#pragma unroll
+        for (int i = 0; i < TAPS; ++i) win[i] = to_f32(st[j * TAPS + i]);
+        win[TAPS] = xv[j];
+        float acc = 0.f;
+#pragma unroll
+        for (int i = 0; i < K; ++i)
+            acc = __fadd_rn(acc, round_bf16(__fmul_rn(to_f32(wt[j * K + i]), win[TAPS + 1 - K + i])));
+        out[j] = silu_f32(round_bf16(acc));
+#pragma unroll
+        for (int i = 0; i < TAPS; ++i) nst[j * TAPS + i] = __float2bfloat16_rn(win[i + 1]);
+    }
+    store8(y + b * C + c8, out);
+    uint4* dst = reinterpret_cast<uint4*>(state + (b * C + c8) * TAPS);
+    const uint4* nst_vec = reinterpret_cast<const uint4*>(nst);
+#pragma unroll
+    for (int i = 0; i < N / 8; ++i) dst[i] = nst_vec[i];
+}
+
+template <int TAPS>
+static int conv_step_taps(const bf16* x, int64_t sxb, bf16* st, const bf16* w, bf16* y, int64_t B, int64_t C, int K,
+                          unsigned blocks, int threads, cudaStream_t s) {
+    switch (K) {
+        case 2: conv1d_silu_step_kernel<TAPS, 2><<<blocks, threads, 0, s>>>(x, sxb, st, w, y, B, C); break;
+        case 3: conv1d_silu_step_kernel<TAPS, 3><<<blocks, threads, 0, s>>>(x, sxb, st, w, y, B, C); break;
+        case 4:
+            if (TAPS >= 3) conv1d_silu_step_kernel<TAPS, (TAPS >= 3 ? 4 : 3)><<<blocks, threads, 0, s>>>(x, sxb, st, w, y, B, C);
+            else return GDN_ERR_SHAPE;
+            break;
+        default: return GDN_ERR_UNSUPPORTED;
+    }
+    return launch_status();
 }
 
 int launch_conv1d_silu_step(const void* x, int64_t sxb, void* state, const void* w, void* y, int64_t B, int64_t C,
                             int taps, int K, cudaStream_t s) {
     if (B * C == 0) return GDN_OK;
+    if (C % 8 || K > taps + 1 || K < 2) return GDN_ERR_SHAPE;
     constexpr int threads = 256;
-    const int64_t blocks = (B * C + threads - 1) / threads;
-    conv1d_silu_step_kernel<<<(unsigned)blocks, threads, 0, s>>>(static_cast<const bf16*>(x), sxb,
-                                                                 static_cast<bf16*>(state), static_cast<const bf16*>(w),
-                                                                 static_cast<bf16*>(y), B, C, taps, K);
-    return launch_status();
-}
-
-// Rolls the conv state forward by one token (used after the fused decode layer).
-__global__ void conv_state_shift_kernel(const bf16* __restrict__ x, int64_t sxb, bf16* __restrict__ state, int64_t B,
-                                        int64_t C, int taps) {
-    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (idx >= B * C) return;
-    const int64_t b = idx / C, c = idx % C;
-    bf16* st = state + idx * taps;
-    bf16 vals[kMaxTaps];
-    for (int i = 1; i < taps; ++i) vals[i - 1] = st[i];
-    vals[taps - 1] = x[b * sxb + c];
-    for (int i = 0; i < taps; ++i) st[i] = vals[i];
-}
-
-int launch_conv_state_shift(const void* x, int64_t sxb, void* state, int64_t B, int64_t C, int taps, cudaStream_t s) {
-    if (B * C == 0) return GDN_OK;
-    constexpr int threads = 256;
-    const int64_t blocks = (B * C + threads - 1) / threads;
-    conv_state_shift_kernel<<<(unsigned)blocks, threads, 0, s>>>(static_cast<const bf16*>(x), sxb,
-                                                                 static_cast<bf16*>(state), B, C, taps);
-    return launch_status();
+    const unsigned blocks = (unsigned)((B * (C / 8) + threads - 1) / threads);
+    auto xp = static_cast<const bf16*>(x);
+    auto sp = static_cast<bf16*>(state);
+    auto wp = static_cast<const bf16*>(w);
+    auto yp = static_cast<bf16*>(y);
+    switch (taps) {
+        case 2: return conv_step_taps<2>(xp, sxb, sp, wp, yp, B, C, K, blocks, threads, s);
+        case 3: return conv_step_taps<3>(xp, sxb, sp, wp, yp, B, C, K, blocks, threads, s);
+        case 4: return conv_step_taps<4>(xp, sxb, sp, wp, yp, B, C, K, blocks, threads, s);
+        default: return GDN_ERR_UNSUPPORTED;
+    }
 }
 
 // Verify conv: ext = state ++ qkv^T; output t = silu(bf16(sum_i w_i ext[t + taps - K + 1 + i]))

@@ -60,6 +60,7 @@ struct DecodeLayerArgs {
     const void* z;
     const void* norm_w;
     void* out;
+    void* workspace;  // [B, C] bf16: post-conv activations
     int64_t B;
     int H, HV, taps, K;
     float scale, eps;
@@ -70,7 +71,6 @@ int launch_conv1d_silu(const void* x, int64_t sxb, int64_t sxt, const void* w, v
                        int64_t T, int64_t C, int K, cudaStream_t s);
 int launch_conv1d_silu_step(const void* x, int64_t sxb, void* state, const void* w, void* y, int64_t B, int64_t C,
                             int taps, int K, cudaStream_t s);
-int launch_conv_state_shift(const void* x, int64_t sxb, void* state, int64_t B, int64_t C, int taps, cudaStream_t s);
 int launch_conv_step(const void* state, const void* qkv, int64_t sqb, int64_t sqt, const void* w, void* ext, void* q,
                      void* k, void* v, int64_t B, int64_t T, int taps, int K, int64_t key_dim, int64_t value_dim, int dk,
                      int dv, cudaStream_t s);

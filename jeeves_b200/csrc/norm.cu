@@ -9,8 +9,10 @@
 
 namespace gdn {
 
-__global__ void gated_rmsnorm_kernel(const bf16* __restrict__ x, const bf16* __restrict__ z,
-                                     const bf16* __restrict__ w, bf16* __restrict__ y, int64_t rows, float eps) {
+// x and y may alias (the fused decode layer normalises in place): every lane reads its four
+// elements before the warp reduction and writes them after it.
+__global__ void gated_rmsnorm_kernel(const bf16* x, const bf16* __restrict__ z, const bf16* __restrict__ w, bf16* y,
+                                     int64_t rows, float eps) {
     const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
     if (row >= rows) return;
     const int lane = threadIdx.x & 31;

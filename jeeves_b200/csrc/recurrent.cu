@@ -244,174 +244,45 @@ int launch_snapshot_commit(float* state, const float* snapshots, const int64_t* 
 }
 
 // ---------------------------------------------------------------------------------------
-// Fused decode layer: conv step (+SiLU) over the pre-conv token, q/k L2 norm, gated delta
-// rule step on the state in place, output-gated RMSNorm. One CTA per (row, value head)
-// owns the full 128 x 128 state so that the norm over the head's 128 outputs stays in
-// one warp. The conv state is only read here; launch_conv_state_shift rolls it forward
-// afterwards (an in-place update inside this kernel would race with the other value
-// heads that read the same q/k channels).
+// Decode layer: one new token per row through conv step (+SiLU), q/k L2 norm, the gated
+// delta rule step on the state in place and the output-gated RMSNorm, as three launches on
+// the stream: (1) the conv step over all channels, each channel once, writing the post-conv
+// activations to the caller's workspace and rolling the conv state forward; (2) the
+// recurrent kernel above on 32-column state slices, writing o (bf16, as the reference rounds
+// it before the norm) into `out`; (3) the gated RMSNorm in place on `out`.
 // ---------------------------------------------------------------------------------------
-
-struct DecodeParams {
-    const bf16* qkv;
-    int64_t qkv_sb;
-    const bf16* conv_state;
-    const bf16* conv_w;
-    const float* g;
-    const bf16* beta;
-    float* state;
-    const bf16* z;
-    const bf16* norm_w;
-    bf16* out;
-    int H, HV, rep, taps, K;
-    int64_t C;
-    float scale, eps;
-};
-
-// Conv + SiLU of one channel for the decode token, rounded like the eager step
-// (model/model.py:207-214): bf16 products, fp32 sum, bf16, silu in fp32, bf16.
-__device__ __forceinline__ float conv_token(const DecodeParams& p, int64_t b, int64_t c) {
-    const bf16* st = p.conv_state + (b * p.C + c) * p.taps;
-    const bf16* w = p.conv_w + c * p.K;
-    float acc = 0.f;
-    for (int i = 0; i < p.K; ++i) {
-        // window = last K of (state ++ x): entry i is state[taps - K + 1 + i] or x for i = K-1
-        const float xi = (i == p.K - 1) ? to_f32(p.qkv[b * p.qkv_sb + c]) : to_f32(st[p.taps - p.K + 1 + i]);
-        acc = __fadd_rn(acc, round_bf16(__fmul_rn(xi, to_f32(w[i]))));
-    }
-    return round_bf16(silu_f32(round_bf16(acc)));
-}
-
-template <int NT>
-__global__ void __launch_bounds__(NT) decode_layer_kernel(const DecodeParams p) {
-    constexpr int VS = kHeadDim, COLG = VS / 4, NW = NT / 32, ROWG = NT / COLG, RPT = kHeadDim / ROWG;
-    __shared__ float4 red[2][NW][COLG];
-    __shared__ float kq[2][kHeadDim];
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int cg = tid % COLG, rg = tid / COLG, row0 = rg * RPT, col = cg * 4;
-    const int hv = blockIdx.x;
-    const int64_t b = blockIdx.y;
-    const int h = hv / p.rep;
-    const int64_t tile = (b * p.HV + hv) * (int64_t)(kHeadDim * kHeadDim);
-
-    float4 S[RPT];
-    const float* src = p.state + tile + (int64_t)row0 * kHeadDim + col;
-#pragma unroll
-    for (int r = 0; r < RPT; ++r) S[r] = ldg_stream(reinterpret_cast<const float4*>(src + r * kHeadDim));
-
-    // conv outputs: q and k of key head h (256 channels), v of value head hv (128)
-    const int64_t key_dim = (int64_t)p.H * kHeadDim;
-    if (tid < 2 * kHeadDim) {
-        const int part = tid / kHeadDim, d = tid % kHeadDim;
-        kq[part][d] = conv_token(p, b, part * key_dim + (int64_t)h * kHeadDim + d);
-    }
-    float4 vv;
-    {
-        const int64_t c0 = 2 * key_dim + (int64_t)hv * kHeadDim + col;
-        vv.x = conv_token(p, b, c0);
-        vv.y = conv_token(p, b, c0 + 1);
-        vv.z = conv_token(p, b, c0 + 2);
-        vv.w = conv_token(p, b, c0 + 3);
-    }
-    __syncthreads();
-    const float4 ql = *reinterpret_cast<const float4*>(&kq[0][4 * lane]);
-    const float4 kl = *reinterpret_cast<const float4*>(&kq[1][4 * lane]);
-    const float rk = rsqrtf(warp_sum(kl.x * kl.x + kl.y * kl.y + kl.z * kl.z + kl.w * kl.w) + 1e-6f);
-    const float rq = rsqrtf(warp_sum(ql.x * ql.x + ql.y * ql.y + ql.z * ql.z + ql.w * ql.w) + 1e-6f) * p.scale;
-    const float qk = warp_sum(ql.x * kl.x + ql.y * kl.y + ql.z * kl.z + ql.w * kl.w);
-    const int64_t gi = b * p.HV + hv;
-    const float decay = expf(p.g[gi]);
-    const float bt = to_f32(p.beta[gi]);
-
-    float4 pk = make_float4(0.f, 0.f, 0.f, 0.f), pq = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-    for (int r = 0; r < RPT; ++r) {
-        const float ki = kq[1][row0 + r] * rk;
-        const float qi = kq[0][row0 + r] * rq;
-        pk.x += ki * S[r].x; pk.y += ki * S[r].y; pk.z += ki * S[r].z; pk.w += ki * S[r].w;
-        pq.x += qi * S[r].x; pq.y += qi * S[r].y; pq.z += qi * S[r].z; pq.w += qi * S[r].w;
-    }
-    if (lane < COLG || COLG == 32) {
-        red[0][warp][cg] = pk;
-        red[1][warp][cg] = pq;
-    }
-    __syncthreads();
-    float4 rs = red[0][0][cg];
-#pragma unroll
-    for (int w = 1; w < NW; ++w) {
-        const float4 x = red[0][w][cg];
-        rs.x += x.x; rs.y += x.y; rs.z += x.z; rs.w += x.w;
-    }
-    float4 delta;
-    delta.x = bt * (vv.x - decay * rs.x);
-    delta.y = bt * (vv.y - decay * rs.y);
-    delta.z = bt * (vv.z - decay * rs.z);
-    delta.w = bt * (vv.w - decay * rs.w);
-    if (warp == 0) {
-        float4 ps = red[1][0][cg];
-#pragma unroll
-        for (int w = 1; w < NW; ++w) {
-            const float4 x = red[1][w][cg];
-            ps.x += x.x; ps.y += x.y; ps.z += x.z; ps.w += x.w;
-        }
-        const float qkn = qk * rk * rq;
-        float o[4] = {decay * ps.x + qkn * delta.x, decay * ps.y + qkn * delta.y, decay * ps.z + qkn * delta.z,
-                      decay * ps.w + qkn * delta.w};
-        // The reference rounds o to bf16 before the norm (o.to(q.dtype), model/model.py:239).
-        float sq = 0.f;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            o[i] = round_bf16(o[i]);
-            sq += o[i] * o[i];
-        }
-        const float inv = inv_sqrt_rn(warp_sum(sq) * (1.0f / kHeadDim) + p.eps);
-        const float4 zz = load4(p.z + gi * kHeadDim + col);
-        const float4 ww = load4(p.norm_w + col);
-        const float zv[4] = {zz.x, zz.y, zz.z, zz.w}, wv[4] = {ww.x, ww.y, ww.z, ww.w};
-        float4 y;
-        float* yv = &y.x;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const float normed = round_bf16(o[i] * inv);
-            const float weighted = round_bf16(wv[i] * normed);
-            yv[i] = weighted * silu_f32(zv[i]);
-        }
-        store4(p.out + gi * kHeadDim + col, y);
-    }
-    float* dst = p.state + tile + (int64_t)row0 * kHeadDim + col;
-#pragma unroll
-    for (int r = 0; r < RPT; ++r) {
-        const float ki = kq[1][row0 + r] * rk;
-        float4 x;
-        x.x = decay * S[r].x + ki * delta.x;
-        x.y = decay * S[r].y + ki * delta.y;
-        x.z = decay * S[r].z + ki * delta.z;
-        x.w = decay * S[r].w + ki * delta.w;
-        stg_stream(reinterpret_cast<float4*>(dst + r * kHeadDim), x);
-    }
-}
-
 int launch_decode_layer(const DecodeLayerArgs& a, cudaStream_t s) {
     if (a.B == 0) return GDN_OK;
-    DecodeParams p;
-    p.qkv = static_cast<const bf16*>(a.qkv);
-    p.qkv_sb = a.qkv_sb;
-    p.conv_state = static_cast<const bf16*>(a.conv_state);
-    p.conv_w = static_cast<const bf16*>(a.conv_w);
-    p.g = a.g;
-    p.beta = static_cast<const bf16*>(a.beta);
-    p.state = a.state;
-    p.z = static_cast<const bf16*>(a.z);
-    p.norm_w = static_cast<const bf16*>(a.norm_w);
-    p.out = static_cast<bf16*>(a.out);
-    p.H = a.H; p.HV = a.HV; p.rep = a.HV / a.H; p.taps = a.taps; p.K = a.K;
-    p.C = 2 * (int64_t)a.H * kHeadDim + (int64_t)a.HV * kHeadDim;
-    p.scale = a.scale; p.eps = a.eps;
-    dim3 grid((unsigned)a.HV, (unsigned)a.B);
-    decode_layer_kernel<256><<<grid, 256, 0, s>>>(p);
-    int st = launch_status();
+    const int64_t key_dim = (int64_t)a.H * kHeadDim;
+    const int64_t C = 2 * key_dim + (int64_t)a.HV * kHeadDim;
+    int st = launch_conv1d_silu_step(a.qkv, a.qkv_sb, a.conv_state, a.conv_w, a.workspace, a.B, C, a.taps, a.K, s);
     if (st != GDN_OK) return st;
-    return launch_conv_state_shift(a.qkv, a.qkv_sb, a.conv_state, a.B, p.C, a.taps, s);
+    const bf16* y = static_cast<const bf16*>(a.workspace);
+    RecurrentArgs r;
+    r.q = y;
+    r.k = y + key_dim;
+    r.v = y + 2 * key_dim;
+    r.qkv_dtype = GDN_BF16;
+    r.g = a.g;
+    r.beta = a.beta;
+    r.beta_dtype = GDN_BF16;
+    r.state_in = a.state;
+    r.state_out = a.state;
+    r.snapshots = nullptr;
+    r.o = a.out;
+    r.steps = nullptr;
+    r.cu_seqlens = nullptr;
+    r.rows = a.B;
+    r.T = 1;
+    r.H = a.H;
+    r.HV = a.HV;
+    r.qsb = C; r.qst = C; r.qsh = kHeadDim;
+    r.ksb = C; r.kst = C; r.ksh = kHeadDim;
+    r.vsb = C; r.vst = C; r.vsh = kHeadDim;
+    r.scale = a.scale;
+    st = launch_recurrent(r, s);
+    if (st != GDN_OK) return st;
+    return launch_gated_rmsnorm(a.out, a.z, a.norm_w, a.out, a.B * a.HV, kHeadDim, a.eps, s);
 }
 
 }  // namespace gdn

@@ -15,10 +15,11 @@ from .gated_delta import HEAD_DIM, _require_cuda, _stream
 
 
 def decode_layer_step(qkv, conv_state, conv_weight, g, beta, state, z, norm_weight, key_heads: int,
-                      eps: float = 1e-6, scale: float | None = None) -> torch.Tensor:
+                      eps: float = 1e-6, scale: float | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
     """qkv ``[B, C]`` pre-conv bf16 (q | k | v channels); conv_state ``[B, C, taps]`` and state
     ``[B, HV, 128, 128]`` are updated in place; g ``[B, HV]`` fp32, beta ``[B, HV]`` bf16, z
-    ``[B, HV, 128]``; returns the normed output ``[B, HV, 128]`` bf16."""
+    ``[B, HV, 128]``; returns the normed output ``[B, HV, 128]`` bf16. ``workspace`` (``[B, C]``
+    bf16, allocated here when not given) receives the post-conv activations."""
     what = "decode_layer_step"
     _require_cuda(what, qkv, conv_state, conv_weight, g, beta, state, z, norm_weight)
     B, C = qkv.shape
@@ -39,9 +40,15 @@ def decode_layer_step(qkv, conv_state, conv_weight, g, beta, state, z, norm_weig
     beta = beta.reshape(B, HV).to(torch.bfloat16).contiguous()
     z = z.reshape(B, HV, HEAD_DIM).contiguous()
     out = torch.empty(B, HV, HEAD_DIM, dtype=torch.bfloat16, device=qkv.device)
+    if workspace is None:
+        workspace = torch.empty(B, C, dtype=torch.bfloat16, device=qkv.device)
+    elif workspace.shape != (B, C) or workspace.dtype != torch.bfloat16 or not workspace.is_contiguous():
+        raise ValueError(f"workspace: expected a contiguous bfloat16 tensor of shape {(B, C)}, got {workspace.dtype} "
+                         f"{tuple(workspace.shape)}")
     status = _lib.load().gdn_decode_layer(
         qkv.data_ptr(), qkv.stride(0), conv_state.data_ptr(), w.data_ptr(), g.data_ptr(), beta.data_ptr(),
-        state.data_ptr(), z.data_ptr(), norm_weight.contiguous().data_ptr(), out.data_ptr(), B, key_heads, HV,
+        state.data_ptr(), z.data_ptr(), norm_weight.contiguous().data_ptr(), out.data_ptr(), workspace.data_ptr(),
+        B, key_heads, HV,
         HEAD_DIM, HEAD_DIM, taps, w.shape[1], float(HEAD_DIM ** -0.5 if scale is None else scale), float(eps), _stream())
     _lib.check(status, what)
     return out
