@@ -69,58 +69,61 @@ def profiled_traffic():
 # clocks sampled during the timed region
 # ------------------------------------------------------------------------------------------
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-              "clocks_event_reasons.sw_power_cap")
+    """Samples SM clock and throttle reasons through NVML every 10 ms (read-only queries)."""
+
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4}
 
     def __init__(self, device_index: int):
         self.idx = device_index
-        self.proc = None
-        self.lines: list[str] = []
+        self.sm: list[float] = []
+        self.reasons: set[str] = set()
+        self.max_mhz = None
+        self.running = False
+        self.error = None
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
+            import pynvml
+
+            pynvml.nvmlInit()
+            visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+            index = int(visible.split(",")[self.idx]) if visible else self.idx
+            self.handle = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+            self.nvml = pynvml
+            self.running = True
+            self.thread = threading.Thread(target=self._poll, daemon=True)
             self.thread.start()
-        except Exception:
-            self.proc = None
+        except Exception as e:  # no NVML: report the clocks as unsampled
+            self.error = str(e)
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def _poll(self):
+        nv = self.nvml
+        while self.running:
+            try:
+                self.sm.append(float(nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)))
+                mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                for name, bit in self.REASONS.items():
+                    if mask & bit:
+                        self.reasons.add(name)
+            except Exception as e:
+                self.error = str(e)
+                return
+            time.sleep(0.01)
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
+        self.running = False
+        if hasattr(self, "thread"):
+            self.thread.join(timeout=2)
 
     def summary(self):
-        sm, smax, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                smax.append(float(parts[2]))
-            except ValueError:
-                continue
-            for name, flag in zip(names, parts[5:9]):
-                if flag.lower() == "active":
-                    reasons.add(name)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        busy = [s for s in sm if s > 0.5 * max(sm)] or sm
-        return {"sm_mhz": statistics.median(busy), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        if not self.sm:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"],
+                    **({"error": self.error} if self.error else {})}
+        busy = [x for x in self.sm if x > 0.5 * max(self.sm)] or self.sm
+        return {"sm_mhz": statistics.median(busy), "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                "samples": len(self.sm)}
 
 
 # ------------------------------------------------------------------------------------------
@@ -217,8 +220,8 @@ def run_ours(args, rank, world, device, rank_sync, reduce_max):
         ev_pairs.append((a, b))
         gdn.gated_rms_norm(o.view(-1, D), x["z"].view(-1, D), x["nw"])
 
-    with ClockSampler(device.index) as clocks:
-        ms = timed(prefill_step, args.steps, args.warmup, rank_sync)
+    clocks = ClockSampler(device.index).__enter__()  # sampled across every timed region below
+    ms = timed(prefill_step, args.steps, args.warmup, rank_sync)
     torch.cuda.synchronize()
     kernel_ms = [a.elapsed_time(b) for a, b in ev_pairs[args.warmup:]]
     ms = reduce_max(ms)
@@ -271,7 +274,6 @@ def run_ours(args, rank, world, device, rank_sync, reduce_max):
                      "algorithmic_bytes": core_bytes,
                      "traffic": traffic.get("prefill", {}).get("dram_bytes_per_launch"),
                      "tensor_frac": round(prefill_flops(T) / (k_ms / 1e3) / 1e12 / tc_peak, 4)},
-        "clocks": clocks.summary(),
     })
 
     # ---------------- extras: varlen, decode, verify ----------------
@@ -282,6 +284,8 @@ def run_ours(args, rank, world, device, rank_sync, reduce_max):
         extra["verify"] = bench_verify(gdn, args, device, rank, world, rank_sync, reduce_max, hbm_peak)
         result["extra"] = extra
         result["gpu_launches"] += sum(e.get("gpu_launches", 0) for e in extra.values())
+    clocks.__exit__(None, None, None)
+    result["clocks"] = clocks.summary()
     return result
 
 
@@ -437,7 +441,7 @@ def run_reference(args, rank, world):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-extras", dest="extras", action="store_false")
