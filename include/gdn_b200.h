@@ -37,7 +37,8 @@ enum {
     GDN_ERR_NULL = 4,         /* a required pointer is NULL */
     GDN_ERR_LAUNCH = 5,       /* the CUDA launch failed (cudaGetLastError) */
     GDN_ERR_DEVICE_TIMEOUT = 6, /* a bounded device-side wait gave up (see gdn_device_error) */
-    GDN_ERR_UNSUPPORTED = 7   /* a valid but unimplemented configuration (e.g. head dim != 128) */
+    GDN_ERR_UNSUPPORTED = 7,  /* a valid but unimplemented configuration (e.g. head dim != 128) */
+    GDN_ERR_SCRATCH = 8       /* the request does not fit the fixed scratch of gdn_decode_layer_noalloc */
 };
 
 /* Element type codes. */
@@ -182,6 +183,27 @@ GDN_API int gdn_decode_layer(const void* qkv, int64_t qkv_stride_b, void* conv_s
                      int64_t batch, int64_t key_heads, int64_t value_heads,
                      int64_t head_dim_k, int64_t head_dim_v, int64_t taps, int64_t kernel_size,
                      float scale, float eps, void* stream);
+
+/*
+ * gdn_decode_layer without any device allocation, for callers that cannot allocate device
+ * memory or hand the library a buffer: a plugin host or server that has given all device
+ * memory to its own pool, a foreign-language binding with no device buffer to pass, or
+ * code that must not grow the process's device footprint after start-up. No counterpart in
+ * the reference: the reference always runs inside PyTorch, which owns an allocator.
+ * Same arguments and results as gdn_decode_layer, minus `workspace`: the post-conv
+ * activations go to a fixed file-scope device array of 2^21 bf16 values (4 MiB), which every
+ * GPU that loads the library holds until exit. batch * C above 2^21 returns
+ * GDN_ERR_SCRATCH. All calls on a device share the array and it keeps the last call's
+ * contents (each call overwrites what it reads), so calls that overlap on the GPU race. The
+ * first call on a device looks up the array's device address and caches it; make that
+ * first call before any stream capture. Calls no cudaMalloc, cudaFree or other allocator.
+ */
+GDN_API int gdn_decode_layer_noalloc(const void* qkv, int64_t qkv_stride_b, void* conv_state, const void* conv_w,
+                                     const float* g, const void* beta, float* state, const void* z,
+                                     const void* norm_w, void* out,
+                                     int64_t batch, int64_t key_heads, int64_t value_heads,
+                                     int64_t head_dim_k, int64_t head_dim_v, int64_t taps, int64_t kernel_size,
+                                     float scale, float eps, void* stream);
 
 #ifdef __cplusplus
 }

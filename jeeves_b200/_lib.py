@@ -13,7 +13,7 @@ import threading
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "_lib", "libgdn_b200.so")
 
-OK, ERR_SHAPE, ERR_DTYPE, ERR_ALIGN, ERR_NULL, ERR_LAUNCH, ERR_DEVICE_TIMEOUT, ERR_UNSUPPORTED = range(8)
+OK, ERR_SHAPE, ERR_DTYPE, ERR_ALIGN, ERR_NULL, ERR_LAUNCH, ERR_DEVICE_TIMEOUT, ERR_UNSUPPORTED, ERR_SCRATCH = range(9)
 F32, BF16 = 0, 1
 
 _p = ctypes.c_void_p
@@ -38,6 +38,8 @@ SIGNATURES: dict[str, list] = {
     "gdn_gated_rmsnorm": [_p, _p, _p, _p, _i64, _i64, _f32, _p],
     "gdn_decode_layer": [_p, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                          _f32, _f32, _p],
+    "gdn_decode_layer_noalloc": [_p, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
+                                 _f32, _f32, _p],
 }
 
 _lock = threading.Lock()
@@ -76,6 +78,6 @@ def check(status: int, what: str) -> None:
     if status == OK:
         return
     text = f"{what}: {status_text(status)} (status {status})"
-    if status in (ERR_SHAPE, ERR_DTYPE, ERR_ALIGN, ERR_NULL, ERR_UNSUPPORTED):
+    if status in (ERR_SHAPE, ERR_DTYPE, ERR_ALIGN, ERR_NULL, ERR_UNSUPPORTED, ERR_SCRATCH):
         raise ValueError(text)
     raise RuntimeError(text)

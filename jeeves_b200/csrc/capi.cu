@@ -35,6 +35,7 @@ const char* gdn_status_string(int status) {
         case GDN_ERR_LAUNCH: return "CUDA kernel launch failed";
         case GDN_ERR_DEVICE_TIMEOUT: return "a bounded device-side wait timed out";
         case GDN_ERR_UNSUPPORTED: return "unsupported configuration";
+        case GDN_ERR_SCRATCH: return "request larger than the fixed scratch of the no-allocation entry point";
         default: return "unknown status";
     }
 }

@@ -5,3 +5,4 @@
 #include "conv.cu"
 #include "norm.cu"
 #include "chunk.cu"
+#include "noalloc.cu"
