@@ -279,7 +279,7 @@ def run_ours(args, rank, world, device, rank_sync, reduce_max):
     # ---------------- extras: varlen, decode, verify ----------------
     if args.extras:
         extra = {}
-        extra["varlen"] = bench_varlen(gdn, args, device, rank_sync, reduce_max, world, hbm_peak)
+        extra["varlen"] = bench_varlen(gdn, args, device, rank_sync, reduce_max, world, hbm_peak, rank)
         extra["decode"] = bench_decode(gdn, args, device, rank, world, rank_sync, reduce_max, hbm_peak)
         extra["verify"] = bench_verify(gdn, args, device, rank, world, rank_sync, reduce_max, hbm_peak)
         result["extra"] = extra
@@ -289,11 +289,15 @@ def run_ours(args, rank, world, device, rank_sync, reduce_max):
     return result
 
 
-def bench_varlen(gdn, args, device, rank_sync, reduce_max, world, hbm_peak):
-    lens = varlen_lengths()
+def bench_varlen(gdn, args, device, rank_sync, reduce_max, world, hbm_peak, rank=0):
+    from jeeves_b200 import sharding
+
+    lens_all = varlen_lengths()
+    Ttot_all = sum(lens_all)
+    idx, lens, cu_local = sharding.local_varlen(lens_all, rank, world)  # longest-first balance
     N = len(lens)
     Ttot = sum(lens)
-    gen = torch.Generator().manual_seed(2)
+    gen = torch.Generator().manual_seed(2 + 1000 * rank)
     q = torch.randn(1, Ttot, H, D, generator=gen)
     q = (q * torch.rsqrt((q * q).sum(-1, keepdim=True) + 1e-6)).to(torch.bfloat16).to(device)
     k = torch.randn(1, Ttot, H, D, generator=gen)
@@ -302,7 +306,7 @@ def bench_varlen(gdn, args, device, rank_sync, reduce_max, world, hbm_peak):
     g = (-torch.exp(torch.randn(1, Ttot, HV, generator=gen) * 0.5 - 3.0)).to(device)
     beta = torch.sigmoid(torch.randn(1, Ttot, HV, generator=gen)).to(torch.bfloat16).to(device)
     h0 = (torch.randn(N, HV, D, D, generator=gen) * 0.02).to(device)
-    cu = torch.tensor([0] + torch.tensor(lens).cumsum(0).tolist(), dtype=torch.int32, device=device)
+    cu = cu_local.to(device)
 
     def step(i):
         gdn.gated_delta_rule_chunk(q, k, v, g, beta, initial_state=h0, output_final_state=True, cu_seqlens=cu)
@@ -311,16 +315,19 @@ def bench_varlen(gdn, args, device, rank_sync, reduce_max, world, hbm_peak):
     ms = reduce_max(timed(step, steps, args.warmup, rank_sync)) / steps
     bytes_ = prefill_core_bytes(Ttot, n_seq=N, with_h0=True)
     ach = bytes_ / (ms / 1e3) / 1e9
-    return {"workload": "config 2: 32 packed sequences U{128..2048} (seed 2), cu_seqlens, initial+final state",
-            "tokens": Ttot, "value": round(world * Ttot / (ms / 1e3), 1), "unit": "tokens/s", "ms_per_step": round(ms, 4),
+    return {"workload": f"config 2: 32 packed sequences U{{128..2048}} (seed 2), cu_seqlens, initial+final state; "
+                        f"sequences balanced longest-first over {world} GPU(s), {N} here",
+            "tokens": Ttot_all, "value": round(Ttot_all / (ms / 1e3), 1), "unit": "tokens/s", "ms_per_step": round(ms, 4),
             "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(ach / hbm_peak, 4), "algorithmic_bytes": bytes_},
             "gpu_launches": steps}
 
 
 def shard(n, rank, world):
-    per = n // world
-    return per, rank * per
+    from jeeves_b200 import sharding
+
+    start, count = sharding.row_shard(n, rank, world)
+    return count, start
 
 
 def bench_decode(gdn, args, device, rank, world, rank_sync, reduce_max, hbm_peak, layers=24, B_total=256, taps=3):
@@ -438,6 +445,55 @@ def run_reference(args, rank, world):
             "e2e": {"value": round(value, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+def profile_case(name, device):
+    """Runs one workload twice without timing, for `ncu -k ... -s 1 -c 1 python bench.py --profile NAME`."""
+    import jeeves_b200 as gdn
+
+    if name == "prefill":
+        x = make_prefill_inputs(seed=1, device=device)
+        for _ in range(2):
+            prefill_layer(gdn, x)
+    elif name == "varlen":
+        lens = varlen_lengths()
+        Tt, N = sum(lens), len(lens)
+        q = torch.randn(1, Tt, H, D, device=device).to(torch.bfloat16)
+        k = torch.randn(1, Tt, H, D, device=device).to(torch.bfloat16)
+        v = torch.randn(1, Tt, HV, D, device=device).to(torch.bfloat16)
+        g = -torch.rand(1, Tt, HV, device=device) * 0.1
+        beta = torch.rand(1, Tt, HV, device=device).to(torch.bfloat16)
+        h0 = torch.randn(N, HV, D, D, device=device) * 0.02
+        cu = torch.tensor([0] + torch.tensor(lens).cumsum(0).tolist(), dtype=torch.int32, device=device)
+        for _ in range(2):
+            gdn.gated_delta_rule_chunk(q, k, v, g, beta, initial_state=h0, output_final_state=True, cu_seqlens=cu)
+    elif name == "decode":
+        B = 256
+        state = torch.randn(B, HV, D, D, device=device) * 0.02
+        cs = torch.randn(B, C_QKV, 3, device=device).to(torch.bfloat16)
+        w = (torch.randn(C_QKV, 4, device=device) * 0.5).to(torch.bfloat16)
+        qkv = torch.randn(B, C_QKV, device=device).to(torch.bfloat16)
+        g = -torch.rand(B, HV, device=device) * 0.1
+        beta = torch.rand(B, HV, device=device).to(torch.bfloat16)
+        z = torch.randn(B, HV, D, device=device).to(torch.bfloat16)
+        nw = torch.ones(D, device=device, dtype=torch.bfloat16)
+        for _ in range(2):
+            gdn.decode_layer_step(qkv, cs, w, g, beta, state, z, nw, H)
+    elif name == "verify":
+        B, T = 128, 5
+        state = torch.randn(B, HV, D, D, device=device) * 0.02
+        q = torch.randn(B, T, H, D, device=device).to(torch.bfloat16)
+        v = torch.randn(B, T, HV, D, device=device).to(torch.bfloat16)
+        g = -torch.rand(B, T, HV, device=device) * 0.1
+        beta = torch.rand(B, T, HV, device=device).to(torch.bfloat16)
+        acc = torch.randint(1, T + 1, (B,), device=device)
+        for _ in range(2):
+            _, snaps = gdn.gated_delta_rule_verify(q, q, v, g, beta, state)
+            gdn.gated_delta_rule_rollback(state, snaps, acc)
+    else:
+        raise SystemExit(f"unknown profile case {name}")
+    torch.cuda.synchronize()
+    print(f"profile case {name}: ok")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -446,6 +502,8 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-extras", dest="extras", action="store_false")
     ap.add_argument("--no-cpu-baseline", dest="cpu", action="store_false")
+    ap.add_argument("--profile", choices=("prefill", "varlen", "decode", "verify"),
+                    help="run one workload twice, untimed, for an ncu capture")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
@@ -464,6 +522,9 @@ def main():
         sys.exit(1)
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
+    if args.profile:
+        profile_case(args.profile, device)
+        return
     if world > 1:
         import datetime
         import torch.distributed as dist
