@@ -148,9 +148,9 @@ int gdn_conv1d_silu(const void* x, int64_t x_stride_b, int64_t x_stride_t, const
     if (kernel_size < 2 || kernel_size > 4) return GDN_ERR_UNSUPPORTED;
     if (batch == 0 || seqlen == 0) return GDN_OK;
     if (!x || !w || !y) return GDN_ERR_NULL;
-    if (!rows_aligned(x, 2, x_stride_b, x_stride_t, 0) || !aligned16(y)) return GDN_ERR_ALIGN;
-    if (cu_seqlens && batch > 65535) return GDN_ERR_SHAPE;
+    if (!rows_aligned(x, 2, x_stride_b, x_stride_t, 0) || !aligned16(y) || !aligned16(w)) return GDN_ERR_ALIGN;
     if (!cu_seqlens && batch > 65535) return GDN_ERR_SHAPE;
+    if (channels / 8 > 65535 * 128 || seqlen > INT32_MAX) return GDN_ERR_SHAPE;
     return launch_conv1d_silu(x, x_stride_b, x_stride_t, w, y, cu_seqlens, batch, seqlen, channels, (int)kernel_size,
                               as_stream(stream));
 }

@@ -13,10 +13,9 @@ namespace gdn {
 
 constexpr int kMaxTaps = 8;
 
-// Prefill: each thread owns 8 channels and walks a run of tokens with the last K-1
-// inputs in registers, so every input is read from memory once.
-constexpr int kConvTokens = 32;
-
+// Prefill: one thread per (8 channels, token). It reads its K-token window with 16-byte
+// loads (neighbouring tokens' windows overlap in L1, so HBM sees every input once) and writes
+// 16 bytes of output. With cu_seqlens the window stops at the start of the token's sequence.
 __device__ __forceinline__ void load8(const bf16* p, float* out) {
     const uint4 raw = *reinterpret_cast<const uint4*>(p);
     const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
@@ -37,72 +36,61 @@ __device__ __forceinline__ void store8(bf16* p, const float* v) {
 }
 
 template <int K>
-__global__ void conv1d_silu_kernel(const bf16* __restrict__ x, int64_t sxb, int64_t sxt, const bf16* __restrict__ w,
-                                   bf16* __restrict__ y, const int32_t* __restrict__ cu, int nseq, int64_t T, int64_t C) {
-    const int64_t c8 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8;
+__global__ void __launch_bounds__(128) conv1d_silu_kernel(const bf16* __restrict__ x, int64_t sxb, int64_t sxt,
+                                                          const bf16* __restrict__ w, bf16* __restrict__ y,
+                                                          const int32_t* __restrict__ cu, int nseq, int64_t T,
+                                                          int64_t C) {
+    const int64_t c8 = ((int64_t)blockIdx.y * blockDim.x + threadIdx.x) * 8;
     if (c8 >= C) return;
+    const int64_t t = blockIdx.x;  // tokens on x: up to 2^31 - 1
     const int64_t b = blockIdx.z;
-    const int64_t t0 = (int64_t)blockIdx.y * kConvTokens;
-    if (t0 >= T) return;
-    const int64_t t1 = t0 + kConvTokens < T ? t0 + kConvTokens : T;
-
-    float wt[8][K];
-#pragma unroll
-    for (int j = 0; j < 8; ++j)
-#pragma unroll
-        for (int i = 0; i < K; ++i) wt[j][i] = to_f32(w[(c8 + j) * K + i]);
-
-    // sequence boundaries: a window never reaches back past the start of its sequence
-    int64_t seq_start = 0, seq_end = T;
-    int s = 0;
-    if (cu) {
-        while (s + 1 < nseq && cu[s + 1] <= t0) ++s;
-        seq_start = cu[s];
-        seq_end = cu[s + 1];
+    int64_t seq_start = 0;
+    if (cu) {  // last sequence start <= t (binary search over nseq + 1 offsets)
+        int lo = 0, hi = nseq;
+        while (hi - lo > 1) {
+            const int mid = (lo + hi) >> 1;
+            if (cu[mid] <= t) lo = mid;
+            else hi = mid;
+        }
+        seq_start = cu[lo];
     }
-    float win[K][8];  // win[K-1] is the current token; win[0] the oldest
+    float wt[8][K];
+    {
+        bf16 wr[8 * K];
+        const uint4* wsrc = reinterpret_cast<const uint4*>(w + c8 * K);
 #pragma unroll
-    for (int i = 0; i < K - 1; ++i) {
-        const int64_t t = t0 - (K - 1) + i;
-        if (t >= seq_start) load8(x + b * sxb + t * sxt + c8, win[i]);
+        for (int i = 0; i < K; ++i) reinterpret_cast<uint4*>(wr)[i] = __ldg(wsrc + i);
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+#pragma unroll
+            for (int i = 0; i < K; ++i) wt[j][i] = to_f32(wr[j * K + i]);
+    }
+    float win[K][8];
+#pragma unroll
+    for (int i = 0; i < K; ++i) {
+        const int64_t tt = t - (K - 1) + i;
+        if (tt >= seq_start) load8(x + b * sxb + tt * sxt + c8, win[i]);
         else
 #pragma unroll
             for (int j = 0; j < 8; ++j) win[i][j] = 0.f;
     }
-    for (int64_t t = t0; t < t1; ++t) {
-        if (cu && t >= seq_end) {  // next sequence starts here: clear the window
-            while (s + 1 < nseq && cu[s + 1] <= t) ++s;
-            seq_start = cu[s];
-            seq_end = cu[s + 1];
+    float out[8];
 #pragma unroll
-            for (int i = 0; i < K - 1; ++i)
+    for (int j = 0; j < 8; ++j) {
+        float acc = 0.f;
 #pragma unroll
-                for (int j = 0; j < 8; ++j) win[i][j] = 0.f;
-        }
-        load8(x + b * sxb + t * sxt + c8, win[K - 1]);
-        float out[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            float acc = 0.f;
-#pragma unroll
-            for (int i = 0; i < K; ++i) acc = __fadd_rn(acc, __fmul_rn(wt[j][i], win[i][j]));
-            out[j] = silu_f32(round_bf16(acc));
-        }
-        store8(y + (b * T + t) * C + c8, out);
-#pragma unroll
-        for (int i = 0; i < K - 1; ++i)
-#pragma unroll
-            for (int j = 0; j < 8; ++j) win[i][j] = win[i + 1][j];
+        for (int i = 0; i < K; ++i) acc = __fadd_rn(acc, __fmul_rn(wt[j][i], win[i][j]));
+        out[j] = silu_f32(round_bf16(acc));
     }
+    store8(y + (b * T + t) * C + c8, out);
 }
 
 int launch_conv1d_silu(const void* x, int64_t sxb, int64_t sxt, const void* w, void* y, const int32_t* cu, int64_t B,
                        int64_t T, int64_t C, int K, cudaStream_t s) {
     if (B == 0 || T == 0) return GDN_OK;
     constexpr int threads = 128;
-    dim3 grid((unsigned)((C / 8 + threads - 1) / threads), (unsigned)((T + kConvTokens - 1) / kConvTokens), (unsigned)B);
     const int nseq = cu ? (int)B : 0;  // with cu_seqlens the caller passes the sequence count as B
-    if (cu) grid.z = 1;
+    dim3 grid((unsigned)T, (unsigned)((C / 8 + threads - 1) / threads), cu ? 1u : (unsigned)B);
     auto xp = static_cast<const bf16*>(x);
     auto wp = static_cast<const bf16*>(w);
     auto yp = static_cast<bf16*>(y);
