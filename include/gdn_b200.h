@@ -38,7 +38,8 @@ enum {
     GDN_ERR_LAUNCH = 5,       /* the CUDA launch failed (cudaGetLastError) */
     GDN_ERR_DEVICE_TIMEOUT = 6, /* a bounded device-side wait gave up (see gdn_device_error) */
     GDN_ERR_UNSUPPORTED = 7,  /* a valid but unimplemented configuration (e.g. head dim != 128) */
-    GDN_ERR_SCRATCH = 8       /* the request does not fit the fixed scratch of gdn_decode_layer_noalloc */
+    GDN_ERR_SCRATCH = 8,      /* the request does not fit the fixed scratch of gdn_decode_layer_noalloc */
+    GDN_ERR_WORKSPACE = 9     /* the workspace is missing or smaller than the call needs */
 };
 
 /* Element type codes. */
@@ -90,8 +91,8 @@ GDN_API int gdn_recurrent(const void* q, const void* k, const void* v, int qkv_d
                   float scale, void* stream);
 
 /*
- * Chunked prefill on tcgen05 tensor cores (chunk 64, WY/UT form) with an fp32 state in
- * TMEM. Replaces gated_delta_rule_chunk, model/model.py:289-294 (fla chunk_gated_delta_rule
+ * Chunked prefill on tcgen05 tensor cores (chunk 64, WY/UT form) with an fp32 state.
+ * Replaces gated_delta_rule_chunk, model/model.py:289-294 (fla chunk_gated_delta_rule
  * on CUDA; fp32 eager torch_chunk_gated_delta_rule :242-286). bf16 q, k: [B, T, H, Dk],
  * v: [B, T, HV, Dv] with element strides for the b, t, h dims; g: [B, T, HV] fp32
  * contiguous; beta: [B, T, HV] contiguous, bf16 or fp32; o: [B, T, HV, Dv] bf16 contiguous.
@@ -99,6 +100,9 @@ GDN_API int gdn_recurrent(const void* q, const void* k, const void* v, int qkv_d
  * With cu_seqlens (int32, [batch + 1]) the tensors hold one packed row of `seqlen` tokens
  * and `batch` is the number of sequences N (fla 0.5.x varlen convention); otherwise N =
  * batch. q is L2-normalised and scaled by `scale`, k L2-normalised, in the kernel.
+ * workspace: device memory of at least gdn_chunk_prefill_workspace_size(...) bytes, 16-byte
+ * aligned, for the per-chunk factors handed from the first kernel to the second; it holds
+ * nothing between calls (GDN_ERR_WORKSPACE when missing or too small).
  */
 GDN_API int gdn_chunk_prefill(const void* q, const void* k, const void* v, const float* g, const void* beta,
                               int beta_dtype, const float* initial_state, float* final_state, void* o,
@@ -107,7 +111,15 @@ GDN_API int gdn_chunk_prefill(const void* q, const void* k, const void* v, const
                               int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h,
                               int64_t k_stride_b, int64_t k_stride_t, int64_t k_stride_h,
                               int64_t v_stride_b, int64_t v_stride_t, int64_t v_stride_h,
-                              float scale, void* stream);
+                              float scale, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Workspace bytes gdn_chunk_prefill needs for the same batch, seqlen and value_heads
+ * (packed != 0 when cu_seqlens is passed, batch then being the number of sequences):
+ * 33,792 bytes per (value head, chunk slot); B * ceil(T/64) slots, or ceil(T/64) + N packed.
+ * No counterpart in the reference (fla allocates its intermediates inside the call).
+ */
+GDN_API size_t gdn_chunk_prefill_workspace_size(int64_t batch, int64_t seqlen, int64_t value_heads, int packed);
 
 /*
  * Rollback by snapshot: for each row b with accepted[b] >= 1, copy snapshot

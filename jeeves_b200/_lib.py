@@ -13,13 +13,15 @@ import threading
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "_lib", "libgdn_b200.so")
 
-OK, ERR_SHAPE, ERR_DTYPE, ERR_ALIGN, ERR_NULL, ERR_LAUNCH, ERR_DEVICE_TIMEOUT, ERR_UNSUPPORTED, ERR_SCRATCH = range(9)
+(OK, ERR_SHAPE, ERR_DTYPE, ERR_ALIGN, ERR_NULL, ERR_LAUNCH, ERR_DEVICE_TIMEOUT, ERR_UNSUPPORTED, ERR_SCRATCH,
+ ERR_WORKSPACE) = range(10)
 F32, BF16 = 0, 1
 
 _p = ctypes.c_void_p
 _i64 = ctypes.c_int64
 _i32 = ctypes.c_int
 _f32 = ctypes.c_float
+_sz = ctypes.c_size_t
 
 # name -> argument types, in declaration order of include/gdn_b200.h
 SIGNATURES: dict[str, list] = {
@@ -30,7 +32,8 @@ SIGNATURES: dict[str, list] = {
                       _i64, _i64, _i64, _i64, _i64, _i64,
                       _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _p],
     "gdn_chunk_prefill": [_p, _p, _p, _p, _p, _i32, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64,
-                          _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _p],
+                          _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _p, _sz, _p],
+    "gdn_chunk_prefill_workspace_size": [_i64, _i64, _i64, _i32],
     "gdn_snapshot_commit": [_p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p],
     "gdn_conv1d_silu": [_p, _i64, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _p],
     "gdn_conv1d_silu_step": [_p, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _p],
@@ -41,6 +44,8 @@ SIGNATURES: dict[str, list] = {
     "gdn_decode_layer_noalloc": [_p, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                                  _f32, _f32, _p],
 }
+
+RESTYPES = {"gdn_status_string": ctypes.c_char_p, "gdn_chunk_prefill_workspace_size": ctypes.c_size_t}
 
 _lock = threading.Lock()
 _lib = None
@@ -64,7 +69,7 @@ def load() -> ctypes.CDLL:
         for name, args in SIGNATURES.items():
             fn = getattr(lib, name)
             fn.argtypes = args
-            fn.restype = ctypes.c_char_p if name == "gdn_status_string" else ctypes.c_int
+            fn.restype = RESTYPES.get(name, ctypes.c_int)
         _lib = lib
         return lib
 
@@ -78,6 +83,6 @@ def check(status: int, what: str) -> None:
     if status == OK:
         return
     text = f"{what}: {status_text(status)} (status {status})"
-    if status in (ERR_SHAPE, ERR_DTYPE, ERR_ALIGN, ERR_NULL, ERR_UNSUPPORTED, ERR_SCRATCH):
+    if status in (ERR_SHAPE, ERR_DTYPE, ERR_ALIGN, ERR_NULL, ERR_UNSUPPORTED, ERR_SCRATCH, ERR_WORKSPACE):
         raise ValueError(text)
     raise RuntimeError(text)

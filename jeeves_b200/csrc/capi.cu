@@ -7,7 +7,7 @@ using namespace gdn;
 
 namespace {
 
-constexpr int kAbiVersion = 1;
+constexpr int kAbiVersion = 2;
 
 inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
 
@@ -36,6 +36,7 @@ const char* gdn_status_string(int status) {
         case GDN_ERR_DEVICE_TIMEOUT: return "a bounded device-side wait timed out";
         case GDN_ERR_UNSUPPORTED: return "unsupported configuration";
         case GDN_ERR_SCRATCH: return "request larger than the fixed scratch of the no-allocation entry point";
+        case GDN_ERR_WORKSPACE: return "workspace missing or smaller than gdn_chunk_prefill_workspace_size";
         default: return "unknown status";
     }
 }
@@ -106,7 +107,8 @@ int gdn_chunk_prefill(const void* q, const void* k, const void* v, const float* 
                       int64_t batch, int64_t seqlen, int64_t key_heads, int64_t value_heads, int64_t head_dim_k,
                       int64_t head_dim_v, int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h,
                       int64_t k_stride_b, int64_t k_stride_t, int64_t k_stride_h, int64_t v_stride_b,
-                      int64_t v_stride_t, int64_t v_stride_h, float scale, void* stream) {
+                      int64_t v_stride_t, int64_t v_stride_h, float scale, void* workspace, size_t workspace_bytes,
+                      void* stream) {
     if (!known_dtype(beta_dtype)) return GDN_ERR_DTYPE;
     if (batch < 0 || seqlen < 0 || key_heads <= 0 || value_heads <= 0 || value_heads % key_heads) return GDN_ERR_SHAPE;
     if (batch > 65535 || value_heads > 512) return GDN_ERR_SHAPE;
@@ -128,7 +130,15 @@ int gdn_chunk_prefill(const void* q, const void* k, const void* v, const float* 
     a.ksb = k_stride_b; a.kst = k_stride_t; a.ksh = k_stride_h;
     a.vsb = v_stride_b; a.vst = v_stride_t; a.vsh = v_stride_h;
     a.scale = scale;
+    a.workspace = workspace;
+    a.workspace_bytes = workspace_bytes;
+    if (workspace && !aligned16(workspace)) return GDN_ERR_ALIGN;
     return launch_chunk(a, as_stream(stream));
+}
+
+size_t gdn_chunk_prefill_workspace_size(int64_t batch, int64_t seqlen, int64_t value_heads, int packed) {
+    if (batch < 0 || seqlen < 0 || value_heads <= 0) return 0;
+    return chunk_workspace_bytes(packed ? 1 : batch, seqlen, batch, packed != 0, value_heads);
 }
 
 int gdn_snapshot_commit(float* state, const float* snapshots, const int64_t* accepted, int64_t batch, int64_t seqlen,

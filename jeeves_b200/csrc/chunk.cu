@@ -4,8 +4,6 @@
 // fla's chunk_gated_delta_rule on CUDA, model/model.py:289-294), with varlen packing
 // through cu_seqlens as in fla 0.5.x.
 //
-// One CTA owns one (sequence, value head, slice of VS = 64 value columns) and walks the
-// sequence's chunks in order with its fp32 state slice S [128 x VS] resident in TMEM.
 // Per chunk of 64 tokens (gc = cumulative log decay, rk / rq = inverse L2 norms of the raw
 // bf16 k / q rows, the q scale folded into rq):
 //   KK = K K^T, QK = Q K^T                                 tcgen05, raw bf16 operands
@@ -17,20 +15,21 @@
 //   o  = rq e^gc O1 + P VN
 //   S <- e^{g_last} S + K^T diag(rk e^{g_last-gc}) VN      VN split into bf16 hi + lo
 // Rows past the end of a sequence get beta = 0 and g = 0, which makes them identity steps.
+// The intra-chunk output is folded into the inter-chunk accumulator: with eq_i = rq_i e^{gc_i},
+// o_i = eq_i (Q S + P' VN)_i where P'_ij = rk_j QK_ij e^{-gc_j}; e^{gc_i - gc_j} is formed as
+// e^{gc_i} e^{-gc_j} while the chunk's decay stays above 2^-100 and element by element otherwise.
 //
-// Implementation notes:
-//   * the intra-chunk output is folded into the inter-chunk accumulator: with
-//     eq_i = rq_i e^{gc_i}, o_i = eq_i (Q S + P' VN)_i where P' = P / eq (row-wise), i.e.
-//     P'_ij = rk_j QK_ij e^{-gc_j}; e^{gc_i - gc_j} is formed as e^{gc_i} e^{-gc_j} while the
-//     chunk's decay stays above 2^-100 and element by element otherwise;
-//   * the chain keeps its fp32 state rows in registers; each chunk's update K^T(...) lands in
-//     a fresh TMEM accumulator and is added as S <- e^{g_last} S + dS.
-//
-// Warp roles (384 threads): warp 0 loads tiles (TMA) and gates; warps 4-7 ("prep") build the
-// chunk-local factors P', X, W of chunk c+1 and issue their own MMAs, while warps 8-11
-// ("chain") advance the state through chunk c and issue theirs. The roles hand buffers to
-// each other through mbarriers; K/Q/V tiles, P', W and the chain's TMEM accumulators are
-// double buffered by chunk parity.
+// Two kernels:
+//   chunk_factor_kernel  one CTA per (value head, chunk), all chunks at once: everything that
+//                        does not depend on the state (norms, gates, P', X, W) goes into a
+//                        33 KB record per (value head, chunk) in a caller-provided workspace,
+//                        laid out as the scan kernel's shared-memory stage.
+//   chunk_scan_kernel    one CTA per (sequence, value head, 64-column slice of the state),
+//                        walking the chunks in order with the fp32 state slice in registers.
+//                        A loader warp streams K/Q/V tiles (TMA) and records (bulk copy); the
+//                        chain warpgroup runs U, VN = U - W S, dS = K^T VN and the state update;
+//                        an epilogue warpgroup drains O = Q S + P' VN to global memory, so the
+//                        chain's critical path per chunk is two MMA round trips and two readouts.
 //
 // Every wait is bounded (sm100.cuh): a wait that gives up raises the device error word and
 // the CTA's abort flag; every role then leaves its loop, the loader waits for the copies it
@@ -44,87 +43,28 @@ namespace gdn {
 
 using namespace sm100;
 
-struct ChunkParams {
-    CUtensorMap tm_q;  // 4-D (128, H, T, B) bf16, box (64, 1, 64, 1), 128-byte swizzle
-    CUtensorMap tm_k;
-    CUtensorMap tm_v;  // 4-D (128, HV, T, B)
-    const float* g;    // [B, T, HV]
-    const void* beta;  // [B, T, HV] bf16 or fp32
-    int beta_f32;
-    const float* h0;   // [N, HV, 128, 128] or null
-    float* ht;         // [N, HV, 128, 128] or null
-    bf16* o;           // [B, T, HV, 128]
-    const int32_t* cu_seqlens;
-    int64_t T;
-    int HV, rep;
-    float scale;
-};
-
-constexpr int kVS = 64;                       // value columns per CTA
-constexpr uint32_t kPanel = 64 * 128;         // one 128-byte panel of 64 rows
+constexpr int kVS = 64;                       // value columns per scan CTA
+constexpr uint32_t kPanel = 64 * 128;         // one 128-byte-swizzled panel of 64 rows
 constexpr int kAfStride = 68;                 // fp32 row stride of the inverse workspace
 
-// dynamic shared memory layout (byte offsets, 1024-aligned where TMA or MMA reads)
-struct Smem {
-    static constexpr uint32_t K = 0;                         // [2] K tiles: two d-panels each
-    static constexpr uint32_t Q = K + 2 * 2 * kPanel;        // [2] Q tiles
-    static constexpr uint32_t V = Q + 2 * 2 * kPanel;        // [2] V tiles: one panel each
-    static constexpr uint32_t PM = V + 2 * kPanel;           // [2] P' (bf16, K-major)
-    static constexpr uint32_t WB = PM + 2 * kPanel;          // [2] W (bf16, K-major, two d-panels)
-    static constexpr uint32_t AU = WB + 2 * 2 * kPanel;      // X diag(beta); E32 during the inverse
-    static constexpr uint32_t AW = AU + kPanel;              // X diag(cw); D32 during the inverse
-    static constexpr uint32_t T2 = AW + kPanel;              // E32 D32 (bf16, MN-major)
-    static constexpr uint32_t SB = T2 + kPanel;              // S^T [v][d] bf16, two d-panels
-    static constexpr uint32_t VHI = SB + 2 * kPanel;         // hi(ce VN) [tok][v]
-    static constexpr uint32_t VLO = VHI + kPanel;            // lo(ce VN)
-    static constexpr uint32_t VBF = VLO + kPanel;            // VN [tok][v]
-    static constexpr uint32_t AF = VBF + kPanel;             // fp32 [64][kAfStride]
-    static constexpr uint32_t END = AF + 64 * kAfStride * 4;
-    static constexpr uint32_t BYTES = END + 1024;            // + alignment slack
+// ---- per-(value head, chunk) record, produced by the factor kernel, consumed by the scan kernel
+struct RecScalars {
+    float ce[64];  // rk 2^(glast - gcl)
+    float eq[64];  // rq 2^max(gcl, -100)
+    float dec;     // 2^glast
+    float pad[127];
 };
+static_assert(sizeof(RecScalars) == 1024, "record scalars are one 1 KB block");
 
-struct Bars {
-    uint64_t kqv_full[2], kqv_empty[2], gates_full[2], gates_empty[2];
-    uint64_t acc_kq, acc_t2, acc_x, acc_wu[2], acc_vn[2], acc_s, drain_prep, drain_chain;
-    uint64_t wb_ready, o_free[2];
-};
-
-struct Shared {
-    Bars bar;
-    uint32_t tmem_base;
-    int abort;
-    // gates ring, written by the loader warp
-    float graw[2][64];
-    float braw[2][64];
-    // prep scalars of the chunk being prepared
-    float gcl[64];   // cumulative log2 decay
-    float beta[64];
-    float rk[64];    // 1/|k| (0 past the end)
-    float rq[64];    // scale/|q|
-    float rowA[64];  // beta rk 2^gcl
-    float colS[64];  // rk 2^-gcl
-    float cw[64];    // beta rk 2^gcl
-    float mx[64];    // max(gcl, -100)
-    float scan_carry;
-    int fast;        // every gcl of the chunk is above -100: product-form decay
-    // chain scalars per chunk parity
-    float ce[2][64];  // rk 2^(glast - gcl)
-    float eq[2][64];  // rq 2^mx
-    float dec[2];     // 2^glast
-};
+constexpr uint32_t kRecW = 0;               // W: bf16, K-major, two d-panels (rows = tokens)
+constexpr uint32_t kRecXB = 2 * kPanel;     // X diag(beta): bf16, K-major
+constexpr uint32_t kRecPM = 3 * kPanel;     // P': bf16, K-major
+constexpr uint32_t kRecSc = 4 * kPanel;     // RecScalars
+constexpr uint32_t kRecBytes = kRecSc + sizeof(RecScalars);
 
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kDecayFloor = -100.f;     // log2 floor of the product-form decay factors
-constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColDS = 0;           // dS = K^T (hi + lo), all lanes, 64 columns
-constexpr uint32_t kColR = 64;           // per-parity accumulators: 64 + 128 * parity
-constexpr uint32_t kColKQ = 320;         // KK (lanes A) / QK (lanes B)
-constexpr uint32_t kColT2 = 384;         // T2 (lanes A) / X_LL (lanes B)
-constexpr uint32_t kHalfB = 16u << 16;   // lane offset of the second M=64 accumulator
-// inside a parity region R: W[:, 0:64] lanes A and W[:, 64:128] lanes B at R; U -> VN lanes A
-// and O = Q S + P' VN lanes B at R + 64.
-
-enum : uint32_t { kBarPrep = 1, kBarChain = 2 };
+constexpr uint32_t kHalfB = 16u << 16;    // lane offset of the second M=64 accumulator
 
 // 8 fp32 values -> one 16-byte bf16 chunk of a swizzled panel row.
 __device__ __forceinline__ void put_chunk(uint8_t* panel, uint32_t row, uint32_t chunk, const float* v) {
@@ -155,11 +95,483 @@ __device__ __forceinline__ float sum_squares_row(const uint8_t* tile, uint32_t r
 
 __device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
 
-__global__ void __launch_bounds__(384, 1) chunk_prefill_kernel(const __grid_constant__ ChunkParams p) {
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+    return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+// =========================================================================================
+// factor kernel
+// =========================================================================================
+struct FactorParams {
+    CUtensorMap tm_q;  // 4-D (128, H, T, B) bf16, box (64, 1, 64, 1), 128-byte swizzle
+    CUtensorMap tm_k;
+    const float* g;    // [B, T, HV]
+    const void* beta;  // [B, T, HV] bf16 or fp32
+    int beta_f32;
+    const int32_t* cu_seqlens;
+    uint8_t* records;  // [slots, HV] records
+    int64_t T;
+    int nseq, ncd;     // sequences; chunks per row of the dense layout
+    int HV, rep;
+    float scale;
+};
+
+struct FSmem {
+    static constexpr uint32_t K = 0;                   // K tile (two d-panels); W staging at the end
+    static constexpr uint32_t Q = K + 2 * kPanel;      // Q tile; P' and T2 once KK / QK are done
+    static constexpr uint32_t PM = Q;
+    static constexpr uint32_t T2 = Q + kPanel;         // E32 D32 (bf16, MN-major)
+    static constexpr uint32_t AU = Q + 2 * kPanel;     // X diag(beta); E32 during the inverse
+    static constexpr uint32_t AW = AU + kPanel;        // X diag(cw); D32 during the inverse
+    static constexpr uint32_t AF = AW + kPanel;        // fp32 [64][kAfStride]
+    static constexpr uint32_t END = AF + 64 * kAfStride * 4;
+    static constexpr uint32_t BYTES = END + 1024;      // + alignment slack
+};
+
+struct FShared {
+    uint64_t tma, acc_kq, acc_t2, acc_x, acc_w, drain;
+    uint32_t tmem_base;
+    // read with 16-byte vector loads: every array starts on a 16-byte boundary
+    alignas(16) float graw[64];
+    alignas(16) float braw[64];
+    alignas(16) float gcl[64];   // cumulative log2 decay
+    alignas(16) float beta[64];
+    alignas(16) float rk[64];    // 1/|k| (0 past the end)
+    alignas(16) float rq[64];    // scale/|q|
+    alignas(16) float rowA[64];  // beta rk 2^gcl
+    alignas(16) float colS[64];  // rk 2^-max(gcl, -100)
+    alignas(16) float cw[64];    // beta rk 2^gcl
+    alignas(16) float mx[64];    // max(gcl, -100)
+    float scan_carry;
+    int fast;        // every gcl of the chunk is above -100: product-form decay
+    alignas(128) RecScalars rs;
+};
+static_assert(offsetof(FShared, colS) % 16 == 0 && offsetof(FShared, beta) % 16 == 0 &&
+                  offsetof(FShared, cw) % 16 == 0 && offsetof(FShared, rs) % 16 == 0,
+              "vector-loaded arrays are 16-byte aligned");
+
+constexpr uint32_t kFactorTmemCols = 128;
+constexpr uint32_t kColKQ = 0;    // KK (lanes A) / QK (lanes B); W halves (lanes A / B) later
+constexpr uint32_t kColT2 = 64;   // T2 (lanes A) / X_LL (lanes B)
+enum : uint32_t { kBarFactor = 1, kBarChain = 2, kBarEpi = 3 };
+
+// The slot of chunk c of sequence n: n * ncd + c for the dense layout; cu[n] / 64 + n + c for
+// a packed batch. Slots of different sequences never collide because a sequence of length L
+// starting at token b has at most floor((b + L) / 64) - floor(b / 64) + 1 chunks.
+__global__ void __launch_bounds__(128, 3) chunk_factor_kernel(const __grid_constant__ FactorParams p) {
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    __shared__ Shared sh;
-    Bars& bar = sh.bar;
+    uint8_t* sm = align1024(smem_raw);
+    __shared__ FShared sh;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int hv = (int)(blockIdx.x % (unsigned)p.HV);
+    const int64_t slot = blockIdx.x / (unsigned)p.HV;
+    const int h = hv / p.rep;
+    int64_t bos = 0, len = p.T, brow = 0, c = 0;
+    if (p.cu_seqlens == nullptr) {
+        brow = slot / p.ncd;
+        c = slot % p.ncd;
+    } else {
+        int lo = 0, hi = p.nseq - 1;  // last sequence whose first slot is <= slot
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (p.cu_seqlens[mid] / 64 + (int64_t)mid <= slot) lo = mid;
+            else hi = mid - 1;
+        }
+        bos = p.cu_seqlens[lo];
+        len = p.cu_seqlens[lo + 1] - bos;
+        c = slot - (bos / 64 + lo);
+        if (c < 0 || 64 * c >= len) return;  // a slot no chunk maps to (uniform over the CTA)
+    }
+    const int t = (int)(bos + 64 * c);
+    const int nvalid = (int)(len - 64 * c < 64 ? len - 64 * c : 64);
+    const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
+    const int half_row = 16 * warp + (lane & 15);
+    const bool lanes_a = lane < 16;
+    const int pt = tid;
+    uint8_t* kt = sm + FSmem::K;
+    uint8_t* qt = sm + FSmem::Q;
+    float* Af = reinterpret_cast<float*>(sm + FSmem::AF);
+
+    if (tid == 0) {
+        mbar_init(&sh.tma, 1);
+        mbar_init(&sh.acc_kq, 1);
+        mbar_init(&sh.acc_t2, 1);
+        mbar_init(&sh.acc_x, 1);
+        mbar_init(&sh.acc_w, 1);
+        mbar_init(&sh.drain, 1);
+        fence_mbar_init();
+        mbar_arrive_expect_tx(&sh.tma, 4 * kPanel);
+        tma_load_4d(kt, &p.tm_k, &sh.tma, 0, h, t, (int)brow);
+        tma_load_4d(kt + kPanel, &p.tm_k, &sh.tma, 64, h, t, (int)brow);
+        tma_load_4d(qt, &p.tm_q, &sh.tma, 0, h, t, (int)brow);
+        tma_load_4d(qt + kPanel, &p.tm_q, &sh.tma, 64, h, t, (int)brow);
+    }
+    if (warp == 0) {
+        tmem_alloc(&sh.tmem_base, kFactorTmemCols);
+        tmem_relinquish();
+    }
+    if (pt < 64) {
+        float gv = 0.f, bv = 0.f;
+        if (pt < nvalid) {
+            const int64_t gi = (brow * p.T + t + pt) * p.HV + hv;
+            gv = p.g[gi];
+            bv = p.beta_f32 ? static_cast<const float*>(p.beta)[gi] : to_f32(static_cast<const bf16*>(p.beta)[gi]);
+        }
+        sh.graw[pt] = gv;
+        sh.braw[pt] = bv;
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tb = sh.tmem_base;
+    const uint32_t id_sq = make_idesc(64, 64, kFmtBF16, false, false);
+    const uint32_t id_mn64 = make_idesc(64, 64, kFmtBF16, false, true);
+    bool tiles_landed = false, mma_issued = false;
+
+    do {
+        tiles_landed = named_sync_all(kBarFactor, 128, mbar_wait(&sh.tma, 0, kSiteTmaLoad));
+        if (!tiles_landed) break;
+        if (pt == 0) {  // KK, QK; the norms below overlap them
+            tc_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+                const uint32_t po = (kk >> 2) * kPanel, ko = (kk & 3) * 32;
+                const uint64_t bd = sdesc_kmajor(kt + po, ko);
+                mma_f16(tb + kColKQ, sdesc_kmajor(kt + po, ko), bd, id_sq, kk > 0);
+                mma_f16(tb + kColKQ + kHalfB, sdesc_kmajor(qt + po, ko), bd, id_sq, kk > 0);
+            }
+            mma_commit(&sh.acc_kq);
+            mma_issued = true;
+        }
+        // ---- gates (scan in log2 units) and inverse norms
+        float gsum = 0.f;
+        if (pt < 64) {
+            float x = sh.graw[pt] * kLog2e;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const float y = __shfl_up_sync(0xffffffffu, x, o);
+                if (lane >= o) x += y;
+            }
+            gsum = x;
+            if (pt == 31) sh.scan_carry = x;
+            sh.beta[pt] = sh.braw[pt];
+            const float inv = rsqrtf(sum_squares_row(kt, pt) + 1e-6f);
+            sh.rk[pt] = pt < nvalid ? inv : 0.f;
+        } else {
+            const int r = pt - 64;
+            sh.rq[r] = rsqrtf(sum_squares_row(qt, r) + 1e-6f) * p.scale;
+        }
+        named_sync(kBarFactor, 128);
+        if (pt < 64) sh.gcl[pt] = pt >= 32 ? gsum + sh.scan_carry : gsum;
+        named_sync(kBarFactor, 128);
+        if (pt < 64) {
+            const float gl = sh.gcl[pt];
+            const float glast = sh.gcl[63];
+            const float rk = sh.rk[pt], bt = sh.beta[pt], rq = sh.rq[pt];
+            const float mxv = fmaxf(gl, kDecayFloor);
+            const float e_gl = exp2f(gl);
+            sh.rowA[pt] = bt * rk * e_gl;
+            sh.colS[pt] = rk * exp2f(-fmaxf(gl, kDecayFloor));
+            sh.cw[pt] = bt * rk * e_gl;
+            sh.mx[pt] = mxv;
+            sh.rs.ce[pt] = rk * exp2f(glast - gl);
+            sh.rs.eq[pt] = rq * exp2f(mxv);
+            if (pt == 0) {
+                sh.rs.dec = exp2f(glast);
+                sh.fast = glast > kDecayFloor;
+            }
+        }
+        named_sync(kBarFactor, 128);
+        // ---- A (fp32 rows, from KK in lanes A) and P' (bf16 rows, from QK in lanes B)
+        if (!named_sync_all(kBarFactor, 128, mbar_wait(&sh.acc_kq, 0, kSiteMma))) break;
+        tc_fence_after();
+        {
+            const int i = half_row;
+            const int lim = lanes_a ? i : i + 1;  // columns kept: j < lim
+            const bool fast = sh.fast;
+            const float rs_fast = lanes_a ? sh.rowA[i] : 1.f;
+            const float gli = sh.gcl[i];
+            const float rs_slow = lanes_a ? sh.beta[i] * sh.rk[i] : 1.f;
+            const float shift = lanes_a ? 0.f : sh.mx[i];
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                float r[32];
+                tmem_ld32_wait(tb + kColKQ + lane_base + 32 * half, r);
+                if (fast) {
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4) {
+                        const float4 cs = ld4(&sh.colS[32 * half + j]);
+                        r[j] *= rs_fast * cs.x;
+                        r[j + 1] *= rs_fast * cs.y;
+                        r[j + 2] *= rs_fast * cs.z;
+                        r[j + 3] *= rs_fast * cs.w;
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const int col = 32 * half + j;
+                        const float e = exp2f(fminf(gli - sh.gcl[col] - shift, 0.f));
+                        r[j] *= rs_slow * sh.rk[col] * e;
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < 32; ++j) r[j] = (32 * half + j) < lim ? r[j] : 0.f;
+                if (lanes_a) {
+                    float* arow = Af + i * kAfStride + 32 * half;
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4)
+                        *reinterpret_cast<float4*>(arow + j) = make_float4(r[j], r[j + 1], r[j + 2], r[j + 3]);
+                } else {
+#pragma unroll
+                    for (int ch = 0; ch < 4; ++ch) put_chunk(sm + FSmem::PM, i, 4 * half + ch, r + 8 * ch);
+                }
+            }
+        }
+        tc_fence_before();
+        named_sync(kBarFactor, 128);
+        // ---- inverses of the four 16x16 diagonal blocks of I + A (two partial sums per row)
+        {
+            float x[16];
+            const int b = pt >> 4, col = pt & 15;
+            if (pt < 64) {
+                const float* blk = Af + 16 * b * kAfStride + 16 * b;
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+                    for (int j = 0; j < i; ++j) {
+                        if (j & 1) a1 = fmaf(blk[i * kAfStride + j], x[j], a1);
+                        else a0 = fmaf(blk[i * kAfStride + j], x[j], a0);
+                    }
+                    x[i] = (i == col) ? 1.f : (i > col ? -(a0 + a1) : 0.f);
+                }
+            }
+            named_sync(kBarFactor, 128);
+            if (pt < 64) {
+                float* blk = Af + 16 * b * kAfStride + 16 * b;
+#pragma unroll
+                for (int i = 0; i < 16; ++i) blk[i * kAfStride + col] = x[i];
+            }
+        }
+        named_sync(kBarFactor, 128);
+        // ---- 16 -> 32 merge inside each 32-block: X10 = -X11 (A10 X00)
+        {
+            const int blk = pt >> 6, e = pt & 63;
+            const int i = e >> 2, j0 = (e & 3) * 4, r0 = 32 * blk;
+            float t4[4] = {0.f, 0.f, 0.f, 0.f};
+            const float* arow = Af + (r0 + 16 + i) * kAfStride + r0;
+#pragma unroll
+            for (int kx = 0; kx < 16; kx += 4) {
+                const float4 a = ld4(arow + kx);
+                const float av[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const float4 xv = ld4(&Af[(r0 + kx + q) * kAfStride + r0 + j0]);
+                    t4[0] = fmaf(av[q], xv.x, t4[0]); t4[1] = fmaf(av[q], xv.y, t4[1]);
+                    t4[2] = fmaf(av[q], xv.z, t4[2]); t4[3] = fmaf(av[q], xv.w, t4[3]);
+                }
+            }
+            named_sync(kBarFactor, 128);
+            *reinterpret_cast<float4*>(&Af[(r0 + 16 + i) * kAfStride + r0 + j0]) = make_float4(t4[0], t4[1], t4[2], t4[3]);
+            named_sync(kBarFactor, 128);
+            float x4[4] = {0.f, 0.f, 0.f, 0.f};
+            const float* xrow = Af + (r0 + 16 + i) * kAfStride + r0 + 16;
+#pragma unroll
+            for (int kx = 0; kx < 16; kx += 4) {
+                const float4 a = ld4(xrow + kx);
+                const float av[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const float4 tv = ld4(&Af[(r0 + 16 + kx + q) * kAfStride + r0 + j0]);
+                    x4[0] = fmaf(av[q], tv.x, x4[0]); x4[1] = fmaf(av[q], tv.y, x4[1]);
+                    x4[2] = fmaf(av[q], tv.z, x4[2]); x4[3] = fmaf(av[q], tv.w, x4[3]);
+                }
+            }
+            named_sync(kBarFactor, 128);
+            *reinterpret_cast<float4*>(&Af[(r0 + 16 + i) * kAfStride + r0 + j0]) =
+                make_float4(-x4[0], -x4[1], -x4[2], -x4[3]);
+        }
+        named_sync(kBarFactor, 128);
+        // ---- bf16 operands of the 32 -> 64 merge: E32 (lower-left block of A) and D32
+        {
+            const int i = pt & 63, hf = pt >> 6;  // two threads per row, 32 columns each
+            const float* arow = Af + i * kAfStride + 32 * hf;
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) {
+                float e8[8], d8[8];
+                const float4 a0 = ld4(arow + 8 * cc), a1 = ld4(arow + 8 * cc + 4);
+                const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    const int j = 32 * hf + 8 * cc + q;
+                    e8[q] = (i >= 32 && j < 32) ? av[q] : 0.f;
+                    d8[q] = ((i >> 5) == (j >> 5) && j <= i) ? av[q] : 0.f;
+                }
+                put_chunk(sm + FSmem::AU, i, 4 * hf + cc, e8);
+                put_chunk(sm + FSmem::AW, i, 4 * hf + cc, d8);
+            }
+        }
+        fence_async_smem();
+        tc_fence_before();
+        named_sync(kBarFactor, 128);
+        if (pt == 0) {  // T2 = E32 D32 (lanes A)
+            tc_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+                mma_f16(tb + kColT2, sdesc_kmajor(sm + FSmem::AU, kk * 32),
+                        sdesc_mnmajor(sm + FSmem::AW + kk * 2048, kPanel), id_mn64, kk > 0);
+            mma_commit(&sh.acc_t2);
+        }
+        // ---- T2 -> bf16 operand
+        if (!named_sync_all(kBarFactor, 128, mbar_wait(&sh.acc_t2, 0, kSiteMma))) break;
+        tc_fence_after();
+        {
+            float r[64];
+            tmem_ld64_wait(tb + kColT2 + lane_base, r);
+            if (lanes_a)
+#pragma unroll
+                for (int ch = 0; ch < 8; ++ch) put_chunk(sm + FSmem::T2, half_row, ch, r + 8 * ch);
+        }
+        fence_async_smem();
+        tc_fence_before();
+        named_sync(kBarFactor, 128);
+        if (pt == 0) {  // X_LL = D32 T2 (lanes B)
+            tc_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+                mma_f16(tb + kColT2 + kHalfB, sdesc_kmajor(sm + FSmem::AW, kk * 32),
+                        sdesc_mnmajor(sm + FSmem::T2 + kk * 2048, kPanel), id_mn64, kk > 0);
+            mma_commit(&sh.acc_x);
+        }
+        // ---- X = D32 - X_LL; two column-scaled bf16 copies: X diag(beta) (record) and X diag(cw)
+        // (W product). Row i is shared by lanes l (columns 32-63) and l + 16 (columns 0-31, whose
+        // TMEM lanes hold X_LL).
+        if (!named_sync_all(kBarFactor, 128, mbar_wait(&sh.acc_x, 0, kSiteMma))) break;
+        tc_fence_after();
+        {
+            const int i = half_row;
+            const int cbase = lanes_a ? 32 : 0;
+            float r[32];
+            tmem_ld32_wait(tb + kColT2 + lane_base, r);  // lanes B: X_LL columns 0-31
+            const float* arow = Af + i * kAfStride + cbase;
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) {
+                float xu[8], xw[8];
+                const float4 a0 = ld4(arow + 8 * cc), a1 = ld4(arow + 8 * cc + 4);
+                const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+                const float4 b0 = ld4(&sh.beta[cbase + 8 * cc]), b1 = ld4(&sh.beta[cbase + 8 * cc + 4]);
+                const float4 w0 = ld4(&sh.cw[cbase + 8 * cc]), w1 = ld4(&sh.cw[cbase + 8 * cc + 4]);
+                const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+                const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    const int col = cbase + 8 * cc + q;
+                    float xv;
+                    if (col > i) xv = 0.f;
+                    else if (!lanes_a && i >= 32) xv = -r[8 * cc + q];
+                    else xv = av[q];
+                    xu[q] = xv * bv[q];
+                    xw[q] = xv * wv[q];
+                }
+                put_chunk(sm + FSmem::AU, i, cbase / 8 + cc, xu);
+                put_chunk(sm + FSmem::AW, i, cbase / 8 + cc, xw);
+            }
+        }
+        fence_async_smem();
+        tc_fence_before();
+        named_sync(kBarFactor, 128);
+        if (pt == 0) {  // W[:, 0:64] (lanes A) and W[:, 64:128] (lanes B) = (X diag(cw)) K
+            tc_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+                const uint64_t ad = sdesc_kmajor(sm + FSmem::AW, kk * 32);
+                mma_f16(tb + kColKQ, ad, sdesc_mnmajor(kt + kk * 2048, kPanel), id_mn64, kk > 0);
+                mma_f16(tb + kColKQ + kHalfB, ad, sdesc_mnmajor(kt + kPanel + kk * 2048, kPanel), id_mn64, kk > 0);
+            }
+            mma_commit(&sh.acc_w);
+        }
+        // ---- W -> bf16 (lanes A: d 0-63, lanes B: d 64-127) into the dead K tile, then the
+        // record goes out with four bulk stores
+        if (!named_sync_all(kBarFactor, 128, mbar_wait(&sh.acc_w, 0, kSiteMma))) break;
+        tc_fence_after();
+        {
+            float r[64];
+            tmem_ld64_wait(tb + kColKQ + lane_base, r);
+            uint8_t* panel = kt + (lanes_a ? 0 : kPanel);
+#pragma unroll
+            for (int ch = 0; ch < 8; ++ch) put_chunk(panel, half_row, ch, r + 8 * ch);
+        }
+        fence_async_smem();
+        named_sync(kBarFactor, 128);
+        if (pt == 0) {
+            uint8_t* rec = p.records + ((int64_t)slot * p.HV + hv) * (int64_t)kRecBytes;
+            bulk_store(rec + kRecW, kt, 2 * kPanel);
+            bulk_store(rec + kRecXB, sm + FSmem::AU, kPanel);
+            bulk_store(rec + kRecPM, sm + FSmem::PM, kPanel);
+            bulk_store(rec + kRecSc, &sh.rs, sizeof(RecScalars));
+            bulk_commit();
+            bulk_wait_all();
+        }
+    } while (false);
+
+    if (pt == 0) {
+        if (!tiles_landed) mbar_wait(&sh.tma, 0, kSiteDrain);  // the tiles must land before exit
+        if (mma_issued) {
+            mma_commit(&sh.drain);
+            mbar_wait(&sh.drain, 0, kSiteDrain);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tb, kFactorTmemCols);
+}
+
+// =========================================================================================
+// scan kernel
+// =========================================================================================
+struct ScanParams {
+    CUtensorMap tm_q;  // 4-D (128, H, T, B) bf16, box (64, 1, 64, 1), 128-byte swizzle
+    CUtensorMap tm_k;
+    CUtensorMap tm_v;  // 4-D (128, HV, T, B)
+    const float* h0;   // [N, HV, 128, 128] or null
+    float* ht;         // [N, HV, 128, 128] or null
+    bf16* o;           // [B, T, HV, 128]
+    const int32_t* cu_seqlens;
+    const uint8_t* records;
+    int64_t T;
+    int ncd;
+    int HV, rep;
+};
+
+struct SSmem {
+    static constexpr uint32_t K = 0;                         // [2] K tiles: two d-panels each
+    static constexpr uint32_t Q = K + 2 * 2 * kPanel;        // [2] Q tiles
+    static constexpr uint32_t V = Q + 2 * 2 * kPanel;        // [2] V slices: one panel each
+    static constexpr uint32_t REC = V + 2 * kPanel;          // [2] records
+    static constexpr uint32_t SB = REC + 2 * kRecBytes;      // S [d][v] bf16, MN-major, 128 rows
+    static constexpr uint32_t VHI = SB + 2 * kPanel;         // hi(ce VN) [tok][v]
+    static constexpr uint32_t VLO = VHI + kPanel;            // lo(ce VN)
+    static constexpr uint32_t VBF = VLO + kPanel;            // VN [tok][v]
+    static constexpr uint32_t END = VBF + kPanel;
+    static constexpr uint32_t BYTES = END + 1024;            // + alignment slack
+};
+static_assert(SSmem::REC % 1024 == 0 && kRecBytes % 1024 == 0 && SSmem::SB % 1024 == 0, "swizzle atoms");
+
+struct SShared {
+    uint64_t full[2], empty[2], acc_vn[2], acc_s, acc_o[2], o_free[2], drain;
+    uint32_t tmem_base;
+    int abort;
+};
+
+constexpr uint32_t kScanTmemCols = 256;
+constexpr uint32_t kColDS = 0;    // dS = K^T (hi + lo), all lanes, 64 columns
+constexpr uint32_t kColVO = 64;   // per parity (64 + 64 * parity): U -> VN lanes A, O lanes B
+
+__global__ void __launch_bounds__(384, 1) chunk_scan_kernel(const __grid_constant__ ScanParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* sm = align1024(smem_raw);
+    __shared__ SShared sh;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     constexpr int kSlices = kHeadDim / kVS;
@@ -167,11 +579,12 @@ __global__ void __launch_bounds__(384, 1) chunk_prefill_kernel(const __grid_cons
     const int v0 = (blockIdx.x % kSlices) * kVS;
     const int h = hv / p.rep;
     const int n = blockIdx.y;
-    int64_t bos = 0, len = p.T, brow = n;
+    int64_t bos = 0, len = p.T, brow = n, slot0 = (int64_t)n * p.ncd;
     if (p.cu_seqlens) {
         bos = p.cu_seqlens[n];
         len = p.cu_seqlens[n + 1] - bos;
         brow = 0;
+        slot0 = bos / 64 + n;
     }
     const int nchunks = (int)((len + 63) / 64);
     const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;  // TMEM lane quarter of this warp
@@ -180,15 +593,22 @@ __global__ void __launch_bounds__(384, 1) chunk_prefill_kernel(const __grid_cons
 
     if (tid == 0) {
         sh.abort = 0;
-        uint64_t* all = reinterpret_cast<uint64_t*>(&bar);
-        for (uint32_t i = 0; i < sizeof(Bars) / sizeof(uint64_t); ++i) mbar_init(all + i, 1);
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&sh.full[s], 1);
+            mbar_init(&sh.empty[s], 2);  // the chain's MMAs and the epilogue
+            mbar_init(&sh.acc_vn[s], 1);
+            mbar_init(&sh.acc_o[s], 1);
+            mbar_init(&sh.o_free[s], 1);
+        }
+        mbar_init(&sh.acc_s, 1);
+        mbar_init(&sh.drain, 1);
         fence_mbar_init();
         tma_prefetch_map(&p.tm_q);
         tma_prefetch_map(&p.tm_k);
         tma_prefetch_map(&p.tm_v);
     }
     if (warp == 0) {
-        tmem_alloc(&sh.tmem_base, kTmemCols);
+        tmem_alloc(&sh.tmem_base, kScanTmemCols);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -210,365 +630,81 @@ __global__ void __launch_bounds__(384, 1) chunk_prefill_kernel(const __grid_cons
         for (int c = 0; c < nchunks; ++c) {
             const int s = c & 1;
             if (c >= 2) {
-                bool w = wait(&bar.kqv_empty[s], ((c >> 1) + 1) & 1, kSiteTmaLoad);
-                w = w && wait(&bar.gates_empty[s], ((c >> 1) + 1) & 1, kSiteTmaLoad);
+                const bool w = wait(&sh.empty[s], ((c >> 1) + 1) & 1, kSiteTmaLoad);
                 if (!__all_sync(0xffffffffu, w)) {
                     fail();
                     break;
                 }
             }
-            const int t = (int)(bos + 64 * c);
             if (lane == 0) {
-                mbar_arrive_expect_tx(&bar.kqv_full[s], 5 * kPanel);
-                uint8_t* kt = sm + Smem::K + s * 2 * kPanel;
-                uint8_t* qt = sm + Smem::Q + s * 2 * kPanel;
-                tma_load_4d(kt, &p.tm_k, &bar.kqv_full[s], 0, h, t, (int)brow);
-                tma_load_4d(kt + kPanel, &p.tm_k, &bar.kqv_full[s], 64, h, t, (int)brow);
-                tma_load_4d(qt, &p.tm_q, &bar.kqv_full[s], 0, h, t, (int)brow);
-                tma_load_4d(qt + kPanel, &p.tm_q, &bar.kqv_full[s], 64, h, t, (int)brow);
-                tma_load_4d(sm + Smem::V + s * kPanel, &p.tm_v, &bar.kqv_full[s], v0, hv, t, (int)brow);
+                const int t = (int)(bos + 64 * c);
+                mbar_arrive_expect_tx(&sh.full[s], 5 * kPanel + kRecBytes);
+                uint8_t* kt = sm + SSmem::K + s * 2 * kPanel;
+                uint8_t* qt = sm + SSmem::Q + s * 2 * kPanel;
+                tma_load_4d(kt, &p.tm_k, &sh.full[s], 0, h, t, (int)brow);
+                tma_load_4d(kt + kPanel, &p.tm_k, &sh.full[s], 64, h, t, (int)brow);
+                tma_load_4d(qt, &p.tm_q, &sh.full[s], 0, h, t, (int)brow);
+                tma_load_4d(qt + kPanel, &p.tm_q, &sh.full[s], 64, h, t, (int)brow);
+                tma_load_4d(sm + SSmem::V + s * kPanel, &p.tm_v, &sh.full[s], v0, hv, t, (int)brow);
+                bulk_load(sm + SSmem::REC + s * kRecBytes,
+                          p.records + ((slot0 + c) * p.HV + hv) * (int64_t)kRecBytes, kRecBytes, &sh.full[s]);
                 issued[s] = c + 1;
             }
-            const int nvalid = nvalid_of(c);
-#pragma unroll
-            for (int e = 0; e < 2; ++e) {
-                const int j = 2 * lane + e;
-                float gv = 0.f, bv = 0.f;
-                if (j < nvalid) {
-                    const int64_t gi = (brow * p.T + t + j) * p.HV + hv;
-                    gv = p.g[gi];
-                    bv = p.beta_f32 ? static_cast<const float*>(p.beta)[gi]
-                                    : to_f32(static_cast<const bf16*>(p.beta)[gi]);
-                }
-                sh.graw[s][j] = gv;
-                sh.braw[s][j] = bv;
-            }
             __syncwarp();
-            if (lane == 0) mbar_arrive(&bar.gates_full[s]);
         }
-        // let every tile this warp asked for land before the CTA can exit
+        // let every copy this warp started land before the CTA can exit
         if (lane == 0)
             for (int s = 0; s < 2; ++s)
-                if (issued[s]) mbar_wait(&bar.kqv_full[s], ((issued[s] - 1) >> 1) & 1, kSiteDrain);
+                if (issued[s]) mbar_wait(&sh.full[s], ((issued[s] - 1) >> 1) & 1, kSiteDrain);
     } else if (warp >= 4 && warp < 8) {
-        // ================================ prep ================================
-        const int pt = tid - 128;  // 0..127
-        float* Af = reinterpret_cast<float*>(sm + Smem::AF);
-        const uint32_t id_sq = make_idesc(64, 64, kFmtBF16, false, false);
-        const uint32_t id_mn64 = make_idesc(64, 64, kFmtBF16, false, true);
-        auto issue_kq = [&](int c) {
-            const uint8_t* kt = sm + Smem::K + (c & 1) * 2 * kPanel;
-            const uint8_t* qt = sm + Smem::Q + (c & 1) * 2 * kPanel;
-#pragma unroll
-            for (int kk = 0; kk < 8; ++kk) {
-                const uint32_t po = (kk >> 2) * kPanel, ko = (kk & 3) * 32;
-                const uint64_t bd = sdesc_kmajor(kt + po, ko);
-                mma_f16(tb + kColKQ, sdesc_kmajor(kt + po, ko), bd, id_sq, kk > 0);
-                mma_f16(tb + kColKQ + kHalfB, sdesc_kmajor(qt + po, ko), bd, id_sq, kk > 0);
-            }
-            mma_commit(&bar.acc_kq);
-        };
-        bool issued_any = false;
+        // =============================== epilogue ===============================
+        const int et = tid - 128;
         for (int c = 0; c < nchunks; ++c) {
             const int s = c & 1;
-            const uint32_t ph = c & 1, phs = (c >> 1) & 1;
-            const int nvalid = nvalid_of(c);
-            const uint8_t* kt = sm + Smem::K + s * 2 * kPanel;
-            const uint8_t* qt = sm + Smem::Q + s * 2 * kPanel;
-            bool ok = wait(&bar.gates_full[s], phs, kSiteTmaLoad) && wait(&bar.kqv_full[s], phs, kSiteTmaLoad);
-            // the chain of chunk c-2 must be done with this parity's scalars and accumulators
-            if (ok && c >= 2) ok = wait(&bar.o_free[s], ((c >> 1) + 1) & 1, kSiteMma);
-            if (!named_sync_all(kBarPrep, 128, ok)) { fail(); break; }
-            if (pt == 0) {  // KK, QK of this chunk; the norms below overlap them
-                tc_fence_after();
-                issue_kq(c);
-                issued_any = true;
+            const uint32_t phs = (c >> 1) & 1;
+            const uint32_t tVO = tb + kColVO + 64 * s;
+            const bool ok = wait(&sh.acc_o[s], phs, kSiteMma) && wait(&sh.full[s], phs, kSiteTmaLoad);
+            if (!named_sync_all(kBarEpi, 128, ok)) {
+                fail();
+                break;
             }
-            // ---- gates (scan in log2 units) and inverse norms
-            float gsum = 0.f;
-            if (pt < 64) {
-                float x = sh.graw[s][pt] * kLog2e;
-#pragma unroll
-                for (int o = 1; o < 32; o <<= 1) {
-                    const float y = __shfl_up_sync(0xffffffffu, x, o);
-                    if (lane >= o) x += y;
-                }
-                gsum = x;
-                if (pt == 31) sh.scan_carry = x;
-                sh.beta[pt] = sh.braw[s][pt];
-                const float inv = rsqrtf(sum_squares_row(kt, pt) + 1e-6f);
-                sh.rk[pt] = pt < nvalid ? inv : 0.f;
-            } else {
-                const int r = pt - 64;
-                sh.rq[r] = rsqrtf(sum_squares_row(qt, r) + 1e-6f) * p.scale;
-            }
-            named_sync(kBarPrep, 128);
-            if (pt < 64) sh.gcl[pt] = pt >= 32 ? gsum + sh.scan_carry : gsum;
-            named_sync(kBarPrep, 128);
-            if (pt == 0) mbar_arrive(&bar.gates_empty[s]);
-            if (pt < 64) {
-                const float gl = sh.gcl[pt];
-                const float glast = sh.gcl[63];
-                const float rk = sh.rk[pt], bt = sh.beta[pt], rq = sh.rq[pt];
-                const float mxv = fmaxf(gl, kDecayFloor);
-                const float e_gl = exp2f(gl);
-                sh.rowA[pt] = bt * rk * e_gl;
-                sh.colS[pt] = rk * exp2f(-fmaxf(gl, kDecayFloor));
-                sh.cw[pt] = bt * rk * e_gl;
-                sh.mx[pt] = mxv;
-                sh.ce[s][pt] = rk * exp2f(glast - gl);
-                sh.eq[s][pt] = rq * exp2f(mxv);
-                if (pt == 0) {
-                    sh.dec[s] = exp2f(glast);
-                    sh.fast = glast > kDecayFloor;
-                }
-            }
-            named_sync(kBarPrep, 128);
-            // ---- A (fp32 rows, from KK in lanes A) and P' (bf16 rows, from QK in lanes B)
-            if (!named_sync_all(kBarPrep, 128, wait(&bar.acc_kq, ph, kSiteMma))) { fail(); break; }
             tc_fence_after();
-            {
-                const int i = half_row;
-                const int lim = lanes_a ? i : i + 1;  // columns kept: j < lim
-                const bool fast = sh.fast;
-                const float rs_fast = lanes_a ? sh.rowA[i] : 1.f;
-                const float gli = sh.gcl[i];
-                const float rs_slow = lanes_a ? sh.beta[i] * sh.rk[i] : 1.f;
-                const float shift = lanes_a ? 0.f : sh.mx[i];
+            const RecScalars* rs = reinterpret_cast<const RecScalars*>(sm + SSmem::REC + s * kRecBytes + kRecSc);
+            const int i = half_row;
+            const bool store = !lanes_a && i < nvalid_of(c);
+            const float eqi = rs->eq[i];
+            bf16* orow = p.o + ((brow * p.T + bos + 64 * (int64_t)c + i) * p.HV + hv) * kHeadDim + v0;
 #pragma unroll
-                for (int half = 0; half < 2; ++half) {
-                    float r[32];
-                    tmem_ld32_wait(tb + kColKQ + lane_base + 32 * half, r);
-                    if (fast) {
-#pragma unroll
-                        for (int j = 0; j < 32; j += 4) {
-                            const float4 cs = ld4(&sh.colS[32 * half + j]);
-                            r[j] *= rs_fast * cs.x;
-                            r[j + 1] *= rs_fast * cs.y;
-                            r[j + 2] *= rs_fast * cs.z;
-                            r[j + 3] *= rs_fast * cs.w;
-                        }
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            const int col = 32 * half + j;
-                            const float e = exp2f(fminf(gli - sh.gcl[col] - shift, 0.f));
-                            r[j] *= rs_slow * sh.rk[col] * e;
-                        }
-                    }
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) r[j] = (32 * half + j) < lim ? r[j] : 0.f;
-                    if (lanes_a) {
-                        float* arow = Af + i * kAfStride + 32 * half;
-#pragma unroll
-                        for (int j = 0; j < 32; j += 4)
-                            *reinterpret_cast<float4*>(arow + j) = make_float4(r[j], r[j + 1], r[j + 2], r[j + 3]);
-                    } else {
-                        uint8_t* pm = sm + Smem::PM + s * kPanel;
-#pragma unroll
-                        for (int ch = 0; ch < 4; ++ch) put_chunk(pm, i, 4 * half + ch, r + 8 * ch);
-                    }
-                }
-            }
-            fence_async_smem();
-            tc_fence_before();
-            named_sync(kBarPrep, 128);
-            // ---- inverses of the four 16x16 diagonal blocks of I + A (two partial sums per row)
-            {
-                float x[16];
-                const int b = pt >> 4, col = pt & 15;
-                if (pt < 64) {
-                    const float* blk = Af + 16 * b * kAfStride + 16 * b;
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        float a0 = 0.f, a1 = 0.f;
-#pragma unroll
-                        for (int j = 0; j < i; ++j) {
-                            if (j & 1) a1 = fmaf(blk[i * kAfStride + j], x[j], a1);
-                            else a0 = fmaf(blk[i * kAfStride + j], x[j], a0);
-                        }
-                        x[i] = (i == col) ? 1.f : (i > col ? -(a0 + a1) : 0.f);
-                    }
-                }
-                named_sync(kBarPrep, 128);
-                if (pt < 64) {
-                    float* blk = Af + 16 * b * kAfStride + 16 * b;
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) blk[i * kAfStride + col] = x[i];
-                }
-            }
-            named_sync(kBarPrep, 128);
-            // ---- 16 -> 32 merge inside each 32-block: X10 = -X11 (A10 X00)
-            {
-                const int blk = pt >> 6, e = pt & 63;
-                const int i = e >> 2, j0 = (e & 3) * 4, r0 = 32 * blk;
-                float t4[4] = {0.f, 0.f, 0.f, 0.f};
-                const float* arow = Af + (r0 + 16 + i) * kAfStride + r0;
-#pragma unroll
-                for (int kx = 0; kx < 16; kx += 4) {
-                    const float4 a = ld4(arow + kx);
-                    const float av[4] = {a.x, a.y, a.z, a.w};
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const float4 xv = ld4(&Af[(r0 + kx + q) * kAfStride + r0 + j0]);
-                        t4[0] = fmaf(av[q], xv.x, t4[0]); t4[1] = fmaf(av[q], xv.y, t4[1]);
-                        t4[2] = fmaf(av[q], xv.z, t4[2]); t4[3] = fmaf(av[q], xv.w, t4[3]);
-                    }
-                }
-                named_sync(kBarPrep, 128);
-                *reinterpret_cast<float4*>(&Af[(r0 + 16 + i) * kAfStride + r0 + j0]) = make_float4(t4[0], t4[1], t4[2], t4[3]);
-                named_sync(kBarPrep, 128);
-                float x4[4] = {0.f, 0.f, 0.f, 0.f};
-                const float* xrow = Af + (r0 + 16 + i) * kAfStride + r0 + 16;
-#pragma unroll
-                for (int kx = 0; kx < 16; kx += 4) {
-                    const float4 a = ld4(xrow + kx);
-                    const float av[4] = {a.x, a.y, a.z, a.w};
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const float4 tv = ld4(&Af[(r0 + 16 + kx + q) * kAfStride + r0 + j0]);
-                        x4[0] = fmaf(av[q], tv.x, x4[0]); x4[1] = fmaf(av[q], tv.y, x4[1]);
-                        x4[2] = fmaf(av[q], tv.z, x4[2]); x4[3] = fmaf(av[q], tv.w, x4[3]);
-                    }
-                }
-                named_sync(kBarPrep, 128);
-                *reinterpret_cast<float4*>(&Af[(r0 + 16 + i) * kAfStride + r0 + j0]) =
-                    make_float4(-x4[0], -x4[1], -x4[2], -x4[3]);
-            }
-            named_sync(kBarPrep, 128);
-            // ---- bf16 operands of the 32 -> 64 merge: E32 (lower-left block of A) and D32
-            {
-                const int i = pt & 63, hf = pt >> 6;  // two threads per row, 32 columns each
-                const float* arow = Af + i * kAfStride + 32 * hf;
-#pragma unroll
-                for (int cc = 0; cc < 4; ++cc) {
-                    float e8[8], d8[8];
-                    const float4 a0 = ld4(arow + 8 * cc), a1 = ld4(arow + 8 * cc + 4);
-                    const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-#pragma unroll
-                    for (int q = 0; q < 8; ++q) {
-                        const int j = 32 * hf + 8 * cc + q;
-                        e8[q] = (i >= 32 && j < 32) ? av[q] : 0.f;
-                        d8[q] = ((i >> 5) == (j >> 5) && j <= i) ? av[q] : 0.f;
-                    }
-                    put_chunk(sm + Smem::AU, i, 4 * hf + cc, e8);
-                    put_chunk(sm + Smem::AW, i, 4 * hf + cc, d8);
-                }
-            }
-            fence_async_smem();
-            tc_fence_before();
-            named_sync(kBarPrep, 128);
-            if (pt == 0) {  // T2 = E32 D32 (lanes A)
-                tc_fence_after();
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    mma_f16(tb + kColT2, sdesc_kmajor(sm + Smem::AU, kk * 32),
-                            sdesc_mnmajor(sm + Smem::AW + kk * 2048, kPanel), id_mn64, kk > 0);
-                mma_commit(&bar.acc_t2);
-            }
-            // ---- T2 -> bf16 operand
-            if (!named_sync_all(kBarPrep, 128, wait(&bar.acc_t2, ph, kSiteMma))) { fail(); break; }
-            tc_fence_after();
-            {
-                float r[64];
-                tmem_ld64_wait(tb + kColT2 + lane_base, r);
-                if (lanes_a)
-#pragma unroll
-                    for (int ch = 0; ch < 8; ++ch) put_chunk(sm + Smem::T2, half_row, ch, r + 8 * ch);
-            }
-            fence_async_smem();
-            tc_fence_before();
-            named_sync(kBarPrep, 128);
-            if (pt == 0) {  // X_LL = D32 T2 (lanes B)
-                tc_fence_after();
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    mma_f16(tb + kColT2 + kHalfB, sdesc_kmajor(sm + Smem::AW, kk * 32),
-                            sdesc_mnmajor(sm + Smem::T2 + kk * 2048, kPanel), id_mn64, kk > 0);
-                mma_commit(&bar.acc_x);
-            }
-            // ---- X = D32 - X_LL; two column-scaled bf16 copies feed U and W. Row i is shared
-            // by lanes l (columns 32-63) and l + 16 (columns 0-31, whose TMEM lanes hold X_LL).
-            if (!named_sync_all(kBarPrep, 128, wait(&bar.acc_x, ph, kSiteMma))) { fail(); break; }
-            tc_fence_after();
-            {
-                const int i = half_row;
-                const int cbase = lanes_a ? 32 : 0;
+            for (int half = 0; half < 2; ++half) {
                 float r[32];
-                tmem_ld32_wait(tb + kColT2 + lane_base, r);  // lanes B: X_LL columns 0-31
-                const float* arow = Af + i * kAfStride + cbase;
+                tmem_ld32_wait(tVO + lane_base + 32 * half, r);  // lanes B: O rows
+                if (store) {
 #pragma unroll
-                for (int cc = 0; cc < 4; ++cc) {
-                    float xu[8], xw[8];
-                    const float4 a0 = ld4(arow + 8 * cc), a1 = ld4(arow + 8 * cc + 4);
-                    const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-                    const float4 b0 = ld4(&sh.beta[cbase + 8 * cc]), b1 = ld4(&sh.beta[cbase + 8 * cc + 4]);
-                    const float4 w0 = ld4(&sh.cw[cbase + 8 * cc]), w1 = ld4(&sh.cw[cbase + 8 * cc + 4]);
-                    const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-                    const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+                    for (int ch = 0; ch < 4; ++ch) {
+                        uint4 raw;
+                        __nv_bfloat162* hh = reinterpret_cast<__nv_bfloat162*>(&raw);
 #pragma unroll
-                    for (int q = 0; q < 8; ++q) {
-                        const int col = cbase + 8 * cc + q;
-                        float xv;
-                        if (col > i) xv = 0.f;
-                        else if (!lanes_a && i >= 32) xv = -r[8 * cc + q];
-                        else xv = av[q];
-                        xu[q] = xv * bv[q];
-                        xw[q] = xv * wv[q];
+                        for (int j = 0; j < 4; ++j)
+                            hh[j] = __floats2bfloat162_rn(eqi * r[8 * ch + 2 * j], eqi * r[8 * ch + 2 * j + 1]);
+                        *reinterpret_cast<uint4*>(orow + 32 * half + 8 * ch) = raw;
                     }
-                    put_chunk(sm + Smem::AU, i, cbase / 8 + cc, xu);
-                    put_chunk(sm + Smem::AW, i, cbase / 8 + cc, xw);
                 }
             }
-            fence_async_smem();
             tc_fence_before();
-            named_sync(kBarPrep, 128);
-            if (pt == 0) {
-                // W[:, 0:64] (lanes A) and W[:, 64:128] (lanes B) = (X diag(cw)) K; U = (X diag(beta)) V
-                tc_fence_after();
-                const uint32_t tR = tb + kColR + 128 * s;
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk) {
-                    const uint64_t ad = sdesc_kmajor(sm + Smem::AW, kk * 32);
-                    mma_f16(tR, ad, sdesc_mnmajor(kt + kk * 2048, kPanel), id_mn64, kk > 0);
-                    mma_f16(tR + kHalfB, ad, sdesc_mnmajor(kt + kPanel + kk * 2048, kPanel), id_mn64, kk > 0);
-                    mma_f16(tR + 64, sdesc_kmajor(sm + Smem::AU, kk * 32),
-                            sdesc_mnmajor(sm + Smem::V + s * kPanel + kk * 2048, kPanel), id_mn64, kk > 0);
-                }
-                mma_commit(&bar.acc_wu[s]);
+            named_sync(kBarEpi, 128);
+            if (et == 0) {
+                mbar_arrive(&sh.o_free[s]);
+                mbar_arrive(&sh.empty[s]);
             }
-            // ---- W -> bf16 operand (lanes A: d 0-63, lanes B: d 64-127)
-            if (!named_sync_all(kBarPrep, 128, wait(&bar.acc_wu[s], phs, kSiteMma))) { fail(); break; }
-            tc_fence_after();
-            {
-                float r[64];
-                tmem_ld64_wait(tb + kColR + 128 * s + lane_base, r);
-                uint8_t* panel = sm + Smem::WB + s * 2 * kPanel + (lanes_a ? 0 : kPanel);
-#pragma unroll
-                for (int ch = 0; ch < 8; ++ch) put_chunk(panel, half_row, ch, r + 8 * ch);
-            }
-            fence_async_smem();
-            tc_fence_before();
-            named_sync(kBarPrep, 128);
-            if (pt == 0) mbar_arrive(&bar.wb_ready);
-        }
-        // every MMA this warpgroup issued is complete before TMEM can be freed
-        if (pt == 0 && issued_any) {
-            mma_commit(&bar.drain_prep);
-            mbar_wait(&bar.drain_prep, 0, kSiteDrain);
         }
     } else if (warp >= 8) {
         // ================================ chain ================================
         const int ct = tid - 256;  // 0..127: the state row (and TMEM lane) of this thread
         const int d = ct;
-        uint8_t* sbp = sm + Smem::SB + (d >> 6) * kPanel;
-        const uint32_t sb_off = (d & 7) * 2;
-        const uint32_t sb_chunk = (d & 63) >> 3;
         const int64_t state_row = (((int64_t)n * p.HV + hv) * kHeadDim + d) * kHeadDim + v0;
-        const uint32_t id_vn = make_idesc(64, kVS, kFmtBF16, false, false, true);
-        const uint32_t id_o1 = make_idesc(64, kVS, kFmtBF16, false, false);
+        const uint32_t id_u = make_idesc(64, kVS, kFmtBF16, false, true);
+        const uint32_t id_vn = make_idesc(64, kVS, kFmtBF16, false, true, true);
         const uint32_t id_s = make_idesc(128, kVS, kFmtBF16, true, true);
-        const uint32_t id_o2 = make_idesc(64, kVS, kFmtBF16, false, true);
         float S[kVS];
         if (p.h0) {
 #pragma unroll
@@ -587,59 +723,80 @@ __global__ void __launch_bounds__(384, 1) chunk_prefill_kernel(const __grid_cons
                     *reinterpret_cast<float4*>(p.ht + state_row + j) = make_float4(S[j], S[j + 1], S[j + 2], S[j + 3]);
         } else {
 #pragma unroll
-            for (int v = 0; v < kVS; ++v)
-                *reinterpret_cast<bf16*>(sbp + sw128(v, sb_chunk) + sb_off) = __float2bfloat16_rn(S[v]);
+            for (int ch = 0; ch < 8; ++ch) put_chunk(sm + SSmem::SB, d, ch, S + 8 * ch);
         }
         fence_async_smem();
         named_sync(kBarChain, 128);
-        bool issued_any = false;
+        // U(c) = (X diag beta) V into the lanes-A accumulator of parity c & 1
+        auto issue_u = [&](int c) {
+            const int s = c & 1;
+            const uint8_t* rec = sm + SSmem::REC + s * kRecBytes;
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+                mma_f16(tb + kColVO + 64 * s, sdesc_kmajor(rec + kRecXB, kk * 32),
+                        sdesc_mnmajor(sm + SSmem::V + s * kPanel + kk * 2048, kPanel), id_u, kk > 0);
+        };
+        bool issued_any = false, issuer_ok = true;
+        if (ct == 0 && nchunks > 0) {
+            issuer_ok = wait(&sh.full[0], 0, kSiteTmaLoad);
+            if (issuer_ok) {
+                tc_fence_after();
+                issue_u(0);
+                issued_any = true;
+            }
+        }
         for (int c = 0; c < nchunks; ++c) {
             const int s = c & 1;
             const uint32_t ph = c & 1, phs = (c >> 1) & 1;
-            const uint32_t tR = tb + kColR + 128 * s;
-            const uint8_t* kt = sm + Smem::K + s * 2 * kPanel;
-            const uint8_t* qt = sm + Smem::Q + s * 2 * kPanel;
-            const int64_t t0 = bos + 64 * (int64_t)c;
-            const int nvalid = nvalid_of(c);
+            const uint32_t tVO = tb + kColVO + 64 * s;
+            const uint8_t* rec = sm + SSmem::REC + s * kRecBytes;
+            const uint8_t* kt = sm + SSmem::K + s * 2 * kPanel;
+            const uint8_t* qt = sm + SSmem::Q + s * 2 * kPanel;
+            const bool landed = wait(&sh.full[s], phs, kSiteTmaLoad) && issuer_ok;
+            if (!named_sync_all(kBarChain, 128, landed)) {
+                fail();
+                break;
+            }
+            // the stage can be refilled once the MMAs below are done: read its scalars now
+            const RecScalars* rs = reinterpret_cast<const RecScalars*>(rec + kRecSc);
+            const float cei = rs->ce[half_row];
+            const float decay = rs->dec;
             // ---- VN = U - W S (lanes A, onto U); O = Q S (lanes B)
-            if (!named_sync_all(kBarChain, 128, wait(&bar.wb_ready, ph, kSiteMma))) { fail(); break; }
             if (ct == 0) {
                 tc_fence_after();
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk) {
                     const uint32_t po = (kk >> 2) * kPanel, ko = (kk & 3) * 32;
-                    const uint64_t bd = sdesc_kmajor(sm + Smem::SB + po, ko);
-                    mma_f16(tR + 64, sdesc_kmajor(sm + Smem::WB + s * 2 * kPanel + po, ko), bd, id_vn, 1);
-                    mma_f16(tR + 64 + kHalfB, sdesc_kmajor(qt + po, ko), bd, id_o1, kk > 0);
+                    const uint64_t bd = sdesc_mnmajor(sm + SSmem::SB + kk * 2048, kPanel);
+                    mma_f16(tVO, sdesc_kmajor(rec + kRecW + po, ko), bd, id_vn, 1);
+                    mma_f16(tVO + kHalfB, sdesc_kmajor(qt + po, ko), bd, id_u, kk > 0);
                 }
-                mma_commit(&bar.acc_vn[s]);
-                issued_any = true;
+                mma_commit(&sh.acc_vn[s]);
             }
-            if (!named_sync_all(kBarChain, 128, wait(&bar.acc_vn[s], phs, kSiteMma))) { fail(); break; }
+            if (!named_sync_all(kBarChain, 128, wait(&sh.acc_vn[s], phs, kSiteMma))) {
+                fail();
+                break;
+            }
             tc_fence_after();
             // ---- VN -> bf16 VN and the split ce VN
-            {
-                const int i = half_row;
-                const float cei = sh.ce[s][i];
 #pragma unroll
-                for (int half = 0; half < 2; ++half) {
-                    float r[32];
-                    tmem_ld32_wait(tR + 64 + lane_base + 32 * half, r);  // lanes A: VN rows
-                    if (lanes_a) {
+            for (int half = 0; half < 2; ++half) {
+                float r[32];
+                tmem_ld32_wait(tVO + lane_base + 32 * half, r);  // lanes A: VN rows
+                if (lanes_a) {
 #pragma unroll
-                        for (int cc = 0; cc < 4; ++cc) {
-                            float hi[8], lo[8];
+                    for (int cc = 0; cc < 4; ++cc) {
+                        float hi[8], lo[8];
 #pragma unroll
-                            for (int j = 0; j < 8; ++j) {
-                                const float x = cei * r[8 * cc + j];
-                                hi[j] = round_bf16(x);
-                                lo[j] = x - hi[j];
-                            }
-                            const int ch = 4 * half + cc;
-                            put_chunk(sm + Smem::VBF, i, ch, r + 8 * cc);
-                            put_chunk(sm + Smem::VHI, i, ch, hi);
-                            put_chunk(sm + Smem::VLO, i, ch, lo);
+                        for (int j = 0; j < 8; ++j) {
+                            const float x = cei * r[8 * cc + j];
+                            hi[j] = round_bf16(x);
+                            lo[j] = x - hi[j];
                         }
+                        const int ch = 4 * half + cc;
+                        put_chunk(sm + SSmem::VBF, half_row, ch, r + 8 * cc);
+                        put_chunk(sm + SSmem::VHI, half_row, ch, hi);
+                        put_chunk(sm + SSmem::VLO, half_row, ch, lo);
                     }
                 }
             }
@@ -647,78 +804,64 @@ __global__ void __launch_bounds__(384, 1) chunk_prefill_kernel(const __grid_cons
             tc_fence_before();
             named_sync(kBarChain, 128);
             if (ct == 0) {
-                // dS = K^T hi + K^T lo (all lanes, fresh); O += P' VN (lanes B)
+                // dS = K^T hi + K^T lo (all lanes, fresh); O += P' VN (lanes B); then U of the
+                // next chunk, once its stage has landed and the epilogue has drained that parity
                 tc_fence_after();
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
                     const uint64_t ad = sdesc_mnmajor(kt + kk * 2048, kPanel);
-                    mma_f16(tb + kColDS, ad, sdesc_mnmajor(sm + Smem::VHI + kk * 2048, kPanel), id_s, kk > 0);
-                    mma_f16(tb + kColDS, ad, sdesc_mnmajor(sm + Smem::VLO + kk * 2048, kPanel), id_s, 1);
-                    mma_f16(tR + 64 + kHalfB, sdesc_kmajor(sm + Smem::PM + s * kPanel, kk * 32),
-                            sdesc_mnmajor(sm + Smem::VBF + kk * 2048, kPanel), id_o2, 1);
+                    mma_f16(tb + kColDS, ad, sdesc_mnmajor(sm + SSmem::VHI + kk * 2048, kPanel), id_s, kk > 0);
+                    mma_f16(tb + kColDS, ad, sdesc_mnmajor(sm + SSmem::VLO + kk * 2048, kPanel), id_s, 1);
+                    mma_f16(tVO + kHalfB, sdesc_kmajor(rec + kRecPM, kk * 32),
+                            sdesc_mnmajor(sm + SSmem::VBF + kk * 2048, kPanel), id_u, 1);
                 }
-                mma_commit(&bar.acc_s);
-                mma_commit(&bar.kqv_empty[s]);
-            }
-            if (!named_sync_all(kBarChain, 128, wait(&bar.acc_s, ph, kSiteMma))) { fail(); break; }
-            tc_fence_after();
-            // ---- S <- 2^glast S + dS; o = eq O (32 columns at a time keeps the state in registers)
-            {
-                const float decay = sh.dec[s];
-                const bool last = c + 1 == nchunks;
-#pragma unroll
-                for (int half = 0; half < 2; ++half) {
-                    float r[32];
-                    tmem_ld32_wait(tb + kColDS + lane_base + 32 * half, r);
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) S[32 * half + j] = fmaf(decay, S[32 * half + j], r[j]);
-                }
-                if (last) {
-                    if (p.ht)
-#pragma unroll
-                        for (int j = 0; j < kVS; j += 4)
-                            *reinterpret_cast<float4*>(p.ht + state_row + j) =
-                                make_float4(S[j], S[j + 1], S[j + 2], S[j + 3]);
-                } else {
-#pragma unroll
-                    for (int v = 0; v < kVS; ++v)
-                        *reinterpret_cast<bf16*>(sbp + sw128(v, sb_chunk) + sb_off) = __float2bfloat16_rn(S[v]);
-                }
-                const int i = half_row;
-                const bool store = !lanes_a && i < nvalid;
-                const float eqi = sh.eq[s][i];
-                bf16* orow = p.o + ((brow * p.T + t0 + i) * p.HV + hv) * kHeadDim + v0;
-#pragma unroll
-                for (int half = 0; half < 2; ++half) {
-                    float r[32];
-                    tmem_ld32_wait(tR + 64 + lane_base + 32 * half, r);  // lanes B: O rows
-                    if (store) {
-#pragma unroll
-                        for (int ch = 0; ch < 4; ++ch) {
-                            uint4 raw;
-                            __nv_bfloat162* hh = reinterpret_cast<__nv_bfloat162*>(&raw);
-#pragma unroll
-                            for (int j = 0; j < 4; ++j)
-                                hh[j] = __floats2bfloat162_rn(eqi * r[8 * ch + 2 * j], eqi * r[8 * ch + 2 * j + 1]);
-                            *reinterpret_cast<uint4*>(orow + 32 * half + 8 * ch) = raw;
-                        }
+                mma_commit(&sh.acc_s);
+                mma_commit(&sh.acc_o[s]);
+                mma_commit(&sh.empty[s]);
+                if (c + 1 < nchunks) {
+                    issuer_ok = wait(&sh.full[s ^ 1], ((c + 1) >> 1) & 1, kSiteTmaLoad);
+                    if (issuer_ok && c >= 1) issuer_ok = wait(&sh.o_free[s ^ 1], ((c - 1) >> 1) & 1, kSiteMma);
+                    if (issuer_ok) {
+                        tc_fence_after();
+                        issue_u(c + 1);
                     }
                 }
+            }
+            if (!named_sync_all(kBarChain, 128, wait(&sh.acc_s, ph, kSiteMma) && issuer_ok)) {
+                fail();
+                break;
+            }
+            tc_fence_after();
+            // ---- S <- 2^glast S + dS (32 columns at a time keeps the state in registers)
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                float r[32];
+                tmem_ld32_wait(tb + kColDS + lane_base + 32 * half, r);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) S[32 * half + j] = fmaf(decay, S[32 * half + j], r[j]);
+            }
+            if (c + 1 == nchunks) {
+                if (p.ht)
+#pragma unroll
+                    for (int j = 0; j < kVS; j += 4)
+                        *reinterpret_cast<float4*>(p.ht + state_row + j) = make_float4(S[j], S[j + 1], S[j + 2], S[j + 3]);
+            } else {
+#pragma unroll
+                for (int ch = 0; ch < 8; ++ch) put_chunk(sm + SSmem::SB, d, ch, S + 8 * ch);
             }
             fence_async_smem();
             tc_fence_before();
             named_sync(kBarChain, 128);
-            if (ct == 0) mbar_arrive(&bar.o_free[s]);
         }
         if (ct == 0 && issued_any) {
-            mma_commit(&bar.drain_chain);
-            mbar_wait(&bar.drain_chain, 0, kSiteDrain);
+            mma_commit(&sh.drain);
+            mbar_wait(&sh.drain, 0, kSiteDrain);
         }
     }
 
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) tmem_dealloc(tb, kTmemCols);
+    if (warp == 0) tmem_dealloc(tb, kScanTmemCols);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -754,34 +897,69 @@ static bool make_map(CUtensorMap* map, const void* base, int64_t B, int64_t T, i
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+int64_t chunk_workspace_slots(int64_t B, int64_t T, int64_t nseq, bool packed) {
+    const int64_t ncd = (T + 63) / 64;
+    return packed ? ncd + nseq : B * ncd;
+}
+
+size_t chunk_workspace_bytes(int64_t B, int64_t T, int64_t nseq, bool packed, int64_t HV) {
+    return (size_t)chunk_workspace_slots(B, T, nseq, packed) * (size_t)HV * kRecBytes;
+}
+
 int launch_chunk(const ChunkArgs& a, cudaStream_t s) {
     if (a.nseq == 0) return GDN_OK;
-    ChunkParams p;
-    memset(&p, 0, sizeof(p));
-    if (!make_map(&p.tm_q, a.q, a.B, a.T, a.H, a.qsb, a.qst, a.qsh) ||
-        !make_map(&p.tm_k, a.k, a.B, a.T, a.H, a.ksb, a.kst, a.ksh) ||
-        !make_map(&p.tm_v, a.v, a.B, a.T, a.HV, a.vsb, a.vst, a.vsh))
+    const bool packed = a.cu_seqlens != nullptr;
+    const int64_t slots = chunk_workspace_slots(a.B, a.T, a.nseq, packed);
+    if (slots * a.HV > INT32_MAX) return GDN_ERR_SHAPE;
+    if (a.workspace == nullptr || a.workspace_bytes < chunk_workspace_bytes(a.B, a.T, a.nseq, packed, a.HV))
+        return GDN_ERR_WORKSPACE;
+    FactorParams f;
+    ScanParams sp;
+    memset(&f, 0, sizeof(f));
+    memset(&sp, 0, sizeof(sp));
+    if (!make_map(&f.tm_q, a.q, a.B, a.T, a.H, a.qsb, a.qst, a.qsh) ||
+        !make_map(&f.tm_k, a.k, a.B, a.T, a.H, a.ksb, a.kst, a.ksh) ||
+        !make_map(&sp.tm_v, a.v, a.B, a.T, a.HV, a.vsb, a.vst, a.vsh))
         return GDN_ERR_LAUNCH;
-    p.g = a.g;
-    p.beta = a.beta;
-    p.beta_f32 = a.beta_dtype == GDN_F32;
-    p.h0 = a.h0;
-    p.ht = a.ht;
-    p.o = static_cast<bf16*>(a.o);
-    p.cu_seqlens = a.cu_seqlens;
-    p.T = a.T;
-    p.HV = a.HV;
-    p.rep = a.HV / a.H;
-    p.scale = a.scale;
+    sp.tm_q = f.tm_q;
+    sp.tm_k = f.tm_k;
+    const int ncd = (int)((a.T + 63) / 64);
+    f.g = a.g;
+    f.beta = a.beta;
+    f.beta_f32 = a.beta_dtype == GDN_F32;
+    f.cu_seqlens = a.cu_seqlens;
+    f.records = static_cast<uint8_t*>(a.workspace);
+    f.T = a.T;
+    f.nseq = (int)a.nseq;
+    f.ncd = ncd;
+    f.HV = a.HV;
+    f.rep = a.HV / a.H;
+    f.scale = a.scale;
+    sp.h0 = a.h0;
+    sp.ht = a.ht;
+    sp.o = static_cast<bf16*>(a.o);
+    sp.cu_seqlens = a.cu_seqlens;
+    sp.records = static_cast<const uint8_t*>(a.workspace);
+    sp.T = a.T;
+    sp.ncd = ncd;
+    sp.HV = a.HV;
+    sp.rep = f.rep;
     static bool configured = false;
     if (!configured) {
-        if (cudaFuncSetAttribute(chunk_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)Smem::BYTES) != cudaSuccess)
+        if (cudaFuncSetAttribute(chunk_factor_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)FSmem::BYTES) != cudaSuccess ||
+            cudaFuncSetAttribute(chunk_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)SSmem::BYTES) != cudaSuccess)
             return GDN_ERR_LAUNCH;
         configured = true;
     }
-    dim3 grid((unsigned)(p.HV * (kHeadDim / kVS)), (unsigned)a.nseq);
-    chunk_prefill_kernel<<<grid, 384, Smem::BYTES, s>>>(p);
+    if (slots > 0) {
+        chunk_factor_kernel<<<(unsigned)(slots * a.HV), 128, FSmem::BYTES, s>>>(f);
+        const int st = launch_status();
+        if (st != GDN_OK) return st;
+    }
+    dim3 grid((unsigned)(a.HV * (kHeadDim / kVS)), (unsigned)a.nseq);
+    chunk_scan_kernel<<<grid, 384, SSmem::BYTES, s>>>(sp);
     return launch_status();
 }
 

@@ -43,8 +43,11 @@ struct ChunkArgs {
     int H, HV;
     int64_t qsb, qst, qsh, ksb, kst, ksh, vsb, vst, vsh;
     float scale;
+    void* workspace;
+    size_t workspace_bytes;
 };
 int launch_chunk(const ChunkArgs& a, cudaStream_t s);
+size_t chunk_workspace_bytes(int64_t B, int64_t T, int64_t nseq, bool packed, int64_t HV);
 
 int launch_snapshot_commit(float* state, const float* snapshots, const int64_t* accepted, int64_t B, int64_t T,
                            int64_t HV, cudaStream_t s);

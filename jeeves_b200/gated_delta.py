@@ -148,11 +148,14 @@ def gated_delta_rule_chunk(q, k, v, g, beta, initial_state=None, output_final_st
             final.copy_(h0) if h0 is not None else final.zero_()
         return o, final
     q, k, v = (_heads_last_contiguous(t) for t in (q, k, v))
-    status = _lib.load().gdn_chunk_prefill(
+    lib = _lib.load()
+    ws_bytes = lib.gdn_chunk_prefill_workspace_size(rows, T, HV, int(cu is not None))
+    workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
+    status = lib.gdn_chunk_prefill(
         q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(), beta.data_ptr(), _DTYPES[beta.dtype], _ptr(h0),
         _ptr(final), o.data_ptr(), _ptr(cu), rows, T, H, HV, HEAD_DIM, HEAD_DIM,
         q.stride(0), q.stride(1), q.stride(2), k.stride(0), k.stride(1), k.stride(2), v.stride(0), v.stride(1),
-        v.stride(2), float(HEAD_DIM ** -0.5 if scale is None else scale), _stream())
+        v.stride(2), float(HEAD_DIM ** -0.5 if scale is None else scale), workspace.data_ptr(), ws_bytes, _stream())
     _lib.check(status, what)
     return o, final
 

@@ -75,3 +75,19 @@ def test_status_mapping_to_exceptions():
     with pytest.raises(RuntimeError):
         _lib.check(_lib.ERR_LAUNCH, "x")
     _lib.check(_lib.OK, "x")
+
+
+def test_chunk_workspace_size_and_checks():
+    """The prefill's workspace: its size rule, and a missing / short / misaligned one is refused."""
+    lib = _lib.load()
+    rec = 33792  # bytes per (value head, chunk slot)
+    assert lib.gdn_chunk_prefill_workspace_size(1, 4096, 32, 0) == 64 * 32 * rec
+    assert lib.gdn_chunk_prefill_workspace_size(3, 100, 4, 0) == 3 * 2 * 4 * rec
+    assert lib.gdn_chunk_prefill_workspace_size(5, 300, 4, 1) == (5 + 5) * 4 * rec  # ceil(T/64) + N slots
+    args = [16, 16, 16, 16, 16, _lib.BF16, None, None, 16, None, 1, 64, 1, 1, 128, 128] + [128] * 9 + [0.088]
+    need = lib.gdn_chunk_prefill_workspace_size(1, 64, 1, 0)
+    assert lib.gdn_chunk_prefill(*args, None, need, None) == _lib.ERR_WORKSPACE
+    assert lib.gdn_chunk_prefill(*args, 16, need - 16, None) == _lib.ERR_WORKSPACE
+    assert lib.gdn_chunk_prefill(*args, 24, need, None) == _lib.ERR_ALIGN
+    with pytest.raises(ValueError, match="workspace"):
+        _lib.check(_lib.ERR_WORKSPACE, "gdn_chunk_prefill")
