@@ -26,10 +26,12 @@
 //                        laid out as the scan kernel's shared-memory stage.
 //   chunk_scan_kernel    one CTA per (sequence, value head, 64-column slice of the state),
 //                        walking the chunks in order with the fp32 state slice in registers.
-//                        A loader warp streams K/Q/V tiles (TMA) and records (bulk copy); the
-//                        chain warpgroup runs U, VN = U - W S, dS = K^T VN and the state update;
-//                        an epilogue warpgroup drains O = Q S + P' VN to global memory, so the
-//                        chain's critical path per chunk is two MMA round trips and two readouts.
+//                        A loader warp streams K/Q/V tiles (TMA) and records (bulk copy); two
+//                        chain warpgroups (one per 32-column half of the slice) run U,
+//                        VN = U - W S, dS = K^T VN and the state update; an epilogue warpgroup
+//                        drains O = Q S + P' VN to global memory. The chain's critical path per
+//                        chunk is two MMA round trips (W S, then dS) and two half-width readouts;
+//                        the output MMAs are committed after them and never waited on there.
 //
 // Every wait is bounded (sm100.cuh): a wait that gives up raises the device error word and
 // the CTA's abort flag; every role then leaves its loop, the loader waits for the copies it
@@ -232,14 +234,19 @@ __global__ void __launch_bounds__(128, 3) chunk_factor_kernel(const __grid_const
     do {
         tiles_landed = named_sync_all(kBarFactor, 128, mbar_wait(&sh.tma, 0, kSiteTmaLoad));
         if (!tiles_landed) break;
+        // shared-memory descriptors, built once: each MMA below only adds a byte offset
+        const uint64_t dK = sdesc_kmajor(kt, 0), dQ = sdesc_kmajor(qt, 0);
+        const uint64_t dKmn = sdesc_mnmajor(kt, kPanel);
+        const uint64_t dAU = sdesc_kmajor(sm + FSmem::AU, 0), dAW = sdesc_kmajor(sm + FSmem::AW, 0);
+        const uint64_t dAWmn = sdesc_mnmajor(sm + FSmem::AW, kPanel), dT2mn = sdesc_mnmajor(sm + FSmem::T2, kPanel);
         if (pt == 0) {  // KK, QK; the norms below overlap them
             tc_fence_after();
 #pragma unroll
             for (int kk = 0; kk < 8; ++kk) {
-                const uint32_t po = (kk >> 2) * kPanel, ko = (kk & 3) * 32;
-                const uint64_t bd = sdesc_kmajor(kt + po, ko);
-                mma_f16(tb + kColKQ, sdesc_kmajor(kt + po, ko), bd, id_sq, kk > 0);
-                mma_f16(tb + kColKQ + kHalfB, sdesc_kmajor(qt + po, ko), bd, id_sq, kk > 0);
+                const uint32_t off = (kk >> 2) * kPanel + (kk & 3) * 32;
+                const uint64_t bd = sdesc_add(dK, off);
+                mma_f16(tb + kColKQ, bd, bd, id_sq, kk > 0);
+                mma_f16(tb + kColKQ + kHalfB, sdesc_add(dQ, off), bd, id_sq, kk > 0);
             }
             mma_commit(&sh.acc_kq);
             mma_issued = true;
@@ -419,8 +426,7 @@ __global__ void __launch_bounds__(128, 3) chunk_factor_kernel(const __grid_const
             tc_fence_after();
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
-                mma_f16(tb + kColT2, sdesc_kmajor(sm + FSmem::AU, kk * 32),
-                        sdesc_mnmajor(sm + FSmem::AW + kk * 2048, kPanel), id_mn64, kk > 0);
+                mma_f16(tb + kColT2, sdesc_add(dAU, kk * 32), sdesc_add(dAWmn, kk * 2048), id_mn64, kk > 0);
             mma_commit(&sh.acc_t2);
         }
         // ---- T2 -> bf16 operand
@@ -440,8 +446,7 @@ __global__ void __launch_bounds__(128, 3) chunk_factor_kernel(const __grid_const
             tc_fence_after();
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
-                mma_f16(tb + kColT2 + kHalfB, sdesc_kmajor(sm + FSmem::AW, kk * 32),
-                        sdesc_mnmajor(sm + FSmem::T2 + kk * 2048, kPanel), id_mn64, kk > 0);
+                mma_f16(tb + kColT2 + kHalfB, sdesc_add(dAW, kk * 32), sdesc_add(dT2mn, kk * 2048), id_mn64, kk > 0);
             mma_commit(&sh.acc_x);
         }
         // ---- X = D32 - X_LL; two column-scaled bf16 copies: X diag(beta) (record) and X diag(cw)
@@ -485,9 +490,9 @@ __global__ void __launch_bounds__(128, 3) chunk_factor_kernel(const __grid_const
             tc_fence_after();
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
-                const uint64_t ad = sdesc_kmajor(sm + FSmem::AW, kk * 32);
-                mma_f16(tb + kColKQ, ad, sdesc_mnmajor(kt + kk * 2048, kPanel), id_mn64, kk > 0);
-                mma_f16(tb + kColKQ + kHalfB, ad, sdesc_mnmajor(kt + kPanel + kk * 2048, kPanel), id_mn64, kk > 0);
+                const uint64_t ad = sdesc_add(dAW, kk * 32);
+                mma_f16(tb + kColKQ, ad, sdesc_add(dKmn, kk * 2048), id_mn64, kk > 0);
+                mma_f16(tb + kColKQ + kHalfB, ad, sdesc_add(dKmn, kPanel + kk * 2048), id_mn64, kk > 0);
             }
             mma_commit(&sh.acc_w);
         }
@@ -568,7 +573,10 @@ constexpr uint32_t kScanTmemCols = 256;
 constexpr uint32_t kColDS = 0;    // dS = K^T (hi + lo), all lanes, 64 columns
 constexpr uint32_t kColVO = 64;   // per parity (64 + 64 * parity): U -> VN lanes A, O lanes B
 
-__global__ void __launch_bounds__(384, 1) chunk_scan_kernel(const __grid_constant__ ScanParams p) {
+constexpr int kScanThreads = 512;  // warp 0 loader, 4-7 epilogue, 8-15 chain (two column halves)
+constexpr int kChainThreads = 256;
+
+__global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __grid_constant__ ScanParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = align1024(smem_raw);
     __shared__ SShared sh;
@@ -617,6 +625,9 @@ __global__ void __launch_bounds__(384, 1) chunk_scan_kernel(const __grid_constan
     const uint32_t tb = sh.tmem_base;
     auto wait = [&](uint64_t* b, uint32_t parity, int site) -> bool {
         return mbar_wait_or_abort(b, parity, site, &sh.abort);
+    };
+    auto spin = [&](uint64_t* b, uint32_t parity, int site) -> bool {  // the chain's critical waits
+        return mbar_wait_or_abort(b, parity, site, &sh.abort, false);
     };
     auto fail = [&]() { atomicExch(&sh.abort, 1); };
     auto nvalid_of = [&](int c) -> int {
@@ -699,42 +710,51 @@ __global__ void __launch_bounds__(384, 1) chunk_scan_kernel(const __grid_constan
         }
     } else if (warp >= 8) {
         // ================================ chain ================================
-        const int ct = tid - 256;  // 0..127: the state row (and TMEM lane) of this thread
-        const int d = ct;
-        const int64_t state_row = (((int64_t)n * p.HV + hv) * kHeadDim + d) * kHeadDim + v0;
+        const int ct = tid - 256;       // 0..255
+        const int d = ct & 127;         // the state row (and TMEM lane) of this thread
+        const int cg = ct >> 7;         // column half of the slice: columns 32 cg .. 32 cg + 31
+        const int64_t state_row = (((int64_t)n * p.HV + hv) * kHeadDim + d) * kHeadDim + v0 + 32 * cg;
         const uint32_t id_u = make_idesc(64, kVS, kFmtBF16, false, true);
         const uint32_t id_vn = make_idesc(64, kVS, kFmtBF16, false, true, true);
         const uint32_t id_s = make_idesc(128, kVS, kFmtBF16, true, true);
-        float S[kVS];
+        float S[32];
         if (p.h0) {
 #pragma unroll
-            for (int j = 0; j < kVS; j += 4) {
+            for (int j = 0; j < 32; j += 4) {
                 const float4 x4 = ld4(p.h0 + state_row + j);
                 S[j] = x4.x; S[j + 1] = x4.y; S[j + 2] = x4.z; S[j + 3] = x4.w;
             }
         } else {
 #pragma unroll
-            for (int j = 0; j < kVS; ++j) S[j] = 0.f;
+            for (int j = 0; j < 32; ++j) S[j] = 0.f;
         }
         if (nchunks == 0) {
             if (p.ht)
 #pragma unroll
-                for (int j = 0; j < kVS; j += 4)
+                for (int j = 0; j < 32; j += 4)
                     *reinterpret_cast<float4*>(p.ht + state_row + j) = make_float4(S[j], S[j + 1], S[j + 2], S[j + 3]);
         } else {
 #pragma unroll
-            for (int ch = 0; ch < 8; ++ch) put_chunk(sm + SSmem::SB, d, ch, S + 8 * ch);
+            for (int ch = 0; ch < 4; ++ch) put_chunk(sm + SSmem::SB, d, 4 * cg + ch, S + 8 * ch);
         }
         fence_async_smem();
-        named_sync(kBarChain, 128);
+        named_sync(kBarChain, kChainThreads);
+        // Shared-memory descriptors, built once: each MMA below only adds a byte offset.
+        const uint64_t dREC = sdesc_kmajor(sm + SSmem::REC, 0);   // K-major W, X diag(beta), P'
+        const uint64_t dQ = sdesc_kmajor(sm + SSmem::Q, 0);       // K-major Q
+        const uint64_t dKT = sdesc_mnmajor(sm + SSmem::K, kPanel); // K^T as an MN-major A
+        const uint64_t dV = sdesc_mnmajor(sm + SSmem::V, kPanel);
+        const uint64_t dSB = sdesc_mnmajor(sm + SSmem::SB, kPanel);
+        const uint64_t dVHI = sdesc_mnmajor(sm + SSmem::VHI, kPanel);
+        const uint64_t dVLO = sdesc_mnmajor(sm + SSmem::VLO, kPanel);
+        const uint64_t dVBF = sdesc_mnmajor(sm + SSmem::VBF, kPanel);
         // U(c) = (X diag beta) V into the lanes-A accumulator of parity c & 1
         auto issue_u = [&](int c) {
             const int s = c & 1;
-            const uint8_t* rec = sm + SSmem::REC + s * kRecBytes;
+            const uint64_t a = sdesc_add(dREC, s * kRecBytes + kRecXB), b = sdesc_add(dV, s * kPanel);
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
-                mma_f16(tb + kColVO + 64 * s, sdesc_kmajor(rec + kRecXB, kk * 32),
-                        sdesc_mnmajor(sm + SSmem::V + s * kPanel + kk * 2048, kPanel), id_u, kk > 0);
+                mma_f16(tb + kColVO + 64 * s, sdesc_add(a, kk * 32), sdesc_add(b, kk * 2048), id_u, kk > 0);
         };
         bool issued_any = false, issuer_ok = true;
         if (ct == 0 && nchunks > 0) {
@@ -750,10 +770,8 @@ __global__ void __launch_bounds__(384, 1) chunk_scan_kernel(const __grid_constan
             const uint32_t ph = c & 1, phs = (c >> 1) & 1;
             const uint32_t tVO = tb + kColVO + 64 * s;
             const uint8_t* rec = sm + SSmem::REC + s * kRecBytes;
-            const uint8_t* kt = sm + SSmem::K + s * 2 * kPanel;
-            const uint8_t* qt = sm + SSmem::Q + s * 2 * kPanel;
-            const bool landed = wait(&sh.full[s], phs, kSiteTmaLoad) && issuer_ok;
-            if (!named_sync_all(kBarChain, 128, landed)) {
+            const bool landed = spin(&sh.full[s], phs, kSiteTmaLoad) && issuer_ok;
+            if (!named_sync_all(kBarChain, kChainThreads, landed)) {
                 fail();
                 break;
             }
@@ -761,28 +779,28 @@ __global__ void __launch_bounds__(384, 1) chunk_scan_kernel(const __grid_constan
             const RecScalars* rs = reinterpret_cast<const RecScalars*>(rec + kRecSc);
             const float cei = rs->ce[half_row];
             const float decay = rs->dec;
-            // ---- VN = U - W S (lanes A, onto U); O = Q S (lanes B)
+            // ---- VN = U - W S (lanes A, onto U), committed alone; then O = Q S (lanes B)
             if (ct == 0) {
                 tc_fence_after();
+                const uint64_t aw = sdesc_add(dREC, s * kRecBytes + kRecW), aq = sdesc_add(dQ, s * 2 * kPanel);
 #pragma unroll
-                for (int kk = 0; kk < 8; ++kk) {
-                    const uint32_t po = (kk >> 2) * kPanel, ko = (kk & 3) * 32;
-                    const uint64_t bd = sdesc_mnmajor(sm + SSmem::SB + kk * 2048, kPanel);
-                    mma_f16(tVO, sdesc_kmajor(rec + kRecW + po, ko), bd, id_vn, 1);
-                    mma_f16(tVO + kHalfB, sdesc_kmajor(qt + po, ko), bd, id_u, kk > 0);
-                }
+                for (int kk = 0; kk < 8; ++kk)
+                    mma_f16(tVO, sdesc_add(aw, (kk >> 2) * kPanel + (kk & 3) * 32), sdesc_add(dSB, kk * 2048), id_vn, 1);
                 mma_commit(&sh.acc_vn[s]);
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk)
+                    mma_f16(tVO + kHalfB, sdesc_add(aq, (kk >> 2) * kPanel + (kk & 3) * 32), sdesc_add(dSB, kk * 2048),
+                            id_u, kk > 0);
             }
-            if (!named_sync_all(kBarChain, 128, wait(&sh.acc_vn[s], phs, kSiteMma))) {
+            if (!named_sync_all(kBarChain, kChainThreads, spin(&sh.acc_vn[s], phs, kSiteMma))) {
                 fail();
                 break;
             }
             tc_fence_after();
-            // ---- VN -> bf16 VN and the split ce VN
-#pragma unroll
-            for (int half = 0; half < 2; ++half) {
+            // ---- VN -> bf16 VN and the split ce VN, this warpgroup's 32 columns
+            {
                 float r[32];
-                tmem_ld32_wait(tVO + lane_base + 32 * half, r);  // lanes A: VN rows
+                tmem_ld32_wait(tVO + lane_base + 32 * cg, r);  // lanes A: VN rows
                 if (lanes_a) {
 #pragma unroll
                     for (int cc = 0; cc < 4; ++cc) {
@@ -793,7 +811,7 @@ __global__ void __launch_bounds__(384, 1) chunk_scan_kernel(const __grid_constan
                             hi[j] = round_bf16(x);
                             lo[j] = x - hi[j];
                         }
-                        const int ch = 4 * half + cc;
+                        const int ch = 4 * cg + cc;
                         put_chunk(sm + SSmem::VBF, half_row, ch, r + 8 * cc);
                         put_chunk(sm + SSmem::VHI, half_row, ch, hi);
                         put_chunk(sm + SSmem::VLO, half_row, ch, lo);
@@ -802,20 +820,23 @@ __global__ void __launch_bounds__(384, 1) chunk_scan_kernel(const __grid_constan
             }
             fence_async_smem();
             tc_fence_before();
-            named_sync(kBarChain, 128);
+            named_sync(kBarChain, kChainThreads);
             if (ct == 0) {
-                // dS = K^T hi + K^T lo (all lanes, fresh); O += P' VN (lanes B); then U of the
-                // next chunk, once its stage has landed and the epilogue has drained that parity
+                // dS = K^T hi + K^T lo (all lanes, fresh), committed alone; then O += P' VN
+                // (lanes B) and U of the next chunk, once its stage has landed and the epilogue
+                // has drained that parity
                 tc_fence_after();
+                const uint64_t ak = sdesc_add(dKT, s * 2 * kPanel), ap = sdesc_add(dREC, s * kRecBytes + kRecPM);
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
-                    const uint64_t ad = sdesc_mnmajor(kt + kk * 2048, kPanel);
-                    mma_f16(tb + kColDS, ad, sdesc_mnmajor(sm + SSmem::VHI + kk * 2048, kPanel), id_s, kk > 0);
-                    mma_f16(tb + kColDS, ad, sdesc_mnmajor(sm + SSmem::VLO + kk * 2048, kPanel), id_s, 1);
-                    mma_f16(tVO + kHalfB, sdesc_kmajor(rec + kRecPM, kk * 32),
-                            sdesc_mnmajor(sm + SSmem::VBF + kk * 2048, kPanel), id_u, 1);
+                    const uint64_t ad = sdesc_add(ak, kk * 2048);
+                    mma_f16(tb + kColDS, ad, sdesc_add(dVHI, kk * 2048), id_s, kk > 0);
+                    mma_f16(tb + kColDS, ad, sdesc_add(dVLO, kk * 2048), id_s, 1);
                 }
                 mma_commit(&sh.acc_s);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    mma_f16(tVO + kHalfB, sdesc_add(ap, kk * 32), sdesc_add(dVBF, kk * 2048), id_u, 1);
                 mma_commit(&sh.acc_o[s]);
                 mma_commit(&sh.empty[s]);
                 if (c + 1 < nchunks) {
@@ -827,31 +848,30 @@ __global__ void __launch_bounds__(384, 1) chunk_scan_kernel(const __grid_constan
                     }
                 }
             }
-            if (!named_sync_all(kBarChain, 128, wait(&sh.acc_s, ph, kSiteMma) && issuer_ok)) {
+            if (!named_sync_all(kBarChain, kChainThreads, spin(&sh.acc_s, ph, kSiteMma) && issuer_ok)) {
                 fail();
                 break;
             }
             tc_fence_after();
-            // ---- S <- 2^glast S + dS (32 columns at a time keeps the state in registers)
-#pragma unroll
-            for (int half = 0; half < 2; ++half) {
+            // ---- S <- 2^glast S + dS, this warpgroup's 32 columns
+            {
                 float r[32];
-                tmem_ld32_wait(tb + kColDS + lane_base + 32 * half, r);
+                tmem_ld32_wait(tb + kColDS + lane_base + 32 * cg, r);
 #pragma unroll
-                for (int j = 0; j < 32; ++j) S[32 * half + j] = fmaf(decay, S[32 * half + j], r[j]);
+                for (int j = 0; j < 32; ++j) S[j] = fmaf(decay, S[j], r[j]);
             }
             if (c + 1 == nchunks) {
                 if (p.ht)
 #pragma unroll
-                    for (int j = 0; j < kVS; j += 4)
+                    for (int j = 0; j < 32; j += 4)
                         *reinterpret_cast<float4*>(p.ht + state_row + j) = make_float4(S[j], S[j + 1], S[j + 2], S[j + 3]);
             } else {
 #pragma unroll
-                for (int ch = 0; ch < 8; ++ch) put_chunk(sm + SSmem::SB, d, ch, S + 8 * ch);
+                for (int ch = 0; ch < 4; ++ch) put_chunk(sm + SSmem::SB, d, 4 * cg + ch, S + 8 * ch);
             }
             fence_async_smem();
             tc_fence_before();
-            named_sync(kBarChain, 128);
+            named_sync(kBarChain, kChainThreads);
         }
         if (ct == 0 && issued_any) {
             mma_commit(&sh.drain);
@@ -959,7 +979,7 @@ int launch_chunk(const ChunkArgs& a, cudaStream_t s) {
         if (st != GDN_OK) return st;
     }
     dim3 grid((unsigned)(a.HV * (kHeadDim / kVS)), (unsigned)a.nseq);
-    chunk_scan_kernel<<<grid, 384, SSmem::BYTES, s>>>(sp);
+    chunk_scan_kernel<<<grid, kScanThreads, SSmem::BYTES, s>>>(sp);
     return launch_status();
 }
 

@@ -13,11 +13,13 @@ namespace gdn {
 
 constexpr int kMaxTaps = 8;
 
-// Prefill: one thread per (8 channels, token). It reads its K-token window with 16-byte
-// loads (neighbouring tokens' windows overlap in L1, so HBM sees every input once) and writes
-// 16 bytes of output. With cu_seqlens the window stops at the start of the token's sequence.
-__device__ __forceinline__ void load8(const bf16* p, float* out) {
-    const uint4 raw = *reinterpret_cast<const uint4*>(p);
+// Prefill: one thread per (8 channels, run of kConvRun tokens). It loads the run plus the
+// K - 1 tokens before it with 16-byte loads into registers (neighbouring runs re-read only
+// that halo) and writes 16 bytes per token. With cu_seqlens a tap before the start of the
+// token's sequence reads as zero, exactly like the zero padding of a per-sequence conv.
+constexpr int kConvRun = 4;
+
+__device__ __forceinline__ void unpack8(const uint4& raw, float* out) {
     const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -26,6 +28,8 @@ __device__ __forceinline__ void load8(const bf16* p, float* out) {
         out[2 * i + 1] = f.y;
     }
 }
+
+__device__ __forceinline__ void load8(const bf16* p, float* out) { unpack8(*reinterpret_cast<const uint4*>(p), out); }
 
 __device__ __forceinline__ void store8(bf16* p, const float* v) {
     uint4 raw;
@@ -42,17 +46,15 @@ __global__ void __launch_bounds__(128) conv1d_silu_kernel(const bf16* __restrict
                                                           int64_t C) {
     const int64_t c8 = ((int64_t)blockIdx.y * blockDim.x + threadIdx.x) * 8;
     if (c8 >= C) return;
-    const int64_t t = blockIdx.x;  // tokens on x: up to 2^31 - 1
+    const int64_t t0 = (int64_t)blockIdx.x * kConvRun;  // runs on x: up to 2^31 - 1
     const int64_t b = blockIdx.z;
-    int64_t seq_start = 0;
-    if (cu) {  // last sequence start <= t (binary search over nseq + 1 offsets)
-        int lo = 0, hi = nseq;
-        while (hi - lo > 1) {
-            const int mid = (lo + hi) >> 1;
-            if (cu[mid] <= t) lo = mid;
-            else hi = mid;
-        }
-        seq_start = cu[lo];
+    constexpr int R = kConvRun + K - 1;
+    uint4 raw[R];
+    const bf16* xb = x + b * sxb + c8;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const int64_t tt = t0 - (K - 1) + r;
+        raw[r] = (tt >= 0 && tt < T) ? __ldg(reinterpret_cast<const uint4*>(xb + tt * sxt)) : make_uint4(0, 0, 0, 0);
     }
     float wt[8][K];
     {
@@ -65,24 +67,43 @@ __global__ void __launch_bounds__(128) conv1d_silu_kernel(const bf16* __restrict
 #pragma unroll
             for (int i = 0; i < K; ++i) wt[j][i] = to_f32(wr[j * K + i]);
     }
-    float win[K][8];
-#pragma unroll
-    for (int i = 0; i < K; ++i) {
-        const int64_t tt = t - (K - 1) + i;
-        if (tt >= seq_start) load8(x + b * sxb + tt * sxt + c8, win[i]);
-        else
-#pragma unroll
-            for (int j = 0; j < 8; ++j) win[i][j] = 0.f;
+    int lo = 0;  // with cu_seqlens: the sequence of the current token
+    if (cu) {
+        int hi = nseq;
+        while (hi - lo > 1) {
+            const int mid = (lo + hi) >> 1;
+            if (cu[mid] <= t0) lo = mid;
+            else hi = mid;
+        }
     }
-    float out[8];
+    bf16* yb = y + (b * T + t0) * C + c8;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        float acc = 0.f;
+    for (int j = 0; j < kConvRun; ++j) {
+        const int64_t t = t0 + j;
+        if (t >= T) break;
+        int64_t seq_start = 0;
+        if (cu) {
+            while (lo + 1 < nseq && cu[lo + 1] <= t) ++lo;
+            seq_start = cu[lo];
+        }
+        float win[K][8];
 #pragma unroll
-        for (int i = 0; i < K; ++i) acc = __fadd_rn(acc, __fmul_rn(wt[j][i], win[i][j]));
-        out[j] = silu_f32(round_bf16(acc));
+        for (int i = 0; i < K; ++i) {
+            if (t - (K - 1) + i >= seq_start) unpack8(raw[j + i], win[i]);
+            else
+#pragma unroll
+                for (int q = 0; q < 8; ++q) win[i][q] = 0.f;
+        }
+        float out[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            float acc = 0.f;
+#pragma unroll
+            for (int i = 0; i < K; ++i) acc = __fadd_rn(acc, __fmul_rn(wt[q][i], win[i][q]));
+            out[q] = silu_f32(round_bf16(acc));
+        }
+        store8(yb + j * C, out);
     }
-    store8(y + (b * T + t) * C + c8, out);
 }
 
 int launch_conv1d_silu(const void* x, int64_t sxb, int64_t sxt, const void* w, void* y, const int32_t* cu, int64_t B,
@@ -90,7 +111,7 @@ int launch_conv1d_silu(const void* x, int64_t sxb, int64_t sxt, const void* w, v
     if (B == 0 || T == 0) return GDN_OK;
     constexpr int threads = 128;
     const int nseq = cu ? (int)B : 0;  // with cu_seqlens the caller passes the sequence count as B
-    dim3 grid((unsigned)T, (unsigned)((C / 8 + threads - 1) / threads), cu ? 1u : (unsigned)B);
+    dim3 grid((unsigned)((T + kConvRun - 1) / kConvRun), (unsigned)((C / 8 + threads - 1) / threads), cu ? 1u : (unsigned)B);
     auto xp = static_cast<const bf16*>(x);
     auto wp = static_cast<const bf16*>(w);
     auto yp = static_cast<bf16*>(y);

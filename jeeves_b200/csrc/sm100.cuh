@@ -91,7 +91,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int si
 // (so that one failed wait does not leave the other roles waiting out their own limits).
 // After a few failed polls the waiting warp backs off with nanosleep, so that a role that
 // waits for a long time leaves the issue slots of its SM sub-partition to the roles that work.
-__device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parity, int site, const int* abort) {
+// `backoff` = false keeps polling without sleeping, for waits on a latency-critical path.
+__device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parity, int site, const int* abort,
+                                                   bool backoff = true) {
     if (mbar_test(bar, parity)) return true;
     const long long start = clock64();
     uint32_t sleep_ns = 0;
@@ -101,6 +103,7 @@ __device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parit
             raise_device_error(site);
             return false;
         }
+        if (!backoff) continue;
         if (sleep_ns) __nanosleep(sleep_ns);
         sleep_ns = sleep_ns ? (sleep_ns < 256 ? 2 * sleep_ns : 256) : 32;
     }
@@ -219,6 +222,12 @@ __device__ __forceinline__ uint64_t sdesc_kmajor(const void* panel, uint32_t k_b
 // MN-major operand: LBO = distance between 128-byte MN panels, SBO = 1024 between 8-row K atoms.
 __device__ __forceinline__ uint64_t sdesc_mnmajor(const void* base, uint32_t panel_stride_bytes) {
     return make_sdesc(smem_u32(base), panel_stride_bytes, 1024);
+}
+
+// A descriptor moved by `byte_offset` bytes: the start address field holds address >> 4 in
+// its low 14 bits, and every operand here lies below 256 KB, so the add never carries out.
+__device__ __forceinline__ uint64_t sdesc_add(uint64_t desc, uint32_t byte_offset) {
+    return desc + (byte_offset >> 4);
 }
 
 // D[tmem] (+)= A[smem] * B[smem]; issued by one thread.
