@@ -549,32 +549,46 @@ struct ScanParams {
     int HV, rep;
 };
 
-struct SSmem {
-    static constexpr uint32_t K = 0;                         // [2] K tiles: two d-panels each
-    static constexpr uint32_t Q = K + 2 * 2 * kPanel;        // [2] Q tiles
-    static constexpr uint32_t V = Q + 2 * 2 * kPanel;        // [2] V slices: one panel each
-    static constexpr uint32_t REC = V + 2 * kPanel;          // [2] records
-    static constexpr uint32_t SB = REC + 2 * kRecBytes;      // S [d][v] bf16, MN-major, 128 rows
-    static constexpr uint32_t VHI = SB + 2 * kPanel;         // hi(ce VN) [tok][v]
-    static constexpr uint32_t VLO = VHI + kPanel;            // lo(ce VN)
-    static constexpr uint32_t VBF = VLO + kPanel;            // VN [tok][v]
-    static constexpr uint32_t END = VBF + kPanel;
-    static constexpr uint32_t BYTES = END + 1024;            // + alignment slack
+// One pipeline stage (81 KB). Three 128-row K-major operands stack two 64-row factors each, so
+// that one M=128 product serves both the state update and the output:
+//   WQ = [W; Q] per d-panel  (W from the record, Q from the q tile)
+//   XZ = [X diag(beta); 0]   ZP = [0; P']   (the zero panel is shared by both)
+struct SStage {
+    static constexpr uint32_t WQ = 0;                 // [W0][Q0][W1][Q1], 8 KB each
+    static constexpr uint32_t XZ = 4 * kPanel;        // X diag(beta), then the zero panel
+    static constexpr uint32_t ZP = 5 * kPanel;        // the zero panel, then P'
+    static constexpr uint32_t SC = 7 * kPanel;        // RecScalars
+    static constexpr uint32_t K = SC + 1024;          // K tile (two d-panels)
+    static constexpr uint32_t V = K + 2 * kPanel;     // V slice (one panel)
+    static constexpr uint32_t BYTES = V + kPanel;
+    static constexpr uint32_t TX = 2 * 4 * kPanel / 2 + 2 * kPanel + 1024 + 2 * kPanel + kPanel;  // bytes landing
 };
-static_assert(SSmem::REC % 1024 == 0 && kRecBytes % 1024 == 0 && SSmem::SB % 1024 == 0, "swizzle atoms");
+static_assert(SStage::TX == 4 * kPanel + 2 * kPanel + 1024 + 3 * kPanel, "W, Q, X diag(beta), P', scalars, K, V");
+
+struct SSmem {
+    static constexpr uint32_t ST = 0;                         // [2] stages
+    static constexpr uint32_t SB = 2 * SStage::BYTES;         // S [d][v] bf16, MN-major, 128 rows
+    static constexpr uint32_t VHI = SB + 2 * kPanel;          // hi(ce VN) [tok][v]
+    static constexpr uint32_t VLO = VHI + kPanel;             // lo(ce VN)
+    static constexpr uint32_t VBF = VLO + kPanel;             // VN [tok][v]
+    static constexpr uint32_t END = VBF + kPanel;
+    static constexpr uint32_t BYTES = END + 1024;             // + alignment slack
+};
+static_assert(SStage::BYTES % 1024 == 0 && SStage::K % 1024 == 0 && SSmem::SB % 1024 == 0, "swizzle atoms");
 
 struct SShared {
-    uint64_t full[2], empty[2], acc_vn[2], acc_s, acc_o[2], o_free[2], drain;
+    uint64_t full[2], empty[2], u_done[2], acc_vn[2], vn_ready[2], acc_o[2], o_free[2], acc_s;
+    uint64_t drain_chain, drain_helper;
     uint32_t tmem_base;
     int abort;
 };
 
-constexpr uint32_t kScanTmemCols = 256;
-constexpr uint32_t kColDS = 0;    // dS = K^T (hi + lo), all lanes, 64 columns
-constexpr uint32_t kColVO = 64;   // per parity (64 + 64 * parity): U -> VN lanes A, O lanes B
-
-constexpr int kScanThreads = 512;  // warp 0 loader, 4-7 epilogue, 8-15 chain (two column halves)
+constexpr int kScanThreads = 512;  // warp 0 loader, 1 MMA helper, 6-7 epilogue, 8-15 chain
 constexpr int kChainThreads = 256;
+constexpr int kEpiThreads = 64;
+constexpr uint32_t kScanTmemCols = 256;
+constexpr uint32_t kColDS = 0;    // dS = K^T (hi + lo), 64 columns
+constexpr uint32_t kColD = 64;    // per parity (64 + 64 * parity): VN in lanes 0-63, -O in lanes 64-127
 
 __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __grid_constant__ ScanParams p) {
     extern __shared__ uint8_t smem_raw[];
@@ -582,6 +596,8 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
     __shared__ SShared sh;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int quarter = warp & 3;                                   // TMEM lane quarter of this warp
+    const uint32_t lane_base = (uint32_t)(32 * quarter) << 16;
     constexpr int kSlices = kHeadDim / kVS;
     const int hv = blockIdx.x / kSlices;
     const int v0 = (blockIdx.x % kSlices) * kVS;
@@ -595,21 +611,21 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
         slot0 = bos / 64 + n;
     }
     const int nchunks = (int)((len + 63) / 64);
-    const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;  // TMEM lane quarter of this warp
-    const int half_row = 16 * (warp & 3) + (lane & 15);           // row of an M=64 accumulator
-    const bool lanes_a = lane < 16;
 
     if (tid == 0) {
         sh.abort = 0;
         for (int s = 0; s < 2; ++s) {
             mbar_init(&sh.full[s], 1);
-            mbar_init(&sh.empty[s], 2);  // the chain's MMAs and the epilogue
+            mbar_init(&sh.empty[s], 3);  // the chain's and the helper's MMAs, and the epilogue
+            mbar_init(&sh.u_done[s], 1);
             mbar_init(&sh.acc_vn[s], 1);
+            mbar_init(&sh.vn_ready[s], 1);
             mbar_init(&sh.acc_o[s], 1);
             mbar_init(&sh.o_free[s], 1);
         }
         mbar_init(&sh.acc_s, 1);
-        mbar_init(&sh.drain, 1);
+        mbar_init(&sh.drain_chain, 1);
+        mbar_init(&sh.drain_helper, 1);
         fence_mbar_init();
         tma_prefetch_map(&p.tm_q);
         tma_prefetch_map(&p.tm_k);
@@ -619,6 +635,12 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
         tmem_alloc(&sh.tmem_base, kScanTmemCols);
         tmem_relinquish();
     }
+    // the zero panel of both stages (never written by a copy)
+    for (int i = tid; i < 2 * (int)(kPanel / 16); i += kScanThreads) {
+        const int s = i / (int)(kPanel / 16), j = i % (int)(kPanel / 16);
+        reinterpret_cast<uint4*>(sm + SSmem::ST + s * SStage::BYTES + SStage::ZP)[j] = make_uint4(0, 0, 0, 0);
+    }
+    fence_async_smem();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -634,6 +656,10 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
         const int64_t rest = len - 64 * (int64_t)c;
         return (int)(rest < 64 ? rest : 64);
     };
+    auto stage = [&](int s) -> uint8_t* { return sm + SSmem::ST + s * SStage::BYTES; };
+    const uint32_t id_pos = make_idesc(128, kVS, kFmtBF16, false, true);        // D (+)= A B
+    const uint32_t id_neg = make_idesc(128, kVS, kFmtBF16, false, true, true);  // D += -A B
+    const uint32_t id_s = make_idesc(128, kVS, kFmtBF16, true, true);
 
     if (warp == 0) {
         // ================================ loader ================================
@@ -649,16 +675,20 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
             }
             if (lane == 0) {
                 const int t = (int)(bos + 64 * c);
-                mbar_arrive_expect_tx(&sh.full[s], 5 * kPanel + kRecBytes);
-                uint8_t* kt = sm + SSmem::K + s * 2 * kPanel;
-                uint8_t* qt = sm + SSmem::Q + s * 2 * kPanel;
-                tma_load_4d(kt, &p.tm_k, &sh.full[s], 0, h, t, (int)brow);
-                tma_load_4d(kt + kPanel, &p.tm_k, &sh.full[s], 64, h, t, (int)brow);
-                tma_load_4d(qt, &p.tm_q, &sh.full[s], 0, h, t, (int)brow);
-                tma_load_4d(qt + kPanel, &p.tm_q, &sh.full[s], 64, h, t, (int)brow);
-                tma_load_4d(sm + SSmem::V + s * kPanel, &p.tm_v, &sh.full[s], v0, hv, t, (int)brow);
-                bulk_load(sm + SSmem::REC + s * kRecBytes,
-                          p.records + ((slot0 + c) * p.HV + hv) * (int64_t)kRecBytes, kRecBytes, &sh.full[s]);
+                uint8_t* st = stage(s);
+                const uint8_t* rec = p.records + ((slot0 + c) * p.HV + hv) * (int64_t)kRecBytes;
+                uint64_t* bar = &sh.full[s];
+                mbar_arrive_expect_tx(bar, SStage::TX);
+                bulk_load(st + SStage::WQ, rec + kRecW, kPanel, bar);
+                bulk_load(st + SStage::WQ + 2 * kPanel, rec + kRecW + kPanel, kPanel, bar);
+                tma_load_4d(st + SStage::WQ + kPanel, &p.tm_q, bar, 0, h, t, (int)brow);
+                tma_load_4d(st + SStage::WQ + 3 * kPanel, &p.tm_q, bar, 64, h, t, (int)brow);
+                bulk_load(st + SStage::XZ, rec + kRecXB, kPanel, bar);
+                bulk_load(st + SStage::ZP + kPanel, rec + kRecPM, kPanel, bar);
+                bulk_load(st + SStage::SC, rec + kRecSc, 1024, bar);
+                tma_load_4d(st + SStage::K, &p.tm_k, bar, 0, h, t, (int)brow);
+                tma_load_4d(st + SStage::K + kPanel, &p.tm_k, bar, 64, h, t, (int)brow);
+                tma_load_4d(st + SStage::V, &p.tm_v, bar, v0, hv, t, (int)brow);
                 issued[s] = c + 1;
             }
             __syncwarp();
@@ -667,28 +697,75 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
         if (lane == 0)
             for (int s = 0; s < 2; ++s)
                 if (issued[s]) mbar_wait(&sh.full[s], ((issued[s] - 1) >> 1) & 1, kSiteDrain);
-    } else if (warp >= 4 && warp < 8) {
+    } else if (warp == 1) {
+        // ============================== MMA helper ==============================
+        // Issues the products off the chain's critical path: U(c) = [X diag(beta); 0] V into
+        // the accumulator of parity c & 1, and, once the chain has read VN out, the output
+        // part -[0; P'] VN. Ordering with the chain's own MMAs goes through mbarriers.
+        if (lane == 0 && nchunks > 0) {
+            const uint64_t dVBF = sdesc_mnmajor(sm + SSmem::VBF, kPanel);
+            auto issue_u = [&](int c) {
+                const int s = c & 1;
+                const uint64_t a = sdesc_kmajor(stage(s) + SStage::XZ, 0), b = sdesc_mnmajor(stage(s) + SStage::V, kPanel);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    mma_f16(tb + kColD + 64 * s, sdesc_add(a, kk * 32), sdesc_add(b, kk * 2048), id_pos, kk > 0);
+                mma_commit(&sh.u_done[s]);
+            };
+            bool issued_any = false;
+            if (wait(&sh.full[0], 0, kSiteTmaLoad)) {
+                tc_fence_after();
+                issue_u(0);
+                issued_any = true;
+                for (int c = 0; c < nchunks; ++c) {
+                    const int s = c & 1;
+                    if (!wait(&sh.vn_ready[s], (c >> 1) & 1, kSiteMma)) { fail(); break; }
+                    tc_fence_after();
+                    const uint64_t a = sdesc_kmajor(stage(s) + SStage::ZP, 0);
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk)
+                        mma_f16(tb + kColD + 64 * s, sdesc_add(a, kk * 32), sdesc_add(dVBF, kk * 2048), id_neg, 1);
+                    mma_commit(&sh.acc_o[s]);
+                    mma_commit(&sh.empty[s]);
+                    if (c + 1 < nchunks) {
+                        bool ok = wait(&sh.full[s ^ 1], ((c + 1) >> 1) & 1, kSiteTmaLoad);
+                        if (ok && c >= 1) ok = wait(&sh.o_free[s ^ 1], ((c - 1) >> 1) & 1, kSiteMma);
+                        if (!ok) { fail(); break; }
+                        tc_fence_after();
+                        issue_u(c + 1);
+                    }
+                }
+            } else {
+                fail();
+            }
+            if (issued_any) {
+                mma_commit(&sh.drain_helper);
+                mbar_wait(&sh.drain_helper, 0, kSiteDrain);
+            }
+        }
+    } else if (warp == 6 || warp == 7) {
         // =============================== epilogue ===============================
-        const int et = tid - 128;
+        // -O sits in TMEM lanes 64-127 (rows 0-63 of the lower half of the M=128 accumulator).
+        const int et = tid - 192;        // 0..63
+        const int row = et;              // output row of this thread (lane quarter 2 or 3)
         for (int c = 0; c < nchunks; ++c) {
             const int s = c & 1;
             const uint32_t phs = (c >> 1) & 1;
-            const uint32_t tVO = tb + kColVO + 64 * s;
+            const uint32_t tD = tb + kColD + 64 * s;
             const bool ok = wait(&sh.acc_o[s], phs, kSiteMma) && wait(&sh.full[s], phs, kSiteTmaLoad);
-            if (!named_sync_all(kBarEpi, 128, ok)) {
+            if (!named_sync_all(kBarEpi, kEpiThreads, ok)) {
                 fail();
                 break;
             }
             tc_fence_after();
-            const RecScalars* rs = reinterpret_cast<const RecScalars*>(sm + SSmem::REC + s * kRecBytes + kRecSc);
-            const int i = half_row;
-            const bool store = !lanes_a && i < nvalid_of(c);
-            const float eqi = rs->eq[i];
-            bf16* orow = p.o + ((brow * p.T + bos + 64 * (int64_t)c + i) * p.HV + hv) * kHeadDim + v0;
+            const RecScalars* rs = reinterpret_cast<const RecScalars*>(stage(s) + SStage::SC);
+            const bool store = row < nvalid_of(c);
+            const float neg_eq = -rs->eq[row];
+            bf16* orow = p.o + ((brow * p.T + bos + 64 * (int64_t)c + row) * p.HV + hv) * kHeadDim + v0;
 #pragma unroll
             for (int half = 0; half < 2; ++half) {
                 float r[32];
-                tmem_ld32_wait(tVO + lane_base + 32 * half, r);  // lanes B: O rows
+                tmem_ld32_wait(tD + lane_base + 32 * half, r);
                 if (store) {
 #pragma unroll
                     for (int ch = 0; ch < 4; ++ch) {
@@ -696,13 +773,13 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
                         __nv_bfloat162* hh = reinterpret_cast<__nv_bfloat162*>(&raw);
 #pragma unroll
                         for (int j = 0; j < 4; ++j)
-                            hh[j] = __floats2bfloat162_rn(eqi * r[8 * ch + 2 * j], eqi * r[8 * ch + 2 * j + 1]);
+                            hh[j] = __floats2bfloat162_rn(neg_eq * r[8 * ch + 2 * j], neg_eq * r[8 * ch + 2 * j + 1]);
                         *reinterpret_cast<uint4*>(orow + 32 * half + 8 * ch) = raw;
                     }
                 }
             }
             tc_fence_before();
-            named_sync(kBarEpi, 128);
+            named_sync(kBarEpi, kEpiThreads);
             if (et == 0) {
                 mbar_arrive(&sh.o_free[s]);
                 mbar_arrive(&sh.empty[s]);
@@ -713,10 +790,9 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
         const int ct = tid - 256;       // 0..255
         const int d = ct & 127;         // the state row (and TMEM lane) of this thread
         const int cg = ct >> 7;         // column half of the slice: columns 32 cg .. 32 cg + 31
+        const bool vn_rows = quarter < 2;  // lanes 0-63 hold VN: token row 32 quarter + lane
+        const int vrow = 32 * quarter + lane;
         const int64_t state_row = (((int64_t)n * p.HV + hv) * kHeadDim + d) * kHeadDim + v0 + 32 * cg;
-        const uint32_t id_u = make_idesc(64, kVS, kFmtBF16, false, true);
-        const uint32_t id_vn = make_idesc(64, kVS, kFmtBF16, false, true, true);
-        const uint32_t id_s = make_idesc(128, kVS, kFmtBF16, true, true);
         float S[32];
         if (p.h0) {
 #pragma unroll
@@ -739,94 +815,69 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
         }
         fence_async_smem();
         named_sync(kBarChain, kChainThreads);
-        // Shared-memory descriptors, built once: each MMA below only adds a byte offset.
-        const uint64_t dREC = sdesc_kmajor(sm + SSmem::REC, 0);   // K-major W, X diag(beta), P'
-        const uint64_t dQ = sdesc_kmajor(sm + SSmem::Q, 0);       // K-major Q
-        const uint64_t dKT = sdesc_mnmajor(sm + SSmem::K, kPanel); // K^T as an MN-major A
-        const uint64_t dV = sdesc_mnmajor(sm + SSmem::V, kPanel);
         const uint64_t dSB = sdesc_mnmajor(sm + SSmem::SB, kPanel);
         const uint64_t dVHI = sdesc_mnmajor(sm + SSmem::VHI, kPanel);
         const uint64_t dVLO = sdesc_mnmajor(sm + SSmem::VLO, kPanel);
-        const uint64_t dVBF = sdesc_mnmajor(sm + SSmem::VBF, kPanel);
-        // U(c) = (X diag beta) V into the lanes-A accumulator of parity c & 1
-        auto issue_u = [&](int c) {
-            const int s = c & 1;
-            const uint64_t a = sdesc_add(dREC, s * kRecBytes + kRecXB), b = sdesc_add(dV, s * kPanel);
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-                mma_f16(tb + kColVO + 64 * s, sdesc_add(a, kk * 32), sdesc_add(b, kk * 2048), id_u, kk > 0);
-        };
-        bool issued_any = false, issuer_ok = true;
-        if (ct == 0 && nchunks > 0) {
-            issuer_ok = wait(&sh.full[0], 0, kSiteTmaLoad);
-            if (issuer_ok) {
-                tc_fence_after();
-                issue_u(0);
-                issued_any = true;
-            }
-        }
+        bool issued_any = false;
         for (int c = 0; c < nchunks; ++c) {
             const int s = c & 1;
             const uint32_t ph = c & 1, phs = (c >> 1) & 1;
-            const uint32_t tVO = tb + kColVO + 64 * s;
-            const uint8_t* rec = sm + SSmem::REC + s * kRecBytes;
-            const bool landed = spin(&sh.full[s], phs, kSiteTmaLoad) && issuer_ok;
+            const uint32_t tD = tb + kColD + 64 * s;
+            uint8_t* st = stage(s);
+            const bool landed = spin(&sh.full[s], phs, kSiteTmaLoad) && spin(&sh.u_done[s], phs, kSiteMma);
             if (!named_sync_all(kBarChain, kChainThreads, landed)) {
                 fail();
                 break;
             }
             // the stage can be refilled once the MMAs below are done: read its scalars now
-            const RecScalars* rs = reinterpret_cast<const RecScalars*>(rec + kRecSc);
-            const float cei = rs->ce[half_row];
+            const RecScalars* rs = reinterpret_cast<const RecScalars*>(st + SStage::SC);
+            const float cei = rs->ce[vrow & 63];
             const float decay = rs->dec;
-            // ---- VN = U - W S (lanes A, onto U), committed alone; then O = Q S (lanes B)
+            // ---- D -= [W; Q] S: VN = U - W S (lanes 0-63), -Q S (lanes 64-127)
             if (ct == 0) {
                 tc_fence_after();
-                const uint64_t aw = sdesc_add(dREC, s * kRecBytes + kRecW), aq = sdesc_add(dQ, s * 2 * kPanel);
+                const uint64_t a = sdesc_kmajor(st + SStage::WQ, 0);
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk)
-                    mma_f16(tVO, sdesc_add(aw, (kk >> 2) * kPanel + (kk & 3) * 32), sdesc_add(dSB, kk * 2048), id_vn, 1);
+                    mma_f16(tD, sdesc_add(a, (kk >> 2) * 2 * kPanel + (kk & 3) * 32), sdesc_add(dSB, kk * 2048), id_neg, 1);
                 mma_commit(&sh.acc_vn[s]);
-#pragma unroll
-                for (int kk = 0; kk < 8; ++kk)
-                    mma_f16(tVO + kHalfB, sdesc_add(aq, (kk >> 2) * kPanel + (kk & 3) * 32), sdesc_add(dSB, kk * 2048),
-                            id_u, kk > 0);
+                issued_any = true;
             }
-            if (!named_sync_all(kBarChain, kChainThreads, spin(&sh.acc_vn[s], phs, kSiteMma))) {
+            // VN is read out once the previous chunk's output product is done with VBF
+            bool ready = spin(&sh.acc_vn[s], phs, kSiteMma);
+            if (ready && c >= 1) ready = spin(&sh.acc_o[s ^ 1], ((c - 1) >> 1) & 1, kSiteMma);
+            if (!named_sync_all(kBarChain, kChainThreads, ready)) {
                 fail();
                 break;
             }
             tc_fence_after();
             // ---- VN -> bf16 VN and the split ce VN, this warpgroup's 32 columns
-            {
+            if (vn_rows) {
                 float r[32];
-                tmem_ld32_wait(tVO + lane_base + 32 * cg, r);  // lanes A: VN rows
-                if (lanes_a) {
+                tmem_ld32_wait(tD + lane_base + 32 * cg, r);
 #pragma unroll
-                    for (int cc = 0; cc < 4; ++cc) {
-                        float hi[8], lo[8];
+                for (int cc = 0; cc < 4; ++cc) {
+                    float hi[8], lo[8];
 #pragma unroll
-                        for (int j = 0; j < 8; ++j) {
-                            const float x = cei * r[8 * cc + j];
-                            hi[j] = round_bf16(x);
-                            lo[j] = x - hi[j];
-                        }
-                        const int ch = 4 * cg + cc;
-                        put_chunk(sm + SSmem::VBF, half_row, ch, r + 8 * cc);
-                        put_chunk(sm + SSmem::VHI, half_row, ch, hi);
-                        put_chunk(sm + SSmem::VLO, half_row, ch, lo);
+                    for (int j = 0; j < 8; ++j) {
+                        const float x = cei * r[8 * cc + j];
+                        hi[j] = round_bf16(x);
+                        lo[j] = x - hi[j];
                     }
+                    const int ch = 4 * cg + cc;
+                    put_chunk(sm + SSmem::VBF, vrow, ch, r + 8 * cc);
+                    put_chunk(sm + SSmem::VHI, vrow, ch, hi);
+                    put_chunk(sm + SSmem::VLO, vrow, ch, lo);
                 }
             }
             fence_async_smem();
             tc_fence_before();
             named_sync(kBarChain, kChainThreads);
             if (ct == 0) {
-                // dS = K^T hi + K^T lo (all lanes, fresh), committed alone; then O += P' VN
-                // (lanes B) and U of the next chunk, once its stage has landed and the epilogue
-                // has drained that parity
+                mbar_arrive(&sh.vn_ready[s]);  // the helper adds -[0; P'] VN
+                // dS = K^T hi + K^T lo (all lanes, fresh)
                 tc_fence_after();
-                const uint64_t ak = sdesc_add(dKT, s * 2 * kPanel), ap = sdesc_add(dREC, s * kRecBytes + kRecPM);
+                const uint64_t ak = sdesc_mnmajor(st + SStage::K, kPanel);
 #pragma unroll
                 for (int kk = 0; kk < 4; ++kk) {
                     const uint64_t ad = sdesc_add(ak, kk * 2048);
@@ -834,21 +885,9 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
                     mma_f16(tb + kColDS, ad, sdesc_add(dVLO, kk * 2048), id_s, 1);
                 }
                 mma_commit(&sh.acc_s);
-#pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    mma_f16(tVO + kHalfB, sdesc_add(ap, kk * 32), sdesc_add(dVBF, kk * 2048), id_u, 1);
-                mma_commit(&sh.acc_o[s]);
                 mma_commit(&sh.empty[s]);
-                if (c + 1 < nchunks) {
-                    issuer_ok = wait(&sh.full[s ^ 1], ((c + 1) >> 1) & 1, kSiteTmaLoad);
-                    if (issuer_ok && c >= 1) issuer_ok = wait(&sh.o_free[s ^ 1], ((c - 1) >> 1) & 1, kSiteMma);
-                    if (issuer_ok) {
-                        tc_fence_after();
-                        issue_u(c + 1);
-                    }
-                }
             }
-            if (!named_sync_all(kBarChain, kChainThreads, spin(&sh.acc_s, ph, kSiteMma) && issuer_ok)) {
+            if (!named_sync_all(kBarChain, kChainThreads, spin(&sh.acc_s, ph, kSiteMma))) {
                 fail();
                 break;
             }
@@ -874,8 +913,8 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
             named_sync(kBarChain, kChainThreads);
         }
         if (ct == 0 && issued_any) {
-            mma_commit(&sh.drain);
-            mbar_wait(&sh.drain, 0, kSiteDrain);
+            mma_commit(&sh.drain_chain);
+            mbar_wait(&sh.drain_chain, 0, kSiteDrain);
         }
     }
 
