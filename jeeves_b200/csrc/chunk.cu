@@ -553,6 +553,10 @@ struct ScanParams {
 // that one M=128 product serves both the state update and the output:
 //   WQ = [W; Q] per d-panel  (W from the record, Q from the q tile)
 //   XZ = [X diag(beta); 0]   ZP = [0; P']   (the zero panel is shared by both)
+// A stage fills as two parts with their own barriers: part A (W, Q, X diag(beta), V) is free
+// again as soon as the chain's [W; Q] S product is done, so the next-but-one chunk's part A
+// streams in early; part B (P', scalars, K) once the chain's dS and the helper's output
+// product are done (the epilogue reads its row scales from the record in global memory).
 struct SStage {
     static constexpr uint32_t WQ = 0;                 // [W0][Q0][W1][Q1], 8 KB each
     static constexpr uint32_t XZ = 4 * kPanel;        // X diag(beta), then the zero panel
@@ -561,9 +565,9 @@ struct SStage {
     static constexpr uint32_t K = SC + 1024;          // K tile (two d-panels)
     static constexpr uint32_t V = K + 2 * kPanel;     // V slice (one panel)
     static constexpr uint32_t BYTES = V + kPanel;
-    static constexpr uint32_t TX = 2 * 4 * kPanel / 2 + 2 * kPanel + 1024 + 2 * kPanel + kPanel;  // bytes landing
+    static constexpr uint32_t TX_A = 4 * kPanel + kPanel + kPanel;   // W, Q, X diag(beta), V
+    static constexpr uint32_t TX_B = kPanel + 1024 + 2 * kPanel;     // P', scalars, K
 };
-static_assert(SStage::TX == 4 * kPanel + 2 * kPanel + 1024 + 3 * kPanel, "W, Q, X diag(beta), P', scalars, K, V");
 
 struct SSmem {
     static constexpr uint32_t ST = 0;                         // [2] stages
@@ -577,7 +581,8 @@ struct SSmem {
 static_assert(SStage::BYTES % 1024 == 0 && SStage::K % 1024 == 0 && SSmem::SB % 1024 == 0, "swizzle atoms");
 
 struct SShared {
-    uint64_t full[2], empty[2], u_done[2], acc_vn[2], vn_ready[2], acc_o[2], o_free[2], acc_s;
+    uint64_t full_a[2], full_b[2], empty_a[2], empty_b[2];
+    uint64_t u_done[2], acc_vn[2], ds_issued[2], acc_o[2], o_free[2], acc_s;
     uint64_t drain_chain, drain_helper;
     uint32_t tmem_base;
     int abort;
@@ -615,11 +620,13 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
     if (tid == 0) {
         sh.abort = 0;
         for (int s = 0; s < 2; ++s) {
-            mbar_init(&sh.full[s], 1);
-            mbar_init(&sh.empty[s], 3);  // the chain's and the helper's MMAs, and the epilogue
+            mbar_init(&sh.full_a[s], 1);
+            mbar_init(&sh.full_b[s], 1);
+            mbar_init(&sh.empty_a[s], 1);  // the chain's [W; Q] S product
+            mbar_init(&sh.empty_b[s], 2);  // the chain's dS and the helper's output product
             mbar_init(&sh.u_done[s], 1);
             mbar_init(&sh.acc_vn[s], 1);
-            mbar_init(&sh.vn_ready[s], 1);
+            mbar_init(&sh.ds_issued[s], 1);
             mbar_init(&sh.acc_o[s], 1);
             mbar_init(&sh.o_free[s], 1);
         }
@@ -663,45 +670,63 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
 
     if (warp == 0) {
         // ================================ loader ================================
-        int issued[2] = {0, 0};
+        int issued[2] = {0, 0};  // 1 + chunk of the last copy started per stage; negative: both parts
         for (int c = 0; c < nchunks; ++c) {
             const int s = c & 1;
+            const int t = (int)(bos + 64 * c);
+            uint8_t* st = stage(s);
+            const uint8_t* rec = p.records + ((slot0 + c) * p.HV + hv) * (int64_t)kRecBytes;
             if (c >= 2) {
-                const bool w = wait(&sh.empty[s], ((c >> 1) + 1) & 1, kSiteTmaLoad);
+                const bool w = wait(&sh.empty_a[s], ((c >> 1) + 1) & 1, kSiteTmaLoad);
                 if (!__all_sync(0xffffffffu, w)) {
                     fail();
                     break;
                 }
             }
             if (lane == 0) {
-                const int t = (int)(bos + 64 * c);
-                uint8_t* st = stage(s);
-                const uint8_t* rec = p.records + ((slot0 + c) * p.HV + hv) * (int64_t)kRecBytes;
-                uint64_t* bar = &sh.full[s];
-                mbar_arrive_expect_tx(bar, SStage::TX);
+                uint64_t* bar = &sh.full_a[s];
+                mbar_arrive_expect_tx(bar, SStage::TX_A);
                 bulk_load(st + SStage::WQ, rec + kRecW, kPanel, bar);
                 bulk_load(st + SStage::WQ + 2 * kPanel, rec + kRecW + kPanel, kPanel, bar);
                 tma_load_4d(st + SStage::WQ + kPanel, &p.tm_q, bar, 0, h, t, (int)brow);
                 tma_load_4d(st + SStage::WQ + 3 * kPanel, &p.tm_q, bar, 64, h, t, (int)brow);
                 bulk_load(st + SStage::XZ, rec + kRecXB, kPanel, bar);
+                tma_load_4d(st + SStage::V, &p.tm_v, bar, v0, hv, t, (int)brow);
+                issued[s] = c + 1;
+            }
+            if (c >= 2) {
+                const bool w = wait(&sh.empty_b[s], ((c >> 1) + 1) & 1, kSiteTmaLoad);
+                if (!__all_sync(0xffffffffu, w)) {
+                    fail();
+                    break;
+                }
+            }
+            if (lane == 0) {
+                uint64_t* bar = &sh.full_b[s];
+                mbar_arrive_expect_tx(bar, SStage::TX_B);
                 bulk_load(st + SStage::ZP + kPanel, rec + kRecPM, kPanel, bar);
                 bulk_load(st + SStage::SC, rec + kRecSc, 1024, bar);
                 tma_load_4d(st + SStage::K, &p.tm_k, bar, 0, h, t, (int)brow);
                 tma_load_4d(st + SStage::K + kPanel, &p.tm_k, bar, 64, h, t, (int)brow);
-                tma_load_4d(st + SStage::V, &p.tm_v, bar, v0, hv, t, (int)brow);
-                issued[s] = c + 1;
+                issued[s] = -(c + 1);
             }
             __syncwarp();
         }
         // let every copy this warp started land before the CTA can exit
         if (lane == 0)
-            for (int s = 0; s < 2; ++s)
-                if (issued[s]) mbar_wait(&sh.full[s], ((issued[s] - 1) >> 1) & 1, kSiteDrain);
+            for (int s = 0; s < 2; ++s) {
+                const int c = (issued[s] < 0 ? -issued[s] : issued[s]) - 1;
+                if (c < 0) continue;
+                mbar_wait(&sh.full_a[s], (c >> 1) & 1, kSiteDrain);
+                if (issued[s] < 0) mbar_wait(&sh.full_b[s], (c >> 1) & 1, kSiteDrain);
+            }
     } else if (warp == 1) {
         // ============================== MMA helper ==============================
-        // Issues the products off the chain's critical path: U(c) = [X diag(beta); 0] V into
-        // the accumulator of parity c & 1, and, once the chain has read VN out, the output
-        // part -[0; P'] VN. Ordering with the chain's own MMAs goes through mbarriers.
+        // Issues the products off the chain's critical path. U(c+1) = [X diag(beta); 0] V goes
+        // into the accumulator of parity (c+1) & 1 as soon as the chain's [W; Q] S product of
+        // chunk c is done (so it never delays it) and its inputs have landed; the output part
+        // -[0; P'] VN of chunk c queues behind the chain's dS. Ordering with the chain's MMAs
+        // goes through mbarriers.
         if (lane == 0 && nchunks > 0) {
             const uint64_t dVBF = sdesc_mnmajor(sm + SSmem::VBF, kPanel);
             auto issue_u = [&](int c) {
@@ -713,27 +738,29 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
                 mma_commit(&sh.u_done[s]);
             };
             bool issued_any = false;
-            if (wait(&sh.full[0], 0, kSiteTmaLoad)) {
+            if (wait(&sh.full_a[0], 0, kSiteTmaLoad)) {
                 tc_fence_after();
                 issue_u(0);
                 issued_any = true;
                 for (int c = 0; c < nchunks; ++c) {
                     const int s = c & 1;
-                    if (!wait(&sh.vn_ready[s], (c >> 1) & 1, kSiteMma)) { fail(); break; }
+                    const uint32_t phs = (c >> 1) & 1;
+                    if (c + 1 < nchunks) {
+                        bool ok = wait(&sh.acc_vn[s], phs, kSiteMma);
+                        if (ok) ok = wait(&sh.full_a[s ^ 1], ((c + 1) >> 1) & 1, kSiteTmaLoad);
+                        if (ok && c >= 1) ok = wait(&sh.o_free[s ^ 1], ((c - 1) >> 1) & 1, kSiteMma);
+                        if (!ok) { fail(); break; }
+                        tc_fence_after();
+                        issue_u(c + 1);
+                    }
+                    if (!wait(&sh.ds_issued[s], phs, kSiteMma)) { fail(); break; }
                     tc_fence_after();
                     const uint64_t a = sdesc_kmajor(stage(s) + SStage::ZP, 0);
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk)
                         mma_f16(tb + kColD + 64 * s, sdesc_add(a, kk * 32), sdesc_add(dVBF, kk * 2048), id_neg, 1);
                     mma_commit(&sh.acc_o[s]);
-                    mma_commit(&sh.empty[s]);
-                    if (c + 1 < nchunks) {
-                        bool ok = wait(&sh.full[s ^ 1], ((c + 1) >> 1) & 1, kSiteTmaLoad);
-                        if (ok && c >= 1) ok = wait(&sh.o_free[s ^ 1], ((c - 1) >> 1) & 1, kSiteMma);
-                        if (!ok) { fail(); break; }
-                        tc_fence_after();
-                        issue_u(c + 1);
-                    }
+                    mma_commit(&sh.empty_b[s]);
                 }
             } else {
                 fail();
@@ -748,19 +775,21 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
         // -O sits in TMEM lanes 64-127 (rows 0-63 of the lower half of the M=128 accumulator).
         const int et = tid - 192;        // 0..63
         const int row = et;              // output row of this thread (lane quarter 2 or 3)
+        const float* eq_rec = reinterpret_cast<const float*>(p.records + kRecSc + offsetof(RecScalars, eq)) + row;
+        float eq_next = nchunks > 0 ? __ldg(eq_rec + ((slot0 * p.HV + hv) * (int64_t)kRecBytes) / 4) : 0.f;
         for (int c = 0; c < nchunks; ++c) {
             const int s = c & 1;
             const uint32_t phs = (c >> 1) & 1;
             const uint32_t tD = tb + kColD + 64 * s;
-            const bool ok = wait(&sh.acc_o[s], phs, kSiteMma) && wait(&sh.full[s], phs, kSiteTmaLoad);
-            if (!named_sync_all(kBarEpi, kEpiThreads, ok)) {
+            const float neg_eq = -eq_next;
+            if (c + 1 < nchunks)  // the next chunk's row scale, fetched while this one waits
+                eq_next = __ldg(eq_rec + (((slot0 + c + 1) * p.HV + hv) * (int64_t)kRecBytes) / 4);
+            if (!named_sync_all(kBarEpi, kEpiThreads, wait(&sh.acc_o[s], phs, kSiteMma))) {
                 fail();
                 break;
             }
             tc_fence_after();
-            const RecScalars* rs = reinterpret_cast<const RecScalars*>(stage(s) + SStage::SC);
             const bool store = row < nvalid_of(c);
-            const float neg_eq = -rs->eq[row];
             bf16* orow = p.o + ((brow * p.T + bos + 64 * (int64_t)c + row) * p.HV + hv) * kHeadDim + v0;
 #pragma unroll
             for (int half = 0; half < 2; ++half) {
@@ -780,10 +809,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
             }
             tc_fence_before();
             named_sync(kBarEpi, kEpiThreads);
-            if (et == 0) {
-                mbar_arrive(&sh.o_free[s]);
-                mbar_arrive(&sh.empty[s]);
-            }
+            if (et == 0) mbar_arrive(&sh.o_free[s]);
         }
     } else if (warp >= 8) {
         // ================================ chain ================================
@@ -824,7 +850,8 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
             const uint32_t ph = c & 1, phs = (c >> 1) & 1;
             const uint32_t tD = tb + kColD + 64 * s;
             uint8_t* st = stage(s);
-            const bool landed = spin(&sh.full[s], phs, kSiteTmaLoad) && spin(&sh.u_done[s], phs, kSiteMma);
+            const bool landed = spin(&sh.full_a[s], phs, kSiteTmaLoad) && spin(&sh.full_b[s], phs, kSiteTmaLoad) &&
+                                spin(&sh.u_done[s], phs, kSiteMma);
             if (!named_sync_all(kBarChain, kChainThreads, landed)) {
                 fail();
                 break;
@@ -841,6 +868,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
                 for (int kk = 0; kk < 8; ++kk)
                     mma_f16(tD, sdesc_add(a, (kk >> 2) * 2 * kPanel + (kk & 3) * 32), sdesc_add(dSB, kk * 2048), id_neg, 1);
                 mma_commit(&sh.acc_vn[s]);
+                mma_commit(&sh.empty_a[s]);
                 issued_any = true;
             }
             // VN is read out once the previous chunk's output product is done with VBF
@@ -874,8 +902,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
             tc_fence_before();
             named_sync(kBarChain, kChainThreads);
             if (ct == 0) {
-                mbar_arrive(&sh.vn_ready[s]);  // the helper adds -[0; P'] VN
-                // dS = K^T hi + K^T lo (all lanes, fresh)
+                // dS = K^T hi + K^T lo (all lanes, fresh); the helper's output product queues behind it
                 tc_fence_after();
                 const uint64_t ak = sdesc_mnmajor(st + SStage::K, kPanel);
 #pragma unroll
@@ -885,7 +912,8 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
                     mma_f16(tb + kColDS, ad, sdesc_add(dVLO, kk * 2048), id_s, 1);
                 }
                 mma_commit(&sh.acc_s);
-                mma_commit(&sh.empty[s]);
+                mma_commit(&sh.empty_b[s]);
+                mbar_arrive(&sh.ds_issued[s]);
             }
             if (!named_sync_all(kBarChain, kChainThreads, spin(&sh.acc_s, ph, kSiteMma))) {
                 fail();
