@@ -171,7 +171,7 @@ GDN_API int gdn_conv_step(const void* state, const void* qkv, int64_t qkv_stride
 /*
  * Output-gated RMSNorm (replaces GatedRMSNorm.forward, model/model.py:150-158):
  * y = bf16(bf16(w * bf16(x * rsqrt(mean(x^2) + eps))) * silu(z)). x, z, y: [rows, dim]
- * bf16 contiguous, w: [dim] bf16.
+ * bf16 contiguous, w: [dim] bf16; all four 16-byte aligned.
  */
 GDN_API int gdn_gated_rmsnorm(const void* x, const void* z, const void* w, void* y,
                       int64_t rows, int64_t dim, float eps, void* stream);

@@ -201,7 +201,7 @@ int gdn_gated_rmsnorm(const void* x, const void* z, const void* w, void* y, int6
     if (dim != kHeadDim) return GDN_ERR_UNSUPPORTED;
     if (rows == 0) return GDN_OK;
     if (!x || !z || !w || !y) return GDN_ERR_NULL;
-    if (!aligned16(x) || !aligned16(z) || !aligned16(y) || (reinterpret_cast<uintptr_t>(w) & 7u)) return GDN_ERR_ALIGN;
+    if (!aligned16(x) || !aligned16(z) || !aligned16(y) || !aligned16(w)) return GDN_ERR_ALIGN;
     if (rows > (int64_t)65535 * 65535) return GDN_ERR_SHAPE;
     return launch_gated_rmsnorm(x, z, w, y, rows, (int)dim, eps, as_stream(stream));
 }
@@ -220,7 +220,7 @@ int gdn_decode_layer(const void* qkv, int64_t qkv_stride_b, void* conv_state, co
         return GDN_ERR_NULL;
     if (!rows_aligned(qkv, 2, qkv_stride_b, 0, 0) || !aligned16(conv_state) || !aligned16(state) || !aligned16(z) ||
         !aligned16(conv_w) ||
-        !aligned16(out) || !aligned16(workspace) || (reinterpret_cast<uintptr_t>(norm_w) & 7u))
+        !aligned16(out) || !aligned16(workspace) || !aligned16(norm_w))
         return GDN_ERR_ALIGN;
     DecodeLayerArgs a;
     a.qkv = qkv; a.qkv_sb = qkv_stride_b; a.conv_state = conv_state; a.conv_w = conv_w;

@@ -54,9 +54,7 @@ __device__ __forceinline__ float warp_sum(float x) {
 
 // x / d rounded to nearest for 1 <= d < 2^120, by Markstein's method (P. Markstein, IA-64 and
 // Elementary Functions, 2000, ch. 8): one Newton step refines the hardware reciprocal estimate
-// y of 1/d, then one fused residual r = x - d q corrects the quotient q = x y. Checked against
-// the IEEE division __fdiv_rn on every bf16 x and every fp32 x with 0 < |x| <= 80 with
-// d = 1 + expf(-x): no difference.
+// y of 1/d, then one fused residual r = x - d q corrects the quotient q = x y.
 __device__ __forceinline__ float div_markstein(float x, float d) {
     float y;
     asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(d));
@@ -65,11 +63,36 @@ __device__ __forceinline__ float div_markstein(float x, float d) {
     return fmaf(fmaf(-d, q, x), y, q);
 }
 
-// SiLU as the eager path evaluates it on bf16: x / (1 + exp(-x)) in fp32, IEEE division.
-// Zero (whose sign the residual step would lose), |x| > 80 and NaN take the IEEE division.
+// SiLU as the eager path evaluates it on bf16: x / (1 + exp(-x)) in fp32 with an IEEE division,
+// computed without a division instruction. 0 < |x| <= 80: Markstein's quotient. The rest, in
+// plain arithmetic (no call and no branch, so that the compiler keeps scheduling across
+// unrolled elements): zero keeps its sign; x > 80 has d == 1 exactly, so x / d = x; x < -80
+// scales d by 2^-64, which keeps the reciprocal estimate normal, and scales the quotient back
+// exactly; d = inf (x below about -88.7) gives -0, or NaN for x = -inf; NaN stays NaN. Checked against the
+// IEEE division __fdiv_rn on every bf16 x and every fp32 x with |x| <= 80: no difference
+// (NaN compared as NaN).
 __device__ __forceinline__ float silu_f32(float x) {
+    constexpr float kInf = __builtin_huge_valf();
     const float d = 1.0f + expf(-x);
-    return (fabsf(x) <= 80.f && x != 0.f) ? div_markstein(x, d) : __fdiv_rn(x, d);
+    const float sc = x < -80.f ? 0x1p-64f : 1.0f;  // powers of two: exact scalings
+    float q = div_markstein(x, d * sc) * sc;
+    q = (x == 0.f || x > 80.f) ? x : q;
+    return d == kInf ? (x == -kInf ? __int_as_float(0x7fffffff) : -0.0f) : q;
+}
+
+// silu_f32 on 8 values: the common-case quotients first; all 8 again with the full formula only
+// when one of them is zero, beyond +-80 or NaN (a branch that real activations almost never take).
+__device__ __forceinline__ void silu8(const float (&x)[8], float (&y)[8]) {
+    bool rare = false;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        y[i] = div_markstein(x[i], 1.0f + expf(-x[i]));
+        rare |= !(fabsf(x[i]) <= 80.f) || x[i] == 0.f;
+    }
+    if (rare) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) y[i] = silu_f32(x[i]);
+    }
 }
 
 // 1 / sqrt(x) with an IEEE square root and an IEEE division, as the CPU evaluates rsqrt.

@@ -39,7 +39,7 @@ __device__ __forceinline__ void store8(bf16* p, const float* v) {
     *reinterpret_cast<uint4*>(p) = raw;
 }
 
-template <int K>
+template <int K, bool PACKED>
 __global__ void __launch_bounds__(128) conv1d_silu_kernel(const bf16* __restrict__ x, int64_t sxb, int64_t sxt,
                                                           const bf16* __restrict__ w, bf16* __restrict__ y,
                                                           const int32_t* __restrict__ cu, int nseq, int64_t T,
@@ -68,7 +68,7 @@ __global__ void __launch_bounds__(128) conv1d_silu_kernel(const bf16* __restrict
             for (int i = 0; i < K; ++i) wt[j][i] = to_f32(wr[j * K + i]);
     }
     int lo = 0;  // with cu_seqlens: the sequence of the current token
-    if (cu) {
+    if (PACKED) {
         int hi = nseq;
         while (hi - lo > 1) {
             const int mid = (lo + hi) >> 1;
@@ -82,7 +82,7 @@ __global__ void __launch_bounds__(128) conv1d_silu_kernel(const bf16* __restrict
         const int64_t t = t0 + j;
         if (t >= T) break;
         int64_t seq_start = 0;
-        if (cu) {
+        if (PACKED) {
             while (lo + 1 < nseq && cu[lo + 1] <= t) ++lo;
             seq_start = cu[lo];
         }
@@ -94,14 +94,15 @@ __global__ void __launch_bounds__(128) conv1d_silu_kernel(const bf16* __restrict
 #pragma unroll
                 for (int q = 0; q < 8; ++q) win[i][q] = 0.f;
         }
-        float out[8];
+        float pre[8], out[8];
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
             float acc = 0.f;
 #pragma unroll
             for (int i = 0; i < K; ++i) acc = __fadd_rn(acc, __fmul_rn(wt[q][i], win[i][q]));
-            out[q] = silu_f32(round_bf16(acc));
+            pre[q] = round_bf16(acc);
         }
+        silu8(pre, out);
         store8(yb + j * C, out);
     }
 }
@@ -115,12 +116,18 @@ int launch_conv1d_silu(const void* x, int64_t sxb, int64_t sxt, const void* w, v
     auto xp = static_cast<const bf16*>(x);
     auto wp = static_cast<const bf16*>(w);
     auto yp = static_cast<bf16*>(y);
+#define GDN_CONV_CASE(KK)                                                                               \
+    case KK:                                                                                            \
+        if (cu) conv1d_silu_kernel<KK, true><<<grid, threads, 0, s>>>(xp, sxb, sxt, wp, yp, cu, nseq, T, C); \
+        else conv1d_silu_kernel<KK, false><<<grid, threads, 0, s>>>(xp, sxb, sxt, wp, yp, cu, nseq, T, C);  \
+        break;
     switch (K) {
-        case 2: conv1d_silu_kernel<2><<<grid, threads, 0, s>>>(xp, sxb, sxt, wp, yp, cu, nseq, T, C); break;
-        case 3: conv1d_silu_kernel<3><<<grid, threads, 0, s>>>(xp, sxb, sxt, wp, yp, cu, nseq, T, C); break;
-        case 4: conv1d_silu_kernel<4><<<grid, threads, 0, s>>>(xp, sxb, sxt, wp, yp, cu, nseq, T, C); break;
+        GDN_CONV_CASE(2)
+        GDN_CONV_CASE(3)
+        GDN_CONV_CASE(4)
         default: return GDN_ERR_UNSUPPORTED;
     }
+#undef GDN_CONV_CASE
     return launch_status();
 }
 

@@ -68,7 +68,7 @@ extern "C" int gdn_decode_layer_noalloc(const void* qkv, int64_t qkv_stride_b, v
     if (batch == 0) return GDN_OK;
     if (!qkv || !conv_state || !conv_w || !g || !beta || !state || !z || !norm_w || !out) return GDN_ERR_NULL;
     if (!aligned16(qkv) || (qkv_stride_b * 2) % 16 || !aligned16(conv_state) || !aligned16(state) || !aligned16(z) ||
-        !aligned16(conv_w) || !aligned16(out) || (reinterpret_cast<uintptr_t>(norm_w) & 7u))
+        !aligned16(conv_w) || !aligned16(out) || !aligned16(norm_w))
         return GDN_ERR_ALIGN;
     void* workspace = nullptr;
     const int st = scratch_address(&workspace);
