@@ -177,6 +177,20 @@ GDN_API int gdn_gated_rmsnorm(const void* x, const void* z, const void* w, void*
                       int64_t rows, int64_t dim, float eps, void* stream);
 
 /*
+ * Delta-rule gates (replaces delta_gates, model/model.py:314-321, and its CUDA kernel
+ * model/triton_kernels.py:76-114): beta = bf16(sigmoid(b)), g = log_decay_rate *
+ * softplus(a + dt_bias) in fp32, both times valid[row] when valid is not NULL. b, a: [rows, HV]
+ * bf16 with row strides b_stride / a_stride (heads contiguous); dt_bias: [HV] bf16 or fp32
+ * (dt_bias_dtype); log_decay_rate: [HV] fp32; valid: [rows] bytes (0 / 1) or NULL;
+ * beta: [rows, HV] bf16 and g: [rows, HV] fp32, contiguous. Rounds as PyTorch's CUDA eager
+ * ops (expf, log1pf, IEEE division, subnormals kept).
+ */
+GDN_API int gdn_delta_gates(const void* b, int64_t b_stride, const void* a, int64_t a_stride,
+                            const void* dt_bias, int dt_bias_dtype, const float* log_decay_rate,
+                            const uint8_t* valid, void* beta, float* g, int64_t rows, int64_t value_heads,
+                            void* stream);
+
+/*
  * Decode layer for one new token per row: conv step (+SiLU) over the pre-conv qkv, q/k L2
  * norm, gated delta rule step with the state updated in place, and the output-gated
  * RMSNorm. Replaces the StaticCache decode branch of GatedDeltaNet.forward

@@ -195,6 +195,19 @@ int gdn_conv_step(const void* state, const void* qkv, int64_t qkv_stride_b, int6
                             (int)kernel_size, key_dim, value_dim, (int)head_dim_k, (int)head_dim_v, as_stream(stream));
 }
 
+int gdn_delta_gates(const void* b, int64_t b_stride, const void* a, int64_t a_stride, const void* dt_bias,
+                    int dt_bias_dtype, const float* log_decay_rate, const uint8_t* valid, void* beta, float* g,
+                    int64_t rows, int64_t value_heads, void* stream) {
+    if (!known_dtype(dt_bias_dtype)) return GDN_ERR_DTYPE;
+    if (rows < 0 || value_heads <= 0 || value_heads > 4096 || b_stride < value_heads || a_stride < value_heads)
+        return GDN_ERR_SHAPE;
+    if (rows > INT64_MAX / value_heads || rows * value_heads > (int64_t)INT32_MAX * 256) return GDN_ERR_SHAPE;
+    if (rows == 0) return GDN_OK;
+    if (!b || !a || !dt_bias || !log_decay_rate || !beta || !g) return GDN_ERR_NULL;
+    return launch_delta_gates(b, b_stride, a, a_stride, dt_bias, dt_bias_dtype == GDN_F32, log_decay_rate, valid,
+                              beta, g, rows, (int)value_heads, as_stream(stream));
+}
+
 int gdn_gated_rmsnorm(const void* x, const void* z, const void* w, void* y, int64_t rows, int64_t dim, float eps,
                       void* stream) {
     if (rows < 0 || dim <= 0) return GDN_ERR_SHAPE;

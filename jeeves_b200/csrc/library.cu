@@ -6,3 +6,4 @@
 #include "norm.cu"
 #include "chunk.cu"
 #include "noalloc.cu"
+#include "gates.cu"

@@ -6,8 +6,8 @@ dispatchers then call fla's functions through module attributes (``_fla_chunk_gd
 ``_fla_recurrent_gdr``, ``fla_inplace``, ``_fla_causal_conv1d``,
 ``_fla_causal_conv1d_update``, ``_fla_rms_norm_gated``). ``install`` replaces those
 attributes with adapters that have fla's signatures, marks the families available, and
-wraps the two dispatchers whose CUDA branch needs Triton (``conv_step``,
-``gated_delta_rule_advance_inplace``). CPU tensors still take the reference's eager path,
+wraps the dispatchers whose CUDA branch needs Triton (``conv_step``,
+``gated_delta_rule_advance_inplace``, ``delta_gates``). CPU tensors still take the reference's eager path,
 so ``set_kernels(gdn=False)`` and friends keep working.
 """
 
@@ -20,11 +20,12 @@ from .conv import causal_conv1d as _conv1d
 from .conv import causal_conv1d_step as _conv1d_step
 from .conv import conv_step as _conv_step
 from .gated_delta import gated_delta_rule_chunk, gated_delta_rule_step
+from .gates import delta_gates as _delta_gates
 from .norm import gated_rms_norm
 
 KERNEL_FAMILIES = ("gdn", "causal_conv1d", "rms_norm_gated")
 IMPORTED_NAMES = ("gated_delta_rule_chunk", "gated_delta_rule_step", "gated_delta_rule_advance_inplace", "conv_step",
-                  "eager_conv_step", "causal_conv1d", "causal_conv1d_step")
+                  "eager_conv_step", "causal_conv1d", "causal_conv1d_step", "delta_gates")
 
 
 def fla_chunk_gated_delta_rule(q, k, v, g=None, beta=None, scale=None, initial_state=None, output_final_state=False,
@@ -136,6 +137,15 @@ def install(model_module: ModuleType, *importers: ModuleType) -> Installed:
     handle.set(m, "conv_step", conv_step)
     handle.set(m, "eager_conv_step", eager_conv_step)
     handle.set(m, "gated_delta_rule_advance_inplace", gated_delta_rule_advance_inplace)
+    if hasattr(m, "delta_gates"):
+        gates_dispatch = m.delta_gates
+
+        def delta_gates(b, a, dt_bias, log_decay_rate, valid=None):
+            if m._on("gdn", b):
+                return _delta_gates(b, a, dt_bias, log_decay_rate, valid)
+            return gates_dispatch(b, a, dt_bias, log_decay_rate, valid)
+
+        handle.set(m, "delta_gates", delta_gates)
     # Keep the reference's norm module class but let its fla branch reach our kernel: done
     # through _fla_rms_norm_gated above, since GatedRMSNorm.forward calls it under _on.
     for mod in importers:

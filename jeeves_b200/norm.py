@@ -23,6 +23,8 @@ def gated_rms_norm(x: torch.Tensor, z: torch.Tensor, weight: torch.Tensor, eps: 
         raise ValueError(f"x, z, weight: expected bfloat16 with weight of shape {(D,)}, got {x.dtype}, {z.dtype}, "
                          f"{weight.dtype} {tuple(weight.shape)}")
     x, z, w = x.contiguous(), z.contiguous(), weight.contiguous()
+    if w.data_ptr() % 16:  # the kernel reads the weight with 16-byte loads
+        w = w.clone()
     y = torch.empty_like(x)
     rows = x.numel() // D if D else 0
     status = _lib.load().gdn_gated_rmsnorm(x.data_ptr(), z.data_ptr(), w.data_ptr(), y.data_ptr(), rows, D, float(eps),

@@ -41,6 +41,7 @@ def fake_reference_module():
     m.gated_delta_rule_step = lambda *a, **k: "step"
     m.causal_conv1d = lambda *a, **k: "c1d"
     m.causal_conv1d_step = lambda *a, **k: "c1ds"
+    m.delta_gates = lambda *a, **k: m.calls.append("gates") or "gates"
     m.fla_inplace = None
     return m
 
@@ -50,20 +51,22 @@ def test_install_sets_hooks_and_restores():
     engine = types.ModuleType("fake_engine")
     engine.conv_step = m.conv_step
     engine.gated_delta_rule_advance_inplace = m.gated_delta_rule_advance_inplace
-    before = (m._AVAILABLE, m.KERNELS, m.conv_step, engine.conv_step)
+    engine.delta_gates = m.delta_gates
+    before = (m._AVAILABLE, m.KERNELS, m.conv_step, engine.conv_step, m.delta_gates, engine.delta_gates)
     h = gdn.install(m, engine)
     assert m._fla_chunk_gdr is integration.fla_chunk_gated_delta_rule
     assert m._fla_recurrent_gdr is integration.fla_fused_recurrent_gated_delta_rule
     assert m.fla_inplace is gdn.fla_inplace
     assert all(m.KERNELS[f] for f in integration.KERNEL_FAMILIES)
-    assert engine.conv_step is m.conv_step
+    assert engine.conv_step is m.conv_step and engine.delta_gates is m.delta_gates
     # CPU tensors keep the reference's own eager path
     cpu = torch.zeros(1, 1, 8, dtype=torch.bfloat16)
     assert m.conv_step(None, cpu, None, 2, 4, 1, 1) == "conv"
     m.gated_delta_rule_advance_inplace(cpu, cpu, None, None, None, None)
-    assert m.calls == ["conv", "advance"]
+    assert m.delta_gates(cpu, cpu, None, None) == "gates"
+    assert m.calls == ["conv", "advance", "gates"]
     h.uninstall()
-    assert (m._AVAILABLE, m.KERNELS, m.conv_step, engine.conv_step) == before
+    assert (m._AVAILABLE, m.KERNELS, m.conv_step, engine.conv_step, m.delta_gates, engine.delta_gates) == before
     assert not hasattr(m, "_fla_chunk_gdr")
 
 
@@ -88,5 +91,8 @@ def test_install_into_reference_module():
         b = torch.rand(1, 3, 2)
         o, S = ref.gated_delta_rule_chunk(x, x, x, g, b, output_final_state=True)
         assert o.shape == (1, 3, 2, 128) and S.shape == (1, 2, 128, 128)
+        raw = torch.randn(2, 3, 4).to(torch.bfloat16)
+        beta, gg = ref.delta_gates(raw, raw, torch.zeros(4), -torch.ones(4))
+        assert beta.dtype == torch.bfloat16 and gg.dtype == torch.float32
     finally:
         h.uninstall()
