@@ -112,6 +112,8 @@ struct FactorParams {
     int beta_f32;
     const int32_t* cu_seqlens;
     uint8_t* records;  // [slots, HV] records
+    uint32_t* ready;   // [slots, HV] flags set once a record is written (fused launch), or null
+    int64_t slots;
     int64_t T;
     int nseq, ncd;     // sequences; chunks per row of the dense layout
     int HV, rep;
@@ -157,17 +159,33 @@ constexpr uint32_t kColKQ = 0;    // KK (lanes A) / QK (lanes B); W halves (lane
 constexpr uint32_t kColT2 = 64;   // T2 (lanes A) / X_LL (lanes B)
 enum : uint32_t { kBarFactor = 1, kBarChain = 2, kBarEpi = 3 };
 
+// Release / acquire of a record's ready flag between the factor and the scan roles of the fused
+// launch (the record itself moves through the async proxy: bulk stores, then bulk loads).
+__device__ __forceinline__ void flag_release(uint32_t* flag) {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(flag), "r"(1u) : "memory");
+}
+
+__device__ __forceinline__ uint32_t flag_acquire(const uint32_t* flag) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+    return v;
+}
+
+// One factor unit, i.e. one (value head, chunk slot), run by the 128 threads of one warpgroup
+// (pt = 0..127, named barrier `bar`). The barriers in `sh` are initialised once per warpgroup
+// and complete once per unit: `ph` is this unit's phase parity. Result: 1 when the unit ran
+// (its barrier phases completed), 0 for a slot no chunk maps to, -1 once a bounded wait has
+// given up (the device error word is set; the warpgroup then stops).
+//
 // The slot of chunk c of sequence n: n * ncd + c for the dense layout; cu[n] / 64 + n + c for
 // a packed batch. Slots of different sequences never collide because a sequence of length L
 // starting at token b has at most floor((b + L) / 64) - floor(b / 64) + 1 chunks.
-__global__ void __launch_bounds__(128, 3) chunk_factor_kernel(const __grid_constant__ FactorParams p) {
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* sm = align1024(smem_raw);
-    __shared__ FShared sh;
-
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int hv = (int)(blockIdx.x % (unsigned)p.HV);
-    const int64_t slot = blockIdx.x / (unsigned)p.HV;
+__device__ __forceinline__ int factor_unit(const FactorParams& p, int64_t unit, FShared& sh, uint8_t* sm, uint32_t tb,
+                                           uint32_t bar, int pt, uint32_t ph) {
+    const int warp = pt >> 5, lane = pt & 31;
+    const int hv = (int)(unit % p.HV);
+    const int64_t slot = unit / p.HV;
     const int h = hv / p.rep;
     int64_t bos = 0, len = p.T, brow = 0, c = 0;
     if (p.cu_seqlens == nullptr) {
@@ -183,35 +201,23 @@ __global__ void __launch_bounds__(128, 3) chunk_factor_kernel(const __grid_const
         bos = p.cu_seqlens[lo];
         len = p.cu_seqlens[lo + 1] - bos;
         c = slot - (bos / 64 + lo);
-        if (c < 0 || 64 * c >= len) return;  // a slot no chunk maps to (uniform over the CTA)
+        if (c < 0 || 64 * c >= len) return 0;  // a slot no chunk maps to (uniform over the warpgroup)
     }
     const int t = (int)(bos + 64 * c);
     const int nvalid = (int)(len - 64 * c < 64 ? len - 64 * c : 64);
     const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
     const int half_row = 16 * warp + (lane & 15);
     const bool lanes_a = lane < 16;
-    const int pt = tid;
     uint8_t* kt = sm + FSmem::K;
     uint8_t* qt = sm + FSmem::Q;
     float* Af = reinterpret_cast<float*>(sm + FSmem::AF);
 
-    if (tid == 0) {
-        mbar_init(&sh.tma, 1);
-        mbar_init(&sh.acc_kq, 1);
-        mbar_init(&sh.acc_t2, 1);
-        mbar_init(&sh.acc_x, 1);
-        mbar_init(&sh.acc_w, 1);
-        mbar_init(&sh.drain, 1);
-        fence_mbar_init();
+    if (pt == 0) {
         mbar_arrive_expect_tx(&sh.tma, 4 * kPanel);
         tma_load_4d(kt, &p.tm_k, &sh.tma, 0, h, t, (int)brow);
         tma_load_4d(kt + kPanel, &p.tm_k, &sh.tma, 64, h, t, (int)brow);
         tma_load_4d(qt, &p.tm_q, &sh.tma, 0, h, t, (int)brow);
         tma_load_4d(qt + kPanel, &p.tm_q, &sh.tma, 64, h, t, (int)brow);
-    }
-    if (warp == 0) {
-        tmem_alloc(&sh.tmem_base, kFactorTmemCols);
-        tmem_relinquish();
     }
     if (pt < 64) {
         float gv = 0.f, bv = 0.f;
@@ -223,16 +229,13 @@ __global__ void __launch_bounds__(128, 3) chunk_factor_kernel(const __grid_const
         sh.graw[pt] = gv;
         sh.braw[pt] = bv;
     }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tb = sh.tmem_base;
+    named_sync(bar, 128);
     const uint32_t id_sq = make_idesc(64, 64, kFmtBF16, false, false);
     const uint32_t id_mn64 = make_idesc(64, 64, kFmtBF16, false, true);
     bool tiles_landed = false, mma_issued = false;
 
     do {
-        tiles_landed = named_sync_all(kBarFactor, 128, mbar_wait(&sh.tma, 0, kSiteTmaLoad));
+        tiles_landed = named_sync_all(bar, 128, mbar_wait(&sh.tma, ph, kSiteTmaLoad));
         if (!tiles_landed) break;
         // shared-memory descriptors, built once: each MMA below only adds a byte offset
         const uint64_t dK = sdesc_kmajor(kt, 0), dQ = sdesc_kmajor(qt, 0);
@@ -269,9 +272,9 @@ __global__ void __launch_bounds__(128, 3) chunk_factor_kernel(const __grid_const
             const int r = pt - 64;
             sh.rq[r] = rsqrtf(sum_squares_row(qt, r) + 1e-6f) * p.scale;
         }
-        named_sync(kBarFactor, 128);
+        named_sync(bar, 128);
         if (pt < 64) sh.gcl[pt] = pt >= 32 ? gsum + sh.scan_carry : gsum;
-        named_sync(kBarFactor, 128);
+        named_sync(bar, 128);
         if (pt < 64) {
             const float gl = sh.gcl[pt];
             const float glast = sh.gcl[63];
@@ -289,9 +292,9 @@ __global__ void __launch_bounds__(128, 3) chunk_factor_kernel(const __grid_const
                 sh.fast = glast > kDecayFloor;
             }
         }
-        named_sync(kBarFactor, 128);
+        named_sync(bar, 128);
         // ---- A (fp32 rows, from KK in lanes A) and P' (bf16 rows, from QK in lanes B)
-        if (!named_sync_all(kBarFactor, 128, mbar_wait(&sh.acc_kq, 0, kSiteMma))) break;
+        if (!named_sync_all(bar, 128, mbar_wait(&sh.acc_kq, ph, kSiteMma))) break;
         tc_fence_after();
         {
             const int i = half_row;
@@ -336,7 +339,7 @@ __global__ void __launch_bounds__(128, 3) chunk_factor_kernel(const __grid_const
             }
         }
         tc_fence_before();
-        named_sync(kBarFactor, 128);
+        named_sync(bar, 128);
         // ---- inverses of the four 16x16 diagonal blocks of I + A (two partial sums per row)
         {
             float x[16];
@@ -354,14 +357,14 @@ __global__ void __launch_bounds__(128, 3) chunk_factor_kernel(const __grid_const
                     x[i] = (i == col) ? 1.f : (i > col ? -(a0 + a1) : 0.f);
                 }
             }
-            named_sync(kBarFactor, 128);
+            named_sync(bar, 128);
             if (pt < 64) {
                 float* blk = Af + 16 * b * kAfStride + 16 * b;
 #pragma unroll
                 for (int i = 0; i < 16; ++i) blk[i * kAfStride + col] = x[i];
             }
         }
-        named_sync(kBarFactor, 128);
+        named_sync(bar, 128);
         // ---- 16 -> 32 merge inside each 32-block: X10 = -X11 (A10 X00)
         {
             const int blk = pt >> 6, e = pt & 63;
@@ -379,9 +382,9 @@ __global__ void __launch_bounds__(128, 3) chunk_factor_kernel(const __grid_const
                     t4[2] = fmaf(av[q], xv.z, t4[2]); t4[3] = fmaf(av[q], xv.w, t4[3]);
                 }
             }
-            named_sync(kBarFactor, 128);
+            named_sync(bar, 128);
             *reinterpret_cast<float4*>(&Af[(r0 + 16 + i) * kAfStride + r0 + j0]) = make_float4(t4[0], t4[1], t4[2], t4[3]);
-            named_sync(kBarFactor, 128);
+            named_sync(bar, 128);
             float x4[4] = {0.f, 0.f, 0.f, 0.f};
             const float* xrow = Af + (r0 + 16 + i) * kAfStride + r0 + 16;
 #pragma unroll
@@ -395,11 +398,11 @@ __global__ void __launch_bounds__(128, 3) chunk_factor_kernel(const __grid_const
                     x4[2] = fmaf(av[q], tv.z, x4[2]); x4[3] = fmaf(av[q], tv.w, x4[3]);
                 }
             }
-            named_sync(kBarFactor, 128);
+            named_sync(bar, 128);
             *reinterpret_cast<float4*>(&Af[(r0 + 16 + i) * kAfStride + r0 + j0]) =
                 make_float4(-x4[0], -x4[1], -x4[2], -x4[3]);
         }
-        named_sync(kBarFactor, 128);
+        named_sync(bar, 128);
         // ---- bf16 operands of the 32 -> 64 merge: E32 (lower-left block of A) and D32
         {
             const int i = pt & 63, hf = pt >> 6;  // two threads per row, 32 columns each
@@ -421,7 +424,7 @@ __global__ void __launch_bounds__(128, 3) chunk_factor_kernel(const __grid_const
         }
         fence_async_smem();
         tc_fence_before();
-        named_sync(kBarFactor, 128);
+        named_sync(bar, 128);
         if (pt == 0) {  // T2 = E32 D32 (lanes A)
             tc_fence_after();
 #pragma unroll
@@ -430,7 +433,7 @@ __global__ void __launch_bounds__(128, 3) chunk_factor_kernel(const __grid_const
             mma_commit(&sh.acc_t2);
         }
         // ---- T2 -> bf16 operand
-        if (!named_sync_all(kBarFactor, 128, mbar_wait(&sh.acc_t2, 0, kSiteMma))) break;
+        if (!named_sync_all(bar, 128, mbar_wait(&sh.acc_t2, ph, kSiteMma))) break;
         tc_fence_after();
         {
             float r[64];
@@ -441,7 +444,7 @@ __global__ void __launch_bounds__(128, 3) chunk_factor_kernel(const __grid_const
         }
         fence_async_smem();
         tc_fence_before();
-        named_sync(kBarFactor, 128);
+        named_sync(bar, 128);
         if (pt == 0) {  // X_LL = D32 T2 (lanes B)
             tc_fence_after();
 #pragma unroll
@@ -452,7 +455,7 @@ __global__ void __launch_bounds__(128, 3) chunk_factor_kernel(const __grid_const
         // ---- X = D32 - X_LL; two column-scaled bf16 copies: X diag(beta) (record) and X diag(cw)
         // (W product). Row i is shared by lanes l (columns 32-63) and l + 16 (columns 0-31, whose
         // TMEM lanes hold X_LL).
-        if (!named_sync_all(kBarFactor, 128, mbar_wait(&sh.acc_x, 0, kSiteMma))) break;
+        if (!named_sync_all(bar, 128, mbar_wait(&sh.acc_x, ph, kSiteMma))) break;
         tc_fence_after();
         {
             const int i = half_row;
@@ -485,7 +488,7 @@ __global__ void __launch_bounds__(128, 3) chunk_factor_kernel(const __grid_const
         }
         fence_async_smem();
         tc_fence_before();
-        named_sync(kBarFactor, 128);
+        named_sync(bar, 128);
         if (pt == 0) {  // W[:, 0:64] (lanes A) and W[:, 64:128] (lanes B) = (X diag(cw)) K
             tc_fence_after();
 #pragma unroll
@@ -498,7 +501,7 @@ __global__ void __launch_bounds__(128, 3) chunk_factor_kernel(const __grid_const
         }
         // ---- W -> bf16 (lanes A: d 0-63, lanes B: d 64-127) into the dead K tile, then the
         // record goes out with four bulk stores
-        if (!named_sync_all(kBarFactor, 128, mbar_wait(&sh.acc_w, 0, kSiteMma))) break;
+        if (!named_sync_all(bar, 128, mbar_wait(&sh.acc_w, ph, kSiteMma))) break;
         tc_fence_after();
         {
             float r[64];
@@ -508,7 +511,7 @@ __global__ void __launch_bounds__(128, 3) chunk_factor_kernel(const __grid_const
             for (int ch = 0; ch < 8; ++ch) put_chunk(panel, half_row, ch, r + 8 * ch);
         }
         fence_async_smem();
-        named_sync(kBarFactor, 128);
+        named_sync(bar, 128);
         if (pt == 0) {
             uint8_t* rec = p.records + ((int64_t)slot * p.HV + hv) * (int64_t)kRecBytes;
             bulk_store(rec + kRecW, kt, 2 * kPanel);
@@ -517,19 +520,62 @@ __global__ void __launch_bounds__(128, 3) chunk_factor_kernel(const __grid_const
             bulk_store(rec + kRecSc, &sh.rs, sizeof(RecScalars));
             bulk_commit();
             bulk_wait_all();
+            if (p.ready) flag_release(p.ready + slot * p.HV + hv);
         }
+        tc_fence_before();
+        named_sync(bar, 128);  // the next unit reuses the shared memory and TMEM
+        return 1;
     } while (false);
 
+    // a wait gave up: let this unit's copies and products finish before the caller frees TMEM
     if (pt == 0) {
-        if (!tiles_landed) mbar_wait(&sh.tma, 0, kSiteDrain);  // the tiles must land before exit
+        if (!tiles_landed) mbar_wait(&sh.tma, ph, kSiteDrain);
         if (mma_issued) {
             mma_commit(&sh.drain);
             mbar_wait(&sh.drain, 0, kSiteDrain);
         }
     }
+    return -1;
+}
+
+// One warpgroup working through units first, first + stride, ... below total, in order.
+// `relinquish` gives up the CTA's right to allocate more TMEM once this warpgroup has its
+// columns, so that the next CTA on the SM can allocate without waiting; a CTA whose other
+// warpgroups still allocate passes false.
+__device__ __forceinline__ void factor_worker(const FactorParams& p, FShared& sh, uint8_t* sm, uint32_t bar, int pt,
+                                              int64_t first, int64_t stride, int64_t total, bool relinquish) {
+    if (pt == 0) {
+        mbar_init(&sh.tma, 1);
+        mbar_init(&sh.acc_kq, 1);
+        mbar_init(&sh.acc_t2, 1);
+        mbar_init(&sh.acc_x, 1);
+        mbar_init(&sh.acc_w, 1);
+        mbar_init(&sh.drain, 1);
+        fence_mbar_init();
+    }
+    if (pt < 32) {
+        tmem_alloc(&sh.tmem_base, kFactorTmemCols);
+        if (relinquish) tmem_relinquish();
+    }
     tc_fence_before();
-    __syncthreads();
-    if (warp == 0) tmem_dealloc(tb, kFactorTmemCols);
+    named_sync(bar, 128);
+    tc_fence_after();
+    const uint32_t tb = sh.tmem_base;
+    uint32_t ph = 0;
+    for (int64_t u = first; u < total; u += stride) {
+        const int r = factor_unit(p, u, sh, sm, tb, bar, pt, ph);
+        if (r < 0) break;
+        ph ^= (uint32_t)r;
+    }
+    tc_fence_before();
+    named_sync(bar, 128);
+    if (pt < 32) tmem_dealloc(tb, kFactorTmemCols);
+}
+
+__global__ void __launch_bounds__(128, 3) chunk_factor_kernel(const __grid_constant__ FactorParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ FShared sh;
+    factor_worker(p, sh, align1024(smem_raw), kBarFactor, threadIdx.x, blockIdx.x, gridDim.x, (int64_t)gridDim.x, true);
 }
 
 // =========================================================================================
@@ -544,10 +590,28 @@ struct ScanParams {
     bf16* o;           // [B, T, HV, 128]
     const int32_t* cu_seqlens;
     const uint8_t* records;
+    const uint32_t* ready;  // per-record flags to wait for (fused launch), or null
     int64_t T;
     int ncd;
     int HV, rep;
 };
+
+// Waits (bounded, backing off) until the factor role has published a record.
+__device__ __forceinline__ bool wait_ready(const uint32_t* flag, const int* abort) {
+    uint32_t sleep_ns = 32;
+    const long long start = clock64();
+    while (!flag_acquire(flag)) {
+        if (*reinterpret_cast<const volatile int*>(abort)) return false;
+        if (clock64() - start > kWaitCycles) {
+            raise_device_error(kSiteReady);
+            return false;
+        }
+        __nanosleep(sleep_ns);
+        sleep_ns = sleep_ns < 1024 ? 2 * sleep_ns : 1024;
+    }
+    asm volatile("fence.proxy.async.global;" ::: "memory");  // the bulk loads below read the record
+    return true;
+}
 
 // One pipeline stage (81 KB). Three 128-row K-major operands stack two 64-row factors each, so
 // that one M=128 product serves both the state update and the output:
@@ -595,7 +659,8 @@ constexpr uint32_t kScanTmemCols = 256;
 constexpr uint32_t kColDS = 0;    // dS = K^T (hi + lo), 64 columns
 constexpr uint32_t kColD = 64;    // per parity (64 + 64 * parity): VN in lanes 0-63, -O in lanes 64-127
 
-__global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __grid_constant__ ScanParams p) {
+// One scan CTA: (bx, by) = (value head * slices + slice, sequence).
+__device__ __forceinline__ void scan_cta(const ScanParams& p, int bx, int by) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = align1024(smem_raw);
     __shared__ SShared sh;
@@ -604,10 +669,10 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
     const int quarter = warp & 3;                                   // TMEM lane quarter of this warp
     const uint32_t lane_base = (uint32_t)(32 * quarter) << 16;
     constexpr int kSlices = kHeadDim / kVS;
-    const int hv = blockIdx.x / kSlices;
-    const int v0 = (blockIdx.x % kSlices) * kVS;
+    const int hv = bx / kSlices;
+    const int v0 = (bx % kSlices) * kVS;
     const int h = hv / p.rep;
-    const int n = blockIdx.y;
+    const int n = by;
     int64_t bos = 0, len = p.T, brow = n, slot0 = (int64_t)n * p.ncd;
     if (p.cu_seqlens) {
         bos = p.cu_seqlens[n];
@@ -682,6 +747,11 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
                     fail();
                     break;
                 }
+            }
+            const bool ready = !(p.ready && lane == 0) || wait_ready(p.ready + (slot0 + c) * p.HV + hv, &sh.abort);
+            if (!__all_sync(0xffffffffu, ready)) {
+                fail();
+                break;
             }
             if (lane == 0) {
                 uint64_t* bar = &sh.full_a[s];
@@ -776,18 +846,16 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
         const int et = tid - 192;        // 0..63
         const int row = et;              // output row of this thread (lane quarter 2 or 3)
         const float* eq_rec = reinterpret_cast<const float*>(p.records + kRecSc + offsetof(RecScalars, eq)) + row;
-        float eq_next = nchunks > 0 ? __ldg(eq_rec + ((slot0 * p.HV + hv) * (int64_t)kRecBytes) / 4) : 0.f;
         for (int c = 0; c < nchunks; ++c) {
             const int s = c & 1;
             const uint32_t phs = (c >> 1) & 1;
             const uint32_t tD = tb + kColD + 64 * s;
-            const float neg_eq = -eq_next;
-            if (c + 1 < nchunks)  // the next chunk's row scale, fetched while this one waits
-                eq_next = __ldg(eq_rec + (((slot0 + c + 1) * p.HV + hv) * (int64_t)kRecBytes) / 4);
             if (!named_sync_all(kBarEpi, kEpiThreads, wait(&sh.acc_o[s], phs, kSiteMma))) {
                 fail();
                 break;
             }
+            // the record of chunk c has been read by this CTA's products, so it is written
+            const float neg_eq = -eq_rec[(((slot0 + c) * p.HV + hv) * (int64_t)kRecBytes) / 4];
             tc_fence_after();
             const bool store = row < nvalid_of(c);
             bf16* orow = p.o + ((brow * p.T + bos + 64 * (int64_t)c + row) * p.HV + hv) * kHeadDim + v0;
@@ -951,6 +1019,39 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __gri
     if (warp == 0) tmem_dealloc(tb, kScanTmemCols);
 }
 
+__global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __grid_constant__ ScanParams p) {
+    scan_cta(p, blockIdx.x, blockIdx.y);
+}
+
+// =========================================================================================
+// fused launch: when the scan leaves SMs idle (few sequences times heads), one cooperative
+// launch runs the scan CTAs and, on the remaining SMs, three factor warpgroups per CTA that
+// produce the records in chunk order; each record carries a ready flag the scan's loader waits
+// for. The factor role never waits for the scan role, and a cooperative launch keeps every
+// CTA resident, so the waits always end.
+// =========================================================================================
+constexpr int kFusedFactorGroups = 3;
+constexpr int kMinFactorCtas = 16;
+constexpr uint32_t kFusedSmemBytes =
+    (SSmem::BYTES > kFusedFactorGroups * FSmem::END + 1024) ? SSmem::BYTES : kFusedFactorGroups * FSmem::END + 1024;
+static_assert(FSmem::END % 1024 == 0, "factor warpgroup regions stay 1024-aligned");
+
+__global__ void __launch_bounds__(kScanThreads, 1) chunk_fused_kernel(const __grid_constant__ FactorParams f,
+                                                                       const __grid_constant__ ScanParams sp, int nscan,
+                                                                       int scan_gx) {
+    if ((int)blockIdx.x < nscan) {
+        scan_cta(sp, (int)blockIdx.x % scan_gx, (int)blockIdx.x / scan_gx);
+        return;
+    }
+    const int g = threadIdx.x >> 7;
+    if (g >= kFusedFactorGroups) return;
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ FShared fsh[kFusedFactorGroups];
+    const int64_t groups = (int64_t)(gridDim.x - nscan) * kFusedFactorGroups;
+    factor_worker(f, fsh[g], align1024(smem_raw) + g * FSmem::END, 1 + g, threadIdx.x & 127,
+                  (int64_t)(blockIdx.x - nscan) * kFusedFactorGroups + g, groups, f.slots * f.HV, false);
+}
+
 // ---------------------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------------------
@@ -989,8 +1090,45 @@ int64_t chunk_workspace_slots(int64_t B, int64_t T, int64_t nseq, bool packed) {
     return packed ? ncd + nseq : B * ncd;
 }
 
+// Workspace: the records, then one ready flag per record (used by the fused launch).
+static size_t ready_offset(int64_t slots, int64_t HV) { return (size_t)slots * (size_t)HV * kRecBytes; }
+
 size_t chunk_workspace_bytes(int64_t B, int64_t T, int64_t nseq, bool packed, int64_t HV) {
-    return (size_t)chunk_workspace_slots(B, T, nseq, packed) * (size_t)HV * kRecBytes;
+    const int64_t slots = chunk_workspace_slots(B, T, nseq, packed);
+    return ready_offset(slots, HV) + (((size_t)slots * (size_t)HV * sizeof(uint32_t) + 255) & ~size_t(255));
+}
+
+// Per-device launch facts, looked up once: SM count, cooperative launch support and the
+// shared-memory opt-ins of the three kernels.
+struct ChunkDevice {
+    bool ready = false, ok = false, fused = false;
+    int sms = 0;
+};
+
+static const ChunkDevice& chunk_device() {
+    static ChunkDevice devices[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        static ChunkDevice none;
+        return none;
+    }
+    ChunkDevice& d = devices[dev];
+    if (!d.ready) {
+        int coop = 0, active = 0;
+        d.ok = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess &&
+               cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev) == cudaSuccess &&
+               cudaFuncSetAttribute(chunk_factor_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)FSmem::BYTES) == cudaSuccess &&
+               cudaFuncSetAttribute(chunk_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)SSmem::BYTES) == cudaSuccess &&
+               cudaFuncSetAttribute(chunk_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)kFusedSmemBytes) == cudaSuccess &&
+               cudaOccupancyMaxActiveBlocksPerMultiprocessor(&active, chunk_fused_kernel, kScanThreads,
+                                                             kFusedSmemBytes) == cudaSuccess;
+        d.fused = d.ok && coop && active >= 1;
+        d.ready = true;
+    }
+    return d;
 }
 
 int launch_chunk(const ChunkArgs& a, cudaStream_t s) {
@@ -1000,6 +1138,8 @@ int launch_chunk(const ChunkArgs& a, cudaStream_t s) {
     if (slots * a.HV > INT32_MAX) return GDN_ERR_SHAPE;
     if (a.workspace == nullptr || a.workspace_bytes < chunk_workspace_bytes(a.B, a.T, a.nseq, packed, a.HV))
         return GDN_ERR_WORKSPACE;
+    const ChunkDevice& dev = chunk_device();
+    if (!dev.ok) return GDN_ERR_LAUNCH;
     FactorParams f;
     ScanParams sp;
     memset(&f, 0, sizeof(f));
@@ -1016,6 +1156,7 @@ int launch_chunk(const ChunkArgs& a, cudaStream_t s) {
     f.beta_f32 = a.beta_dtype == GDN_F32;
     f.cu_seqlens = a.cu_seqlens;
     f.records = static_cast<uint8_t*>(a.workspace);
+    f.slots = slots;
     f.T = a.T;
     f.nseq = (int)a.nseq;
     f.ncd = ncd;
@@ -1031,21 +1172,27 @@ int launch_chunk(const ChunkArgs& a, cudaStream_t s) {
     sp.ncd = ncd;
     sp.HV = a.HV;
     sp.rep = f.rep;
-    static bool configured = false;
-    if (!configured) {
-        if (cudaFuncSetAttribute(chunk_factor_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)FSmem::BYTES) != cudaSuccess ||
-            cudaFuncSetAttribute(chunk_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)SSmem::BYTES) != cudaSuccess)
+    const int scan_gx = a.HV * (kHeadDim / kVS);
+    const int64_t nscan = (int64_t)scan_gx * a.nseq;
+    if (dev.fused && slots > 0 && nscan + kMinFactorCtas <= dev.sms) {
+        uint32_t* ready = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(a.workspace) + ready_offset(slots, a.HV));
+        if (cudaMemsetAsync(ready, 0, (size_t)slots * a.HV * sizeof(uint32_t), s) != cudaSuccess)
             return GDN_ERR_LAUNCH;
-        configured = true;
+        f.ready = ready;
+        sp.ready = ready;
+        int ns = (int)nscan, gx = scan_gx;
+        void* args[] = {&f, &sp, &ns, &gx};
+        if (cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(chunk_fused_kernel), dim3((unsigned)dev.sms),
+                                        dim3(kScanThreads), args, kFusedSmemBytes, s) != cudaSuccess)
+            return GDN_ERR_LAUNCH;
+        return launch_status();
     }
     if (slots > 0) {
         chunk_factor_kernel<<<(unsigned)(slots * a.HV), 128, FSmem::BYTES, s>>>(f);
         const int st = launch_status();
         if (st != GDN_OK) return st;
     }
-    dim3 grid((unsigned)(a.HV * (kHeadDim / kVS)), (unsigned)a.nseq);
+    dim3 grid((unsigned)scan_gx, (unsigned)a.nseq);
     chunk_scan_kernel<<<grid, kScanThreads, SSmem::BYTES, s>>>(sp);
     return launch_status();
 }

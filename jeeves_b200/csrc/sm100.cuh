@@ -43,6 +43,7 @@ enum WaitSite : int {
     kSiteTmaLoad = 0x101,
     kSiteMma = 0x102,
     kSiteDrain = 0x103,
+    kSiteReady = 0x104,
 };
 
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {

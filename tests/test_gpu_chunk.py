@@ -9,7 +9,7 @@ import torch
 
 import jeeves_b200 as gdn
 import oracle
-from tests.helpers import cuda, gdn_inputs, maxabs, rel
+from tests.helpers import cuda, gdn_inputs, maxabs, rel, same_bits
 
 pytestmark = pytest.mark.gpu
 O_TOL, S_TOL = 2e-2, 1e-3
@@ -119,3 +119,15 @@ def test_no_device_error_after_runs():
     from jeeves_b200 import _lib
     torch.cuda.synchronize()
     assert _lib.load().gdn_device_error(None, 0) == 0
+
+
+def test_fused_and_two_kernel_launches_agree_bitwise():
+    """One sequence (64 scan CTAs: the cooperative launch that overlaps the factor work with the
+    scan) against the same sequence inside a batch of 40 (2,560 scan CTAs: factor kernel, then
+    scan kernel). The per-sequence arithmetic is the same, so the results are equal to the bit."""
+    H, HV, T = 16, 32, 300
+    q, k, v, g, beta, h0 = gdn_inputs(21, 40, T, H, HV)
+    big_o, big_s = gdn.gated_delta_rule_chunk(*cuda(q, k, v, g, beta), initial_state=h0.cuda(), output_final_state=True)
+    one_o, one_s = gdn.gated_delta_rule_chunk(*cuda(q[:1], k[:1], v[:1], g[:1], beta[:1]), initial_state=h0[:1].cuda(),
+                                              output_final_state=True)
+    assert same_bits(one_o, big_o[:1]) and same_bits(one_s, big_s[:1])
