@@ -531,7 +531,17 @@ def main():
         import datetime
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+        # NCCL prints its version banner on file descriptor 1 when the communicator is made;
+        # stdout must carry the single JSON line alone, so fd 1 points at stderr meanwhile.
+        sys.stdout.flush()
+        saved_stdout = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+            dist.barrier()
+        finally:
+            os.dup2(saved_stdout, 1)
+            os.close(saved_stdout)
 
         def rank_sync():
             dist.barrier()
