@@ -1,6 +1,7 @@
 """Benchmark of the gated-delta hot path on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload prefill|varlen|decode|verify]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--no-extras] [--no-cpu-baseline]
+    python bench.py --profile prefill|varlen|decode|verify     (one untimed run of a case, for ncu)
 
 Workloads (synthetic inputs with the benchmark configs' shapes and distributions; no
 dataset or checkpoint is involved):
@@ -232,19 +233,54 @@ def run_ours(args, rank, world, device, rank_sync, reduce_max):
     achieved = core_bytes / (k_ms / 1e3) / 1e9
     launches_per_step = 4  # conv, chunk factor, chunk scan, gated norm
 
-    # e2e: host buffers in, result out, through the public API
-    dev_in = make_prefill_inputs(seed=1, T=T, device=device)
+    # e2e: host buffers in, result out, through the public API. Every step uploads its inputs from
+    # pinned host memory and downloads its output and final state; uploads, compute and downloads
+    # run on three streams with two device input sets, so that step i+1's upload and step i-1's
+    # download overlap step i's compute, as a serving pipeline would run them.
+    dev_sets = [make_prefill_inputs(seed=1, T=T, device=device) for _ in range(2)]
     out_host = torch.empty(T * HV, D, dtype=torch.bfloat16).pin_memory()
     state_host = torch.empty(1, HV, D, D, dtype=torch.float32).pin_memory()
+    compute = torch.cuda.current_stream()
+    up, down = torch.cuda.Stream(), torch.cuda.Stream()
+    uploaded = [torch.cuda.Event() for _ in range(2)]
+    computed = [torch.cuda.Event() for _ in range(2)]
 
     def e2e_step(i):
-        for key in ("qkv", "g", "beta", "z"):
-            dev_in[key].copy_(host[key], non_blocking=True)
-        out, final, _ = prefill_layer(gdn, dev_in)
-        out_host.copy_(out, non_blocking=True)
-        state_host.copy_(final, non_blocking=True)
+        b = i % 2
+        with torch.cuda.stream(up):
+            up.wait_event(computed[b])  # the set's previous step is done with it
+            for key in ("qkv", "g", "beta", "z"):
+                dev_sets[b][key].copy_(host[key], non_blocking=True)
+            uploaded[b].record(up)
+        compute.wait_event(uploaded[b])
+        out, final, _ = prefill_layer(gdn, dev_sets[b])
+        computed[b].record(compute)
+        with torch.cuda.stream(down):
+            down.wait_event(computed[b])
+            out_host.copy_(out, non_blocking=True)
+            state_host.copy_(final, non_blocking=True)
+        out.record_stream(down)
+        final.record_stream(down)
 
-    e2e_ms = reduce_max(timed(e2e_step, args.steps, args.warmup, rank_sync))
+    def e2e_timed(steps, warmup):
+        for i in range(warmup):
+            e2e_step(i)
+        torch.cuda.synchronize()
+        rank_sync()
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(compute)
+        up.wait_stream(compute)
+        down.wait_stream(compute)
+        for i in range(steps):
+            e2e_step(i)
+        compute.wait_stream(up)
+        compute.wait_stream(down)
+        stop.record(compute)
+        torch.cuda.synchronize()
+        rank_sync()
+        return start.elapsed_time(stop)
+
+    e2e_ms = reduce_max(e2e_timed(args.steps, args.warmup))
     h2d = sum(host[k].numel() * host[k].element_size() for k in ("qkv", "g", "beta", "z"))
     d2h = out_host.numel() * 2 + state_host.numel() * 4
 
