@@ -117,7 +117,8 @@ GDN_API int gdn_chunk_prefill(const void* q, const void* k, const void* v, const
  * Workspace bytes gdn_chunk_prefill needs for the same batch, seqlen and value_heads
  * (packed != 0 when cu_seqlens is passed, batch then being the number of sequences):
  * 33,792 bytes of factors and a 4-byte ready flag per (value head, chunk slot), the flags
- * rounded up to 256 bytes; B * ceil(T/64) slots, or ceil(T/64) + N packed.
+ * rounded up to 256 bytes, and for a packed batch 4 bytes per sequence (rounded up to 256);
+ * B * ceil(T/64) slots, or ceil(T/64) + N packed.
  * No counterpart in the reference (fla allocates its intermediates inside the call).
  */
 GDN_API size_t gdn_chunk_prefill_workspace_size(int64_t batch, int64_t seqlen, int64_t value_heads, int packed);

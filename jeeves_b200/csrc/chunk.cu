@@ -591,6 +591,7 @@ struct ScanParams {
     const int32_t* cu_seqlens;
     const uint8_t* records;
     const uint32_t* ready;  // per-record flags to wait for (fused launch), or null
+    const int32_t* order;   // packed batch: sequences longest first (grid row -> sequence), or null
     int64_t T;
     int ncd;
     int HV, rep;
@@ -672,7 +673,7 @@ __device__ __forceinline__ void scan_cta(const ScanParams& p, int bx, int by) {
     const int hv = bx / kSlices;
     const int v0 = (bx % kSlices) * kVS;
     const int h = hv / p.rep;
-    const int n = by;
+    const int n = p.order ? p.order[by] : by;
     int64_t bos = 0, len = p.T, brow = n, slot0 = (int64_t)n * p.ncd;
     if (p.cu_seqlens) {
         bos = p.cu_seqlens[n];
@@ -1095,7 +1096,26 @@ static size_t ready_offset(int64_t slots, int64_t HV) { return (size_t)slots * (
 
 size_t chunk_workspace_bytes(int64_t B, int64_t T, int64_t nseq, bool packed, int64_t HV) {
     const int64_t slots = chunk_workspace_slots(B, T, nseq, packed);
-    return ready_offset(slots, HV) + (((size_t)slots * (size_t)HV * sizeof(uint32_t) + 255) & ~size_t(255));
+    const size_t flags = ((size_t)slots * (size_t)HV * sizeof(uint32_t) + 255) & ~size_t(255);
+    const size_t order = packed ? (((size_t)nseq * sizeof(int32_t) + 255) & ~size_t(255)) : 0;
+    return ready_offset(slots, HV) + flags + order;
+}
+
+// Packed batches: the scan's grid rows take the sequences longest first, so that the longest
+// sequences do not start in the last wave of CTAs. Rank of sequence n = the number of sequences
+// that are longer, or as long with a smaller index; one thread per sequence.
+constexpr int kMaxOrderedSeqs = 1024;
+
+__global__ void seq_order_kernel(const int32_t* __restrict__ cu, int nseq, int32_t* __restrict__ order) {
+    const int n = blockIdx.x * blockDim.x + threadIdx.x;
+    if (n >= nseq) return;
+    const int32_t len = cu[n + 1] - cu[n];
+    int rank = 0;
+    for (int m = 0; m < nseq; ++m) {
+        const int32_t lm = cu[m + 1] - cu[m];
+        rank += (lm > len || (lm == len && m < n)) ? 1 : 0;
+    }
+    order[rank] = n;
 }
 
 // Per-device launch facts, looked up once: SM count, cooperative launch support and the
@@ -1191,6 +1211,14 @@ int launch_chunk(const ChunkArgs& a, cudaStream_t s) {
         chunk_factor_kernel<<<(unsigned)(slots * a.HV), 128, FSmem::BYTES, s>>>(f);
         const int st = launch_status();
         if (st != GDN_OK) return st;
+    }
+    if (packed && a.nseq > 1 && a.nseq <= kMaxOrderedSeqs) {
+        const size_t flags = ((size_t)slots * a.HV * sizeof(uint32_t) + 255) & ~size_t(255);
+        int32_t* order = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(a.workspace) + ready_offset(slots, a.HV) + flags);
+        seq_order_kernel<<<(unsigned)((a.nseq + 127) / 128), 128, 0, s>>>(a.cu_seqlens, (int)a.nseq, order);
+        const int st = launch_status();
+        if (st != GDN_OK) return st;
+        sp.order = order;
     }
     dim3 grid((unsigned)scan_gx, (unsigned)a.nseq);
     chunk_scan_kernel<<<grid, kScanThreads, SSmem::BYTES, s>>>(sp);

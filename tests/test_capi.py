@@ -82,12 +82,12 @@ def test_chunk_workspace_size_and_checks():
     lib = _lib.load()
     rec = 33792  # record bytes per (value head, chunk slot), then a 4-byte ready flag each
 
-    def size(records):
-        return records * rec + (records * 4 + 255) // 256 * 256
+    def size(records, seqs=0):  # records, their flags, and the sequence order of a packed batch
+        return records * rec + (records * 4 + 255) // 256 * 256 + (seqs * 4 + 255) // 256 * 256
 
     assert lib.gdn_chunk_prefill_workspace_size(1, 4096, 32, 0) == size(64 * 32)
     assert lib.gdn_chunk_prefill_workspace_size(3, 100, 4, 0) == size(3 * 2 * 4)
-    assert lib.gdn_chunk_prefill_workspace_size(5, 300, 4, 1) == size((5 + 5) * 4)  # ceil(T/64) + N slots
+    assert lib.gdn_chunk_prefill_workspace_size(5, 300, 4, 1) == size((5 + 5) * 4, 5)  # ceil(T/64) + N slots
     args = [16, 16, 16, 16, 16, _lib.BF16, None, None, 16, None, 1, 64, 1, 1, 128, 128] + [128] * 9 + [0.088]
     need = lib.gdn_chunk_prefill_workspace_size(1, 64, 1, 0)
     assert lib.gdn_chunk_prefill(*args, None, need, None) == _lib.ERR_WORKSPACE

@@ -131,3 +131,24 @@ def test_fused_and_two_kernel_launches_agree_bitwise():
     one_o, one_s = gdn.gated_delta_rule_chunk(*cuda(q[:1], k[:1], v[:1], g[:1], beta[:1]), initial_state=h0[:1].cuda(),
                                               output_final_state=True)
     assert same_bits(one_o, big_o[:1]) and same_bits(one_s, big_s[:1])
+
+
+def test_packed_batch_longest_first_equals_single_sequence_calls():
+    """A packed batch of 12 sequences at 32 value heads (768 scan CTAs: the factor kernel, then
+    the scan kernel taking the sequences longest first) against one call per sequence."""
+    H, HV = 16, 32
+    lens = [70, 300, 1, 129, 64, 0, 257, 5, 191, 64, 400, 33]
+    T = sum(lens)
+    q, k, v, g, beta, _ = gdn_inputs(31, 1, T, H, HV)
+    h0 = torch.randn(len(lens), HV, 128, 128, generator=torch.Generator().manual_seed(32)) * 0.02
+    cu = torch.tensor([0] + torch.tensor(lens).cumsum(0).tolist(), dtype=torch.int32)
+    qc, kc, vc, gc, bc = cuda(q, k, v, g, beta)
+    o, S = gdn.gated_delta_rule_chunk(qc, kc, vc, gc, bc, initial_state=h0.cuda(), output_final_state=True,
+                                      cu_seqlens=cu.cuda())
+    for n, (a, b) in enumerate(zip(cu[:-1].tolist(), cu[1:].tolist())):
+        if b == a:
+            assert same_bits(S[n], h0[n].cuda())
+            continue
+        o1, S1 = gdn.gated_delta_rule_chunk(qc[:, a:b], kc[:, a:b], vc[:, a:b], gc[:, a:b], bc[:, a:b],
+                                            initial_state=h0[n:n + 1].cuda(), output_final_state=True)
+        assert same_bits(o[:, a:b], o1) and same_bits(S[n:n + 1], S1), n
