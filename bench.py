@@ -169,6 +169,20 @@ def prefill_flops(T):
     return T * HV * 180_224
 
 
+def chunk_plan(n_seq, packed, device):
+    """Kernels one gdn_chunk_prefill call launches, as the library chooses them: one cooperative
+    chunk_fused_kernel when the scan CTAs (two per value head and sequence) plus 16 factor CTAs fit
+    on the SMs at once; otherwise chunk_factor_kernel and chunk_scan_kernel, with seq_order_kernel
+    between them for a packed batch of 2 to 1024 sequences."""
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    if 2 * HV * n_seq + 16 <= sms:
+        return ["chunk_fused_kernel"]
+    names = ["chunk_factor_kernel"]
+    if packed and 1 < n_seq <= 1024:
+        names.append("seq_order_kernel")
+    return names + ["chunk_scan_kernel"]
+
+
 def varlen_lengths(seed=2, n=32):
     gen = torch.Generator().manual_seed(seed)
     return torch.randint(128, 2049, (n,), generator=gen).tolist()
@@ -231,7 +245,8 @@ def run_ours(args, rank, world, device, rank_sync, reduce_max):
     k_ms = statistics.mean(kernel_ms)
     core_bytes = prefill_core_bytes(T)
     achieved = core_bytes / (k_ms / 1e3) / 1e9
-    launches_per_step = 4  # conv, chunk factor, chunk scan, gated norm
+    plan = chunk_plan(1, False, device)
+    launches_per_step = 2 + len(plan)  # conv, the chunk kernels, gated norm
 
     # e2e: host buffers in, result out, through the public API. Every step uploads its inputs from
     # pinned host memory and downloads its output and final state; uploads, compute and downloads
@@ -306,7 +321,7 @@ def run_ours(args, rank, world, device, rank_sync, reduce_max):
         "gpu_launches": launches_per_step * args.steps,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(achieved / hbm_peak, 4), "peak_kind": peak_kind,
-                     "kernel": "gated_delta_rule_chunk (chunk_factor_kernel + chunk_scan_kernel)",
+                     "kernel": "gated_delta_rule_chunk (" + " + ".join(plan) + ")",
                      "kernel_ms": round(k_ms, 4),
                      "algorithmic_bytes": core_bytes,
                      "traffic": traffic.get("prefill", {}).get("dram_bytes_per_launch"),
@@ -358,7 +373,7 @@ def bench_varlen(gdn, args, device, rank_sync, reduce_max, world, hbm_peak, rank
             "tokens": Ttot_all, "value": round(Ttot_all / (ms / 1e3), 1), "unit": "tokens/s", "ms_per_step": round(ms, 4),
             "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(ach / hbm_peak, 4), "algorithmic_bytes": bytes_},
-            "gpu_launches": 2 * steps}
+            "gpu_launches": len(chunk_plan(N, True, device)) * steps}
 
 
 def shard(n, rank, world):

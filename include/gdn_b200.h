@@ -101,8 +101,10 @@ GDN_API int gdn_recurrent(const void* q, const void* k, const void* v, int qkv_d
  * and `batch` is the number of sequences N (fla 0.5.x varlen convention); otherwise N =
  * batch. q is L2-normalised and scaled by `scale`, k L2-normalised, in the kernel.
  * workspace: device memory of at least gdn_chunk_prefill_workspace_size(...) bytes, 16-byte
- * aligned, for the per-chunk factors handed from the first kernel to the second; it holds
- * nothing between calls (GDN_ERR_WORKSPACE when missing or too small).
+ * aligned, for the per-chunk factors handed from the factor work to the scan (one cooperative
+ * launch when the grid fits on the SMs at once, two launches otherwise); it holds nothing
+ * between calls (GDN_ERR_WORKSPACE when missing or too small). Calls that share one workspace
+ * must be ordered on one stream.
  */
 GDN_API int gdn_chunk_prefill(const void* q, const void* k, const void* v, const float* g, const void* beta,
                               int beta_dtype, const float* initial_state, float* final_state, void* o,
