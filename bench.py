@@ -147,15 +147,8 @@ def make_prefill_inputs(seed=1, T=4096, device="cpu", pin=False):
 
 
 def prefill_layer(gdn, x):
-    """conv1d + SiLU -> chunked gated delta rule (final state) -> gated RMSNorm."""
-    T = x["qkv"].shape[1]
-    y = gdn.causal_conv1d(x["qkv"], x["w"])
-    q = y[..., :H * D].view(1, T, H, D)
-    k = y[..., H * D:2 * H * D].view(1, T, H, D)
-    v = y[..., 2 * H * D:].view(1, T, HV, D)
-    o, final = gdn.gated_delta_rule_chunk(q, k, v, x["g"], x["beta"], output_final_state=True)
-    out = gdn.gated_rms_norm(o.view(-1, D), x["z"].view(-1, D), x["nw"])
-    return out, final, (q, k, v)
+    """conv1d + SiLU -> chunked gated delta rule (final state) with the gated RMSNorm fused in."""
+    return gdn.prefill_layer(x["qkv"], x["w"], x["g"], x["beta"], x["z"], x["nw"], H)
 
 
 def prefill_core_bytes(T, n_seq=1, with_h0=False):
@@ -169,18 +162,20 @@ def prefill_flops(T):
     return T * HV * 180_224
 
 
-def chunk_plan(n_seq, packed, device):
-    """Kernels one gdn_chunk_prefill call launches, as the library chooses them: one cooperative
-    chunk_fused_kernel when the scan CTAs (two per value head and sequence) plus 16 factor CTAs fit
-    on the SMs at once; otherwise chunk_factor_kernel and chunk_scan_kernel, with seq_order_kernel
-    between them for a packed batch of 2 to 1024 sequences."""
+def chunk_plan(n_seq, packed, device, norm=False):
+    """Kernels one gdn_chunk_prefill (norm: gdn_chunk_prefill_gated_norm) call launches, as the
+    library chooses them: one cooperative chunk_fused_kernel when the scan CTAs (two per value
+    head and sequence) plus 16 factor CTAs fit on the SMs at once; otherwise chunk_factor_kernel
+    and chunk_scan_kernel, with seq_order_kernel between them for a packed batch of 2 to 1024
+    sequences; then gated_rmsnorm_kernel for the norm."""
     sms = torch.cuda.get_device_properties(device).multi_processor_count
+    norm_k = ["gated_rmsnorm_kernel"] if norm else []
     if 2 * HV * n_seq + 16 <= sms:
-        return ["chunk_fused_kernel"]
+        return ["chunk_fused_kernel"] + norm_k
     names = ["chunk_factor_kernel"]
     if packed and 1 < n_seq <= 1024:
         names.append("seq_order_kernel")
-    return names + ["chunk_scan_kernel"]
+    return names + ["chunk_scan_kernel"] + norm_k
 
 
 def varlen_lengths(seed=2, n=32):
@@ -268,11 +263,11 @@ def run_ours(args, rank, world, device, rank_sync, reduce_max):
                 dev_sets[b][key].copy_(host[key], non_blocking=True)
             uploaded[b].record(up)
         compute.wait_event(uploaded[b])
-        out, final, _ = prefill_layer(gdn, dev_sets[b])
+        out, final = prefill_layer(gdn, dev_sets[b])
         computed[b].record(compute)
         with torch.cuda.stream(down):
             down.wait_event(computed[b])
-            out_host.copy_(out, non_blocking=True)
+            out_host.copy_(out.view(-1, D), non_blocking=True)
             state_host.copy_(final, non_blocking=True)
         out.record_stream(down)
         final.record_stream(down)

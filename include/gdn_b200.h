@@ -116,6 +116,28 @@ GDN_API int gdn_chunk_prefill(const void* q, const void* k, const void* v, const
                               float scale, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * Chunked prefill followed by the output-gated RMSNorm of its output, in one call: the prefill
+ * branch of GatedDeltaNet.forward from gated_delta_rule_chunk to self.norm
+ * (model/model.py:505-506 then :516; GatedRMSNorm.forward, :150-158). Arguments as for
+ * gdn_chunk_prefill, plus z: [rows, 128] bf16 in o's row order ((b * seqlen + t) * value_heads
+ * + hv), norm_weight: [128] bf16, eps, and out: [rows, 128] bf16, which may be o itself (the
+ * norm is then in place). out equals gdn_chunk_prefill then gdn_gated_rmsnorm bit for bit; o
+ * holds the un-normed output unless out == o. The norm is one more launch on the same stream
+ * after the prefill's kernels. z, norm_weight and out 16-byte aligned; the same workspace as
+ * gdn_chunk_prefill.
+ */
+GDN_API int gdn_chunk_prefill_gated_norm(const void* q, const void* k, const void* v, const float* g,
+                                         const void* beta, int beta_dtype, const float* initial_state,
+                                         float* final_state, void* o, const int32_t* cu_seqlens, int64_t batch,
+                                         int64_t seqlen, int64_t key_heads, int64_t value_heads,
+                                         int64_t head_dim_k, int64_t head_dim_v,
+                                         int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h,
+                                         int64_t k_stride_b, int64_t k_stride_t, int64_t k_stride_h,
+                                         int64_t v_stride_b, int64_t v_stride_t, int64_t v_stride_h, float scale,
+                                         const void* z, const void* norm_weight, float eps, void* out,
+                                         void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Workspace bytes gdn_chunk_prefill needs for the same batch, seqlen and value_heads
  * (packed != 0 when cu_seqlens is passed, batch then being the number of sequences):
  * 33,792 bytes of factors and a 4-byte ready flag per (value head, chunk slot), the flags

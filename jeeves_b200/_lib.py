@@ -33,6 +33,9 @@ SIGNATURES: dict[str, list] = {
                       _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _p],
     "gdn_chunk_prefill": [_p, _p, _p, _p, _p, _i32, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64,
                           _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _p, _sz, _p],
+    "gdn_chunk_prefill_gated_norm": [_p, _p, _p, _p, _p, _i32, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64,
+                                     _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _p, _p, _f32, _p,
+                                     _p, _sz, _p],
     "gdn_chunk_prefill_workspace_size": [_i64, _i64, _i64, _i32],
     "gdn_snapshot_commit": [_p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p],
     "gdn_conv1d_silu": [_p, _i64, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _p],

@@ -102,13 +102,13 @@ int gdn_recurrent(const void* q, const void* k, const void* v, int qkv_dtype, co
     return launch_recurrent(a, as_stream(stream));
 }
 
-int gdn_chunk_prefill(const void* q, const void* k, const void* v, const float* g, const void* beta, int beta_dtype,
-                      const float* initial_state, float* final_state, void* o, const int32_t* cu_seqlens,
-                      int64_t batch, int64_t seqlen, int64_t key_heads, int64_t value_heads, int64_t head_dim_k,
-                      int64_t head_dim_v, int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h,
-                      int64_t k_stride_b, int64_t k_stride_t, int64_t k_stride_h, int64_t v_stride_b,
-                      int64_t v_stride_t, int64_t v_stride_h, float scale, void* workspace, size_t workspace_bytes,
-                      void* stream) {
+static int chunk_prefill(const void* q, const void* k, const void* v, const float* g, const void* beta, int beta_dtype,
+                         const float* initial_state, float* final_state, void* o, const int32_t* cu_seqlens,
+                         int64_t batch, int64_t seqlen, int64_t key_heads, int64_t value_heads, int64_t head_dim_k,
+                         int64_t head_dim_v, int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h,
+                         int64_t k_stride_b, int64_t k_stride_t, int64_t k_stride_h, int64_t v_stride_b,
+                         int64_t v_stride_t, int64_t v_stride_h, float scale, void* workspace, size_t workspace_bytes,
+                         const void* z, const void* norm_weight, float eps, void* out, void* stream) {
     if (!known_dtype(beta_dtype)) return GDN_ERR_DTYPE;
     if (batch < 0 || seqlen < 0 || key_heads <= 0 || value_heads <= 0 || value_heads % key_heads) return GDN_ERR_SHAPE;
     if (batch > 65535 || value_heads > 512) return GDN_ERR_SHAPE;
@@ -121,7 +121,7 @@ int gdn_chunk_prefill(const void* q, const void* k, const void* v, const float* 
         !rows_aligned(v, 2, v_stride_b, v_stride_t, v_stride_h) || !aligned16(o))
         return GDN_ERR_ALIGN;
     if ((initial_state && !aligned16(initial_state)) || (final_state && !aligned16(final_state))) return GDN_ERR_ALIGN;
-    ChunkArgs a;
+    ChunkArgs a{};
     a.q = q; a.k = k; a.v = v; a.g = g; a.beta = beta; a.beta_dtype = beta_dtype;
     a.h0 = initial_state; a.ht = final_state; a.o = o; a.cu_seqlens = cu_seqlens;
     a.B = cu_seqlens ? 1 : batch; a.T = seqlen; a.nseq = batch;
@@ -132,8 +132,41 @@ int gdn_chunk_prefill(const void* q, const void* k, const void* v, const float* 
     a.scale = scale;
     a.workspace = workspace;
     a.workspace_bytes = workspace_bytes;
+    a.z = z;
+    a.norm_w = norm_weight;
+    a.y = out;
+    a.eps = eps;
     if (workspace && !aligned16(workspace)) return GDN_ERR_ALIGN;
     return launch_chunk(a, as_stream(stream));
+}
+
+int gdn_chunk_prefill(const void* q, const void* k, const void* v, const float* g, const void* beta, int beta_dtype,
+                      const float* initial_state, float* final_state, void* o, const int32_t* cu_seqlens,
+                      int64_t batch, int64_t seqlen, int64_t key_heads, int64_t value_heads, int64_t head_dim_k,
+                      int64_t head_dim_v, int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h,
+                      int64_t k_stride_b, int64_t k_stride_t, int64_t k_stride_h, int64_t v_stride_b,
+                      int64_t v_stride_t, int64_t v_stride_h, float scale, void* workspace, size_t workspace_bytes,
+                      void* stream) {
+    return chunk_prefill(q, k, v, g, beta, beta_dtype, initial_state, final_state, o, cu_seqlens, batch, seqlen,
+                         key_heads, value_heads, head_dim_k, head_dim_v, q_stride_b, q_stride_t, q_stride_h, k_stride_b,
+                         k_stride_t, k_stride_h, v_stride_b, v_stride_t, v_stride_h, scale, workspace, workspace_bytes,
+                         nullptr, nullptr, 0.f, nullptr, stream);
+}
+
+int gdn_chunk_prefill_gated_norm(const void* q, const void* k, const void* v, const float* g, const void* beta,
+                                 int beta_dtype, const float* initial_state, float* final_state, void* o,
+                                 const int32_t* cu_seqlens, int64_t batch, int64_t seqlen, int64_t key_heads,
+                                 int64_t value_heads, int64_t head_dim_k, int64_t head_dim_v, int64_t q_stride_b,
+                                 int64_t q_stride_t, int64_t q_stride_h, int64_t k_stride_b, int64_t k_stride_t,
+                                 int64_t k_stride_h, int64_t v_stride_b, int64_t v_stride_t, int64_t v_stride_h,
+                                 float scale, const void* z, const void* norm_weight, float eps, void* out,
+                                 void* workspace, size_t workspace_bytes, void* stream) {
+    if (batch > 0 && (!z || !norm_weight || !out)) return GDN_ERR_NULL;
+    if (!aligned16(z) || !aligned16(norm_weight) || !aligned16(out)) return GDN_ERR_ALIGN;
+    return chunk_prefill(q, k, v, g, beta, beta_dtype, initial_state, final_state, o, cu_seqlens, batch, seqlen,
+                         key_heads, value_heads, head_dim_k, head_dim_v, q_stride_b, q_stride_t, q_stride_h, k_stride_b,
+                         k_stride_t, k_stride_h, v_stride_b, v_stride_t, v_stride_h, scale, workspace, workspace_bytes,
+                         z, norm_weight, eps, out, stream);
 }
 
 size_t gdn_chunk_prefill_workspace_size(int64_t batch, int64_t seqlen, int64_t value_heads, int packed) {

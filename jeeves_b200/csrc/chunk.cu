@@ -46,6 +46,7 @@ namespace gdn {
 using namespace sm100;
 
 constexpr int kVS = 64;                       // value columns per scan CTA
+constexpr int kSlices = kHeadDim / kVS;         // scan CTAs per (sequence, value head)
 constexpr uint32_t kPanel = 64 * 128;         // one 128-byte-swizzled panel of 64 rows
 constexpr int kAfStride = 68;                 // fp32 row stride of the inverse workspace
 
@@ -538,12 +539,31 @@ __device__ __forceinline__ int factor_unit(const FactorParams& p, int64_t unit, 
     return -1;
 }
 
-// One warpgroup working through units first, first + stride, ... below total, in order.
-// `relinquish` gives up the CTA's right to allocate more TMEM once this warpgroup has its
-// columns, so that the next CTA on the SM can allocate without waiting; a CTA whose other
-// warpgroups still allocate passes false.
+// Units of the fused launch in chunk-major order: u -> (chunk c, sequence n, value head hv), so
+// that chunk c of every sequence comes before any chunk c + 1. Returns the (slot * HV + hv) unit,
+// or -1 where sequence n has no chunk c. u runs below ncd * nseq * HV.
+__device__ __forceinline__ int64_t chunk_major_unit(const FactorParams& p, int64_t u) {
+    const int64_t per_chunk = (int64_t)p.nseq * p.HV;
+    const int64_t c = u / per_chunk;
+    const int64_t r = u - c * per_chunk;
+    const int n = (int)(r / p.HV), hv = (int)(r - (int64_t)n * p.HV);
+    int64_t slot = (int64_t)n * p.ncd + c;
+    if (p.cu_seqlens) {
+        const int64_t bos = p.cu_seqlens[n], len = p.cu_seqlens[n + 1] - bos;
+        if (64 * c >= len) return -1;
+        slot = bos / 64 + n + c;
+    }
+    return slot * p.HV + hv;
+}
+
+// One warpgroup working through units first, first + stride, ... below total, in order (in
+// chunk-major order when `chunk_major`, else u is the unit itself). `relinquish` gives up the
+// CTA's right to allocate more TMEM once this warpgroup has its columns, so that the next CTA
+// on the SM can allocate without waiting; a CTA whose other warpgroups still allocate passes
+// false.
 __device__ __forceinline__ void factor_worker(const FactorParams& p, FShared& sh, uint8_t* sm, uint32_t bar, int pt,
-                                              int64_t first, int64_t stride, int64_t total, bool relinquish) {
+                                              int64_t first, int64_t stride, int64_t total, bool relinquish,
+                                              bool chunk_major) {
     if (pt == 0) {
         mbar_init(&sh.tma, 1);
         mbar_init(&sh.acc_kq, 1);
@@ -563,7 +583,9 @@ __device__ __forceinline__ void factor_worker(const FactorParams& p, FShared& sh
     const uint32_t tb = sh.tmem_base;
     uint32_t ph = 0;
     for (int64_t u = first; u < total; u += stride) {
-        const int r = factor_unit(p, u, sh, sm, tb, bar, pt, ph);
+        const int64_t unit = chunk_major ? chunk_major_unit(p, u) : u;
+        if (unit < 0) continue;
+        const int r = factor_unit(p, unit, sh, sm, tb, bar, pt, ph);
         if (r < 0) break;
         ph ^= (uint32_t)r;
     }
@@ -575,7 +597,8 @@ __device__ __forceinline__ void factor_worker(const FactorParams& p, FShared& sh
 __global__ void __launch_bounds__(128, 3) chunk_factor_kernel(const __grid_constant__ FactorParams p) {
     extern __shared__ uint8_t smem_raw[];
     __shared__ FShared sh;
-    factor_worker(p, sh, align1024(smem_raw), kBarFactor, threadIdx.x, blockIdx.x, gridDim.x, (int64_t)gridDim.x, true);
+    factor_worker(p, sh, align1024(smem_raw), kBarFactor, threadIdx.x, blockIdx.x, gridDim.x, (int64_t)gridDim.x, true,
+                  false);
 }
 
 // =========================================================================================
@@ -669,7 +692,6 @@ __device__ __forceinline__ void scan_cta(const ScanParams& p, int bx, int by) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int quarter = warp & 3;                                   // TMEM lane quarter of this warp
     const uint32_t lane_base = (uint32_t)(32 * quarter) << 16;
-    constexpr int kSlices = kHeadDim / kVS;
     const int hv = bx / kSlices;
     const int v0 = (bx % kSlices) * kVS;
     const int h = hv / p.rep;
@@ -1048,9 +1070,10 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_fused_kernel(const __gr
     if (g >= kFusedFactorGroups) return;
     extern __shared__ uint8_t smem_raw[];
     __shared__ FShared fsh[kFusedFactorGroups];
-    const int64_t groups = (int64_t)(gridDim.x - nscan) * kFusedFactorGroups;
+    const int64_t ctas = (int64_t)(gridDim.x - nscan);
     factor_worker(f, fsh[g], align1024(smem_raw) + g * FSmem::END, 1 + g, threadIdx.x & 127,
-                  (int64_t)(blockIdx.x - nscan) * kFusedFactorGroups + g, groups, f.slots * f.HV, false);
+                  (int64_t)(blockIdx.x - nscan) * kFusedFactorGroups + g, ctas * kFusedFactorGroups,
+                  (int64_t)f.ncd * f.nseq * f.HV, false, true);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -1151,6 +1174,13 @@ static const ChunkDevice& chunk_device() {
     return d;
 }
 
+// After the chunk kernels: the launch status, then the output-gated RMSNorm of o when asked for.
+static int finish_chunk(const ChunkArgs& a, cudaStream_t s) {
+    const int st = launch_status();
+    if (st != GDN_OK || a.y == nullptr) return st;
+    return launch_gated_rmsnorm(a.o, a.z, a.norm_w, a.y, a.B * a.T * a.HV, kHeadDim, a.eps, s);
+}
+
 int launch_chunk(const ChunkArgs& a, cudaStream_t s) {
     if (a.nseq == 0) return GDN_OK;
     const bool packed = a.cu_seqlens != nullptr;
@@ -1205,7 +1235,7 @@ int launch_chunk(const ChunkArgs& a, cudaStream_t s) {
         if (cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(chunk_fused_kernel), dim3((unsigned)dev.sms),
                                         dim3(kScanThreads), args, kFusedSmemBytes, s) != cudaSuccess)
             return GDN_ERR_LAUNCH;
-        return launch_status();
+        return finish_chunk(a, s);
     }
     if (slots > 0) {
         chunk_factor_kernel<<<(unsigned)(slots * a.HV), 128, FSmem::BYTES, s>>>(f);
@@ -1222,7 +1252,7 @@ int launch_chunk(const ChunkArgs& a, cudaStream_t s) {
     }
     dim3 grid((unsigned)scan_gx, (unsigned)a.nseq);
     chunk_scan_kernel<<<grid, kScanThreads, SSmem::BYTES, s>>>(sp);
-    return launch_status();
+    return finish_chunk(a, s);
 }
 
 }  // namespace gdn

@@ -45,6 +45,11 @@ struct ChunkArgs {
     float scale;
     void* workspace;
     size_t workspace_bytes;
+    // output-gated RMSNorm of o fused into the call (y null: none); z in o's row layout, y may be o
+    const void* z;
+    const void* norm_w;
+    void* y;
+    float eps;
 };
 int launch_chunk(const ChunkArgs& a, cudaStream_t s);
 size_t chunk_workspace_bytes(int64_t B, int64_t T, int64_t nseq, bool packed, int64_t HV);

@@ -1,0 +1,54 @@
+// Output-gated RMSNorm of one row of 128 (GatedRMSNorm.forward, model/model.py:150-158), shared by
+// the standalone norm kernel and the chunked prefill's fused norm role, so that both round alike.
+//
+// Sixteen lanes hold one row: lane l of the half-warp holds elements 8l..8l+7. Rounding follows
+// the eager path on bf16: normed = bf16(x * rsqrt(mean(x^2) + eps)), weighted = bf16(w * normed),
+// y = bf16(weighted * silu(z)) with silu in fp32.
+#pragma once
+
+#include "common.cuh"
+
+namespace gdn {
+
+__device__ __forceinline__ void unpack8f(const uint4& raw, float (&v)[8]) {
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(h[i]);
+        v[2 * i] = f.x;
+        v[2 * i + 1] = f.y;
+    }
+}
+
+__device__ __forceinline__ void load8f(const bf16* p, float (&v)[8]) { unpack8f(*reinterpret_cast<const uint4*>(p), v); }
+
+// The normed, gated eight elements of this lane, packed as bf16. Every lane of the warp must
+// call it (the sum of squares is reduced over the half-warp with shuffles).
+__device__ __forceinline__ uint4 gated_norm_row8(const float (&xs)[8], const float (&zs)[8], const float (&ws)[8],
+                                                 float eps) {
+    float sq = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) sq = fmaf(xs[i], xs[i], sq);
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    const float inv = inv_sqrt_rn(sq * (1.0f / kHeadDim) + eps);
+    float sil[8];
+    silu8(zs, sil);
+    uint4 raw;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        float o2[2];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int e = 2 * i + k;
+            const float normed = round_bf16(xs[e] * inv);
+            const float weighted = round_bf16(ws[e] * normed);
+            o2[k] = weighted * sil[e];
+        }
+        h[i] = __floats2bfloat162_rn(o2[0], o2[1]);
+    }
+    return raw;
+}
+
+}  // namespace gdn

@@ -143,21 +143,74 @@ def gated_delta_rule_chunk(q, k, v, g, beta, initial_state=None, output_final_st
     if q.dtype == torch.float32:
         _recurrent(what, q, k, v, g, beta, state_in=h0, state_out=final, o=o, cu_seqlens=cu, rows=rows, scale=scale)
         return o, final
+    _chunk_prefill(what, q, k, v, g, beta, h0, final, o, cu, rows, scale)
+    return o, final
+
+
+def _chunk_prefill(what, q, k, v, g, beta, h0, final, o, cu, rows, scale, norm=None):
+    """One gdn_chunk_prefill call (or gdn_chunk_prefill_gated_norm when ``norm`` = (z, weight,
+    eps, out)), with the workspace taken from PyTorch's caching allocator."""
+    B, T, H = k.shape[:3]
+    HV = v.shape[2]
     if T == 0:
         if final is not None:
             final.copy_(h0) if h0 is not None else final.zero_()
-        return o, final
+        return
     q, k, v = (_heads_last_contiguous(t) for t in (q, k, v))
     lib = _lib.load()
     ws_bytes = lib.gdn_chunk_prefill_workspace_size(rows, T, HV, int(cu is not None))
     workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
-    status = lib.gdn_chunk_prefill(
-        q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(), beta.data_ptr(), _DTYPES[beta.dtype], _ptr(h0),
-        _ptr(final), o.data_ptr(), _ptr(cu), rows, T, H, HV, HEAD_DIM, HEAD_DIM,
-        q.stride(0), q.stride(1), q.stride(2), k.stride(0), k.stride(1), k.stride(2), v.stride(0), v.stride(1),
-        v.stride(2), float(HEAD_DIM ** -0.5 if scale is None else scale), workspace.data_ptr(), ws_bytes, _stream())
+    args = (q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(), beta.data_ptr(), _DTYPES[beta.dtype], _ptr(h0),
+            _ptr(final), o.data_ptr(), _ptr(cu), rows, T, H, HV, HEAD_DIM, HEAD_DIM,
+            q.stride(0), q.stride(1), q.stride(2), k.stride(0), k.stride(1), k.stride(2), v.stride(0), v.stride(1),
+            v.stride(2), float(HEAD_DIM ** -0.5 if scale is None else scale))
+    if norm is None:
+        status = lib.gdn_chunk_prefill(*args, workspace.data_ptr(), ws_bytes, _stream())
+    else:
+        z, w, eps, out = norm
+        status = lib.gdn_chunk_prefill_gated_norm(*args, z.data_ptr(), w.data_ptr(), float(eps), out.data_ptr(),
+                                                  workspace.data_ptr(), ws_bytes, _stream())
     _lib.check(status, what)
-    return o, final
+
+
+def gated_delta_rule_chunk_gated_norm(q, k, v, g, beta, z, norm_weight, eps=1e-6, initial_state=None,
+                                      output_final_state=False, scale=None, cu_seqlens=None, out=None):
+    """Chunked prefill and the output-gated RMSNorm of its output; returns ``(y, final_state or None)``.
+
+    Equals ``gated_rms_norm(gated_delta_rule_chunk(...)[0], z, norm_weight, eps)`` bit for bit:
+    the prefill branch of ``GatedDeltaNet.forward`` from ``gated_delta_rule_chunk`` to
+    ``self.norm`` (``model/model.py:505-506``, ``:516``). bf16 only. ``z`` holds
+    ``B * T * HV * 128`` bf16 values in the output's order (``[B, T, HV, 128]``); ``out``
+    (``[B, T, HV, 128]`` bf16) receives ``y`` and is allocated when not given. The un-normed
+    output is not kept.
+    """
+    what = "gated_delta_rule_chunk_gated_norm"
+    _require_cuda(what, q, k, v, g, beta, z, norm_weight, initial_state, out)
+    B, T, H, HV = _check_qkv(what, q, k, v)
+    if q.dtype != torch.bfloat16:
+        raise ValueError(f"{what}: expected bfloat16 q, k, v, got {q.dtype}")
+    shape = (B, T, HV, HEAD_DIM)
+    if z.dtype != torch.bfloat16 or z.numel() != B * T * HV * HEAD_DIM:
+        raise ValueError(f"z: expected {B * T * HV * HEAD_DIM} bfloat16 values {shape}, got {z.dtype} {tuple(z.shape)}")
+    if norm_weight.dtype != torch.bfloat16 or norm_weight.shape != (HEAD_DIM,):
+        raise ValueError(f"norm_weight: expected bfloat16 of shape {(HEAD_DIM,)}, got {norm_weight.dtype} "
+                         f"{tuple(norm_weight.shape)}")
+    if out is not None and (out.shape != shape or out.dtype != torch.bfloat16 or not out.is_contiguous()):
+        raise ValueError(f"out: expected a contiguous bfloat16 tensor of shape {shape}, got {out.dtype} "
+                         f"{tuple(out.shape)}")
+    g, beta = _gates(what, g, beta, B, T, HV)
+    cu, rows = _cu_seqlens_arg(what, cu_seqlens, B, T)
+    h0 = _state_arg(what, initial_state, rows, HV)
+    z = z.reshape(shape).contiguous()
+    w = norm_weight.contiguous()
+    if w.data_ptr() % 16:  # read with 16-byte loads
+        w = w.clone()
+    if out is None:
+        out = torch.empty(shape, dtype=torch.bfloat16, device=q.device)
+    final = torch.empty(rows, HV, HEAD_DIM, HEAD_DIM, dtype=torch.float32, device=q.device) if output_final_state else None
+    # the scan's output goes to `out` and is normalised there in place
+    _chunk_prefill(what, q, k, v, g, beta, h0, final, out, cu, rows, scale, norm=(z, w, eps, out))
+    return out, final
 
 
 def _check_state_inplace(what, state, B, HV):

@@ -1,9 +1,11 @@
-"""Fused decode step of one gated-delta layer (CUDA only).
+"""One gated-delta layer between the input projections and ``out_proj`` (CUDA only).
 
 ``decode_layer_step`` does, for one new token per row, what the StaticCache decode branch
-of ``GatedDeltaNet.forward`` (``model/model.py:465-467``, ``:496-499``, ``:516``) does
-between the input projections and ``out_proj``: conv step + SiLU, q/k L2 norm, gated
-delta rule step on the state in place, and the output-gated RMSNorm.
+of ``GatedDeltaNet.forward`` (``model/model.py:465-467``, ``:496-499``, ``:516``) does:
+conv step + SiLU, q/k L2 norm, gated delta rule step on the state in place, and the
+output-gated RMSNorm. ``prefill_layer`` does the same for a prompt (the prefill branch,
+``:478-479``, ``:482-489``, ``:505-506``, ``:516``): causal conv1d + SiLU, then the chunked
+gated delta rule with the output-gated RMSNorm fused into the same call.
 """
 
 from __future__ import annotations
@@ -11,7 +13,34 @@ from __future__ import annotations
 import torch
 
 from . import _lib
-from .gated_delta import HEAD_DIM, _require_cuda, _stream
+from .conv import causal_conv1d
+from .gated_delta import HEAD_DIM, _require_cuda, _stream, gated_delta_rule_chunk_gated_norm
+
+
+def prefill_layer(qkv, conv_weight, g, beta, z, norm_weight, key_heads: int, eps: float = 1e-6, initial_state=None,
+                  output_final_state: bool = True, scale: float | None = None, cu_seqlens=None):
+    """qkv ``[B, T, C]`` pre-conv bf16 (q | k | v channels, C = 2 * key_heads * 128 + HV * 128),
+    conv_weight ``[C, taps]`` (or ``[C, 1, taps]``), g ``[B, T, HV]`` fp32, beta ``[B, T, HV]``,
+    z ``[B, T, HV, 128]`` bf16, norm_weight ``[128]`` bf16; returns ``(y [B, T, HV, 128] bf16,
+    final_state [rows, HV, 128, 128] fp32 or None)``. With ``cu_seqlens`` (B = 1) the packed
+    sequences are convolved and scanned separately. q and k are read as views of the conv
+    output; the key heads are never repeated in memory."""
+    what = "prefill_layer"
+    _require_cuda(what, qkv, conv_weight, g, beta, z, norm_weight)
+    if qkv.dim() != 3:
+        raise ValueError(f"qkv: expected [B, T, C], got {tuple(qkv.shape)}")
+    B, T, C = qkv.shape
+    kd = key_heads * HEAD_DIM
+    if C <= 2 * kd or (C - 2 * kd) % HEAD_DIM:
+        raise ValueError(f"qkv: {C} channels do not split into 2 x {kd} key channels and whole value heads")
+    HV = (C - 2 * kd) // HEAD_DIM
+    y = causal_conv1d(qkv, conv_weight.reshape(C, -1), cu_seqlens=cu_seqlens)
+    q = y[..., :kd].view(B, T, key_heads, HEAD_DIM)
+    k = y[..., kd:2 * kd].view(B, T, key_heads, HEAD_DIM)
+    v = y[..., 2 * kd:].view(B, T, HV, HEAD_DIM)
+    return gated_delta_rule_chunk_gated_norm(q, k, v, g, beta, z, norm_weight, eps=eps, initial_state=initial_state,
+                                             output_final_state=output_final_state, scale=scale,
+                                             cu_seqlens=cu_seqlens)
 
 
 def decode_layer_step(qkv, conv_state, conv_weight, g, beta, state, z, norm_weight, key_heads: int,

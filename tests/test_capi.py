@@ -95,3 +95,10 @@ def test_chunk_workspace_size_and_checks():
     assert lib.gdn_chunk_prefill(*args, 24, need, None) == _lib.ERR_ALIGN
     with pytest.raises(ValueError, match="workspace"):
         _lib.check(_lib.ERR_WORKSPACE, "gdn_chunk_prefill")
+    # the norm-fused form checks its own pointers first, then the same workspace
+    norm = lambda z, w, out, ws, n: lib.gdn_chunk_prefill_gated_norm(*args, z, w, 1e-6, out, ws, n, None)  # noqa: E731
+    assert norm(None, 16, 16, 16, need) == _lib.ERR_NULL
+    assert norm(16, 16, None, 16, need) == _lib.ERR_NULL
+    assert norm(16, 8, 16, 16, need) == _lib.ERR_ALIGN
+    assert norm(16, 16, 40, 16, need) == _lib.ERR_ALIGN
+    assert norm(16, 16, 16, None, need) == _lib.ERR_WORKSPACE

@@ -1,11 +1,12 @@
-"""GPU parity of the fused decode layer against the composition of the oracle's ops."""
+"""GPU parity of the fused decode and prefill layers against the composition of the oracle's ops,
+and of the norm-fused chunked prefill against the separate chunk and norm calls."""
 
 import pytest
 import torch
 
 import jeeves_b200 as gdn
 import oracle
-from tests.helpers import maxabs, rel, same_bits
+from tests.helpers import gdn_inputs, maxabs, rel, same_bits
 
 pytestmark = pytest.mark.gpu
 
@@ -48,3 +49,114 @@ def test_decode_layer_matches_composition(B, H, HV, taps):
     assert rel(st_gpu, S_ref) < 1e-5
     assert maxabs(out, out_ref) < 2e-2
     assert (out.cpu() != out_ref).float().mean().item() < 0.02
+
+
+def reference_prefill_layer(qkv, w, g, beta, z, nw, H, HV, h0=None):
+    B, T, C = qkv.shape
+    y = oracle.causal_conv1d(qkv, w)
+    kd = H * 128
+    q = y[..., :kd].reshape(B, T, H, 128)
+    k = y[..., kd:2 * kd].reshape(B, T, H, 128)
+    v = y[..., 2 * kd:].reshape(B, T, HV, 128)
+    o, S = oracle.chunk_gated_delta_rule(q, k, v, g, beta, initial_state=h0, output_final_state=True)
+    out = oracle.gated_rms_norm(o.reshape(-1, 128), z.reshape(-1, 128), nw).reshape(B, T, HV, 128)
+    return out, S
+
+
+def layer_inputs(seed, B, T, H, HV):
+    gen = torch.Generator().manual_seed(seed)
+    C = 2 * H * 128 + HV * 128
+    qkv = torch.randn(B, T, C, generator=gen).to(torch.bfloat16)
+    w = (torch.randn(C, 4, generator=gen) * 0.5).to(torch.bfloat16)
+    g = -torch.exp(torch.randn(B, T, HV, generator=gen) * 0.5 - 3.0)
+    beta = torch.sigmoid(torch.randn(B, T, HV, generator=gen)).to(torch.bfloat16)
+    z = torch.randn(B, T, HV, 128, generator=gen).to(torch.bfloat16)
+    nw = (torch.rand(128, generator=gen) + 0.5).to(torch.bfloat16)
+    h0 = torch.randn(B, HV, 128, 128, generator=gen) * 0.02
+    return qkv, w, g, beta, z, nw, h0
+
+
+@pytest.mark.parametrize("B,T,H,HV", [(1, 700, 16, 32), (2, 130, 2, 4)])
+def test_prefill_layer_matches_oracle_composition(B, T, H, HV):
+    """conv + SiLU, chunked gated delta rule and gated norm (the prefill branch of the layer)
+    against the oracle's ops. The norm divides each row by its rms (about 0.01 with these inputs),
+    which magnifies the chunk output's absolute error about a hundredfold, so the layer is checked
+    step by step: the conv bit for bit, the chunk output within the bf16 output bound (max-abs
+    2e-2) and the state within 1e-3 relative, the norm of that output within one bf16 ulp of
+    the oracle's norm of the same values, and the whole output within 1e-2 relative (Frobenius)."""
+    qkv, w, g, beta, z, nw, h0 = layer_inputs(B * 100 + T, B, T, H, HV)
+    out_ref, S_ref = reference_prefill_layer(qkv, w, g, beta, z, nw, H, HV, h0)
+    qkv_d, w_d, g_d, b_d, z_d, nw_d, h0_d = (t.cuda() for t in (qkv, w, g, beta, z, nw, h0))
+    out, S = gdn.prefill_layer(qkv_d, w_d, g_d, b_d, z_d, nw_d, H, initial_state=h0_d)
+    assert out.shape == (B, T, HV, 128)
+    assert torch.isfinite(out.float()).all()
+    assert rel(S, S_ref) < 1e-3, rel(S, S_ref)
+    # the steps: conv, chunk output, norm of that output
+    y = gdn.causal_conv1d(qkv_d, w_d)
+    assert same_bits(y, oracle.causal_conv1d(qkv, w))
+    kd = H * 128
+    o, S2 = gdn.gated_delta_rule_chunk(y[..., :kd].view(B, T, H, 128), y[..., kd:2 * kd].view(B, T, H, 128),
+                                       y[..., 2 * kd:].view(B, T, HV, 128), g_d, b_d, initial_state=h0_d,
+                                       output_final_state=True)
+    assert same_bits(S2, S)
+    o_ref, _ = oracle.chunk_gated_delta_rule(*(t.cpu() for t in (y[..., :kd].reshape(B, T, H, 128),
+                                                                 y[..., kd:2 * kd].reshape(B, T, H, 128),
+                                                                 y[..., 2 * kd:].reshape(B, T, HV, 128))),
+                                             g, beta, initial_state=h0)
+    assert maxabs(o, o_ref) < 2e-2, maxabs(o, o_ref)
+    normed = oracle.gated_rms_norm(o.cpu().reshape(-1, 128), z.reshape(-1, 128), nw).reshape(B, T, HV, 128)
+    ulp = torch.ldexp(torch.ones_like(normed.float()), torch.frexp(normed.float())[1] - 8)  # one bf16 ulp each
+    assert ((out.cpu().float() - normed.float()).abs() <= ulp).all()
+    assert (out.cpu() != normed).float().mean().item() < 0.01
+    assert rel(out, out_ref) < 1e-2, rel(out, out_ref)
+
+
+def _chunk_then_norm(q, k, v, g, beta, z, nw, h0, cu=None):
+    o, S = gdn.gated_delta_rule_chunk(q, k, v, g, beta, initial_state=h0, output_final_state=True, cu_seqlens=cu)
+    y = gdn.gated_rms_norm(o.reshape(-1, 128), z.reshape(-1, 128), nw).reshape(o.shape)
+    return y, S
+
+
+@pytest.mark.parametrize("B,T,H,HV,state", [
+    (1, 1000, 16, 32, True),   # 64 scan CTAs: the cooperative launch, then the norm
+    (2, 300, 16, 32, False),   # 128 scan CTAs: still one chunk launch, two sequences in chunk-major order
+    (1, 65, 2, 4, True),       # 8 scan CTAs, a ragged last chunk
+    (3, 130, 16, 32, True),    # 192 scan CTAs: factor kernel, scan kernel, then the norm
+])
+def test_chunk_gated_norm_equals_chunk_then_norm_bitwise(B, T, H, HV, state):
+    q, k, v, g, beta, h0 = gdn_inputs(B * 7 + T, B, T, H, HV, state=state, normalise=False)
+    gen = torch.Generator().manual_seed(T)
+    z = torch.randn(B, T, HV, 128, generator=gen).to(torch.bfloat16).cuda()
+    nw = (torch.rand(128, generator=gen) + 0.5).to(torch.bfloat16).cuda()
+    q, k, v, g, beta = (t.cuda() for t in (q, k, v, g, beta))
+    h0 = None if h0 is None else h0.cuda()
+    y_ref, S_ref = _chunk_then_norm(q, k, v, g, beta, z, nw, h0)
+    y, S = gdn.gated_delta_rule_chunk_gated_norm(q, k, v, g, beta, z, nw, initial_state=h0, output_final_state=True)
+    assert same_bits(y, y_ref) and same_bits(S, S_ref)
+    out = torch.full_like(y, float("nan"))  # a caller-given output buffer
+    y2, _ = gdn.gated_delta_rule_chunk_gated_norm(q, k, v, g, beta, z, nw, initial_state=h0, out=out)
+    assert y2.data_ptr() == out.data_ptr() and same_bits(out, y_ref)
+
+
+@pytest.mark.parametrize("lens", [[300, 77], [1, 64, 0, 129, 400, 33, 2, 90]])
+def test_packed_chunk_gated_norm_equals_chunk_then_norm_bitwise(lens):
+    """Two packed sequences (128 scan CTAs: one chunk launch, chunks of the shorter sequence
+    skipped in chunk-major order) and eight (512 scan CTAs: factor, order and scan kernels)."""
+    H, HV, T = 16, 32, sum(lens)
+    q, k, v, g, beta, _ = gdn_inputs(len(lens), 1, T, H, HV, normalise=False)
+    gen = torch.Generator().manual_seed(len(lens) + 1)
+    h0 = (torch.randn(len(lens), HV, 128, 128, generator=gen) * 0.02).cuda()
+    z = torch.randn(1, T, HV, 128, generator=gen).to(torch.bfloat16).cuda()
+    nw = (torch.rand(128, generator=gen) + 0.5).to(torch.bfloat16).cuda()
+    cu = torch.tensor([0] + torch.tensor(lens).cumsum(0).tolist(), dtype=torch.int32).cuda()
+    q, k, v, g, beta = (t.cuda() for t in (q, k, v, g, beta))
+    y_ref, S_ref = _chunk_then_norm(q, k, v, g, beta, z, nw, h0, cu)
+    y, S = gdn.gated_delta_rule_chunk_gated_norm(q, k, v, g, beta, z, nw, initial_state=h0, output_final_state=True,
+                                                 cu_seqlens=cu)
+    assert same_bits(y, y_ref) and same_bits(S, S_ref)
+
+
+def test_prefill_layer_leaves_no_device_error():
+    from jeeves_b200 import _lib
+    torch.cuda.synchronize()
+    assert _lib.load().gdn_device_error(None, 0) == 0
