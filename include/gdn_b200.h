@@ -57,6 +57,25 @@ GDN_API int gdn_abi_version(void);
 GDN_API int gdn_device_error(void* stream, int reset);
 
 /*
+ * The layer's raw gate projections, for the entry points that compute beta and g themselves
+ * instead of reading them (delta_gates, model/model.py:314-321, with the rounding of
+ * model/triton_kernels.py:76-92; as gdn_delta_gates):
+ *   beta = bf16(sigmoid(b)),  g = log_decay_rate * softplus(a + dt_bias)  (fp32),
+ * both times valid[row] when `valid` is given. Rows follow the [B, T] token layout of the call
+ * (b * seqlen + t; t for a packed batch).
+ */
+typedef struct gdn_gate_inputs {
+    const void* b;                /* [rows, HV] bf16, row stride b_row_stride elements */
+    int64_t b_row_stride;
+    const void* a;                /* [rows, HV] bf16, row stride a_row_stride elements */
+    int64_t a_row_stride;
+    const void* dt_bias;          /* [HV] */
+    int dt_bias_dtype;            /* GDN_F32 or GDN_BF16 */
+    const float* log_decay_rate;  /* [HV] fp32, -exp(A_log) */
+    const uint8_t* valid;         /* [rows] bool, or NULL */
+} gdn_gate_inputs;
+
+/*
  * Gated delta rule, recurrent form, on CUDA cores in fp32. One launch covers:
  *   - the decode step with the state updated in place (state_out == state_in):
  *       replaces model/fla_inplace.py:17-26 (gated_delta_rule_step_inplace) and the
@@ -91,6 +110,21 @@ GDN_API int gdn_recurrent(const void* q, const void* k, const void* v, int qkv_d
                   float scale, void* stream);
 
 /*
+ * gdn_recurrent with beta and g computed in the kernel from the raw gate projections (the
+ * engine's delta_gates then delta_outputs / advance, inference/engine.py:429-430); results equal
+ * gdn_delta_gates followed by gdn_recurrent bit for bit.
+ */
+GDN_API int gdn_recurrent_gates(const void* q, const void* k, const void* v, int qkv_dtype,
+                                const gdn_gate_inputs* gates, const float* state_in, float* state_out,
+                                float* snapshots, void* o, const int64_t* steps, const int32_t* cu_seqlens,
+                                int64_t batch, int64_t seqlen, int64_t key_heads, int64_t value_heads,
+                                int64_t head_dim_k, int64_t head_dim_v,
+                                int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h,
+                                int64_t k_stride_b, int64_t k_stride_t, int64_t k_stride_h,
+                                int64_t v_stride_b, int64_t v_stride_t, int64_t v_stride_h,
+                                float scale, void* stream);
+
+/*
  * Chunked prefill on tcgen05 tensor cores (chunk 64, WY/UT form) with an fp32 state.
  * Replaces gated_delta_rule_chunk, model/model.py:289-294 (fla chunk_gated_delta_rule
  * on CUDA; fp32 eager torch_chunk_gated_delta_rule :242-286). bf16 q, k: [B, T, H, Dk],
@@ -114,6 +148,21 @@ GDN_API int gdn_chunk_prefill(const void* q, const void* k, const void* v, const
                               int64_t k_stride_b, int64_t k_stride_t, int64_t k_stride_h,
                               int64_t v_stride_b, int64_t v_stride_t, int64_t v_stride_h,
                               float scale, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * gdn_chunk_prefill with beta and g computed by the factor work from the raw gate projections
+ * (the engine's extend pass, delta_gates then delta_extend, inference/engine.py:378-379): no
+ * separate gates launch and no beta / g round trip through memory. Results equal
+ * gdn_delta_gates followed by gdn_chunk_prefill bit for bit. Same workspace as gdn_chunk_prefill.
+ */
+GDN_API int gdn_chunk_prefill_gates(const void* q, const void* k, const void* v, const gdn_gate_inputs* gates,
+                                    const float* initial_state, float* final_state, void* o,
+                                    const int32_t* cu_seqlens, int64_t batch, int64_t seqlen, int64_t key_heads,
+                                    int64_t value_heads, int64_t head_dim_k, int64_t head_dim_v,
+                                    int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h,
+                                    int64_t k_stride_b, int64_t k_stride_t, int64_t k_stride_h,
+                                    int64_t v_stride_b, int64_t v_stride_t, int64_t v_stride_h, float scale,
+                                    void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Chunked prefill followed by the output-gated RMSNorm of its output, in one call: the prefill

@@ -23,6 +23,14 @@ _i32 = ctypes.c_int
 _f32 = ctypes.c_float
 _sz = ctypes.c_size_t
 
+
+class GateInputs(ctypes.Structure):
+    """``gdn_gate_inputs``: the raw gate projections for the ``*_gates`` entry points."""
+
+    _fields_ = [("b", _p), ("b_row_stride", _i64), ("a", _p), ("a_row_stride", _i64), ("dt_bias", _p),
+                ("dt_bias_dtype", _i32), ("log_decay_rate", _p), ("valid", _p)]
+
+
 # name -> argument types, in declaration order of include/gdn_b200.h
 SIGNATURES: dict[str, list] = {
     "gdn_status_string": [_i32],
@@ -31,8 +39,13 @@ SIGNATURES: dict[str, list] = {
     "gdn_recurrent": [_p, _p, _p, _i32, _p, _p, _i32, _p, _p, _p, _p, _p, _p,
                       _i64, _i64, _i64, _i64, _i64, _i64,
                       _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _p],
+    "gdn_recurrent_gates": [_p, _p, _p, _i32, ctypes.POINTER(GateInputs), _p, _p, _p, _p, _p, _p,
+                            _i64, _i64, _i64, _i64, _i64, _i64,
+                            _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _p],
     "gdn_chunk_prefill": [_p, _p, _p, _p, _p, _i32, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64,
                           _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _p, _sz, _p],
+    "gdn_chunk_prefill_gates": [_p, _p, _p, ctypes.POINTER(GateInputs), _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64,
+                                _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _p, _sz, _p],
     "gdn_chunk_prefill_gated_norm": [_p, _p, _p, _p, _p, _i32, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64,
                                      _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _p, _p, _f32, _p,
                                      _p, _sz, _p],

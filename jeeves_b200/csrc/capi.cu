@@ -59,12 +59,28 @@ int gdn_device_error(void* stream, int reset) {
     return value;
 }
 
-int gdn_recurrent(const void* q, const void* k, const void* v, int qkv_dtype, const float* g, const void* beta,
-                  int beta_dtype, const float* state_in, float* state_out, float* snapshots, void* o,
-                  const int64_t* steps, const int32_t* cu_seqlens, int64_t batch, int64_t seqlen, int64_t key_heads,
-                  int64_t value_heads, int64_t head_dim_k, int64_t head_dim_v, int64_t q_stride_b, int64_t q_stride_t,
-                  int64_t q_stride_h, int64_t k_stride_b, int64_t k_stride_t, int64_t k_stride_h, int64_t v_stride_b,
-                  int64_t v_stride_t, int64_t v_stride_h, float scale, void* stream) {
+// gdn_gate_inputs -> the kernels' GateInputs; status of its checks (null pointers, dtype).
+static int gate_args(const gdn_gate_inputs* in, GateInputs* out) {
+    if (!in->b || !in->a || !in->dt_bias || !in->log_decay_rate) return GDN_ERR_NULL;
+    if (!known_dtype(in->dt_bias_dtype)) return GDN_ERR_DTYPE;
+    out->b = in->b;
+    out->sb = in->b_row_stride;
+    out->a = in->a;
+    out->sa = in->a_row_stride;
+    out->dt_bias = in->dt_bias;
+    out->dt_f32 = in->dt_bias_dtype == GDN_F32;
+    out->rate = in->log_decay_rate;
+    out->valid = in->valid;
+    return GDN_OK;
+}
+
+static int recurrent(const void* q, const void* k, const void* v, int qkv_dtype, const float* g, const void* beta,
+                     int beta_dtype, const gdn_gate_inputs* gates, const float* state_in, float* state_out,
+                     float* snapshots, void* o, const int64_t* steps, const int32_t* cu_seqlens, int64_t batch,
+                     int64_t seqlen, int64_t key_heads, int64_t value_heads, int64_t head_dim_k, int64_t head_dim_v,
+                     int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h, int64_t k_stride_b,
+                     int64_t k_stride_t, int64_t k_stride_h, int64_t v_stride_b, int64_t v_stride_t,
+                     int64_t v_stride_h, float scale, void* stream) {
     if (!known_dtype(qkv_dtype) || !known_dtype(beta_dtype)) return GDN_ERR_DTYPE;
     if (batch < 0 || seqlen < 0 || key_heads <= 0 || value_heads <= 0 || value_heads % key_heads) return GDN_ERR_SHAPE;
     if (batch > 65535 || value_heads > 65535) return GDN_ERR_SHAPE;
@@ -79,8 +95,13 @@ int gdn_recurrent(const void* q, const void* k, const void* v, int qkv_dtype, co
         }
         return GDN_OK;
     }
-    if (!k || !v || !g || !beta) return GDN_ERR_NULL;
+    if (!k || !v || (!gates && (!g || !beta))) return GDN_ERR_NULL;
     if (o && !q) return GDN_ERR_NULL;
+    GateInputs G{};
+    if (gates) {
+        const int st = gate_args(gates, &G);
+        if (st != GDN_OK) return st;
+    }
     if (steps && (o || snapshots)) return GDN_ERR_SHAPE;  // an advance writes only the state
     const int es = elem_size(qkv_dtype);
     if (!rows_aligned(k, es, k_stride_b, k_stride_t, k_stride_h) || !rows_aligned(v, es, v_stride_b, v_stride_t, v_stride_h))
@@ -89,7 +110,7 @@ int gdn_recurrent(const void* q, const void* k, const void* v, int qkv_dtype, co
     if ((state_in && !aligned16(state_in)) || (state_out && !aligned16(state_out)) ||
         (snapshots && !aligned16(snapshots)) || (o && !aligned16(o)))
         return GDN_ERR_ALIGN;
-    RecurrentArgs a;
+    RecurrentArgs a{};
     a.q = q; a.k = k; a.v = v; a.qkv_dtype = qkv_dtype;
     a.g = g; a.beta = beta; a.beta_dtype = beta_dtype;
     a.state_in = state_in; a.state_out = state_out; a.snapshots = snapshots; a.o = o;
@@ -99,11 +120,36 @@ int gdn_recurrent(const void* q, const void* k, const void* v, int qkv_dtype, co
     a.ksb = k_stride_b; a.kst = k_stride_t; a.ksh = k_stride_h;
     a.vsb = v_stride_b; a.vst = v_stride_t; a.vsh = v_stride_h;
     a.scale = scale;
+    a.gates = G;
     return launch_recurrent(a, as_stream(stream));
 }
 
+int gdn_recurrent(const void* q, const void* k, const void* v, int qkv_dtype, const float* g, const void* beta,
+                  int beta_dtype, const float* state_in, float* state_out, float* snapshots, void* o,
+                  const int64_t* steps, const int32_t* cu_seqlens, int64_t batch, int64_t seqlen, int64_t key_heads,
+                  int64_t value_heads, int64_t head_dim_k, int64_t head_dim_v, int64_t q_stride_b, int64_t q_stride_t,
+                  int64_t q_stride_h, int64_t k_stride_b, int64_t k_stride_t, int64_t k_stride_h, int64_t v_stride_b,
+                  int64_t v_stride_t, int64_t v_stride_h, float scale, void* stream) {
+    return recurrent(q, k, v, qkv_dtype, g, beta, beta_dtype, nullptr, state_in, state_out, snapshots, o, steps,
+                     cu_seqlens, batch, seqlen, key_heads, value_heads, head_dim_k, head_dim_v, q_stride_b, q_stride_t,
+                     q_stride_h, k_stride_b, k_stride_t, k_stride_h, v_stride_b, v_stride_t, v_stride_h, scale, stream);
+}
+
+int gdn_recurrent_gates(const void* q, const void* k, const void* v, int qkv_dtype, const gdn_gate_inputs* gates,
+                        const float* state_in, float* state_out, float* snapshots, void* o, const int64_t* steps,
+                        const int32_t* cu_seqlens, int64_t batch, int64_t seqlen, int64_t key_heads,
+                        int64_t value_heads, int64_t head_dim_k, int64_t head_dim_v, int64_t q_stride_b,
+                        int64_t q_stride_t, int64_t q_stride_h, int64_t k_stride_b, int64_t k_stride_t,
+                        int64_t k_stride_h, int64_t v_stride_b, int64_t v_stride_t, int64_t v_stride_h, float scale,
+                        void* stream) {
+    if (!gates) return GDN_ERR_NULL;
+    return recurrent(q, k, v, qkv_dtype, nullptr, nullptr, GDN_BF16, gates, state_in, state_out, snapshots, o, steps,
+                     cu_seqlens, batch, seqlen, key_heads, value_heads, head_dim_k, head_dim_v, q_stride_b, q_stride_t,
+                     q_stride_h, k_stride_b, k_stride_t, k_stride_h, v_stride_b, v_stride_t, v_stride_h, scale, stream);
+}
+
 static int chunk_prefill(const void* q, const void* k, const void* v, const float* g, const void* beta, int beta_dtype,
-                         const float* initial_state, float* final_state, void* o, const int32_t* cu_seqlens,
+                         const gdn_gate_inputs* gates, const float* initial_state, float* final_state, void* o, const int32_t* cu_seqlens,
                          int64_t batch, int64_t seqlen, int64_t key_heads, int64_t value_heads, int64_t head_dim_k,
                          int64_t head_dim_v, int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h,
                          int64_t k_stride_b, int64_t k_stride_t, int64_t k_stride_h, int64_t v_stride_b,
@@ -115,7 +161,12 @@ static int chunk_prefill(const void* q, const void* k, const void* v, const floa
     if (seqlen > INT32_MAX - 64) return GDN_ERR_SHAPE;  // TMA coordinates are 32-bit
     if (head_dim_k != kHeadDim || head_dim_v != kHeadDim) return GDN_ERR_UNSUPPORTED;
     if (batch == 0) return GDN_OK;
-    if (!q || !k || !v || !g || !beta || !o) return GDN_ERR_NULL;
+    if (!q || !k || !v || !o || (!gates && (!g || !beta))) return GDN_ERR_NULL;
+    GateInputs G{};
+    if (gates) {
+        const int st = gate_args(gates, &G);
+        if (st != GDN_OK) return st;
+    }
     if (cu_seqlens == nullptr && seqlen == 0) return GDN_OK;
     if (!rows_aligned(q, 2, q_stride_b, q_stride_t, q_stride_h) || !rows_aligned(k, 2, k_stride_b, k_stride_t, k_stride_h) ||
         !rows_aligned(v, 2, v_stride_b, v_stride_t, v_stride_h) || !aligned16(o))
@@ -132,6 +183,7 @@ static int chunk_prefill(const void* q, const void* k, const void* v, const floa
     a.scale = scale;
     a.workspace = workspace;
     a.workspace_bytes = workspace_bytes;
+    a.gates = G;
     a.z = z;
     a.norm_w = norm_weight;
     a.y = out;
@@ -147,7 +199,7 @@ int gdn_chunk_prefill(const void* q, const void* k, const void* v, const float* 
                       int64_t k_stride_b, int64_t k_stride_t, int64_t k_stride_h, int64_t v_stride_b,
                       int64_t v_stride_t, int64_t v_stride_h, float scale, void* workspace, size_t workspace_bytes,
                       void* stream) {
-    return chunk_prefill(q, k, v, g, beta, beta_dtype, initial_state, final_state, o, cu_seqlens, batch, seqlen,
+    return chunk_prefill(q, k, v, g, beta, beta_dtype, nullptr, initial_state, final_state, o, cu_seqlens, batch, seqlen,
                          key_heads, value_heads, head_dim_k, head_dim_v, q_stride_b, q_stride_t, q_stride_h, k_stride_b,
                          k_stride_t, k_stride_h, v_stride_b, v_stride_t, v_stride_h, scale, workspace, workspace_bytes,
                          nullptr, nullptr, 0.f, nullptr, stream);
@@ -163,10 +215,24 @@ int gdn_chunk_prefill_gated_norm(const void* q, const void* k, const void* v, co
                                  void* workspace, size_t workspace_bytes, void* stream) {
     if (batch > 0 && (!z || !norm_weight || !out)) return GDN_ERR_NULL;
     if (!aligned16(z) || !aligned16(norm_weight) || !aligned16(out)) return GDN_ERR_ALIGN;
-    return chunk_prefill(q, k, v, g, beta, beta_dtype, initial_state, final_state, o, cu_seqlens, batch, seqlen,
+    return chunk_prefill(q, k, v, g, beta, beta_dtype, nullptr, initial_state, final_state, o, cu_seqlens, batch, seqlen,
                          key_heads, value_heads, head_dim_k, head_dim_v, q_stride_b, q_stride_t, q_stride_h, k_stride_b,
                          k_stride_t, k_stride_h, v_stride_b, v_stride_t, v_stride_h, scale, workspace, workspace_bytes,
                          z, norm_weight, eps, out, stream);
+}
+
+int gdn_chunk_prefill_gates(const void* q, const void* k, const void* v, const gdn_gate_inputs* gates,
+                            const float* initial_state, float* final_state, void* o, const int32_t* cu_seqlens,
+                            int64_t batch, int64_t seqlen, int64_t key_heads, int64_t value_heads, int64_t head_dim_k,
+                            int64_t head_dim_v, int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h,
+                            int64_t k_stride_b, int64_t k_stride_t, int64_t k_stride_h, int64_t v_stride_b,
+                            int64_t v_stride_t, int64_t v_stride_h, float scale, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+    if (!gates) return GDN_ERR_NULL;
+    return chunk_prefill(q, k, v, nullptr, nullptr, GDN_BF16, gates, initial_state, final_state, o, cu_seqlens, batch,
+                         seqlen, key_heads, value_heads, head_dim_k, head_dim_v, q_stride_b, q_stride_t, q_stride_h,
+                         k_stride_b, k_stride_t, k_stride_h, v_stride_b, v_stride_t, v_stride_h, scale, workspace,
+                         workspace_bytes, nullptr, nullptr, 0.f, nullptr, stream);
 }
 
 size_t gdn_chunk_prefill_workspace_size(int64_t batch, int64_t seqlen, int64_t value_heads, int packed) {

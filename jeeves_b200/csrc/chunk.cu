@@ -38,6 +38,7 @@
 // started, the issuer for the MMAs it issued, TMEM is freed and the CTA returns.
 
 #include "common.cuh"
+#include "gates.cuh"
 #include "launch.h"
 #include "sm100.cuh"
 
@@ -119,6 +120,7 @@ struct FactorParams {
     int nseq, ncd;     // sequences; chunks per row of the dense layout
     int HV, rep;
     float scale;
+    GateInputs gates;  // beta and g from the raw projections when gates.b is set
 };
 
 struct FSmem {
@@ -224,8 +226,12 @@ __device__ __forceinline__ int factor_unit(const FactorParams& p, int64_t unit, 
         float gv = 0.f, bv = 0.f;
         if (pt < nvalid) {
             const int64_t gi = (brow * p.T + t + pt) * p.HV + hv;
-            gv = p.g[gi];
-            bv = p.beta_f32 ? static_cast<const float*>(p.beta)[gi] : to_f32(static_cast<const bf16*>(p.beta)[gi]);
+            if (p.gates.b) {
+                delta_gate(p.gates, brow * p.T + t + pt, hv, bv, gv);
+            } else {
+                gv = p.g[gi];
+                bv = p.beta_f32 ? static_cast<const float*>(p.beta)[gi] : to_f32(static_cast<const bf16*>(p.beta)[gi]);
+            }
         }
         sh.graw[pt] = gv;
         sh.braw[pt] = bv;
@@ -1203,6 +1209,7 @@ int launch_chunk(const ChunkArgs& a, cudaStream_t s) {
     const int ncd = (int)((a.T + 63) / 64);
     f.g = a.g;
     f.beta = a.beta;
+    f.gates = a.gates;
     f.beta_f32 = a.beta_dtype == GDN_F32;
     f.cu_seqlens = a.cu_seqlens;
     f.records = static_cast<uint8_t*>(a.workspace);

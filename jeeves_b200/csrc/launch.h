@@ -6,6 +6,19 @@
 
 namespace gdn {
 
+// The layer's raw gate projections, from which a kernel computes beta and g itself (the
+// device copy of gdn_gate_inputs; the arithmetic is delta_gate in gates.cuh). b == null: none.
+struct GateInputs {
+    const void* b;  // [rows, HV] bf16 with row stride sb
+    int64_t sb;
+    const void* a;  // [rows, HV] bf16 with row stride sa
+    int64_t sa;
+    const void* dt_bias;  // [HV], fp32 (dt_f32) or bf16
+    int dt_f32;
+    const float* rate;     // [HV] log decay rate (-exp(A_log))
+    const uint8_t* valid;  // [rows] or null
+};
+
 struct RecurrentArgs {
     const void* q;
     const void* k;
@@ -25,6 +38,7 @@ struct RecurrentArgs {
     int H, HV;
     int64_t qsb, qst, qsh, ksb, kst, ksh, vsb, vst, vsh;
     float scale;
+    GateInputs gates;  // used instead of g and beta when gates.b is set
 };
 int launch_recurrent(const RecurrentArgs& a, cudaStream_t s);
 
@@ -45,6 +59,7 @@ struct ChunkArgs {
     float scale;
     void* workspace;
     size_t workspace_bytes;
+    GateInputs gates;  // used instead of g and beta when gates.b is set
     // output-gated RMSNorm of o fused into the call (y null: none); z in o's row layout, y may be o
     const void* z;
     const void* norm_w;

@@ -13,6 +13,7 @@
 // reduction round per token serves both the delta and the output.
 
 #include "common.cuh"
+#include "gates.cuh"
 #include "launch.h"
 
 namespace gdn {
@@ -33,6 +34,7 @@ struct RecurrentParams {
     int HV, rep;
     int64_t qsb, qst, qsh, ksb, kst, ksh, vsb, vst, vsh;
     float scale;
+    GateInputs gates;  // beta and g from the raw projections when gates.b is set
 };
 
 template <typename TIn, typename TBeta, int VS, int NT>
@@ -90,8 +92,15 @@ __global__ void __launch_bounds__(NT) recurrent_kernel(const RecurrentParams p) 
         if (outputs) ql = load4(qbase + tok * p.qst + 4 * lane);
         const float4 vv = load4(vbase + tok * p.vst + col);
         const int64_t gi = (brow * p.T + tok) * p.HV + hv;
-        const float decay = expf(p.g[gi]);
-        const float bt = to_f32(beta[gi]);
+        float decay, bt;
+        if (p.gates.b) {
+            float gv;
+            delta_gate(p.gates, brow * p.T + tok, hv, bt, gv);
+            decay = expf(gv);
+        } else {
+            decay = expf(p.g[gi]);
+            bt = to_f32(beta[gi]);
+        }
 
         const float kk = warp_sum(kl.x * kl.x + kl.y * kl.y + kl.z * kl.z + kl.w * kl.w);
         const float rk = rsqrtf(kk + 1e-6f);
@@ -210,6 +219,7 @@ int launch_recurrent(const RecurrentArgs& a, cudaStream_t s) {
     p.ksb = a.ksb; p.kst = a.kst; p.ksh = a.ksh;
     p.vsb = a.vsb; p.vst = a.vst; p.vsh = a.vsh;
     p.scale = a.scale;
+    p.gates = a.gates;
     if (a.rows == 0) return GDN_OK;
     if (a.qkv_dtype == GDN_BF16) {
         return a.beta_dtype == GDN_BF16 ? dispatch_recurrent<bf16, bf16>(p, a.rows, s)
@@ -258,7 +268,7 @@ int launch_decode_layer(const DecodeLayerArgs& a, cudaStream_t s) {
     int st = launch_conv1d_silu_step(a.qkv, a.qkv_sb, a.conv_state, a.conv_w, a.workspace, a.B, C, a.taps, a.K, s);
     if (st != GDN_OK) return st;
     const bf16* y = static_cast<const bf16*>(a.workspace);
-    RecurrentArgs r;
+    RecurrentArgs r{};
     r.q = y;
     r.k = y + key_dim;
     r.v = y + 2 * key_dim;

@@ -72,7 +72,8 @@ def _state_arg(what: str, state, rows, HV, *, name="initial_state"):
 
 
 def _recurrent(what, q, k, v, g, beta, *, state_in=None, state_out=None, snapshots=None, o=None, steps=None,
-               cu_seqlens=None, rows=None, scale=None):
+               cu_seqlens=None, rows=None, scale=None, gates=None):
+    """One gdn_recurrent call, or gdn_recurrent_gates when ``gates`` (a ``_lib.GateInputs``) is given."""
     B, T = k.shape[:2]
     H, HV = k.shape[2], v.shape[2]
     q = None if q is None else _heads_last_contiguous(q)
@@ -80,12 +81,15 @@ def _recurrent(what, q, k, v, g, beta, *, state_in=None, state_out=None, snapsho
     if scale is None:
         scale = HEAD_DIM ** -0.5
     qs = (0, 0, 0) if q is None else (q.stride(0), q.stride(1), q.stride(2))
-    status = _lib.load().gdn_recurrent(
-        _ptr(q), _ptr(k), _ptr(v), _DTYPES[k.dtype], _ptr(g), _ptr(beta), _DTYPES[beta.dtype],
-        _ptr(state_in), _ptr(state_out), _ptr(snapshots), _ptr(o), _ptr(steps), _ptr(cu_seqlens),
-        B if rows is None else rows, T, H, HV, HEAD_DIM, HEAD_DIM,
-        *qs, k.stride(0), k.stride(1), k.stride(2), v.stride(0), v.stride(1), v.stride(2),
-        float(scale), _stream())
+    tail = (_ptr(state_in), _ptr(state_out), _ptr(snapshots), _ptr(o), _ptr(steps), _ptr(cu_seqlens),
+            B if rows is None else rows, T, H, HV, HEAD_DIM, HEAD_DIM,
+            *qs, k.stride(0), k.stride(1), k.stride(2), v.stride(0), v.stride(1), v.stride(2), float(scale), _stream())
+    lib = _lib.load()
+    if gates is None:
+        status = lib.gdn_recurrent(_ptr(q), _ptr(k), _ptr(v), _DTYPES[k.dtype], _ptr(g), _ptr(beta),
+                                   _DTYPES[beta.dtype], *tail)
+    else:
+        status = lib.gdn_recurrent_gates(_ptr(q), _ptr(k), _ptr(v), _DTYPES[k.dtype], gates, *tail)
     _lib.check(status, what)
 
 
@@ -147,9 +151,10 @@ def gated_delta_rule_chunk(q, k, v, g, beta, initial_state=None, output_final_st
     return o, final
 
 
-def _chunk_prefill(what, q, k, v, g, beta, h0, final, o, cu, rows, scale, norm=None):
-    """One gdn_chunk_prefill call (or gdn_chunk_prefill_gated_norm when ``norm`` = (z, weight,
-    eps, out)), with the workspace taken from PyTorch's caching allocator."""
+def _chunk_prefill(what, q, k, v, g, beta, h0, final, o, cu, rows, scale, norm=None, gates=None):
+    """One gdn_chunk_prefill call (gdn_chunk_prefill_gated_norm when ``norm`` = (z, weight, eps,
+    out); gdn_chunk_prefill_gates when ``gates`` is a ``_lib.GateInputs``), with the workspace
+    taken from PyTorch's caching allocator."""
     B, T, H = k.shape[:3]
     HV = v.shape[2]
     if T == 0:
@@ -160,10 +165,15 @@ def _chunk_prefill(what, q, k, v, g, beta, h0, final, o, cu, rows, scale, norm=N
     lib = _lib.load()
     ws_bytes = lib.gdn_chunk_prefill_workspace_size(rows, T, HV, int(cu is not None))
     workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device)
-    args = (q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(), beta.data_ptr(), _DTYPES[beta.dtype], _ptr(h0),
-            _ptr(final), o.data_ptr(), _ptr(cu), rows, T, H, HV, HEAD_DIM, HEAD_DIM,
+    tail = (_ptr(h0), _ptr(final), o.data_ptr(), _ptr(cu), rows, T, H, HV, HEAD_DIM, HEAD_DIM,
             q.stride(0), q.stride(1), q.stride(2), k.stride(0), k.stride(1), k.stride(2), v.stride(0), v.stride(1),
             v.stride(2), float(HEAD_DIM ** -0.5 if scale is None else scale))
+    if gates is not None:
+        status = lib.gdn_chunk_prefill_gates(q.data_ptr(), k.data_ptr(), v.data_ptr(), gates, *tail,
+                                             workspace.data_ptr(), ws_bytes, _stream())
+        _lib.check(status, what)
+        return
+    args = (q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(), beta.data_ptr(), _DTYPES[beta.dtype], *tail)
     if norm is None:
         status = lib.gdn_chunk_prefill(*args, workspace.data_ptr(), ws_bytes, _stream())
     else:

@@ -102,3 +102,26 @@ def test_chunk_workspace_size_and_checks():
     assert norm(16, 8, 16, 16, need) == _lib.ERR_ALIGN
     assert norm(16, 16, 40, 16, need) == _lib.ERR_ALIGN
     assert norm(16, 16, 16, None, need) == _lib.ERR_WORKSPACE
+
+
+def test_gate_entry_points_check_their_inputs():
+    """The *_gates entry points refuse a missing gate struct, missing projections and a bad
+    dt_bias dtype before any launch."""
+    lib = _lib.load()
+    qkv = [16, 16, 16]
+    strides = [128] * 9
+    good = _lib.GateInputs(16, 32, 16, 32, 16, _lib.F32, 16, None)
+    no_a = _lib.GateInputs(16, 32, None, 32, 16, _lib.F32, 16, None)
+    bad_dt = _lib.GateInputs(16, 32, 16, 32, 16, 7, 16, None)
+    rec = lambda gates: lib.gdn_recurrent_gates(*qkv, _lib.BF16, gates, None, None, None, 16, None, None,  # noqa: E731
+                                                1, 1, 1, 1, 128, 128, *strides, 0.088, None)
+    assert rec(None) == _lib.ERR_NULL
+    assert rec(ctypes.byref(no_a)) == _lib.ERR_NULL
+    assert rec(ctypes.byref(bad_dt)) == _lib.ERR_DTYPE
+    need = lib.gdn_chunk_prefill_workspace_size(1, 64, 1, 0)
+    chunk = lambda gates, ws: lib.gdn_chunk_prefill_gates(*qkv, gates, None, None, 16, None, 1, 64, 1, 1,  # noqa: E731
+                                                          128, 128, *strides, 0.088, ws, need, None)
+    assert chunk(None, 16) == _lib.ERR_NULL
+    assert chunk(ctypes.byref(no_a), 16) == _lib.ERR_NULL
+    assert chunk(ctypes.byref(bad_dt), 16) == _lib.ERR_DTYPE
+    assert chunk(ctypes.byref(good), None) == _lib.ERR_WORKSPACE

@@ -64,3 +64,65 @@ def test_delta_gates_rejects_bad_inputs():
         gdn.delta_gates(b, b, dt, r, torch.ones(2, device="cuda"))
     with pytest.raises(ValueError, match="dt_bias"):
         gdn.delta_gates(b, b, torch.zeros(3, device="cuda"), r)
+
+
+def _gated_inputs(seed, B, T, H, HV, dt_f32=True, with_valid=False):
+    gen = torch.Generator().manual_seed(seed)
+    q = torch.randn(B, T, H, 128, generator=gen).to(torch.bfloat16)
+    k = torch.randn(B, T, H, 128, generator=gen).to(torch.bfloat16)
+    v = torch.randn(B, T, HV, 128, generator=gen).to(torch.bfloat16)
+    proj = (torch.randn(B, T, 2 * HV + 8, generator=gen) * 3).to(torch.bfloat16)  # one merged projection
+    proj[..., 0, 8 + HV:8 + HV + 4] = 25.0  # softplus beyond 20 takes the identity branch
+    b, a = proj[..., 8:8 + HV], proj[..., 8 + HV:]
+    dt = torch.randn(HV, generator=gen) if dt_f32 else torch.randn(HV, generator=gen).to(torch.bfloat16)
+    rate = -torch.rand(HV, generator=gen).exp() * 0.05
+    valid = (torch.rand(B, T, generator=gen) < 0.8) if with_valid else None
+    h0 = torch.randn(B, HV, 128, 128, generator=gen) * 0.02
+    dev = [None if t is None else t.cuda() for t in (q, k, v, b, a, dt, rate, valid, h0)]
+    return dev
+
+
+@pytest.mark.parametrize("B,T,H,HV,dt_f32,with_valid", [
+    (1, 700, 16, 32, True, False),   # the cooperative launch (64 scan CTAs)
+    (3, 130, 16, 32, False, True),   # factor kernel + scan kernel, bf16 dt_bias, a valid mask
+    (2, 65, 2, 4, True, True),
+])
+def test_chunk_gates_equal_gates_then_chunk_bitwise(B, T, H, HV, dt_f32, with_valid):
+    """The gates computed by the prefill's factor work give the same bits as delta_gates followed
+    by gated_delta_rule_chunk (the engine's extend pass, inference/engine.py:378-379)."""
+    q, k, v, b, a, dt, rate, valid, h0 = _gated_inputs(B * 10 + T, B, T, H, HV, dt_f32, with_valid)
+    beta, g = gdn.delta_gates(b, a, dt, rate, valid)
+    o_ref, s_ref = gdn.gated_delta_rule_chunk(q, k, v, g, beta, initial_state=h0, output_final_state=True)
+    o, s = gdn.gated_delta_rule_chunk_gates(q, k, v, b, a, dt, rate, valid, initial_state=h0, output_final_state=True)
+    assert same_bits(o, o_ref) and same_bits(s, s_ref)
+
+
+def test_packed_chunk_gates_equal_gates_then_chunk_bitwise():
+    lens = [70, 300, 1, 129, 0, 257]
+    q, k, v, b, a, dt, rate, valid, _ = _gated_inputs(5, 1, sum(lens), 16, 32, True, True)
+    h0 = (torch.randn(len(lens), 32, 128, 128, generator=torch.Generator().manual_seed(6)) * 0.02).cuda()
+    cu = torch.tensor([0] + torch.tensor(lens).cumsum(0).tolist(), dtype=torch.int32).cuda()
+    beta, g = gdn.delta_gates(b, a, dt, rate, valid)
+    o_ref, s_ref = gdn.gated_delta_rule_chunk(q, k, v, g, beta, initial_state=h0, output_final_state=True, cu_seqlens=cu)
+    o, s = gdn.gated_delta_rule_chunk_gates(q, k, v, b, a, dt, rate, valid, initial_state=h0, output_final_state=True,
+                                            cu_seqlens=cu)
+    assert same_bits(o, o_ref) and same_bits(s, s_ref)
+
+
+@pytest.mark.parametrize("B,T,with_valid", [(4, 1, False), (3, 5, True)])
+def test_step_gates_equal_gates_then_step_bitwise(B, T, with_valid):
+    """Decode (T = 1) and verify (T = 5) steps with the gates computed in the recurrent kernel."""
+    q, k, v, b, a, dt, rate, valid, h0 = _gated_inputs(B + T, B, T, 16, 32, True, with_valid)
+    beta, g = gdn.delta_gates(b, a, dt, rate, valid)
+    o_ref, s_ref = gdn.gated_delta_rule_step(q, k, v, g, beta, initial_state=h0, output_final_state=True)
+    o, s = gdn.gated_delta_rule_step_gates(q, k, v, b, a, dt, rate, valid, initial_state=h0, output_final_state=True)
+    assert same_bits(o, o_ref) and same_bits(s, s_ref)
+
+
+def test_fp32_chunk_gates_equal_gates_then_chunk_bitwise():
+    q, k, v, b, a, dt, rate, _, h0 = _gated_inputs(9, 2, 40, 2, 4)
+    q, k, v = q.float(), k.float(), v.float()
+    beta, g = gdn.delta_gates(b, a, dt, rate)
+    o_ref, s_ref = gdn.gated_delta_rule_chunk(q, k, v, g, beta, initial_state=h0, output_final_state=True)
+    o, s = gdn.gated_delta_rule_chunk_gates(q, k, v, b, a, dt, rate, initial_state=h0, output_final_state=True)
+    assert same_bits(o, o_ref) and same_bits(s, s_ref)
