@@ -266,6 +266,62 @@ GDN_API int gdn_delta_gates(const void* b, int64_t b_stride, const void* a, int6
                             void* stream);
 
 /*
+ * Decode attention over a KV cache (replaces decode_attention, model/model.py:354-361, whose CUDA
+ * path is the split-key kernel of model/triton_kernels.py:117-211): the drafter's mask-row
+ * queries over the delta layers' key cache (inference/engine.py:436-437) and the attention
+ * layers' rows. q: [B, R, H, D] bf16 (element strides b, r, h); k_cache, v_cache: [cache_rows,
+ * cache_len, Hkv, D] bf16 (strides b, s, h), of which rows 0..B-1 and keys 0..keys-1 are read;
+ * mask: [B, 1, R, keys] bf16 additive (strides b, r; keys contiguous); o: [B, R, H, D] bf16
+ * contiguous. o = softmax(scale q k^T + mask) v per query head, key head h / (H / Hkv); a row
+ * whose keys are all masked gets zeros; keys == 0 gives zeros. D is 128 or 256, R * H / Hkv at
+ * most 64, every pointer and stride 16-byte aligned (mask row strides included). On tcgen05: one
+ * CTA per (batch row, key head, split of 128 keys at D = 128, 64 at D = 256); with more than one
+ * split, per-split results go to the workspace and a second kernel combines them.
+ */
+GDN_API int gdn_decode_attention(const void* q, int64_t q_stride_b, int64_t q_stride_r, int64_t q_stride_h,
+                                 const void* k_cache, int64_t k_stride_b, int64_t k_stride_s, int64_t k_stride_h,
+                                 const void* v_cache, int64_t v_stride_b, int64_t v_stride_s, int64_t v_stride_h,
+                                 const void* mask, int64_t mask_stride_b, int64_t mask_stride_r, void* o,
+                                 int64_t batch, int64_t rows, int64_t heads, int64_t kv_heads, int64_t head_dim,
+                                 int64_t keys, int64_t cache_rows, int64_t cache_len, float scale,
+                                 void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Workspace bytes gdn_decode_attention needs: (D + 1) * 4 bytes per (batch row, key head, split,
+ * 64 query rows) when there is more than one split, else 0. No counterpart in the reference
+ * (its wrapper allocates the partials inside the call).
+ */
+GDN_API size_t gdn_decode_attention_workspace_size(int64_t batch, int64_t kv_heads, int64_t keys, int64_t head_dim);
+
+/*
+ * Rotary embedding with per-row positions (replaces apply_rotary with 3-D cos / sin,
+ * model/model.py:182-196, and its CUDA kernel model/triton_kernels.py:54-75). x, out:
+ * [B, T, H, D] bf16 contiguous; cos, sin: [B, T, F] fp32 contiguous, 2F <= D. Rounds like the
+ * eager path on bf16: out = bf16(bf16(x c) + bf16(rotate_half(x) s)) over the first 2F elements
+ * with c, s rounded to bf16; the rest copied. Bit-identical to the eager path.
+ */
+GDN_API int gdn_rotary(const void* x, const float* cos, const float* sin, void* out, int64_t batch, int64_t seqlen,
+                       int64_t heads, int64_t head_dim, int64_t n_freqs, void* stream);
+
+/*
+ * The drafter's cache writes of one decode cycle (replaces rotate_into_cache, model/model.py:342-351;
+ * CUDA kernel model/triton_kernels.py:214-262). k, v: [B, K, H, D] bf16 contiguous; qm, km, vm:
+ * [B, M, H, D] bf16 sharing element strides (m_stride_b, m_stride_t), heads contiguous; cos_c,
+ * sin_c: [B, K, F] fp32; cos_m, sin_m: [B, M, F] fp32; k_cache, v_cache: [rows, slots, H, D]
+ * bf16 sharing strides (cache_stride_b, cache_stride_s), heads contiguous; rows: [B, K] int64
+ * (strides b, t); positions: [B, K] int64 contiguous. Writes k_cache / v_cache[rows[b, t],
+ * positions[b, t]] = rotary(k), v; q_out [B, M, H, D] = rotary(qm); k_cache / v_cache[b,
+ * tail_start + m] = rotary(km), vm. Bit-identical to the eager path.
+ */
+GDN_API int gdn_rotate_into_cache(const void* k, const void* v, const void* qm, const void* km, const void* vm,
+                                  int64_t m_stride_b, int64_t m_stride_t, const float* cos_c, const float* sin_c,
+                                  const float* cos_m, const float* sin_m, void* k_cache, void* v_cache,
+                                  int64_t cache_stride_b, int64_t cache_stride_s, void* q_out, const int64_t* rows,
+                                  int64_t rows_stride_b, int64_t rows_stride_t, const int64_t* positions,
+                                  int64_t tail_start, int64_t batch, int64_t candidates, int64_t mask_rows,
+                                  int64_t heads, int64_t head_dim, int64_t n_freqs, void* stream);
+
+/*
  * Decode layer for one new token per row: conv step (+SiLU) over the pre-conv qkv, q/k L2
  * norm, gated delta rule step with the state updated in place, and the output-gated
  * RMSNorm. Replaces the StaticCache decode branch of GatedDeltaNet.forward

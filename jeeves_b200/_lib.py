@@ -56,13 +56,20 @@ SIGNATURES: dict[str, list] = {
     "gdn_conv_step": [_p, _p, _i64, _i64, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p],
     "gdn_gated_rmsnorm": [_p, _p, _p, _p, _i64, _i64, _f32, _p],
     "gdn_delta_gates": [_p, _i64, _p, _i64, _p, _i32, _p, _p, _p, _p, _i64, _i64, _p],
+    "gdn_decode_attention": [_p, _i64, _i64, _i64, _p, _i64, _i64, _i64, _p, _i64, _i64, _i64, _p, _i64, _i64, _p,
+                             _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _p, _sz, _p],
+    "gdn_decode_attention_workspace_size": [_i64, _i64, _i64, _i64],
+    "gdn_rotary": [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p],
+    "gdn_rotate_into_cache": [_p, _p, _p, _p, _p, _i64, _i64, _p, _p, _p, _p, _p, _p, _i64, _i64, _p, _p, _i64, _i64,
+                              _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p],
     "gdn_decode_layer": [_p, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                          _f32, _f32, _p],
     "gdn_decode_layer_noalloc": [_p, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                                  _f32, _f32, _p],
 }
 
-RESTYPES = {"gdn_status_string": ctypes.c_char_p, "gdn_chunk_prefill_workspace_size": ctypes.c_size_t}
+RESTYPES = {"gdn_status_string": ctypes.c_char_p, "gdn_chunk_prefill_workspace_size": ctypes.c_size_t,
+            "gdn_decode_attention_workspace_size": ctypes.c_size_t}
 
 _lock = threading.Lock()
 _lib = None

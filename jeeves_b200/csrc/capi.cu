@@ -36,7 +36,7 @@ const char* gdn_status_string(int status) {
         case GDN_ERR_DEVICE_TIMEOUT: return "a bounded device-side wait timed out";
         case GDN_ERR_UNSUPPORTED: return "unsupported configuration";
         case GDN_ERR_SCRATCH: return "request larger than the fixed scratch of the no-allocation entry point";
-        case GDN_ERR_WORKSPACE: return "workspace missing or smaller than gdn_chunk_prefill_workspace_size";
+        case GDN_ERR_WORKSPACE: return "workspace missing or smaller than the call's *_workspace_size";
         default: return "unknown status";
     }
 }
@@ -316,6 +316,84 @@ int gdn_gated_rmsnorm(const void* x, const void* z, const void* w, void* y, int6
     if (!aligned16(x) || !aligned16(z) || !aligned16(y) || !aligned16(w)) return GDN_ERR_ALIGN;
     if (rows > (int64_t)65535 * 65535) return GDN_ERR_SHAPE;
     return launch_gated_rmsnorm(x, z, w, y, rows, (int)dim, eps, as_stream(stream));
+}
+
+size_t gdn_decode_attention_workspace_size(int64_t batch, int64_t kv_heads, int64_t keys, int64_t head_dim) {
+    if (batch < 0 || kv_heads <= 0 || keys < 0 || (head_dim != 128 && head_dim != 256)) return 0;
+    return decode_attention_workspace_bytes(batch, kv_heads, keys, head_dim);
+}
+
+int gdn_decode_attention(const void* q, int64_t q_stride_b, int64_t q_stride_r, int64_t q_stride_h,
+                         const void* k_cache, int64_t k_stride_b, int64_t k_stride_s, int64_t k_stride_h,
+                         const void* v_cache, int64_t v_stride_b, int64_t v_stride_s, int64_t v_stride_h,
+                         const void* mask, int64_t mask_stride_b, int64_t mask_stride_r, void* o, int64_t batch,
+                         int64_t rows, int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t keys,
+                         int64_t cache_rows, int64_t cache_len, float scale, void* workspace, size_t workspace_bytes,
+                         void* stream) {
+    if (batch < 0 || rows <= 0 || kv_heads <= 0 || heads <= 0 || heads % kv_heads || keys < 0) return GDN_ERR_SHAPE;
+    if (batch > cache_rows || keys > cache_len || batch > 65535 || kv_heads > 65535 || cache_len > INT32_MAX)
+        return GDN_ERR_SHAPE;
+    if (head_dim != 128 && head_dim != 256) return GDN_ERR_UNSUPPORTED;
+    if (rows * (heads / kv_heads) > 64) return GDN_ERR_UNSUPPORTED;  // query rows per key head
+    if (batch == 0) return GDN_OK;
+    if (!q || !o || (keys > 0 && (!k_cache || !v_cache || !mask))) return GDN_ERR_NULL;
+    if (!aligned16(o) || !rows_aligned(q, 2, q_stride_b, q_stride_r, q_stride_h)) return GDN_ERR_ALIGN;
+    if (keys > 0 && (!rows_aligned(k_cache, 2, k_stride_b, k_stride_s, k_stride_h) ||
+                     !rows_aligned(v_cache, 2, v_stride_b, v_stride_s, v_stride_h) ||
+                     !rows_aligned(mask, 2, mask_stride_b, mask_stride_r, 0)))
+        return GDN_ERR_ALIGN;
+    if (workspace && !aligned16(workspace)) return GDN_ERR_ALIGN;
+    AttentionArgs a{};
+    a.q = q; a.qsb = q_stride_b; a.qsr = q_stride_r; a.qsh = q_stride_h;
+    a.k = k_cache; a.ksb = k_stride_b; a.kss = k_stride_s; a.ksh = k_stride_h;
+    a.v = v_cache; a.vsb = v_stride_b; a.vss = v_stride_s; a.vsh = v_stride_h;
+    a.mask = mask; a.msb = mask_stride_b; a.msr = mask_stride_r;
+    a.o = o;
+    a.B = batch; a.R = rows; a.H = heads; a.Hkv = kv_heads; a.D = head_dim; a.L = keys;
+    a.cache_rows = cache_rows; a.cache_len = cache_len;
+    a.scale = scale;
+    a.workspace = workspace;
+    a.workspace_bytes = workspace_bytes;
+    return launch_decode_attention(a, as_stream(stream));
+}
+
+int gdn_rotary(const void* x, const float* cos, const float* sin, void* out, int64_t batch, int64_t seqlen,
+               int64_t heads, int64_t head_dim, int64_t n_freqs, void* stream) {
+    if (batch < 0 || seqlen < 0 || heads <= 0 || head_dim <= 0 || n_freqs < 0) return GDN_ERR_SHAPE;
+    if (2 * n_freqs > head_dim) return GDN_ERR_SHAPE;
+    if (head_dim > 1024) return GDN_ERR_UNSUPPORTED;
+    const int64_t rows = batch * seqlen * heads;
+    if (rows == 0) return GDN_OK;
+    if (!x || !out || (n_freqs > 0 && (!cos || !sin))) return GDN_ERR_NULL;
+    if (rows > INT32_MAX) return GDN_ERR_SHAPE;
+    return launch_rotary(x, cos, sin, out, rows, (int)heads, (int)head_dim, (int)n_freqs, as_stream(stream));
+}
+
+int gdn_rotate_into_cache(const void* k, const void* v, const void* qm, const void* km, const void* vm,
+                          int64_t m_stride_b, int64_t m_stride_t, const float* cos_c, const float* sin_c,
+                          const float* cos_m, const float* sin_m, void* k_cache, void* v_cache, int64_t cache_stride_b,
+                          int64_t cache_stride_s, void* q_out, const int64_t* rows, int64_t rows_stride_b,
+                          int64_t rows_stride_t, const int64_t* positions, int64_t tail_start, int64_t batch,
+                          int64_t candidates, int64_t mask_rows, int64_t heads, int64_t head_dim, int64_t n_freqs,
+                          void* stream) {
+    if (batch < 0 || candidates < 0 || mask_rows < 0 || heads <= 0 || head_dim <= 0 || n_freqs < 0 || tail_start < 0)
+        return GDN_ERR_SHAPE;
+    if (2 * n_freqs > head_dim) return GDN_ERR_SHAPE;
+    if (head_dim > 1024) return GDN_ERR_UNSUPPORTED;
+    const int64_t progs = batch * (candidates + mask_rows) * heads;
+    if (progs == 0) return GDN_OK;
+    if (progs > INT32_MAX || candidates + mask_rows > INT32_MAX) return GDN_ERR_SHAPE;
+    if (!k_cache || !v_cache) return GDN_ERR_NULL;
+    if (candidates > 0 && (!k || !v || !rows || !positions || (n_freqs > 0 && (!cos_c || !sin_c)))) return GDN_ERR_NULL;
+    if (mask_rows > 0 && (!qm || !km || !vm || !q_out || (n_freqs > 0 && (!cos_m || !sin_m)))) return GDN_ERR_NULL;
+    RotateCacheArgs a{};
+    a.k = k; a.v = v; a.qm = qm; a.km = km; a.vm = vm; a.msb = m_stride_b; a.mst = m_stride_t;
+    a.cos_c = cos_c; a.sin_c = sin_c; a.cos_m = cos_m; a.sin_m = sin_m;
+    a.k_cache = k_cache; a.v_cache = v_cache; a.csb = cache_stride_b; a.css = cache_stride_s;
+    a.q_out = q_out; a.rows = rows; a.rsb = rows_stride_b; a.rst = rows_stride_t; a.positions = positions;
+    a.tail_start = tail_start;
+    a.B = batch; a.K = (int)candidates; a.M = (int)mask_rows; a.H = (int)heads; a.D = (int)head_dim; a.nf = (int)n_freqs;
+    return launch_rotate_into_cache(a, as_stream(stream));
 }
 
 int gdn_decode_layer(const void* qkv, int64_t qkv_stride_b, void* conv_state, const void* conv_w, const float* g,

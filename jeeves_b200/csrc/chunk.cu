@@ -41,6 +41,7 @@
 #include "gates.cuh"
 #include "launch.h"
 #include "sm100.cuh"
+#include "tensor_map.h"
 
 namespace gdn {
 
@@ -1085,22 +1086,6 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_fused_kernel(const __gr
 // ---------------------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------------------
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = nullptr;
-    if (!fn) {
-        cudaDriverEntryPointQueryResult q;
-        void* ptr = nullptr;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiledFn>(ptr);
-    }
-    return fn;
-}
-
 // 4-D map over [B, T, heads, 128] bf16 with element strides (sb, st, sh); box (64, 1, 64, 1).
 static bool make_map(CUtensorMap* map, const void* base, int64_t B, int64_t T, int64_t heads, int64_t sb, int64_t st,
                      int64_t sh) {

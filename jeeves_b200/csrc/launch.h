@@ -100,6 +100,53 @@ int launch_conv_step(const void* state, const void* qkv, int64_t sqb, int64_t sq
 int launch_delta_gates(const void* b, int64_t sb, const void* a, int64_t sa, const void* dt_bias, int dt_f32,
                        const float* rate, const uint8_t* valid, void* beta, float* g, int64_t rows, int HV,
                        cudaStream_t s);
+// Decode attention over a KV cache (attention.cu). q: [B, R, H, D]; caches [cache_rows,
+// cache_len, Hkv, D]; mask [B, 1, R, L] bf16 additive; o [B, R, H, D] contiguous.
+struct AttentionArgs {
+    const void* q;
+    int64_t qsb, qsr, qsh;
+    const void* k;
+    int64_t ksb, kss, ksh;
+    const void* v;
+    int64_t vsb, vss, vsh;
+    const void* mask;
+    int64_t msb, msr;
+    void* o;
+    int64_t B, R, H, Hkv, D, L, cache_rows, cache_len;
+    float scale;
+    void* workspace;
+    size_t workspace_bytes;
+};
+int launch_decode_attention(const AttentionArgs& a, cudaStream_t s);
+size_t decode_attention_workspace_bytes(int64_t B, int64_t Hkv, int64_t L, int64_t D);
+
+// Rotary embedding with per-row cos / sin, and the drafter's rotate-into-cache (rotary.cu).
+int launch_rotary(const void* x, const float* cs, const float* sn, void* out, int64_t rows, int H, int D, int nf,
+                  cudaStream_t s);
+struct RotateCacheArgs {
+    const void* k;   // [B, K, H, D] contiguous
+    const void* v;
+    const void* qm;  // [B, M, H, D] with element strides (msb, mst); heads contiguous
+    const void* km;
+    const void* vm;
+    int64_t msb, mst;
+    const float* cos_c;  // [B, K, F] fp32 contiguous
+    const float* sin_c;
+    const float* cos_m;  // [B, M, F]
+    const float* sin_m;
+    void* k_cache;  // element strides (csb, css); [.., H, D] contiguous
+    void* v_cache;
+    int64_t csb, css;
+    void* q_out;             // [B, M, H, D] contiguous
+    const int64_t* rows;     // [B, K] with element strides (rsb, rst)
+    int64_t rsb, rst;
+    const int64_t* positions;  // [B, K] contiguous
+    int64_t tail_start;
+    int64_t B;
+    int K, M, H, D, nf;
+};
+int launch_rotate_into_cache(const RotateCacheArgs& a, cudaStream_t s);
+
 int launch_gated_rmsnorm(const void* x, const void* z, const void* w, void* y, int64_t rows, int dim, float eps,
                          cudaStream_t s);
 

@@ -7,3 +7,5 @@
 #include "chunk.cu"
 #include "noalloc.cu"
 #include "gates.cu"
+#include "attention.cu"
+#include "rotary.cu"

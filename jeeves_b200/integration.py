@@ -15,17 +15,24 @@ from __future__ import annotations
 
 from types import ModuleType
 
+import torch
+
 from . import fla_inplace as _fla_inplace
 from .conv import causal_conv1d as _conv1d
 from .conv import causal_conv1d_step as _conv1d_step
 from .conv import conv_step as _conv_step
 from .gated_delta import gated_delta_rule_chunk, gated_delta_rule_step
+from .attention import decode_attention as _decode_attention
+from .attention import decode_attention_supported as _attention_supported
+from .attention import rotary as _rotary
+from .attention import rotate_into_cache as _rotate_into_cache
 from .gates import delta_gates as _delta_gates
 from .norm import gated_rms_norm
 
 KERNEL_FAMILIES = ("gdn", "causal_conv1d", "rms_norm_gated")
 IMPORTED_NAMES = ("gated_delta_rule_chunk", "gated_delta_rule_step", "gated_delta_rule_advance_inplace", "conv_step",
-                  "eager_conv_step", "causal_conv1d", "causal_conv1d_step", "delta_gates")
+                  "eager_conv_step", "causal_conv1d", "causal_conv1d_step", "delta_gates", "decode_attention",
+                  "rotate_into_cache", "apply_rotary")
 
 
 def fla_chunk_gated_delta_rule(q, k, v, g=None, beta=None, scale=None, initial_state=None, output_final_state=False,
@@ -146,6 +153,38 @@ def install(model_module: ModuleType, *importers: ModuleType) -> Installed:
             return gates_dispatch(b, a, dt_bias, log_decay_rate, valid)
 
         handle.set(m, "delta_gates", delta_gates)
+    # The drafter's attention-side dispatchers (model/model.py:182, :342, :354), under the "gdn"
+    # family: the supported CUDA cases run here, everything else keeps the reference's path.
+    if hasattr(m, "decode_attention"):
+        attention_dispatch = m.decode_attention
+
+        def decode_attention(q, k_cache, v_cache, mask, scale):
+            if m._on("gdn", q) and _attention_supported(q, k_cache, v_cache, mask):
+                return _decode_attention(q, k_cache, v_cache, mask, scale)
+            return attention_dispatch(q, k_cache, v_cache, mask, scale)
+
+        handle.set(m, "decode_attention", decode_attention)
+    if hasattr(m, "rotate_into_cache"):
+        rotate_dispatch = m.rotate_into_cache
+
+        def rotate_into_cache(k, v, qm, km, vm, cos_c, sin_c, cos_m, sin_m, k_cache, v_cache, rows, positions,
+                              tail_start):
+            if m._on("gdn", k) and k.dtype == k_cache.dtype == torch.bfloat16:
+                return _rotate_into_cache(k, v, qm, km, vm, cos_c, sin_c, cos_m, sin_m, k_cache, v_cache, rows,
+                                          positions, tail_start)
+            return rotate_dispatch(k, v, qm, km, vm, cos_c, sin_c, cos_m, sin_m, k_cache, v_cache, rows, positions,
+                                   tail_start)
+
+        handle.set(m, "rotate_into_cache", rotate_into_cache)
+    if hasattr(m, "apply_rotary"):
+        rotary_dispatch = m.apply_rotary
+
+        def apply_rotary(x, cos, sin):
+            if x.dim() == 4 and cos.dim() == 3 and x.dtype == torch.bfloat16 and m._on("gdn", x):
+                return _rotary(x, cos, sin)
+            return rotary_dispatch(x, cos, sin)
+
+        handle.set(m, "apply_rotary", apply_rotary)
     # Keep the reference's norm module class but let its fla branch reach our kernel: done
     # through _fla_rms_norm_gated above, since GatedRMSNorm.forward calls it under _on.
     for mod in importers:

@@ -27,4 +27,7 @@ from .wrappers import (  # noqa: F401
     conv_step,
     gated_rms_norm,
     delta_gates,
+    apply_rotary,
+    rotate_into_cache,
+    decode_attention_f32,
 )

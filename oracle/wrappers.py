@@ -94,3 +94,43 @@ def delta_gates(b, a, dt_bias, log_decay_rate, valid=None):
         return beta, g
     kept = valid[..., None]
     return beta * kept.to(beta.dtype), g * kept.float()
+
+
+def apply_rotary(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """Rotary embedding on bf16 with per-row cos / sin ``[B, T, F]`` (``model/model.py:188-196``,
+    ``_rotate_half`` ``:177-179``): cos and sin rounded to x's dtype, every product and the sum
+    rounded to x's dtype, the elements past 2F copied."""
+    cos, sin = cos.to(x.dtype), sin.to(x.dtype)
+    rd = 2 * cos.shape[-1]
+    cos = torch.cat((cos, cos), dim=-1).unsqueeze(-2)
+    sin = torch.cat((sin, sin), dim=-1).unsqueeze(-2)
+    x_rot, x_pass = x[..., :rd], x[..., rd:]
+    x1, x2 = x_rot.chunk(2, dim=-1)
+    turned = torch.cat((-x2, x1), dim=-1)
+    return torch.cat((x_rot * cos + turned * sin, x_pass), dim=-1)
+
+
+def rotate_into_cache(k, v, qm, km, vm, cos_c, sin_c, cos_m, sin_m, k_cache, v_cache, rows, positions, tail_start):
+    """The drafter's cache writes (``model/model.py:342-351``), in place on the caches; returns
+    the rotated mask-row queries."""
+    k_cache[rows, positions] = apply_rotary(k, cos_c, sin_c)
+    v_cache[rows, positions] = v
+    B, M = qm.shape[:2]
+    q = apply_rotary(qm, cos_m, sin_m)
+    k_cache[:B, tail_start:tail_start + M] = apply_rotary(km, cos_m, sin_m)
+    v_cache[:B, tail_start:tail_start + M] = vm
+    return q
+
+
+def decode_attention_f32(q, k_cache, v_cache, mask, scale):
+    """Attention of q ``[B, R, H, D]`` over the first ``L`` keys of the caches ``[rows, slots, Hkv, D]``
+    with the additive mask ``[B, 1, R, L]``, in fp32 (the float32 reference that
+    ``model/triton_kernels_test.py:122-126`` holds ``decode_attention``, ``model/model.py:354-361``,
+    to). Key head ``h // (H // Hkv)``; a row with every key masked gets zeros."""
+    B, R, H, D = q.shape
+    L = mask.shape[-1]
+    G = H // k_cache.shape[2]
+    keys, values = (t[:B, :L].float().repeat_interleave(G, dim=2) for t in (k_cache, v_cache))
+    scores = torch.einsum("brhd,blhd->bhrl", q.float(), keys) * scale + mask.float()
+    probs = torch.softmax(scores, dim=-1).nan_to_num(0.0)
+    return torch.einsum("bhrl,blhd->brhd", probs, values)

@@ -127,6 +127,50 @@ def main() -> None:
     beta, gg = ref.delta_gates(b, a, dt_bias, rate, valid)
     out["delta_gates"] = dict(b=b, a=a, dt_bias=dt_bias, rate=rate, valid=valid, beta=beta, g=gg)
 
+    # Rotary with per-row positions (3-D cos / sin), one NaN to propagate.
+    gen = seeded(19)
+    x = torch.randn(2, 5, 4, 128, generator=gen).to(torch.bfloat16)
+    x[0, 1, 2, 7] = float("nan")
+    pos = (torch.arange(5)[None] + torch.randint(0, 8000, (2, 1), generator=gen)).float()[..., None]
+    freqs = pos * torch.logspace(0, -7, 32)
+    cos, sin = freqs.cos(), freqs.sin()
+    out["rotary"] = dict(x=x, cos=cos, sin=sin, y=ref.apply_rotary(x, cos, sin))
+
+    # The drafter's cache writes: K candidate rows to shuffled cache rows, M mask rows to the tail.
+    gen = seeded(20)
+    B, K, M, H, D, nf, tail = 2, 3, 6, 4, 128, 32, 40
+    k = torch.randn(B, K, H, D, generator=gen).to(torch.bfloat16)
+    v = torch.randn(B, K, H, D, generator=gen).to(torch.bfloat16)
+    merged = torch.randn(B, M, 3 * H * D + 8, generator=gen).to(torch.bfloat16)
+    qm, km, vm = (merged[..., i * H * D:(i + 1) * H * D].view(B, M, H, D) for i in range(3))
+    f = torch.rand(B, K + M, 1, generator=gen) * 4000 * torch.logspace(0, -7, nf)
+    cos, sin = f.cos(), f.sin()
+    rows = torch.tensor([[2], [0]]).expand(B, K)
+    positions = torch.randint(0, tail - K, (B, 1), generator=gen) + torch.arange(K)[None]
+    k_cache = torch.randn(4, 64, H, D, generator=gen).to(torch.bfloat16)
+    v_cache = torch.randn(4, 64, H, D, generator=gen).to(torch.bfloat16)
+    kc, vc = k_cache.clone(), v_cache.clone()
+    q_out = ref.rotate_into_cache(k, v, qm, km, vm, cos[:, :K], sin[:, :K], cos[:, K:], sin[:, K:], kc, vc, rows,
+                                  positions, tail)
+    out["rotate_into_cache"] = dict(k=k, v=v, merged=merged, cos=cos, sin=sin, rows=rows.contiguous(),
+                                    positions=positions, k_cache=k_cache, v_cache=v_cache, tail=tail, K=K, M=M,
+                                    q_out=q_out, k_cache_after=kc, v_cache_after=vc)
+
+    # Decode attention (grouped heads, masked slices, one fully masked row) with the fp32
+    # reference of model/triton_kernels_test.py:122-126 stored beside it.
+    gen = seeded(21)
+    B, R, H, Hkv, D, L = 2, 6, 8, 2, 128, 280
+    q = torch.randn(B, R, H, D, generator=gen).to(torch.bfloat16)
+    k_cache = torch.randn(3, 300, Hkv, D, generator=gen).to(torch.bfloat16)
+    v_cache = torch.randn(3, 300, Hkv, D, generator=gen).to(torch.bfloat16)
+    allowed = torch.rand(B, 1, R, L, generator=gen) < 0.6
+    allowed[0, 0, 2] = False
+    mask = torch.full((B, 1, R, L + 8), float("-inf"), dtype=torch.bfloat16)[..., :L].masked_fill_(allowed, 0.0)
+    keys, values = (t[:B, :L].float().repeat_interleave(H // Hkv, dim=2) for t in (k_cache, v_cache))
+    scores = torch.einsum("brhd,blhd->bhrl", q.float(), keys) * D ** -0.5 + mask.float()
+    f32 = torch.einsum("bhrl,blhd->brhd", scores.softmax(-1).nan_to_num(0.0), values)
+    out["decode_attention"] = dict(q=q, k_cache=k_cache, v_cache=v_cache, mask=mask, scale=D ** -0.5, o_f32=f32)
+
     for name, case in out.items():
         torch.save(case, os.path.join(HERE, f"{name}.pt"))
         print(name, {k: tuple(v.shape) if torch.is_tensor(v) else v for k, v in case.items()})

@@ -125,3 +125,23 @@ def test_gate_entry_points_check_their_inputs():
     assert chunk(ctypes.byref(no_a), 16) == _lib.ERR_NULL
     assert chunk(ctypes.byref(bad_dt), 16) == _lib.ERR_DTYPE
     assert chunk(ctypes.byref(good), None) == _lib.ERR_WORKSPACE
+
+
+def test_attention_entry_points_check_their_inputs():
+    lib = _lib.load()
+    s3 = [128 * 4, 128 * 4, 128]
+    args = lambda **kw: [kw.get("q", 16), *s3, 16, *s3, 16, *s3, kw.get("mask", 16), 64, 64, 16,  # noqa: E731
+                         kw.get("B", 1), kw.get("R", 4), kw.get("H", 4), kw.get("Hkv", 4), kw.get("D", 128),
+                         kw.get("L", 64), 1, 64, 0.1, None, 0, None]
+    assert lib.gdn_decode_attention(*args(D=64)) == _lib.ERR_UNSUPPORTED
+    assert lib.gdn_decode_attention(*args(R=65)) == _lib.ERR_UNSUPPORTED
+    assert lib.gdn_decode_attention(*args(H=6)) == _lib.ERR_SHAPE
+    assert lib.gdn_decode_attention(*args(L=65)) == _lib.ERR_SHAPE  # more keys than the cache holds
+    assert lib.gdn_decode_attention(*args(mask=None)) == _lib.ERR_NULL
+    assert lib.gdn_decode_attention(*args(q=24)) == _lib.ERR_ALIGN
+    assert lib.gdn_decode_attention_workspace_size(2, 4, 128, 128) == 0  # one split
+    assert lib.gdn_decode_attention_workspace_size(2, 4, 300, 128) == 2 * 4 * 3 * 64 * 129 * 4
+    assert lib.gdn_rotary(16, 16, 16, 16, 1, 1, 1, 128, 65, None) == _lib.ERR_SHAPE
+    assert lib.gdn_rotary(None, 16, 16, 16, 1, 1, 1, 128, 32, None) == _lib.ERR_NULL
+    assert lib.gdn_rotate_into_cache(16, 16, 16, 16, 16, 0, 0, 16, 16, 16, 16, None, 16, 0, 0, 16, 16, 0, 0, 16, 0,
+                                     1, 1, 1, 1, 128, 32, None) == _lib.ERR_NULL

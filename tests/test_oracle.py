@@ -3,6 +3,7 @@
 import torch
 
 import oracle
+from tests.helpers import same_bits
 
 
 def rel(a, b):
@@ -116,3 +117,27 @@ def test_delta_gates_match_reference(golden):
     c = golden("delta_gates")
     beta, g = oracle.delta_gates(c["b"], c["a"], c["dt_bias"], c["rate"], c["valid"])
     assert torch.equal(beta, c["beta"]) and torch.equal(g, c["g"])
+
+
+def test_rotary_matches_reference(golden):
+    c = golden("rotary")
+    assert same_bits(oracle.apply_rotary(c["x"], c["cos"], c["sin"]), c["y"])
+
+
+def test_rotate_into_cache_matches_reference(golden):
+    c = golden("rotate_into_cache")
+    K, H, D = c["K"], c["k"].shape[2], c["k"].shape[3]
+    B, M = c["merged"].shape[:2]
+    qm, km, vm = (c["merged"][..., i * H * D:(i + 1) * H * D].view(B, M, H, D) for i in range(3))
+    kc, vc = c["k_cache"].clone(), c["v_cache"].clone()
+    cos, sin = c["cos"], c["sin"]
+    q = oracle.rotate_into_cache(c["k"], c["v"], qm, km, vm, cos[:, :K], sin[:, :K], cos[:, K:], sin[:, K:], kc, vc,
+                                 c["rows"], c["positions"], c["tail"])
+    assert same_bits(q, c["q_out"]) and same_bits(kc, c["k_cache_after"]) and same_bits(vc, c["v_cache_after"])
+
+
+def test_decode_attention_f32_matches_reference_formula(golden):
+    c = golden("decode_attention")
+    o = oracle.decode_attention_f32(c["q"], c["k_cache"], c["v_cache"], c["mask"], c["scale"])
+    assert torch.allclose(o, c["o_f32"], atol=1e-6, rtol=0)
+    assert torch.equal(o[0, 2], torch.zeros_like(o[0, 2]))  # a fully masked row gives zeros
