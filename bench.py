@@ -1,7 +1,7 @@
 """Benchmark of the gated-delta hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--no-extras] [--no-cpu-baseline]
-    python bench.py --profile prefill|varlen|decode|verify     (one untimed run of a case, for ncu)
+    python bench.py --profile prefill|varlen|decode|verify|attention   (one untimed run of a case, for ncu)
 
 Workloads (synthetic inputs with the benchmark configs' shapes and distributions; no
 dataset or checkpoint is involved):
@@ -17,6 +17,8 @@ dataset or checkpoint is involved):
   through the fused decode layer of all 24 layers.
 * ``verify`` (config 4): 128 sequences score 5 tokens through 24 layers writing the 5
   per-token fp32 states, then roll back to an accepted length U{1..5}.
+* ``attention`` (the drafter side of a delta layer, not a BASELINE config): the mask-row
+  attention of one decode cycle, 32 sequences x 12 mask rows x 32 heads over 4,108 cached keys.
 
 Multi-GPU (torchrun, one process per GPU): every rank runs its own shard with no
 collective on the data path (prefill: an independent replica per GPU; decode/verify:
@@ -330,6 +332,7 @@ def run_ours(args, rank, world, device, rank_sync, reduce_max):
         extra["varlen"]["roofline"]["traffic"] = traffic.get("varlen", {}).get("dram_bytes_per_launch")
         extra["decode"] = bench_decode(gdn, args, device, rank, world, rank_sync, reduce_max, hbm_peak)
         extra["verify"] = bench_verify(gdn, args, device, rank, world, rank_sync, reduce_max, hbm_peak)
+        extra["attention"] = bench_attention(gdn, args, device, rank, world, rank_sync, reduce_max, hbm_peak)
         result["extra"] = extra
         result["gpu_launches"] += sum(e.get("gpu_launches", 0) for e in extra.values())
     clocks.__exit__(None, None, None)
@@ -408,6 +411,48 @@ def bench_decode(gdn, args, device, rank, world, rank_sync, reduce_max, hbm_peak
             "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(ach / hbm_peak, 4), "algorithmic_bytes_per_unit": unit_bytes},
             "gpu_launches": 3 * layers * args.steps}
+
+
+def attention_case(B, device, K=4, Hq=HV, Hkv=HV, Dh=D, Lw=4096, seed=5):
+    """The drafter's mask-row attention of one decode cycle over a delta layer's key cache
+    (inference/engine.py:436-437): B sequences, M = K (K - 1) mask rows, Lw cached keys plus the
+    M tail keys; every row sees the cache up to its own limit and its block's tail keys."""
+    gen = torch.Generator().manual_seed(seed)
+    M = K * (K - 1)
+    L = Lw + M
+    q = torch.randn(B, M, Hq, Dh, generator=gen).to(torch.bfloat16).to(device)
+    k_cache = torch.randn(B, L, Hkv, Dh, generator=gen).to(torch.bfloat16).to(device)
+    v_cache = torch.randn(B, L, Hkv, Dh, generator=gen).to(torch.bfloat16).to(device)
+    block = torch.arange(K).repeat_interleave(K - 1)
+    n = torch.randint(Lw // 2, Lw - K, (B,), generator=gen)
+    allow_cache = torch.arange(Lw)[None, None] <= (n[:, None] + block[None])[..., None]
+    allow_tail = (block[:, None] == block[None, :])[None].expand(B, -1, -1)
+    allowed = torch.cat((allow_cache, allow_tail), dim=2)[:, None]
+    padded = torch.full((B, 1, M, L + 16 - L % 16), float("-inf"), dtype=torch.bfloat16)
+    padded[..., :L].masked_fill_(allowed, 0.0)
+    mask = padded.to(device)[..., :L]
+    return q, k_cache, v_cache, mask
+
+
+def bench_attention(gdn, args, device, rank, world, rank_sync, reduce_max, hbm_peak, B_total=32):
+    B, _ = shard(B_total, rank, world)
+    q, k_cache, v_cache, mask = attention_case(B, device)
+    M, L = q.shape[1], mask.shape[-1]
+    scale = D ** -0.5
+
+    def step(i):
+        gdn.decode_attention(q, k_cache, v_cache, mask, scale)
+
+    ms = reduce_max(timed(step, args.steps, args.warmup, rank_sync)) / args.steps
+    bytes_ = B * L * HV * D * 2 * 2 + q.numel() * 2 * 2 + B * M * L * 2  # K, V; q and o; mask
+    ach = bytes_ / (ms / 1e3) / 1e9
+    splits = -(-L // 128)
+    return {"workload": f"drafter mask-row attention over a delta layer's key cache: {B_total} sequences x {M} mask rows x "
+                        f"{HV} heads, d=128, {L} cached keys, bf16, additive mask; {B} sequences per GPU",
+            "value": round(world * B * M / (ms / 1e3), 1), "unit": "query rows/s", "ms_per_step": round(ms, 4),
+            "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(ach / hbm_peak, 4), "algorithmic_bytes": bytes_},
+            "gpu_launches": (2 if splits > 1 else 1) * args.steps}
 
 
 def bench_verify(gdn, args, device, rank, world, rank_sync, reduce_max, hbm_peak, layers=24, B_total=128, T=5):
@@ -525,6 +570,10 @@ def profile_case(name, device):
         nw = torch.ones(D, device=device, dtype=torch.bfloat16)
         for _ in range(2):
             gdn.decode_layer_step(qkv, cs, w, g, beta, state, z, nw, H)
+    elif name == "attention":
+        q, k_cache, v_cache, mask = attention_case(32, device)
+        for _ in range(2):
+            gdn.decode_attention(q, k_cache, v_cache, mask, D ** -0.5)
     elif name == "verify":
         B, T = 128, 5
         state = torch.randn(B, HV, D, D, device=device) * 0.02
@@ -550,7 +599,7 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-extras", dest="extras", action="store_false")
     ap.add_argument("--no-cpu-baseline", dest="cpu", action="store_false")
-    ap.add_argument("--profile", choices=("prefill", "varlen", "decode", "verify"),
+    ap.add_argument("--profile", choices=("prefill", "varlen", "decode", "verify", "attention"),
                     help="run one workload twice, untimed, for an ncu capture")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)

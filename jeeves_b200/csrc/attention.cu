@@ -4,20 +4,22 @@
 // the attention layers' candidate + mask rows (G = 4, D = 256).
 //
 // o[b, r, h] = softmax_n(scale * q[b, r, h] . k[b, n, h / G] + mask[b, 0, r, n]) v[b, n, h / G]
-// over keys n < L. One CTA per (batch row, key head, split of NK keys): the query rows of the key
-// head (R * G <= 64, row rq = r * G + g, padded to 64), the split's keys and values are loaded
-// whole with TMA (128-byte swizzle, 64-element d-panels), so the softmax of the split is exact
-// (no running rescale):
+// over keys n < L. One CTA per (batch row, key head, range of key blocks); with at least as many
+// (batch row, key head) pairs as SMs there is one range, else the keys are split so that every SM
+// gets work. The query rows of the key head (R * G <= 64, row rq = r * G + g, padded to 64) stay in
+// shared memory; key blocks of NK keys stream through two K / V stages with TMA (128-byte swizzle,
+// 64-element d-panels), block j + 2 loading while block j + 1 is computed:
 //   S = Q K^T   two M=64 accumulators (keys 0..NK/2-1 at TMEM lane offset 0, the rest at +16),
 //               so that each of the 4 warps reads 16 rows x 2 key halves;
-//   P = exp2(S * scale * log2 e + mask * log2 e - m), m the row max over the split (0 when every
-//       key of the row is masked), stored as bf16 (the operand of the next product), l = sum of
-//       the fp32 values;
-//   O = P V     one M=64 accumulator per 64-wide d-panel (panels 2j and 2j + 1 share columns at
-//               lane offsets 0 and +16).
-// With one split the CTA writes o = O / l in bf16 (0 for a row with every key masked); otherwise
+//   online softmax per row: m' = max(m, max_n s), p = exp2(s - m') with s = S scale log2 e +
+//       mask log2 e (m' = -inf shifts by 0 so that p = 0), alpha = exp2(m - m'), l' = l alpha +
+//       sum p; p goes to shared memory in bf16 as the operand of the next product;
+//   O_blk = P V one M=64 accumulator per 64-wide d-panel (panels 2j and 2j + 1 share columns at
+//               lane offsets 0 and +16); each thread keeps its row's O = O alpha + O_blk in
+//               registers.
+// With one range the CTA writes o = O / l in bf16 (0 for a row with every key masked); otherwise
 // it writes O / l and lse = m + log2 l (or -inf) in fp32 and decode_attention_combine_kernel
-// weights the splits by exp2(lse - max lse), as the reference's second kernel does.
+// weights the ranges by exp2(lse - max lse), as the reference's second kernel does.
 
 #include <cstring>
 
@@ -37,20 +39,21 @@ constexpr float kLog2e = 1.4426950408889634f;
 
 template <int D>
 struct Tile {
-    static constexpr int NK = D == 128 ? 128 : 64;                   // keys per split
+    static constexpr int NK = 64;                                    // keys per block
     static constexpr int DP = D / 64;                                // d-panels
     static constexpr uint32_t Q = 0;                                 // DP panels of 64 rows
     static constexpr uint32_t QPanel = kRows * kPanelRow;            // 8 KB
-    static constexpr uint32_t K = Q + DP * QPanel;                   // DP panels of NK rows
     static constexpr uint32_t KPanel = NK * kPanelRow;
-    static constexpr uint32_t V = K + DP * KPanel;
-    static constexpr uint32_t P = V + DP * KPanel;                   // NK / 64 panels of 64 rows
+    static constexpr uint32_t KV = Q + DP * QPanel;                  // two stages of K then V panels
+    static constexpr uint32_t Stage = 2 * DP * KPanel;               // 64 KB
+    static constexpr uint32_t P = KV + 2 * Stage;                    // NK / 64 panels of 64 rows
     static constexpr uint32_t END = P + (NK / 64) * QPanel;
     static constexpr uint32_t BYTES = END + 1024;                    // + alignment slack
-    static constexpr uint32_t COL_S = 0;                             // NK / 2 columns
-    static constexpr uint32_t COL_O = 64;                            // D / 2 columns
-    static constexpr uint32_t TMEM_COLS = COL_O + D / 2 <= 128 ? 128 : 256;
-    static_assert(NK % 64 == 0 && NK / 2 <= COL_O, "keys per split");
+    static constexpr uint32_t COL_S = 0;                             // NK columns
+    static constexpr uint32_t COL_O = 64;                            // 128 columns
+    static constexpr uint32_t TMEM_COLS = 256;
+    static_assert(NK == 64 && NK <= COL_O, "keys per block");
+    static_assert(D != 128 || 2 * BYTES <= 227 * 1024, "two CTAs per SM at D = 128");
 };
 
 struct Params {
@@ -59,15 +62,15 @@ struct Params {
     CUtensorMap tm_v;
     const bf16* mask;  // [B, 1, R, L] additive, element strides (smb, smr), keys contiguous
     int64_t smb, smr;
-    bf16* o;           // [B, R, H, D] contiguous (one split)
-    float* part_o;     // [B * Hkv * splits * 64, D] (several splits)
+    bf16* o;           // [B, R, H, D] contiguous (one range)
+    float* part_o;     // [B * Hkv * splits * 64, D] (several ranges)
     float* part_lse;   // [B * Hkv * splits * 64]
-    int R, G, Hkv, L, splits;
+    int R, G, Hkv, L, splits, blocks_per_split;
     float scale_log2e;
 };
 
 struct Shared {
-    uint64_t tma, s_done, o_done;
+    uint64_t qbar, full[2], s_done, o_done;
     uint32_t tmem_base;
 };
 
@@ -87,17 +90,21 @@ __device__ __forceinline__ void put_chunk8(uint8_t* panel, uint32_t row, uint32_
 template <int D>
 __global__ void __launch_bounds__(128) decode_attention_kernel(const __grid_constant__ Params p) {
     using TL = Tile<D>;
-    constexpr int NK = TL::NK, DP = TL::DP, NH = NK / 2;
+    constexpr int NK = TL::NK, DP = TL::DP;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = align1024(smem_raw);
     __shared__ Shared sh;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
-    const int n0 = split * NK;
     const int rows = p.R * p.G;
+    const int blocks_total = (p.L + NK - 1) / NK;
+    const int j0 = split * p.blocks_per_split;
+    const int nb = min(p.blocks_per_split, blocks_total - j0);  // key blocks of this CTA (>= 1)
 
     if (tid == 0) {
-        mbar_init(&sh.tma, 1);
+        mbar_init(&sh.qbar, 1);
+        mbar_init(&sh.full[0], 1);
+        mbar_init(&sh.full[1], 1);
         mbar_init(&sh.s_done, 1);
         mbar_init(&sh.o_done, 1);
         fence_mbar_init();
@@ -107,10 +114,10 @@ __global__ void __launch_bounds__(128) decode_attention_kernel(const __grid_cons
         tmem_relinquish();
     }
     // query rows past R * G: zeros (TMA writes rows 0 .. R * G - 1 of each panel)
-    for (int i = rows * 8 + tid; i < kRows * 8; i += 128) {
+    for (int c = rows * 8 + tid; c < kRows * 8; c += 128) {
 #pragma unroll
         for (int dp = 0; dp < DP; ++dp)
-            *reinterpret_cast<uint4*>(sm + TL::Q + dp * TL::QPanel + (i >> 3) * kPanelRow + ((i & 7) << 4)) =
+            *reinterpret_cast<uint4*>(sm + TL::Q + dp * TL::QPanel + (c >> 3) * kPanelRow + ((c & 7) << 4)) =
                 make_uint4(0, 0, 0, 0);
     }
     fence_async_smem();
@@ -119,145 +126,183 @@ __global__ void __launch_bounds__(128) decode_attention_kernel(const __grid_cons
     tc_fence_after();
     const uint32_t tb = sh.tmem_base;
 
-    if (tid == 0) {
-        constexpr uint32_t kv_bytes = 2u * DP * NK * kPanelRow;
-        mbar_arrive_expect_tx(&sh.tma, (uint32_t)(DP * rows) * kPanelRow + kv_bytes);
+    auto load_block = [&](int j) {  // thread 0: keys and values of block j0 + j into stage j & 1
+        uint8_t* st = sm + TL::KV + (j & 1) * TL::Stage;
+        const int n0 = (j0 + j) * NK;
+        mbar_arrive_expect_tx(&sh.full[j & 1], TL::Stage);
 #pragma unroll
         for (int dp = 0; dp < DP; ++dp) {
-            tma_load_4d(sm + TL::Q + dp * TL::QPanel, &p.tm_q, &sh.tma, 64 * dp, kvh * p.G, 0, b);
-            tma_load_4d(sm + TL::K + dp * TL::KPanel, &p.tm_k, &sh.tma, 64 * dp, kvh, n0, b);
-            tma_load_4d(sm + TL::V + dp * TL::KPanel, &p.tm_v, &sh.tma, 64 * dp, kvh, n0, b);
+            tma_load_4d(st + dp * TL::KPanel, &p.tm_k, &sh.full[j & 1], 64 * dp, kvh, n0, b);
+            tma_load_4d(st + (DP + dp) * TL::KPanel, &p.tm_v, &sh.full[j & 1], 64 * dp, kvh, n0, b);
         }
-    }
-    bool ok = mbar_wait(&sh.tma, 0, kSiteTmaLoad);
-    bool s_issued = false, o_issued = false;  // (thread 0) products to drain if a wait gives up
-    if (tid == 0 && ok) {
-        // S = Q K^T: keys 0 .. NH - 1 into lane offset 0, NH .. NK - 1 into lane offset 16
-        tc_fence_after();
-        const uint32_t id_s = make_idesc(kRows, NH, kFmtBF16, false, false);
-        const uint64_t dq = sdesc_kmajor(sm + TL::Q, 0), dk = sdesc_kmajor(sm + TL::K, 0);
+    };
+    int loaded = 0;  // (thread 0) blocks whose copies were issued
+    if (tid == 0) {
+        mbar_arrive_expect_tx(&sh.qbar, (uint32_t)(DP * rows) * kPanelRow);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t qo = (kk >> 2) * TL::QPanel + (kk & 3) * 32;
-            const uint32_t ko = (kk >> 2) * TL::KPanel + (kk & 3) * 32;
-            mma_f16(tb + TL::COL_S, sdesc_add(dq, qo), sdesc_add(dk, ko), id_s, kk > 0);
-            mma_f16(tb + TL::COL_S + (16u << 16), sdesc_add(dq, qo), sdesc_add(dk, ko + NH * kPanelRow), id_s, kk > 0);
-        }
-        mma_commit(&sh.s_done);
-        s_issued = true;
+        for (int dp = 0; dp < DP; ++dp)
+            tma_load_4d(sm + TL::Q + dp * TL::QPanel, &p.tm_q, &sh.qbar, 64 * dp, kvh * p.G, 0, b);
+        for (; loaded < 2 && loaded < nb; ++loaded) load_block(loaded);
     }
-    // ---- softmax of this thread's row half: row i = 16 warp + lane % 16, keys of half lane / 16
-    const int i = 16 * warp + (lane & 15), half = lane >> 4;
+
+    // S (M=64, N=64) and O (M=64, N=128: d 0..127 at lane offset 0, d 128..255 at +16): row i of
+    // an M=64 accumulator sits in lane i % 16 of quarter i / 16, so lanes 0-15 of each warp hold
+    // the softmax rows, and at D = 256 lanes 16-31 hold the second half of O.
+    const uint32_t id_s = make_idesc(kRows, NK, kFmtBF16, false, false);
+    const uint32_t id_o = make_idesc(kRows, 128, kFmtBF16, false, true);
+    const int i = 16 * warp + (lane & 15);
+    const bool owner = lane < 16;                   // holds row i of S
     const bool row_ok = i < rows;
+    const bool holds_o = D == 256 || owner;         // holds 128 values of O
     const int r = row_ok ? i / p.G : 0;
-    ok = __all_sync(0xffffffffu, ok) && mbar_wait(&sh.s_done, 0, kSiteMma);
-    float m = -INFINITY, l = 0.f;
-    if (__all_sync(0xffffffffu, ok)) {
-        tc_fence_after();
-        float s[NH];
-        if constexpr (NH == 64) {
-            tmem_ld64_wait(tb + TL::COL_S + ((uint32_t)(32 * warp) << 16), s);
-        } else {
-            tmem_ld32_wait(tb + TL::COL_S + ((uint32_t)(32 * warp) << 16), s);
-        }
-        const int nb = n0 + half * NH;
-        const bf16* mrow = p.mask + (int64_t)b * p.smb + (int64_t)r * p.smr + nb;
+    const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
+    const bf16* mrow = p.mask + (int64_t)b * p.smb + (int64_t)r * p.smr;
+    float m = -INFINITY, l = 0.f;  // valid in the owner lanes
+    float acc[128];
 #pragma unroll
-        for (int c = 0; c < NH / 8; ++c) {
-            float mv[8];
-            if (row_ok && nb + 8 * c + 8 <= p.L) {
-                const uint4 raw = *reinterpret_cast<const uint4*>(mrow + 8 * c);
-                const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+    for (int e = 0; e < 128; ++e) acc[e] = 0.f;
+    bool ok = mbar_wait(&sh.qbar, 0, kSiteTmaLoad);
+    int s_issued = 0, o_issued = 0;  // (thread 0) products issued, for the drain after a failed wait
+
+    for (int j = 0; j < nb && __syncthreads_and(ok); ++j) {
+        const int st = j & 1;
+        const uint8_t* stage = sm + TL::KV + st * TL::Stage;
+        const int n0 = (j0 + j) * NK;
+        if (tid == 0) {
+            ok = mbar_wait(&sh.full[st], (uint32_t)(j >> 1) & 1, kSiteTmaLoad);
+            if (ok) {  // S = Q K^T
+                tc_fence_after();
+                const uint64_t dq = sdesc_kmajor(sm + TL::Q, 0), dk = sdesc_kmajor(stage, 0);
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk)
+                    mma_f16(tb + TL::COL_S, sdesc_add(dq, (kk >> 2) * TL::QPanel + (kk & 3) * 32),
+                            sdesc_add(dk, (kk >> 2) * TL::KPanel + (kk & 3) * 32), id_s, kk > 0);
+                mma_commit(&sh.s_done);
+                ++s_issued;
+            }
+        }
+        // the mask of this row's keys (bf16, kept packed), loaded while the product runs; keys past L
+        // and rows past R * G read as -inf
+        uint4 mraw[NK / 8];
+        const bool live = owner && row_ok;
+#pragma unroll
+        for (int c = 0; c < NK / 8; ++c) {
+            const int n = n0 + 8 * c;
+            if (live && n + 8 <= p.L) {
+                mraw[c] = *reinterpret_cast<const uint4*>(mrow + n);
+            } else {
+                __nv_bfloat162 h2[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const bf16 lo = (live && n + 2 * e < p.L) ? mrow[n + 2 * e] : __float2bfloat16_rn(-INFINITY);
+                    const bf16 hi = (live && n + 2 * e + 1 < p.L) ? mrow[n + 2 * e + 1] : __float2bfloat16_rn(-INFINITY);
+                    h2[e] = __halves2bfloat162(lo, hi);
+                }
+                mraw[c] = *reinterpret_cast<const uint4*>(h2);
+            }
+        }
+        ok = __syncthreads_and(ok) && mbar_wait(&sh.s_done, (uint32_t)j & 1, kSiteMma);
+        if (!__syncthreads_and(ok)) break;
+        tc_fence_after();
+        float sv[NK];
+        tmem_ld64_wait(tb + TL::COL_S + lane_base, sv);
+        float alpha = 0.f;
+        if (owner) {
+            float mb = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < NK / 8; ++c) {
+                const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&mraw[c]);
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
                     const float2 f = __bfloat1622float2(h2[e]);
-                    mv[2 * e] = f.x;
-                    mv[2 * e + 1] = f.y;
+                    const int k0 = 8 * c + 2 * e;
+                    sv[k0] = sv[k0] * p.scale_log2e + f.x * kLog2e;
+                    sv[k0 + 1] = sv[k0 + 1] * p.scale_log2e + f.y * kLog2e;
+                    mb = fmaxf(mb, fmaxf(sv[k0], sv[k0 + 1]));
                 }
-            } else {
-#pragma unroll
-                for (int e = 0; e < 8; ++e)
-                    mv[e] = (row_ok && nb + 8 * c + e < p.L) ? __bfloat162float(mrow[8 * c + e]) : -INFINITY;
             }
+            const float m_new = fmaxf(m, mb);
+            const float shift = m_new == -INFINITY ? 0.f : m_new;  // a row with every key masked keeps p = 0
+            alpha = exp2f(m - shift);
+            float ls = 0.f;
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                const float x = s[8 * c + e] * p.scale_log2e + mv[e] * kLog2e;
-                s[8 * c + e] = x;
-                m = fmaxf(m, x);
+            for (int e = 0; e < NK; ++e) {
+                sv[e] = exp2f(sv[e] - shift);
+                ls += sv[e];
             }
-        }
-        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 16));
-        const float shift = m == -INFINITY ? 0.f : m;  // a row with every key masked keeps p = 0
+            l = l * alpha + ls;
+            m = m_new;
+            // P (bf16) as the K-major A operand of O_blk = P V: one 64-key panel, row i
 #pragma unroll
-        for (int j = 0; j < NH; ++j) {
-            s[j] = exp2f(s[j] - shift);
-            l += s[j];
+            for (int c = 0; c < NK / 8; ++c) put_chunk8(sm + TL::P, i, c, sv + 8 * c);
         }
-        l += __shfl_xor_sync(0xffffffffu, l, 16);
-        // P (bf16) as the K-major A operand of O = P V: panel of keys (64 per panel), row i
-        uint8_t* ppanel = sm + TL::P + (half * NH / 64) * TL::QPanel;
-        const int chunk0 = (half * NH % 64) / 8;
+        alpha = __shfl_sync(0xffffffffu, alpha, lane & 15);
+        fence_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        if (tid == 0) {  // O_blk = P V
+            tc_fence_after();
+            const uint64_t dpn = sdesc_kmajor(sm + TL::P, 0);
 #pragma unroll
-        for (int c = 0; c < NH / 8; ++c) put_chunk8(ppanel, i, chunk0 + c, s + 8 * c);
+            for (int h = 0; h < DP / 2; ++h) {  // d 128 h .. 128 h + 127 (two V panels)
+                const uint64_t dv = sdesc_mnmajor(stage + (DP + 2 * h) * TL::KPanel, TL::KPanel);
+                const uint32_t dst = tb + TL::COL_O + ((uint32_t)(16 * h) << 16);
+#pragma unroll
+                for (int kk = 0; kk < NK / 16; ++kk)
+                    mma_f16(dst, sdesc_add(dpn, kk * 32), sdesc_add(dv, kk * 2048), id_o, kk > 0);
+            }
+            mma_commit(&sh.o_done);
+            ++o_issued;
+        }
+        ok = mbar_wait(&sh.o_done, (uint32_t)j & 1, kSiteMma);
+        if (!__all_sync(0xffffffffu, ok)) continue;  // the loop condition ends every thread together
+        tc_fence_after();
+        // the stage is free again: block j + 2 streams in while block j + 1 is computed
+        if (tid == 0 && loaded < nb) load_block(loaded++);
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+            float ob[64];
+            tmem_ld64_wait(tb + TL::COL_O + 64 * c + lane_base, ob);
+#pragma unroll
+            for (int e = 0; e < 64; ++e) acc[64 * c + e] = acc[64 * c + e] * alpha + ob[e];
+        }
+        tc_fence_before();
     }
-    fence_async_smem();
-    tc_fence_before();
     ok = __syncthreads_and(ok);
-    if (tid == 0 && ok) {
-        // O = P V: d-panel dp into columns COL_O + 64 (dp / 2), lane offset 16 (dp % 2)
-        tc_fence_after();
-        const uint32_t id_o = make_idesc(kRows, 64, kFmtBF16, false, true);
-        const uint64_t dpn = sdesc_kmajor(sm + TL::P, 0);
-#pragma unroll
-        for (int dp = 0; dp < DP; ++dp) {
-            const uint64_t dv = sdesc_mnmajor(sm + TL::V + dp * TL::KPanel, TL::KPanel);
-            const uint32_t dst = tb + TL::COL_O + 64 * (dp >> 1) + ((uint32_t)(16 * (dp & 1)) << 16);
-#pragma unroll
-            for (int kk = 0; kk < NK / 16; ++kk)
-                mma_f16(dst, sdesc_add(dpn, (kk >> 2) * TL::QPanel + (kk & 3) * 32), sdesc_add(dv, kk * 2048), id_o,
-                        kk > 0);
-        }
-        mma_commit(&sh.o_done);
-        o_issued = true;
-    }
-    ok = ok && mbar_wait(&sh.o_done, 0, kSiteMma);
-    if (__all_sync(0xffffffffu, ok)) {
-        tc_fence_after();
+
+    l = __shfl_sync(0xffffffffu, l, lane & 15);
+    m = __shfl_sync(0xffffffffu, m, lane & 15);
+    if (ok && row_ok && holds_o) {
         const float inv = l > 0.f ? 1.f / l : 0.f;
-        const float lse = l > 0.f ? m + log2f(l) : -INFINITY;
-        const int g = row_ok ? i % p.G : 0;
+        const int g = i % p.G;
+        const int d0 = owner ? 0 : 128;  // this thread's 128 values of O
+        if (p.splits == 1) {
+            bf16* dst = p.o + (((int64_t)b * p.R + r) * (p.Hkv * p.G) + kvh * p.G + g) * D + d0;
 #pragma unroll
-        for (int j = 0; j < DP / 2; ++j) {
-            float o[64];
-            tmem_ld64_wait(tb + TL::COL_O + 64 * j + ((uint32_t)(32 * warp) << 16), o);
-            const int d0 = 64 * (2 * j + half);  // this thread's d-panel
-            if (!row_ok) continue;
-            if (p.splits == 1) {
-                bf16* dst = p.o + (((int64_t)b * p.R + r) * (p.Hkv * p.G) + kvh * p.G + g) * D + d0;
+            for (int c = 0; c < 16; ++c) {
+                uint4 raw;
+                __nv_bfloat162* h2 = reinterpret_cast<__nv_bfloat162*>(&raw);
 #pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    uint4 raw;
-                    __nv_bfloat162* h2 = reinterpret_cast<__nv_bfloat162*>(&raw);
-#pragma unroll
-                    for (int e = 0; e < 4; ++e)
-                        h2[e] = __floats2bfloat162_rn(o[8 * c + 2 * e] * inv, o[8 * c + 2 * e + 1] * inv);
-                    *reinterpret_cast<uint4*>(dst + 8 * c) = raw;
-                }
-            } else {
-                const int64_t slot = (((int64_t)b * p.Hkv + kvh) * p.splits + split) * kRows + i;
-                float* dst = p.part_o + slot * D + d0;
-#pragma unroll
-                for (int c = 0; c < 16; ++c)
-                    *reinterpret_cast<float4*>(dst + 4 * c) =
-                        make_float4(o[4 * c] * inv, o[4 * c + 1] * inv, o[4 * c + 2] * inv, o[4 * c + 3] * inv);
-                if (j == 0 && half == 0) p.part_lse[slot] = lse;
+                for (int e = 0; e < 4; ++e)
+                    h2[e] = __floats2bfloat162_rn(acc[8 * c + 2 * e] * inv, acc[8 * c + 2 * e + 1] * inv);
+                *reinterpret_cast<uint4*>(dst + 8 * c) = raw;
             }
+        } else {
+            const int64_t slot = (((int64_t)b * p.Hkv + kvh) * p.splits + split) * kRows + i;
+            float* dst = p.part_o + slot * D + d0;
+#pragma unroll
+            for (int c = 0; c < 32; ++c)
+                *reinterpret_cast<float4*>(dst + 4 * c) =
+                    make_float4(acc[4 * c] * inv, acc[4 * c + 1] * inv, acc[4 * c + 2] * inv, acc[4 * c + 3] * inv);
+            if (owner) p.part_lse[slot] = l > 0.f ? m + log2f(l) : -INFINITY;
         }
     }
     if (tid == 0) {  // after a failed wait: the copies and products in flight finish before TMEM is freed
-        mbar_wait(&sh.tma, 0, kSiteDrain);
-        if (s_issued) mbar_wait(&sh.s_done, 0, kSiteDrain);
-        if (o_issued) mbar_wait(&sh.o_done, 0, kSiteDrain);
+        mbar_wait(&sh.qbar, 0, kSiteDrain);
+        for (int j = loaded - 2 < 0 ? 0 : loaded - 2; j < loaded; ++j)
+            mbar_wait(&sh.full[j & 1], (uint32_t)(j >> 1) & 1, kSiteDrain);
+        if (s_issued) mbar_wait(&sh.s_done, (uint32_t)(s_issued - 1) & 1, kSiteDrain);
+        if (o_issued) mbar_wait(&sh.o_done, (uint32_t)(o_issued - 1) & 1, kSiteDrain);
     }
     tc_fence_before();
     __syncthreads();
@@ -305,7 +350,34 @@ static bool make_map4(CUtensorMap* map, const void* base, int64_t D, int64_t n1,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-static int keys_per_split(int64_t D) { return D == 128 ? Tile<128>::NK : Tile<256>::NK; }
+static int keys_per_block(int64_t D) { return D == 128 ? Tile<128>::NK : Tile<256>::NK; }
+
+static int sm_count() {
+    static int sms[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+    if (sms[dev] == 0 && cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        sms[dev] = 0;
+    return sms[dev];
+}
+
+// Key blocks per CTA and the number of ranges: one range per (batch row, key head) when those
+// pairs fill the SMs; otherwise each pair's blocks are split so that the CTAs cover every SM.
+struct Ranges {
+    int64_t per, splits;
+};
+static Ranges key_ranges(int64_t B, int64_t Hkv, int64_t L, int64_t D) {
+    const int64_t nk = keys_per_block(D);
+    const int64_t blocks = (L + nk - 1) / nk;
+    const int64_t pairs = B * Hkv, sms = sm_count();
+    Ranges rg{blocks, 1};
+    if (blocks > 0 && pairs > 0 && pairs < sms) {
+        const int64_t want = (sms + pairs - 1) / pairs;
+        rg.per = (blocks + want - 1) / want;
+        rg.splits = (blocks + rg.per - 1) / rg.per;
+    }
+    return rg;
+}
 
 template <int D>
 static int launch(const AttentionArgs& a, cudaStream_t s) {
@@ -333,7 +405,9 @@ static int launch(const AttentionArgs& a, cudaStream_t s) {
     p.G = G;
     p.Hkv = (int)a.Hkv;
     p.L = (int)a.L;
-    p.splits = (int)((a.L + Tile<D>::NK - 1) / Tile<D>::NK);
+    const Ranges rg = key_ranges(a.B, a.Hkv, a.L, D);
+    p.splits = (int)rg.splits;
+    p.blocks_per_split = (int)rg.per;
     p.scale_log2e = a.scale * kLog2e;
     if (p.splits > 1) {
         const int64_t slots = a.B * a.Hkv * p.splits * kRows;
@@ -352,9 +426,9 @@ static int launch(const AttentionArgs& a, cudaStream_t s) {
 }  // namespace attn
 
 size_t decode_attention_workspace_bytes(int64_t B, int64_t Hkv, int64_t L, int64_t D) {
-    const int64_t nk = attn::keys_per_split(D);
-    const int64_t splits = (L + nk - 1) / nk;
-    if (splits <= 1 || B <= 0 || Hkv <= 0) return 0;
+    if (B <= 0 || Hkv <= 0 || L <= 0) return 0;
+    const int64_t splits = attn::key_ranges(B, Hkv, L, D).splits;
+    if (splits <= 1) return 0;
     const int64_t slots = B * Hkv * splits * attn::kRows;
     return (size_t)slots * (size_t)(D + 1) * sizeof(float);
 }

@@ -37,7 +37,9 @@ struct RecurrentParams {
     GateInputs gates;  // beta and g from the raw projections when gates.b is set
 };
 
-template <typename TIn, typename TBeta, int VS, int NT>
+// GATES: beta and g are computed from p.gates (a separate instantiation, so that the plain
+// path keeps its code unchanged).
+template <typename TIn, typename TBeta, int VS, int NT, bool GATES>
 __global__ void __launch_bounds__(NT) recurrent_kernel(const RecurrentParams p) {
     constexpr int COLG = VS / 4;   // threads along one state row
     constexpr int NW = NT / 32;
@@ -93,7 +95,7 @@ __global__ void __launch_bounds__(NT) recurrent_kernel(const RecurrentParams p) 
         const float4 vv = load4(vbase + tok * p.vst + col);
         const int64_t gi = (brow * p.T + tok) * p.HV + hv;
         float decay, bt;
-        if (p.gates.b) {
+        if constexpr (GATES) {
             float gv;
             delta_gate(p.gates, brow * p.T + tok, hv, bt, gv);
             decay = expf(gv);
@@ -195,16 +197,16 @@ __global__ void __launch_bounds__(NT) recurrent_kernel(const RecurrentParams p) 
     }
 }
 
-template <typename TIn, typename TBeta>
+template <typename TIn, typename TBeta, bool GATES = false>
 static int dispatch_recurrent(const RecurrentParams& p, int64_t rows, cudaStream_t s) {
     // Small grids split the value columns finer so that more SMs share the work.
     const int64_t heads = rows * p.HV;
     if (heads >= 2048) {
         dim3 grid(kHeadDim / 32, p.HV, (unsigned)rows);
-        recurrent_kernel<TIn, TBeta, 32, 128><<<grid, 128, 0, s>>>(p);
+        recurrent_kernel<TIn, TBeta, 32, 128, GATES><<<grid, 128, 0, s>>>(p);
     } else {
         dim3 grid(kHeadDim / 16, p.HV, (unsigned)rows);
-        recurrent_kernel<TIn, TBeta, 16, 64><<<grid, 64, 0, s>>>(p);
+        recurrent_kernel<TIn, TBeta, 16, 64, GATES><<<grid, 64, 0, s>>>(p);
     }
     return launch_status();
 }
@@ -221,6 +223,10 @@ int launch_recurrent(const RecurrentArgs& a, cudaStream_t s) {
     p.scale = a.scale;
     p.gates = a.gates;
     if (a.rows == 0) return GDN_OK;
+    if (a.gates.b) {
+        return a.qkv_dtype == GDN_BF16 ? dispatch_recurrent<bf16, bf16, true>(p, a.rows, s)
+                                       : dispatch_recurrent<float, bf16, true>(p, a.rows, s);
+    }
     if (a.qkv_dtype == GDN_BF16) {
         return a.beta_dtype == GDN_BF16 ? dispatch_recurrent<bf16, bf16>(p, a.rows, s)
                                         : dispatch_recurrent<bf16, float>(p, a.rows, s);

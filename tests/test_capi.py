@@ -139,8 +139,8 @@ def test_attention_entry_points_check_their_inputs():
     assert lib.gdn_decode_attention(*args(L=65)) == _lib.ERR_SHAPE  # more keys than the cache holds
     assert lib.gdn_decode_attention(*args(mask=None)) == _lib.ERR_NULL
     assert lib.gdn_decode_attention(*args(q=24)) == _lib.ERR_ALIGN
-    assert lib.gdn_decode_attention_workspace_size(2, 4, 128, 128) == 0  # one split
-    assert lib.gdn_decode_attention_workspace_size(2, 4, 300, 128) == 2 * 4 * 3 * 64 * 129 * 4
+    assert lib.gdn_decode_attention_workspace_size(2, 4, 128, 128) == 0  # one key block: one range
+    assert lib.gdn_decode_attention_workspace_size(64, 32, 4096, 128) == 0  # 2,048 (row, head) pairs: one range each
     assert lib.gdn_rotary(16, 16, 16, 16, 1, 1, 1, 128, 65, None) == _lib.ERR_SHAPE
     assert lib.gdn_rotary(None, 16, 16, 16, 1, 1, 1, 128, 32, None) == _lib.ERR_NULL
     assert lib.gdn_rotate_into_cache(16, 16, 16, 16, 16, 0, 0, 16, 16, 16, 16, None, 16, 0, 0, 16, 16, 0, 0, 16, 0,
