@@ -333,6 +333,7 @@ def run_ours(args, rank, world, device, rank_sync, reduce_max):
         extra["decode"] = bench_decode(gdn, args, device, rank, world, rank_sync, reduce_max, hbm_peak)
         extra["verify"] = bench_verify(gdn, args, device, rank, world, rank_sync, reduce_max, hbm_peak)
         extra["attention"] = bench_attention(gdn, args, device, rank, world, rank_sync, reduce_max, hbm_peak)
+        extra["attention"]["roofline"]["traffic"] = traffic.get("attention", {}).get("dram_bytes_per_launch")
         result["extra"] = extra
         result["gpu_launches"] += sum(e.get("gpu_launches", 0) for e in extra.values())
     clocks.__exit__(None, None, None)
