@@ -329,11 +329,13 @@ def run_ours(args, rank, world, device, rank_sync, reduce_max):
     if args.extras:
         extra = {}
         extra["varlen"] = bench_varlen(gdn, args, device, rank_sync, reduce_max, world, hbm_peak, rank)
-        extra["varlen"]["roofline"]["traffic"] = traffic.get("varlen", {}).get("dram_bytes_per_launch")
+        # ncu traffic was captured on one GPU running the whole case; with N ranks each runs a shard
+        extra["varlen"]["roofline"]["traffic"] = traffic.get("varlen", {}).get("dram_bytes_per_launch") if world == 1 else None
         extra["decode"] = bench_decode(gdn, args, device, rank, world, rank_sync, reduce_max, hbm_peak)
         extra["verify"] = bench_verify(gdn, args, device, rank, world, rank_sync, reduce_max, hbm_peak)
         extra["attention"] = bench_attention(gdn, args, device, rank, world, rank_sync, reduce_max, hbm_peak)
-        extra["attention"]["roofline"]["traffic"] = traffic.get("attention", {}).get("dram_bytes_per_launch")
+        extra["attention"]["roofline"]["traffic"] = (traffic.get("attention", {}).get("dram_bytes_per_launch")
+                                                     if world == 1 else None)
         result["extra"] = extra
         result["gpu_launches"] += sum(e.get("gpu_launches", 0) for e in extra.values())
     clocks.__exit__(None, None, None)
