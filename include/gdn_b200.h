@@ -57,6 +57,15 @@ GDN_API int gdn_abi_version(void);
 GDN_API int gdn_device_error(void* stream, int reset);
 
 /*
+ * Diagnostics, no counterpart in the reference: runs the bounded device wait that every kernel of
+ * the library uses, on an mbarrier that nothing completes, with a limit of limit_cycles SM clock
+ * cycles (1,000 to 2e9; the kernels themselves use about one second). The wait runs out, raises
+ * site code 0x1FF in the device error word (read it with gdn_device_error) and the kernel returns;
+ * the context stays usable. For tests of the failure path; it faults and hangs nothing.
+ */
+GDN_API int gdn_probe_bounded_wait(int64_t limit_cycles, void* stream);
+
+/*
  * The layer's raw gate projections, for the entry points that compute beta and g themselves
  * instead of reading them (delta_gates, model/model.py:314-321, with the rounding of
  * model/triton_kernels.py:76-92; as gdn_delta_gates):

@@ -36,6 +36,7 @@ SIGNATURES: dict[str, list] = {
     "gdn_status_string": [_i32],
     "gdn_abi_version": [],
     "gdn_device_error": [_p, _i32],
+    "gdn_probe_bounded_wait": [_i64, _p],
     "gdn_recurrent": [_p, _p, _p, _i32, _p, _p, _i32, _p, _p, _p, _p, _p, _p,
                       _i64, _i64, _i64, _i64, _i64, _i64,
                       _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _p],

@@ -43,6 +43,11 @@ const char* gdn_status_string(int status) {
 
 int gdn_abi_version(void) { return kAbiVersion; }
 
+int gdn_probe_bounded_wait(int64_t limit_cycles, void* stream) {
+    if (limit_cycles < 1000 || limit_cycles > 2000000000LL) return GDN_ERR_SHAPE;
+    return launch_bounded_wait_probe(limit_cycles, as_stream(stream));
+}
+
 int gdn_device_error(void* stream, int reset) {
     int value = 0;
     if (cudaMemcpyFromSymbolAsync(&value, g_device_error, sizeof(int), 0, cudaMemcpyDeviceToHost, as_stream(stream)) !=

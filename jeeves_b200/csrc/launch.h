@@ -147,6 +147,9 @@ struct RotateCacheArgs {
 };
 int launch_rotate_into_cache(const RotateCacheArgs& a, cudaStream_t s);
 
+// Runs a bounded device wait that is meant to run out after `limit_cycles` (probe.cu).
+int launch_bounded_wait_probe(int64_t limit_cycles, cudaStream_t s);
+
 int launch_gated_rmsnorm(const void* x, const void* z, const void* w, void* y, int64_t rows, int dim, float eps,
                          cudaStream_t s);
 

@@ -9,3 +9,4 @@
 #include "gates.cu"
 #include "attention.cu"
 #include "rotary.cu"
+#include "probe.cu"

@@ -44,6 +44,7 @@ enum WaitSite : int {
     kSiteMma = 0x102,
     kSiteDrain = 0x103,
     kSiteReady = 0x104,
+    kSiteProbe = 0x1FF,  // gdn_probe_bounded_wait: a wait that is meant to run out
 };
 
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
@@ -76,11 +77,11 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
 }
 
 // Waits for the phase with the given parity to complete; false after the time limit.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int site) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int site, long long limit = kWaitCycles) {
     if (mbar_test(bar, parity)) return true;
     const long long start = clock64();
     while (!mbar_test(bar, parity)) {
-        if (clock64() - start > kWaitCycles) {
+        if (clock64() - start > limit) {
             raise_device_error(site);
             return false;
         }
@@ -94,13 +95,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int si
 // waits for a long time leaves the issue slots of its SM sub-partition to the roles that work.
 // `backoff` = false keeps polling without sleeping, for waits on a latency-critical path.
 __device__ __forceinline__ bool mbar_wait_or_abort(uint64_t* bar, uint32_t parity, int site, const int* abort,
-                                                   bool backoff = true) {
+                                                   bool backoff = true, long long limit = kWaitCycles) {
     if (mbar_test(bar, parity)) return true;
     const long long start = clock64();
     uint32_t sleep_ns = 0;
     while (!mbar_test(bar, parity)) {
         if (*reinterpret_cast<const volatile int*>(abort)) return false;
-        if (clock64() - start > kWaitCycles) {
+        if (clock64() - start > limit) {
             raise_device_error(site);
             return false;
         }

@@ -145,3 +145,9 @@ def test_attention_entry_points_check_their_inputs():
     assert lib.gdn_rotary(None, 16, 16, 16, 1, 1, 1, 128, 32, None) == _lib.ERR_NULL
     assert lib.gdn_rotate_into_cache(16, 16, 16, 16, 16, 0, 0, 16, 16, 16, 16, None, 16, 0, 0, 16, 16, 0, 0, 16, 0,
                                      1, 1, 1, 1, 128, 32, None) == _lib.ERR_NULL
+
+
+def test_probe_limit_is_checked():
+    lib = _lib.load()
+    assert lib.gdn_probe_bounded_wait(10, None) == _lib.ERR_SHAPE
+    assert lib.gdn_probe_bounded_wait(10 ** 12, None) == _lib.ERR_SHAPE

@@ -152,3 +152,21 @@ def test_packed_batch_longest_first_equals_single_sequence_calls():
         o1, S1 = gdn.gated_delta_rule_chunk(qc[:, a:b], kc[:, a:b], vc[:, a:b], gc[:, a:b], bc[:, a:b],
                                             initial_state=h0[n:n + 1].cuda(), output_final_state=True)
         assert same_bits(o[:, a:b], o1) and same_bits(S[n:n + 1], S1), n
+
+
+def test_bounded_wait_runs_out_and_the_context_stays_usable():
+    """The failure path of every kernel's waits, without a fault: a wait on an mbarrier that nothing
+    completes gives up after its limit (here 2e6 cycles, about a millisecond), raises its site code
+    and returns; afterwards the device error word resets and a prefill runs correctly."""
+    from jeeves_b200 import _lib
+    lib = _lib.load()
+    torch.cuda.synchronize()
+    lib.gdn_device_error(None, 1)
+    assert lib.gdn_probe_bounded_wait(2_000_000, None) == _lib.OK
+    torch.cuda.synchronize()
+    assert lib.gdn_device_error(None, 1) == 0x1FF
+    assert lib.gdn_device_error(None, 0) == 0
+    q, k, v, g, beta, h0 = gdn_inputs(41, 1, 100, 2, 4)
+    o_ref, s_ref = oracle.chunk_gated_delta_rule(q, k, v, g, beta, initial_state=h0, output_final_state=True)
+    o, s = gdn.gated_delta_rule_chunk(*cuda(q, k, v, g, beta), initial_state=h0.cuda(), output_final_state=True)
+    check(o, s, o_ref, s_ref)

@@ -32,7 +32,19 @@ def _inputs(seed):
              nw=(torch.rand(128, generator=gen) + 0.5).to(torch.bfloat16),
              graw=(torch.randn(1, T, 2 * HV, generator=gen) * 3).to(torch.bfloat16),
              dt=torch.randn(HV, generator=gen), rate=-torch.rand(HV, generator=gen).exp(),
-             valid=torch.rand(1, T, generator=gen) < 0.9)
+             valid=torch.rand(1, T, generator=gen) < 0.9,
+             # the drafter side: mask-row attention over a key cache, rotary, rotate-into-cache
+             aq=torch.randn(2, 12, HV, 128, generator=gen).to(torch.bfloat16),
+             kc=torch.randn(3, 200, HV, 128, generator=gen).to(torch.bfloat16),
+             vc=torch.randn(3, 200, HV, 128, generator=gen).to(torch.bfloat16),
+             amask=torch.where(torch.rand(2, 1, 12, 192, generator=gen) < 0.7, 0.0, float("-inf")).to(torch.bfloat16),
+             rx=torch.randn(2, 3, HV, 128, generator=gen).to(torch.bfloat16),
+             rcos=torch.randn(2, 3, 32, generator=gen), rsin=torch.randn(2, 3, 32, generator=gen),
+             ck=torch.randn(2, 2, HV, 128, generator=gen).to(torch.bfloat16),
+             cm=torch.randn(2, 2, 3 * HV * 128, generator=gen).to(torch.bfloat16),
+             kcache=torch.randn(3, 64, HV, 128, generator=gen).to(torch.bfloat16),
+             vcache=torch.randn(3, 64, HV, 128, generator=gen).to(torch.bfloat16),
+             rows=torch.tensor([[2, 2], [0, 0]]), positions=torch.tensor([[5, 6], [11, 12]]))
     return {name: t.cuda() for name, t in x.items()}
 
 
@@ -45,7 +57,19 @@ def _step(x, cu):
     od = fla_inplace.gated_delta_rule_step_inplace(x["dq"], x["dk"], x["dv"], x["dg"], x["db"], x["ds"])
     ov, snaps = gdn.gated_delta_rule_verify(x["vq"], x["vk"], x["vv"], x["vg"], x["vb"], x["vs"])
     gdn.gated_delta_rule_rollback(x["vs"], snaps, x["acc"])
-    return y, beta_g, g_g, o, ht, out, od, ov
+    # the gates inside the prefill and the gated norm fused into the call
+    og, hg = gdn.gated_delta_rule_chunk_gates(x["q"], x["k"], x["v"], x["graw"][..., :HV], x["graw"][..., HV:],
+                                              x["dt"], x["rate"], x["valid"], initial_state=x["h0"],
+                                              output_final_state=True, cu_seqlens=cu)
+    on, hn = gdn.gated_delta_rule_chunk_gated_norm(x["q"], x["k"], x["v"], x["g"], x["beta"], x["z"], x["nw"],
+                                                   initial_state=x["h0"], output_final_state=True, cu_seqlens=cu)
+    oa = gdn.decode_attention(x["aq"], x["kc"], x["vc"], x["amask"], 128 ** -0.5)
+    orot = gdn.rotary(x["rx"], x["rcos"], x["rsin"])
+    D3 = HV * 128
+    qm, km, vm = (x["cm"][..., i * D3:(i + 1) * D3].view(2, 2, HV, 128) for i in range(3))
+    qr = gdn.rotate_into_cache(x["ck"], x["ck"], qm, km, vm, x["rcos"][:, :2], x["rsin"][:, :2], x["rcos"][:, 1:],
+                               x["rsin"][:, 1:], x["kcache"], x["vcache"], x["rows"], x["positions"], 40)
+    return y, beta_g, g_g, o, ht, out, od, ov, og, hg, on, hn, oa, orot, qr
 
 
 def test_captured_layer_step_replays_equal_to_eager():
@@ -70,4 +94,5 @@ def test_captured_layer_step_replays_equal_to_eager():
         for a, b in zip(outs, eager):
             assert same_bits(a, b)
         assert same_bits(static["ds"], fresh["ds"]) and same_bits(static["vs"], fresh["vs"])
+        assert same_bits(static["kcache"], fresh["kcache"]) and same_bits(static["vcache"], fresh["vcache"])
     del graph
