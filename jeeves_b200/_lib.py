@@ -63,6 +63,7 @@ SIGNATURES: dict[str, list] = {
     "gdn_rotary": [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p],
     "gdn_rotate_into_cache": [_p, _p, _p, _p, _p, _i64, _i64, _p, _p, _p, _p, _p, _p, _i64, _i64, _p, _p, _i64, _i64,
                               _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p],
+    "gdn_in_proj_conv": [_p, _i64, _p, _i64, _p, _p, _p, _i64, _p, _i64, _i64, _i64, _i64, _i64, _i64, _p],
     "gdn_decode_layer": [_p, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                          _f32, _f32, _p],
     "gdn_decode_layer_noalloc": [_p, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64,

@@ -401,6 +401,29 @@ int gdn_rotate_into_cache(const void* k, const void* v, const void* qm, const vo
     return launch_rotate_into_cache(a, as_stream(stream));
 }
 
+int gdn_in_proj_conv(const void* x, int64_t x_stride, const void* w, int64_t w_stride, const void* conv_w,
+                     const int32_t* cu_seqlens, void* out, int64_t out_stride, void* conv_state, int64_t tokens,
+                     int64_t hidden, int64_t out_channels, int64_t conv_channels, int64_t sequences,
+                     int64_t conv_kernel, void* stream) {
+    if (tokens < 0 || hidden <= 0 || out_channels <= 0 || conv_channels < 0 || conv_channels > out_channels)
+        return GDN_ERR_SHAPE;
+    if (hidden % 64 || out_channels % 8 || conv_channels % 8 || tokens > INT32_MAX - 256) return GDN_ERR_SHAPE;
+    if (out_channels > (int64_t)65535 * 256 || hidden > INT32_MAX) return GDN_ERR_SHAPE;
+    if (conv_kernel != 4) return GDN_ERR_UNSUPPORTED;
+    if (cu_seqlens ? sequences < 1 : sequences != 1) return GDN_ERR_SHAPE;
+    if (tokens == 0) return GDN_OK;
+    if (!x || !w || !out || (conv_channels > 0 && !conv_w)) return GDN_ERR_NULL;
+    if (!rows_aligned(x, 2, x_stride, 0, 0) || !rows_aligned(w, 2, w_stride, 0, 0) ||
+        !rows_aligned(out, 2, out_stride, 0, 0) || (conv_w && !aligned16(conv_w)) ||
+        (conv_state && !aligned16(conv_state)))
+        return GDN_ERR_ALIGN;
+    InProjArgs a{};
+    a.x = x; a.ldx = x_stride; a.w = w; a.ldw = w_stride; a.conv_w = conv_w; a.cu_seqlens = cu_seqlens;
+    a.out = out; a.ldo = out_stride; a.conv_tail = conv_channels > 0 ? conv_state : nullptr;
+    a.T = tokens; a.K = hidden; a.N = out_channels; a.C = conv_channels; a.nseq = sequences;
+    return launch_in_proj_conv(a, as_stream(stream));
+}
+
 int gdn_decode_layer(const void* qkv, int64_t qkv_stride_b, void* conv_state, const void* conv_w, const float* g,
                      const void* beta, float* state, const void* z, const void* norm_w, void* out, void* workspace,
                      int64_t batch, int64_t key_heads, int64_t value_heads, int64_t head_dim_k, int64_t head_dim_v,

@@ -147,6 +147,23 @@ struct RotateCacheArgs {
 };
 int launch_rotate_into_cache(const RotateCacheArgs& a, cudaStream_t s);
 
+// Merged input projection with the causal conv in the epilogue (inproj.cu). x: [T, K] (row
+// stride ldx); w: [N, K] (row stride ldw); conv_w: [C, 4]; out: [T, N] (row stride ldo);
+// conv_tail: [nseq, C, 4] or null; cu_seqlens: [nseq + 1] or null.
+struct InProjArgs {
+    const void* x;
+    int64_t ldx;
+    const void* w;
+    int64_t ldw;
+    const void* conv_w;
+    const int32_t* cu_seqlens;
+    void* out;
+    int64_t ldo;
+    void* conv_tail;
+    int64_t T, K, N, C, nseq;
+};
+int launch_in_proj_conv(const InProjArgs& a, cudaStream_t s);
+
 // Runs a bounded device wait that is meant to run out after `limit_cycles` (probe.cu).
 int launch_bounded_wait_probe(int64_t limit_cycles, cudaStream_t s);
 

@@ -10,3 +10,4 @@
 #include "attention.cu"
 #include "rotary.cu"
 #include "probe.cu"
+#include "inproj.cu"

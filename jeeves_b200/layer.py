@@ -81,3 +81,40 @@ def decode_layer_step(qkv, conv_state, conv_weight, g, beta, state, z, norm_weig
         HEAD_DIM, HEAD_DIM, taps, w.shape[1], float(HEAD_DIM ** -0.5 if scale is None else scale), float(eps), _stream())
     _lib.check(status, what)
     return out
+
+
+def in_proj_conv(x, weight, conv_weight, conv_channels: int, cu_seqlens=None, conv_state: bool = False):
+    """The merged input projection of a gated-delta layer with the causal conv + SiLU fused into the
+    GEMM: ``y = x @ weight.T`` (bf16, fp32 accumulation), then ``silu(causal_conv1d)`` over the first
+    ``conv_channels`` columns (the qkv channels; ``weight`` holds their rows first, then z, b, a).
+    x ``[T, hidden]`` or ``[1, T, hidden]`` bf16; conv_weight ``[conv_channels, 4]`` (or ``[C, 1,
+    4]``). Returns ``out [.., T, N]``, and with ``conv_state`` also the last 4 pre-conv rows of
+    every sequence ``[sequences, conv_channels, 4]`` (the cache's conv state)."""
+    what = "in_proj_conv"
+    _require_cuda(what, x, weight, conv_weight, cu_seqlens)
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, x.shape[-1])
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    T, K = x2.shape
+    N = weight.shape[0]
+    if weight.dim() != 2 or weight.shape[1] != K:
+        raise ValueError(f"weight: expected [N, {K}], got {tuple(weight.shape)}")
+    if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16 or conv_weight.dtype != torch.bfloat16:
+        raise ValueError(f"x, weight, conv_weight: expected bfloat16, got {x.dtype}, {weight.dtype}, {conv_weight.dtype}")
+    cw = conv_weight.reshape(conv_channels, -1).contiguous()
+    if cw.shape[1] != 4:
+        raise ValueError(f"conv_weight: expected {conv_channels} channels of 4 taps, got {tuple(conv_weight.shape)}")
+    w = weight if weight.stride(-1) == 1 else weight.contiguous()
+    cu = None
+    seqs = 1
+    if cu_seqlens is not None:
+        cu = cu_seqlens.to(device=x.device, dtype=torch.int32).contiguous()
+        seqs = cu.numel() - 1
+    out = torch.empty(*lead, N, dtype=torch.bfloat16, device=x.device)
+    state = torch.empty(seqs, conv_channels, 4, dtype=torch.bfloat16, device=x.device) if conv_state else None
+    status = _lib.load().gdn_in_proj_conv(
+        x2.data_ptr(), x2.stride(0), w.data_ptr(), w.stride(0), cw.data_ptr(), None if cu is None else cu.data_ptr(),
+        out.data_ptr(), N, None if state is None else state.data_ptr(), T, K, N, conv_channels, seqs, 4, _stream())
+    _lib.check(status, what)
+    return (out, state) if conv_state else out

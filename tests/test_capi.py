@@ -139,7 +139,7 @@ def test_attention_entry_points_check_their_inputs():
     assert lib.gdn_decode_attention(*args(L=65)) == _lib.ERR_SHAPE  # more keys than the cache holds
     assert lib.gdn_decode_attention(*args(mask=None)) == _lib.ERR_NULL
     assert lib.gdn_decode_attention(*args(q=24)) == _lib.ERR_ALIGN
-    assert lib.gdn_decode_attention_workspace_size(2, 4, 128, 128) == 0  # one key block: one range
+    assert lib.gdn_decode_attention_workspace_size(2, 4, 64, 128) == 0  # one 64-key block: one range
     assert lib.gdn_decode_attention_workspace_size(64, 32, 4096, 128) == 0  # 2,048 (row, head) pairs: one range each
     assert lib.gdn_rotary(16, 16, 16, 16, 1, 1, 1, 128, 65, None) == _lib.ERR_SHAPE
     assert lib.gdn_rotary(None, 16, 16, 16, 1, 1, 1, 128, 32, None) == _lib.ERR_NULL
@@ -151,3 +151,15 @@ def test_probe_limit_is_checked():
     lib = _lib.load()
     assert lib.gdn_probe_bounded_wait(10, None) == _lib.ERR_SHAPE
     assert lib.gdn_probe_bounded_wait(10 ** 12, None) == _lib.ERR_SHAPE
+
+
+def test_in_proj_conv_checks_its_inputs():
+    lib = _lib.load()
+    args = lambda **kw: [16, kw.get("ldx", 64), 16, 64, 16, None, 16, 24, None, kw.get("T", 10), kw.get("K", 64),  # noqa: E731
+                         kw.get("N", 24), kw.get("C", 16), 1, kw.get("taps", 4), None]
+    assert lib.gdn_in_proj_conv(*args(K=96)) == _lib.ERR_SHAPE        # hidden not a multiple of 64
+    assert lib.gdn_in_proj_conv(*args(C=12)) == _lib.ERR_SHAPE        # channels not multiples of 8
+    assert lib.gdn_in_proj_conv(*args(C=32)) == _lib.ERR_SHAPE        # more conv channels than outputs
+    assert lib.gdn_in_proj_conv(*args(taps=3)) == _lib.ERR_UNSUPPORTED
+    assert lib.gdn_in_proj_conv(*args(ldx=60)) == _lib.ERR_ALIGN
+    assert lib.gdn_in_proj_conv(*args(T=0)) == _lib.OK

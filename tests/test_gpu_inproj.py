@@ -1,0 +1,63 @@
+"""GPU parity of the merged input projection with the causal conv in the GEMM epilogue: the
+projection against PyTorch's bf16 matmul (the reference's nn.Linear on CUDA, fp32 accumulation),
+and the conv part against the library's conv kernel on that matmul's output (same rounding), so
+that only a different summation order of the GEMM can move a bf16 value, by one ulp."""
+
+import pytest
+import torch
+
+import jeeves_b200 as gdn
+from tests.helpers import bf16_ulps
+
+pytestmark = pytest.mark.gpu
+
+
+def _case(seed, T, K, C, rest):
+    gen = torch.Generator().manual_seed(seed)
+    x = torch.randn(T, K, generator=gen).to(torch.bfloat16).cuda()
+    w = (torch.randn(C + rest, K, generator=gen) * K ** -0.5).to(torch.bfloat16).cuda()
+    cw = (torch.randn(C, 4, generator=gen) * 0.5).to(torch.bfloat16).cuda()
+    return x, w, cw
+
+
+def _close(got, want, max_ulps=1, frac=0.01):
+    """At most `frac` of the values differ, each by at most `max_ulps` bf16 ulps of the larger
+    magnitude (values near zero, where a tiny absolute difference spans many ulps, by 1e-3)."""
+    g, w = got.float().cpu(), want.float().cpu()
+    tol = max_ulps * 2.0 ** -7 * torch.maximum(g.abs(), w.abs()) + 1e-3
+    assert bool(((g - w).abs() <= tol).all()), float(((g - w).abs() - tol).max())
+    n, _ = bf16_ulps(got, want)
+    assert n <= max(1, int(frac * got.numel())), (n, got.numel())
+
+
+@pytest.mark.parametrize("T,K,C,rest", [(300, 256, 512, 264), (125, 128, 256, 0), (1, 64, 8, 8), (4096, 512, 1024, 520)])
+def test_in_proj_conv_matches_matmul_then_conv(T, K, C, rest):
+    x, w, cw = _case(T + K, T, K, C, rest)
+    out = gdn.in_proj_conv(x, w, cw, C)
+    y = x @ w.T  # bf16 output, fp32 accumulation
+    _close(out[:, C:], y[:, C:])
+    if C:
+        _close(out[:, :C], gdn.causal_conv1d(y[None, :, :C].contiguous(), cw)[0], max_ulps=2, frac=0.02)
+
+
+def test_in_proj_conv_packed_sequences_and_conv_state():
+    lens = [70, 1, 129, 0, 100, 3]
+    T, K, C, rest = sum(lens), 192, 256, 72
+    x, w, cw = _case(7, T, K, C, rest)
+    cu = torch.tensor([0] + torch.tensor(lens).cumsum(0).tolist(), dtype=torch.int32, device="cuda")
+    out, state = gdn.in_proj_conv(x, w, cw, C, cu_seqlens=cu, conv_state=True)
+    y = x @ w.T
+    _close(out[:, C:], y[:, C:])
+    _close(out[:, :C], gdn.causal_conv1d(y[None, :, :C].contiguous(), cw, cu_seqlens=cu)[0], max_ulps=2, frac=0.02)
+    for n, (a, b) in enumerate(zip(cu[:-1].tolist(), cu[1:].tolist())):
+        want = torch.zeros(C, 4, dtype=torch.bfloat16, device="cuda")
+        m = min(4, b - a)
+        if m:
+            want[:, 4 - m:] = y[b - m:b, :C].T
+        _close(state[n], want)
+
+
+def test_in_proj_conv_leaves_no_device_error():
+    from jeeves_b200 import _lib
+    torch.cuda.synchronize()
+    assert _lib.load().gdn_device_error(None, 0) == 0
