@@ -1,7 +1,7 @@
 """Benchmark of the gated-delta hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--no-extras] [--no-cpu-baseline]
-    python bench.py --profile prefill|varlen|decode|verify|attention   (one untimed run of a case, for ncu)
+    python bench.py --profile prefill|varlen|decode|verify|attention|in_proj   (one untimed run of a case, for ncu)
 
 Workloads (synthetic inputs with the benchmark configs' shapes and distributions; no
 dataset or checkpoint is involved):
@@ -19,6 +19,9 @@ dataset or checkpoint is involved):
   per-token fp32 states, then roll back to an accepted length U{1..5}.
 * ``attention`` (the drafter side of a delta layer, not a BASELINE config): the mask-row
   attention of one decode cycle, 32 sequences x 12 mask rows x 32 heads over 4,108 cached keys.
+* ``in_proj`` (the GEMM in front of the path, not a BASELINE config): the merged input projection
+  of one 9B-shaped layer, 4096 tokens x 4096 -> 12,352, with the causal conv + SiLU fused into the
+  tcgen05 GEMM's epilogue; timed beside cuBLAS's matmul followed by the conv kernel.
 
 Multi-GPU (torchrun, one process per GPU): every rank runs its own shard with no
 collective on the data path (prefill: an independent replica per GPU; decode/verify:
@@ -336,6 +339,7 @@ def run_ours(args, rank, world, device, rank_sync, reduce_max):
         extra["attention"] = bench_attention(gdn, args, device, rank, world, rank_sync, reduce_max, hbm_peak)
         extra["attention"]["roofline"]["traffic"] = (traffic.get("attention", {}).get("dram_bytes_per_launch")
                                                      if world == 1 else None)
+        extra["in_proj"] = bench_in_proj(gdn, args, device, rank_sync, reduce_max, world, tc_peak)
         result["extra"] = extra
         result["gpu_launches"] += sum(e.get("gpu_launches", 0) for e in extra.values())
     clocks.__exit__(None, None, None)
@@ -458,6 +462,42 @@ def bench_attention(gdn, args, device, rank, world, rank_sync, reduce_max, hbm_p
             "gpu_launches": (2 if splits > 1 else 1) * args.steps}
 
 
+IN_PROJ_N = C_QKV + HV * D + 2 * HV  # merged projection rows: qkv, z, b, a (12,352 at the 9B shape)
+
+
+def in_proj_case(device, T=4096, K=4096, seed=6):
+    """The merged input projection of one 9B-shaped gated-delta layer (hidden 4096 -> qkv 8192,
+    z 4096, b 32, a 32) over T tokens, with the depthwise conv weights of the qkv channels."""
+    gen = torch.Generator().manual_seed(seed)
+    x = torch.randn(T, K, generator=gen).to(torch.bfloat16).to(device)
+    w = (torch.randn(IN_PROJ_N, K, generator=gen) * K ** -0.5).to(torch.bfloat16).to(device)
+    cw = (torch.randn(C_QKV, 4, generator=gen) * 0.5).to(torch.bfloat16).to(device)
+    return x, w, cw
+
+
+def bench_in_proj(gdn, args, device, rank_sync, reduce_max, world, tc_peak, T=4096, K=4096):
+    """Fused projection + conv (one tcgen05 kernel) against cuBLAS's matmul followed by the
+    library's conv kernel, the unfused form of the same two steps; every rank runs its own replica."""
+    x, w, cw = in_proj_case(device, T, K)
+    fused_ms = reduce_max(timed(lambda i: gdn.in_proj_conv(x, w, cw, C_QKV), args.steps, args.warmup, rank_sync)) / args.steps
+
+    def unfused(i):
+        y = x @ w.T
+        gdn.causal_conv1d(y[None, :, :C_QKV], cw)
+
+    unfused_ms = reduce_max(timed(unfused, args.steps, args.warmup, rank_sync)) / args.steps
+    flops = 2 * T * K * IN_PROJ_N
+    ach = flops / (fused_ms / 1e3) / 1e12
+    return {"workload": f"merged input projection of a 9B-shaped delta layer, T={T}, hidden {K} -> {IN_PROJ_N} "
+                        f"(qkv {C_QKV} with causal conv k=4 + SiLU fused in the GEMM epilogue, z, b, a), bf16; "
+                        f"one replica per GPU; x and w ({(T + IN_PROJ_N) * K * 2 / 2 ** 20:.0f} MiB) exceed L2",
+            "value": round(world * T / (fused_ms / 1e3), 1), "unit": "tokens/s", "ms_per_step": round(fused_ms, 4),
+            "unfused_ms": round(unfused_ms, 4), "unfused": "torch matmul (cuBLAS) then gdn.causal_conv1d",
+            "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": tc_peak, "unit": "TFLOP/s",
+                         "frac": round(ach / tc_peak, 4), "algorithmic_flops": flops},
+            "gpu_launches": args.steps}
+
+
 def bench_verify(gdn, args, device, rank, world, rank_sync, reduce_max, hbm_peak, layers=24, B_total=128, T=5):
     B, _ = shard(B_total, rank, world)
     gen = torch.Generator().manual_seed(4)
@@ -577,6 +617,10 @@ def profile_case(name, device):
         q, k_cache, v_cache, mask = attention_case(32, device)
         for _ in range(2):
             gdn.decode_attention(q, k_cache, v_cache, mask, D ** -0.5)
+    elif name == "in_proj":
+        x, w, cw = in_proj_case(device)
+        for _ in range(2):
+            gdn.in_proj_conv(x, w, cw, C_QKV)
     elif name == "verify":
         B, T = 128, 5
         state = torch.randn(B, HV, D, D, device=device) * 0.02
@@ -602,7 +646,7 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-extras", dest="extras", action="store_false")
     ap.add_argument("--no-cpu-baseline", dest="cpu", action="store_false")
-    ap.add_argument("--profile", choices=("prefill", "varlen", "decode", "verify", "attention"),
+    ap.add_argument("--profile", choices=("prefill", "varlen", "decode", "verify", "attention", "in_proj"),
                     help="run one workload twice, untimed, for an ncu capture")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)

@@ -12,13 +12,19 @@
 // each sequence go to conv_tail [nseq, C, taps] (the conv state the cache keeps,
 // model/model.py:468-469).
 //
-// Tiles: 128 GEMM rows x 256 channels. A tile's 128 rows are tokens t0 - 3 .. t0 + 124 (the three
-// before t0 recomputed for the conv window; TMA fills rows before 0 and past T with zeros), so it
-// writes the 125 rows t0 .. t0 + 124. Warp 4 streams 64-wide K slices of X and W through four
-// stages with TMA (128-byte swizzle); thread 160 issues tcgen05.mma (M = 128, N = 256, K = 16) into
-// a 256-column fp32 accumulator in TMEM and frees each stage with a commit; warps 0-3 read the
-// accumulator (one row per thread), round to bf16 into a shared-memory tile and compute the conv
-// from it.
+// The product is computed transposed, Y^T = W X^T, so that a tile's accumulator holds 128
+// channels in the TMEM lanes and `bn` consecutive tokens in its columns: the thread that owns a
+// channel's lane walks its tokens in order and keeps the conv window in registers, with no
+// shared-memory staging. A tile's columns are tokens t0 - 3 .. t0 + bn - 4 (the three before t0
+// recomputed for the window; TMA fills rows before 0 and past T with zeros), and it writes the
+// bn - 3 tokens from t0 on.
+//
+// The kernel is persistent (one CTA per SM, tiles strided by the grid, tokens fastest so that the
+// CTAs running at once share the activations and a few weight panels in L2). Warp 8 streams
+// 64-wide K slices of W and X through four stages with TMA (128-byte swizzle); warp 9 issues
+// tcgen05.mma (M = 128, N = bn, K = 16) into one of two 256-column accumulators, so that the
+// products of the next tile run while warps 0-7 drain the previous one (warp w reads TMEM lane
+// quadrant w % 4 and half w / 4 of the columns).
 
 #include <cstring>
 
@@ -32,38 +38,37 @@ namespace inproj {
 
 using namespace sm100;
 
-constexpr int kBM = 128;                 // GEMM rows per tile
-constexpr int kHalo = 3;                 // rows before the tile's outputs (taps - 1 of a 4-tap conv)
-constexpr int kOutRows = kBM - kHalo;    // 125 output rows per tile
-constexpr int kBN = 256;                 // channels per tile
+constexpr int kBM = 128;                 // channels per tile (the MMA's M)
+constexpr int kHalo = 3;                 // tokens before the tile's outputs (taps - 1 of a 4-tap conv)
+constexpr int kMaxBN = 256;              // tokens per tile at most (the MMA's N)
 constexpr int kBK = 64;                  // K per stage (one 128-byte swizzle panel)
 constexpr int kStages = 4;
-constexpr uint32_t kAStage = kBM * 128;  // 16 KB
-constexpr uint32_t kBStage = kBN * 128;  // 32 KB
+constexpr uint32_t kAStage = kBM * 128;     // 16 KB of W
+constexpr uint32_t kBStage = kMaxBN * 128;  // up to 32 KB of X
 constexpr uint32_t kStageBytes = kAStage + kBStage;
 constexpr uint32_t kSmemBytes = kStages * kStageBytes + 1024;
-constexpr uint32_t kTileRowBytes = kBN * 2;  // the bf16 tile row in the epilogue (reuses the stages)
-constexpr int kThreads = 192;            // warps 0-3 epilogue, 4 producer, 5 MMA issuer
-constexpr uint32_t kBarEpilogue = 1;
-static_assert(kBM * kTileRowBytes <= kStages * kStageBytes, "the epilogue tile fits in the stages");
+constexpr int kEpilogueWarps = 8;
+constexpr int kProducerWarp = 8, kMmaWarp = 9;
+constexpr int kThreads = 32 * (kEpilogueWarps + 2);
+constexpr uint32_t kAccCols = 256;       // columns of one accumulator; two of them fill TMEM
+constexpr int kChunk = 16;               // accumulator columns per TMEM load
 
 struct Params {
-    CUtensorMap tm_x;  // 2-D (K, T), box (64, 128)
-    CUtensorMap tm_w;  // 2-D (K, N), box (64, 256)
-    const bf16* conv_w;  // [C, taps]
+    CUtensorMap tm_w;  // 2-D (K, N), box (64, 128)
+    CUtensorMap tm_x;  // 2-D (K, T), box (64, bn)
+    const bf16* conv_w;  // [C, 4]
     const int32_t* cu_seqlens;  // [nseq + 1] or null (one sequence of T tokens)
     bf16* out;           // [T, N], row stride ldo
-    bf16* conv_tail;     // [nseq, C, taps] or null
+    bf16* conv_tail;     // [nseq, C, 4] or null
     int64_t ldo;
     int T, N, C, K, nseq;
+    int bn;              // tokens per tile, a multiple of 32 in [64, 256]
+    int tiles_t, tiles;  // token tiles, all tiles
 };
 
 struct Shared {
-    uint64_t full[kStages], empty[kStages], acc_full;
+    uint64_t full[kStages], empty[kStages], acc_full[2], acc_empty[2], mma_done;
     uint32_t tmem_base;
-    int seq_start[kBM];  // first token of the sequence of each tile row (a packed batch)
-    int seq_end[kBM];
-    int seq_id[kBM];
     int abort;
 };
 
@@ -71,9 +76,103 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
     return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
 }
 
-// 16-byte chunk j (0..31) of tile row r in the epilogue tile: chunks XOR-swizzled by the row, so
-// that the 32 lanes writing one column chunk of 32 rows hit distinct banks.
-__device__ __forceinline__ uint32_t tile_off(int r, int j) { return r * kTileRowBytes + (((j ^ r) & 31) << 4); }
+// The sequence of token t of a packed batch: its first token, its end and its index.
+__device__ __forceinline__ void find_sequence(const int32_t* cu, int nseq, int t, int& start, int& end, int& id) {
+    int lo = 0, hi = nseq - 1;  // the last sequence that starts at or before t
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (__ldg(cu + mid) <= t) lo = mid;
+        else hi = mid - 1;
+    }
+    id = lo;
+    start = __ldg(cu + lo);
+    end = __ldg(cu + lo + 1);
+}
+
+}  // namespace inproj
+}  // namespace gdn
+
+namespace gdn {
+namespace inproj {
+
+// Drains one warp's share of a finished accumulator: channel c (this lane's TMEM lane of quadrant
+// `acc`), columns col0 .. col0 + ncols - 1, where column j is token row0 + j. The window carries
+// the bf16-rounded pre-conv values of the three tokens before the current one; the drain of the
+// second half of the columns starts it from the last three columns of the first half.
+template <bool VARLEN>
+__device__ __forceinline__ void drain(const Params& p, uint32_t acc, int col0, int ncols, int row0, int c, int lane) {
+    const bool in_n = c < p.N, conv = c < p.C;
+    float w0 = 0.f, w1 = 0.f, w2 = 0.f, w3 = 0.f;
+    if (conv) {
+        const uint2 raw = __ldg(reinterpret_cast<const uint2*>(p.conv_w + (int64_t)c * 4));
+        const bf16* h = reinterpret_cast<const bf16*>(&raw);
+        w0 = to_f32(h[0]);
+        w1 = to_f32(h[1]);
+        w2 = to_f32(h[2]);
+        w3 = to_f32(h[3]);
+    }
+    float x1 = 0.f, x2 = 0.f, x3 = 0.f;  // pre-conv values of tokens t - 3, t - 2, t - 1
+    if (col0 > 0) {
+        float v[kChunk];
+        tmem_ld16_wait(acc + col0 - kChunk, v);
+        x1 = round_bf16(v[kChunk - 3]);
+        x2 = round_bf16(v[kChunk - 2]);
+        x3 = round_bf16(v[kChunk - 1]);
+    }
+    bf16* out_c = p.out + c;
+#pragma unroll 1
+    for (int j = col0; j < col0 + ncols; j += kChunk) {
+        float v[kChunk];
+        tmem_ld16_wait(acc + j, v);
+        const int tb = row0 + j;  // token of column j
+        int s_start = 0, s_end = p.T, s_id = 0;
+        if (VARLEN) {
+            const int t = tb + (lane & (kChunk - 1));
+            if (t >= 0 && t < p.T) find_sequence(p.cu_seqlens, p.nseq, t, s_start, s_end, s_id);
+        }
+        float y[kChunk], pre[kChunk], res[kChunk];
+#pragma unroll
+        for (int e = 0; e < kChunk; ++e) {
+            y[e] = round_bf16(v[e]);
+            float a1 = x1, a2 = x2, a3 = x3;
+            if (VARLEN) {  // the window restarts at the token's sequence start
+                const int t = tb + e, st = __shfl_sync(0xffffffffu, s_start, e);
+                a1 = t - 3 >= st ? a1 : 0.f;
+                a2 = t - 2 >= st ? a2 : 0.f;
+                a3 = t - 1 >= st ? a3 : 0.f;
+            }
+            float s = __fadd_rn(0.f, __fmul_rn(w0, a1));  // from 0, in the conv kernel's order
+            s = __fadd_rn(s, __fmul_rn(w1, a2));
+            s = __fadd_rn(s, __fmul_rn(w2, a3));
+            s = __fadd_rn(s, __fmul_rn(w3, y[e]));
+            pre[e] = round_bf16(s);
+            x1 = x2;
+            x2 = x3;
+            x3 = y[e];
+        }
+        if (conv) {
+            silu8(reinterpret_cast<const float(&)[8]>(pre[0]), reinterpret_cast<float(&)[8]>(res[0]));
+            silu8(reinterpret_cast<const float(&)[8]>(pre[8]), reinterpret_cast<float(&)[8]>(res[8]));
+        }
+        if (in_n) {
+#pragma unroll
+            for (int e = 0; e < kChunk; ++e) {
+                const int t = tb + e;
+                if (j + e >= kHalo && t < p.T) out_c[(int64_t)t * p.ldo] = __float2bfloat16_rn(conv ? res[e] : y[e]);
+            }
+        }
+        if (conv && p.conv_tail) {  // the last four pre-conv tokens of each sequence (the cache's conv state)
+#pragma unroll
+            for (int e = 0; e < kChunk; ++e) {
+                const int t = tb + e;
+                const int end = VARLEN ? __shfl_sync(0xffffffffu, s_end, e) : p.T;
+                const int id = VARLEN ? __shfl_sync(0xffffffffu, s_id, e) : 0;
+                if (j + e >= kHalo && t < p.T && t >= end - 4)
+                    p.conv_tail[((int64_t)id * p.C + c) * 4 + (4 - (end - t))] = __float2bfloat16_rn(y[e]);
+            }
+        }
+    }
+}
 
 }  // namespace inproj
 }  // namespace gdn
@@ -86,9 +185,6 @@ __global__ void __launch_bounds__(kThreads, 1) in_proj_conv_kernel(const __grid_
     uint8_t* sm = align1024(smem_raw);
     __shared__ Shared sh;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int t0 = blockIdx.x * kOutRows;  // first output token of the tile
-    const int row0 = t0 - kHalo;           // token of GEMM row 0
-    const int n0 = blockIdx.y * kBN;
     const int kblocks = p.K / kBK;
 
     if (tid == 0) {
@@ -96,163 +192,116 @@ __global__ void __launch_bounds__(kThreads, 1) in_proj_conv_kernel(const __grid_
             mbar_init(&sh.full[s], 1);
             mbar_init(&sh.empty[s], 1);
         }
-        mbar_init(&sh.acc_full, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&sh.acc_full[b], 1);
+            mbar_init(&sh.acc_empty[b], kEpilogueWarps);
+        }
+        mbar_init(&sh.mma_done, 1);
         sh.abort = 0;
         fence_mbar_init();
-        tma_prefetch_map(&p.tm_x);
         tma_prefetch_map(&p.tm_w);
+        tma_prefetch_map(&p.tm_x);
     }
     if (warp == 0) {
-        tmem_alloc(&sh.tmem_base, kBN);
+        tmem_alloc(&sh.tmem_base, 2 * kAccCols);
         tmem_relinquish();
-    }
-    if (tid < kBM) {  // the sequence of each tile row's token
-        const int t = row0 + tid;
-        int s0 = 0, s1 = p.T, id = 0;
-        if (p.cu_seqlens && t >= 0 && t < p.T) {
-            int lo = 0, hi = p.nseq - 1;  // the last sequence that starts at or before t
-            while (lo < hi) {
-                const int mid = (lo + hi + 1) >> 1;
-                if (p.cu_seqlens[mid] <= t) lo = mid;
-                else hi = mid - 1;
-            }
-            id = lo;
-            s0 = p.cu_seqlens[lo];
-            s1 = p.cu_seqlens[lo + 1];
-        }
-        sh.seq_start[tid] = s0;
-        sh.seq_end[tid] = s1;
-        sh.seq_id[tid] = id;
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tb = sh.tmem_base;
 
-    if (warp == 4) {
+    if (warp == kProducerWarp) {
         // ============================== producer ==============================
-        if (lane != 0) return;
-        int issued = 0;
-        for (int kb = 0; kb < kblocks; ++kb) {
-            const int s = kb % kStages;
-            if (kb >= kStages &&
-                !mbar_wait_or_abort(&sh.empty[s], (uint32_t)((kb / kStages) - 1) & 1, kSiteTmaLoad, &sh.abort)) {
-                atomicExch(&sh.abort, 1);
-                break;
-            }
-            uint8_t* st = sm + s * kStageBytes;
-            mbar_arrive_expect_tx(&sh.full[s], kStageBytes);
-            tma_load_2d(st, &p.tm_x, &sh.full[s], kb * kBK, row0);
-            tma_load_2d(st + kAStage, &p.tm_w, &sh.full[s], kb * kBK, n0);
-            ++issued;
-        }
-        // the copies in flight land before the CTA's shared memory can go away
-        for (int kb = issued - kStages > 0 ? issued - kStages : 0; kb < issued; ++kb)
-            mbar_wait(&sh.full[kb % kStages], (uint32_t)(kb / kStages) & 1, kSiteDrain);
-        return;
-    }
-    if (warp == 5) {
-        // ============================== MMA issuer ==============================
-        if (lane != 0) return;
-        const uint32_t idesc = make_idesc(kBM, kBN, kFmtBF16, false, false);
-        for (int kb = 0; kb < kblocks; ++kb) {
-            const int s = kb % kStages;
-            if (!mbar_wait_or_abort(&sh.full[s], (uint32_t)(kb / kStages) & 1, kSiteTmaLoad, &sh.abort)) {
-                atomicExch(&sh.abort, 1);
-                break;
-            }
-            tc_fence_after();
-            const uint8_t* st = sm + s * kStageBytes;
-            const uint64_t da = sdesc_kmajor(st, 0), db = sdesc_kmajor(st + kAStage, 0);
-#pragma unroll
-            for (int kk = 0; kk < kBK / 16; ++kk)
-                mma_f16(tb, sdesc_add(da, kk * 32), sdesc_add(db, kk * 32), idesc, (kb | kk) != 0 ? 1u : 0u);
-            mma_commit(&sh.empty[s]);  // the stage is free once these products have read it
-        }
-        mma_commit(&sh.acc_full);  // after every product issued (also after a failed wait)
-        return;
-    }
-
-    // ================================ epilogue ================================
-    const int r = 32 * warp + lane;  // tile row = TMEM lane
-    const bool ok = mbar_wait(&sh.acc_full, 0, kSiteMma) && !*reinterpret_cast<volatile int*>(&sh.abort);
-    tc_fence_after();
-    // every product is done, so the stages are free: the bf16 tile goes there
-    uint8_t* tile = sm;
-#pragma unroll 1
-    for (int c = 0; c < kBN / 32; ++c) {
-        float v[32];
-        tmem_ld32_wait(tb + ((uint32_t)(32 * warp) << 16) + 32 * c, v);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            uint4 raw;
-            __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&raw);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[8 * q + 2 * e], v[8 * q + 2 * e + 1]);
-            *reinterpret_cast<uint4*>(tile + tile_off(r, 4 * c + q)) = raw;
-        }
-    }
-    tc_fence_before();
-    named_sync(kBarEpilogue, kBM);
-    if (ok) {
-        for (int task = tid; task < kOutRows * (kBN / 8); task += kBM) {
-            const int rr = kHalo + task / (kBN / 8), j = task % (kBN / 8);
-            const int t = row0 + rr;
-            const int c = n0 + 8 * j;
-            if (t >= p.T || c >= p.N) continue;
-            const uint4 cur = *reinterpret_cast<const uint4*>(tile + tile_off(rr, j));
-            uint4 res = cur;
-            if (c < p.C) {
-                float win[4][8];
-                const int start = sh.seq_start[rr];
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    if (t - 3 + i >= start) {
-                        const uint4 raw = *reinterpret_cast<const uint4*>(tile + tile_off(rr - 3 + i, j));
-                        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const float2 f = __bfloat1622float2(h[e]);
-                            win[i][2 * e] = f.x;
-                            win[i][2 * e + 1] = f.y;
-                        }
-                    } else {
-#pragma unroll
-                        for (int e = 0; e < 8; ++e) win[i][e] = 0.f;
+        if (lane == 0) {
+            const uint32_t bytes = kAStage + (uint32_t)p.bn * 128;
+            int it = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; ok && tile < p.tiles; tile += gridDim.x) {
+                const int n0 = (tile / p.tiles_t) * kBM;
+                const int row0 = (tile % p.tiles_t) * (p.bn - kHalo) - kHalo;
+                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                    const int s = it % kStages;
+                    if (it >= kStages && !mbar_wait_or_abort(&sh.empty[s], (uint32_t)(it / kStages - 1) & 1,
+                                                             kSiteTmaLoad, &sh.abort, false)) {
+                        atomicExch(&sh.abort, 1);
+                        ok = false;
+                        break;
                     }
-                }
-                bf16 wr[32];
-                const uint4* wsrc = reinterpret_cast<const uint4*>(p.conv_w + (int64_t)c * 4);
-#pragma unroll
-                for (int i = 0; i < 4; ++i) reinterpret_cast<uint4*>(wr)[i] = __ldg(wsrc + i);
-                float pre[8], out[8];
-#pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    float acc = 0.f;
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) acc = __fadd_rn(acc, __fmul_rn(to_f32(wr[4 * q + i]), win[i][q]));
-                    pre[q] = round_bf16(acc);
-                }
-                silu8(pre, out);
-                __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&res);
-#pragma unroll
-                for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(out[2 * e], out[2 * e + 1]);
-                if (p.conv_tail && t >= sh.seq_end[rr] - 4) {  // the pre-conv rows the cache keeps
-                    const int pos = 4 - (sh.seq_end[rr] - t);
-                    const bf16* cv = reinterpret_cast<const bf16*>(&cur);
-                    bf16* dst = p.conv_tail + ((int64_t)sh.seq_id[rr] * p.C + c) * 4 + pos;
-#pragma unroll
-                    for (int q = 0; q < 8; ++q) dst[4 * q] = cv[q];
+                    uint8_t* st = sm + s * kStageBytes;
+                    mbar_arrive_expect_tx(&sh.full[s], bytes);
+                    tma_load_2d(st, &p.tm_w, &sh.full[s], kb * kBK, n0);
+                    tma_load_2d(st + kAStage, &p.tm_x, &sh.full[s], kb * kBK, row0);
                 }
             }
-            *reinterpret_cast<uint4*>(p.out + (int64_t)t * p.ldo + c) = res;
+            // the copies in flight land before the CTA's shared memory can go away
+            for (int i = it > kStages ? it - kStages : 0; i < it; ++i)
+                mbar_wait(&sh.full[i % kStages], (uint32_t)(i / kStages) & 1, kSiteDrain);
+        }
+    } else if (warp == kMmaWarp) {
+        // ============================== MMA issuer ==============================
+        if (lane == 0) {
+            const uint32_t idesc = make_idesc(kBM, (uint32_t)p.bn, kFmtBF16, false, false);
+            int it = 0, lt = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; ok && tile < p.tiles; tile += gridDim.x, ++lt) {
+                const int b = lt & 1;
+                const uint32_t acc = tb + b * kAccCols;
+                if (lt >= 2 && !mbar_wait_or_abort(&sh.acc_empty[b], (uint32_t)((lt >> 1) - 1) & 1, kSiteReady,
+                                                   &sh.abort, false)) {
+                    atomicExch(&sh.abort, 1);
+                    break;
+                }
+                tc_fence_after();
+                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                    const int s = it % kStages;
+                    if (!mbar_wait_or_abort(&sh.full[s], (uint32_t)(it / kStages) & 1, kSiteTmaLoad, &sh.abort,
+                                            false)) {
+                        atomicExch(&sh.abort, 1);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint8_t* st = sm + s * kStageBytes;
+                    const uint64_t da = sdesc_kmajor(st, 0), db = sdesc_kmajor(st + kAStage, 0);
+#pragma unroll
+                    for (int kk = 0; kk < kBK / 16; ++kk)
+                        mma_f16(acc, sdesc_add(da, kk * 32), sdesc_add(db, kk * 32), idesc, (kb | kk) != 0 ? 1u : 0u);
+                    mma_commit(&sh.empty[s]);  // the stage is free once these products have read it
+                }
+                mma_commit(&sh.acc_full[b]);  // also after a failed wait, so that no drain waits in vain
+            }
+            mma_commit(&sh.mma_done);
+            mbar_wait(&sh.mma_done, 0, kSiteMma);  // every product issued is done before TMEM goes away
+        }
+    } else {
+        // ================================ epilogue ================================
+        const int q = warp & 3, half = p.bn >> 1, col0 = (warp >> 2) * half;
+        int lt = 0;
+        for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x, ++lt) {
+            const int b = lt & 1;
+            if (!mbar_wait_or_abort(&sh.acc_full[b], (uint32_t)(lt >> 1) & 1, kSiteMma, &sh.abort)) {
+                atomicExch(&sh.abort, 1);
+                break;
+            }
+            if (*reinterpret_cast<volatile int*>(&sh.abort)) break;
+            tc_fence_after();
+            const int n0 = (tile / p.tiles_t) * kBM;
+            const int row0 = (tile % p.tiles_t) * (p.bn - kHalo) - kHalo;
+            const uint32_t acc = tb + b * kAccCols + ((uint32_t)(32 * q) << 16);
+            const int c = n0 + 32 * q + lane;
+            if (p.cu_seqlens) drain<true>(p, acc, col0, half, row0, c, lane);
+            else drain<false>(p, acc, col0, half, row0, c, lane);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sh.acc_empty[b]);  // the MMA may overwrite this accumulator
         }
     }
     tc_fence_before();
-    named_sync(kBarEpilogue, kBM);
+    __syncthreads();
     if (warp == 0) {
         tc_fence_after();
-        tmem_dealloc(tb, kBN);
+        tmem_dealloc(tb, 2 * kAccCols);
     }
 }
 
@@ -269,23 +318,47 @@ static bool make_map2(CUtensorMap* map, const void* base, int64_t rows, int64_t 
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Tokens per tile: the candidate with the shortest estimated makespan, counted as rounds of tiles
+// over the persistent CTAs times the tile's columns plus a fixed cost per tile (pipeline fill and
+// drain, in columns); ties go to the wider tile, which reads fewer bytes per product.
+static int choose_bn(int64_t T, int64_t N, int ctas) {
+    static const int kCandidates[] = {256, 224, 192, 160, 128, 96, 64};
+    constexpr int64_t kTileCost = 32;
+    const int64_t tiles_n = (N + kBM - 1) / kBM;
+    int best = 256;
+    int64_t best_cost = INT64_MAX;
+    for (int bn : kCandidates) {
+        const int64_t tiles = (T + bn - kHalo - 1) / (bn - kHalo) * tiles_n;
+        const int64_t grid = tiles < ctas ? tiles : ctas;
+        const int64_t cost = (tiles + grid - 1) / grid * (bn + kTileCost);
+        if (cost < best_cost) {
+            best_cost = cost;
+            best = bn;
+        }
+    }
+    return best;
+}
+
 }  // namespace inproj
 
 int launch_in_proj_conv(const InProjArgs& a, cudaStream_t s) {
     using namespace inproj;
     if (a.T == 0 || a.N == 0) return GDN_OK;
     static bool ready[64] = {false};
+    static int sms[64] = {0};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return GDN_ERR_LAUNCH;
     if (!ready[dev]) {
         if (cudaFuncSetAttribute(in_proj_conv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes) !=
-            cudaSuccess)
+                cudaSuccess ||
+            cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms[dev] < 1)
             return GDN_ERR_LAUNCH;
         ready[dev] = true;
     }
     Params p;
     memset(&p, 0, sizeof(p));
-    if (!make_map2(&p.tm_x, a.x, a.T, a.K, a.ldx, kBM) || !make_map2(&p.tm_w, a.w, a.N, a.K, a.ldw, kBN))
+    p.bn = choose_bn(a.T, a.N, sms[dev]);
+    if (!make_map2(&p.tm_w, a.w, a.N, a.K, a.ldw, kBM) || !make_map2(&p.tm_x, a.x, a.T, a.K, a.ldx, (uint32_t)p.bn))
         return GDN_ERR_LAUNCH;
     p.conv_w = static_cast<const bf16*>(a.conv_w);
     p.cu_seqlens = a.cu_seqlens;
@@ -297,10 +370,14 @@ int launch_in_proj_conv(const InProjArgs& a, cudaStream_t s) {
     p.C = (int)a.C;
     p.K = (int)a.K;
     p.nseq = (int)a.nseq;
+    const int64_t tiles_t = (a.T + p.bn - kHalo - 1) / (p.bn - kHalo), tiles = tiles_t * ((a.N + kBM - 1) / kBM);
+    if (tiles > INT32_MAX) return GDN_ERR_SHAPE;
+    p.tiles_t = (int)tiles_t;
+    p.tiles = (int)tiles;
     if (a.conv_tail &&
         cudaMemsetAsync(a.conv_tail, 0, (size_t)a.nseq * a.C * 4 * sizeof(bf16), s) != cudaSuccess)
         return GDN_ERR_LAUNCH;
-    dim3 grid((unsigned)((a.T + kOutRows - 1) / kOutRows), (unsigned)((a.N + kBN - 1) / kBN));
+    const int grid = (int)(tiles < sms[dev] ? tiles : sms[dev]);
     in_proj_conv_kernel<<<grid, kThreads, kSmemBytes, s>>>(p);
     return launch_status();
 }

@@ -30,7 +30,11 @@ def _close(got, want, max_ulps=1, frac=0.01):
     assert n <= max(1, int(frac * got.numel())), (n, got.numel())
 
 
-@pytest.mark.parametrize("T,K,C,rest", [(300, 256, 512, 264), (125, 128, 256, 0), (1, 64, 8, 8), (4096, 512, 1024, 520)])
+# The tile width (tokens per tile, 64 .. 256) follows the shape; these shapes reach every width on
+# a 148-SM B200: 64 (the first three), 192, 256, 224, 160, 128, 96.
+@pytest.mark.parametrize("T,K,C,rest", [(300, 256, 512, 264), (125, 128, 256, 0), (1, 64, 8, 8), (4096, 512, 1024, 520),
+                                        (2024, 128, 2048, 256), (571, 128, 4096, 768), (382, 128, 4096, 768),
+                                        (284, 128, 4096, 768), (200, 128, 4096, 768)])
 def test_in_proj_conv_matches_matmul_then_conv(T, K, C, rest):
     x, w, cw = _case(T + K, T, K, C, rest)
     out = gdn.in_proj_conv(x, w, cw, C)
@@ -40,9 +44,10 @@ def test_in_proj_conv_matches_matmul_then_conv(T, K, C, rest):
         _close(out[:, :C], gdn.causal_conv1d(y[None, :, :C].contiguous(), cw)[0], max_ulps=2, frac=0.02)
 
 
-def test_in_proj_conv_packed_sequences_and_conv_state():
-    lens = [70, 1, 129, 0, 100, 3]
-    T, K, C, rest = sum(lens), 192, 256, 72
+@pytest.mark.parametrize("lens,K,C,rest", [([70, 1, 129, 0, 100, 3], 192, 256, 72),
+                                           ([700, 2, 900, 0, 3, 419, 1], 128, 2048, 256)])
+def test_in_proj_conv_packed_sequences_and_conv_state(lens, K, C, rest):
+    T = sum(lens)
     x, w, cw = _case(7, T, K, C, rest)
     cu = torch.tensor([0] + torch.tensor(lens).cumsum(0).tolist(), dtype=torch.int32, device="cuda")
     out, state = gdn.in_proj_conv(x, w, cw, C, cu_seqlens=cu, conv_state=True)
@@ -55,6 +60,17 @@ def test_in_proj_conv_packed_sequences_and_conv_state():
         if m:
             want[:, 4 - m:] = y[b - m:b, :C].T
         _close(state[n], want)
+
+
+@pytest.mark.parametrize("T", [2, 700])
+def test_in_proj_conv_dense_conv_state(T):
+    x, w, cw = _case(11, T, 128, 512, 136)
+    out, state = gdn.in_proj_conv(x, w, cw, 512, conv_state=True)
+    y = x @ w.T
+    want = torch.zeros(1, 512, 4, dtype=torch.bfloat16, device="cuda")
+    want[0, :, 4 - min(4, T):] = y[-min(4, T):, :512].T
+    _close(state, want)
+    _close(out[:, 512:], y[:, 512:])
 
 
 def test_in_proj_conv_leaves_no_device_error():
