@@ -6,8 +6,9 @@
 // layout) and writes
 //   out[t, c] = silu(conv_c(Y_bf16[t-3..t, c]))   for c < C (the qkv channels),
 //   out[t, c] = Y_bf16[t, c]                       for c >= C,
-// with Y rounded to bf16 first, as the two eager steps do, and the conv / SiLU in the rounding of
-// the conv kernel (fp32 sum of fp32 products in tap order, rounded to bf16, exact SiLU). With
+// with Y rounded to bf16 first and the conv output rounded to bf16 before the SiLU, as the two
+// eager steps do (the conv in fp32 fused multiply-adds in tap order, the SiLU with the hardware
+// exponential and reciprocal: within one bf16 unit of the conv kernel's exact rounding). With
 // cu_seqlens the window restarts at every sequence. Optionally the last `taps` pre-conv rows of
 // each sequence go to conv_tail [nseq, C, taps] (the conv state the cache keeps,
 // model/model.py:468-469).
@@ -76,6 +77,13 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
     return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
 }
 
+// SiLU of a bf16-valued input with the hardware exponential and reciprocal: x / (1 + 2^(-x log2 e)).
+// The epilogue's arithmetic runs beside the tensor cores and slows them (it shares the SM's power
+// budget), so it takes the short form; against the exact quotient the bf16 result differs by at
+// most one unit in the last place, and rarely. x below about -88 gives -0 (the divisor is
+// infinite), 0 gives 0, NaN stays NaN.
+__device__ __forceinline__ float silu_fast(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+
 // The sequence of token t of a packed batch: its first token, its end and its index.
 __device__ __forceinline__ void find_sequence(const int32_t* cu, int nseq, int t, int& start, int& end, int& id) {
     int lo = 0, hi = nseq - 1;  // the last sequence that starts at or before t
@@ -141,18 +149,18 @@ __device__ __forceinline__ void drain(const Params& p, uint32_t acc, int col0, i
                 a2 = t - 2 >= st ? a2 : 0.f;
                 a3 = t - 1 >= st ? a3 : 0.f;
             }
-            float s = __fadd_rn(0.f, __fmul_rn(w0, a1));  // from 0, in the conv kernel's order
-            s = __fadd_rn(s, __fmul_rn(w1, a2));
-            s = __fadd_rn(s, __fmul_rn(w2, a3));
-            s = __fadd_rn(s, __fmul_rn(w3, y[e]));
+            float s = w0 * a1;  // fused multiply-adds in tap order
+            s = fmaf(w1, a2, s);
+            s = fmaf(w2, a3, s);
+            s = fmaf(w3, y[e], s);
             pre[e] = round_bf16(s);
             x1 = x2;
             x2 = x3;
             x3 = y[e];
         }
         if (conv) {
-            silu8(reinterpret_cast<const float(&)[8]>(pre[0]), reinterpret_cast<float(&)[8]>(res[0]));
-            silu8(reinterpret_cast<const float(&)[8]>(pre[8]), reinterpret_cast<float(&)[8]>(res[8]));
+#pragma unroll
+            for (int e = 0; e < kChunk; ++e) res[e] = silu_fast(pre[e]);
         }
         if (in_n) {
 #pragma unroll
@@ -305,6 +313,170 @@ __global__ void __launch_bounds__(kThreads, 1) in_proj_conv_kernel(const __grid_
     }
 }
 
+// ------------------------------------------------------------------------------------------
+// The CTA-pair form: a cluster of two CTAs computes a 256-channel x bn-token tile with
+// tcgen05.mma.cta_group::2 (M = 256). Each CTA stages its own 128 weight rows and half of the
+// tile's tokens (32 KB a stage instead of 48 KB), so that each SM reads two thirds of the bytes
+// per product from L2 and from its shared memory; the leader's thread 320 issues the products
+// into both SMs' accumulators, and each CTA drains its own 128 channels as above.
+// ------------------------------------------------------------------------------------------
+constexpr int kPairStages = 6;
+constexpr uint32_t kPairStageBytes = kAStage + (kMaxBN / 2) * 128;  // 32 KB
+constexpr uint32_t kPairSmemBytes = kPairStages * kPairStageBytes + 1024;
+constexpr int kPairBM = 2 * kBM;  // channels per pair tile
+
+struct PairShared {
+    uint64_t full[kPairStages], empty[kPairStages], acc_full[2], acc_empty[2], mma_done;
+    uint32_t tmem_base;
+    int abort;
+};
+
+// Raises the abort flag of both CTAs of the pair, so that the other's waits give up too.
+__device__ __forceinline__ void pair_abort(int* abort, uint32_t rank) {
+    atomicExch(abort, 1);
+    asm volatile("st.relaxed.cluster.shared::cluster.u32 [%0], %1;" ::"r"(mapa_shared(abort, rank ^ 1u)), "r"(1)
+                 : "memory");
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    in_proj_conv_pair_kernel(const __grid_constant__ Params p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* sm = align1024(smem_raw);
+    __shared__ PairShared sh;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t rank = cluster_rank();  // 0: the leader, which issues the products
+    const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+    const int kblocks = p.K / kBK;
+    const int half_bn = p.bn >> 1;
+
+    if (tid == 0) {
+        for (int s = 0; s < kPairStages; ++s) {
+            mbar_init(&sh.full[s], 1);
+            mbar_init(&sh.empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&sh.acc_full[b], 1);
+            mbar_init(&sh.acc_empty[b], 2 * kEpilogueWarps);  // the drains of both CTAs
+        }
+        mbar_init(&sh.mma_done, 1);
+        sh.abort = 0;
+        fence_mbar_init();
+        tma_prefetch_map(&p.tm_w);
+        tma_prefetch_map(&p.tm_x);
+    }
+    if (warp == 0) {
+        tmem_alloc_pair(&sh.tmem_base, 2 * kAccCols);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync();  // both CTAs' barriers are initialised before either signals the other's
+    tc_fence_after();
+    const uint32_t tb = sh.tmem_base;
+
+    if (warp == kProducerWarp) {
+        // ============================== producers (both CTAs) ==============================
+        if (lane == 0) {
+            const uint32_t bytes = 2 * (kAStage + (uint32_t)half_bn * 128);  // both CTAs' copies
+            int it = 0;
+            bool ok = true;
+            for (int tile = pair; ok && tile < p.tiles; tile += npairs) {
+                const int tt = tile % p.tiles_t, nn = tile / p.tiles_t;
+                // this CTA's weight rows and token rows; a start past the matrix is moved back
+                // inside it (those rows feed only channels or tokens that are not written)
+                int n0 = nn * kPairBM + kBM * (int)rank;
+                int r0 = tt * (p.bn - kHalo) - kHalo + (int)rank * half_bn;
+                if (n0 >= p.N) n0 = max(p.N - kBM, 0);
+                if (r0 >= p.T) r0 = p.T - 1;
+                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                    const int s = it % kPairStages;
+                    if (it >= kPairStages &&
+                        !mbar_wait_or_abort(&sh.empty[s], (uint32_t)(it / kPairStages - 1) & 1, kSiteTmaLoad,
+                                            &sh.abort, false, kWaitCycles, true)) {
+                        pair_abort(&sh.abort, rank);
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* st = sm + s * kPairStageBytes;
+                    if (rank == 0) mbar_arrive_expect_tx(&sh.full[s], bytes);
+                    const uint32_t bar = mapa_shared(&sh.full[s], 0);
+                    tma_load_2d_pair(st, &p.tm_w, bar, kb * kBK, n0);
+                    tma_load_2d_pair(st + kAStage, &p.tm_x, bar, kb * kBK, r0);
+                }
+            }
+            if (rank == 0)  // the copies in flight land before the shared memory can go away
+                for (int i = it > kPairStages ? it - kPairStages : 0; i < it; ++i)
+                    mbar_wait(&sh.full[i % kPairStages], (uint32_t)(i / kPairStages) & 1, kSiteDrain);
+        }
+    } else if (warp == kMmaWarp) {
+        // ============================== MMA issuer (leader) ==============================
+        if (lane == 0 && rank == 0) {
+            const uint32_t idesc = make_idesc(kPairBM, (uint32_t)p.bn, kFmtBF16, false, false);
+            int it = 0, lt = 0;
+            bool ok = true;
+            for (int tile = pair; ok && tile < p.tiles; tile += npairs, ++lt) {
+                const int b = lt & 1;
+                const uint32_t acc = tb + b * kAccCols;
+                if (lt >= 2 && !mbar_wait_or_abort(&sh.acc_empty[b], (uint32_t)((lt >> 1) - 1) & 1, kSiteReady,
+                                                   &sh.abort, false, kWaitCycles, true)) {
+                    pair_abort(&sh.abort, rank);
+                    break;
+                }
+                tc_fence_after();
+                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                    const int s = it % kPairStages;
+                    if (!mbar_wait_or_abort(&sh.full[s], (uint32_t)(it / kPairStages) & 1, kSiteTmaLoad, &sh.abort,
+                                            false, kWaitCycles, true)) {
+                        pair_abort(&sh.abort, rank);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint8_t* st = sm + s * kPairStageBytes;
+                    const uint64_t da = sdesc_kmajor(st, 0), db = sdesc_kmajor(st + kAStage, 0);
+#pragma unroll
+                    for (int kk = 0; kk < kBK / 16; ++kk)
+                        mma_f16_pair(acc, sdesc_add(da, kk * 32), sdesc_add(db, kk * 32), idesc,
+                                     (kb | kk) != 0 ? 1u : 0u);
+                    mma_commit_pair(&sh.empty[s], 3);  // both CTAs' stages are free once read
+                }
+                mma_commit_pair(&sh.acc_full[b], 3);  // also after a failed wait
+            }
+            mma_commit_pair(&sh.mma_done, 1);
+            mbar_wait(&sh.mma_done, 0, kSiteMma);  // every product issued is done before TMEM goes away
+        }
+    } else {
+        // ================================ epilogue (both CTAs) ================================
+        const int q = warp & 3, half = p.bn >> 1, col0 = (warp >> 2) * half;
+        int lt = 0;
+        for (int tile = pair; tile < p.tiles; tile += npairs, ++lt) {
+            const int b = lt & 1;
+            if (!mbar_wait_or_abort(&sh.acc_full[b], (uint32_t)(lt >> 1) & 1, kSiteMma, &sh.abort, true, kWaitCycles,
+                                    true)) {
+                pair_abort(&sh.abort, rank);
+                break;
+            }
+            if (*reinterpret_cast<volatile int*>(&sh.abort)) break;
+            tc_fence_after();
+            const int tt = tile % p.tiles_t, nn = tile / p.tiles_t;
+            const int row0 = tt * (p.bn - kHalo) - kHalo;
+            const uint32_t acc = tb + b * kAccCols + ((uint32_t)(32 * q) << 16);
+            const int c = nn * kPairBM + kBM * (int)rank + 32 * q + lane;
+            if (p.cu_seqlens) drain<true>(p, acc, col0, half, row0, c, lane);
+            else drain<false>(p, acc, col0, half, row0, c, lane);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(mapa_shared(&sh.acc_empty[b], 0));  // the leader may overwrite it
+        }
+    }
+    __syncwarp();
+    tc_fence_before();
+    cluster_sync();  // no CTA frees its TMEM or leaves while the other may still signal it
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc_pair(tb, 2 * kAccCols);
+    }
+}
+
 // 2-D map over a [rows, K] bf16 matrix with row stride ld (elements), box (64, box_rows).
 static bool make_map2(CUtensorMap* map, const void* base, int64_t rows, int64_t K, int64_t ld, uint32_t box_rows) {
     EncodeTiledFn enc = encode_fn();
@@ -319,12 +491,13 @@ static bool make_map2(CUtensorMap* map, const void* base, int64_t rows, int64_t 
 }
 
 // Tokens per tile: the candidate with the shortest estimated makespan, counted as rounds of tiles
-// over the persistent CTAs times the tile's columns plus a fixed cost per tile (pipeline fill and
-// drain, in columns); ties go to the wider tile, which reads fewer bytes per product.
-static int choose_bn(int64_t T, int64_t N, int ctas) {
+// over the persistent CTAs (or CTA pairs) times the tile's columns plus a fixed cost per tile
+// (pipeline fill and drain, in columns); ties go to the wider tile, which reads fewer bytes per
+// product.
+static int choose_bn(int64_t T, int64_t N, int ctas, int tile_channels) {
     static const int kCandidates[] = {256, 224, 192, 160, 128, 96, 64};
-    constexpr int64_t kTileCost = 32;
-    const int64_t tiles_n = (N + kBM - 1) / kBM;
+    constexpr int64_t kTileCost = 288;  // fitted to the measured times of the widths at T = 4096
+    const int64_t tiles_n = (N + tile_channels - 1) / tile_channels;
     int best = 256;
     int64_t best_cost = INT64_MAX;
     for (int bn : kCandidates) {
@@ -351,14 +524,22 @@ int launch_in_proj_conv(const InProjArgs& a, cudaStream_t s) {
     if (!ready[dev]) {
         if (cudaFuncSetAttribute(in_proj_conv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes) !=
                 cudaSuccess ||
+            cudaFuncSetAttribute(in_proj_conv_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kPairSmemBytes) != cudaSuccess ||
             cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms[dev] < 1)
             return GDN_ERR_LAUNCH;
         ready[dev] = true;
     }
+    // CTA pairs when the pair tiles occupy every pair of SMs; single CTAs for smaller problems
+    const int pairs = sms[dev] / 2;
+    const int bn_pair = choose_bn(a.T, a.N, pairs, kPairBM);
+    const int64_t pair_tiles = (a.T + bn_pair - kHalo - 1) / (bn_pair - kHalo) * ((a.N + kPairBM - 1) / kPairBM);
+    const bool use_pair = pairs >= 1 && pair_tiles >= pairs;
     Params p;
     memset(&p, 0, sizeof(p));
-    p.bn = choose_bn(a.T, a.N, sms[dev]);
-    if (!make_map2(&p.tm_w, a.w, a.N, a.K, a.ldw, kBM) || !make_map2(&p.tm_x, a.x, a.T, a.K, a.ldx, (uint32_t)p.bn))
+    p.bn = use_pair ? bn_pair : choose_bn(a.T, a.N, sms[dev], kBM);
+    if (!make_map2(&p.tm_w, a.w, a.N, a.K, a.ldw, kBM) ||
+        !make_map2(&p.tm_x, a.x, a.T, a.K, a.ldx, (uint32_t)(use_pair ? p.bn / 2 : p.bn)))
         return GDN_ERR_LAUNCH;
     p.conv_w = static_cast<const bf16*>(a.conv_w);
     p.cu_seqlens = a.cu_seqlens;
@@ -370,15 +551,22 @@ int launch_in_proj_conv(const InProjArgs& a, cudaStream_t s) {
     p.C = (int)a.C;
     p.K = (int)a.K;
     p.nseq = (int)a.nseq;
-    const int64_t tiles_t = (a.T + p.bn - kHalo - 1) / (p.bn - kHalo), tiles = tiles_t * ((a.N + kBM - 1) / kBM);
+    const int tile_channels = use_pair ? kPairBM : kBM;
+    const int64_t tiles_t = (a.T + p.bn - kHalo - 1) / (p.bn - kHalo);
+    const int64_t tiles = tiles_t * ((a.N + tile_channels - 1) / tile_channels);
     if (tiles > INT32_MAX) return GDN_ERR_SHAPE;
     p.tiles_t = (int)tiles_t;
     p.tiles = (int)tiles;
     if (a.conv_tail &&
         cudaMemsetAsync(a.conv_tail, 0, (size_t)a.nseq * a.C * 4 * sizeof(bf16), s) != cudaSuccess)
         return GDN_ERR_LAUNCH;
-    const int grid = (int)(tiles < sms[dev] ? tiles : sms[dev]);
-    in_proj_conv_kernel<<<grid, kThreads, kSmemBytes, s>>>(p);
+    if (use_pair) {
+        const int grid = 2 * (int)(tiles < pairs ? tiles : pairs);
+        in_proj_conv_pair_kernel<<<grid, kThreads, kPairSmemBytes, s>>>(p);
+    } else {
+        const int grid = (int)(tiles < sms[dev] ? tiles : sms[dev]);
+        in_proj_conv_kernel<<<grid, kThreads, kSmemBytes, s>>>(p);
+    }
     return launch_status();
 }
 

@@ -30,11 +30,17 @@ def _close(got, want, max_ulps=1, frac=0.01):
     assert n <= max(1, int(frac * got.numel())), (n, got.numel())
 
 
-# The tile width (tokens per tile, 64 .. 256) follows the shape; these shapes reach every width on
-# a 148-SM B200: 64 (the first three), 192, 256, 224, 160, 128, 96.
-@pytest.mark.parametrize("T,K,C,rest", [(300, 256, 512, 264), (125, 128, 256, 0), (1, 64, 8, 8), (4096, 512, 1024, 520),
-                                        (2024, 128, 2048, 256), (571, 128, 4096, 768), (382, 128, 4096, 768),
-                                        (284, 128, 4096, 768), (200, 128, 4096, 768)])
+# The kernel (single CTAs, or CTA pairs once the pair tiles fill the GPU) and the tile width
+# (tokens per tile, 64 .. 256) follow the shape; on a 148-SM B200 these shapes reach every width of
+# both: single 64 (the first three), 256, 224, 160, 128, 96, 192; pairs 224, 64, 96, 128, 160, 192,
+# 224, 256 (the 9B-shaped projection, 4096 tokens x 12,352 channels, takes pairs of 256).
+SHAPES = [(300, 256, 512, 264), (125, 128, 256, 0), (1, 64, 8, 8), (2024, 128, 2048, 256), (571, 128, 4096, 768),
+          (382, 128, 4096, 768), (284, 128, 4096, 768), (200, 128, 4096, 768), (321, 128, 4096, 2304),
+          (4096, 512, 1024, 520), (2206, 128, 256, 128), (3350, 128, 256, 128), (516, 128, 4096, 2176),
+          (516, 128, 4096, 3456), (659, 128, 4096, 3456), (763, 128, 4096, 3456), (893, 128, 4096, 3456)]
+
+
+@pytest.mark.parametrize("T,K,C,rest", SHAPES)
 def test_in_proj_conv_matches_matmul_then_conv(T, K, C, rest):
     x, w, cw = _case(T + K, T, K, C, rest)
     out = gdn.in_proj_conv(x, w, cw, C)
@@ -44,8 +50,10 @@ def test_in_proj_conv_matches_matmul_then_conv(T, K, C, rest):
         _close(out[:, :C], gdn.causal_conv1d(y[None, :, :C].contiguous(), cw)[0], max_ulps=2, frac=0.02)
 
 
-@pytest.mark.parametrize("lens,K,C,rest", [([70, 1, 129, 0, 100, 3], 192, 256, 72),
-                                           ([700, 2, 900, 0, 3, 419, 1], 128, 2048, 256)])
+@pytest.mark.parametrize("lens,K,C,rest", [([70, 1, 129, 0, 100, 3], 192, 256, 72),        # single CTAs
+                                           ([700, 2, 900, 0, 3, 419, 1], 128, 2048, 256),  # pairs, 160 tokens
+                                           ([1000, 1, 0, 700, 3, 502], 128, 256, 128),     # pairs, 64 tokens
+                                           ([400, 1, 0, 300, 192], 128, 4096, 3456)])      # pairs, 256 tokens
 def test_in_proj_conv_packed_sequences_and_conv_state(lens, K, C, rest):
     T = sum(lens)
     x, w, cw = _case(7, T, K, C, rest)
@@ -62,15 +70,15 @@ def test_in_proj_conv_packed_sequences_and_conv_state(lens, K, C, rest):
         _close(state[n], want)
 
 
-@pytest.mark.parametrize("T", [2, 700])
-def test_in_proj_conv_dense_conv_state(T):
-    x, w, cw = _case(11, T, 128, 512, 136)
-    out, state = gdn.in_proj_conv(x, w, cw, 512, conv_state=True)
+@pytest.mark.parametrize("T,C,rest", [(2, 512, 136), (700, 512, 136), (893, 4096, 3456)])
+def test_in_proj_conv_dense_conv_state(T, C, rest):
+    x, w, cw = _case(11, T, 128, C, rest)
+    out, state = gdn.in_proj_conv(x, w, cw, C, conv_state=True)
     y = x @ w.T
-    want = torch.zeros(1, 512, 4, dtype=torch.bfloat16, device="cuda")
-    want[0, :, 4 - min(4, T):] = y[-min(4, T):, :512].T
+    want = torch.zeros(1, C, 4, dtype=torch.bfloat16, device="cuda")
+    want[0, :, 4 - min(4, T):] = y[-min(4, T):, :C].T
     _close(state, want)
-    _close(out[:, 512:], y[:, 512:])
+    _close(out[:, C:], y[:, C:])
 
 
 def test_in_proj_conv_leaves_no_device_error():
