@@ -332,16 +332,17 @@ GDN_API int gdn_rotate_into_cache(const void* k, const void* v, const void* qm, 
 
 /*
  * The layer's merged input projection with the causal conv + SiLU in the GEMM's epilogue, on
- * tcgen05 (replaces in_proj_qkv / in_proj_z / in_proj_b / in_proj_a, model/model.py:458-461, as
- * the engine merges them, inference/engine.py:154-166, :374-375, followed by causal_conv1d,
- * :478-479). x: [tokens, hidden] bf16 (row stride x_stride); w: [out_channels, hidden] bf16, the
+ * tcgen05 (replaces in_proj_qkv / in_proj_z / in_proj_b / in_proj_a, model/model.py:459-462, which
+ * the engine runs as one merged GEMM on CUDA, inference/engine.py:155-166, :376, followed by
+ * causal_conv1d, model/model.py:470, :479). x: [tokens, hidden] bf16 (row stride x_stride); w: [out_channels, hidden] bf16, the
  * merged nn.Linear weight with the conv_channels qkv rows first (row stride w_stride); conv_w:
  * [conv_channels, 4] bf16. out: [tokens, out_channels] bf16 (row stride out_stride):
  * silu(conv(y)) for the first conv_channels columns and y for the rest, with y = x w^T accumulated
- * in fp32 and rounded to bf16 (the conv and SiLU round as gdn_conv1d_silu). With cu_seqlens
+ * in fp32 and rounded to bf16, the conv output rounded to bf16 before the SiLU (within one bf16 unit
+ * of gdn_conv1d_silu on y: fused multiply-adds and the hardware exponential). With cu_seqlens
  * (int32, [sequences + 1]) the conv restarts at every sequence; otherwise sequences = 1. conv_state
  * (optional, [sequences, conv_channels, 4] bf16) receives each sequence's last 4 pre-conv rows,
- * zero-padded in front for shorter sequences (the conv state the cache keeps, :468-469). hidden a
+ * zero-padded in front for shorter sequences (the conv state the cache keeps, :469, :478). hidden a
  * multiple of 64, channels multiples of 8, conv_kernel 4, rows 16-byte aligned.
  */
 GDN_API int gdn_in_proj_conv(const void* x, int64_t x_stride, const void* w, int64_t w_stride, const void* conv_w,

@@ -1,7 +1,8 @@
 // The gated-delta layer's merged input projection with the causal conv fused into the GEMM's
 // epilogue (tcgen05). The prefill branch of GatedDeltaNet.forward computes qkv = in_proj_qkv(x)
-// and, beside it, z, b and a (model/model.py:458-461; the engine merges the projections,
-// inference/engine.py:154-166, :374-375), then qkv = silu(causal_conv1d(qkv)) (:478-479). Here
+// and, beside it, z, b and a (model/model.py:459-462; on CUDA the engine runs the projections that
+// read one input as one GEMM, inference/engine.py:155-166, :376), then keeps the last pre-conv rows
+// as the conv state and applies qkv = silu(causal_conv1d(qkv)) (model/model.py:469-470, :478-479). Here
 // one call computes Y = X W^T for the merged weight W = [W_qkv; W_rest] ([N, K], nn.Linear
 // layout) and writes
 //   out[t, c] = silu(conv_c(Y_bf16[t-3..t, c]))   for c < C (the qkv channels),
@@ -11,7 +12,7 @@
 // exponential and reciprocal: within one bf16 unit of the conv kernel's exact rounding). With
 // cu_seqlens the window restarts at every sequence. Optionally the last `taps` pre-conv rows of
 // each sequence go to conv_tail [nseq, C, taps] (the conv state the cache keeps,
-// model/model.py:468-469).
+// model/model.py:469, :478).
 //
 // The product is computed transposed, Y^T = W X^T, so that a tile's accumulator holds 128
 // channels in the TMEM lanes and `bn` consecutive tokens in its columns: the thread that owns a
@@ -103,6 +104,21 @@ __device__ __forceinline__ void find_sequence(const int32_t* cu, int nseq, int t
 namespace gdn {
 namespace inproj {
 
+// Stores a lane's 16 values of one channel, tokens tb .. tb + 15 (column j of the tile first),
+// skipping the halo columns and the tokens past T unless the whole chunk is known to be inside.
+__device__ __forceinline__ void store_chunk(bf16* out_c, int64_t ldo, int tb, int j, int T, bool whole,
+                                            const float (&v)[kChunk]) {
+    bf16* q = out_c + (int64_t)tb * ldo;
+    if (whole) {
+#pragma unroll
+        for (int e = 0; e < kChunk; ++e) q[e * ldo] = __float2bfloat16_rn(v[e]);
+    } else {
+#pragma unroll
+        for (int e = 0; e < kChunk; ++e)
+            if (j + e >= kHalo && tb + e < T) q[e * ldo] = __float2bfloat16_rn(v[e]);
+    }
+}
+
 // Drains one warp's share of a finished accumulator: channel c (this lane's TMEM lane of quadrant
 // `acc`), columns col0 .. col0 + ncols - 1, where column j is token row0 + j. The window carries
 // the bf16-rounded pre-conv values of the three tokens before the current one; the drain of the
@@ -162,13 +178,10 @@ __device__ __forceinline__ void drain(const Params& p, uint32_t acc, int col0, i
 #pragma unroll
             for (int e = 0; e < kChunk; ++e) res[e] = silu_fast(pre[e]);
         }
-        if (in_n) {
-#pragma unroll
-            for (int e = 0; e < kChunk; ++e) {
-                const int t = tb + e;
-                if (j + e >= kHalo && t < p.T) out_c[(int64_t)t * p.ldo] = __float2bfloat16_rn(conv ? res[e] : y[e]);
-            }
-        }
+        // a chunk past the halo and inside the tokens stores without per-token checks (warp-uniform)
+        const bool whole = j >= kHalo && tb + kChunk <= p.T;
+        if (conv) store_chunk(out_c, p.ldo, tb, j, p.T, whole, res);
+        else if (in_n) store_chunk(out_c, p.ldo, tb, j, p.T, whole, y);
         if (conv && p.conv_tail) {  // the last four pre-conv tokens of each sequence (the cache's conv state)
 #pragma unroll
             for (int e = 0; e < kChunk; ++e) {
