@@ -350,6 +350,21 @@ GDN_API int gdn_in_proj_conv(const void* x, int64_t x_stride, const void* w, int
                              int64_t tokens, int64_t hidden, int64_t out_channels, int64_t conv_channels,
                              int64_t sequences, int64_t conv_kernel, void* stream);
 
+/* gdn_in_proj_conv with fp8 weights, the reference's FP8Linear (inference/fp8.py:62-148, 150-190):
+ * codes: [out_channels, hidden] e4m3 (row stride codes_stride bytes, a multiple of 16), w_scale:
+ * [out_channels] fp32, y = (x codes^T) * w_scale. As the reference computes it, the activation rows
+ * go to fp16 with a power-of-two scale per row (largest magnitude in [2^13, 2^14)), the codes to
+ * fp16 (exact), the products are fp16 x fp16 with fp32 accumulation, and y = (acc * row scale) *
+ * w_scale before the bf16 rounding; conv_channels = 0 gives the plain fp8 GEMM (an FP8Linear
+ * forward or the output projection). workspace: gdn_in_proj_fp8_workspace_size(tokens, hidden)
+ * bytes, 16-byte aligned (the fp16 rows and their scales). The other arguments as gdn_in_proj_conv. */
+GDN_API size_t gdn_in_proj_fp8_workspace_size(int64_t tokens, int64_t hidden);
+GDN_API int gdn_in_proj_conv_fp8(const void* x, int64_t x_stride, const void* codes, int64_t codes_stride,
+                                 const float* w_scale, const void* conv_w, const int32_t* cu_seqlens, void* out,
+                                 int64_t out_stride, void* conv_state, void* workspace, size_t workspace_bytes,
+                                 int64_t tokens, int64_t hidden, int64_t out_channels, int64_t conv_channels,
+                                 int64_t sequences, int64_t conv_kernel, void* stream);
+
 /*
  * Decode layer for one new token per row: conv step (+SiLU) over the pre-conv qkv, q/k L2
  * norm, gated delta rule step with the state updated in place, and the output-gated

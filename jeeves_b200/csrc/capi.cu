@@ -401,10 +401,10 @@ int gdn_rotate_into_cache(const void* k, const void* v, const void* qm, const vo
     return launch_rotate_into_cache(a, as_stream(stream));
 }
 
-int gdn_in_proj_conv(const void* x, int64_t x_stride, const void* w, int64_t w_stride, const void* conv_w,
-                     const int32_t* cu_seqlens, void* out, int64_t out_stride, void* conv_state, int64_t tokens,
-                     int64_t hidden, int64_t out_channels, int64_t conv_channels, int64_t sequences,
-                     int64_t conv_kernel, void* stream) {
+// The checks both forms of the merged projection share; GDN_OK lets the call go on (tokens > 0).
+static int in_proj_checks(const void* x, int64_t x_stride, const void* conv_w, const int32_t* cu_seqlens, void* out,
+                          int64_t out_stride, void* conv_state, int64_t tokens, int64_t hidden, int64_t out_channels,
+                          int64_t conv_channels, int64_t sequences, int64_t conv_kernel) {
     if (tokens < 0 || hidden <= 0 || out_channels <= 0 || conv_channels < 0 || conv_channels > out_channels)
         return GDN_ERR_SHAPE;
     if (hidden % 64 || out_channels % 8 || conv_channels % 8 || tokens > INT32_MAX - 256) return GDN_ERR_SHAPE;
@@ -412,11 +412,48 @@ int gdn_in_proj_conv(const void* x, int64_t x_stride, const void* w, int64_t w_s
     if (conv_kernel != 4) return GDN_ERR_UNSUPPORTED;
     if (cu_seqlens ? sequences < 1 : sequences != 1) return GDN_ERR_SHAPE;
     if (tokens == 0) return GDN_OK;
-    if (!x || !w || !out || (conv_channels > 0 && !conv_w)) return GDN_ERR_NULL;
-    if (!rows_aligned(x, 2, x_stride, 0, 0) || !rows_aligned(w, 2, w_stride, 0, 0) ||
-        !rows_aligned(out, 2, out_stride, 0, 0) || (conv_w && !aligned16(conv_w)) ||
-        (conv_state && !aligned16(conv_state)))
+    if (!x || !out || (conv_channels > 0 && !conv_w)) return GDN_ERR_NULL;
+    if (!rows_aligned(x, 2, x_stride, 0, 0) || !rows_aligned(out, 2, out_stride, 0, 0) ||
+        (conv_w && !aligned16(conv_w)) || (conv_state && !aligned16(conv_state)))
         return GDN_ERR_ALIGN;
+    return GDN_OK;
+}
+
+size_t gdn_in_proj_fp8_workspace_size(int64_t tokens, int64_t hidden) {
+    if (tokens <= 0 || hidden <= 0) return 0;
+    return in_proj_fp8_workspace_bytes(tokens, hidden);
+}
+
+int gdn_in_proj_conv_fp8(const void* x, int64_t x_stride, const void* codes, int64_t codes_stride,
+                         const float* w_scale, const void* conv_w, const int32_t* cu_seqlens, void* out,
+                         int64_t out_stride, void* conv_state, void* workspace, size_t workspace_bytes,
+                         int64_t tokens, int64_t hidden, int64_t out_channels, int64_t conv_channels,
+                         int64_t sequences, int64_t conv_kernel, void* stream) {
+    const int st = in_proj_checks(x, x_stride, conv_w, cu_seqlens, out, out_stride, conv_state, tokens, hidden,
+                                  out_channels, conv_channels, sequences, conv_kernel);
+    if (st != GDN_OK || tokens == 0) return st;
+    if (!codes || !w_scale) return GDN_ERR_NULL;
+    if (!aligned16(codes) || codes_stride < hidden || codes_stride % 16) return GDN_ERR_ALIGN;
+    if (!workspace || workspace_bytes < in_proj_fp8_workspace_bytes(tokens, hidden)) return GDN_ERR_WORKSPACE;
+    if (!aligned16(workspace)) return GDN_ERR_ALIGN;
+    InProjArgs a{};
+    a.x = x; a.ldx = x_stride; a.conv_w = conv_w; a.cu_seqlens = cu_seqlens;
+    a.out = out; a.ldo = out_stride; a.conv_tail = conv_channels > 0 ? conv_state : nullptr;
+    a.T = tokens; a.K = hidden; a.N = out_channels; a.C = conv_channels; a.nseq = sequences;
+    a.codes = codes; a.ldc = codes_stride; a.w_scale = w_scale; a.workspace = workspace;
+    a.workspace_bytes = workspace_bytes;
+    return launch_in_proj_conv(a, as_stream(stream));
+}
+
+int gdn_in_proj_conv(const void* x, int64_t x_stride, const void* w, int64_t w_stride, const void* conv_w,
+                     const int32_t* cu_seqlens, void* out, int64_t out_stride, void* conv_state, int64_t tokens,
+                     int64_t hidden, int64_t out_channels, int64_t conv_channels, int64_t sequences,
+                     int64_t conv_kernel, void* stream) {
+    const int st = in_proj_checks(x, x_stride, conv_w, cu_seqlens, out, out_stride, conv_state, tokens, hidden,
+                                  out_channels, conv_channels, sequences, conv_kernel);
+    if (st != GDN_OK || tokens == 0) return st;
+    if (!w) return GDN_ERR_NULL;
+    if (!rows_aligned(w, 2, w_stride, 0, 0)) return GDN_ERR_ALIGN;
     InProjArgs a{};
     a.x = x; a.ldx = x_stride; a.w = w; a.ldw = w_stride; a.conv_w = conv_w; a.cu_seqlens = cu_seqlens;
     a.out = out; a.ldo = out_stride; a.conv_tail = conv_channels > 0 ? conv_state : nullptr;

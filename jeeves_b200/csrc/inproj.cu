@@ -52,6 +52,8 @@ constexpr uint32_t kSmemBytes = kStages * kStageBytes + 1024;
 constexpr int kEpilogueWarps = 8;
 constexpr int kProducerWarp = 8, kMmaWarp = 9;
 constexpr int kThreads = 32 * (kEpilogueWarps + 2);
+constexpr int kConvertWarps = 2;  // fp8 weights: warps 10-11 turn e4m3 codes into the fp16 operand
+constexpr int kFp8Threads = kThreads + 32 * kConvertWarps;
 constexpr uint32_t kAccCols = 256;       // columns of one accumulator; two of them fill TMEM
 constexpr int kChunk = 16;               // accumulator columns per TMEM load
 
@@ -66,6 +68,13 @@ struct Params {
     int T, N, C, K, nseq;
     int bn;              // tokens per tile, a multiple of 32 in [64, 256]
     int tiles_t, tiles;  // token tiles, all tiles
+    // fp8 weights (the single-CTA kernel with FP8 = true): e4m3 codes [N, K] (row stride ldc
+    // bytes) with one fp32 scale per row, and the activations as fp16 rows with a power-of-two
+    // scale per row (tm_x then maps those fp16 rows)
+    const uint8_t* codes;
+    int64_t ldc;
+    const float* w_scale;
+    const float* row_scale;
 };
 
 struct Shared {
@@ -123,9 +132,11 @@ __device__ __forceinline__ void store_chunk(bf16* out_c, int64_t ldo, int tb, in
 // `acc`), columns col0 .. col0 + ncols - 1, where column j is token row0 + j. The window carries
 // the bf16-rounded pre-conv values of the three tokens before the current one; the drain of the
 // second half of the columns starts it from the last three columns of the first half.
-template <bool VARLEN>
+template <bool VARLEN, bool SCALED = false>
 __device__ __forceinline__ void drain(const Params& p, uint32_t acc, int col0, int ncols, int row0, int c, int lane) {
     const bool in_n = c < p.N, conv = c < p.C;
+    // fp8 weights: y = (acc x row scale) x weight scale, the order of the reference's fp8 GEMM
+    const float ws = SCALED && in_n ? __ldg(p.w_scale + c) : 1.f;
     float w0 = 0.f, w1 = 0.f, w2 = 0.f, w3 = 0.f;
     if (conv) {
         const uint2 raw = __ldg(reinterpret_cast<const uint2*>(p.conv_w + (int64_t)c * 4));
@@ -139,6 +150,12 @@ __device__ __forceinline__ void drain(const Params& p, uint32_t acc, int col0, i
     if (col0 > 0) {
         float v[kChunk];
         tmem_ld16_wait(acc + col0 - kChunk, v);
+        if (SCALED) {
+            const int t0 = row0 + col0 - kChunk;
+#pragma unroll
+            for (int e = kChunk - 3; e < kChunk; ++e)
+                v[e] = v[e] * __ldg(p.row_scale + min(max(t0 + e, 0), p.T - 1)) * ws;
+        }
         x1 = round_bf16(v[kChunk - 3]);
         x2 = round_bf16(v[kChunk - 2]);
         x3 = round_bf16(v[kChunk - 1]);
@@ -157,6 +174,7 @@ __device__ __forceinline__ void drain(const Params& p, uint32_t acc, int col0, i
         float y[kChunk], pre[kChunk], res[kChunk];
 #pragma unroll
         for (int e = 0; e < kChunk; ++e) {
+            if (SCALED) v[e] = v[e] * __ldg(p.row_scale + min(max(tb + e, 0), p.T - 1)) * ws;
             y[e] = round_bf16(v[e]);
             float a1 = x1, a2 = x2, a3 = x3;
             if (VARLEN) {  // the window restarts at the token's sequence start
@@ -201,7 +219,20 @@ __device__ __forceinline__ void drain(const Params& p, uint32_t acc, int col0, i
 namespace gdn {
 namespace inproj {
 
-__global__ void __launch_bounds__(kThreads, 1) in_proj_conv_kernel(const __grid_constant__ Params p) {
+// Two e4m3 codes (the low 16 bits) as an fp16 pair: exact, every e4m3 value is an fp16 value.
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t codes) {
+    uint32_t r;
+    asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"((unsigned short)(codes & 0xFFFFu)));
+    return r;
+}
+
+// The single-CTA kernel. FP8: the weight operand comes from e4m3 codes, which warps 10-11 read
+// from global memory (a stage's 128 rows x 64 codes, one 16-byte load per thread per 16 codes,
+// the next stage's loads in flight while this one converts) and write as fp16 in the 128-byte
+// swizzled layout that TMA would have produced; the products are fp16 x fp16 (kind::f16) against
+// the fp16 activation rows, and the drain applies the row and weight scales.
+template <bool FP8>
+__global__ void __launch_bounds__(FP8 ? kFp8Threads : kThreads, 1) in_proj_conv_kernel(const __grid_constant__ Params p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = align1024(smem_raw);
     __shared__ Shared sh;
@@ -210,7 +241,7 @@ __global__ void __launch_bounds__(kThreads, 1) in_proj_conv_kernel(const __grid_
 
     if (tid == 0) {
         for (int s = 0; s < kStages; ++s) {
-            mbar_init(&sh.full[s], 1);
+            mbar_init(&sh.full[s], FP8 ? 1 + kConvertWarps : 1);  // the producer (+ the converters)
             mbar_init(&sh.empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
@@ -220,7 +251,7 @@ __global__ void __launch_bounds__(kThreads, 1) in_proj_conv_kernel(const __grid_
         mbar_init(&sh.mma_done, 1);
         sh.abort = 0;
         fence_mbar_init();
-        tma_prefetch_map(&p.tm_w);
+        if (!FP8) tma_prefetch_map(&p.tm_w);
         tma_prefetch_map(&p.tm_x);
     }
     if (warp == 0) {
@@ -235,7 +266,7 @@ __global__ void __launch_bounds__(kThreads, 1) in_proj_conv_kernel(const __grid_
     if (warp == kProducerWarp) {
         // ============================== producer ==============================
         if (lane == 0) {
-            const uint32_t bytes = kAStage + (uint32_t)p.bn * 128;
+            const uint32_t bytes = (FP8 ? 0u : kAStage) + (uint32_t)p.bn * 128;
             int it = 0;
             bool ok = true;
             for (int tile = blockIdx.x; ok && tile < p.tiles; tile += gridDim.x) {
@@ -251,7 +282,7 @@ __global__ void __launch_bounds__(kThreads, 1) in_proj_conv_kernel(const __grid_
                     }
                     uint8_t* st = sm + s * kStageBytes;
                     mbar_arrive_expect_tx(&sh.full[s], bytes);
-                    tma_load_2d(st, &p.tm_w, &sh.full[s], kb * kBK, n0);
+                    if (!FP8) tma_load_2d(st, &p.tm_w, &sh.full[s], kb * kBK, n0);
                     tma_load_2d(st + kAStage, &p.tm_x, &sh.full[s], kb * kBK, row0);
                 }
             }
@@ -262,7 +293,7 @@ __global__ void __launch_bounds__(kThreads, 1) in_proj_conv_kernel(const __grid_
     } else if (warp == kMmaWarp) {
         // ============================== MMA issuer ==============================
         if (lane == 0) {
-            const uint32_t idesc = make_idesc(kBM, (uint32_t)p.bn, kFmtBF16, false, false);
+            const uint32_t idesc = make_idesc(kBM, (uint32_t)p.bn, FP8 ? kFmtF16 : kFmtBF16, false, false);
             int it = 0, lt = 0;
             bool ok = true;
             for (int tile = blockIdx.x; ok && tile < p.tiles; tile += gridDim.x, ++lt) {
@@ -295,7 +326,7 @@ __global__ void __launch_bounds__(kThreads, 1) in_proj_conv_kernel(const __grid_
             mma_commit(&sh.mma_done);
             mbar_wait(&sh.mma_done, 0, kSiteMma);  // every product issued is done before TMEM goes away
         }
-    } else {
+    } else if (warp < kEpilogueWarps) {
         // ================================ epilogue ================================
         const int q = warp & 3, half = p.bn >> 1, col0 = (warp >> 2) * half;
         int lt = 0;
@@ -311,11 +342,56 @@ __global__ void __launch_bounds__(kThreads, 1) in_proj_conv_kernel(const __grid_
             const int row0 = (tile % p.tiles_t) * (p.bn - kHalo) - kHalo;
             const uint32_t acc = tb + b * kAccCols + ((uint32_t)(32 * q) << 16);
             const int c = n0 + 32 * q + lane;
-            if (p.cu_seqlens) drain<true>(p, acc, col0, half, row0, c, lane);
-            else drain<false>(p, acc, col0, half, row0, c, lane);
+            if (p.cu_seqlens) drain<true, FP8>(p, acc, col0, half, row0, c, lane);
+            else drain<false, FP8>(p, acc, col0, half, row0, c, lane);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&sh.acc_empty[b]);  // the MMA may overwrite this accumulator
+        }
+    } else if constexpr (FP8) {
+        // ============================ e4m3 -> fp16 converters ============================
+        constexpr int kPer = kBM * kBK / 16 / (32 * kConvertWarps);  // 16-code pieces per thread: 8
+        const int ct = tid - 32 * kEpilogueWarps - 64;                // 0 .. 63
+        const int my_tiles = blockIdx.x < p.tiles ? (p.tiles - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+        const int total = my_tiles * kblocks;
+        uint4 cur[kPer], nxt[kPer];
+        auto load = [&](int it, uint4 (&r)[kPer]) {
+            const int tile = blockIdx.x + (it / kblocks) * gridDim.x, kb = it % kblocks;
+            const int n0 = (tile / p.tiles_t) * kBM;
+#pragma unroll
+            for (int i = 0; i < kPer; ++i) {
+                const int id = ct + 64 * i, n = n0 + (id >> 2);
+                r[i] = n < p.N ? __ldg(reinterpret_cast<const uint4*>(p.codes + (int64_t)n * p.ldc + kb * kBK +
+                                                                      (id & 3) * 16))
+                               : make_uint4(0u, 0u, 0u, 0u);
+            }
+        };
+        if (total > 0) load(0, cur);
+        for (int it = 0; it < total; ++it) {
+            if (it + 1 < total) load(it + 1, nxt);
+            const int s = it % kStages;
+            if (it >= kStages && !mbar_wait_or_abort(&sh.empty[s], (uint32_t)(it / kStages - 1) & 1, kSiteTmaLoad,
+                                                     &sh.abort, false)) {
+                atomicExch(&sh.abort, 1);
+                break;
+            }
+            uint8_t* a_tile = sm + s * kStageBytes;
+#pragma unroll
+            for (int i = 0; i < kPer; ++i) {
+                const int id = ct + 64 * i, row = id >> 2, part = id & 3;
+                const uint4 w = cur[i];
+                const uint4 lo = make_uint4(e4m3x2_to_f16x2(w.x), e4m3x2_to_f16x2(w.x >> 16), e4m3x2_to_f16x2(w.y),
+                                            e4m3x2_to_f16x2(w.y >> 16));
+                const uint4 hi = make_uint4(e4m3x2_to_f16x2(w.z), e4m3x2_to_f16x2(w.z >> 16), e4m3x2_to_f16x2(w.w),
+                                            e4m3x2_to_f16x2(w.w >> 16));
+                *reinterpret_cast<uint4*>(a_tile + sw128(row, 2 * part)) = lo;
+                *reinterpret_cast<uint4*>(a_tile + sw128(row, 2 * part + 1)) = hi;
+            }
+            fence_async_smem();  // the generic-proxy stores become visible to the tensor cores
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sh.full[s]);
+#pragma unroll
+            for (int i = 0; i < kPer; ++i) cur[i] = nxt[i];
         }
     }
     tc_fence_before();
@@ -324,6 +400,46 @@ __global__ void __launch_bounds__(kThreads, 1) in_proj_conv_kernel(const __grid_
         tc_fence_after();
         tmem_dealloc(tb, 2 * kAccCols);
     }
+}
+
+// Activation rows for the fp8 GEMM: each bf16 row scaled by a power of two that puts its largest
+// magnitude in [2^13, 2^14) (the exponent at most 126 down), converted to fp16, with the scale
+// kept per row; the scaled bf16 values are exact in fp16 down to 2^-30 of the row's largest
+// (the activation conversion of inference/fp8.py:30-52, FP16_TOP_EXPONENT = 13).
+__global__ void __launch_bounds__(256) fp16_rows_kernel(const bf16* __restrict__ x, int64_t ldx, int K,
+                                                        __half* __restrict__ xh, float* __restrict__ row_scale) {
+    __shared__ float red[8];
+    const int64_t row = blockIdx.x;
+    const bf16* xr = x + row * ldx;
+    float amax = 0.f;
+    for (int k = threadIdx.x * 8; k < K; k += 256 * 8) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(xr + k);
+        const bf16* h = reinterpret_cast<const bf16*>(&raw);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(to_f32(h[e])));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    amax = red[0];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) amax = fmaxf(amax, red[w]);
+    const int exponent = (int)((__float_as_uint(amax) >> 23) & 0xFFu) - 127;
+    const int shift = max(exponent - 13, -126);
+    const float down = __uint_as_float((uint32_t)(127 - shift) << 23);  // 2^-shift
+    __half* out = xh + row * K;
+    for (int k = threadIdx.x * 8; k < K; k += 256 * 8) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(xr + k);
+        const bf16* h = reinterpret_cast<const bf16*>(&raw);
+        uint4 o;
+        __half2* o2 = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+            o2[e] = __halves2half2(__float2half_rn(to_f32(h[2 * e]) * down), __float2half_rn(to_f32(h[2 * e + 1]) * down));
+        *reinterpret_cast<uint4*>(out + k) = o;
+    }
+    if (threadIdx.x == 0) row_scale[row] = __uint_as_float((uint32_t)(shift + 127) << 23);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -490,15 +606,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
 }
 
-// 2-D map over a [rows, K] bf16 matrix with row stride ld (elements), box (64, box_rows).
-static bool make_map2(CUtensorMap* map, const void* base, int64_t rows, int64_t K, int64_t ld, uint32_t box_rows) {
+// 2-D map over a [rows, K] 16-bit matrix (bf16, or fp16 for the fp8 path's activation rows) with
+// row stride ld (elements), box (64, box_rows).
+static bool make_map2(CUtensorMap* map, const void* base, int64_t rows, int64_t K, int64_t ld, uint32_t box_rows,
+                      CUtensorMapDataType type = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16) {
     EncodeTiledFn enc = encode_fn();
     if (!enc) return false;
     cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
     cuuint32_t box[2] = {64, box_rows};
     cuuint32_t estr[2] = {1, 1};
-    return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+    return enc(map, type, 2, const_cast<void*>(base), dims, strides, box, estr,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -527,6 +645,10 @@ static int choose_bn(int64_t T, int64_t N, int ctas, int tile_channels) {
 
 }  // namespace inproj
 
+size_t in_proj_fp8_workspace_bytes(int64_t T, int64_t K) {
+    return ((size_t)T * K * 2 + 255) / 256 * 256 + (size_t)T * 4;
+}
+
 int launch_in_proj_conv(const InProjArgs& a, cudaStream_t s) {
     using namespace inproj;
     if (a.T == 0 || a.N == 0) return GDN_OK;
@@ -535,25 +657,41 @@ int launch_in_proj_conv(const InProjArgs& a, cudaStream_t s) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return GDN_ERR_LAUNCH;
     if (!ready[dev]) {
-        if (cudaFuncSetAttribute(in_proj_conv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes) !=
-                cudaSuccess ||
+        if (cudaFuncSetAttribute(in_proj_conv_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kSmemBytes) != cudaSuccess ||
+            cudaFuncSetAttribute(in_proj_conv_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kSmemBytes) != cudaSuccess ||
             cudaFuncSetAttribute(in_proj_conv_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)kPairSmemBytes) != cudaSuccess ||
             cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms[dev] < 1)
             return GDN_ERR_LAUNCH;
         ready[dev] = true;
     }
-    // CTA pairs when the pair tiles occupy every pair of SMs; single CTAs for smaller problems
+    // bf16 weights: CTA pairs when the pair tiles occupy every pair of SMs, single CTAs for smaller
+    // problems. fp8 weights: single CTAs (the converters feed one CTA's operand).
+    const bool fp8 = a.codes != nullptr;
     const int pairs = sms[dev] / 2;
     const int bn_pair = choose_bn(a.T, a.N, pairs, kPairBM);
     const int64_t pair_tiles = (a.T + bn_pair - kHalo - 1) / (bn_pair - kHalo) * ((a.N + kPairBM - 1) / kPairBM);
-    const bool use_pair = pairs >= 1 && pair_tiles >= pairs;
+    const bool use_pair = !fp8 && pairs >= 1 && pair_tiles >= pairs;
     Params p;
     memset(&p, 0, sizeof(p));
     p.bn = use_pair ? bn_pair : choose_bn(a.T, a.N, sms[dev], kBM);
-    if (!make_map2(&p.tm_w, a.w, a.N, a.K, a.ldw, kBM) ||
-        !make_map2(&p.tm_x, a.x, a.T, a.K, a.ldx, (uint32_t)(use_pair ? p.bn / 2 : p.bn)))
+    __half* xh = nullptr;
+    if (fp8) {
+        if (!a.workspace || a.workspace_bytes < in_proj_fp8_workspace_bytes(a.T, a.K)) return GDN_ERR_WORKSPACE;
+        xh = static_cast<__half*>(a.workspace);
+        p.codes = static_cast<const uint8_t*>(a.codes);
+        p.ldc = a.ldc;
+        p.w_scale = a.w_scale;
+        p.row_scale = reinterpret_cast<const float*>(static_cast<uint8_t*>(a.workspace) +
+                                                     ((size_t)a.T * a.K * 2 + 255) / 256 * 256);
+        if (!make_map2(&p.tm_x, xh, a.T, a.K, a.K, (uint32_t)p.bn, CU_TENSOR_MAP_DATA_TYPE_FLOAT16))
+            return GDN_ERR_LAUNCH;
+    } else if (!make_map2(&p.tm_w, a.w, a.N, a.K, a.ldw, kBM) ||
+               !make_map2(&p.tm_x, a.x, a.T, a.K, a.ldx, (uint32_t)(use_pair ? p.bn / 2 : p.bn))) {
         return GDN_ERR_LAUNCH;
+    }
     p.conv_w = static_cast<const bf16*>(a.conv_w);
     p.cu_seqlens = a.cu_seqlens;
     p.out = static_cast<bf16*>(a.out);
@@ -573,12 +711,17 @@ int launch_in_proj_conv(const InProjArgs& a, cudaStream_t s) {
     if (a.conv_tail &&
         cudaMemsetAsync(a.conv_tail, 0, (size_t)a.nseq * a.C * 4 * sizeof(bf16), s) != cudaSuccess)
         return GDN_ERR_LAUNCH;
-    if (use_pair) {
+    if (fp8) {
+        fp16_rows_kernel<<<(unsigned)a.T, 256, 0, s>>>(static_cast<const bf16*>(a.x), a.ldx, (int)a.K, xh,
+                                                         const_cast<float*>(p.row_scale));
+        const int grid = (int)(tiles < sms[dev] ? tiles : sms[dev]);
+        in_proj_conv_kernel<true><<<grid, kFp8Threads, kSmemBytes, s>>>(p);
+    } else if (use_pair) {
         const int grid = 2 * (int)(tiles < pairs ? tiles : pairs);
         in_proj_conv_pair_kernel<<<grid, kThreads, kPairSmemBytes, s>>>(p);
     } else {
         const int grid = (int)(tiles < sms[dev] ? tiles : sms[dev]);
-        in_proj_conv_kernel<<<grid, kThreads, kSmemBytes, s>>>(p);
+        in_proj_conv_kernel<false><<<grid, kThreads, kSmemBytes, s>>>(p);
     }
     return launch_status();
 }

@@ -161,8 +161,16 @@ struct InProjArgs {
     int64_t ldo;
     void* conv_tail;
     int64_t T, K, N, C, nseq;
+    // fp8 weights (codes non-null): e4m3 codes [N, K] with row stride ldc bytes, one fp32 scale
+    // per row, and a workspace of in_proj_fp8_workspace_bytes for the fp16 activation rows
+    const void* codes;
+    int64_t ldc;
+    const float* w_scale;
+    void* workspace;
+    size_t workspace_bytes;
 };
 int launch_in_proj_conv(const InProjArgs& a, cudaStream_t s);
+size_t in_proj_fp8_workspace_bytes(int64_t T, int64_t K);
 
 // Runs a bounded device wait that is meant to run out after `limit_cycles` (probe.cu).
 int launch_bounded_wait_probe(int64_t limit_cycles, cudaStream_t s);

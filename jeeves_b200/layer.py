@@ -83,15 +83,21 @@ def decode_layer_step(qkv, conv_state, conv_weight, g, beta, state, z, norm_weig
     return out
 
 
-def in_proj_conv(x, weight, conv_weight, conv_channels: int, cu_seqlens=None, conv_state: bool = False):
+def in_proj_conv(x, weight, conv_weight, conv_channels: int, cu_seqlens=None, conv_state: bool = False,
+                 weight_scale=None):
     """The merged input projection of a gated-delta layer with the causal conv + SiLU fused into the
     GEMM: ``y = x @ weight.T`` (bf16, fp32 accumulation), then ``silu(causal_conv1d)`` over the first
     ``conv_channels`` columns (the qkv channels; ``weight`` holds their rows first, then z, b, a).
     x ``[T, hidden]`` or ``[1, T, hidden]`` bf16; conv_weight ``[conv_channels, 4]`` (or ``[C, 1,
     4]``). Returns ``out [.., T, N]``, and with ``conv_state`` also the last 4 pre-conv rows of
-    every sequence ``[sequences, conv_channels, 4]`` (the cache's conv state)."""
+    every sequence ``[sequences, conv_channels, 4]`` (the cache's conv state).
+
+    ``weight`` may be fp8 (``torch.float8_e4m3fn`` codes with ``weight_scale`` [N] fp32, the
+    reference's ``FP8Linear`` buffers): then ``y = (x @ codes.T) * weight_scale`` computed as
+    ``inference/fp8.py`` does (fp16 activation rows with a power-of-two scale per row, fp16 codes,
+    fp32 accumulation)."""
     what = "in_proj_conv"
-    _require_cuda(what, x, weight, conv_weight, cu_seqlens)
+    _require_cuda(what, x, weight, conv_weight, cu_seqlens, weight_scale)
     lead = x.shape[:-1]
     x2 = x.reshape(-1, x.shape[-1])
     if x2.stride(-1) != 1:
@@ -100,11 +106,19 @@ def in_proj_conv(x, weight, conv_weight, conv_channels: int, cu_seqlens=None, co
     N = weight.shape[0]
     if weight.dim() != 2 or weight.shape[1] != K:
         raise ValueError(f"weight: expected [N, {K}], got {tuple(weight.shape)}")
-    if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16 or conv_weight.dtype != torch.bfloat16:
-        raise ValueError(f"x, weight, conv_weight: expected bfloat16, got {x.dtype}, {weight.dtype}, {conv_weight.dtype}")
-    cw = conv_weight.reshape(conv_channels, -1).contiguous()
-    if cw.shape[1] != 4:
-        raise ValueError(f"conv_weight: expected {conv_channels} channels of 4 taps, got {tuple(conv_weight.shape)}")
+    fp8 = weight.dtype == torch.float8_e4m3fn
+    if x.dtype != torch.bfloat16 or not (fp8 or weight.dtype == torch.bfloat16):
+        raise ValueError(f"x, weight: expected bfloat16 and bfloat16 or float8_e4m3fn, got {x.dtype}, {weight.dtype}")
+    if fp8 and (weight_scale is None or weight_scale.dtype != torch.float32 or weight_scale.numel() != N):
+        raise ValueError(f"weight_scale: expected {N} float32 row scales for an fp8 weight")
+    if conv_channels:
+        if conv_weight is None or conv_weight.dtype != torch.bfloat16:
+            raise ValueError("conv_weight: expected bfloat16")
+        cw = conv_weight.reshape(conv_channels, -1).contiguous()
+        if cw.shape[1] != 4:
+            raise ValueError(f"conv_weight: expected {conv_channels} channels of 4 taps, got {tuple(conv_weight.shape)}")
+    else:
+        cw = None
     w = weight if weight.stride(-1) == 1 else weight.contiguous()
     cu = None
     seqs = 1
@@ -113,8 +127,26 @@ def in_proj_conv(x, weight, conv_weight, conv_channels: int, cu_seqlens=None, co
         seqs = cu.numel() - 1
     out = torch.empty(*lead, N, dtype=torch.bfloat16, device=x.device)
     state = torch.empty(seqs, conv_channels, 4, dtype=torch.bfloat16, device=x.device) if conv_state else None
-    status = _lib.load().gdn_in_proj_conv(
-        x2.data_ptr(), x2.stride(0), w.data_ptr(), w.stride(0), cw.data_ptr(), None if cu is None else cu.data_ptr(),
-        out.data_ptr(), N, None if state is None else state.data_ptr(), T, K, N, conv_channels, seqs, 4, _stream())
+    lib = _lib.load()
+    common = (None if cw is None else cw.data_ptr(), None if cu is None else cu.data_ptr(), out.data_ptr(), N,
+              None if state is None else state.data_ptr())
+    if fp8:
+        ws_bytes = lib.gdn_in_proj_fp8_workspace_size(T, K)
+        ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=x.device)
+        scale = weight_scale.contiguous()
+        status = lib.gdn_in_proj_conv_fp8(x2.data_ptr(), x2.stride(0), w.data_ptr(), w.stride(0), scale.data_ptr(),
+                                          *common, ws.data_ptr(), ws_bytes, T, K, N, conv_channels, seqs, 4, _stream())
+    else:
+        status = lib.gdn_in_proj_conv(x2.data_ptr(), x2.stride(0), w.data_ptr(), w.stride(0), *common, T, K, N,
+                                      conv_channels, seqs, 4, _stream())
     _lib.check(status, what)
     return (out, state) if conv_state else out
+
+
+def fp8_linear(x, weight, scale):
+    """The reference's fp8 GEMM (``fp8_matmul`` / ``FP8Linear.forward``, inference/fp8.py:112-148,
+    :177-184): x ``[.., K]`` (cast to bf16) times e4m3 codes ``[N, K]`` with fp32 row scales
+    ``[N]`` -> bf16 ``[.., N]``, on the tcgen05 kernel without a conv."""
+    shape = x.shape
+    y = in_proj_conv(x.reshape(-1, shape[-1]).to(torch.bfloat16), weight, None, 0, weight_scale=scale)
+    return y.view(*shape[:-1], weight.shape[0])
