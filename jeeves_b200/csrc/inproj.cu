@@ -52,13 +52,18 @@ constexpr uint32_t kSmemBytes = kStages * kStageBytes + 1024;
 constexpr int kEpilogueWarps = 8;
 constexpr int kProducerWarp = 8, kMmaWarp = 9;
 constexpr int kThreads = 32 * (kEpilogueWarps + 2);
-constexpr int kConvertWarps = 2;  // fp8 weights: warps 10-11 turn e4m3 codes into the fp16 operand
+constexpr int kConvertWarps = 4;  // fp8 weights: warps 10-13 turn e4m3 codes into the fp16 operand
 constexpr int kFp8Threads = kThreads + 32 * kConvertWarps;
+// fp8 stages: the fp16 weight operand (16 KB), the activation rows (up to 32 KB), the raw codes
+// that TMA brings (128 rows x 64 codes, 8 KB)
+constexpr uint32_t kRawStage = kBM * kBK;
+constexpr uint32_t kFp8StageBytes = kStageBytes + kRawStage;
+constexpr uint32_t kFp8SmemBytes = kStages * kFp8StageBytes + 1024;
 constexpr uint32_t kAccCols = 256;       // columns of one accumulator; two of them fill TMEM
 constexpr int kChunk = 16;               // accumulator columns per TMEM load
 
 struct Params {
-    CUtensorMap tm_w;  // 2-D (K, N), box (64, 128)
+    CUtensorMap tm_w;  // 2-D (K, N), box (64, 128); fp8: the codes, uint8, no swizzle
     CUtensorMap tm_x;  // 2-D (K, T), box (64, bn)
     const bf16* conv_w;  // [C, 4]
     const int32_t* cu_seqlens;  // [nseq + 1] or null (one sequence of T tokens)
@@ -79,6 +84,7 @@ struct Params {
 
 struct Shared {
     uint64_t full[kStages], empty[kStages], acc_full[2], acc_empty[2], mma_done;
+    uint64_t codes_full[kStages];  // fp8: the raw codes of a stage have landed
     uint32_t tmem_base;
     int abort;
 };
@@ -226,15 +232,15 @@ __device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t codes) {
     return r;
 }
 
-// The single-CTA kernel. FP8: the weight operand comes from e4m3 codes, which warps 10-11 read
-// from global memory (a stage's 128 rows x 64 codes, one 16-byte load per thread per 16 codes,
-// the next stage's loads in flight while this one converts) and write as fp16 in the 128-byte
-// swizzled layout that TMA would have produced; the products are fp16 x fp16 (kind::f16) against
-// the fp16 activation rows, and the drain applies the row and weight scales.
+// The single-CTA kernel. FP8: the weight operand comes from e4m3 codes, which TMA brings into a
+// raw area of each stage (128 rows x 64 codes) and warps 10-13 convert to fp16 in the 128-byte
+// swizzled layout that TMA would have produced for bf16; the products are fp16 x fp16 (kind::f16)
+// against the fp16 activation rows, and the drain applies the row and weight scales.
 template <bool FP8>
 __global__ void __launch_bounds__(FP8 ? kFp8Threads : kThreads, 1) in_proj_conv_kernel(const __grid_constant__ Params p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = align1024(smem_raw);
+    constexpr uint32_t kStride = FP8 ? kFp8StageBytes : kStageBytes;
     __shared__ Shared sh;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int kblocks = p.K / kBK;
@@ -243,6 +249,7 @@ __global__ void __launch_bounds__(FP8 ? kFp8Threads : kThreads, 1) in_proj_conv_
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&sh.full[s], FP8 ? 1 + kConvertWarps : 1);  // the producer (+ the converters)
             mbar_init(&sh.empty[s], 1);
+            mbar_init(&sh.codes_full[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&sh.acc_full[b], 1);
@@ -251,7 +258,7 @@ __global__ void __launch_bounds__(FP8 ? kFp8Threads : kThreads, 1) in_proj_conv_
         mbar_init(&sh.mma_done, 1);
         sh.abort = 0;
         fence_mbar_init();
-        if (!FP8) tma_prefetch_map(&p.tm_w);
+        tma_prefetch_map(&p.tm_w);
         tma_prefetch_map(&p.tm_x);
     }
     if (warp == 0) {
@@ -280,15 +287,22 @@ __global__ void __launch_bounds__(FP8 ? kFp8Threads : kThreads, 1) in_proj_conv_
                         ok = false;
                         break;
                     }
-                    uint8_t* st = sm + s * kStageBytes;
+                    uint8_t* st = sm + s * kStride;
                     mbar_arrive_expect_tx(&sh.full[s], bytes);
-                    if (!FP8) tma_load_2d(st, &p.tm_w, &sh.full[s], kb * kBK, n0);
+                    if (FP8) {
+                        mbar_arrive_expect_tx(&sh.codes_full[s], kRawStage);
+                        tma_load_2d(st + kStageBytes, &p.tm_w, &sh.codes_full[s], kb * kBK, n0);
+                    } else {
+                        tma_load_2d(st, &p.tm_w, &sh.full[s], kb * kBK, n0);
+                    }
                     tma_load_2d(st + kAStage, &p.tm_x, &sh.full[s], kb * kBK, row0);
                 }
             }
             // the copies in flight land before the CTA's shared memory can go away
-            for (int i = it > kStages ? it - kStages : 0; i < it; ++i)
+            for (int i = it > kStages ? it - kStages : 0; i < it; ++i) {
+                if (FP8) mbar_wait(&sh.codes_full[i % kStages], (uint32_t)(i / kStages) & 1, kSiteDrain);
                 mbar_wait(&sh.full[i % kStages], (uint32_t)(i / kStages) & 1, kSiteDrain);
+            }
         }
     } else if (warp == kMmaWarp) {
         // ============================== MMA issuer ==============================
@@ -314,7 +328,7 @@ __global__ void __launch_bounds__(FP8 ? kFp8Threads : kThreads, 1) in_proj_conv_
                         break;
                     }
                     tc_fence_after();
-                    const uint8_t* st = sm + s * kStageBytes;
+                    const uint8_t* st = sm + s * kStride;
                     const uint64_t da = sdesc_kmajor(st, 0), db = sdesc_kmajor(st + kAStage, 0);
 #pragma unroll
                     for (int kk = 0; kk < kBK / 16; ++kk)
@@ -350,48 +364,33 @@ __global__ void __launch_bounds__(FP8 ? kFp8Threads : kThreads, 1) in_proj_conv_
         }
     } else if constexpr (FP8) {
         // ============================ e4m3 -> fp16 converters ============================
-        constexpr int kPer = kBM * kBK / 16 / (32 * kConvertWarps);  // 16-code pieces per thread: 8
-        const int ct = tid - 32 * kEpilogueWarps - 64;                // 0 .. 63
+        constexpr int kPer = kBM * kBK / 16 / (32 * kConvertWarps);  // 16-code pieces per thread: 4
+        const int ct = tid - 32 * (kEpilogueWarps + 2);              // 0 .. 127
         const int my_tiles = blockIdx.x < p.tiles ? (p.tiles - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
         const int total = my_tiles * kblocks;
-        uint4 cur[kPer], nxt[kPer];
-        auto load = [&](int it, uint4 (&r)[kPer]) {
-            const int tile = blockIdx.x + (it / kblocks) * gridDim.x, kb = it % kblocks;
-            const int n0 = (tile / p.tiles_t) * kBM;
-#pragma unroll
-            for (int i = 0; i < kPer; ++i) {
-                const int id = ct + 64 * i, n = n0 + (id >> 2);
-                r[i] = n < p.N ? __ldg(reinterpret_cast<const uint4*>(p.codes + (int64_t)n * p.ldc + kb * kBK +
-                                                                      (id & 3) * 16))
-                               : make_uint4(0u, 0u, 0u, 0u);
-            }
-        };
-        if (total > 0) load(0, cur);
         for (int it = 0; it < total; ++it) {
-            if (it + 1 < total) load(it + 1, nxt);
             const int s = it % kStages;
-            if (it >= kStages && !mbar_wait_or_abort(&sh.empty[s], (uint32_t)(it / kStages - 1) & 1, kSiteTmaLoad,
-                                                     &sh.abort, false)) {
+            if (!mbar_wait_or_abort(&sh.codes_full[s], (uint32_t)(it / kStages) & 1, kSiteTmaLoad, &sh.abort,
+                                    false)) {
                 atomicExch(&sh.abort, 1);
                 break;
             }
-            uint8_t* a_tile = sm + s * kStageBytes;
+            uint8_t* st = sm + s * kStride;
+            const uint8_t* raw = st + kStageBytes;  // row r of the codes at r * 64
 #pragma unroll
             for (int i = 0; i < kPer; ++i) {
-                const int id = ct + 64 * i, row = id >> 2, part = id & 3;
-                const uint4 w = cur[i];
+                const int id = ct + 32 * kConvertWarps * i, row = id >> 2, part = id & 3;
+                const uint4 w = *reinterpret_cast<const uint4*>(raw + row * kBK + part * 16);
                 const uint4 lo = make_uint4(e4m3x2_to_f16x2(w.x), e4m3x2_to_f16x2(w.x >> 16), e4m3x2_to_f16x2(w.y),
                                             e4m3x2_to_f16x2(w.y >> 16));
                 const uint4 hi = make_uint4(e4m3x2_to_f16x2(w.z), e4m3x2_to_f16x2(w.z >> 16), e4m3x2_to_f16x2(w.w),
                                             e4m3x2_to_f16x2(w.w >> 16));
-                *reinterpret_cast<uint4*>(a_tile + sw128(row, 2 * part)) = lo;
-                *reinterpret_cast<uint4*>(a_tile + sw128(row, 2 * part + 1)) = hi;
+                *reinterpret_cast<uint4*>(st + sw128(row, 2 * part)) = lo;
+                *reinterpret_cast<uint4*>(st + sw128(row, 2 * part + 1)) = hi;
             }
             fence_async_smem();  // the generic-proxy stores become visible to the tensor cores
             __syncwarp();
             if (lane == 0) mbar_arrive(&sh.full[s]);
-#pragma unroll
-            for (int i = 0; i < kPer; ++i) cur[i] = nxt[i];
         }
     }
     tc_fence_before();
@@ -621,6 +620,19 @@ static bool make_map2(CUtensorMap* map, const void* base, int64_t rows, int64_t 
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 2-D map over the e4m3 codes [rows, K] (row stride ld bytes), box (64, 128), rows kept as they are.
+static bool make_codes_map(CUtensorMap* map, const void* base, int64_t rows, int64_t K, int64_t ld) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)ld};
+    cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)kBM};
+    cuuint32_t estr[2] = {1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // Tokens per tile: the candidate with the shortest estimated makespan, counted as rounds of tiles
 // over the persistent CTAs (or CTA pairs) times the tile's columns plus a fixed cost per tile
 // (pipeline fill and drain, in columns); ties go to the wider tile, which reads fewer bytes per
@@ -660,7 +672,7 @@ int launch_in_proj_conv(const InProjArgs& a, cudaStream_t s) {
         if (cudaFuncSetAttribute(in_proj_conv_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)kSmemBytes) != cudaSuccess ||
             cudaFuncSetAttribute(in_proj_conv_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)kSmemBytes) != cudaSuccess ||
+                                 (int)kFp8SmemBytes) != cudaSuccess ||
             cudaFuncSetAttribute(in_proj_conv_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)kPairSmemBytes) != cudaSuccess ||
             cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms[dev] < 1)
@@ -686,7 +698,8 @@ int launch_in_proj_conv(const InProjArgs& a, cudaStream_t s) {
         p.w_scale = a.w_scale;
         p.row_scale = reinterpret_cast<const float*>(static_cast<uint8_t*>(a.workspace) +
                                                      ((size_t)a.T * a.K * 2 + 255) / 256 * 256);
-        if (!make_map2(&p.tm_x, xh, a.T, a.K, a.K, (uint32_t)p.bn, CU_TENSOR_MAP_DATA_TYPE_FLOAT16))
+        if (!make_map2(&p.tm_x, xh, a.T, a.K, a.K, (uint32_t)p.bn, CU_TENSOR_MAP_DATA_TYPE_FLOAT16) ||
+            !make_codes_map(&p.tm_w, a.codes, a.N, a.K, a.ldc))
             return GDN_ERR_LAUNCH;
     } else if (!make_map2(&p.tm_w, a.w, a.N, a.K, a.ldw, kBM) ||
                !make_map2(&p.tm_x, a.x, a.T, a.K, a.ldx, (uint32_t)(use_pair ? p.bn / 2 : p.bn))) {
@@ -715,7 +728,7 @@ int launch_in_proj_conv(const InProjArgs& a, cudaStream_t s) {
         fp16_rows_kernel<<<(unsigned)a.T, 256, 0, s>>>(static_cast<const bf16*>(a.x), a.ldx, (int)a.K, xh,
                                                          const_cast<float*>(p.row_scale));
         const int grid = (int)(tiles < sms[dev] ? tiles : sms[dev]);
-        in_proj_conv_kernel<true><<<grid, kFp8Threads, kSmemBytes, s>>>(p);
+        in_proj_conv_kernel<true><<<grid, kFp8Threads, kFp8SmemBytes, s>>>(p);
     } else if (use_pair) {
         const int grid = 2 * (int)(tiles < pairs ? tiles : pairs);
         in_proj_conv_pair_kernel<<<grid, kThreads, kPairSmemBytes, s>>>(p);
