@@ -23,7 +23,8 @@
 //
 // The kernel is persistent (one CTA per SM, tiles strided by the grid, tokens fastest so that the
 // CTAs running at once share the activations and a few weight panels in L2). Warp 8 streams
-// 64-wide K slices of W and X through four stages with TMA (128-byte swizzle); warp 9 issues
+// 64-wide K slices of W and X with TMA (128-byte swizzle) through as many stages as fit (four at
+// the widest tile, up to eight for narrow ones); warp 9 issues
 // tcgen05.mma (M = 128, N = bn, K = 16) into one of two 256-column accumulators, so that the
 // products of the next tile run while warps 0-7 drain the previous one (warp w reads TMEM lane
 // quadrant w % 4 and half w / 4 of the columns).
@@ -44,11 +45,9 @@ constexpr int kBM = 128;                 // channels per tile (the MMA's M)
 constexpr int kHalo = 3;                 // tokens before the tile's outputs (taps - 1 of a 4-tap conv)
 constexpr int kMaxBN = 256;              // tokens per tile at most (the MMA's N)
 constexpr int kBK = 64;                  // K per stage (one 128-byte swizzle panel)
-constexpr int kStages = 4;
+constexpr int kMaxStages = 8;             // single-CTA stages: as many as fit (4 at the widest tile)
+constexpr uint32_t kSmemLimit = 232448 - 1024;  // 227 KB a CTA, less room for the static variables
 constexpr uint32_t kAStage = kBM * 128;     // 16 KB of W
-constexpr uint32_t kBStage = kMaxBN * 128;  // up to 32 KB of X
-constexpr uint32_t kStageBytes = kAStage + kBStage;
-constexpr uint32_t kSmemBytes = kStages * kStageBytes + 1024;
 constexpr int kEpilogueWarps = 8;
 constexpr int kProducerWarp = 8, kMmaWarp = 9;
 constexpr int kThreads = 32 * (kEpilogueWarps + 2);
@@ -57,8 +56,7 @@ constexpr int kFp8Threads = kThreads + 32 * kConvertWarps;
 // fp8 stages: the fp16 weight operand (16 KB), the activation rows (up to 32 KB), the raw codes
 // that TMA brings (128 rows x 64 codes, 8 KB)
 constexpr uint32_t kRawStage = kBM * kBK;
-constexpr uint32_t kFp8StageBytes = kStageBytes + kRawStage;
-constexpr uint32_t kFp8SmemBytes = kStages * kFp8StageBytes + 1024;
+
 constexpr uint32_t kAccCols = 256;       // columns of one accumulator; two of them fill TMEM
 constexpr int kChunk = 16;               // accumulator columns per TMEM load
 
@@ -73,6 +71,8 @@ struct Params {
     int T, N, C, K, nseq;
     int bn;              // tokens per tile, a multiple of 32 in [64, 256]
     int tiles_t, tiles;  // token tiles, all tiles
+    int stages;          // single-CTA kernel: pipeline stages (as many as fit, at most 8)
+    uint32_t stage_bytes;  // single-CTA kernel: W (16 KB) + X (bn x 128 B) [+ raw codes (8 KB)]
     // fp8 weights (the single-CTA kernel with FP8 = true): e4m3 codes [N, K] (row stride ldc
     // bytes) with one fp32 scale per row, and the activations as fp16 rows with a power-of-two
     // scale per row (tm_x then maps those fp16 rows)
@@ -83,8 +83,8 @@ struct Params {
 };
 
 struct Shared {
-    uint64_t full[kStages], empty[kStages], acc_full[2], acc_empty[2], mma_done;
-    uint64_t codes_full[kStages];  // fp8: the raw codes of a stage have landed
+    uint64_t full[kMaxStages], empty[kMaxStages], acc_full[2], acc_empty[2], mma_done;
+    uint64_t codes_full[kMaxStages];  // fp8: the raw codes of a stage have landed
     uint32_t tmem_base;
     int abort;
 };
@@ -240,13 +240,14 @@ template <bool FP8>
 __global__ void __launch_bounds__(FP8 ? kFp8Threads : kThreads, 1) in_proj_conv_kernel(const __grid_constant__ Params p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = align1024(smem_raw);
-    constexpr uint32_t kStride = FP8 ? kFp8StageBytes : kStageBytes;
+    const int S = p.stages;
+    const uint32_t stride = p.stage_bytes, raw_off = kAStage + (uint32_t)p.bn * 128;
     __shared__ Shared sh;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int kblocks = p.K / kBK;
 
     if (tid == 0) {
-        for (int s = 0; s < kStages; ++s) {
+        for (int s = 0; s < S; ++s) {
             mbar_init(&sh.full[s], FP8 ? 1 + kConvertWarps : 1);  // the producer (+ the converters)
             mbar_init(&sh.empty[s], 1);
             mbar_init(&sh.codes_full[s], 1);
@@ -274,41 +275,46 @@ __global__ void __launch_bounds__(FP8 ? kFp8Threads : kThreads, 1) in_proj_conv_
         // ============================== producer ==============================
         if (lane == 0) {
             const uint32_t bytes = (FP8 ? 0u : kAStage) + (uint32_t)p.bn * 128;
-            int it = 0;
+            int it = 0, s = 0;
+            uint32_t ph = 0;  // parity of stage s's current use (the index and parity advance by steps:
+                              // no division by the run-time stage count on these threads)
             bool ok = true;
             for (int tile = blockIdx.x; ok && tile < p.tiles; tile += gridDim.x) {
                 const int n0 = (tile / p.tiles_t) * kBM;
                 const int row0 = (tile % p.tiles_t) * (p.bn - kHalo) - kHalo;
                 for (int kb = 0; kb < kblocks; ++kb, ++it) {
-                    const int s = it % kStages;
-                    if (it >= kStages && !mbar_wait_or_abort(&sh.empty[s], (uint32_t)(it / kStages - 1) & 1,
-                                                             kSiteTmaLoad, &sh.abort, false)) {
+                    if (it >= S && !mbar_wait_or_abort(&sh.empty[s], ph ^ 1u, kSiteTmaLoad, &sh.abort, false)) {
                         atomicExch(&sh.abort, 1);
                         ok = false;
                         break;
                     }
-                    uint8_t* st = sm + s * kStride;
+                    uint8_t* st = sm + s * stride;
                     mbar_arrive_expect_tx(&sh.full[s], bytes);
                     if (FP8) {
                         mbar_arrive_expect_tx(&sh.codes_full[s], kRawStage);
-                        tma_load_2d(st + kStageBytes, &p.tm_w, &sh.codes_full[s], kb * kBK, n0);
+                        tma_load_2d(st + raw_off, &p.tm_w, &sh.codes_full[s], kb * kBK, n0);
                     } else {
                         tma_load_2d(st, &p.tm_w, &sh.full[s], kb * kBK, n0);
                     }
                     tma_load_2d(st + kAStage, &p.tm_x, &sh.full[s], kb * kBK, row0);
+                    if (++s == S) {
+                        s = 0;
+                        ph ^= 1u;
+                    }
                 }
             }
             // the copies in flight land before the CTA's shared memory can go away
-            for (int i = it > kStages ? it - kStages : 0; i < it; ++i) {
-                if (FP8) mbar_wait(&sh.codes_full[i % kStages], (uint32_t)(i / kStages) & 1, kSiteDrain);
-                mbar_wait(&sh.full[i % kStages], (uint32_t)(i / kStages) & 1, kSiteDrain);
+            for (int i = it > S ? it - S : 0; i < it; ++i) {
+                if (FP8) mbar_wait(&sh.codes_full[i % S], (uint32_t)(i / S) & 1, kSiteDrain);
+                mbar_wait(&sh.full[i % S], (uint32_t)(i / S) & 1, kSiteDrain);
             }
         }
     } else if (warp == kMmaWarp) {
         // ============================== MMA issuer ==============================
         if (lane == 0) {
             const uint32_t idesc = make_idesc(kBM, (uint32_t)p.bn, FP8 ? kFmtF16 : kFmtBF16, false, false);
-            int it = 0, lt = 0;
+            int lt = 0, s = 0;
+            uint32_t ph = 0;
             bool ok = true;
             for (int tile = blockIdx.x; ok && tile < p.tiles; tile += gridDim.x, ++lt) {
                 const int b = lt & 1;
@@ -319,21 +325,23 @@ __global__ void __launch_bounds__(FP8 ? kFp8Threads : kThreads, 1) in_proj_conv_
                     break;
                 }
                 tc_fence_after();
-                for (int kb = 0; kb < kblocks; ++kb, ++it) {
-                    const int s = it % kStages;
-                    if (!mbar_wait_or_abort(&sh.full[s], (uint32_t)(it / kStages) & 1, kSiteTmaLoad, &sh.abort,
-                                            false)) {
+                for (int kb = 0; kb < kblocks; ++kb) {
+                    if (!mbar_wait_or_abort(&sh.full[s], ph, kSiteTmaLoad, &sh.abort, false)) {
                         atomicExch(&sh.abort, 1);
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint8_t* st = sm + s * kStride;
+                    const uint8_t* st = sm + s * stride;
                     const uint64_t da = sdesc_kmajor(st, 0), db = sdesc_kmajor(st + kAStage, 0);
 #pragma unroll
                     for (int kk = 0; kk < kBK / 16; ++kk)
                         mma_f16(acc, sdesc_add(da, kk * 32), sdesc_add(db, kk * 32), idesc, (kb | kk) != 0 ? 1u : 0u);
                     mma_commit(&sh.empty[s]);  // the stage is free once these products have read it
+                    if (++s == S) {
+                        s = 0;
+                        ph ^= 1u;
+                    }
                 }
                 mma_commit(&sh.acc_full[b]);  // also after a failed wait, so that no drain waits in vain
             }
@@ -368,15 +376,15 @@ __global__ void __launch_bounds__(FP8 ? kFp8Threads : kThreads, 1) in_proj_conv_
         const int ct = tid - 32 * (kEpilogueWarps + 2);              // 0 .. 127
         const int my_tiles = blockIdx.x < p.tiles ? (p.tiles - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
         const int total = my_tiles * kblocks;
+        int s = 0;
+        uint32_t ph = 0;
         for (int it = 0; it < total; ++it) {
-            const int s = it % kStages;
-            if (!mbar_wait_or_abort(&sh.codes_full[s], (uint32_t)(it / kStages) & 1, kSiteTmaLoad, &sh.abort,
-                                    false)) {
+            if (!mbar_wait_or_abort(&sh.codes_full[s], ph, kSiteTmaLoad, &sh.abort, false)) {
                 atomicExch(&sh.abort, 1);
                 break;
             }
-            uint8_t* st = sm + s * kStride;
-            const uint8_t* raw = st + kStageBytes;  // row r of the codes at r * 64
+            uint8_t* st = sm + s * stride;
+            const uint8_t* raw = st + raw_off;  // row r of the codes at r * 64
 #pragma unroll
             for (int i = 0; i < kPer; ++i) {
                 const int id = ct + 32 * kConvertWarps * i, row = id >> 2, part = id & 3;
@@ -391,6 +399,10 @@ __global__ void __launch_bounds__(FP8 ? kFp8Threads : kThreads, 1) in_proj_conv_
             fence_async_smem();  // the generic-proxy stores become visible to the tensor cores
             __syncwarp();
             if (lane == 0) mbar_arrive(&sh.full[s]);
+            if (++s == S) {
+                s = 0;
+                ph ^= 1u;
+            }
         }
     }
     tc_fence_before();
@@ -670,9 +682,9 @@ int launch_in_proj_conv(const InProjArgs& a, cudaStream_t s) {
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return GDN_ERR_LAUNCH;
     if (!ready[dev]) {
         if (cudaFuncSetAttribute(in_proj_conv_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)kSmemBytes) != cudaSuccess ||
+                                 (int)kSmemLimit) != cudaSuccess ||
             cudaFuncSetAttribute(in_proj_conv_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)kFp8SmemBytes) != cudaSuccess ||
+                                 (int)kSmemLimit) != cudaSuccess ||
             cudaFuncSetAttribute(in_proj_conv_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)kPairSmemBytes) != cudaSuccess ||
             cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms[dev] < 1)
@@ -724,17 +736,21 @@ int launch_in_proj_conv(const InProjArgs& a, cudaStream_t s) {
     if (a.conv_tail &&
         cudaMemsetAsync(a.conv_tail, 0, (size_t)a.nseq * a.C * 4 * sizeof(bf16), s) != cudaSuccess)
         return GDN_ERR_LAUNCH;
+    p.stage_bytes = kAStage + (uint32_t)p.bn * 128 + (fp8 ? kRawStage : 0u);
+    p.stages = (int)((kSmemLimit - 1024) / p.stage_bytes);
+    if (p.stages > kMaxStages) p.stages = kMaxStages;
+    const uint32_t single_smem = (uint32_t)p.stages * p.stage_bytes + 1024;
     if (fp8) {
         fp16_rows_kernel<<<(unsigned)a.T, 256, 0, s>>>(static_cast<const bf16*>(a.x), a.ldx, (int)a.K, xh,
                                                          const_cast<float*>(p.row_scale));
         const int grid = (int)(tiles < sms[dev] ? tiles : sms[dev]);
-        in_proj_conv_kernel<true><<<grid, kFp8Threads, kFp8SmemBytes, s>>>(p);
+        in_proj_conv_kernel<true><<<grid, kFp8Threads, single_smem, s>>>(p);
     } else if (use_pair) {
         const int grid = 2 * (int)(tiles < pairs ? tiles : pairs);
         in_proj_conv_pair_kernel<<<grid, kThreads, kPairSmemBytes, s>>>(p);
     } else {
         const int grid = (int)(tiles < sms[dev] ? tiles : sms[dev]);
-        in_proj_conv_kernel<false><<<grid, kThreads, kSmemBytes, s>>>(p);
+        in_proj_conv_kernel<false><<<grid, kThreads, single_smem, s>>>(p);
     }
     return launch_status();
 }
