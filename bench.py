@@ -19,6 +19,8 @@ dataset or checkpoint is involved):
   per-token fp32 states, then roll back to an accepted length U{1..5}.
 * ``attention`` (the drafter side of a delta layer, not a BASELINE config): the mask-row
   attention of one decode cycle, 32 sequences x 12 mask rows x 32 heads over 4,108 cached keys.
+* ``fp8`` (not a BASELINE config): the qkv projection with the reference's fp8 weights, at a decode
+  batch and at prefill with the conv, beside bf16 weights (library and cuBLAS).
 * ``in_proj`` (the GEMM in front of the path, not a BASELINE config): the merged input projection
   of one 9B-shaped layer, 4096 tokens x 4096 -> 12,352, with the causal conv + SiLU fused into the
   tcgen05 GEMM's epilogue; timed beside cuBLAS's matmul followed by the conv kernel.
@@ -340,6 +342,7 @@ def run_ours(args, rank, world, device, rank_sync, reduce_max):
         extra["attention"]["roofline"]["traffic"] = (traffic.get("attention", {}).get("dram_bytes_per_launch")
                                                      if world == 1 else None)
         extra["in_proj"] = bench_in_proj(gdn, args, device, rank_sync, reduce_max, world, tc_peak)
+        extra["fp8"] = bench_fp8(gdn, args, device, rank_sync, reduce_max, world, hbm_peak, tc_peak)
         result["extra"] = extra
         result["gpu_launches"] += sum(e.get("gpu_launches", 0) for e in extra.values())
     clocks.__exit__(None, None, None)
@@ -495,7 +498,44 @@ def bench_in_proj(gdn, args, device, rank_sync, reduce_max, world, tc_peak, T=40
             "unfused_ms": round(unfused_ms, 4), "unfused": "torch matmul (cuBLAS) then gdn.causal_conv1d",
             "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": tc_peak, "unit": "TFLOP/s",
                          "frac": round(ach / tc_peak, 4), "algorithmic_flops": flops},
-            "gpu_launches": args.steps}
+            "gpu_launches": 2 * args.steps}  # the fused kernel, and the conv kernel of the unfused arm
+
+
+def bench_fp8(gdn, args, device, rank_sync, reduce_max, world, hbm_peak, tc_peak, K=4096, N=C_QKV):
+    """The qkv projection with fp8 weights (the reference's FP8Linear: e4m3 codes, fp32 row
+    scales; in fp8 the engine runs in_proj_qkv on its own, inference/engine.py:155-166): at a
+    decode batch (256 rows, bound by the codes' bytes) and at prefill (4096 tokens with the conv
+    in the epilogue, bound by the tensor pipe); beside them the same shapes with bf16 weights
+    through the library and through cuBLAS."""
+    gen = torch.Generator().manual_seed(8)
+    w = (torch.randn(N, K, generator=gen) * K ** -0.5).to(torch.bfloat16).to(device)
+    scale = (w.float().abs().amax(1).clamp(min=1e-12) / torch.finfo(torch.float8_e4m3fn).max).contiguous()
+    codes = (w.float() / scale[:, None]).to(torch.float8_e4m3fn).contiguous()
+    cw = (torch.randn(N, 4, generator=gen) * 0.5).to(torch.bfloat16).to(device)
+    res = {}
+    for name, M, conv in (("decode", 256, 0), ("prefill", 4096, N)):
+        x = torch.randn(M, K, generator=gen).to(torch.bfloat16).to(device)
+        arms = {"fp8": lambda i: gdn.in_proj_conv(x, codes, cw, conv, weight_scale=scale),
+                "bf16": lambda i: gdn.in_proj_conv(x, w, cw, conv),
+                "cublas_bf16": lambda i: x @ w.T}
+        ms = {k: reduce_max(timed(f, args.steps, args.warmup, rank_sync)) / args.steps for k, f in arms.items()}
+        entry = {k + "_ms": round(v, 4) for k, v in ms.items()}
+        if conv == 0:
+            bytes_ = N * K + N * 4 + M * K * 2 + M * N * 2  # codes, scales, x, out
+            ach = bytes_ / (ms["fp8"] / 1e3) / 1e9
+            entry["roofline"] = {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm_peak, "unit": "GB/s",
+                                 "frac": round(ach / hbm_peak, 4), "algorithmic_bytes": bytes_}
+        else:
+            ach = 2 * M * K * N / (ms["fp8"] / 1e3) / 1e12
+            entry["roofline"] = {"bound": "tensor", "achieved": round(ach, 1), "peak": tc_peak, "unit": "TFLOP/s",
+                                 "frac": round(ach / tc_peak, 4)}
+        entry["rows"] = M
+        entry["conv"] = bool(conv)
+        res[name] = entry
+    return {"workload": f"qkv projection {K} -> {N} with fp8 (e4m3, per-row scale) weights; decode: 256 rows, no conv; "
+                        f"prefill: 4096 tokens with the causal conv + SiLU in the epilogue; one replica per GPU",
+            "value": round(world * 256 / (res["decode"]["fp8_ms"] / 1e3), 1), "unit": "rows/s (decode)",
+            **res, "gpu_launches": 6 * args.steps}  # per step of each arm: fp8 2 (row kernel, GEMM), bf16 1; two shapes
 
 
 def bench_verify(gdn, args, device, rank, world, rank_sync, reduce_max, hbm_peak, layers=24, B_total=128, T=5):
