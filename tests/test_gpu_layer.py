@@ -82,8 +82,8 @@ def test_prefill_layer_matches_oracle_composition(B, T, H, HV):
     against the oracle's ops. The norm divides each row by its rms (about 0.01 with these inputs),
     which magnifies the chunk output's absolute error about a hundredfold, so the layer is checked
     step by step: the conv bit for bit, the chunk output within the bf16 output bound (max-abs
-    2e-2) and the state within 1e-3 relative, the norm of that output within one bf16 ulp of
-    the oracle's norm of the same values, and the whole output within 1e-2 relative (Frobenius)."""
+    2e-2) and the state within 1e-3 relative, the norm of that output within two bf16 ulps of
+    the oracle's norm of the same values (under 1% of the elements differing at all), and the whole output within 1e-2 relative (Frobenius)."""
     qkv, w, g, beta, z, nw, h0 = layer_inputs(B * 100 + T, B, T, H, HV)
     out_ref, S_ref = reference_prefill_layer(qkv, w, g, beta, z, nw, H, HV, h0)
     qkv_d, w_d, g_d, b_d, z_d, nw_d, h0_d = (t.cuda() for t in (qkv, w, g, beta, z, nw, h0))
@@ -106,7 +106,10 @@ def test_prefill_layer_matches_oracle_composition(B, T, H, HV):
     assert maxabs(o, o_ref) < 2e-2, maxabs(o, o_ref)
     normed = oracle.gated_rms_norm(o.cpu().reshape(-1, 128), z.reshape(-1, 128), nw).reshape(B, T, HV, 128)
     ulp = torch.ldexp(torch.ones_like(normed.float()), torch.frexp(normed.float())[1] - 8)  # one bf16 ulp each
-    assert ((out.cpu().float() - normed.float()).abs() <= ulp).all()
+    # the norm kernel's bound (as in test_gpu_conv_norm): its sum of squares and rsqrt can round
+    # the normalised value one ulp away from the CPU's, and the product with the weight (up to
+    # 1.5) rounds again, so an element can land two ulps away
+    assert ((out.cpu().float() - normed.float()).abs() <= 2 * ulp).all()
     assert (out.cpu() != normed).float().mean().item() < 0.01
     assert rel(out, out_ref) < 1e-2, rel(out, out_ref)
 
