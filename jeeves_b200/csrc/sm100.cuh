@@ -404,6 +404,26 @@ __device__ __forceinline__ void tmem_ld16_wait(uint32_t taddr, float (&r)[16]) {
     for (int i = 0; i < 16; ++i) r[i] = __uint_as_float(u[i]);
 }
 
+// Two 16-column loads (at taddr_a and taddr_b) with one tcgen05.wait::ld, in one asm statement.
+__device__ __forceinline__ void tmem_ld16x2_wait(uint32_t taddr_a, uint32_t taddr_b, float (&a)[16], float (&b)[16]) {
+    uint32_t u[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%32];\n\t"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%33];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(u[0]), "=r"(u[1]), "=r"(u[2]), "=r"(u[3]), "=r"(u[4]), "=r"(u[5]), "=r"(u[6]), "=r"(u[7]), "=r"(u[8]),
+          "=r"(u[9]), "=r"(u[10]), "=r"(u[11]), "=r"(u[12]), "=r"(u[13]), "=r"(u[14]), "=r"(u[15]), "=r"(u[16]),
+          "=r"(u[17]), "=r"(u[18]), "=r"(u[19]), "=r"(u[20]), "=r"(u[21]), "=r"(u[22]), "=r"(u[23]), "=r"(u[24]),
+          "=r"(u[25]), "=r"(u[26]), "=r"(u[27]), "=r"(u[28]), "=r"(u[29]), "=r"(u[30]), "=r"(u[31])
+        : "r"(taddr_a), "r"(taddr_b)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        a[i] = __uint_as_float(u[i]);
+        b[i] = __uint_as_float(u[16 + i]);
+    }
+}
+
 __device__ __forceinline__ void tmem_ld64_wait(uint32_t taddr, float (&r)[64]) {
     uint32_t u[64];
     asm volatile(
