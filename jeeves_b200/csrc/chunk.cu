@@ -40,7 +40,6 @@
 #include "common.cuh"
 #include "gates.cuh"
 #include "launch.h"
-#include "norm.cuh"
 #include "sm100.cuh"
 #include "tensor_map.h"
 
@@ -123,14 +122,6 @@ struct FactorParams {
     int HV, rep;
     float scale;
     GateInputs gates;  // beta and g from the raw projections when gates.b is set
-    // fused launch with the output-gated RMSNorm: once their factor work is done, the factor CTAs
-    // normalise o (row layout [B, T, HV, 128]) into y as the scan stores it
-    int fuse_norm;
-    const bf16* o;
-    const bf16* z;
-    const bf16* norm_w;
-    bf16* y;
-    float eps;
 };
 
 struct FSmem {
@@ -177,10 +168,6 @@ enum : uint32_t { kBarFactor = 1, kBarChain = 2, kBarEpi = 3 };
 __device__ __forceinline__ void flag_release(uint32_t* flag) {
     asm volatile("fence.proxy.async.global;" ::: "memory");
     asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(flag), "r"(1u) : "memory");
-}
-
-__device__ __forceinline__ void flag_add_release(uint32_t* flag) {
-    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(flag) : "memory");
 }
 
 __device__ __forceinline__ uint32_t flag_acquire(const uint32_t* flag) {
@@ -635,7 +622,6 @@ struct ScanParams {
     const uint8_t* records;
     const uint32_t* ready;  // per-record flags to wait for (fused launch), or null
     const int32_t* order;   // packed batch: sequences longest first (grid row -> sequence), or null
-    int signal_out;         // add 1 to a record's ready flag once this CTA has stored its output rows
     int64_t T;
     int ncd;
     int HV, rep;
@@ -922,12 +908,7 @@ __device__ __forceinline__ void scan_cta(const ScanParams& p, int bx, int by) {
             }
             tc_fence_before();
             named_sync(kBarEpi, kEpiThreads);
-            if (et == 0) {
-                mbar_arrive(&sh.o_free[s]);
-                // every epilogue thread's stores precede the barrier above; the release makes them
-                // visible to the norm role of the fused launch that acquires the flag
-                if (p.signal_out) flag_add_release(const_cast<uint32_t*>(p.ready) + (slot0 + c) * p.HV + hv);
-            }
+            if (et == 0) mbar_arrive(&sh.o_free[s]);
         }
     } else if (warp >= 8) {
         // ================================ chain ================================
@@ -1087,91 +1068,6 @@ constexpr uint32_t kFusedSmemBytes =
     (SSmem::BYTES > kFusedFactorGroups * FSmem::END + 1024) ? SSmem::BYTES : kFusedFactorGroups * FSmem::END + 1024;
 static_assert(FSmem::END % 1024 == 0, "factor warpgroup regions stay 1024-aligned");
 
-// The rows of the chunk in `slot`: false for a slot no chunk maps to (packed batches).
-__device__ __forceinline__ bool slot_rows(const FactorParams& p, int64_t slot, int64_t& row0, int& nvalid) {
-    int64_t bos = 0, len = p.T, brow = 0, c = 0;
-    if (p.cu_seqlens == nullptr) {
-        brow = slot / p.ncd;
-        c = slot % p.ncd;
-    } else {
-        int lo = 0, hi = p.nseq - 1;
-        while (lo < hi) {
-            const int mid = (lo + hi + 1) >> 1;
-            if (p.cu_seqlens[mid] / 64 + (int64_t)mid <= slot) lo = mid;
-            else hi = mid - 1;
-        }
-        bos = p.cu_seqlens[lo];
-        len = p.cu_seqlens[lo + 1] - bos;
-        c = slot - (bos / 64 + lo);
-        if (c < 0 || 64 * c >= len) return false;
-    }
-    row0 = brow * p.T + bos + 64 * c;
-    nvalid = (int)(len - 64 * c < 64 ? len - 64 * c : 64);
-    return true;
-}
-
-// Bounded wait (backing off) until a record's flag reaches `target`.
-__device__ __forceinline__ bool wait_count(const uint32_t* flag, uint32_t target) {
-    uint32_t sleep_ns = 64;
-    const long long start = clock64();
-    while (flag_acquire(flag) < target) {
-        if (clock64() - start > kWaitCycles) {
-            raise_device_error(kSiteReady);
-            return false;
-        }
-        __nanosleep(sleep_ns);
-        sleep_ns = sleep_ns < 1024 ? 2 * sleep_ns : 1024;
-    }
-    return true;
-}
-
-// The norm role of a factor CTA, run by each warp once the CTA's factor work is done. Warp unit
-// u covers 16 of the 64 rows (quarter u % 4) of record unit u / 4 in chunk-major order, i.e. one
-// value head of one chunk; it starts once both scan CTAs of that head have stored the chunk (the
-// record's flag reads 1 + kSlices). Each half-warp normalises one row at a time with the same
-// row routine as gated_rmsnorm_kernel, four rows' loads in flight. Kept out of line so that its
-// registers do not add to the factor and scan roles' allocation.
-__device__ __noinline__ void norm_worker(const FactorParams& p, int64_t first, int64_t stride) {
-    const int lane = threadIdx.x & 31, sub = lane & 15, hr = lane >> 4;
-    const int64_t total = 4 * (int64_t)p.ncd * p.nseq * p.HV;
-    float ws[8];
-    load8f(p.norm_w + 8 * sub, ws);
-    for (int64_t u = first; u < total; u += stride) {
-        const int64_t unit = chunk_major_unit(p, u >> 2);
-        if (unit < 0) continue;
-        const int hv = (int)(unit % p.HV);
-        int64_t row0 = 0;
-        int nvalid = 0;
-        if (!slot_rows(p, unit / p.HV, row0, nvalid)) continue;
-        const int r_begin = 16 * (int)(u & 3);
-        if (r_begin >= nvalid) continue;
-        bool ok = true;
-        if (lane == 0) ok = wait_count(p.ready + unit, 1 + kSlices);
-        ok = __shfl_sync(0xffffffffu, ok, 0);
-        __syncwarp();  // lane 0's acquire orders the whole warp's reads of o below
-        if (!ok) return;
-#pragma unroll
-        for (int b = 0; b < 2; ++b) {
-            float xs[4][8], zs[4][8];
-            int64_t off[4];
-            bool valid[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int r = r_begin + 2 * (4 * b + i) + hr;
-                valid[i] = r < nvalid;
-                off[i] = ((row0 + (valid[i] ? r : r_begin)) * p.HV + hv) * kHeadDim + 8 * sub;
-                unpack8f(__ldcg(reinterpret_cast<const uint4*>(p.o + off[i])), xs[i]);
-                load8f(p.z + off[i], zs[i]);
-            }
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const uint4 raw = gated_norm_row8(xs[i], zs[i], ws, p.eps);
-                if (valid[i]) *reinterpret_cast<uint4*>(p.y + off[i]) = raw;
-            }
-        }
-    }
-}
-
 __global__ void __launch_bounds__(kScanThreads, 1) chunk_fused_kernel(const __grid_constant__ FactorParams f,
                                                                        const __grid_constant__ ScanParams sp, int nscan,
                                                                        int scan_gx) {
@@ -1180,17 +1076,13 @@ __global__ void __launch_bounds__(kScanThreads, 1) chunk_fused_kernel(const __gr
         return;
     }
     const int g = threadIdx.x >> 7;
+    if (g >= kFusedFactorGroups) return;
     extern __shared__ uint8_t smem_raw[];
     __shared__ FShared fsh[kFusedFactorGroups];
     const int64_t ctas = (int64_t)(gridDim.x - nscan);
-    if (g < kFusedFactorGroups)
-        factor_worker(f, fsh[g], align1024(smem_raw) + g * FSmem::END, 1 + g, threadIdx.x & 127,
-                      (int64_t)(blockIdx.x - nscan) * kFusedFactorGroups + g, ctas * kFusedFactorGroups,
-                      (int64_t)f.ncd * f.nseq * f.HV, false, true);
-    if (!f.fuse_norm) return;
-    __syncthreads();
-    const int warps = kScanThreads / 32;
-    norm_worker(f, (int64_t)(blockIdx.x - nscan) * warps + (threadIdx.x >> 5), ctas * warps);
+    factor_worker(f, fsh[g], align1024(smem_raw) + g * FSmem::END, 1 + g, threadIdx.x & 127,
+                  (int64_t)(blockIdx.x - nscan) * kFusedFactorGroups + g, ctas * kFusedFactorGroups,
+                  (int64_t)f.ncd * f.nseq * f.HV, false, true);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -1332,21 +1224,12 @@ int launch_chunk(const ChunkArgs& a, cudaStream_t s) {
             return GDN_ERR_LAUNCH;
         f.ready = ready;
         sp.ready = ready;
-        if (a.y != nullptr) {  // the norm runs inside the launch, on the factor CTAs
-            f.fuse_norm = 1;
-            f.o = static_cast<const bf16*>(a.o);
-            f.z = static_cast<const bf16*>(a.z);
-            f.norm_w = static_cast<const bf16*>(a.norm_w);
-            f.y = static_cast<bf16*>(a.y);
-            f.eps = a.eps;
-            sp.signal_out = 1;
-        }
         int ns = (int)nscan, gx = scan_gx;
         void* args[] = {&f, &sp, &ns, &gx};
         if (cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(chunk_fused_kernel), dim3((unsigned)dev.sms),
                                         dim3(kScanThreads), args, kFusedSmemBytes, s) != cudaSuccess)
             return GDN_ERR_LAUNCH;
-        return launch_status();
+        return finish_chunk(a, s);
     }
     if (slots > 0) {
         chunk_factor_kernel<<<(unsigned)(slots * a.HV), 128, FSmem::BYTES, s>>>(f);
