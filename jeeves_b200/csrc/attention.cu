@@ -154,6 +154,11 @@ __global__ void __launch_bounds__(128) decode_attention_kernel(const __grid_cons
     const bool owner = lane < 16;                   // holds row i of S
     const bool row_ok = i < rows;
     const bool holds_o = D == 256 || owner;         // holds 128 values of O
+    // A warp whose 16 rows all lie past R * G (the padding of the MMA's M = 64) skips the softmax,
+    // the P rows and the O update: those rows only feed O rows that are never stored, and the
+    // skipped work would take issue slots from the other CTA on the SM (the drafter's 12 mask rows
+    // leave warps 1-3 idle).
+    const bool warp_live = 16 * warp < rows;
     const int r = row_ok ? i / p.G : 0;
     const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
     const bf16* mrow = p.mask + (int64_t)b * p.smb + (int64_t)r * p.smr;
@@ -205,9 +210,9 @@ __global__ void __launch_bounds__(128) decode_attention_kernel(const __grid_cons
         if (!__syncthreads_and(ok)) break;
         tc_fence_after();
         float sv[NK];
-        tmem_ld64_wait(tb + TL::COL_S + lane_base, sv);
         float alpha = 0.f;
-        if (owner) {
+        if (warp_live) tmem_ld64_wait(tb + TL::COL_S + lane_base, sv);
+        if (warp_live && owner) {
             float mb = -INFINITY;
 #pragma unroll
             for (int c = 0; c < NK / 8; ++c) {
@@ -260,7 +265,7 @@ __global__ void __launch_bounds__(128) decode_attention_kernel(const __grid_cons
         // the stage is free again: block j + 2 streams in while block j + 1 is computed
         if (tid == 0 && loaded < nb) load_block(loaded++);
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
+        for (int c = 0; c < 2 && warp_live; ++c) {
             float ob[64];
             tmem_ld64_wait(tb + TL::COL_O + 64 * c + lane_base, ob);
 #pragma unroll
