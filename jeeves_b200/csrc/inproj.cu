@@ -19,7 +19,8 @@
 // channel's lane walks its tokens in order and keeps the conv window in registers, with no
 // shared-memory staging. A tile's columns are tokens t0 - 3 .. t0 + bn - 4 (the three before t0
 // recomputed for the window; TMA fills rows before 0 and past T with zeros), and it writes the
-// bn - 3 tokens from t0 on.
+// bn - 3 tokens from t0 on. Without conv channels (the decode-time projections and the output
+// projection) there is no window: a tile's bn columns are tokens t0 .. t0 + bn - 1.
 //
 // The kernel is persistent (one CTA per SM, tiles strided by the grid, tokens fastest so that the
 // CTAs running at once share the activations and a few weight panels in L2). Warp 8 streams
@@ -70,6 +71,7 @@ struct Params {
     int64_t ldo;
     int T, N, C, K, nseq;
     int bn;              // tokens per tile, a multiple of 32 in [64, 256]
+    int halo;            // leading columns recomputed for the conv window: kHalo with a conv, else 0
     int tiles_t, tiles;  // token tiles, all tiles
     int stages;          // single-CTA kernel: pipeline stages (as many as fit, at most 8)
     uint32_t stage_bytes;  // single-CTA kernel: W (16 KB) + X (bn x 128 B) [+ raw codes (8 KB)]
@@ -121,7 +123,7 @@ namespace inproj {
 
 // Stores a lane's 16 values of one channel, tokens tb .. tb + 15 (column j of the tile first),
 // skipping the halo columns and the tokens past T unless the whole chunk is known to be inside.
-__device__ __forceinline__ void store_chunk(bf16* out_c, int64_t ldo, int tb, int j, int T, bool whole,
+__device__ __forceinline__ void store_chunk(bf16* out_c, int64_t ldo, int tb, int j, int T, int halo, bool whole,
                                             const float (&v)[kChunk]) {
     bf16* q = out_c + (int64_t)tb * ldo;
     if (whole) {
@@ -130,7 +132,7 @@ __device__ __forceinline__ void store_chunk(bf16* out_c, int64_t ldo, int tb, in
     } else {
 #pragma unroll
         for (int e = 0; e < kChunk; ++e)
-            if (j + e >= kHalo && tb + e < T) q[e * ldo] = __float2bfloat16_rn(v[e]);
+            if (j + e >= halo && tb + e < T) q[e * ldo] = __float2bfloat16_rn(v[e]);
     }
 }
 
@@ -203,16 +205,16 @@ __device__ __forceinline__ void drain(const Params& p, uint32_t acc, int col0, i
             for (int e = 0; e < kChunk; ++e) res[e] = silu_fast(pre[e]);
         }
         // a chunk past the halo and inside the tokens stores without per-token checks (warp-uniform)
-        const bool whole = j >= kHalo && tb + kChunk <= p.T;
-        if (conv) store_chunk(out_c, p.ldo, tb, j, p.T, whole, res);
-        else if (in_n) store_chunk(out_c, p.ldo, tb, j, p.T, whole, y);
+        const bool whole = j >= p.halo && tb + kChunk <= p.T;
+        if (conv) store_chunk(out_c, p.ldo, tb, j, p.T, p.halo, whole, res);
+        else if (in_n) store_chunk(out_c, p.ldo, tb, j, p.T, p.halo, whole, y);
         if (conv && p.conv_tail) {  // the last four pre-conv tokens of each sequence (the cache's conv state)
 #pragma unroll
             for (int e = 0; e < kChunk; ++e) {
                 const int t = tb + e;
                 const int end = VARLEN ? __shfl_sync(0xffffffffu, s_end, e) : p.T;
                 const int id = VARLEN ? __shfl_sync(0xffffffffu, s_id, e) : 0;
-                if (j + e >= kHalo && t < p.T && t >= end - 4)
+                if (j + e >= p.halo && t < p.T && t >= end - 4)
                     p.conv_tail[((int64_t)id * p.C + c) * 4 + (4 - (end - t))] = __float2bfloat16_rn(y[e]);
             }
         }
@@ -281,7 +283,7 @@ __global__ void __launch_bounds__(FP8 ? kFp8Threads : kThreads, 1) in_proj_conv_
             bool ok = true;
             for (int tile = blockIdx.x; ok && tile < p.tiles; tile += gridDim.x) {
                 const int n0 = (tile / p.tiles_t) * kBM;
-                const int row0 = (tile % p.tiles_t) * (p.bn - kHalo) - kHalo;
+                const int row0 = (tile % p.tiles_t) * (p.bn - p.halo) - p.halo;
                 for (int kb = 0; kb < kblocks; ++kb, ++it) {
                     if (it >= S && !mbar_wait_or_abort(&sh.empty[s], ph ^ 1u, kSiteTmaLoad, &sh.abort, false)) {
                         atomicExch(&sh.abort, 1);
@@ -361,7 +363,7 @@ __global__ void __launch_bounds__(FP8 ? kFp8Threads : kThreads, 1) in_proj_conv_
             if (*reinterpret_cast<volatile int*>(&sh.abort)) break;
             tc_fence_after();
             const int n0 = (tile / p.tiles_t) * kBM;
-            const int row0 = (tile % p.tiles_t) * (p.bn - kHalo) - kHalo;
+            const int row0 = (tile % p.tiles_t) * (p.bn - p.halo) - p.halo;
             const uint32_t acc = tb + b * kAccCols + ((uint32_t)(32 * q) << 16);
             const int c = n0 + 32 * q + lane;
             if (p.cu_seqlens) drain<true, FP8>(p, acc, col0, half, row0, c, lane);
@@ -524,7 +526,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 // this CTA's weight rows and token rows; a start past the matrix is moved back
                 // inside it (those rows feed only channels or tokens that are not written)
                 int n0 = nn * kPairBM + kBM * (int)rank;
-                int r0 = tt * (p.bn - kHalo) - kHalo + (int)rank * half_bn;
+                int r0 = tt * (p.bn - p.halo) - p.halo + (int)rank * half_bn;
                 if (n0 >= p.N) n0 = max(p.N - kBM, 0);
                 if (r0 >= p.T) r0 = p.T - 1;
                 for (int kb = 0; kb < kblocks; ++kb, ++it) {
@@ -598,7 +600,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             if (*reinterpret_cast<volatile int*>(&sh.abort)) break;
             tc_fence_after();
             const int tt = tile % p.tiles_t, nn = tile / p.tiles_t;
-            const int row0 = tt * (p.bn - kHalo) - kHalo;
+            const int row0 = tt * (p.bn - p.halo) - p.halo;
             const uint32_t acc = tb + b * kAccCols + ((uint32_t)(32 * q) << 16);
             const int c = nn * kPairBM + kBM * (int)rank + 32 * q + lane;
             if (p.cu_seqlens) drain<true>(p, acc, col0, half, row0, c, lane);
@@ -649,14 +651,14 @@ static bool make_codes_map(CUtensorMap* map, const void* base, int64_t rows, int
 // over the persistent CTAs (or CTA pairs) times the tile's columns plus a fixed cost per tile
 // (pipeline fill and drain, in columns); ties go to the wider tile, which reads fewer bytes per
 // product.
-static int choose_bn(int64_t T, int64_t N, int ctas, int tile_channels) {
+static int choose_bn(int64_t T, int64_t N, int ctas, int tile_channels, int halo) {
     static const int kCandidates[] = {256, 224, 192, 160, 128, 96, 64};
     constexpr int64_t kTileCost = 288;  // fitted to the measured times of the widths at T = 4096
     const int64_t tiles_n = (N + tile_channels - 1) / tile_channels;
     int best = 256;
     int64_t best_cost = INT64_MAX;
     for (int bn : kCandidates) {
-        const int64_t tiles = (T + bn - kHalo - 1) / (bn - kHalo) * tiles_n;
+        const int64_t tiles = (T + bn - halo - 1) / (bn - halo) * tiles_n;
         const int64_t grid = tiles < ctas ? tiles : ctas;
         const int64_t cost = (tiles + grid - 1) / grid * (bn + kTileCost);
         if (cost < best_cost) {
@@ -695,12 +697,15 @@ int launch_in_proj_conv(const InProjArgs& a, cudaStream_t s) {
     // problems. fp8 weights: single CTAs (the converters feed one CTA's operand).
     const bool fp8 = a.codes != nullptr;
     const int pairs = sms[dev] / 2;
-    const int bn_pair = choose_bn(a.T, a.N, pairs, kPairBM);
-    const int64_t pair_tiles = (a.T + bn_pair - kHalo - 1) / (bn_pair - kHalo) * ((a.N + kPairBM - 1) / kPairBM);
+    // without conv channels no tile needs the window's leading tokens
+    const int halo = a.C > 0 ? kHalo : 0;
+    const int bn_pair = choose_bn(a.T, a.N, pairs, kPairBM, halo);
+    const int64_t pair_tiles = (a.T + bn_pair - halo - 1) / (bn_pair - halo) * ((a.N + kPairBM - 1) / kPairBM);
     const bool use_pair = !fp8 && pairs >= 1 && pair_tiles >= pairs;
     Params p;
     memset(&p, 0, sizeof(p));
-    p.bn = use_pair ? bn_pair : choose_bn(a.T, a.N, sms[dev], kBM);
+    p.bn = use_pair ? bn_pair : choose_bn(a.T, a.N, sms[dev], kBM, halo);
+    p.halo = halo;
     __half* xh = nullptr;
     if (fp8) {
         if (!a.workspace || a.workspace_bytes < in_proj_fp8_workspace_bytes(a.T, a.K)) return GDN_ERR_WORKSPACE;
@@ -728,7 +733,7 @@ int launch_in_proj_conv(const InProjArgs& a, cudaStream_t s) {
     p.K = (int)a.K;
     p.nseq = (int)a.nseq;
     const int tile_channels = use_pair ? kPairBM : kBM;
-    const int64_t tiles_t = (a.T + p.bn - kHalo - 1) / (p.bn - kHalo);
+    const int64_t tiles_t = (a.T + p.bn - halo - 1) / (p.bn - halo);
     const int64_t tiles = tiles_t * ((a.N + tile_channels - 1) / tile_channels);
     if (tiles > INT32_MAX) return GDN_ERR_SHAPE;
     p.tiles_t = (int)tiles_t;
