@@ -50,6 +50,16 @@ def test_in_proj_conv_matches_matmul_then_conv(T, K, C, rest):
         _close(out[:, :C], gdn.causal_conv1d(y[None, :, :C].contiguous(), cw)[0], max_ulps=2, frac=0.02)
 
 
+@pytest.mark.parametrize("T", [1, 63, 64, 65, 127, 128, 129, 253, 256, 257, 700])
+def test_in_proj_without_conv_channels_matches_matmul(T):
+    """A projection with no conv channels (the decode-time projections, the output projection):
+    its tiles carry no window tokens, so every column of a tile is an output token. Token counts
+    on both sides of the tile edges."""
+    x, w, cw = _case(T, T, 256, 0, 1152)
+    out = gdn.in_proj_conv(x, w, cw, 0)
+    _close(out, x @ w.T)
+
+
 @pytest.mark.parametrize("lens,K,C,rest", [([70, 1, 129, 0, 100, 3], 192, 256, 72),        # single CTAs
                                            ([700, 2, 900, 0, 3, 419, 1], 128, 2048, 256),  # pairs, 160 tokens
                                            ([1000, 1, 0, 700, 3, 502], 128, 256, 128),     # pairs, 64 tokens
