@@ -136,8 +136,12 @@ __global__ void __launch_bounds__(128) decode_attention_kernel(const __grid_cons
             tma_load_4d(st + (DP + dp) * TL::KPanel, &p.tm_v, &sh.full[j & 1], 64 * dp, kvh, n0, b);
         }
     };
-    int loaded = 0;  // (thread 0) blocks whose copies were issued
-    if (tid == 0) {
+    // the thread that issues the copies and the products: with at most 16 query rows warps 1-3
+    // hold no rows (see warp_live below), so a lane of warp 1 takes the role and warp 0, the only
+    // one with softmax work, never waits for an issue
+    const int issuer = rows <= 16 ? 32 : 0;
+    int loaded = 0;  // (issuer) blocks whose copies were issued
+    if (tid == issuer) {
         mbar_arrive_expect_tx(&sh.qbar, (uint32_t)(DP * rows) * kPanelRow);
 #pragma unroll
         for (int dp = 0; dp < DP; ++dp)
@@ -167,13 +171,13 @@ __global__ void __launch_bounds__(128) decode_attention_kernel(const __grid_cons
 #pragma unroll
     for (int e = 0; e < 128; ++e) acc[e] = 0.f;
     bool ok = mbar_wait(&sh.qbar, 0, kSiteTmaLoad);
-    int s_issued = 0, o_issued = 0;  // (thread 0) products issued, for the drain after a failed wait
+    int s_issued = 0, o_issued = 0;  // (issuer) products issued, for the drain after a failed wait
 
     for (int j = 0; j < nb && __syncthreads_and(ok); ++j) {
         const int st = j & 1;
         const uint8_t* stage = sm + TL::KV + st * TL::Stage;
         const int n0 = (j0 + j) * NK;
-        if (tid == 0) {
+        if (tid == issuer) {
             ok = mbar_wait(&sh.full[st], (uint32_t)(j >> 1) & 1, kSiteTmaLoad);
             if (ok) {  // S = Q K^T
                 tc_fence_after();
@@ -245,7 +249,7 @@ __global__ void __launch_bounds__(128) decode_attention_kernel(const __grid_cons
         fence_async_smem();
         tc_fence_before();
         __syncthreads();
-        if (tid == 0) {  // O_blk = P V
+        if (tid == issuer) {  // O_blk = P V
             tc_fence_after();
             const uint64_t dpn = sdesc_kmajor(sm + TL::P, 0);
 #pragma unroll
@@ -263,7 +267,7 @@ __global__ void __launch_bounds__(128) decode_attention_kernel(const __grid_cons
         if (!__all_sync(0xffffffffu, ok)) continue;  // the loop condition ends every thread together
         tc_fence_after();
         // the stage is free again: block j + 2 streams in while block j + 1 is computed
-        if (tid == 0 && loaded < nb) load_block(loaded++);
+        if (tid == issuer && loaded < nb) load_block(loaded++);
 #pragma unroll
         for (int c = 0; c < 2 && warp_live; ++c) {
             float ob[64];
@@ -302,7 +306,7 @@ __global__ void __launch_bounds__(128) decode_attention_kernel(const __grid_cons
             if (owner) p.part_lse[slot] = l > 0.f ? m + log2f(l) : -INFINITY;
         }
     }
-    if (tid == 0) {  // after a failed wait: the copies and products in flight finish before TMEM is freed
+    if (tid == issuer) {  // after a failed wait: the copies and products in flight finish before TMEM is freed
         mbar_wait(&sh.qbar, 0, kSiteDrain);
         for (int j = loaded - 2 < 0 ? 0 : loaded - 2; j < loaded; ++j)
             mbar_wait(&sh.full[j & 1], (uint32_t)(j >> 1) & 1, kSiteDrain);
