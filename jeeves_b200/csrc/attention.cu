@@ -152,7 +152,10 @@ __global__ void __launch_bounds__(128) decode_attention_kernel(const __grid_cons
     // S (M=64, N=64) and O (M=64, N=128: d 0..127 at lane offset 0, d 128..255 at +16): row i of
     // an M=64 accumulator sits in lane i % 16 of quarter i / 16, so lanes 0-15 of each warp hold
     // the softmax rows, and at D = 256 lanes 16-31 hold the second half of O.
-    const uint32_t id_s = make_idesc(kRows, NK, kFmtBF16, false, false);
+    // S as two M = 64, N = 32 products: keys 0-31 at TMEM lane offset 0, keys 32-63 at +16, so
+    // that lanes l and l + 16 of a warp hold the two key halves of row i and split its softmax
+    const uint32_t id_s = make_idesc(kRows, NK / 2, kFmtBF16, false, false);
+    const int kh = lane >> 4;                       // this lane's key half of row i
     const uint32_t id_o = make_idesc(kRows, 128, kFmtBF16, false, true);
     const int i = 16 * warp + (lane & 15);
     const bool owner = lane < 16;                   // holds row i of S
@@ -166,7 +169,7 @@ __global__ void __launch_bounds__(128) decode_attention_kernel(const __grid_cons
     const int r = row_ok ? i / p.G : 0;
     const uint32_t lane_base = (uint32_t)(32 * warp) << 16;
     const bf16* mrow = p.mask + (int64_t)b * p.smb + (int64_t)r * p.smr;
-    float m = -INFINITY, l = 0.f;  // valid in the owner lanes
+    float m = -INFINITY, l = 0.f;  // the row's running max and sum, the same in both key-half lanes
     float acc[128];
 #pragma unroll
     for (int e = 0; e < 128; ++e) acc[e] = 0.f;
@@ -183,20 +186,23 @@ __global__ void __launch_bounds__(128) decode_attention_kernel(const __grid_cons
                 tc_fence_after();
                 const uint64_t dq = sdesc_kmajor(sm + TL::Q, 0), dk = sdesc_kmajor(stage, 0);
 #pragma unroll
-                for (int kk = 0; kk < D / 16; ++kk)
-                    mma_f16(tb + TL::COL_S, sdesc_add(dq, (kk >> 2) * TL::QPanel + (kk & 3) * 32),
-                            sdesc_add(dk, (kk >> 2) * TL::KPanel + (kk & 3) * 32), id_s, kk > 0);
+                for (int kk = 0; kk < D / 16; ++kk) {
+                    const uint64_t a = sdesc_add(dq, (kk >> 2) * TL::QPanel + (kk & 3) * 32);
+                    const uint32_t kb = (kk >> 2) * TL::KPanel + (kk & 3) * 32;
+                    mma_f16(tb + TL::COL_S, a, sdesc_add(dk, kb), id_s, kk > 0);
+                    mma_f16(tb + TL::COL_S + (16u << 16), a, sdesc_add(dk, kb + (NK / 2) * kPanelRow), id_s, kk > 0);
+                }
                 mma_commit(&sh.s_done);
                 ++s_issued;
             }
         }
         // the mask of this row's keys (bf16, kept packed), loaded while the product runs; keys past L
         // and rows past R * G read as -inf
-        uint4 mraw[NK / 8];
-        const bool live = owner && row_ok;
+        uint4 mraw[NK / 16];
+        const bool live = row_ok;
 #pragma unroll
-        for (int c = 0; c < NK / 8; ++c) {
-            const int n = n0 + 8 * c;
+        for (int c = 0; c < NK / 16; ++c) {
+            const int n = n0 + (NK / 2) * kh + 8 * c;
             if (live && n + 8 <= p.L) {
                 mraw[c] = *reinterpret_cast<const uint4*>(mrow + n);
             } else {
@@ -213,13 +219,13 @@ __global__ void __launch_bounds__(128) decode_attention_kernel(const __grid_cons
         ok = __syncthreads_and(ok) && mbar_wait(&sh.s_done, (uint32_t)j & 1, kSiteMma);
         if (!__syncthreads_and(ok)) break;
         tc_fence_after();
-        float sv[NK];
+        float sv[NK / 2];
         float alpha = 0.f;
-        if (warp_live) tmem_ld64_wait(tb + TL::COL_S + lane_base, sv);
-        if (warp_live && owner) {
+        if (warp_live) {  // warp-uniform: both halves of every row, combined with shuffles
+            tmem_ld32_wait(tb + TL::COL_S + lane_base, sv);
             float mb = -INFINITY;
 #pragma unroll
-            for (int c = 0; c < NK / 8; ++c) {
+            for (int c = 0; c < NK / 16; ++c) {
                 const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&mraw[c]);
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
@@ -230,20 +236,22 @@ __global__ void __launch_bounds__(128) decode_attention_kernel(const __grid_cons
                     mb = fmaxf(mb, fmaxf(sv[k0], sv[k0 + 1]));
                 }
             }
+            mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, 16));
             const float m_new = fmaxf(m, mb);
             const float shift = m_new == -INFINITY ? 0.f : m_new;  // a row with every key masked keeps p = 0
             alpha = exp2f(m - shift);
             float ls = 0.f;
 #pragma unroll
-            for (int e = 0; e < NK; ++e) {
+            for (int e = 0; e < NK / 2; ++e) {
                 sv[e] = exp2f(sv[e] - shift);
                 ls += sv[e];
             }
+            ls += __shfl_xor_sync(0xffffffffu, ls, 16);
             l = l * alpha + ls;
             m = m_new;
-            // P (bf16) as the K-major A operand of O_blk = P V: one 64-key panel, row i
+            // P (bf16) as the K-major A operand of O_blk = P V: one 64-key panel, row i, this half
 #pragma unroll
-            for (int c = 0; c < NK / 8; ++c) put_chunk8(sm + TL::P, i, c, sv + 8 * c);
+            for (int c = 0; c < NK / 16; ++c) put_chunk8(sm + TL::P, i, (NK / 16) * kh + c, sv + 8 * c);
         }
         alpha = __shfl_sync(0xffffffffu, alpha, lane & 15);
         fence_async_smem();
