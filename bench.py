@@ -207,6 +207,22 @@ def timed(fn, steps, warmup, rank_sync, stream=None, inner_events=None):
     return start.elapsed_time(stop)
 
 
+def capture(fn):
+    """One CUDA graph of fn(0), after a warm-up call on a side stream (library state and the
+    caching allocator are set up before the capture), as the engine captures its steps
+    (inference/engine.py:337-345)."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        fn(0)
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fn(0)
+    torch.cuda.synchronize()
+    return graph
+
+
 def run_ours(args, rank, world, device, rank_sync, reduce_max):
     import jeeves_b200 as gdn
 
@@ -301,6 +317,53 @@ def run_ours(args, rank, world, device, rank_sync, reduce_max):
     h2d = sum(host[k].numel() * host[k].element_size() for k in ("qkv", "g", "beta", "z"))
     d2h = out_host.numel() * 2 + state_host.numel() * 4
 
+    # The bound of the e2e number: the same copies with no compute, in the same three-stream
+    # pipeline (every rank at once, as they share the host's PCIe and memory), and each direction
+    # alone. e2e can at best reach max(copy pipeline, device step) per step.
+    out_dev = torch.empty(T * HV, D, dtype=torch.bfloat16, device=device)
+    state_dev = torch.empty(1, HV, D, D, dtype=torch.float32, device=device)
+
+    def copy_step(i, up_dir=True, down_dir=True):
+        b = i % 2
+        if up_dir:
+            with torch.cuda.stream(up):
+                up.wait_event(computed[b])
+                for key in ("qkv", "g", "beta", "z"):
+                    dev_sets[b][key].copy_(host[key], non_blocking=True)
+                uploaded[b].record(up)
+            compute.wait_event(uploaded[b])
+        computed[b].record(compute)
+        if down_dir:
+            with torch.cuda.stream(down):
+                down.wait_event(computed[b])
+                out_host.copy_(out_dev, non_blocking=True)
+                state_host.copy_(state_dev, non_blocking=True)
+
+    def copies_timed(steps, warmup, **dirs):
+        for i in range(warmup):
+            copy_step(i, **dirs)
+        torch.cuda.synchronize()
+        rank_sync()
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(compute)
+        up.wait_stream(compute)
+        down.wait_stream(compute)
+        for i in range(steps):
+            copy_step(i, **dirs)
+        compute.wait_stream(up)
+        compute.wait_stream(down)
+        stop.record(compute)
+        torch.cuda.synchronize()
+        rank_sync()
+        return start.elapsed_time(stop) / steps
+
+    copy_ms = reduce_max(copies_timed(args.steps, args.warmup))
+    h2d_ms = reduce_max(copies_timed(args.steps, args.warmup, down_dir=False))
+    d2h_ms = reduce_max(copies_timed(args.steps, args.warmup, up_dir=False))
+    bound_ms = max(copy_ms, ms_step)
+    e2e_value = world * T * args.steps / (e2e_ms / 1e3)
+    e2e_peak = world * T / (bound_ms / 1e3)
+
     result.update({
         "metric": METRIC,
         "value": round(value, 1),
@@ -318,8 +381,15 @@ def run_ours(args, rank, world, device, rank_sync, reduce_max):
                                "chunked gated delta rule (final state), gated RMSNorm",
                    "tokens_per_gpu_step": T, "parallelism": f"replicas x{world} (no collective)",
                    "l2": f"inputs rotate over {n_sets} sets of {set_bytes / MiB:.0f} MiB (> L2)"},
-        "e2e": {"value": round(world * T * args.steps / (e2e_ms / 1e3), 1), "unit": "tokens/s",
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "roofline": {"bound": "pcie (pinned host copies)", "achieved": round(e2e_value, 1),
+                             "peak": round(e2e_peak, 1), "unit": "tokens/s", "frac": round(e2e_value / e2e_peak, 4),
+                             "copy_pipeline_ms_per_step": round(copy_ms, 4),
+                             "h2d_gbs_per_gpu": round(h2d / (h2d_ms / 1e3) / 1e9, 1),
+                             "d2h_gbs_per_gpu": round(d2h / (d2h_ms / 1e3) / 1e9, 1),
+                             "note": "peak = tokens per step / max(the step's copies alone in the same pipeline, the "
+                                     "device step); all ranks copy at once"}},
         "gpu_launches": launches_per_step * args.steps,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(achieved / hbm_peak, 4), "peak_kind": peak_kind,
@@ -392,6 +462,9 @@ def shard(n, rank, world):
 
 
 def bench_decode(gdn, args, device, rank, world, rank_sync, reduce_max, hbm_peak, layers=24, B_total=256, taps=3):
+    """Config 3: the 24-layer decode step (conv step, L2 norms, gated delta rule step in place, gated
+    RMSNorm per layer) captured once as a CUDA graph and replayed, as the engine replays its cycle
+    graphs (inference/engine.py:486); the eager (uncaptured) time is reported beside it."""
     B, _ = shard(B_total, rank, world)
     gen = torch.Generator().manual_seed(3)
     states = [torch.zeros(B, HV, D, D, device=device) for _ in range(layers)]
@@ -411,16 +484,21 @@ def bench_decode(gdn, args, device, rank, world, rank_sync, reduce_max, hbm_peak
             gdn.decode_layer_step(qkv[l], conv_states[l], w[l], g[l], beta[l], states[l], z[l], nw, H,
                                   workspace=workspace)
 
-    ms = reduce_max(timed(step, args.steps, args.warmup, rank_sync)) / args.steps
+    eager_ms = reduce_max(timed(step, args.steps, args.warmup, rank_sync)) / args.steps
+    graph = capture(step)
+    ms = reduce_max(timed(lambda i: graph.replay(), args.steps, args.warmup, rank_sync)) / args.steps
+    del graph
     unit_bytes = 2 * HV * D * D * 4 + 2 * C_QKV * taps * 2 + C_QKV * 2 + HV * 6 + 2 * HV * D * 2
     total = unit_bytes * B * layers
     ach = total / (ms / 1e3) / 1e9
     return {"workload": f"config 3: 24 layers, {B_total} sequences (state [32,128,128] fp32, conv state [8192,3]), "
-                        f"one token per step, fused conv+L2+GDN+gated norm; {B} sequences per GPU",
+                        f"one token per step, conv step + L2 + GDN step + gated norm per layer, the 24-layer step "
+                        f"replayed as one CUDA graph; {B} sequences per GPU",
             "value": round(world * B / (ms / 1e3), 1), "unit": "tokens/s (sequences x steps)", "ms_per_step": round(ms, 4),
+            "eager_ms_per_step": round(eager_ms, 4),
             "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(ach / hbm_peak, 4), "algorithmic_bytes_per_unit": unit_bytes},
-            "gpu_launches": 3 * layers * args.steps}
+            "gpu_launches": 3 * layers * args.steps * 2}  # graph replays and the eager arm
 
 
 def attention_case(B, device, K=4, Hq=HV, Hkv=HV, Dh=D, Lw=4096, seed=5):
@@ -538,75 +616,285 @@ def bench_fp8(gdn, args, device, rank_sync, reduce_max, world, hbm_peak, tc_peak
             **res, "gpu_launches": 6 * args.steps}  # per step of each arm: fp8 2 (row kernel, GEMM), bf16 1; two shapes
 
 
-def bench_verify(gdn, args, device, rank, world, rank_sync, reduce_max, hbm_peak, layers=24, B_total=128, T=5):
+def verify_unit_bytes(design, T=5, taps=3):
+    """Algorithmic bytes per (sequence, layer, step) of the verify layer, for the design built:
+    conv state read and rolled forward, the ext window written and its kept columns read back, the
+    pre-conv qkv of the T tokens, g / beta, z in and y out; then the recurrent state:
+    * "recompute" (the reference's design, inference/engine.py:250-258): the verify reads the state,
+      the commit reads and writes it once more; k and v of the T tokens are kept for the commit;
+    * "snapshots": the verify reads the state and writes T per-token states; the rollback copy that
+      makes snapshot j-1 live is this library's choice and is not counted."""
+    state = HV * D * D * 4
+    conv = C_QKV * taps * 2 * 3 + C_QKV * (taps + T) * 2
+    io = T * C_QKV * 2 + T * HV * 6 + 2 * T * HV * D * 2
+    if design == "recompute":
+        return 3 * state + conv + io + 2 * T * (H * D + HV * D) * 2
+    return state * (1 + T) + conv + io
+
+
+def bench_verify(gdn, args, device, rank, world, rank_sync, reduce_max, hbm_peak, layers=24, B_total=128, T=5,
+                 taps=3):
+    """Config 4: the verify branch of every delta layer (conv step over the conv-state window and
+    the 5 new tokens, the gated delta rule outputs, gated RMSNorm), then the commit of the accepted
+    tokens (recurrent state of every layer, and the conv states from the ext windows in one launch,
+    inference/engine.py:471-474), the whole step replayed as one CUDA graph. Two designs: the
+    reference's recompute (the commit advances each state by the accepted tokens again) and
+    per-token snapshots (the commit copies the accepted snapshot)."""
     B, _ = shard(B_total, rank, world)
     gen = torch.Generator().manual_seed(4)
     states = [torch.zeros(B, HV, D, D, device=device).normal_(0, 0.02) for _ in range(layers)]
-    snaps = torch.empty(B, T, HV, D, D, device=device)  # reused per layer (rollback runs right after)
-    q = [torch.randn(B, T, H, D, device=device).to(torch.bfloat16) for _ in range(layers)]
-    k = [torch.randn(B, T, H, D, device=device).to(torch.bfloat16) for _ in range(layers)]
-    v = [torch.randn(B, T, HV, D, device=device).to(torch.bfloat16) for _ in range(layers)]
+    conv_states = torch.randn(layers, B, C_QKV, taps, device=device).to(torch.bfloat16)
+    ext = torch.empty(layers, B, C_QKV, taps + T, dtype=torch.bfloat16, device=device)
+    w = [(torch.randn(C_QKV, 4, generator=gen) * 0.5).to(torch.bfloat16).to(device) for _ in range(layers)]
+    nw = (torch.rand(D, generator=gen) + 0.5).to(torch.bfloat16).to(device)
+    qkv = [torch.randn(B, T, C_QKV, device=device).to(torch.bfloat16) for _ in range(layers)]
     g = [(-torch.exp(torch.randn(B, T, HV, device=device) * 0.5 - 3.0)) for _ in range(layers)]
     beta = [torch.sigmoid(torch.randn(B, T, HV, device=device)).to(torch.bfloat16) for _ in range(layers)]
+    z = [torch.randn(B, T, HV, D, device=device).to(torch.bfloat16) for _ in range(layers)]
     accepted = torch.randint(1, T + 1, (B,), generator=gen).to(device)
+    out = {}
+    for design in ("recompute", "snapshots"):
+        snaps = ([torch.empty(B, T, HV, D, D, device=device) for _ in range(layers)] if design == "snapshots"
+                 else [None] * layers)
 
-    def step(i):
-        for l in range(layers):
-            gdn.gated_delta_rule_verify(q[l], k[l], v[l], g[l], beta[l], states[l], snapshots=snaps)
-            gdn.gated_delta_rule_rollback(states[l], snaps, accepted)
+        def step(i):
+            pending = [gdn.verify_layer_step(qkv[l], conv_states[l], w[l], g[l], beta[l], states[l], z[l], nw, H,
+                                             ext_out=ext[l], snapshots=snaps[l])[1] for l in range(layers)]
+            for l in range(layers):
+                gdn.verify_layer_commit(pending[l], states[l], accepted)
+            gdn.conv_state_commit(ext, conv_states, accepted)
 
-    ms = reduce_max(timed(step, args.steps, args.warmup, rank_sync)) / args.steps
-    unit_bytes = (HV * D * D * 4 * (1 + T) + T * (2 * H * D * 2 + HV * D * 2 + HV * 6 + HV * D * 2)
-                  + 2 * HV * D * D * 4)  # verify read + T snapshots + inputs/outputs, then the rollback copy
-    total = unit_bytes * B * layers
-    ach = total / (ms / 1e3) / 1e9
-    return {"workload": f"config 4: 24 layers, {B_total} sequences x 5 tokens, 5 fp32 snapshots, rollback by snapshot "
-                        f"copy to accepted U{{1..5}}; {B} sequences per GPU",
-            "value": round(world * B * T / (ms / 1e3), 1), "unit": "scored tokens/s", "ms_per_step": round(ms, 4),
-            "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm_peak, "unit": "GB/s",
-                         "frac": round(ach / hbm_peak, 4), "algorithmic_bytes_per_unit": unit_bytes},
-            "gpu_launches": 2 * layers * args.steps}
+        graph = capture(step)
+        ms = reduce_max(timed(lambda i: graph.replay(), args.steps, args.warmup, rank_sync)) / args.steps
+        del graph, snaps
+        unit = verify_unit_bytes(design, T, taps)
+        ach = unit * B * layers / (ms / 1e3) / 1e9
+        out[design] = {"ms_per_step": round(ms, 4), "value": round(world * B * T / (ms / 1e3), 1),
+                       "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm_peak, "unit": "GB/s",
+                                    "frac": round(ach / hbm_peak, 4), "algorithmic_bytes_per_unit": unit}}
+    best = out["recompute"]
+    return {"workload": f"config 4: 24 layers, {B_total} sequences x 5 tokens: per layer conv step over the conv-state "
+                        f"window (ext kept), gated delta rule outputs, gated RMSNorm; then the commit of U{{1..5}} "
+                        f"accepted tokens (recurrent states, and the conv states of all layers in one launch); the "
+                        f"step replayed as one CUDA graph; {B} sequences per GPU",
+            "design": "recompute (the reference's: the commit advances the state by the accepted tokens)",
+            "value": best["value"], "unit": "scored tokens/s", "ms_per_step": best["ms_per_step"],
+            "roofline": best["roofline"], "snapshots": out["snapshots"],
+            "gpu_launches": (3 * layers + layers + 1) * args.steps * 2}
 
 
 # ------------------------------------------------------------------------------------------
-# CPU baseline: the oracle (a restatement of the reference's eager path) on host cores
+# CPU baseline: the reference's own eager functions (model/model.py) on the host cores when the
+# reference is installed next to the repository (baseline/_ref, or JEEVES_REFERENCE); otherwise
+# the oracle, a restatement of the same eager path
 # ------------------------------------------------------------------------------------------
-def cpu_prefill_once(x, T):
-    import oracle
+def reference_path():
+    for cand in (os.environ.get("JEEVES_REFERENCE"), os.path.join(ROOT, "baseline", "_ref")):
+        if cand and os.path.isfile(os.path.join(cand, "model", "model.py")):
+            return cand
+    return None
 
-    y = oracle.causal_conv1d(x["qkv"], x["w"])
+
+class CpuPath:
+    """The CPU implementation timed as the baseline: the reference's eager functions
+    (torch_chunk_gated_delta_rule, torch_recurrent_gated_delta_rule, causal_conv1d /
+    causal_conv1d_step / eager_conv_step, GatedRMSNorm, gated_delta_rule_advance_inplace) when
+    importable, else the oracle's restatement of them ("port")."""
+
+    def __init__(self):
+        path = reference_path()
+        self.kind, self.where = "port", "oracle/ (fp32 PyTorch restatement of the reference's eager path)"
+        self.mm = None
+        if path is not None:
+            try:
+                if path not in sys.path:
+                    sys.path.append(path)
+                import model.model as mm  # the reference's own module
+
+                self.mm, self.kind = mm, "reference"
+                self.where = f"the reference's eager functions (model/model.py, imported from {os.path.relpath(path, ROOT)})"
+            except Exception as e:  # fall back to the port, saying why
+                self.where += f"; reference import failed: {type(e).__name__}: {e}"
+        if self.mm is None:
+            import oracle
+
+            self.oracle = oracle
+
+    def conv(self, x, w):
+        return self.mm.causal_conv1d(x, w) if self.mm else self.oracle.causal_conv1d(x, w)
+
+    def chunk(self, q, k, v, g, beta, h0=None, final=False):
+        if self.mm:
+            rep = v.shape[2] // q.shape[2]
+            q, k = q.repeat_interleave(rep, dim=2), k.repeat_interleave(rep, dim=2)
+            return self.mm.torch_chunk_gated_delta_rule(q, k, v, g, beta, initial_state=h0, output_final_state=final)
+        return self.oracle.chunk_gated_delta_rule(q, k, v, g, beta, initial_state=h0, output_final_state=final)
+
+    def recurrent(self, q, k, v, g, beta, h0=None, final=False):
+        if self.mm:
+            rep = v.shape[2] // q.shape[2]
+            q, k = q.repeat_interleave(rep, dim=2), k.repeat_interleave(rep, dim=2)
+            return self.mm.torch_recurrent_gated_delta_rule(q, k, v, g, beta, initial_state=h0,
+                                                            output_final_state=final)
+        return self.oracle.recurrent_gated_delta_rule(q, k, v, g, beta, initial_state=h0, output_final_state=final)
+
+    def norm(self, x, z, w):
+        if self.mm:
+            mod = self.mm.GatedRMSNorm(D)
+            with torch.no_grad():
+                mod.weight.copy_(w.float())
+            mod = mod.to(x.dtype)
+            with torch.no_grad():
+                return mod(x, z)
+        return self.oracle.gated_rms_norm(x, z, w)
+
+    def conv_step(self, x, state, w):
+        return self.mm.causal_conv1d_step(x, state, w) if self.mm else self.oracle.causal_conv1d_step(x, state, w)
+
+    def verify_conv(self, state, qkv, w):
+        if self.mm:
+            return self.mm.eager_conv_step(state, qkv, w.reshape(C_QKV, 1, -1), H * D, HV * D, D, D)
+        return self.oracle.conv_step(state, qkv, w, H * D, HV * D, D, D)
+
+    def advance(self, k, v, g, beta, state, steps):
+        if self.mm:
+            return self.mm.gated_delta_rule_advance_inplace(k, v, g, beta, state, steps)
+        state.copy_(self.oracle.advance_gated_delta_rule(k, v, g, beta, state, steps))
+
+
+def cpu_prefill_once(cpu, x, T):
+    y = cpu.conv(x["qkv"], x["w"])
     q = y[..., :H * D].reshape(1, T, H, D)
     k = y[..., H * D:2 * H * D].reshape(1, T, H, D)
     v = y[..., 2 * H * D:].reshape(1, T, HV, D)
-    o, S = oracle.chunk_gated_delta_rule(q, k, v, x["g"], x["beta"], output_final_state=True)
-    return oracle.gated_rms_norm(o.reshape(-1, D), x["z"].reshape(-1, D), x["nw"])
+    o, S = cpu.chunk(q, k, v, x["g"], x["beta"], final=True)
+    return cpu.norm(o.reshape(-1, D), x["z"].reshape(-1, D), x["nw"])
 
 
-def cpu_baseline(T=4096, reps=2):
+def cpu_threads():
     torch.set_num_threads(os.cpu_count() or 1)
+    return torch.get_num_threads()
+
+
+def cpu_baseline(cpu, T=4096, reps=2):
+    cores = cpu_threads()
     x = make_prefill_inputs(seed=1, T=T)
-    cpu_prefill_once(x, T)
+    cpu_prefill_once(cpu, x, T)
     t0 = time.perf_counter()
     for _ in range(reps):
-        cpu_prefill_once(x, T)
+        cpu_prefill_once(cpu, x, T)
     dt = (time.perf_counter() - t0) / reps
-    return {"value": round(T / dt, 1), "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+    return {"value": round(T / dt, 1), "unit": "tokens/s", "cores": cores, "kind": cpu.kind,
             "sample": f"config 1 prefill layer (conv + chunk GDN + gated norm), full T={T}, 1 warm-up + {reps} timed, "
-                      f"oracle/ fp32 PyTorch on {platform.processor() or platform.machine()}"}
+                      f"{cpu.where} on {platform.processor() or platform.machine()}"}
+
+
+def cpu_varlen(cpu):
+    """Config 2 on the CPU: the reference has no packed path, so one chunk call per sequence with its
+    initial and final state (the oracle's definition of the packed call), all 32 sequences once."""
+    cores = cpu_threads()
+    lens = varlen_lengths()
+    gen = torch.Generator().manual_seed(2)
+    t = 0.0
+    for n, L in enumerate(lens):
+        q = torch.randn(1, L, H, D, generator=gen).to(torch.bfloat16)
+        k = torch.randn(1, L, H, D, generator=gen).to(torch.bfloat16)
+        v = torch.randn(1, L, HV, D, generator=gen).to(torch.bfloat16)
+        g = -torch.exp(torch.randn(1, L, HV, generator=gen) * 0.5 - 3.0)
+        beta = torch.sigmoid(torch.randn(1, L, HV, generator=gen)).to(torch.bfloat16)
+        h0 = torch.randn(1, HV, D, D, generator=gen) * 0.02
+        t0 = time.perf_counter()
+        cpu.chunk(q, k, v, g, beta, h0=h0, final=True)
+        t += time.perf_counter() - t0
+    return {"value": round(sum(lens) / t, 1), "unit": "tokens/s", "cores": cores, "kind": cpu.kind,
+            "sample": f"all 32 sequences ({sum(lens)} tokens) once, one chunk call per sequence with initial and "
+                      f"final state: {cpu.where}"}
+
+
+def cpu_decode(cpu, B=256, layers_timed=2, layers=24, taps=4):
+    """Config 3 on the CPU: the decode branch of one layer (conv step, recurrent step of one token,
+    gated norm) at B=256, timed over `layers_timed` layers after one warm-up layer and extrapolated
+    to the 24-layer step (a full step takes about half a minute per layer set here)."""
+    cores = cpu_threads()
+    gen = torch.Generator().manual_seed(3)
+    w = (torch.randn(C_QKV, 4, generator=gen) * 0.5).to(torch.bfloat16)
+    nw = (torch.rand(D, generator=gen) + 0.5).to(torch.bfloat16)
+    conv_state = torch.randn(B, C_QKV, taps, generator=gen).to(torch.bfloat16)
+    state = torch.randn(B, HV, D, D, generator=gen) * 0.02
+    x = torch.randn(B, C_QKV, generator=gen).to(torch.bfloat16)
+    g = -torch.exp(torch.randn(B, 1, HV, generator=gen) * 0.5 - 3.0)
+    beta = torch.sigmoid(torch.randn(B, 1, HV, generator=gen)).to(torch.bfloat16)
+    z = torch.randn(B * HV, D, generator=gen).to(torch.bfloat16)
+
+    def layer():
+        nonlocal state
+        y = cpu.conv_step(x, conv_state, w)
+        q = y[:, None, :H * D].reshape(B, 1, H, D)
+        k = y[:, None, H * D:2 * H * D].reshape(B, 1, H, D)
+        v = y[:, None, 2 * H * D:].reshape(B, 1, HV, D)
+        o, state = cpu.recurrent(q, k, v, g, beta, h0=state, final=True)
+        cpu.norm(o.reshape(-1, D), z, nw)
+
+    layer()
+    t0 = time.perf_counter()
+    for _ in range(layers_timed):
+        layer()
+    per_layer = (time.perf_counter() - t0) / layers_timed
+    return {"value": round(B / (per_layer * layers), 1), "unit": "tokens/s (sequences x steps)", "cores": cores,
+            "kind": cpu.kind, "extrapolated": True,
+            "sample": f"{layers_timed} layers of the decode branch (conv step, one-token recurrent step, gated norm) "
+                      f"at B={B} after 1 warm-up layer, extrapolated to the {layers}-layer step: {cpu.where}"}
+
+
+def cpu_verify(cpu, B=128, T=5, layers_timed=1, layers=24, taps=4):
+    """Config 4 on the CPU, the reference's recompute design: per layer the verify conv over the
+    window, the recurrent outputs of the 5 tokens from the state, the gated norm, then the commit
+    advance by the accepted tokens (gated_delta_rule_advance_inplace); timed over `layers_timed`
+    layers after one warm-up layer and extrapolated to 24 layers."""
+    cores = cpu_threads()
+    gen = torch.Generator().manual_seed(4)
+    w = (torch.randn(C_QKV, 4, generator=gen) * 0.5).to(torch.bfloat16)
+    nw = (torch.rand(D, generator=gen) + 0.5).to(torch.bfloat16)
+    conv_state = torch.randn(B, C_QKV, taps, generator=gen).to(torch.bfloat16)
+    state = torch.randn(B, HV, D, D, generator=gen) * 0.02
+    qkv = torch.randn(B, T, C_QKV, generator=gen).to(torch.bfloat16)
+    g = -torch.exp(torch.randn(B, T, HV, generator=gen) * 0.5 - 3.0)
+    beta = torch.sigmoid(torch.randn(B, T, HV, generator=gen)).to(torch.bfloat16)
+    z = torch.randn(B * T * HV, D, generator=gen).to(torch.bfloat16)
+    accepted = torch.randint(1, T + 1, (B,), generator=gen)
+
+    def layer():
+        _, q, k, v = cpu.verify_conv(conv_state, qkv, w)
+        o, _ = cpu.recurrent(q, k, v, g, beta, h0=state, final=False)
+        cpu.norm(o.reshape(-1, D), z, nw)
+        cpu.advance(k, v, g, beta, state, accepted)
+
+    layer()
+    t0 = time.perf_counter()
+    for _ in range(layers_timed):
+        layer()
+    per_layer = (time.perf_counter() - t0) / layers_timed
+    return {"value": round(B * T / (per_layer * layers), 1), "unit": "scored tokens/s", "cores": cores,
+            "kind": cpu.kind, "extrapolated": True,
+            "sample": f"{layers_timed} layer(s) of verify (conv over the window, 5-token recurrent outputs, gated "
+                      f"norm) + commit advance at B={B} after 1 warm-up layer, extrapolated to {layers} layers: "
+                      f"{cpu.where}"}
 
 
 def run_reference(args, rank, world):
-    """The reference's CPU implementation of the path (oracle port), on this box's host cores."""
+    """The reference's CPU implementation of the path on this box's host cores (its own eager
+    functions when installed, else the oracle port), config 1."""
     if rank != 0:
         return None
-    torch.set_num_threads(os.cpu_count() or 1)
+    cpu = CpuPath()
+    cores = cpu_threads()
     T = 4096
     x = make_prefill_inputs(seed=1, T=T)
     for _ in range(args.warmup):
-        cpu_prefill_once(x, T)
+        cpu_prefill_once(cpu, x, T)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        cpu_prefill_once(x, T)
+        cpu_prefill_once(cpu, x, T)
     dt = time.perf_counter() - t0
     value = T * args.steps / dt
     return {"impl": "reference", "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
@@ -614,10 +902,9 @@ def run_reference(args, rank, world):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (same generator as the GPU arm)",
             "config": {"workload": "config 1: 9B-shaped prefill layer, B=1, T=4096, 16/32 heads (CPU, rank 0 only)"},
-            "cpu_baseline": {"value": round(value, 1), "unit": "tokens/s", "cores": torch.get_num_threads(),
-                             "kind": "port",
-                             "sample": f"full config-1 layer per step: oracle/ (fp32 PyTorch restatement of "
-                                       f"model/model.py eager path) conv + chunk GDN + gated norm, T={T}"},
+            "cpu_baseline": {"value": round(value, 1), "unit": "tokens/s", "cores": cores, "kind": cpu.kind,
+                             "sample": f"full config-1 layer per step (conv + chunk GDN + gated norm, T={T}): "
+                                       f"{cpu.where}"},
             "e2e": {"value": round(value, 1), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
@@ -741,7 +1028,12 @@ def main():
 
     result = run_ours(args, rank, world, device, rank_sync, reduce_max)
     if rank == 0 and world == 1 and args.cpu:
-        result["cpu_baseline"] = cpu_baseline()
+        cpu = CpuPath()
+        result["cpu_baseline"] = cpu_baseline(cpu)
+        if "extra" in result:
+            result["extra"]["varlen"]["cpu_baseline"] = cpu_varlen(cpu)
+            result["extra"]["decode"]["cpu_baseline"] = cpu_decode(cpu)
+            result["extra"]["verify"]["cpu_baseline"] = cpu_verify(cpu)
     if world > 1:
         import torch.distributed as dist
 

@@ -253,6 +253,21 @@ GDN_API int gdn_conv_step(const void* state, const void* qkv, int64_t qkv_stride
                   void* stream);
 
 /*
+ * Conv-state commit after a verify step (replaces the gather of the conv window at
+ * inference/engine.py:473-474, and :381 after a prefill): for every layer l and row b,
+ * state[l, b, c, i] = ext[l, b, c, clamp(accepted[b], 0, seqlen) + i] for i < taps, i.e. the
+ * last `taps` inputs once accepted[b] of the seqlen new tokens are kept (0 keeps the old state).
+ * ext: [layers, B, C, taps + seqlen] bf16 as gdn_conv_step writes it (row stride ext_stride_b,
+ * layer stride ext_stride_layer, in elements); state: [layers, B, C, taps] bf16 (strides
+ * state_stride_b, state_stride_layer); accepted: [B] int64. One launch covers every layer, as
+ * the engine's one gather over its stacked conv states does.
+ */
+GDN_API int gdn_conv_state_commit(const void* ext, void* state, const int64_t* accepted, int64_t layers,
+                                  int64_t batch, int64_t channels, int64_t taps, int64_t seqlen,
+                                  int64_t ext_stride_layer, int64_t ext_stride_b, int64_t state_stride_layer,
+                                  int64_t state_stride_b, void* stream);
+
+/*
  * Output-gated RMSNorm (replaces GatedRMSNorm.forward, model/model.py:150-158):
  * y = bf16(bf16(w * bf16(x * rsqrt(mean(x^2) + eps))) * silu(z)). x, z, y: [rows, dim]
  * bf16 contiguous, w: [dim] bf16; all four 16-byte aligned.

@@ -55,6 +55,7 @@ SIGNATURES: dict[str, list] = {
     "gdn_conv1d_silu": [_p, _i64, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _p],
     "gdn_conv1d_silu_step": [_p, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _p],
     "gdn_conv_step": [_p, _p, _i64, _i64, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p],
+    "gdn_conv_state_commit": [_p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p],
     "gdn_gated_rmsnorm": [_p, _p, _p, _p, _i64, _i64, _f32, _p],
     "gdn_delta_gates": [_p, _i64, _p, _i64, _p, _i32, _p, _p, _p, _p, _i64, _i64, _p],
     "gdn_decode_attention": [_p, _i64, _i64, _i64, _p, _i64, _i64, _i64, _p, _i64, _i64, _i64, _p, _i64, _i64, _p,

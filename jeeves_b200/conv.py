@@ -98,3 +98,31 @@ def conv_step(state, qkv, weight, key_dim: int, value_dim: int, head_k_dim: int,
 
 
 eager_conv_step = conv_step
+
+
+def conv_state_commit(ext: torch.Tensor, state: torch.Tensor, accepted: torch.Tensor) -> None:
+    """After a verify step, keep the conv window of the accepted tokens: ``state[..., b, :, :] =
+    ext[..., b, :, j : j + taps]`` with ``j = clamp(accepted[b], 0, T)`` (the gather of
+    ``inference/engine.py:473-474``). ext ``[B, C, taps + T]`` or ``[layers, B, C, taps + T]`` (as
+    ``conv_step`` writes it; the layer and row dims may be strided slices), state ``[B, C, taps]`` or
+    ``[layers, B, C, taps]`` bf16 (same layout rule), accepted ``[B]`` integers. One launch for
+    every layer."""
+    what = "conv_state_commit"
+    _require_cuda(what, ext, state, accepted)
+    e4, s4 = (ext[None], state[None]) if ext.dim() == 3 else (ext, state)
+    if e4.dim() != 4 or s4.dim() != 4 or e4.shape[:3] != s4.shape[:3]:
+        raise ValueError(f"{what}: expected ext [layers, B, C, taps + T] and state [layers, B, C, taps], got "
+                         f"{tuple(ext.shape)} and {tuple(state.shape)}")
+    L, B, C, taps = s4.shape
+    T = e4.shape[3] - taps
+    if T < 0 or ext.dtype != torch.bfloat16 or state.dtype != torch.bfloat16:
+        raise ValueError(f"{what}: expected bfloat16 ext with at least {taps} columns, got {ext.dtype} "
+                         f"{tuple(ext.shape)} and state {state.dtype}")
+    if e4.stride(3) != 1 or e4.stride(2) != taps + T or s4.stride(3) != 1 or s4.stride(2) != taps:
+        raise ValueError(f"{what}: each row's channels and taps must be contiguous in ext and state")
+    if accepted.shape != (B,) or accepted.dtype not in (torch.int32, torch.int64):
+        raise ValueError(f"accepted: expected {B} integers, got {accepted.dtype} {tuple(accepted.shape)}")
+    status = _lib.load().gdn_conv_state_commit(e4.data_ptr(), s4.data_ptr(), accepted.to(torch.int64).contiguous().data_ptr(),
+                                               L, B, C, taps, T, e4.stride(0), e4.stride(1), s4.stride(0), s4.stride(1),
+                                               _stream())
+    _lib.check(status, what)

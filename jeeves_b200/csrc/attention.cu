@@ -410,9 +410,12 @@ static int launch(const AttentionArgs& a, cudaStream_t s) {
     const int G = (int)(a.H / a.Hkv);
     Params p;
     memset(&p, 0, sizeof(p));
+    // The key maps end at L, not at the cache's length: the last block's keys past L arrive as
+    // zeros (as the reference's masked loads give them), so stale cache slots holding Inf or NaN
+    // never reach S or the P V product.
     if (!make_map4(&p.tm_q, a.q, D, a.H, a.R, a.B, a.qsh, a.qsr, a.qsb, (uint32_t)G, (uint32_t)a.R) ||
-        !make_map4(&p.tm_k, a.k, D, a.Hkv, a.cache_len, a.cache_rows, a.ksh, a.kss, a.ksb, 1, Tile<D>::NK) ||
-        !make_map4(&p.tm_v, a.v, D, a.Hkv, a.cache_len, a.cache_rows, a.vsh, a.vss, a.vsb, 1, Tile<D>::NK))
+        !make_map4(&p.tm_k, a.k, D, a.Hkv, a.L, a.cache_rows, a.ksh, a.kss, a.ksb, 1, Tile<D>::NK) ||
+        !make_map4(&p.tm_v, a.v, D, a.Hkv, a.L, a.cache_rows, a.vsh, a.vss, a.vsb, 1, Tile<D>::NK))
         return GDN_ERR_LAUNCH;
     p.mask = static_cast<const bf16*>(a.mask);
     p.smb = a.msb;

@@ -299,6 +299,20 @@ int gdn_conv_step(const void* state, const void* qkv, int64_t qkv_stride_b, int6
                             (int)kernel_size, key_dim, value_dim, (int)head_dim_k, (int)head_dim_v, as_stream(stream));
 }
 
+int gdn_conv_state_commit(const void* ext, void* state, const int64_t* accepted, int64_t layers, int64_t batch,
+                          int64_t channels, int64_t taps, int64_t seqlen, int64_t ext_stride_layer,
+                          int64_t ext_stride_b, int64_t state_stride_layer, int64_t state_stride_b, void* stream) {
+    if (layers < 0 || batch < 0 || channels < 0 || seqlen < 0 || taps < 1 || taps > 8) return GDN_ERR_SHAPE;
+    if (layers > 65535 || batch > 65535) return GDN_ERR_SHAPE;
+    if (layers == 0 || batch == 0 || channels == 0) return GDN_OK;
+    if (!ext || !state || !accepted) return GDN_ERR_NULL;
+    if (ext_stride_b < channels * (taps + seqlen) || state_stride_b < channels * taps ||
+        (layers > 1 && (ext_stride_layer < batch * ext_stride_b || state_stride_layer < batch * state_stride_b)))
+        return GDN_ERR_SHAPE;
+    return launch_conv_state_commit(ext, state, accepted, layers, batch, channels, (int)taps, seqlen, ext_stride_layer,
+                                    ext_stride_b, state_stride_layer, state_stride_b, as_stream(stream));
+}
+
 int gdn_delta_gates(const void* b, int64_t b_stride, const void* a, int64_t a_stride, const void* dt_bias,
                     int dt_bias_dtype, const float* log_decay_rate, const uint8_t* valid, void* beta, float* g,
                     int64_t rows, int64_t value_heads, void* stream) {

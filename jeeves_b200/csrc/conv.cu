@@ -264,4 +264,32 @@ int launch_conv_step(const void* state, const void* qkv, int64_t sqb, int64_t sq
     return launch_status();
 }
 
+
+// Conv-state commit after a verify step (the gather of inference/engine.py:473-474 and :381):
+// state[l, b, c, i] = ext[l, b, c, clamp(accepted[b], 0, T) + i] for i < taps, over every layer of
+// one launch. One thread per (layer, row, channel); ext rows are taps + T contiguous values.
+__global__ void conv_state_commit_kernel(const bf16* __restrict__ ext, bf16* __restrict__ state,
+                                         const int64_t* __restrict__ accepted, int64_t B, int64_t C, int taps,
+                                         int64_t T, int64_t esl, int64_t esb, int64_t ssl, int64_t ssb) {
+    const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= C) return;
+    const int64_t b = blockIdx.y, l = blockIdx.z;
+    int64_t j = accepted[b];
+    j = j < 0 ? 0 : (j > T ? T : j);
+    const bf16* src = ext + l * esl + b * esb + c * (taps + T) + j;
+    bf16* dst = state + l * ssl + b * ssb + c * taps;
+    for (int i = 0; i < taps; ++i) dst[i] = src[i];
+}
+
+int launch_conv_state_commit(const void* ext, void* state, const int64_t* accepted, int64_t layers, int64_t B,
+                             int64_t C, int taps, int64_t T, int64_t esl, int64_t esb, int64_t ssl, int64_t ssb,
+                             cudaStream_t s) {
+    if (layers == 0 || B == 0 || C == 0) return GDN_OK;
+    constexpr int threads = 256;
+    dim3 grid((unsigned)((C + threads - 1) / threads), (unsigned)B, (unsigned)layers);
+    conv_state_commit_kernel<<<grid, threads, 0, s>>>(static_cast<const bf16*>(ext), static_cast<bf16*>(state),
+                                                      accepted, B, C, taps, T, esl, esb, ssl, ssb);
+    return launch_status();
+}
+
 }  // namespace gdn

@@ -97,6 +97,9 @@ int launch_conv1d_silu_step(const void* x, int64_t sxb, void* state, const void*
 int launch_conv_step(const void* state, const void* qkv, int64_t sqb, int64_t sqt, const void* w, void* ext, void* q,
                      void* k, void* v, int64_t B, int64_t T, int taps, int K, int64_t key_dim, int64_t value_dim, int dk,
                      int dv, cudaStream_t s);
+int launch_conv_state_commit(const void* ext, void* state, const int64_t* accepted, int64_t layers, int64_t B,
+                             int64_t C, int taps, int64_t T, int64_t esl, int64_t esb, int64_t ssl, int64_t ssb,
+                             cudaStream_t s);
 int launch_delta_gates(const void* b, int64_t sb, const void* a, int64_t sa, const void* dt_bias, int dt_f32,
                        const float* rate, const uint8_t* valid, void* beta, float* g, int64_t rows, int HV,
                        cudaStream_t s);

@@ -13,8 +13,11 @@ from __future__ import annotations
 import torch
 
 from . import _lib
-from .conv import causal_conv1d
-from .gated_delta import HEAD_DIM, _require_cuda, _stream, gated_delta_rule_chunk_gated_norm
+from .conv import causal_conv1d, conv_state_commit, conv_step
+from .gated_delta import (HEAD_DIM, _require_cuda, _stream, gated_delta_rule_advance_inplace,
+                          gated_delta_rule_chunk_gated_norm, gated_delta_rule_rollback, gated_delta_rule_step,
+                          gated_delta_rule_verify)
+from .norm import gated_rms_norm
 
 
 def prefill_layer(qkv, conv_weight, g, beta, z, norm_weight, key_heads: int, eps: float = 1e-6, initial_state=None,
@@ -81,6 +84,51 @@ def decode_layer_step(qkv, conv_state, conv_weight, g, beta, state, z, norm_weig
         HEAD_DIM, HEAD_DIM, taps, w.shape[1], float(HEAD_DIM ** -0.5 if scale is None else scale), float(eps), _stream())
     _lib.check(status, what)
     return out
+
+
+def verify_layer_step(qkv, conv_state, conv_weight, g, beta, state, z, norm_weight, key_heads: int, ext_out=None,
+                      eps: float = 1e-6, scale: float | None = None, snapshots=None):
+    """The verify branch of one delta layer for T drafted tokens per row (``inference/engine.py:427-435``
+    without the drafter's mask rows): ``conv_step`` over the conv-state window and the T new tokens
+    (the window ``ext [B, C, taps + T]`` goes to ``ext_out``), the gated delta rule outputs from
+    ``state`` (``delta_outputs``, ``:250-252``; the state is read, not written) and the output-gated
+    RMSNorm. qkv ``[B, T, C]`` pre-conv bf16; conv_state ``[B, C, taps]``; g, beta ``[B, T, HV]``;
+    z ``[B, T, HV, 128]``. Returns ``(y [B, T, HV, 128] bf16, pending)``; ``pending`` goes to
+    ``verify_layer_commit`` once the accepted lengths are known.
+
+    With ``snapshots`` (a ``[B, T, HV, 128, 128]`` fp32 buffer) the verify also writes the state after
+    every token, and the commit copies the accepted one instead of advancing the state again."""
+    what = "verify_layer_step"
+    _require_cuda(what, qkv, conv_state, conv_weight, g, beta, state, z, norm_weight, ext_out, snapshots)
+    if qkv.dim() != 3:
+        raise ValueError(f"qkv: expected [B, T, C], got {tuple(qkv.shape)}")
+    B, T, C = qkv.shape
+    kd = key_heads * HEAD_DIM
+    if C <= 2 * kd or (C - 2 * kd) % HEAD_DIM:
+        raise ValueError(f"qkv: {C} channels do not split into 2 x {kd} key channels and whole value heads")
+    vd = C - 2 * kd
+    _, q, k, v = conv_step(conv_state, qkv, conv_weight, kd, vd, HEAD_DIM, HEAD_DIM, ext_out=ext_out)
+    if snapshots is None:
+        o, _ = gated_delta_rule_step(q, k, v, g, beta, initial_state=state, output_final_state=False, scale=scale)
+    else:
+        o, snapshots = gated_delta_rule_verify(q, k, v, g, beta, state, snapshots=snapshots, scale=scale)
+    y = gated_rms_norm(o.view(-1, HEAD_DIM), z.reshape(-1, HEAD_DIM), norm_weight, eps).view(o.shape)
+    return y, (k, v, g, beta, snapshots)
+
+
+def verify_layer_commit(pending, state, accepted, ext=None, conv_state=None) -> None:
+    """Keep the first ``accepted[b]`` verified tokens of row b in ``state`` (the commit of
+    ``inference/engine.py:471-472``): advance the state by them again (the reference's design,
+    ``delta_commit``), or copy the snapshot after them when the verify wrote snapshots. With ``ext``
+    and ``conv_state`` the conv state is rolled forward too (``conv_state_commit``; the engine runs
+    that once over every layer's stacked conv state, ``:473-474``)."""
+    k, v, g, beta, snapshots = pending
+    if snapshots is None:
+        gated_delta_rule_advance_inplace(k, v, g, beta, state, accepted)
+    else:
+        gated_delta_rule_rollback(state, snapshots, accepted)
+    if ext is not None:
+        conv_state_commit(ext, conv_state, accepted)
 
 
 def in_proj_conv(x, weight, conv_weight, conv_channels: int, cu_seqlens=None, conv_state: bool = False,

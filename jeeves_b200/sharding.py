@@ -60,3 +60,60 @@ def local_varlen(lengths: list[int], rank: int, world: int):
     indices = balance_sequences(lengths, world)[rank]
     local = [lengths[i] for i in indices]
     return indices, local, cu_seqlens_of(local)
+
+
+class PeerFailure(RuntimeError):
+    """A peer rank failed or stopped answering between steps."""
+
+
+class StepGuard:
+    """Failure detection between steps, on the host, over the process group's key-value store.
+
+    Every rank calls ``enter(step)`` before the first launch of a step: it publishes the step it
+    has reached and waits until every peer has reached it too. A rank that fails between steps
+    calls ``fail(reason)`` (``guard.run`` does it for an exception) and stops; its peers then raise
+    ``PeerFailure`` at their next ``enter`` instead of launching work that would wait on it. A peer
+    that exits without a word is caught by the deadline: ``PeerFailure`` after ``timeout_s``
+    seconds without progress. Nothing here touches a GPU; ranks only ever leave between steps,
+    with none of their kernels or collectives in flight.
+    """
+
+    def __init__(self, store, rank: int, world: int, timeout_s: float = 10.0, prefix: str = "gdn_guard"):
+        if world <= 0 or not 0 <= rank < world:
+            raise ValueError(f"rank {rank} outside a world of {world}")
+        self.store, self.rank, self.world, self.timeout_s, self.prefix = store, rank, world, timeout_s, prefix
+
+    def _step_key(self, r: int) -> str:
+        return f"{self.prefix}/step/{r}"
+
+    def _fail_key(self, r: int) -> str:
+        return f"{self.prefix}/failed/{r}"
+
+    def fail(self, reason: str) -> None:
+        self.store.set(self._fail_key(self.rank), reason)
+
+    def enter(self, step: int) -> None:
+        import time
+
+        self.store.set(self._step_key(self.rank), str(step))
+        deadline = time.monotonic() + self.timeout_s
+        waiting = [r for r in range(self.world) if r != self.rank]
+        while waiting:
+            for r in list(waiting):
+                if self.store.check([self._fail_key(r)]):
+                    raise PeerFailure(f"rank {r} failed before step {step}: {self.store.get(self._fail_key(r)).decode()}")
+                if self.store.check([self._step_key(r)]) and int(self.store.get(self._step_key(r))) >= step:
+                    waiting.remove(r)
+            if waiting and time.monotonic() > deadline:
+                raise PeerFailure(f"ranks {waiting} did not reach step {step} within {self.timeout_s} s")
+            if waiting:
+                time.sleep(0.01)
+
+    def run(self, step: int, fn):
+        """``enter(step)``, then ``fn()``; an exception in ``fn`` is published to the peers first."""
+        self.enter(step)
+        try:
+            return fn()
+        except BaseException as e:
+            self.fail(f"{type(e).__name__}: {e}")
+            raise

@@ -157,3 +157,48 @@ def test_attention_kernels_leave_no_device_error():
     from jeeves_b200 import _lib
     torch.cuda.synchronize()
     assert _lib.load().gdn_device_error(None, 0) == 0
+
+
+@pytest.mark.parametrize("B,first_row,H,Hkv,D,Lw,K", [
+    (1, 0, 32, 32, 128, 512, 4),     # 16 rows: the last row count of the single-warp issue path
+    (2, 12, 16, 4, 256, 512, 4),     # 16 rows (R = 4, G = 4) at D = 256
+    (2, 8, 32, 32, 128, 512, 5),     # 17 rows: one row in warp 1
+    (2, 8, 16, 16, 256, 640, 5),     # 17 rows at D = 256
+    (2, 6, 16, 4, 128, 1024, 4),     # 40 rows (R = 10, G = 4): warp 2 partly filled
+    (2, 6, 16, 4, 256, 1024, 4),     # 40 rows at D = 256
+    (2, 5, 32, 16, 128, 512, 5),     # 40 rows (R = 20, G = 2)
+])
+def test_decode_attention_row_counts_around_the_warp_edges(B, first_row, H, Hkv, D, Lw, K):
+    """Row counts that switch the issuing lane (16 / 17 rows) and leave a live warp past warp 0
+    partly filled, at both head dims, held to the same SDPA-relative bounds."""
+    q, k_cache, v_cache, padded, L, first = _attention_case(B * 77 + Lw + first_row, B, first_row, H, Hkv, D, Lw, K)
+    scale = D ** -0.5
+    ref = oracle.decode_attention_f32(q, k_cache, v_cache, _rows(padded, L, first), scale)
+    qd, kd, vd, md = q.cuda(), k_cache.cuda(), v_cache.cuda(), _rows(padded.cuda(), L, first)
+    out = gdn.decode_attention(qd, kd, vd, md, scale)
+    sdpa = _sdpa(qd, kd, vd, md, scale)
+    err, sdpa_err = (out.float().cpu() - ref).abs(), (sdpa.float().cpu() - ref).abs()
+    assert not out.isnan().any()
+    assert err.mean() <= 1.25 * sdpa_err.mean(), (err.mean(), sdpa_err.mean())
+    assert err.max() <= 2 * sdpa_err.max(), (err.max(), sdpa_err.max())
+
+
+@pytest.mark.parametrize("D,Lw", [(128, 2048), (128, 104), (256, 512)])
+@pytest.mark.parametrize("poison", [float("nan"), float("inf")])
+def test_decode_attention_ignores_cache_slots_past_the_keys(D, Lw, poison):
+    """Cache slots at or past L (stale entries the engine may leave there) hold NaN or Inf: the
+    output must stay finite and equal to the output with finite values in those slots, as the
+    reference's masked loads (other=0) make it."""
+    H = Hkv = 32 if D == 128 else 16
+    q, k_cache, v_cache, padded, L, first = _attention_case(Lw + D, 2, 4, H, Hkv, D, Lw)
+    tail = torch.randn(8, 40, Hkv, D).to(torch.bfloat16)
+    k_clean, v_clean = torch.cat((k_cache, tail), 1), torch.cat((v_cache, tail), 1)
+    k_bad, v_bad = k_clean.clone(), v_clean.clone()
+    k_bad[:, L:] = poison
+    v_bad[:, L:] = poison
+    md = _rows(padded.cuda(), L, first)
+    scale = D ** -0.5
+    clean = gdn.decode_attention(q.cuda(), k_clean.cuda(), v_clean.cuda(), md, scale)
+    bad = gdn.decode_attention(q.cuda(), k_bad.cuda(), v_bad.cuda(), md, scale)
+    assert torch.isfinite(bad.float()).all()
+    assert same_bits(bad, clean)

@@ -86,3 +86,63 @@ def test_two_rank_gloo_varlen_shards_equal_one_process(tmp_path):
     path = str(tmp_path / "ok.pt")
     mp.spawn(_worker, args=(2, _free_port(), path), nprocs=2, join=True)
     assert torch.load(path) is True
+
+
+def _guard_worker(rank, world, port, mode, result_dir):
+    """Four steps; rank 1 fails in step 2 (raises, or exits without a word). Rank 0 must learn of it
+    at its next step boundary, before launching step 3, and record what it saw."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import datetime
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=20))
+    guard = sharding.StepGuard(dist.distributed_c10d._get_default_store(), rank, world, timeout_s=3.0)
+    seen = "no failure seen"
+    try:
+        for step in range(4):
+            def work():
+                if rank == 1 and step == 2:
+                    if mode == "exit":
+                        os._exit(3)  # leaves between steps, nothing in flight, no message
+                    raise RuntimeError("planted failure on rank 1")
+                return step
+            guard.run(step, work)
+    except sharding.PeerFailure as e:
+        seen = f"PeerFailure: {e}"
+    except RuntimeError as e:
+        seen = f"own error: {e}"
+    with open(os.path.join(result_dir, f"rank{rank}.txt"), "w") as fh:
+        fh.write(seen)
+
+
+@pytest.mark.parametrize("mode", ["raise", "exit"])
+def test_step_guard_reports_a_failed_peer_without_hanging(tmp_path, mode):
+    """Two gloo ranks as separate processes (as torchrun starts them). The surviving rank raises
+    PeerFailure at the next step boundary (the failed rank's message, or the deadline when it exits
+    without one), and every process ends within the time limit."""
+    import subprocess
+    import sys
+    import time
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    port = _free_port()
+    code = ("import sys; sys.path.insert(0, {root!r}); from tests.test_sharding import _guard_worker; "
+            "_guard_worker({rank}, 2, {port}, {mode!r}, {out!r})")
+    t0 = time.monotonic()
+    procs = [subprocess.Popen([sys.executable, "-c", code.format(root=root, rank=r, port=port, mode=mode,
+                                                                out=str(tmp_path))],
+                              stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL) for r in range(2)]
+    try:
+        codes = [p.wait(timeout=120) for p in procs]
+    finally:
+        for p in procs:
+            if p.poll() is None:
+                p.kill()
+    assert time.monotonic() - t0 < 100
+    seen0 = (tmp_path / "rank0.txt").read_text()
+    assert seen0.startswith("PeerFailure"), seen0
+    if mode == "raise":
+        assert "planted failure" in seen0
+        assert (tmp_path / "rank1.txt").read_text().startswith("own error")
+    else:
+        assert "did not reach step 3" in seen0
+        assert codes[1] == 3 and not (tmp_path / "rank1.txt").exists()
