@@ -498,7 +498,7 @@ def bench_decode(gdn, args, device, rank, world, rank_sync, reduce_max, hbm_peak
             "eager_ms_per_step": round(eager_ms, 4),
             "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm_peak, "unit": "GB/s",
                          "frac": round(ach / hbm_peak, 4), "algorithmic_bytes_per_unit": unit_bytes},
-            "gpu_launches": 3 * layers * args.steps * 2}  # graph replays and the eager arm
+            "gpu_launches": 3 * layers * args.steps * 2}  # conv step, recurrent step, norm per layer: graph and eager arms
 
 
 def attention_case(B, device, K=4, Hq=HV, Hkv=HV, Dh=D, Lw=4096, seed=5):
@@ -948,17 +948,24 @@ def profile_case(name, device):
         x, w, cw = in_proj_case(device)
         for _ in range(2):
             gdn.in_proj_conv(x, w, cw, C_QKV)
-    elif name == "verify":
-        B, T = 128, 5
-        state = torch.randn(B, HV, D, D, device=device) * 0.02
-        q = torch.randn(B, T, H, D, device=device).to(torch.bfloat16)
-        v = torch.randn(B, T, HV, D, device=device).to(torch.bfloat16)
+    elif name == "verify":  # the config-4 step of bench_verify (recompute design), 24 layers
+        B, T, layers, taps = 128, 5, 24, 3
+        states = [torch.randn(B, HV, D, D, device=device) * 0.02 for _ in range(layers)]
+        conv_states = torch.randn(layers, B, C_QKV, taps, device=device).to(torch.bfloat16)
+        ext = torch.empty(layers, B, C_QKV, taps + T, dtype=torch.bfloat16, device=device)
+        w = (torch.randn(C_QKV, 4, device=device) * 0.5).to(torch.bfloat16)
+        nw = torch.ones(D, device=device, dtype=torch.bfloat16)
+        qkv = torch.randn(B, T, C_QKV, device=device).to(torch.bfloat16)
         g = -torch.rand(B, T, HV, device=device) * 0.1
         beta = torch.rand(B, T, HV, device=device).to(torch.bfloat16)
+        z = torch.randn(B, T, HV, D, device=device).to(torch.bfloat16)
         acc = torch.randint(1, T + 1, (B,), device=device)
         for _ in range(2):
-            _, snaps = gdn.gated_delta_rule_verify(q, q, v, g, beta, state)
-            gdn.gated_delta_rule_rollback(state, snaps, acc)
+            pending = [gdn.verify_layer_step(qkv, conv_states[l], w, g, beta, states[l], z, nw, H, ext_out=ext[l])[1]
+                       for l in range(layers)]
+            for l in range(layers):
+                gdn.verify_layer_commit(pending[l], states[l], acc)
+            gdn.conv_state_commit(ext, conv_states, acc)
     else:
         raise SystemExit(f"unknown profile case {name}")
     torch.cuda.synchronize()

@@ -249,12 +249,137 @@ __global__ void conv_step_kernel(const bf16* __restrict__ state, const bf16* __r
     (void)k_heads;
 }
 
+// The same conv with 16-byte accesses: one thread per (row, 8 consecutive channels), for the
+// engine's shapes (K = 4 taps of weight, L = taps + T ext columns known at compile time). The 8
+// channels' ext rows are one contiguous block of 8 L values: the state block and the T token
+// vectors are loaded with 16-byte loads, the block is stored with 16-byte stores, and each token's
+// 8 outputs go out as one 16-byte store (per repeated head for q and k). Same arithmetic as above.
+template <int TAPS, int T>
+__global__ void conv_step_vec_kernel(const bf16* __restrict__ state, const bf16* __restrict__ qkv, int64_t sqb,
+                                     int64_t sqt, const bf16* __restrict__ w, bf16* __restrict__ ext,
+                                     bf16* __restrict__ q, bf16* __restrict__ k, bf16* __restrict__ v, int64_t B,
+                                     int64_t C, int64_t key_dim, int64_t value_dim, int dk, int rep) {
+    constexpr int K = 4, L = TAPS + T;
+    static_assert(TAPS >= K - 1 && TAPS <= 8, "the window covers every tap");
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t groups = C / 8;
+    if (idx >= B * groups) return;
+    const int64_t b = idx / groups, c8 = (idx % groups) * 8;
+    // the ext block: value j of channel c at e[c * L + j]
+    bf16 e[8 * L];
+    {
+        bf16 st[8 * TAPS];  // 8 channels x TAPS, channel-major as stored
+        const uint4* src = reinterpret_cast<const uint4*>(state + (b * C + c8) * TAPS);
+#pragma unroll
+        for (int i = 0; i < TAPS; ++i) reinterpret_cast<uint4*>(st)[i] = src[i];
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+#pragma unroll
+            for (int j = 0; j < TAPS; ++j) e[c * L + j] = st[c * TAPS + j];
+#pragma unroll
+        for (int t = 0; t < T; ++t) {
+            uint4 raw = *reinterpret_cast<const uint4*>(qkv + b * sqb + (int64_t)t * sqt + c8);
+            const bf16* x = reinterpret_cast<const bf16*>(&raw);
+#pragma unroll
+            for (int c = 0; c < 8; ++c) e[c * L + TAPS + t] = x[c];
+        }
+    }
+    uint4* edst = reinterpret_cast<uint4*>(ext + (b * C + c8) * L);
+#pragma unroll
+    for (int i = 0; i < L; ++i) edst[i] = reinterpret_cast<const uint4*>(e)[i];
+    float wt[8][K];
+    {
+        bf16 wr[8 * K];
+        const uint4* wsrc = reinterpret_cast<const uint4*>(w + c8 * K);
+#pragma unroll
+        for (int i = 0; i < K; ++i) reinterpret_cast<uint4*>(wr)[i] = __ldg(wsrc + i);
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+#pragma unroll
+            for (int i = 0; i < K; ++i) wt[c][i] = to_f32(wr[c * K + i]);
+    }
+    bf16* dst;
+    int64_t head_stride = 0, base;
+    const int64_t v_heads = value_dim / dk;
+    if (c8 < 2 * key_dim) {
+        const int64_t kc = c8 < key_dim ? c8 : c8 - key_dim;
+        dst = c8 < key_dim ? q : k;
+        base = ((kc / dk) * rep) * dk + kc % dk;
+        head_stride = dk;
+    } else {
+        dst = v;
+        base = c8 - 2 * key_dim;
+    }
+    const int64_t tok_stride = v_heads * dk;
+#pragma unroll
+    for (int t = 0; t < T; ++t) {
+        uint4 out;
+        bf16* o = reinterpret_cast<bf16*>(&out);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            float acc = 0.f;
+#pragma unroll
+            for (int i = 0; i < K; ++i)
+                acc = __fadd_rn(acc, __fmul_rn(wt[c][i], to_f32(e[c * L + t + TAPS - K + 1 + i])));
+            o[c] = __float2bfloat16_rn(silu_f32(round_bf16(acc)));
+        }
+        bf16* row = dst + (b * T + t) * tok_stride + base;
+        if (head_stride) {
+            for (int r = 0; r < rep; ++r) *reinterpret_cast<uint4*>(row + r * head_stride) = out;
+        } else {
+            *reinterpret_cast<uint4*>(row) = out;
+        }
+    }
+}
+
+template <int TAPS, int T>
+static void conv_step_vec(const bf16* state, const bf16* qkv, int64_t sqb, int64_t sqt, const bf16* w, bf16* ext,
+                          bf16* q, bf16* k, bf16* v, int64_t B, int64_t C, int64_t key_dim, int64_t value_dim, int dk,
+                          int rep, cudaStream_t s) {
+    constexpr int threads = 128;
+    const unsigned blocks = (unsigned)((B * (C / 8) + threads - 1) / threads);
+    conv_step_vec_kernel<TAPS, T><<<blocks, threads, 0, s>>>(state, qkv, sqb, sqt, w, ext, q, k, v, B, C, key_dim,
+                                                             value_dim, dk, rep);
+}
+
+template <int TAPS>
+static bool conv_step_vec_t(int64_t T, const bf16* sp, const bf16* xp, int64_t sqb, int64_t sqt, const bf16* wp,
+                            bf16* ep, bf16* qp, bf16* kp, bf16* vp, int64_t B, int64_t C, int64_t key_dim,
+                            int64_t value_dim, int dk, int rep, cudaStream_t s) {
+    switch (T) {
+#define GDN_CONV_STEP_T(n) \
+    case n: conv_step_vec<TAPS, n>(sp, xp, sqb, sqt, wp, ep, qp, kp, vp, B, C, key_dim, value_dim, dk, rep, s); return true;
+        GDN_CONV_STEP_T(1) GDN_CONV_STEP_T(2) GDN_CONV_STEP_T(3) GDN_CONV_STEP_T(4)
+        GDN_CONV_STEP_T(5) GDN_CONV_STEP_T(6) GDN_CONV_STEP_T(7) GDN_CONV_STEP_T(8)
+#undef GDN_CONV_STEP_T
+        default: return false;
+    }
+}
+
 int launch_conv_step(const void* state, const void* qkv, int64_t sqb, int64_t sqt, const void* w, void* ext, void* q,
                      void* k, void* v, int64_t B, int64_t T, int taps, int K, int64_t key_dim, int64_t value_dim, int dk,
                      int dv, cudaStream_t s) {
     const int64_t C = 2 * key_dim + value_dim;
     if (B == 0 || C == 0) return GDN_OK;
     const int rep = (int)((value_dim / dv) / (key_dim / dk));
+    auto sp = static_cast<const bf16*>(state);
+    auto xp = static_cast<const bf16*>(qkv);
+    auto wp = static_cast<const bf16*>(w);
+    auto ep = static_cast<bf16*>(ext);
+    auto qp = static_cast<bf16*>(q);
+    auto kp = static_cast<bf16*>(k);
+    auto vp = static_cast<bf16*>(v);
+    // 16-byte path: 8-channel groups that never straddle q / k / v or a head, 16-byte aligned
+    // rows, the engine's 4-tap weight with a 3- or 4-column state, and up to 8 new tokens
+    const bool vec = K == 4 && (taps == 3 || taps == 4) && T >= 1 && T <= 8 && key_dim % 8 == 0 &&
+                     value_dim % 8 == 0 && dk % 8 == 0 && dv == dk && sqb % 8 == 0 && sqt % 8 == 0 &&
+                     aligned16(state) && aligned16(qkv) && aligned16(w) && aligned16(ext) && aligned16(q) &&
+                     aligned16(k) && aligned16(v);
+    if (vec) {
+        if (taps == 3) conv_step_vec_t<3>(T, sp, xp, sqb, sqt, wp, ep, qp, kp, vp, B, C, key_dim, value_dim, dk, rep, s);
+        else conv_step_vec_t<4>(T, sp, xp, sqb, sqt, wp, ep, qp, kp, vp, B, C, key_dim, value_dim, dk, rep, s);
+        return launch_status();
+    }
     constexpr int threads = 128;
     dim3 grid((unsigned)((C + threads - 1) / threads), (unsigned)B);
     conv_step_kernel<<<grid, threads, 0, s>>>(static_cast<const bf16*>(state), static_cast<const bf16*>(qkv), sqb, sqt,

@@ -22,16 +22,10 @@ __device__ __forceinline__ void unpack8f(const uint4& raw, float (&v)[8]) {
 
 __device__ __forceinline__ void load8f(const bf16* p, float (&v)[8]) { unpack8f(*reinterpret_cast<const uint4*>(p), v); }
 
-// The normed, gated eight elements of this lane, packed as bf16. Every lane of the warp must
-// call it (the sum of squares is reduced over the half-warp with shuffles).
-__device__ __forceinline__ uint4 gated_norm_row8(const float (&xs)[8], const float (&zs)[8], const float (&ws)[8],
-                                                 float eps) {
-    float sq = 0.f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) sq = fmaf(xs[i], xs[i], sq);
-#pragma unroll
-    for (int o = 8; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-    const float inv = inv_sqrt_rn(sq * (1.0f / kHeadDim) + eps);
+// The normed, gated eight elements x (bf16-valued) of one row, given the row's
+// inv = 1 / sqrt(mean(x^2) + eps), packed as bf16.
+__device__ __forceinline__ uint4 gated_norm_apply8(const float (&xs)[8], const float (&zs)[8], const float (&ws)[8],
+                                                   float inv) {
     float sil[8];
     silu8(zs, sil);
     uint4 raw;
@@ -49,6 +43,28 @@ __device__ __forceinline__ uint4 gated_norm_row8(const float (&xs)[8], const flo
         h[i] = __floats2bfloat162_rn(o2[0], o2[1]);
     }
     return raw;
+}
+
+// Sum of squares of the eight elements of one lane, in element order.
+__device__ __forceinline__ float sum_squares8(const float (&xs)[8]) {
+    float sq = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) sq = __fmaf_rn(xs[i], xs[i], sq);
+    return sq;
+}
+
+// 1 / sqrt(mean(x^2) + eps) of a row of 128 from its sum of squares (the mean's division by 128
+// is exact).
+__device__ __forceinline__ float gated_norm_inv(float sq, float eps) { return inv_sqrt_rn(sq * (1.0f / kHeadDim) + eps); }
+
+// The normed, gated eight elements of this lane, packed as bf16. Every lane of the warp must
+// call it (the sum of squares is reduced over the half-warp with shuffles: offsets 8, 4, 2, 1).
+__device__ __forceinline__ uint4 gated_norm_row8(const float (&xs)[8], const float (&zs)[8], const float (&ws)[8],
+                                                 float eps) {
+    float sq = sum_squares8(xs);
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) sq = __fadd_rn(sq, __shfl_xor_sync(0xffffffffu, sq, o));
+    return gated_norm_apply8(xs, zs, ws, gated_norm_inv(sq, eps));
 }
 
 }  // namespace gdn

@@ -62,7 +62,7 @@ def test_golden_conv_step(golden):
         assert same_bits(a, b)
 
 
-@pytest.mark.parametrize("B,T", [(1, 4), (4, 5), (2, 8)])
+@pytest.mark.parametrize("B,T", [(1, 4), (4, 5), (2, 8), (2, 9)])  # taps + T up to 12 take the 16-byte path
 def test_conv_step_matches_oracle_and_writes_ext_out_only(B, T):
     gen = torch.Generator().manual_seed(10 + B * T)
     key_dim, value_dim, hd, taps = 2048, 4096, 128, 4

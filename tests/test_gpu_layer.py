@@ -163,3 +163,34 @@ def test_prefill_layer_leaves_no_device_error():
     from jeeves_b200 import _lib
     torch.cuda.synchronize()
     assert _lib.load().gdn_device_error(None, 0) == 0
+
+
+@pytest.mark.parametrize("B,H,HV,taps", [(8, 16, 32, 3), (64, 16, 32, 4), (256, 16, 32, 3), (128, 4, 4, 4),
+                                         (3, 2, 4, 3)])
+def test_decode_layer_equals_the_three_separate_calls(B, H, HV, taps):
+    """gdn_decode_layer's output, recurrent state and conv state equal the separate conv-step,
+    recurrent-step and gated-norm calls bit for bit, with both slice widths of the step."""
+    gen = torch.Generator().manual_seed(B + H + taps)
+    C = 2 * H * 128 + HV * 128
+    qkv = (torch.randn(B, C, generator=gen) * 2).to(torch.bfloat16).cuda()
+    cs = torch.randn(B, C, taps, generator=gen).to(torch.bfloat16).cuda()
+    w = (torch.randn(C, 4, generator=gen) * 0.5).to(torch.bfloat16).cuda()
+    g = (-torch.exp(torch.randn(B, HV, generator=gen) * 0.5 - 3.0)).cuda()
+    beta = torch.sigmoid(torch.randn(B, HV, generator=gen)).to(torch.bfloat16).cuda()
+    state = (torch.randn(B, HV, 128, 128, generator=gen) * 0.02).cuda()
+    z = torch.randn(B, HV, 128, generator=gen).to(torch.bfloat16).cuda()
+    nw = (torch.rand(128, generator=gen) + 0.5).to(torch.bfloat16).cuda()
+
+    cs_sep, st_sep = cs.clone(), state.clone()
+    y = gdn.causal_conv1d_step(qkv, cs_sep, w)
+    kd = H * 128
+    q, k, v = y[:, :kd].view(B, 1, H, 128), y[:, kd:2 * kd].view(B, 1, H, 128), y[:, 2 * kd:].view(B, 1, HV, 128)
+    o, st_sep = gdn.gated_delta_rule_step(q, k, v, g.view(B, 1, HV), beta.view(B, 1, HV), initial_state=st_sep,
+                                          output_final_state=True)
+    out_sep = gdn.gated_rms_norm(o.view(-1, 128), z.view(-1, 128), nw).view(B, HV, 128)
+
+    cs_f, st_f = cs.clone(), state.clone()
+    out_f = gdn.decode_layer_step(qkv, cs_f, w, g, beta, st_f, z, nw, H)
+    assert same_bits(cs_f, cs_sep)
+    assert same_bits(st_f, st_sep)
+    assert same_bits(out_f, out_sep)

@@ -129,6 +129,26 @@ def test_resumed_equals_uninterrupted():
     assert same_bits(torch.cat([o_a, o_b], 1), o_full) and same_bits(S_b, S_full)
 
 
+@pytest.mark.parametrize("T", [2, 3, 5])
+def test_final_state_equals_advance_by_all_tokens_and_snapshots(T):
+    """The final state of a recurrent call, the advance by all T tokens and the last per-token
+    snapshot are the same bits, and advancing by j equals snapshot j - 1 (the property the
+    reference pins between its advance kernel and fla's recurrent one)."""
+    B = 6
+    q, k, v, g, beta, h0 = cuda(*gdn_inputs(90 + T, B, T, 16, 32, normalise=False))
+    _, final = gdn.gated_delta_rule_step(q, k, v, g, beta, initial_state=h0, output_final_state=True)
+    adv = h0.clone()
+    gdn.gated_delta_rule_advance_inplace(k, v, g, beta, adv, torch.full((B,), T, device="cuda"))
+    _, snaps = gdn.gated_delta_rule_verify(q, k, v, g, beta, h0)
+    assert same_bits(final, adv) and same_bits(final, snaps[:, T - 1])
+    steps = torch.arange(B, device="cuda") % (T + 1)
+    part = h0.clone()
+    gdn.gated_delta_rule_advance_inplace(k, v, g, beta, part, steps)
+    for b in range(B):
+        j = int(steps[b])
+        assert same_bits(part[b], h0[b] if j == 0 else snaps[b, j - 1]), b
+
+
 def test_varlen_recurrent_equals_per_sequence():
     lens = [3, 0, 11, 6]
     T = sum(lens)
@@ -153,3 +173,55 @@ def test_errors_follow_reference_convention():
         gdn.gated_delta_rule_advance_inplace(k, v, g, beta, h0.transpose(2, 3), torch.ones(2, device="cuda"))
     with pytest.raises(ValueError, match="steps"):
         gdn.gated_delta_rule_advance_inplace(k, v, g, beta, h0.clone(), torch.ones(2, device="cuda"))
+
+
+@pytest.mark.parametrize("T", [2, 5, 8])
+@pytest.mark.parametrize("H,HV", [(2, 4), (16, 32)])
+def test_outputs_only_call_against_float64_and_the_state_writing_call(T, H, HV):
+    """Outputs of a short block without a state write: within the output bound of the float64
+    recurrence, the same bits as the call that also writes the final state, state untouched."""
+    B = 3
+    q, k, v, g, beta, h0 = gdn_inputs(40 + T + HV, B, T, H, HV, normalise=False)
+    o64, _ = oracle.exact_recurrence_f64(q, k, v, g, beta, h0)
+    qc, kc, vc, gc, bc, hc = cuda(q, k, v, g, beta, h0)
+    o, none = gdn.gated_delta_rule_step(qc, kc, vc, gc, bc, initial_state=hc, output_final_state=False)
+    o_seq, _ = gdn.gated_delta_rule_step(qc, kc, vc, gc, bc, initial_state=hc, output_final_state=True)
+    assert none is None and same_bits(hc, h0.cuda())
+    assert maxabs(o, o64) < O_TOL and same_bits(o, o_seq)
+
+
+def test_outputs_only_call_with_gates_equals_gates_then_call():
+    """The gate-fused form of an outputs-only call equals delta_gates followed by the plain call."""
+    gen = torch.Generator().manual_seed(77)
+    B, T, H, HV = 4, 5, 16, 32
+    q, k, v, _, _, h0 = cuda(*gdn_inputs(78, B, T, H, HV, normalise=False))
+    b = torch.randn(B, T, HV, generator=gen).to(torch.bfloat16).cuda()
+    a = torch.randn(B, T, HV, generator=gen).to(torch.bfloat16).cuda()
+    dt = torch.rand(HV, generator=gen).cuda()
+    rate = (-torch.rand(HV, generator=gen) * 4).cuda()
+    beta, g = gdn.delta_gates(b, a, dt, rate)
+    o_ref, _ = gdn.gated_delta_rule_step(q, k, v, g, beta, initial_state=h0, output_final_state=False)
+    o, _ = gdn.gated_delta_rule_step_gates(q, k, v, b, a, dt, rate, initial_state=h0, output_final_state=False)
+    assert same_bits(o, o_ref)
+
+
+@pytest.mark.parametrize("T", [1, 5, 8])
+@pytest.mark.parametrize("snapshots", [False, True])
+def test_batched_rows_equal_the_same_rows_packed_bitwise(T, snapshots):
+    """A batch of rows and the same rows packed with cu_seqlens give the same outputs, final states
+    and snapshots, bit for bit."""
+    B, H, HV = 16, 16, 32
+    q, k, v, g, beta, h0 = cuda(*gdn_inputs(300 + T, B, T, H, HV, normalise=False))
+    if snapshots:
+        o, snaps = gdn.gated_delta_rule_verify(q, k, v, g, beta, h0)
+    else:
+        o, S = gdn.gated_delta_rule_step(q, k, v, g, beta, initial_state=h0, output_final_state=True)
+    cu = torch.arange(0, B * T + 1, T, dtype=torch.int32, device="cuda")
+    pack = lambda t: t.reshape(1, B * T, *t.shape[2:])
+    o_p, S_p = gdn.gated_delta_rule_step(pack(q), pack(k), pack(v), pack(g), pack(beta), initial_state=h0,
+                                         output_final_state=True, cu_seqlens=cu)
+    assert same_bits(o, o_p.view(B, T, HV, 128))
+    if snapshots:
+        assert same_bits(snaps[:, T - 1], S_p)
+    else:
+        assert same_bits(S, S_p)
