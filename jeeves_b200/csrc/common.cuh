@@ -98,6 +98,13 @@ __device__ __forceinline__ void silu8(const float (&x)[8], float (&y)[8]) {
 // 1 / sqrt(x) with an IEEE square root and an IEEE division, as the CPU evaluates rsqrt.
 __device__ __forceinline__ float inv_sqrt_rn(float x) { return __fdiv_rn(1.0f, __fsqrt_rn(x)); }
 
+// Programmatic dependent launch (sm_90+): a kernel launched with the programmatic-serialization
+// attribute may start while the previous kernel in the stream still runs. pdl_wait() blocks until
+// that kernel has finished and its writes are visible (it returns at once for an ordinary
+// launch); pdl_launch_dependents() lets the next such kernel start before this one ends.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Device-side error word written by bounded waits (one per device image of the library;
 // the library is built as a single translation unit, library.cu).
 __device__ int g_device_error = 0;

@@ -137,6 +137,7 @@ int launch_conv1d_silu(const void* x, int64_t sxb, int64_t sxt, const void* w, v
 template <int TAPS, int K>
 __global__ void conv1d_silu_step_kernel(const bf16* __restrict__ x, int64_t sxb, bf16* __restrict__ state,
                                         const bf16* __restrict__ w, bf16* __restrict__ y, int64_t B, int64_t C) {
+    pdl_launch_dependents();  // the decode layer's recurrent step may start loading its state
     const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // group of 8 channels
     const int64_t groups = C / 8;
     if (idx >= B * groups) return;

@@ -39,6 +39,7 @@ struct RecurrentArgs {
     int64_t qsb, qst, qsh, ksb, kst, ksh, vsb, vst, vsh;
     float scale;
     GateInputs gates;  // used instead of g and beta when gates.b is set
+    bool dependent = false;  // programmatic launch: may start while the previous kernel in the stream runs
 };
 int launch_recurrent(const RecurrentArgs& a, cudaStream_t s);
 
@@ -179,6 +180,7 @@ size_t in_proj_fp8_workspace_bytes(int64_t T, int64_t K);
 int launch_bounded_wait_probe(int64_t limit_cycles, cudaStream_t s);
 
 int launch_gated_rmsnorm(const void* x, const void* z, const void* w, void* y, int64_t rows, int dim, float eps,
-                         cudaStream_t s);
+                         cudaStream_t s,
+                         bool dependent = false);
 
 }  // namespace gdn

@@ -79,6 +79,10 @@ __global__ void __launch_bounds__(NT) recurrent_kernel(const RecurrentParams p) 
 #pragma unroll
         for (int r = 0; r < RPT; ++r) S[r] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
+    // As a programmatic dependent of the decode layer's conv step, the state loads above overlap
+    // that kernel; q, k, v come from it, so they are read only past this point.
+    pdl_wait();
+    pdl_launch_dependents();
 
     const bool outputs = p.o != nullptr;
     const TIn* kbase = static_cast<const TIn*>(p.k) + brow * p.ksb + h * p.ksh;
@@ -197,18 +201,31 @@ __global__ void __launch_bounds__(NT) recurrent_kernel(const RecurrentParams p) 
     }
 }
 
+template <typename Kernel>
+static int launch_maybe_dependent(Kernel kernel, dim3 grid, int threads, bool dependent, const RecurrentParams& p,
+                                  cudaStream_t s) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(threads);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = dependent ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, p) == cudaSuccess ? launch_status() : GDN_ERR_LAUNCH;
+}
+
 template <typename TIn, typename TBeta, bool GATES = false>
-static int dispatch_recurrent(const RecurrentParams& p, int64_t rows, cudaStream_t s) {
+static int dispatch_recurrent(const RecurrentParams& p, int64_t rows, cudaStream_t s, bool dependent) {
     // Small grids split the value columns finer so that more SMs share the work.
     const int64_t heads = rows * p.HV;
     if (heads >= 2048) {
         dim3 grid(kHeadDim / 32, p.HV, (unsigned)rows);
-        recurrent_kernel<TIn, TBeta, 32, 128, GATES><<<grid, 128, 0, s>>>(p);
-    } else {
-        dim3 grid(kHeadDim / 16, p.HV, (unsigned)rows);
-        recurrent_kernel<TIn, TBeta, 16, 64, GATES><<<grid, 64, 0, s>>>(p);
+        return launch_maybe_dependent(recurrent_kernel<TIn, TBeta, 32, 128, GATES>, grid, 128, dependent, p, s);
     }
-    return launch_status();
+    dim3 grid(kHeadDim / 16, p.HV, (unsigned)rows);
+    return launch_maybe_dependent(recurrent_kernel<TIn, TBeta, 16, 64, GATES>, grid, 64, dependent, p, s);
 }
 
 int launch_recurrent(const RecurrentArgs& a, cudaStream_t s) {
@@ -224,15 +241,15 @@ int launch_recurrent(const RecurrentArgs& a, cudaStream_t s) {
     p.gates = a.gates;
     if (a.rows == 0) return GDN_OK;
     if (a.gates.b) {
-        return a.qkv_dtype == GDN_BF16 ? dispatch_recurrent<bf16, bf16, true>(p, a.rows, s)
-                                       : dispatch_recurrent<float, bf16, true>(p, a.rows, s);
+        return a.qkv_dtype == GDN_BF16 ? dispatch_recurrent<bf16, bf16, true>(p, a.rows, s, a.dependent)
+                                       : dispatch_recurrent<float, bf16, true>(p, a.rows, s, a.dependent);
     }
     if (a.qkv_dtype == GDN_BF16) {
-        return a.beta_dtype == GDN_BF16 ? dispatch_recurrent<bf16, bf16>(p, a.rows, s)
-                                        : dispatch_recurrent<bf16, float>(p, a.rows, s);
+        return a.beta_dtype == GDN_BF16 ? dispatch_recurrent<bf16, bf16>(p, a.rows, s, a.dependent)
+                                        : dispatch_recurrent<bf16, float>(p, a.rows, s, a.dependent);
     }
-    return a.beta_dtype == GDN_BF16 ? dispatch_recurrent<float, bf16>(p, a.rows, s)
-                                    : dispatch_recurrent<float, float>(p, a.rows, s);
+    return a.beta_dtype == GDN_BF16 ? dispatch_recurrent<float, bf16>(p, a.rows, s, a.dependent)
+                                    : dispatch_recurrent<float, float>(p, a.rows, s, a.dependent);
 }
 
 // Rollback by snapshot: state[b] <- snapshots[b, accepted[b] - 1].
@@ -296,9 +313,10 @@ int launch_decode_layer(const DecodeLayerArgs& a, cudaStream_t s) {
     r.ksb = C; r.kst = C; r.ksh = kHeadDim;
     r.vsb = C; r.vst = C; r.vsh = kHeadDim;
     r.scale = a.scale;
+    r.dependent = true;  // its state loads overlap the conv step
     st = launch_recurrent(r, s);
     if (st != GDN_OK) return st;
-    return launch_gated_rmsnorm(a.out, a.z, a.norm_w, a.out, a.B * a.HV, kHeadDim, a.eps, s);
+    return launch_gated_rmsnorm(a.out, a.z, a.norm_w, a.out, a.B * a.HV, kHeadDim, a.eps, s, true);
 }
 
 }  // namespace gdn
