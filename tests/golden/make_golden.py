@@ -40,8 +40,11 @@ def gdn_inputs(gen, B, T, H, HV, D, dtype, normalise=True):
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("JEEVES_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("JEEVES_REFERENCE"),
+                    help="the reference checkout to import model.model from (or set JEEVES_REFERENCE)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("name the reference checkout with --reference or JEEVES_REFERENCE")
     sys.path.insert(0, args.reference)
     import model.model as ref  # the reference's own module
 

@@ -10,7 +10,9 @@ import torch
 import jeeves_b200 as gdn
 from jeeves_b200 import integration
 
-REFERENCE = os.environ.get("JEEVES_REFERENCE", "/root/reference")
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+# the reference checkout or install: JEEVES_REFERENCE, else the repository's baseline/_ref
+REFERENCE = os.environ.get("JEEVES_REFERENCE") or os.path.join(ROOT, "baseline", "_ref")
 
 
 def test_cpu_tensors_are_rejected_not_computed():
@@ -77,11 +79,9 @@ def test_fla_adapters_require_in_kernel_l2norm():
 
 @pytest.mark.skipif(not os.path.isdir(os.path.join(REFERENCE, "model")), reason="reference checkout not present")
 def test_install_into_reference_module():
-    sys.path.insert(0, REFERENCE)
-    try:
-        import model.model as ref
-    finally:
-        sys.path.remove(REFERENCE)
+    if REFERENCE not in sys.path:
+        sys.path.append(REFERENCE)
+    import model.model as ref
     h = gdn.install(ref)
     try:
         assert ref._fla_chunk_gdr is integration.fla_chunk_gated_delta_rule
