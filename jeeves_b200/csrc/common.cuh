@@ -80,14 +80,83 @@ __device__ __forceinline__ float silu_f32(float x) {
     return d == kInf ? (x == -kInf ? __int_as_float(0x7fffffff) : -0.0f) : q;
 }
 
-// silu_f32 on 8 values: the common-case quotients first; all 8 again with the full formula only
-// when one of them is zero, beyond +-80 or NaN (a branch that real activations almost never take).
+// Two fp32 values in one 64-bit register pair, for sm_100's packed add / sub / mul / fma .rn.f32x2:
+// each lane is rounded exactly as the scalar instruction rounds it, so a packed operation gives
+// bit for bit the two scalar results at half the issued instructions.
+struct f32x2 {
+    unsigned long long v;
+};
+__device__ __forceinline__ f32x2 pack2(float a, float b) {
+    f32x2 r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r.v) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ float2 unpack2(f32x2 x) {
+    float2 r;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(x.v));
+    return r;
+}
+__device__ __forceinline__ f32x2 add2(f32x2 a, f32x2 b) {
+    f32x2 r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
+    return r;
+}
+__device__ __forceinline__ f32x2 sub2(f32x2 a, f32x2 b) {
+    f32x2 r;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
+    return r;
+}
+__device__ __forceinline__ f32x2 mul2(f32x2 a, f32x2 b) {
+    f32x2 r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
+    return r;
+}
+// a * b + c with one rounding per lane
+__device__ __forceinline__ f32x2 fma2(f32x2 a, f32x2 b, f32x2 c) {
+    f32x2 r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r.v) : "l"(a.v), "l"(b.v), "l"(c.v));
+    return r;
+}
+// A bf16 pair (low half first) widened to fp32 lanes.
+__device__ __forceinline__ f32x2 bf2_to_f2(uint32_t raw) { return pack2(__uint_as_float(raw << 16), __uint_as_float(raw & 0xffff0000u)); }
+// Both lanes rounded to bf16, packed low lane first.
+__device__ __forceinline__ uint32_t f2_to_bf2(f32x2 x) {
+    const float2 f = unpack2(x);
+    const __nv_bfloat162 h = __floats2bfloat162_rn(f.x, f.y);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+// Both lanes rounded to bf16 and widened back (round_bf16 of each lane).
+__device__ __forceinline__ f32x2 round_bf16x2(f32x2 x) { return bf2_to_f2(f2_to_bf2(x)); }
+
+// div_markstein(x, 1 + exp(-x)) on both lanes: the common-case SiLU quotient of a pair. The
+// negated denominator -1 - e equals -(1 + e) exactly (round to nearest is symmetric), so the
+// Newton step and the residual are the scalar ones with -d folded into the packed operand.
+__device__ __forceinline__ f32x2 silu2_common(f32x2 x) {
+    const float2 xs = unpack2(x);
+    const f32x2 e = pack2(expf(-xs.x), expf(-xs.y));
+    const f32x2 d = add2(pack2(1.0f, 1.0f), e);
+    const f32x2 nd = sub2(pack2(-1.0f, -1.0f), e);
+    const float2 ds = unpack2(d);
+    float ya, yb;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(ya) : "f"(ds.x));
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(yb) : "f"(ds.y));
+    f32x2 y = pack2(ya, yb);
+    y = fma2(y, fma2(nd, y, pack2(1.0f, 1.0f)), y);
+    const f32x2 q = mul2(x, y);
+    return fma2(fma2(nd, q, x), y, q);
+}
+
+// silu_f32 on 8 values: the common-case quotients first (in pairs); all 8 again with the full
+// formula only when one of them is zero, beyond +-80 or NaN (a branch that real activations
+// almost never take).
 __device__ __forceinline__ void silu8(const float (&x)[8], float (&y)[8]) {
     bool rare = false;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        y[i] = div_markstein(x[i], 1.0f + expf(-x[i]));
-        rare |= !(fabsf(x[i]) <= 80.f) || x[i] == 0.f;
+    for (int i = 0; i < 8; i += 2) {
+        const float2 r = unpack2(silu2_common(pack2(x[i], x[i + 1])));
+        y[i] = r.x;
+        y[i + 1] = r.y;
+        rare |= !(fabsf(x[i]) <= 80.f) || x[i] == 0.f || !(fabsf(x[i + 1]) <= 80.f) || x[i + 1] == 0.f;
     }
     if (rare) {
 #pragma unroll

@@ -56,40 +56,74 @@ __global__ void __launch_bounds__(128) conv1d_silu_kernel(const bf16* __restrict
         const int64_t tt = t0 - (K - 1) + r;
         raw[r] = (tt >= 0 && tt < T) ? __ldg(reinterpret_cast<const uint4*>(xb + tt * sxt)) : make_uint4(0, 0, 0, 0);
     }
-    float wt[8][K];
+    bf16 wr[8 * K];  // channel j's taps at j * K
     {
-        bf16 wr[8 * K];
         const uint4* wsrc = reinterpret_cast<const uint4*>(w + c8 * K);
 #pragma unroll
         for (int i = 0; i < K; ++i) reinterpret_cast<uint4*>(wr)[i] = __ldg(wsrc + i);
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-#pragma unroll
-            for (int i = 0; i < K; ++i) wt[j][i] = to_f32(wr[j * K + i]);
     }
-    int lo = 0;  // with cu_seqlens: the sequence of the current token
+    // With cu_seqlens: the start of each token's sequence, and whether a window reaches before it.
+    int64_t seq_start[kConvRun];
+    bool edge = false;
     if (PACKED) {
-        int hi = nseq;
+        int lo = 0, hi = nseq;
         while (hi - lo > 1) {
             const int mid = (lo + hi) >> 1;
             if (cu[mid] <= t0) lo = mid;
             else hi = mid;
         }
+#pragma unroll
+        for (int j = 0; j < kConvRun; ++j) {
+            const int64_t t = t0 + j;
+            while (lo + 1 < nseq && cu[lo + 1] <= t) ++lo;
+            seq_start[j] = cu[lo];
+            edge |= t < T && t - (K - 1) < seq_start[j];
+        }
     }
     bf16* yb = y + (b * T + t0) * C + c8;
+    if (!edge) {
+        // Every window lies inside its sequence. Channel pairs (2p, 2p + 1) one after the other:
+        // the pair's inputs are widened once, its sums run in packed lanes (products rounded,
+        // then added in tap order from zero), and its outputs are packed back to bf16.
+        uint32_t packed[kConvRun][4];
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+            f32x2 w2[K], xv[R];
+#pragma unroll
+            for (int i = 0; i < K; ++i) w2[i] = pack2(to_f32(wr[2 * p * K + i]), to_f32(wr[(2 * p + 1) * K + i]));
+#pragma unroll
+            for (int r = 0; r < R; ++r)
+                xv[r] = bf2_to_f2(p == 0 ? raw[r].x : p == 1 ? raw[r].y : p == 2 ? raw[r].z : raw[r].w);
+            float pre[2 * kConvRun], out[2 * kConvRun];
+            static_assert(2 * kConvRun == 8, "silu8 takes one pair of channels over the run");
+#pragma unroll
+            for (int j = 0; j < kConvRun; ++j) {
+                f32x2 acc = pack2(0.f, 0.f);
+#pragma unroll
+                for (int i = 0; i < K; ++i) acc = add2(acc, mul2(w2[i], xv[j + i]));
+                const float2 r2 = unpack2(round_bf16x2(acc));
+                pre[2 * j] = r2.x;
+                pre[2 * j + 1] = r2.y;
+            }
+            silu8(pre, out);
+#pragma unroll
+            for (int j = 0; j < kConvRun; ++j) packed[j][p] = f2_to_bf2(pack2(out[2 * j], out[2 * j + 1]));
+        }
+#pragma unroll
+        for (int j = 0; j < kConvRun; ++j)
+            if (t0 + j < T)
+                *reinterpret_cast<uint4*>(yb + j * C) = make_uint4(packed[j][0], packed[j][1], packed[j][2], packed[j][3]);
+        return;
+    }
+    // A window that reaches before the start of its token's sequence: those taps read as zero.
 #pragma unroll
     for (int j = 0; j < kConvRun; ++j) {
         const int64_t t = t0 + j;
         if (t >= T) break;
-        int64_t seq_start = 0;
-        if (PACKED) {
-            while (lo + 1 < nseq && cu[lo + 1] <= t) ++lo;
-            seq_start = cu[lo];
-        }
         float win[K][8];
 #pragma unroll
         for (int i = 0; i < K; ++i) {
-            if (t - (K - 1) + i >= seq_start) unpack8(raw[j + i], win[i]);
+            if (t - (K - 1) + i >= seq_start[j]) unpack8(raw[j + i], win[i]);
             else
 #pragma unroll
                 for (int q = 0; q < 8; ++q) win[i][q] = 0.f;
@@ -99,7 +133,7 @@ __global__ void __launch_bounds__(128) conv1d_silu_kernel(const bf16* __restrict
         for (int q = 0; q < 8; ++q) {
             float acc = 0.f;
 #pragma unroll
-            for (int i = 0; i < K; ++i) acc = __fadd_rn(acc, __fmul_rn(wt[q][i], win[i][q]));
+            for (int i = 0; i < K; ++i) acc = __fadd_rn(acc, __fmul_rn(to_f32(wr[q * K + i]), win[i][q]));
             pre[q] = round_bf16(acc);
         }
         silu8(pre, out);

@@ -28,21 +28,15 @@ __device__ __forceinline__ uint4 gated_norm_apply8(const float (&xs)[8], const f
                                                    float inv) {
     float sil[8];
     silu8(zs, sil);
-    uint4 raw;
-    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&raw);
+    uint32_t out[4];
+    const f32x2 inv2 = pack2(inv, inv);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        float o2[2];
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-            const int e = 2 * i + k;
-            const float normed = round_bf16(xs[e] * inv);
-            const float weighted = round_bf16(ws[e] * normed);
-            o2[k] = weighted * sil[e];
-        }
-        h[i] = __floats2bfloat162_rn(o2[0], o2[1]);
+    for (int i = 0; i < 4; ++i) {  // element pairs (2i, 2i + 1) in packed lanes
+        const f32x2 normed = round_bf16x2(mul2(pack2(xs[2 * i], xs[2 * i + 1]), inv2));
+        const f32x2 weighted = round_bf16x2(mul2(pack2(ws[2 * i], ws[2 * i + 1]), normed));
+        out[i] = f2_to_bf2(mul2(weighted, pack2(sil[2 * i], sil[2 * i + 1])));
     }
-    return raw;
+    return make_uint4(out[0], out[1], out[2], out[3]);
 }
 
 // Sum of squares of the eight elements of one lane, in element order.

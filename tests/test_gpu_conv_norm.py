@@ -23,6 +23,27 @@ def test_conv1d_matches_oracle(B, T, C):
     assert_bf16_matches_cpu(gdn.causal_conv1d(x.cuda(), w.cuda()), oracle.causal_conv1d(x, w))
 
 
+def test_conv1d_special_values_in_either_lane_of_a_channel_pair():
+    # signed zeros, |x| > 80 on both sides and NaN, placed at even and odd channels so that they
+    # reach both lanes of the packed pairs and the per-element path they fall back to
+    gen = torch.Generator().manual_seed(11)
+    T, C = 64, 256
+    x = (torch.randn(1, T, C, generator=gen) * 2).to(torch.bfloat16)
+    w = (torch.randn(C, 4, generator=gen) * 0.5).to(torch.bfloat16)
+    w[3::5] = 0
+    w[8::11, 3] = 100.0
+    x.view(-1)[1::97] = -0.0
+    x.view(-1)[2::89] = 0.0
+    x.view(-1)[3::83] = 300.0
+    x.view(-1)[4::79] = -300.0
+    x.view(-1)[5::601] = float("nan")
+    y = gdn.causal_conv1d(x.cuda(), w.cuda()).cpu()
+    ref = oracle.causal_conv1d(x, w)
+    assert torch.equal(y.isnan(), ref.isnan())
+    assert_bf16_matches_cpu(torch.nan_to_num(y), torch.nan_to_num(ref))
+    assert torch.equal(torch.signbit(y[y == 0]), torch.signbit(ref[y == 0]))
+
+
 def test_conv1d_varlen_restarts_each_sequence():
     gen = torch.Generator().manual_seed(3)
     lens = [5, 40, 1, 70]
@@ -93,7 +114,7 @@ def test_golden_gated_norm(golden):
     assert ((y.float() - c["y"].float()).abs() <= c["y"].float().abs() * 2 ** -6).all()
 
 
-@pytest.mark.parametrize("rows,scale", [(4096 * 32, 2.0), (64, 1e-3), (1536, 2.0)])
+@pytest.mark.parametrize("rows,scale", [(4096 * 32, 2.0), (65536 + 37, 2.0), (64, 1e-3), (1536, 2.0)])
 def test_gated_norm_matches_oracle(rows, scale):
     gen = torch.Generator().manual_seed(rows)
     x = (torch.randn(rows, 128, generator=gen) * scale).to(torch.bfloat16)
