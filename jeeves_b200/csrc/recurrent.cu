@@ -42,13 +42,20 @@ struct RecurrentParams {
 template <typename TIn, typename TBeta, int VS, int NT, bool GATES>
 __global__ void __launch_bounds__(NT) recurrent_kernel(const RecurrentParams p) {
     constexpr int COLG = VS / 4;   // threads along one state row
-    constexpr int NW = NT / 32;
     constexpr int ROWG = NT / COLG;
     constexpr int RPT = kHeadDim / ROWG;  // state rows per thread
-    static_assert(COLG <= 32 && 32 % COLG == 0 && RPT % 4 == 0, "bad tile");
-    __shared__ float4 red[2][2][NW][COLG];
+    // Every tile sums k^T S and q^T S in one tree: 8-row leaves (in row order), leaves combined
+    // pairwise by xor shuffles up to the 32 / COLG leaves of a warp of the 8-row tile (RPT = 8),
+    // then those warp sums in order through shared memory. A tile with RPT = 16 adds its two
+    // leaves in the thread and continues the same tree, so that both tiles give the same bits.
+    constexpr int LEAVES = RPT / 8;
+    constexpr int L = 32 / COLG;          // leaves a warp of the 8-row tile holds
+    constexpr int NREF = 16 / L;          // warp sums of the 8-row tile
+    constexpr int GROUP = L / LEAVES;     // row groups that hold one warp sum after the shuffles
+    static_assert(COLG <= 32 && 32 % COLG == 0 && (RPT == 8 || RPT == 16) && GROUP >= 1, "bad tile");
+    __shared__ float4 red[2][2][NREF][COLG];
 
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int tid = threadIdx.x, lane = tid & 31;
     const int cg = tid % COLG, rg = tid / COLG;
     const int row0 = rg * RPT;
     const int hv = blockIdx.y;
@@ -117,42 +124,51 @@ __global__ void __launch_bounds__(NT) recurrent_kernel(const RecurrentParams p) 
             rq = rsqrtf(qq + 1e-6f) * p.scale;
         }
 
-        // Partial sums over this thread's rows. Row i of k sits in lane i/4, element i%4;
-        // RPT is a multiple of 4, so the element index is the same across the warp.
-        float4 pk = make_float4(0.f, 0.f, 0.f, 0.f), pq = make_float4(0.f, 0.f, 0.f, 0.f);
+        // Partial sums over this thread's rows, one per 8-row leaf. Row i of k sits in lane i/4,
+        // element i%4; RPT is a multiple of 4, so the element index is the same across the warp.
+        float4 pk[LEAVES], pq[LEAVES];
+#pragma unroll
+        for (int e = 0; e < LEAVES; ++e) pk[e] = pq[e] = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
         for (int r = 0; r < RPT; ++r) {
             const int src = (row0 + r) >> 2;
             const float kr = (r & 3) == 0 ? kl.x : (r & 3) == 1 ? kl.y : (r & 3) == 2 ? kl.z : kl.w;
             const float ki = __shfl_sync(0xffffffffu, kr, src) * rk;
-            pk.x += ki * S[r].x; pk.y += ki * S[r].y; pk.z += ki * S[r].z; pk.w += ki * S[r].w;
+            float4& a = pk[r >> 3];
+            a.x += ki * S[r].x; a.y += ki * S[r].y; a.z += ki * S[r].z; a.w += ki * S[r].w;
             if (outputs) {
                 const float qr = (r & 3) == 0 ? ql.x : (r & 3) == 1 ? ql.y : (r & 3) == 2 ? ql.z : ql.w;
                 const float qi = __shfl_sync(0xffffffffu, qr, src) * rq;
-                pq.x += qi * S[r].x; pq.y += qi * S[r].y; pq.z += qi * S[r].z; pq.w += qi * S[r].w;
+                float4& b = pq[r >> 3];
+                b.x += qi * S[r].x; b.y += qi * S[r].y; b.z += qi * S[r].z; b.w += qi * S[r].w;
             }
+        }
+        float4 sk = pk[0], sq = pq[0];
+        if (LEAVES == 2) {
+            sk.x += pk[LEAVES - 1].x; sk.y += pk[LEAVES - 1].y; sk.z += pk[LEAVES - 1].z; sk.w += pk[LEAVES - 1].w;
+            sq.x += pq[LEAVES - 1].x; sq.y += pq[LEAVES - 1].y; sq.z += pq[LEAVES - 1].z; sq.w += pq[LEAVES - 1].w;
         }
 #pragma unroll
-        for (int off = COLG; off < 32; off <<= 1) {
-            pk.x += __shfl_xor_sync(0xffffffffu, pk.x, off);
-            pk.y += __shfl_xor_sync(0xffffffffu, pk.y, off);
-            pk.z += __shfl_xor_sync(0xffffffffu, pk.z, off);
-            pk.w += __shfl_xor_sync(0xffffffffu, pk.w, off);
+        for (int off = COLG; off < COLG * GROUP; off <<= 1) {
+            sk.x += __shfl_xor_sync(0xffffffffu, sk.x, off);
+            sk.y += __shfl_xor_sync(0xffffffffu, sk.y, off);
+            sk.z += __shfl_xor_sync(0xffffffffu, sk.z, off);
+            sk.w += __shfl_xor_sync(0xffffffffu, sk.w, off);
             if (outputs) {
-                pq.x += __shfl_xor_sync(0xffffffffu, pq.x, off);
-                pq.y += __shfl_xor_sync(0xffffffffu, pq.y, off);
-                pq.z += __shfl_xor_sync(0xffffffffu, pq.z, off);
-                pq.w += __shfl_xor_sync(0xffffffffu, pq.w, off);
+                sq.x += __shfl_xor_sync(0xffffffffu, sq.x, off);
+                sq.y += __shfl_xor_sync(0xffffffffu, sq.y, off);
+                sq.z += __shfl_xor_sync(0xffffffffu, sq.z, off);
+                sq.w += __shfl_xor_sync(0xffffffffu, sq.w, off);
             }
         }
-        if (lane < COLG) {
-            red[buf][0][warp][cg] = pk;
-            if (outputs) red[buf][1][warp][cg] = pq;
+        if (rg % GROUP == 0) {
+            red[buf][0][rg / GROUP][cg] = sk;
+            if (outputs) red[buf][1][rg / GROUP][cg] = sq;
         }
         __syncthreads();
         float4 rs = red[buf][0][0][cg];
 #pragma unroll
-        for (int w = 1; w < NW; ++w) {
+        for (int w = 1; w < NREF; ++w) {
             const float4 x = red[buf][0][w][cg];
             rs.x += x.x; rs.y += x.y; rs.z += x.z; rs.w += x.w;
         }
@@ -164,7 +180,7 @@ __global__ void __launch_bounds__(NT) recurrent_kernel(const RecurrentParams p) 
         if (outputs && rg == 0) {
             float4 ps = red[buf][1][0][cg];
 #pragma unroll
-            for (int w = 1; w < NW; ++w) {
+            for (int w = 1; w < NREF; ++w) {
                 const float4 x = red[buf][1][w][cg];
                 ps.x += x.x; ps.y += x.y; ps.z += x.z; ps.w += x.w;
             }
@@ -219,12 +235,19 @@ static int launch_maybe_dependent(Kernel kernel, dim3 grid, int threads, bool de
 template <typename TIn, typename TBeta, bool GATES = false>
 static int dispatch_recurrent(const RecurrentParams& p, int64_t rows, cudaStream_t s, bool dependent) {
     // Small grids split the value columns finer so that more SMs share the work.
+    // Calls of several tokens a sequence (or packed sequences) hold 16 state rows a thread, which
+    // spreads the per-token work (loads, norms, reductions) over twice the state; one-token
+    // decode keeps 8 rows a thread and twice the threads, to keep more state loads in flight.
+    // Both compute the same bits.
     const int64_t heads = rows * p.HV;
+    const bool multi = p.T > 1 || p.cu_seqlens;
     if (heads >= 2048) {
         dim3 grid(kHeadDim / 32, p.HV, (unsigned)rows);
+        if (multi) return launch_maybe_dependent(recurrent_kernel<TIn, TBeta, 32, 64, GATES>, grid, 64, dependent, p, s);
         return launch_maybe_dependent(recurrent_kernel<TIn, TBeta, 32, 128, GATES>, grid, 128, dependent, p, s);
     }
     dim3 grid(kHeadDim / 16, p.HV, (unsigned)rows);
+    if (multi) return launch_maybe_dependent(recurrent_kernel<TIn, TBeta, 16, 32, GATES>, grid, 32, dependent, p, s);
     return launch_maybe_dependent(recurrent_kernel<TIn, TBeta, 16, 64, GATES>, grid, 64, dependent, p, s);
 }
 

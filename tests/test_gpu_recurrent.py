@@ -207,10 +207,13 @@ def test_outputs_only_call_with_gates_equals_gates_then_call():
 
 @pytest.mark.parametrize("T", [1, 5, 8])
 @pytest.mark.parametrize("snapshots", [False, True])
-def test_batched_rows_equal_the_same_rows_packed_bitwise(T, snapshots):
+@pytest.mark.parametrize("B", [16, 64])
+def test_batched_rows_equal_the_same_rows_packed_bitwise(T, snapshots, B):
     """A batch of rows and the same rows packed with cu_seqlens give the same outputs, final states
-    and snapshots, bit for bit."""
-    B, H, HV = 16, 16, 32
+    and snapshots, bit for bit. With T = 1 the batched call runs the one-token tile (8 state rows a
+    thread) and the packed call the multi-token tile (16 rows a thread), below and at the 2048
+    (row, head) pairs where the column slices widen."""
+    H, HV = 16, 32
     q, k, v, g, beta, h0 = cuda(*gdn_inputs(300 + T, B, T, H, HV, normalise=False))
     if snapshots:
         o, snaps = gdn.gated_delta_rule_verify(q, k, v, g, beta, h0)
