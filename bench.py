@@ -623,12 +623,16 @@ def verify_unit_bytes(design, T=5, taps=3):
     * "recompute" (the reference's design, inference/engine.py:250-258): the verify reads the state,
       the commit reads and writes it once more; k and v of the T tokens are kept for the commit;
     * "snapshots": the verify reads the state and writes T per-token states; the rollback copy that
-      makes snapshot j-1 live is this library's choice and is not counted."""
+      makes snapshot j-1 live is this library's choice and is not counted;
+    * "deltas": as "recompute", but the verify keeps each token's update vector (fp32) and the
+      commit reads those and k instead of k and v."""
     state = HV * D * D * 4
     conv = C_QKV * taps * 2 * 3 + C_QKV * (taps + T) * 2
     io = T * C_QKV * 2 + T * HV * 6 + 2 * T * HV * D * 2
     if design == "recompute":
         return 3 * state + conv + io + 2 * T * (H * D + HV * D) * 2
+    if design == "deltas":
+        return 3 * state + conv + io + 2 * T * H * D * 2 + 2 * T * HV * D * 4
     return state * (1 + T) + conv + io
 
 
@@ -637,9 +641,11 @@ def bench_verify(gdn, args, device, rank, world, rank_sync, reduce_max, hbm_peak
     """Config 4: the verify branch of every delta layer (conv step over the conv-state window and
     the 5 new tokens, the gated delta rule outputs, gated RMSNorm), then the commit of the accepted
     tokens (recurrent state of every layer, and the conv states from the ext windows in one launch,
-    inference/engine.py:471-474), the whole step replayed as one CUDA graph. Two designs: the
-    reference's recompute (the commit advances each state by the accepted tokens again) and
-    per-token snapshots (the commit copies the accepted snapshot)."""
+    inference/engine.py:471-474), the whole step replayed as one CUDA graph. Three designs: the
+    reference's recompute (the commit advances each state by the accepted tokens again), kept
+    update vectors (the verify keeps each token's delta and the commit applies the accepted ones in
+    one streaming pass: the recompute's bits without its reductions) and per-token snapshots (the
+    commit copies the accepted snapshot). The headline is the faster of the first two."""
     B, _ = shard(B_total, rank, world)
     gen = torch.Generator().manual_seed(4)
     states = [torch.zeros(B, HV, D, D, device=device).normal_(0, 0.02) for _ in range(layers)]
@@ -653,34 +659,42 @@ def bench_verify(gdn, args, device, rank, world, rank_sync, reduce_max, hbm_peak
     z = [torch.randn(B, T, HV, D, device=device).to(torch.bfloat16) for _ in range(layers)]
     accepted = torch.randint(1, T + 1, (B,), generator=gen).to(device)
     out = {}
-    for design in ("recompute", "snapshots"):
+    for design in ("recompute", "deltas", "snapshots"):
         snaps = ([torch.empty(B, T, HV, D, D, device=device) for _ in range(layers)] if design == "snapshots"
                  else [None] * layers)
+        deltas = ([torch.empty(B, T, HV, D, device=device) for _ in range(layers)] if design == "deltas"
+                  else [None] * layers)
 
         def step(i):
             pending = [gdn.verify_layer_step(qkv[l], conv_states[l], w[l], g[l], beta[l], states[l], z[l], nw, H,
-                                             ext_out=ext[l], snapshots=snaps[l])[1] for l in range(layers)]
+                                             ext_out=ext[l], snapshots=snaps[l], deltas=deltas[l])[1]
+                       for l in range(layers)]
             for l in range(layers):
                 gdn.verify_layer_commit(pending[l], states[l], accepted)
             gdn.conv_state_commit(ext, conv_states, accepted)
 
         graph = capture(step)
         ms = reduce_max(timed(lambda i: graph.replay(), args.steps, args.warmup, rank_sync)) / args.steps
-        del graph, snaps
+        del graph, snaps, deltas
         unit = verify_unit_bytes(design, T, taps)
         ach = unit * B * layers / (ms / 1e3) / 1e9
         out[design] = {"ms_per_step": round(ms, 4), "value": round(world * B * T / (ms / 1e3), 1),
                        "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm_peak, "unit": "GB/s",
                                     "frac": round(ach / hbm_peak, 4), "algorithmic_bytes_per_unit": unit}}
-    best = out["recompute"]
+    names = {"recompute": "recompute (the reference's: the commit advances the state by the accepted tokens)",
+             "deltas": "kept update vectors (the verify keeps each token's delta; the commit applies the accepted "
+                       "ones in one streaming pass, the same bits as the recompute advance)"}
+    head = min(("recompute", "deltas"), key=lambda d: out[d]["ms_per_step"])
+    other = "deltas" if head == "recompute" else "recompute"
+    best = out[head]
     return {"workload": f"config 4: 24 layers, {B_total} sequences x 5 tokens: per layer conv step over the conv-state "
                         f"window (ext kept), gated delta rule outputs, gated RMSNorm; then the commit of U{{1..5}} "
                         f"accepted tokens (recurrent states, and the conv states of all layers in one launch); the "
                         f"step replayed as one CUDA graph; {B} sequences per GPU",
-            "design": "recompute (the reference's: the commit advances the state by the accepted tokens)",
+            "design": names[head],
             "value": best["value"], "unit": "scored tokens/s", "ms_per_step": best["ms_per_step"],
-            "roofline": best["roofline"], "snapshots": out["snapshots"],
-            "gpu_launches": (3 * layers + layers + 1) * args.steps * 2}
+            "roofline": best["roofline"], other: out[other], "snapshots": out["snapshots"],
+            "gpu_launches": (3 * layers + layers + 1) * args.steps * 3}
 
 
 # ------------------------------------------------------------------------------------------
@@ -948,7 +962,7 @@ def profile_case(name, device):
         x, w, cw = in_proj_case(device)
         for _ in range(2):
             gdn.in_proj_conv(x, w, cw, C_QKV)
-    elif name == "verify":  # the config-4 step of bench_verify (recompute design), 24 layers
+    elif name == "verify":  # the config-4 step of bench_verify (kept update vectors), 24 layers
         B, T, layers, taps = 128, 5, 24, 3
         states = [torch.randn(B, HV, D, D, device=device) * 0.02 for _ in range(layers)]
         conv_states = torch.randn(layers, B, C_QKV, taps, device=device).to(torch.bfloat16)
@@ -960,9 +974,10 @@ def profile_case(name, device):
         beta = torch.rand(B, T, HV, device=device).to(torch.bfloat16)
         z = torch.randn(B, T, HV, D, device=device).to(torch.bfloat16)
         acc = torch.randint(1, T + 1, (B,), device=device)
+        deltas = [torch.empty(B, T, HV, D, device=device) for _ in range(layers)]
         for _ in range(2):
-            pending = [gdn.verify_layer_step(qkv, conv_states[l], w, g, beta, states[l], z, nw, H, ext_out=ext[l])[1]
-                       for l in range(layers)]
+            pending = [gdn.verify_layer_step(qkv, conv_states[l], w, g, beta, states[l], z, nw, H, ext_out=ext[l],
+                                             deltas=deltas[l])[1] for l in range(layers)]
             for l in range(layers):
                 gdn.verify_layer_commit(pending[l], states[l], acc)
             gdn.conv_state_commit(ext, conv_states, acc)

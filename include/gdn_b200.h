@@ -134,6 +134,38 @@ GDN_API int gdn_recurrent_gates(const void* q, const void* k, const void* v, int
                                 float scale, void* stream);
 
 /*
+ * The verify outputs of gdn_recurrent (the state is read, not written: o as with state_out =
+ * snapshots = NULL) that also keep each token's update vector
+ *   deltas[b, t, hv, :] = beta_t (v_t - e^{g_t} S_{t-1}^T k_t)    ([B, T, HV, Dv] fp32)
+ * for gdn_delta_commit. Replaces delta_outputs, inference/engine.py:250-252 (gated_delta_rule_step
+ * of the drafted tokens, model/model.py:297-302); o equals gdn_recurrent's bit for bit. Dense
+ * batches only (no cu_seqlens).
+ */
+GDN_API int gdn_recurrent_deltas(const void* q, const void* k, const void* v, int qkv_dtype,
+                                 const float* g, const void* beta, int beta_dtype,
+                                 const float* state_in, void* o, float* deltas,
+                                 int64_t batch, int64_t seqlen, int64_t key_heads, int64_t value_heads,
+                                 int64_t head_dim_k, int64_t head_dim_v,
+                                 int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h,
+                                 int64_t k_stride_b, int64_t k_stride_t, int64_t k_stride_h,
+                                 int64_t v_stride_b, int64_t v_stride_t, int64_t v_stride_h,
+                                 float scale, void* stream);
+
+/*
+ * The commit after gdn_recurrent_deltas: state[b] ([B, HV, Dk, Dv] fp32, in place) advances by
+ * clamp(accepted[b], 0, T) tokens with S <- e^{g_t} S + k_t delta_t^T (k_t L2-normalised in the
+ * kernel). Replaces delta_commit, inference/engine.py:254-258 (gated_delta_rule_advance_inplace,
+ * model/model.py:305-311, model/fla_inplace.py:63-74): the same arithmetic as the advance without
+ * its reductions, so the state equals gdn_recurrent with steps = accepted bit for bit. k: [B, T, H,
+ * Dk] bf16 or fp32 with element strides; g: [B, T, HV] fp32; deltas as gdn_recurrent_deltas wrote
+ * them from the same state, k, g.
+ */
+GDN_API int gdn_delta_commit(float* state, const void* k, int k_dtype, const float* g, const float* deltas,
+                             const int64_t* accepted, int64_t batch, int64_t seqlen, int64_t key_heads,
+                             int64_t value_heads, int64_t head_dim_k, int64_t head_dim_v,
+                             int64_t k_stride_b, int64_t k_stride_t, int64_t k_stride_h, void* stream);
+
+/*
  * Chunked prefill on tcgen05 tensor cores (chunk 64, WY/UT form) with an fp32 state.
  * Replaces gated_delta_rule_chunk, model/model.py:289-294 (fla chunk_gated_delta_rule
  * on CUDA; fp32 eager torch_chunk_gated_delta_rule :242-286). bf16 q, k: [B, T, H, Dk],

@@ -11,9 +11,11 @@ from .gated_delta import (  # noqa: F401
     gated_delta_rule_advance_inplace,
     gated_delta_rule_chunk,
     gated_delta_rule_chunk_gated_norm,
+    gated_delta_rule_delta_commit,
     gated_delta_rule_rollback,
     gated_delta_rule_step,
     gated_delta_rule_verify,
+    gated_delta_rule_verify_deltas,
 )
 from .conv import causal_conv1d, causal_conv1d_step, conv_state_commit, conv_step, eager_conv_step  # noqa: F401
 from .norm import GatedRMSNorm, gated_rms_norm  # noqa: F401

@@ -85,7 +85,7 @@ static int recurrent(const void* q, const void* k, const void* v, int qkv_dtype,
                      int64_t seqlen, int64_t key_heads, int64_t value_heads, int64_t head_dim_k, int64_t head_dim_v,
                      int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h, int64_t k_stride_b,
                      int64_t k_stride_t, int64_t k_stride_h, int64_t v_stride_b, int64_t v_stride_t,
-                     int64_t v_stride_h, float scale, void* stream) {
+                     int64_t v_stride_h, float scale, void* stream, float* deltas = nullptr) {
     if (!known_dtype(qkv_dtype) || !known_dtype(beta_dtype)) return GDN_ERR_DTYPE;
     if (batch < 0 || seqlen < 0 || key_heads <= 0 || value_heads <= 0 || value_heads % key_heads) return GDN_ERR_SHAPE;
     if (batch > 65535 || value_heads > 65535) return GDN_ERR_SHAPE;
@@ -113,7 +113,7 @@ static int recurrent(const void* q, const void* k, const void* v, int qkv_dtype,
         return GDN_ERR_ALIGN;
     if (q && !rows_aligned(q, es, q_stride_b, q_stride_t, q_stride_h)) return GDN_ERR_ALIGN;
     if ((state_in && !aligned16(state_in)) || (state_out && !aligned16(state_out)) ||
-        (snapshots && !aligned16(snapshots)) || (o && !aligned16(o)))
+        (snapshots && !aligned16(snapshots)) || (o && !aligned16(o)) || (deltas && !aligned16(deltas)))
         return GDN_ERR_ALIGN;
     RecurrentArgs a{};
     a.q = q; a.k = k; a.v = v; a.qkv_dtype = qkv_dtype;
@@ -126,6 +126,7 @@ static int recurrent(const void* q, const void* k, const void* v, int qkv_dtype,
     a.vsb = v_stride_b; a.vst = v_stride_t; a.vsh = v_stride_h;
     a.scale = scale;
     a.gates = G;
+    a.deltas = deltas;
     return launch_recurrent(a, as_stream(stream));
 }
 
@@ -151,6 +152,37 @@ int gdn_recurrent_gates(const void* q, const void* k, const void* v, int qkv_dty
     return recurrent(q, k, v, qkv_dtype, nullptr, nullptr, GDN_BF16, gates, state_in, state_out, snapshots, o, steps,
                      cu_seqlens, batch, seqlen, key_heads, value_heads, head_dim_k, head_dim_v, q_stride_b, q_stride_t,
                      q_stride_h, k_stride_b, k_stride_t, k_stride_h, v_stride_b, v_stride_t, v_stride_h, scale, stream);
+}
+
+int gdn_recurrent_deltas(const void* q, const void* k, const void* v, int qkv_dtype, const float* g, const void* beta,
+                         int beta_dtype, const float* state_in, void* o, float* deltas, int64_t batch, int64_t seqlen,
+                         int64_t key_heads, int64_t value_heads, int64_t head_dim_k, int64_t head_dim_v,
+                         int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h, int64_t k_stride_b,
+                         int64_t k_stride_t, int64_t k_stride_h, int64_t v_stride_b, int64_t v_stride_t,
+                         int64_t v_stride_h, float scale, void* stream) {
+    if (batch > 0 && seqlen > 0 && (!q || !o || !deltas)) return GDN_ERR_NULL;
+    return recurrent(q, k, v, qkv_dtype, g, beta, beta_dtype, nullptr, state_in, nullptr, nullptr, o, nullptr, nullptr,
+                     batch, seqlen, key_heads, value_heads, head_dim_k, head_dim_v, q_stride_b, q_stride_t, q_stride_h,
+                     k_stride_b, k_stride_t, k_stride_h, v_stride_b, v_stride_t, v_stride_h, scale, stream, deltas);
+}
+
+int gdn_delta_commit(float* state, const void* k, int k_dtype, const float* g, const float* deltas,
+                     const int64_t* accepted, int64_t batch, int64_t seqlen, int64_t key_heads, int64_t value_heads,
+                     int64_t head_dim_k, int64_t head_dim_v, int64_t k_stride_b, int64_t k_stride_t,
+                     int64_t k_stride_h, void* stream) {
+    if (!known_dtype(k_dtype)) return GDN_ERR_DTYPE;
+    if (batch < 0 || seqlen < 0 || key_heads <= 0 || value_heads <= 0 || value_heads % key_heads) return GDN_ERR_SHAPE;
+    if (batch > 65535 || value_heads > 65535) return GDN_ERR_SHAPE;
+    if (head_dim_k != kHeadDim || head_dim_v != kHeadDim) return GDN_ERR_UNSUPPORTED;
+    if (batch == 0 || seqlen == 0) return GDN_OK;
+    if (!state || !k || !g || !deltas || !accepted) return GDN_ERR_NULL;
+    if (!aligned16(state) || !aligned16(deltas) || !rows_aligned(k, elem_size(k_dtype), k_stride_b, k_stride_t, k_stride_h))
+        return GDN_ERR_ALIGN;
+    DeltaCommitArgs a{};
+    a.state = state; a.k = k; a.k_dtype = k_dtype; a.g = g; a.deltas = deltas; a.accepted = accepted;
+    a.rows = batch; a.T = seqlen; a.H = (int)key_heads; a.HV = (int)value_heads;
+    a.ksb = k_stride_b; a.kst = k_stride_t; a.ksh = k_stride_h;
+    return launch_delta_commit(a, as_stream(stream));
 }
 
 static int chunk_prefill(const void* q, const void* k, const void* v, const float* g, const void* beta, int beta_dtype,

@@ -40,8 +40,22 @@ struct RecurrentArgs {
     float scale;
     GateInputs gates;  // used instead of g and beta when gates.b is set
     bool dependent = false;  // programmatic launch: may start while the previous kernel in the stream runs
+    float* deltas = nullptr;  // [B, T, HV, 128] fp32: each token's update vector, or null
 };
 int launch_recurrent(const RecurrentArgs& a, cudaStream_t s);
+
+struct DeltaCommitArgs {
+    float* state;             // [rows, HV, 128, 128] fp32, advanced in place
+    const void* k;            // [rows, T, H, 128] with element strides ksb, kst, ksh
+    int k_dtype;
+    const float* g;           // [rows, T, HV]
+    const float* deltas;      // [rows, T, HV, 128] fp32 from the verify
+    const int64_t* accepted;  // [rows]
+    int64_t rows, T;
+    int H, HV;
+    int64_t ksb, kst, ksh;
+};
+int launch_delta_commit(const DeltaCommitArgs& a, cudaStream_t s);
 
 struct ChunkArgs {
     const void* q;

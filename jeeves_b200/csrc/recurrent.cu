@@ -30,12 +30,37 @@ struct RecurrentParams {
     void* o;
     const int64_t* steps;
     const int32_t* cu_seqlens;
+    float* deltas;  // [B, T, HV, 128]: each token's update vector delta_t, or null
     int64_t T;
     int HV, rep;
     int64_t qsb, qst, qsh, ksb, kst, ksh, vsb, vst, vsh;
     float scale;
     GateInputs gates;  // beta and g from the raw projections when gates.b is set
 };
+
+// 1 / sqrt(|k|^2 + 1e-6) of one token's key row; lane l holds elements 4l .. 4l + 3.
+__device__ __forceinline__ float key_rnorm(const float4& kl) {
+    const float kk = warp_sum(kl.x * kl.x + kl.y * kl.y + kl.z * kl.z + kl.w * kl.w);
+    return rsqrtf(kk + 1e-6f);
+}
+
+// S <- e^g S + k delta^T on this thread's RPT state rows row0 .. row0 + RPT - 1 (four columns):
+// the normalised key element of row i is lane i/4's element i%4 times rk. The recurrent step
+// and the delta commit share it, so that they leave the same bits.
+template <int RPT>
+__device__ __forceinline__ void state_step(float4 (&S)[RPT], const float4& kl, float rk, float decay,
+                                           const float4& delta, int row0) {
+#pragma unroll
+    for (int r = 0; r < RPT; ++r) {
+        const int src = (row0 + r) >> 2;
+        const float kr = (r & 3) == 0 ? kl.x : (r & 3) == 1 ? kl.y : (r & 3) == 2 ? kl.z : kl.w;
+        const float ki = __shfl_sync(0xffffffffu, kr, src) * rk;
+        S[r].x = decay * S[r].x + ki * delta.x;
+        S[r].y = decay * S[r].y + ki * delta.y;
+        S[r].z = decay * S[r].z + ki * delta.z;
+        S[r].w = decay * S[r].w + ki * delta.w;
+    }
+}
 
 // GATES: beta and g are computed from p.gates (a separate instantiation, so that the plain
 // path keeps its code unchanged).
@@ -115,8 +140,7 @@ __global__ void __launch_bounds__(NT) recurrent_kernel(const RecurrentParams p) 
             bt = to_f32(beta[gi]);
         }
 
-        const float kk = warp_sum(kl.x * kl.x + kl.y * kl.y + kl.z * kl.z + kl.w * kl.w);
-        const float rk = rsqrtf(kk + 1e-6f);
+        const float rk = key_rnorm(kl);
         float rq = 0.f, qk = 0.f;
         if (outputs) {
             const float qq = warp_sum(ql.x * ql.x + ql.y * ql.y + ql.z * ql.z + ql.w * ql.w);
@@ -192,16 +216,8 @@ __global__ void __launch_bounds__(NT) recurrent_kernel(const RecurrentParams p) 
             out.w = decay * ps.w + qkn * delta.w;
             store4(static_cast<TIn*>(p.o) + gi * kHeadDim + col, out);
         }
-#pragma unroll
-        for (int r = 0; r < RPT; ++r) {
-            const int src = (row0 + r) >> 2;
-            const float kr = (r & 3) == 0 ? kl.x : (r & 3) == 1 ? kl.y : (r & 3) == 2 ? kl.z : kl.w;
-            const float ki = __shfl_sync(0xffffffffu, kr, src) * rk;
-            S[r].x = decay * S[r].x + ki * delta.x;
-            S[r].y = decay * S[r].y + ki * delta.y;
-            S[r].z = decay * S[r].z + ki * delta.z;
-            S[r].w = decay * S[r].w + ki * delta.w;
-        }
+        if (p.deltas && rg == 0) *reinterpret_cast<float4*>(p.deltas + gi * kHeadDim + col) = delta;
+        state_step(S, kl, rk, decay, delta, row0);
         if (p.snapshots) {
             float* dst = p.snapshots + ((brow * p.T + tok) * p.HV + hv) * (int64_t)(kHeadDim * kHeadDim) +
                          (int64_t)row0 * kHeadDim + col;
@@ -215,6 +231,66 @@ __global__ void __launch_bounds__(NT) recurrent_kernel(const RecurrentParams p) 
 #pragma unroll
         for (int r = 0; r < RPT; ++r) stg_stream(reinterpret_cast<float4*>(dst + r * kHeadDim), S[r]);
     }
+}
+
+// The commit of a verify that kept its update vectors (gdn_recurrent_deltas): state[n] advances
+// by clamp(accepted[n], 0, T) tokens with S <- e^{g_t} S + k_t delta_t^T, the recurrent step's
+// own arithmetic (state_step) without its reductions, so it leaves the bits the advance would.
+// Pure streaming: one CTA per 128 x VS slice, the slice loaded once, every token applied in
+// registers, stored once.
+struct DeltaCommitParams {
+    float* state;
+    const void* k;
+    const float* g;
+    const float* deltas;
+    const int64_t* accepted;
+    int64_t T;
+    int HV, rep;
+    int64_t ksb, kst, ksh;
+};
+
+template <typename TIn, int VS, int NT>
+__global__ void __launch_bounds__(NT) delta_commit_kernel(const DeltaCommitParams p) {
+    constexpr int COLG = VS / 4;
+    constexpr int ROWG = NT / COLG;
+    constexpr int RPT = kHeadDim / ROWG;
+    static_assert(COLG <= 32 && 32 % COLG == 0 && RPT % 4 == 0, "bad tile");
+    const int tid = threadIdx.x, lane = tid & 31;
+    const int cg = tid % COLG, rg = tid / COLG;
+    const int row0 = rg * RPT;
+    const int hv = blockIdx.y;
+    const int64_t n = blockIdx.z;
+    const int h = hv / p.rep;
+    const int col = blockIdx.x * VS + cg * 4;
+    const int64_t a = p.accepted[n];
+    const int64_t nsteps = a < 0 ? 0 : (a > p.T ? p.T : a);
+    if (nsteps == 0) return;  // nothing accepted: the state stays as it is
+    float* tile = p.state + (n * p.HV + hv) * (int64_t)(kHeadDim * kHeadDim) + (int64_t)row0 * kHeadDim + col;
+    float4 S[RPT];
+#pragma unroll
+    for (int r = 0; r < RPT; ++r) S[r] = ldg_stream(reinterpret_cast<const float4*>(tile + r * kHeadDim));
+    const TIn* kbase = static_cast<const TIn*>(p.k) + n * p.ksb + h * p.ksh;
+    for (int64_t t = 0; t < nsteps; ++t) {
+        const float4 kl = load4(kbase + t * p.kst + 4 * lane);
+        const int64_t gi = (n * p.T + t) * p.HV + hv;
+        const float decay = expf(p.g[gi]);
+        const float4 delta = *reinterpret_cast<const float4*>(p.deltas + gi * kHeadDim + col);
+        state_step(S, kl, key_rnorm(kl), decay, delta, row0);
+    }
+#pragma unroll
+    for (int r = 0; r < RPT; ++r) stg_stream(reinterpret_cast<float4*>(tile + r * kHeadDim), S[r]);
+}
+
+int launch_delta_commit(const DeltaCommitArgs& a, cudaStream_t s) {
+    if (a.rows == 0 || a.T == 0) return GDN_OK;
+    DeltaCommitParams p;
+    p.state = a.state; p.k = a.k; p.g = a.g; p.deltas = a.deltas; p.accepted = a.accepted;
+    p.T = a.T; p.HV = a.HV; p.rep = a.HV / a.H;
+    p.ksb = a.ksb; p.kst = a.kst; p.ksh = a.ksh;
+    dim3 grid(kHeadDim / 32, a.HV, (unsigned)a.rows);
+    if (a.k_dtype == GDN_BF16) delta_commit_kernel<bf16, 32, 128><<<grid, 128, 0, s>>>(p);
+    else delta_commit_kernel<float, 32, 128><<<grid, 128, 0, s>>>(p);
+    return launch_status();
 }
 
 template <typename Kernel>
@@ -255,7 +331,7 @@ int launch_recurrent(const RecurrentArgs& a, cudaStream_t s) {
     RecurrentParams p;
     p.q = a.q; p.k = a.k; p.v = a.v; p.g = a.g; p.beta = a.beta;
     p.state_in = a.state_in; p.state_out = a.state_out; p.snapshots = a.snapshots; p.o = a.o;
-    p.steps = a.steps; p.cu_seqlens = a.cu_seqlens;
+    p.steps = a.steps; p.cu_seqlens = a.cu_seqlens; p.deltas = a.deltas;
     p.T = a.T; p.HV = a.HV; p.rep = a.HV / a.H;
     p.qsb = a.qsb; p.qst = a.qst; p.qsh = a.qsh;
     p.ksb = a.ksb; p.kst = a.kst; p.ksh = a.ksh;

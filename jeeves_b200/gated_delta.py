@@ -268,6 +268,63 @@ def gated_delta_rule_verify(q, k, v, g, beta, state, snapshots=None, scale=None)
     return o, snapshots
 
 
+def gated_delta_rule_verify_deltas(q, k, v, g, beta, state, deltas=None, scale=None):
+    """Score T drafted tokens from ``state`` (read, not written) and keep each token's update vector;
+    returns ``(o, deltas)`` with ``deltas [B, T, HV, 128]`` fp32 = beta_t (v_t - e^{g_t} S_{t-1}^T k_t).
+
+    ``o`` is ``gated_delta_rule_step(..., output_final_state=False)[0]`` bit for bit (the engine's
+    ``delta_outputs``, ``inference/engine.py:249-252``); ``gated_delta_rule_delta_commit`` then makes the
+    accepted tokens' state live without re-running their reductions."""
+    what = "gated_delta_rule_verify_deltas"
+    _require_cuda(what, q, k, v, g, beta, state, deltas)
+    B, T, H, HV = _check_qkv(what, q, k, v)
+    g, beta = _gates(what, g, beta, B, T, HV)
+    h0 = _state_arg(what, state, B, HV, name="state")
+    shape = (B, T, HV, HEAD_DIM)
+    if deltas is None:
+        deltas = torch.empty(shape, dtype=torch.float32, device=q.device)
+    elif deltas.shape != shape or deltas.dtype != torch.float32 or not deltas.is_contiguous():
+        raise ValueError(f"deltas: expected a contiguous float32 tensor of shape {shape}, got {deltas.dtype} "
+                         f"{tuple(deltas.shape)}")
+    q, k, v = _heads_last_contiguous(q), _heads_last_contiguous(k), _heads_last_contiguous(v)
+    o = torch.empty(B, T, HV, HEAD_DIM, dtype=q.dtype, device=q.device)
+    status = _lib.load().gdn_recurrent_deltas(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), _DTYPES[k.dtype], g.data_ptr(), beta.data_ptr(), _DTYPES[beta.dtype],
+        _ptr(h0), o.data_ptr(), deltas.data_ptr(), B, T, H, HV, HEAD_DIM, HEAD_DIM,
+        q.stride(0), q.stride(1), q.stride(2), k.stride(0), k.stride(1), k.stride(2), v.stride(0), v.stride(1),
+        v.stride(2), float(HEAD_DIM ** -0.5 if scale is None else scale), _stream())
+    _lib.check(status, what)
+    return o, deltas
+
+
+def gated_delta_rule_delta_commit(k, g, deltas, state, accepted) -> None:
+    """Advance ``state[b]`` in place by ``clamp(accepted[b], 0, T)`` tokens from the update vectors of
+    ``gated_delta_rule_verify_deltas`` (run on the same state, k and g): bit for bit the state
+    ``gated_delta_rule_advance_inplace`` leaves (the engine's ``delta_commit``,
+    ``inference/engine.py:254-258``), with one streaming pass over the state."""
+    what = "gated_delta_rule_delta_commit"
+    _require_cuda(what, k, g, deltas, state, accepted)
+    if k.dim() != 4 or k.shape[-1] != HEAD_DIM:
+        raise ValueError(f"k: expected [B, T, H, {HEAD_DIM}], got {tuple(k.shape)}")
+    if deltas.dim() != 4 or deltas.dtype != torch.float32 or not deltas.is_contiguous():
+        raise ValueError(f"deltas: expected a contiguous float32 [B, T, HV, {HEAD_DIM}] tensor")
+    B, T, H = k.shape[:3]
+    HV = deltas.shape[2]
+    if deltas.shape != (B, T, HV, HEAD_DIM) or HV % H:
+        raise ValueError(f"deltas: expected {(B, T, HV, HEAD_DIM)} with HV a multiple of {H}, got {tuple(deltas.shape)}")
+    _check_state_inplace(what, state, B, HV)
+    if g.shape != (B, T, HV) or g.dtype != torch.float32:
+        raise ValueError(f"g: expected float32 {(B, T, HV)}, got {g.dtype} {tuple(g.shape)}")
+    if accepted.shape != (B,) or accepted.dtype not in (torch.int32, torch.int64):
+        raise ValueError(f"accepted: expected {B} integers, got {accepted.dtype} {tuple(accepted.shape)}")
+    k = _heads_last_contiguous(k)
+    g = g.contiguous()
+    status = _lib.load().gdn_delta_commit(state.data_ptr(), k.data_ptr(), _DTYPES[k.dtype], g.data_ptr(),
+                                          deltas.data_ptr(), accepted.to(torch.int64).contiguous().data_ptr(), B, T,
+                                          H, HV, HEAD_DIM, HEAD_DIM, k.stride(0), k.stride(1), k.stride(2), _stream())
+    _lib.check(status, what)
+
+
 def gated_delta_rule_rollback(state, snapshots, accepted) -> None:
     """``state[b] <- snapshots[b, accepted[b] - 1]`` for rows with ``accepted[b] >= 1`` (clamped to T)."""
     what = "gated_delta_rule_rollback"

@@ -15,8 +15,8 @@ import torch
 from . import _lib
 from .conv import causal_conv1d, conv_state_commit, conv_step
 from .gated_delta import (HEAD_DIM, _require_cuda, _stream, gated_delta_rule_advance_inplace,
-                          gated_delta_rule_chunk_gated_norm, gated_delta_rule_rollback, gated_delta_rule_step,
-                          gated_delta_rule_verify)
+                          gated_delta_rule_chunk_gated_norm, gated_delta_rule_delta_commit, gated_delta_rule_rollback,
+                          gated_delta_rule_step, gated_delta_rule_verify, gated_delta_rule_verify_deltas)
 from .norm import gated_rms_norm
 
 
@@ -87,7 +87,7 @@ def decode_layer_step(qkv, conv_state, conv_weight, g, beta, state, z, norm_weig
 
 
 def verify_layer_step(qkv, conv_state, conv_weight, g, beta, state, z, norm_weight, key_heads: int, ext_out=None,
-                      eps: float = 1e-6, scale: float | None = None, snapshots=None):
+                      eps: float = 1e-6, scale: float | None = None, snapshots=None, deltas=None):
     """The verify branch of one delta layer for T drafted tokens per row (``inference/engine.py:427-435``
     without the drafter's mask rows): ``conv_step`` over the conv-state window and the T new tokens
     (the window ``ext [B, C, taps + T]`` goes to ``ext_out``), the gated delta rule outputs from
@@ -97,9 +97,12 @@ def verify_layer_step(qkv, conv_state, conv_weight, g, beta, state, z, norm_weig
     ``verify_layer_commit`` once the accepted lengths are known.
 
     With ``snapshots`` (a ``[B, T, HV, 128, 128]`` fp32 buffer) the verify also writes the state after
-    every token, and the commit copies the accepted one instead of advancing the state again."""
+    every token, and the commit copies the accepted one instead of advancing the state again. With
+    ``deltas`` (a ``[B, T, HV, 128]`` fp32 buffer) it keeps each token's update vector, and the commit
+    advances the state by the accepted tokens in one streaming pass, without the advance's reductions
+    (the same bits as the advance). At most one of the two."""
     what = "verify_layer_step"
-    _require_cuda(what, qkv, conv_state, conv_weight, g, beta, state, z, norm_weight, ext_out, snapshots)
+    _require_cuda(what, qkv, conv_state, conv_weight, g, beta, state, z, norm_weight, ext_out, snapshots, deltas)
     if qkv.dim() != 3:
         raise ValueError(f"qkv: expected [B, T, C], got {tuple(qkv.shape)}")
     B, T, C = qkv.shape
@@ -108,25 +111,32 @@ def verify_layer_step(qkv, conv_state, conv_weight, g, beta, state, z, norm_weig
         raise ValueError(f"qkv: {C} channels do not split into 2 x {kd} key channels and whole value heads")
     vd = C - 2 * kd
     _, q, k, v = conv_step(conv_state, qkv, conv_weight, kd, vd, HEAD_DIM, HEAD_DIM, ext_out=ext_out)
-    if snapshots is None:
-        o, _ = gated_delta_rule_step(q, k, v, g, beta, initial_state=state, output_final_state=False, scale=scale)
-    else:
+    if snapshots is not None and deltas is not None:
+        raise ValueError(f"{what}: pass snapshots or deltas, not both")
+    if snapshots is not None:
         o, snapshots = gated_delta_rule_verify(q, k, v, g, beta, state, snapshots=snapshots, scale=scale)
+    elif deltas is not None:
+        o, deltas = gated_delta_rule_verify_deltas(q, k, v, g, beta, state, deltas=deltas, scale=scale)
+    else:
+        o, _ = gated_delta_rule_step(q, k, v, g, beta, initial_state=state, output_final_state=False, scale=scale)
     y = gated_rms_norm(o.view(-1, HEAD_DIM), z.reshape(-1, HEAD_DIM), norm_weight, eps).view(o.shape)
-    return y, (k, v, g, beta, snapshots)
+    return y, (k, v, g, beta, snapshots, deltas)
 
 
 def verify_layer_commit(pending, state, accepted, ext=None, conv_state=None) -> None:
     """Keep the first ``accepted[b]`` verified tokens of row b in ``state`` (the commit of
     ``inference/engine.py:471-472``): advance the state by them again (the reference's design,
-    ``delta_commit``), or copy the snapshot after them when the verify wrote snapshots. With ``ext``
+    ``delta_commit``), copy the snapshot after them when the verify wrote snapshots, or apply the kept
+    update vectors when it kept them. With ``ext``
     and ``conv_state`` the conv state is rolled forward too (``conv_state_commit``; the engine runs
     that once over every layer's stacked conv state, ``:473-474``)."""
-    k, v, g, beta, snapshots = pending
-    if snapshots is None:
-        gated_delta_rule_advance_inplace(k, v, g, beta, state, accepted)
-    else:
+    k, v, g, beta, snapshots, deltas = pending
+    if snapshots is not None:
         gated_delta_rule_rollback(state, snapshots, accepted)
+    elif deltas is not None:
+        gated_delta_rule_delta_commit(k, g, deltas, state, accepted)
+    else:
+        gated_delta_rule_advance_inplace(k, v, g, beta, state, accepted)
     if ext is not None:
         conv_state_commit(ext, conv_state, accepted)
 

@@ -228,3 +228,38 @@ def test_batched_rows_equal_the_same_rows_packed_bitwise(T, snapshots, B):
         assert same_bits(snaps[:, T - 1], S_p)
     else:
         assert same_bits(S, S_p)
+
+
+@pytest.mark.parametrize("B", [6, 64])
+def test_verify_deltas_and_delta_commit_equal_the_step_and_the_advance(B):
+    """The verify that keeps its update vectors gives the plain step's outputs, and the delta commit
+    leaves the advance's state, bit for bit, for every accepted count (clamped to [0, T])."""
+    T, H, HV = 5, 16, 32
+    q, k, v, g, beta, h0 = cuda(*gdn_inputs(400 + B, B, T, H, HV, normalise=False))
+    o_ref, _ = gdn.gated_delta_rule_step(q, k, v, g, beta, initial_state=h0, output_final_state=False)
+    o, deltas = gdn.gated_delta_rule_verify_deltas(q, k, v, g, beta, h0)
+    assert same_bits(o, o_ref) and deltas.shape == (B, T, HV, 128)
+    accepted = torch.tensor([(-1, 0, 1, 2, 3, 4, 5, 9)[i % 8] for i in range(B)], device="cuda")
+    adv, com = h0.clone(), h0.clone()
+    gdn.gated_delta_rule_advance_inplace(k, v, g, beta, adv, accepted)
+    gdn.gated_delta_rule_delta_commit(k, g, deltas, com, accepted)
+    assert same_bits(com, adv)
+    # the first token's update vector against the float64 formula beta (v - e^g S^T k)
+    kn = k[:, 0].double() / k[:, 0].double().norm(dim=-1, keepdim=True)
+    kn = kn.repeat_interleave(HV // H, dim=1)
+    pred = torch.einsum("bhk,bhkv->bhv", kn, h0.double()) * torch.exp(g[:, 0].double())[..., None]
+    d0 = beta[:, 0].double()[..., None] * (v[:, 0].double() - pred)
+    assert maxabs(deltas[:, 0], d0) < 1e-4
+
+
+def test_delta_commit_checks_its_arguments():
+    B, T, H, HV = 2, 3, 2, 4
+    q, k, v, g, beta, h0 = cuda(*gdn_inputs(450, B, T, H, HV, normalise=False))
+    _, deltas = gdn.gated_delta_rule_verify_deltas(q, k, v, g, beta, h0)
+    acc = torch.tensor([1, 2], device="cuda")
+    with pytest.raises(ValueError):
+        gdn.gated_delta_rule_delta_commit(k, g, deltas[:, :2], h0.clone(), acc)
+    with pytest.raises(ValueError):
+        gdn.gated_delta_rule_delta_commit(k, g, deltas, h0[:1].clone(), acc)
+    with pytest.raises(ValueError):
+        gdn.gated_delta_rule_delta_commit(k, g, deltas, h0.clone(), acc.float())

@@ -29,7 +29,7 @@ def verify_inputs(seed, B, T, H, HV, taps):
 
 
 @pytest.mark.parametrize("B,T,H,HV,taps", [(4, 5, 16, 32, 3), (3, 5, 2, 4, 4), (2, 2, 2, 4, 3)])
-@pytest.mark.parametrize("design", ["recompute", "snapshots"])
+@pytest.mark.parametrize("design", ["recompute", "snapshots", "deltas"])
 def test_verify_layer_matches_oracle_composition(B, T, H, HV, taps, design):
     qkv, cs, w, g, beta, state, z, nw, accepted = verify_inputs(B * 100 + T * 10 + taps, B, T, H, HV, taps)
     C = qkv.shape[-1]
@@ -46,8 +46,9 @@ def test_verify_layer_matches_oracle_composition(B, T, H, HV, taps, design):
              nw=nw.cuda())
     ext = torch.empty(B, C, taps + T, dtype=torch.bfloat16, device="cuda")
     snaps = torch.empty(B, T, HV, 128, 128, device="cuda") if design == "snapshots" else None
+    deltas = torch.empty(B, T, HV, 128, device="cuda") if design == "deltas" else None
     y, pending = gdn.verify_layer_step(d["qkv"], d["cs"], d["w"], d["g"], d["beta"], d["state"], d["z"], d["nw"], H,
-                                       ext_out=ext, snapshots=snaps)
+                                       ext_out=ext, snapshots=snaps, deltas=deltas)
     assert same_bits(ext, ext_ref)
     assert same_bits(d["state"], state)  # the verify reads the state only
     assert maxabs(y, y_ref) < 2e-2
@@ -60,18 +61,23 @@ def test_verify_layer_matches_oracle_composition(B, T, H, HV, taps, design):
 
 
 def test_commit_designs_agree_bit_for_bit():
-    """The snapshot rollback and the recompute advance leave the same state bit for bit."""
+    """The snapshot rollback, the recompute advance and the delta commit leave the same state bit
+    for bit, and the three verifies give the same outputs."""
     B, T, H, HV, taps = 6, 5, 2, 4, 3
     qkv, cs, w, g, beta, state, z, nw, _ = verify_inputs(7, B, T, H, HV, taps)
     accepted = torch.tensor([1, 2, 3, 4, 5, 0]).cuda()
-    results = []
-    for snaps in (None, torch.empty(B, T, HV, 128, 128, device="cuda")):
+    results, ys = [], []
+    designs = ({}, {"snapshots": torch.empty(B, T, HV, 128, 128, device="cuda")},
+               {"deltas": torch.empty(B, T, HV, 128, device="cuda")})
+    for extra in designs:
         st = state.cuda()
-        _, pending = gdn.verify_layer_step(qkv.cuda(), cs.cuda(), w.cuda(), g.cuda(), beta.cuda(), st, z.cuda(),
-                                           nw.cuda(), H, snapshots=snaps)
+        y, pending = gdn.verify_layer_step(qkv.cuda(), cs.cuda(), w.cuda(), g.cuda(), beta.cuda(), st, z.cuda(),
+                                           nw.cuda(), H, **extra)
         gdn.verify_layer_commit(pending, st, accepted)
         results.append(st)
-    assert same_bits(results[0], results[1])
+        ys.append(y)
+    assert same_bits(results[0], results[1]) and same_bits(results[0], results[2])
+    assert same_bits(ys[0], ys[1]) and same_bits(ys[0], ys[2])
 
 
 def test_conv_state_commit_over_stacked_layers_matches_gather():
