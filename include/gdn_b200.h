@@ -137,9 +137,13 @@ GDN_API int gdn_recurrent_gates(const void* q, const void* k, const void* v, int
  * The verify outputs of gdn_recurrent (the state is read, not written: o as with state_out =
  * snapshots = NULL) that also keep each token's update vector
  *   deltas[b, t, hv, :] = beta_t (v_t - e^{g_t} S_{t-1}^T k_t)    ([B, T, HV, Dv] fp32)
- * for gdn_delta_commit. Replaces delta_outputs, inference/engine.py:250-252 (gated_delta_rule_step
- * of the drafted tokens, model/model.py:297-302); o equals gdn_recurrent's bit for bit. Dense
- * batches only (no cu_seqlens).
+ * for gdn_delta_commit. Replaces delta_outputs, inference/engine.py:249-252 (gated_delta_rule_step
+ * of the drafted tokens, model/model.py:297-302). Dense batches only (no cu_seqlens). With bf16
+ * rows, an initial state and T <= 8 the block runs on the tensor cores: one product of each state
+ * with the 2T raw k and q rows (the state as two bf16 parts, within 2^-18 of fp32 element by
+ * element) and the token recurrence unrolled over the block's Gram products; o and deltas then
+ * agree with gdn_recurrent to fp32 rounding, not bit for bit. Otherwise the recurrent kernel
+ * runs and o equals gdn_recurrent's bit for bit.
  */
 GDN_API int gdn_recurrent_deltas(const void* q, const void* k, const void* v, int qkv_dtype,
                                  const float* g, const void* beta, int beta_dtype,
@@ -155,10 +159,11 @@ GDN_API int gdn_recurrent_deltas(const void* q, const void* k, const void* v, in
  * The commit after gdn_recurrent_deltas: state[b] ([B, HV, Dk, Dv] fp32, in place) advances by
  * clamp(accepted[b], 0, T) tokens with S <- e^{g_t} S + k_t delta_t^T (k_t L2-normalised in the
  * kernel). Replaces delta_commit, inference/engine.py:254-258 (gated_delta_rule_advance_inplace,
- * model/model.py:305-311, model/fla_inplace.py:63-74): the same arithmetic as the advance without
- * its reductions, so the state equals gdn_recurrent with steps = accepted bit for bit. k: [B, T, H,
- * Dk] bf16 or fp32 with element strides; g: [B, T, HV] fp32; deltas as gdn_recurrent_deltas wrote
- * them from the same state, k, g.
+ * model/model.py:305-311, model/fla_inplace.py:63-74): the advance's own update arithmetic without
+ * its reductions, so with deltas from the recurrent kernel the state equals gdn_recurrent with
+ * steps = accepted bit for bit (and to fp32 rounding with deltas from the tensor-core block). k:
+ * [B, T, H, Dk] bf16 or fp32 with element strides; g: [B, T, HV] fp32; deltas as
+ * gdn_recurrent_deltas wrote them from the same state, k, g.
  */
 GDN_API int gdn_delta_commit(float* state, const void* k, int k_dtype, const float* g, const float* deltas,
                              const int64_t* accepted, int64_t batch, int64_t seqlen, int64_t key_heads,

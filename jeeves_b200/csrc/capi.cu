@@ -127,6 +127,19 @@ static int recurrent(const void* q, const void* k, const void* v, int qkv_dtype,
     a.scale = scale;
     a.gates = G;
     a.deltas = deltas;
+    if (deltas && qkv_dtype == GDN_BF16 && seqlen <= 8 && !cu_seqlens && state_in && !gates && !state_out &&
+        !snapshots && !steps) {
+        // a verify block of up to 8 tokens: one tensor-core pass over each state
+        VerifyBlockArgs vb{};
+        vb.q = q; vb.k = k; vb.v = v; vb.g = g; vb.beta = beta; vb.beta_dtype = beta_dtype;
+        vb.state_in = state_in; vb.o = o; vb.deltas = deltas;
+        vb.rows = batch; vb.T = seqlen; vb.H = (int)key_heads; vb.HV = (int)value_heads;
+        vb.qsb = q_stride_b; vb.qst = q_stride_t; vb.qsh = q_stride_h;
+        vb.ksb = k_stride_b; vb.kst = k_stride_t; vb.ksh = k_stride_h;
+        vb.vsb = v_stride_b; vb.vst = v_stride_t; vb.vsh = v_stride_h;
+        vb.scale = scale;
+        return launch_verify_block(vb, as_stream(stream));
+    }
     return launch_recurrent(a, as_stream(stream));
 }
 

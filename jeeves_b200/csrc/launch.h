@@ -57,6 +57,25 @@ struct DeltaCommitArgs {
 };
 int launch_delta_commit(const DeltaCommitArgs& a, cudaStream_t s);
 
+// The verify that keeps its update vectors, for T <= 8 tokens of bf16 rows (verify_block.cu):
+// outputs o and deltas ([rows, T, HV, 128]) from state_in ([rows, HV, 128, 128] fp32).
+struct VerifyBlockArgs {
+    const void* q;
+    const void* k;
+    const void* v;
+    const float* g;
+    const void* beta;
+    int beta_dtype;
+    const float* state_in;
+    void* o;
+    float* deltas;
+    int64_t rows, T;
+    int H, HV;
+    int64_t qsb, qst, qsh, ksb, kst, ksh, vsb, vst, vsh;
+    float scale;
+};
+int launch_verify_block(const VerifyBlockArgs& a, cudaStream_t s);
+
 struct ChunkArgs {
     const void* q;
     const void* k;

@@ -2,6 +2,7 @@
 // live in one module, so no relocatable device code or device link step is needed.
 #include "capi.cu"
 #include "recurrent.cu"
+#include "verify_block.cu"
 #include "conv.cu"
 #include "norm.cu"
 #include "chunk.cu"

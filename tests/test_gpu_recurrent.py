@@ -230,12 +230,57 @@ def test_batched_rows_equal_the_same_rows_packed_bitwise(T, snapshots, B):
         assert same_bits(S, S_p)
 
 
+def _f64_verify(q, k, v, g, beta, h0, scale=128 ** -0.5):
+    """Outputs, update vectors and per-token states of the token recurrence in float64 (the
+    oracle's recurrence, model/model.py:221-239, with the update vector kept)."""
+    q, k, v, g, beta, S = (x.detach().double().cpu() for x in (q, k, v, g, beta, h0))
+    B, T, H, _ = q.shape
+    HV = v.shape[2]
+    q = q.repeat_interleave(HV // H, dim=2)
+    k = k.repeat_interleave(HV // H, dim=2)
+    q = q / torch.sqrt((q * q).sum(-1, keepdim=True) + 1e-6) * scale
+    k = k / torch.sqrt((k * k).sum(-1, keepdim=True) + 1e-6)
+    o, d, states = [], [], []
+    for t in range(T):
+        S = S * torch.exp(g[:, t])[..., None, None]
+        dt = beta[:, t, :, None] * (v[:, t] - torch.einsum("bhk,bhkv->bhv", k[:, t], S))
+        S = S + torch.einsum("bhk,bhv->bhkv", k[:, t], dt)
+        o.append(torch.einsum("bhk,bhkv->bhv", q[:, t], S))
+        d.append(dt)
+        states.append(S)
+    return torch.stack(o, 1), torch.stack(d, 1), torch.stack(states, 1)
+
+
+@pytest.mark.parametrize("T", [1, 2, 3, 5, 8])
+@pytest.mark.parametrize("B,H,HV", [(6, 16, 32), (3, 2, 4), (37, 4, 4)])
+def test_verify_deltas_block_against_float64(T, B, H, HV):
+    """bf16 rows and T <= 8: the tensor-core block (the state as two bf16 parts, the recurrence
+    unrolled over the Gram products). Outputs within the bf16 bound, update vectors and the
+    committed state within the fp32 state bound of the float64 recurrence."""
+    q, k, v, g, beta, h0 = gdn_inputs(500 + 10 * T + B, B, T, H, HV, normalise=False)
+    o_ref, d_ref, st_ref = _f64_verify(q, k, v, g, beta, h0)
+    qc, kc, vc, gc, bc, hc = cuda(q, k, v, g, beta, h0)
+    o, deltas = gdn.gated_delta_rule_verify_deltas(qc, kc, vc, gc, bc, hc)
+    assert same_bits(hc, h0.cuda())  # read, not written
+    assert maxabs(o, o_ref) < O_TOL
+    assert rel(deltas, d_ref) < S_TOL
+    accepted = torch.arange(B) % (T + 2) - 1  # -1 .. T + 1: clamped to 0 .. T
+    state = hc.clone()
+    gdn.gated_delta_rule_delta_commit(kc, gc, deltas, state, accepted.cuda())
+    j = accepted.clamp(0, T)
+    want = torch.stack([h0[b].double() if j[b] == 0 else st_ref[b, j[b] - 1] for b in range(B)])
+    assert rel(state, want) < S_TOL
+    keep = (j == 0).cuda()
+    assert same_bits(state[keep], hc[keep])
+
+
 @pytest.mark.parametrize("B", [6, 64])
-def test_verify_deltas_and_delta_commit_equal_the_step_and_the_advance(B):
-    """The verify that keeps its update vectors gives the plain step's outputs, and the delta commit
-    leaves the advance's state, bit for bit, for every accepted count (clamped to [0, T])."""
+def test_verify_deltas_fallback_and_delta_commit_equal_the_step_and_the_advance(B):
+    """fp32 rows (or T > 8, or no initial state) run the recurrent kernel: its outputs are the
+    plain step's, and the delta commit leaves the advance's state, bit for bit, for every
+    accepted count (clamped to [0, T])."""
     T, H, HV = 5, 16, 32
-    q, k, v, g, beta, h0 = cuda(*gdn_inputs(400 + B, B, T, H, HV, normalise=False))
+    q, k, v, g, beta, h0 = cuda(*gdn_inputs(400 + B, B, T, H, HV, dtype=torch.float32, normalise=False))
     o_ref, _ = gdn.gated_delta_rule_step(q, k, v, g, beta, initial_state=h0, output_final_state=False)
     o, deltas = gdn.gated_delta_rule_verify_deltas(q, k, v, g, beta, h0)
     assert same_bits(o, o_ref) and deltas.shape == (B, T, HV, 128)
@@ -244,12 +289,22 @@ def test_verify_deltas_and_delta_commit_equal_the_step_and_the_advance(B):
     gdn.gated_delta_rule_advance_inplace(k, v, g, beta, adv, accepted)
     gdn.gated_delta_rule_delta_commit(k, g, deltas, com, accepted)
     assert same_bits(com, adv)
-    # the first token's update vector against the float64 formula beta (v - e^g S^T k)
-    kn = k[:, 0].double() / k[:, 0].double().norm(dim=-1, keepdim=True)
-    kn = kn.repeat_interleave(HV // H, dim=1)
-    pred = torch.einsum("bhk,bhkv->bhv", kn, h0.double()) * torch.exp(g[:, 0].double())[..., None]
-    d0 = beta[:, 0].double()[..., None] * (v[:, 0].double() - pred)
-    assert maxabs(deltas[:, 0], d0) < 1e-4
+
+
+@pytest.mark.parametrize("B", [6, 64])
+def test_verify_deltas_block_equals_the_step_to_rounding(B):
+    """The block's outputs and the delta commit's state against the recurrent kernel's step and
+    advance on the same bf16 inputs."""
+    T, H, HV = 5, 16, 32
+    q, k, v, g, beta, h0 = cuda(*gdn_inputs(410 + B, B, T, H, HV, normalise=False))
+    o_ref, _ = gdn.gated_delta_rule_step(q, k, v, g, beta, initial_state=h0, output_final_state=False)
+    o, deltas = gdn.gated_delta_rule_verify_deltas(q, k, v, g, beta, h0)
+    assert maxabs(o, o_ref) < 1e-2
+    accepted = torch.tensor([(0, 1, 2, 3, 4, 5)[i % 6] for i in range(B)], device="cuda")
+    adv, com = h0.clone(), h0.clone()
+    gdn.gated_delta_rule_advance_inplace(k, v, g, beta, adv, accepted)
+    gdn.gated_delta_rule_delta_commit(k, g, deltas, com, accepted)
+    assert rel(com, adv) < 2e-6
 
 
 def test_delta_commit_checks_its_arguments():

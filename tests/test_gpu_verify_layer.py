@@ -60,9 +60,10 @@ def test_verify_layer_matches_oracle_composition(B, T, H, HV, taps, design):
     assert same_bits(d["cs"], cs_ref)
 
 
-def test_commit_designs_agree_bit_for_bit():
-    """The snapshot rollback, the recompute advance and the delta commit leave the same state bit
-    for bit, and the three verifies give the same outputs."""
+def test_commit_designs_agree():
+    """The snapshot rollback and the recompute advance leave the same state bit for bit and their
+    verifies give the same outputs; the kept-update-vector design (the tensor-core block for these
+    bf16 rows) agrees with them to fp32 rounding."""
     B, T, H, HV, taps = 6, 5, 2, 4, 3
     qkv, cs, w, g, beta, state, z, nw, _ = verify_inputs(7, B, T, H, HV, taps)
     accepted = torch.tensor([1, 2, 3, 4, 5, 0]).cuda()
@@ -76,8 +77,8 @@ def test_commit_designs_agree_bit_for_bit():
         gdn.verify_layer_commit(pending, st, accepted)
         results.append(st)
         ys.append(y)
-    assert same_bits(results[0], results[1]) and same_bits(results[0], results[2])
-    assert same_bits(ys[0], ys[1]) and same_bits(ys[0], ys[2])
+    assert same_bits(results[0], results[1]) and same_bits(ys[0], ys[1])
+    assert rel(results[2], results[0]) < 2e-6 and maxabs(ys[2], ys[0]) < 2e-2
 
 
 def test_conv_state_commit_over_stacked_layers_matches_gather():
