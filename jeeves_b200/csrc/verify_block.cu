@@ -18,12 +18,12 @@
 // One persistent CTA per SM walks the (row, value head) pairs. Its threads load each pair's 64 KB
 // state into registers one pair ahead (every load of a warp one whole state row) and split it into
 // the two bf16 operands of A = S^T in shared memory (MN-major, 128-byte swizzle: the state rows
-// are A's K). Three threads then issue the products: hi and lo into two accumulators, and the Gram
-// products of the k / q rows into a third, from which warp 0 forms the pair's coefficients while
-// the state product runs. Warps 0-3 drain R, one state column each (TMEM lane = column), while
-// warps 4-7 put the next pair's rows, v and gates in place (also loaded one pair ahead). Every wait
-// is bounded; a wait that gives up raises the device error word, the CTA stops taking pairs, waits
-// for the products it started and frees its TMEM.
+// are A's K). One thread then issues the products: first the Gram products of the k / q rows,
+// committed on their own so that warp 0 forms the pair's coefficients while the tensor cores go
+// on with hi and lo into two accumulators. Warps 0-3 drain R, one state column each (TMEM lane =
+// column), while warps 4-7 put the next pair's rows, v and gates in place (also loaded one pair
+// ahead). Every wait is bounded; a wait that gives up raises the device error word, the CTA stops
+// taking pairs, waits for the products it started and frees its TMEM.
 
 #include "common.cuh"
 #include "launch.h"
@@ -35,9 +35,7 @@ namespace vblock {
 using namespace sm100;
 
 constexpr int kThreads = 256;
-constexpr int kGramIssuer = 160;   // lane 0 of warp 5 issues the Gram product of the rows
-constexpr int kHiIssuer = 192;     // lane 0 of warp 6 issues the hi products
-constexpr int kIssuer = 224;       // lane 0 of warp 7 issues the lo products
+constexpr int kIssuer = 224;       // lane 0 of warp 7 issues the products: the Gram first, then hi and lo
 constexpr int kMaxT = 8;
 constexpr uint32_t kPanel = 128 * 128;              // 128 rows x 128 bytes (64 bf16 columns or K elements)
 constexpr uint32_t kVA = 4 * kPanel;                // after hi (2 panels) and lo (2 panels): the MN-major operands
@@ -146,7 +144,7 @@ __global__ void __launch_bounds__(kThreads, 1) verify_block_kernel(const __grid_
 
     if (tid == 0) {
         sh.abort = 0;
-        mbar_init(&sh.acc, 2);  // the hi and the lo issuer each commit once a pair
+        mbar_init(&sh.acc, 1);
         mbar_init(&sh.acc_gram, 1);
         fence_mbar_init();
     }
@@ -180,7 +178,7 @@ __global__ void __launch_bounds__(kThreads, 1) verify_block_kernel(const __grid_
     __syncthreads();
     const uint32_t tb = sh.tmem_base;
     const uint32_t idesc = make_idesc(128, 16, kFmtBF16, true, false);
-    int computing = -1;  // each issuer: the parity of its product in flight, or -1
+    int computing = -1;  // the issuer: the parity of the products in flight, or -1
 
     for (int j = 0; j < npairs; ++j) {
         const int pair = pair_of(j);
@@ -210,29 +208,28 @@ __global__ void __launch_bounds__(kThreads, 1) verify_block_kernel(const __grid_
         if (j + 1 < npairs) load_state(j + 1);  // lands while this pair is multiplied and drained
         fence_async_smem();
         __syncthreads();
-        if (tid == kHiIssuer || tid == kIssuer || tid == kGramIssuer) {
-            // ---- R_hi = hi^T [k | q], R_lo = lo^T [k | q] (8 steps of K = 16 state rows each) and the
-            // Gram product G = [k | q]^T [k | q] of the rows (8 steps of K = 16 elements, all 128 rows
-            // of the zero-padded operand as A)
+        if (tid == kIssuer) {
+            // ---- the Gram product G = [k | q]^T [k | q] of the rows (M = 64: rows 0-63 of the
+            // zero-padded operand, row r of G in TMEM lane r for r < 16), committed on its own so
+            // that warp 0 forms the coefficients while the tensor cores go on with
+            // R = hi^T [k | q] + lo^T [k | q] (8 steps of K = 16 state rows for each part)
             tc_fence_after();
-            if (tid == kGramIssuer) {
-                const uint32_t gdesc = make_idesc(128, 16, kFmtBF16, false, false);
+            const uint32_t gdesc = make_idesc(64, 16, kFmtBF16, false, false);
 #pragma unroll
-                for (int ks = 0; ks < 8; ++ks) {
-                    const uint64_t rows = sdesc_kmajor(vb + (ks >> 2) * kPanel, (ks & 3) * 32);
-                    mma_f16(tb + 32, rows, rows, gdesc, ks > 0);
-                }
-                mma_commit(&sh.acc_gram);
-            } else {
-                const bool lo = tid == kIssuer;
-                const uint64_t a = sdesc_mnmajor(sm + (lo ? 2 * kPanel : 0), kPanel);
-                const uint32_t d = tb + (lo ? 16 : 0);
+            for (int ks = 0; ks < 8; ++ks) {
+                const uint64_t rows = sdesc_kmajor(vb + (ks >> 2) * kPanel, (ks & 3) * 32);
+                mma_f16(tb + 32, rows, rows, gdesc, ks > 0);
+            }
+            mma_commit(&sh.acc_gram);
+#pragma unroll
+            for (int part = 0; part < 2; ++part) {
+                const uint64_t a = sdesc_mnmajor(sm + part * 2 * kPanel, kPanel);
 #pragma unroll
                 for (int ks = 0; ks < 8; ++ks)
-                    mma_f16(d, sdesc_add(a, ks * 2048), sdesc_kmajor(vb + (ks >> 2) * kPanel, (ks & 3) * 32), idesc,
-                            ks > 0);
-                mma_commit(&sh.acc);
+                    mma_f16(tb + 16 * part, sdesc_add(a, ks * 2048),
+                            sdesc_kmajor(vb + (ks >> 2) * kPanel, (ks & 3) * 32), idesc, ks > 0);
             }
+            mma_commit(&sh.acc);
             computing = j & 1;
         } else if (warp == 0) {
             // ---- meanwhile: the Gram rows (TMEM lanes 0 .. 2T-1), then the pair's coefficients
@@ -326,9 +323,9 @@ __global__ void __launch_bounds__(kThreads, 1) verify_block_kernel(const __grid_
         __syncthreads();
     }
     // products still in flight (after a wait gave up) end before the CTA leaves
-    if (computing >= 0) {
-        if (tid == kIssuer) mbar_wait(&sh.acc, (uint32_t)computing, kSiteProduct);
-        if (tid == kGramIssuer) mbar_wait(&sh.acc_gram, (uint32_t)computing, kSiteGram);
+    if (tid == kIssuer && computing >= 0) {
+        mbar_wait(&sh.acc_gram, (uint32_t)computing, kSiteGram);
+        mbar_wait(&sh.acc, (uint32_t)computing, kSiteProduct);
     }
     tc_fence_before();
     __syncthreads();
