@@ -643,9 +643,10 @@ def bench_verify(gdn, args, device, rank, world, rank_sync, reduce_max, hbm_peak
     tokens (recurrent state of every layer, and the conv states from the ext windows in one launch,
     inference/engine.py:471-474), the whole step replayed as one CUDA graph. Three designs: the
     reference's recompute (the commit advances each state by the accepted tokens again), kept
-    update vectors (the verify keeps each token's delta and the commit applies the accepted ones in
-    one streaming pass: the recompute's bits without its reductions) and per-token snapshots (the
-    commit copies the accepted snapshot). The headline is the faster of the first two."""
+    update vectors (the verify runs as one tensor-core block per (row, head) state and keeps each
+    token's delta; the commit applies the accepted ones in one streaming pass; states agree with
+    the recompute to fp32 rounding) and per-token snapshots (the commit copies the accepted
+    snapshot). The headline is the faster of the first two."""
     B, _ = shard(B_total, rank, world)
     gen = torch.Generator().manual_seed(4)
     states = [torch.zeros(B, HV, D, D, device=device).normal_(0, 0.02) for _ in range(layers)]
@@ -682,8 +683,9 @@ def bench_verify(gdn, args, device, rank, world, rank_sync, reduce_max, hbm_peak
                        "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm_peak, "unit": "GB/s",
                                     "frac": round(ach / hbm_peak, 4), "algorithmic_bytes_per_unit": unit}}
     names = {"recompute": "recompute (the reference's: the commit advances the state by the accepted tokens)",
-             "deltas": "kept update vectors (the verify keeps each token's delta; the commit applies the accepted "
-                       "ones in one streaming pass, the same bits as the recompute advance)"}
+             "deltas": "kept update vectors (the verify as one tensor-core block per state: one product of the "
+                       "state with the 10 k/q rows and their Gram, the 5-token recurrence unrolled per column, each "
+                       "token's delta kept; the commit applies the accepted ones in one streaming pass)"}
     head = min(("recompute", "deltas"), key=lambda d: out[d]["ms_per_step"])
     other = "deltas" if head == "recompute" else "recompute"
     best = out[head]

@@ -272,9 +272,13 @@ def gated_delta_rule_verify_deltas(q, k, v, g, beta, state, deltas=None, scale=N
     """Score T drafted tokens from ``state`` (read, not written) and keep each token's update vector;
     returns ``(o, deltas)`` with ``deltas [B, T, HV, 128]`` fp32 = beta_t (v_t - e^{g_t} S_{t-1}^T k_t).
 
-    ``o`` is ``gated_delta_rule_step(..., output_final_state=False)[0]`` bit for bit (the engine's
-    ``delta_outputs``, ``inference/engine.py:249-252``); ``gated_delta_rule_delta_commit`` then makes the
-    accepted tokens' state live without re-running their reductions."""
+    Replaces the engine's ``delta_outputs`` (``inference/engine.py:249-252``). With bf16 rows and
+    T <= 8 the block runs on the tensor cores: one product of the state (as two bf16 parts, within
+    2^-18 of fp32) with the 2T raw k and q rows, the rows' Gram products, and the token recurrence
+    unrolled per column; ``o`` and ``deltas`` agree with the recurrent kernel to fp32 rounding.
+    Otherwise the recurrent kernel runs and ``o`` is ``gated_delta_rule_step(...)[0]`` bit for bit.
+    ``gated_delta_rule_delta_commit`` then makes the accepted tokens' state live without re-running
+    their reductions."""
     what = "gated_delta_rule_verify_deltas"
     _require_cuda(what, q, k, v, g, beta, state, deltas)
     B, T, H, HV = _check_qkv(what, q, k, v)
@@ -299,9 +303,11 @@ def gated_delta_rule_verify_deltas(q, k, v, g, beta, state, deltas=None, scale=N
 
 def gated_delta_rule_delta_commit(k, g, deltas, state, accepted) -> None:
     """Advance ``state[b]`` in place by ``clamp(accepted[b], 0, T)`` tokens from the update vectors of
-    ``gated_delta_rule_verify_deltas`` (run on the same state, k and g): bit for bit the state
-    ``gated_delta_rule_advance_inplace`` leaves (the engine's ``delta_commit``,
-    ``inference/engine.py:254-258``), with one streaming pass over the state."""
+    ``gated_delta_rule_verify_deltas`` (run on the same state, k and g), with one streaming pass over
+    the state: the advance's own update arithmetic without its reductions (the engine's
+    ``delta_commit``, ``inference/engine.py:254-258``). With update vectors from the recurrent kernel
+    the state is ``gated_delta_rule_advance_inplace``'s bit for bit; from the tensor-core block, to
+    fp32 rounding."""
     what = "gated_delta_rule_delta_commit"
     _require_cuda(what, k, g, deltas, state, accepted)
     if k.dim() != 4 or k.shape[-1] != HEAD_DIM:

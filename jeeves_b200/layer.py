@@ -98,9 +98,10 @@ def verify_layer_step(qkv, conv_state, conv_weight, g, beta, state, z, norm_weig
 
     With ``snapshots`` (a ``[B, T, HV, 128, 128]`` fp32 buffer) the verify also writes the state after
     every token, and the commit copies the accepted one instead of advancing the state again. With
-    ``deltas`` (a ``[B, T, HV, 128]`` fp32 buffer) it keeps each token's update vector, and the commit
-    advances the state by the accepted tokens in one streaming pass, without the advance's reductions
-    (the same bits as the advance). At most one of the two."""
+    ``deltas`` (a ``[B, T, HV, 128]`` fp32 buffer) the verify runs as one tensor-core block per state
+    (for bf16 rows and T <= 8) and keeps each token's update vector, and the commit advances the state
+    by the accepted tokens in one streaming pass, without the advance's reductions (states agree with
+    the advance to fp32 rounding). At most one of the two."""
     what = "verify_layer_step"
     _require_cuda(what, qkv, conv_state, conv_weight, g, beta, state, z, norm_weight, ext_out, snapshots, deltas)
     if qkv.dim() != 3:
