@@ -1,7 +1,7 @@
 """Benchmark of the gated-delta hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--no-extras] [--no-cpu-baseline]
-    python bench.py --profile prefill|varlen|decode|verify|attention|in_proj   (one untimed run of a case, for ncu)
+    python bench.py --profile prefill|varlen|decode|verify|verify_layer|attention|in_proj   (one untimed run of a case, for ncu)
 
 Workloads (synthetic inputs with the benchmark configs' shapes and distributions; no
 dataset or checkpoint is involved):
@@ -964,8 +964,10 @@ def profile_case(name, device):
         x, w, cw = in_proj_case(device)
         for _ in range(2):
             gdn.in_proj_conv(x, w, cw, C_QKV)
-    elif name == "verify":  # the config-4 step of bench_verify (kept update vectors), 24 layers
-        B, T, layers, taps = 128, 5, 24, 3
+    elif name in ("verify", "verify_layer"):  # the config-4 step of bench_verify (kept update vectors):
+        # 24 layers, or one layer (B = 128 rows; 268 MB of state) for captures that replay kernels
+        B, T, taps = 128, 5, 3
+        layers = 24 if name == "verify" else 1
         states = [torch.randn(B, HV, D, D, device=device) * 0.02 for _ in range(layers)]
         conv_states = torch.randn(layers, B, C_QKV, taps, device=device).to(torch.bfloat16)
         ext = torch.empty(layers, B, C_QKV, taps + T, dtype=torch.bfloat16, device=device)
@@ -997,7 +999,7 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-extras", dest="extras", action="store_false")
     ap.add_argument("--no-cpu-baseline", dest="cpu", action="store_false")
-    ap.add_argument("--profile", choices=("prefill", "varlen", "decode", "verify", "attention", "in_proj"),
+    ap.add_argument("--profile", choices=("prefill", "varlen", "decode", "verify", "verify_layer", "attention", "in_proj"),
                     help="run one workload twice, untimed, for an ncu capture")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)

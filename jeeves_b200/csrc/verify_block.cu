@@ -15,7 +15,7 @@
 // S = hi + lo + r with hi = bf16(S), lo = bf16(S - hi), |r| <= 2^-18 |S| element by element,
 // against the bf16 k and q rows (exact), accumulated in fp32.
 //
-// One persistent CTA per SM walks the (row, value head) pairs. Its threads load each pair's 64 KB
+// Two persistent CTAs per SM walk the (row, value head) pairs. Their threads load each pair's 64 KB
 // state into registers one pair ahead (every load of a warp one whole state row) and split it into
 // the two bf16 operands of A = S^T in shared memory (MN-major, 128-byte swizzle: the state rows
 // are A's K). One thread then issues the products: first the Gram products of the k / q rows,
@@ -131,7 +131,7 @@ __device__ __forceinline__ void deposit(const Prefetch& f, uint8_t* vb, Aux& aux
 }
 
 template <int T>
-__global__ void __launch_bounds__(kThreads, 1) verify_block_kernel(const __grid_constant__ Params p) {
+__global__ void __launch_bounds__(kThreads, 2) verify_block_kernel(const __grid_constant__ Params p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     __shared__ Shared sh;
@@ -373,7 +373,8 @@ int launch_verify_block(const VerifyBlockArgs& a, cudaStream_t s) {
     p.rep = a.HV / a.H;
     p.pairs = (int)pairs;
     p.scale = a.scale;
-    const int grid = (int)(pairs < sms[dev] ? pairs : sms[dev]);
+    const int64_t slots = 2 * (int64_t)sms[dev];  // two CTAs an SM: one's serial phases overlap the other's
+    const int grid = (int)(pairs < slots ? pairs : slots);
     switch (a.T) {
 #define GDN_VB_CASE(TT) \
         case TT: verify_block_kernel<TT><<<grid, kThreads, kSmem, s>>>(p); break;
