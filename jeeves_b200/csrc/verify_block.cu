@@ -233,7 +233,8 @@ __global__ void __launch_bounds__(kThreads, 2) verify_block_kernel(const __grid_
             computing = j & 1;
         } else if (warp == 0) {
             // ---- meanwhile: the Gram rows (TMEM lanes 0 .. 2T-1), then the pair's coefficients
-            const bool gok = __all_sync(0xffffffffu, mbar_wait_or_abort(&sh.acc_gram, j & 1, kSiteGram, &sh.abort, false));
+            // lane 0 polls, backing off, so that the wait takes no shared-memory bandwidth from the products
+            const bool gok = __shfl_sync(0xffffffffu, lane != 0 || mbar_wait_or_abort(&sh.acc_gram, j & 1, kSiteGram, &sh.abort), 0);
             if (!gok && lane == 0) atomicExch(&sh.abort, 1);
             if (gok) {
                 tc_fence_after();
@@ -284,7 +285,7 @@ __global__ void __launch_bounds__(kThreads, 2) verify_block_kernel(const __grid_
         // (warp 0 has waited for the Gram product; a failed wait there raised the abort flag)
         const bool done = tid != 0 ||
                           (!*reinterpret_cast<volatile int*>(&sh.abort) &&
-                           mbar_wait_or_abort(&sh.acc, j & 1, kSiteProduct, &sh.abort, false));
+                           mbar_wait_or_abort(&sh.acc, j & 1, kSiteProduct, &sh.abort));
         if (!__syncthreads_and(done)) {
             atomicExch(&sh.abort, 1);
             break;
