@@ -322,16 +322,21 @@ __global__ void conv_step_vec_kernel(const bf16* __restrict__ state, const bf16*
     uint4* edst = reinterpret_cast<uint4*>(ext + (b * C + c8) * L);
 #pragma unroll
     for (int i = 0; i < L; ++i) edst[i] = reinterpret_cast<const uint4*>(e)[i];
-    float wt[8][K];
+    // channel pairs (2p, 2p + 1) in packed lanes: the window's values and the taps' weights
+    f32x2 w2[4][K], x2[L][4];
     {
         bf16 wr[8 * K];
         const uint4* wsrc = reinterpret_cast<const uint4*>(w + c8 * K);
 #pragma unroll
         for (int i = 0; i < K; ++i) reinterpret_cast<uint4*>(wr)[i] = __ldg(wsrc + i);
 #pragma unroll
-        for (int c = 0; c < 8; ++c)
+        for (int p = 0; p < 4; ++p)
 #pragma unroll
-            for (int i = 0; i < K; ++i) wt[c][i] = to_f32(wr[c * K + i]);
+            for (int i = 0; i < K; ++i) w2[p][i] = pack2(to_f32(wr[2 * p * K + i]), to_f32(wr[(2 * p + 1) * K + i]));
+#pragma unroll
+        for (int j = 0; j < L; ++j)
+#pragma unroll
+            for (int p = 0; p < 4; ++p) x2[j][p] = pack2(to_f32(e[2 * p * L + j]), to_f32(e[(2 * p + 1) * L + j]));
     }
     bf16* dst;
     int64_t head_stride = 0, base;
@@ -348,16 +353,23 @@ __global__ void conv_step_vec_kernel(const bf16* __restrict__ state, const bf16*
     const int64_t tok_stride = v_heads * dk;
 #pragma unroll
     for (int t = 0; t < T; ++t) {
-        uint4 out;
-        bf16* o = reinterpret_cast<bf16*>(&out);
+        // products rounded, then added in tap order from zero (two channels a packed instruction),
+        // rounded to bf16, SiLU in fp32 (silu8: the scalar formula's bits)
+        float pre[8], sil[8];
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-            float acc = 0.f;
+        for (int p = 0; p < 4; ++p) {
+            f32x2 acc = pack2(0.f, 0.f);
 #pragma unroll
-            for (int i = 0; i < K; ++i)
-                acc = __fadd_rn(acc, __fmul_rn(wt[c][i], to_f32(e[c * L + t + TAPS - K + 1 + i])));
-            o[c] = __float2bfloat16_rn(silu_f32(round_bf16(acc)));
+            for (int i = 0; i < K; ++i) acc = add2(acc, mul2(w2[p][i], x2[t + TAPS - K + 1 + i][p]));
+            const float2 r2 = unpack2(round_bf16x2(acc));
+            pre[2 * p] = r2.x;
+            pre[2 * p + 1] = r2.y;
         }
+        silu8(pre, sil);
+        uint4 out;
+        uint32_t* o = reinterpret_cast<uint32_t*>(&out);
+#pragma unroll
+        for (int p = 0; p < 4; ++p) o[p] = f2_to_bf2(pack2(sil[2 * p], sil[2 * p + 1]));
         bf16* row = dst + (b * T + t) * tok_stride + base;
         if (head_stride) {
             for (int r = 0; r < rep; ++r) *reinterpret_cast<uint4*>(row + r * head_stride) = out;
