@@ -156,6 +156,25 @@ GDN_API int gdn_recurrent_deltas(const void* q, const void* k, const void* v, in
                                  float scale, void* stream);
 
 /*
+ * gdn_recurrent_deltas on the tensor cores (bf16 q, k, v; 1 <= seqlen <= 8; an initial state) with
+ * the output-gated RMSNorm (GatedRMSNorm.forward, model/model.py:150-158; the engine's self.norm
+ * after delta_outputs, inference/engine.py:435) fused into the drain: y = norm(o) * w * silu(z),
+ * [B, T, HV, Dv] bf16 with z of the same layout and norm_weight [Dv] bf16. y equals
+ * gdn_recurrent_deltas's o through gdn_gated_rmsnorm bit for bit. GDN_ERR_UNSUPPORTED for more
+ * than 8 tokens.
+ */
+GDN_API int gdn_recurrent_deltas_gated_norm(const void* q, const void* k, const void* v,
+                                            const float* g, const void* beta, int beta_dtype,
+                                            const float* state_in, const void* z, const void* norm_weight,
+                                            float eps, void* y, float* deltas,
+                                            int64_t batch, int64_t seqlen, int64_t key_heads, int64_t value_heads,
+                                            int64_t head_dim_k, int64_t head_dim_v,
+                                            int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h,
+                                            int64_t k_stride_b, int64_t k_stride_t, int64_t k_stride_h,
+                                            int64_t v_stride_b, int64_t v_stride_t, int64_t v_stride_h,
+                                            float scale, void* stream);
+
+/*
  * The commit after gdn_recurrent_deltas: state[b] ([B, HV, Dk, Dv] fp32, in place) advances by
  * clamp(accepted[b], 0, T) tokens with S <- e^{g_t} S + k_t delta_t^T (k_t L2-normalised in the
  * kernel). Replaces delta_commit, inference/engine.py:254-258 (gated_delta_rule_advance_inplace,

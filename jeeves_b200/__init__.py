@@ -16,6 +16,7 @@ from .gated_delta import (  # noqa: F401
     gated_delta_rule_step,
     gated_delta_rule_verify,
     gated_delta_rule_verify_deltas,
+    gated_delta_rule_verify_deltas_gated_norm,
 )
 from .conv import causal_conv1d, causal_conv1d_step, conv_state_commit, conv_step, eager_conv_step  # noqa: F401
 from .norm import GatedRMSNorm, gated_rms_norm  # noqa: F401

@@ -46,6 +46,9 @@ SIGNATURES: dict[str, list] = {
     "gdn_recurrent_deltas": [_p, _p, _p, _i32, _p, _p, _i32, _p, _p, _p,
                              _i64, _i64, _i64, _i64, _i64, _i64,
                              _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _p],
+    "gdn_recurrent_deltas_gated_norm": [_p, _p, _p, _p, _p, _i32, _p, _p, _p, _f32, _p, _p,
+                                        _i64, _i64, _i64, _i64, _i64, _i64,
+                                        _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _p],
     "gdn_delta_commit": [_p, _p, _i32, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p],
     "gdn_chunk_prefill": [_p, _p, _p, _p, _p, _i32, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64,
                           _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _p, _sz, _p],

@@ -179,6 +179,36 @@ int gdn_recurrent_deltas(const void* q, const void* k, const void* v, int qkv_dt
                      k_stride_b, k_stride_t, k_stride_h, v_stride_b, v_stride_t, v_stride_h, scale, stream, deltas);
 }
 
+int gdn_recurrent_deltas_gated_norm(const void* q, const void* k, const void* v, const float* g, const void* beta,
+                                    int beta_dtype, const float* state_in, const void* z, const void* norm_weight,
+                                    float eps, void* y, float* deltas, int64_t batch, int64_t seqlen,
+                                    int64_t key_heads, int64_t value_heads, int64_t head_dim_k, int64_t head_dim_v,
+                                    int64_t q_stride_b, int64_t q_stride_t, int64_t q_stride_h, int64_t k_stride_b,
+                                    int64_t k_stride_t, int64_t k_stride_h, int64_t v_stride_b, int64_t v_stride_t,
+                                    int64_t v_stride_h, float scale, void* stream) {
+    if (!known_dtype(beta_dtype)) return GDN_ERR_DTYPE;
+    if (batch < 0 || seqlen < 0 || key_heads <= 0 || value_heads <= 0 || value_heads % key_heads) return GDN_ERR_SHAPE;
+    if (batch > 65535 || value_heads > 65535) return GDN_ERR_SHAPE;
+    if (head_dim_k != kHeadDim || head_dim_v != kHeadDim) return GDN_ERR_UNSUPPORTED;
+    if (seqlen > 8) return GDN_ERR_UNSUPPORTED;  // the tensor-core block takes up to 8 tokens
+    if (batch == 0 || seqlen == 0) return GDN_OK;
+    if (!q || !k || !v || !g || !beta || !state_in || !z || !norm_weight || !y || !deltas) return GDN_ERR_NULL;
+    if (!rows_aligned(q, 2, q_stride_b, q_stride_t, q_stride_h) || !rows_aligned(k, 2, k_stride_b, k_stride_t, k_stride_h) ||
+        !rows_aligned(v, 2, v_stride_b, v_stride_t, v_stride_h) || !aligned16(state_in) || !aligned16(z) ||
+        !aligned16(deltas))
+        return GDN_ERR_ALIGN;
+    VerifyBlockArgs vb{};
+    vb.q = q; vb.k = k; vb.v = v; vb.g = g; vb.beta = beta; vb.beta_dtype = beta_dtype;
+    vb.state_in = state_in; vb.o = nullptr; vb.deltas = deltas;
+    vb.rows = batch; vb.T = seqlen; vb.H = (int)key_heads; vb.HV = (int)value_heads;
+    vb.qsb = q_stride_b; vb.qst = q_stride_t; vb.qsh = q_stride_h;
+    vb.ksb = k_stride_b; vb.kst = k_stride_t; vb.ksh = k_stride_h;
+    vb.vsb = v_stride_b; vb.vst = v_stride_t; vb.vsh = v_stride_h;
+    vb.scale = scale;
+    vb.z = z; vb.norm_w = norm_weight; vb.y = y; vb.eps = eps;
+    return launch_verify_block(vb, as_stream(stream));
+}
+
 int gdn_delta_commit(float* state, const void* k, int k_dtype, const float* g, const float* deltas,
                      const int64_t* accepted, int64_t batch, int64_t seqlen, int64_t key_heads, int64_t value_heads,
                      int64_t head_dim_k, int64_t head_dim_v, int64_t k_stride_b, int64_t k_stride_t,

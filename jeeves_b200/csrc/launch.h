@@ -73,6 +73,11 @@ struct VerifyBlockArgs {
     int H, HV;
     int64_t qsb, qst, qsh, ksb, kst, ksh, vsb, vst, vsh;
     float scale;
+    // the output-gated RMSNorm fused into the drain: y instead of o when y is set
+    const void* z = nullptr;
+    const void* norm_w = nullptr;
+    void* y = nullptr;
+    float eps = 1e-6f;
 };
 int launch_verify_block(const VerifyBlockArgs& a, cudaStream_t s);
 

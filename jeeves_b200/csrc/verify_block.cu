@@ -27,6 +27,7 @@
 
 #include "common.cuh"
 #include "launch.h"
+#include "norm.cuh"
 #include "sm100.cuh"
 
 namespace gdn {
@@ -42,6 +43,7 @@ constexpr uint32_t kVA = 4 * kPanel;                // after hi (2 panels) and l
 constexpr uint32_t kSmem = kVA + 2 * kPanel + 1024; // the k / q rows, K-major in 128-row panels + alignment slack
 constexpr uint32_t kTmemCols = 64;                  // R from hi in columns 0-15, from lo in 16-31, the Gram in 32-47
 constexpr int kRowsPerThread = 16;                  // state rows w + 8 k of one 4-column group a thread holds
+enum : uint32_t { kBarDrain = 1 };                  // named barrier of the drain's warps 0-3
 
 enum : int { kSiteProduct = 0x302, kSiteGram = 0x303 };
 
@@ -53,8 +55,13 @@ struct Params {
     const float* g;
     const void* beta;
     int beta_f32;
-    bf16* o;          // [rows, T, HV, 128]
+    bf16* o;          // [rows, T, HV, 128], or null when the gated norm is fused (y)
     float* deltas;    // [rows, T, HV, 128]
+    // the output-gated RMSNorm fused into the drain, when y is set: y = norm(o) * w * silu(z)
+    const bf16* z;       // [rows, T, HV, 128]
+    const bf16* norm_w;  // [128]
+    bf16* y;             // [rows, T, HV, 128]
+    float eps;
     int64_t qsb, qst, qsh, ksb, kst, ksh, vsb, vst, vsh;
     int HV, rep, pairs;
     float scale;
@@ -66,11 +73,14 @@ struct Coef {
     float ck[kMaxT][kMaxT], cq[kMaxT][kMaxT];
     float dk[kMaxT], dq[kMaxT], dec[kMaxT], beta[kMaxT], rk[kMaxT], rq[kMaxT];
     float gram[2 * kMaxT][2 * kMaxT];  // raw row products: [a][b] = row a . row b (k rows, then q rows)
+    float xs[kMaxT][kHeadDim];         // the fused norm: the outputs as bf16 values
+    float inv[kMaxT];                  // and each token's 1 / sqrt(mean square + eps)
 };
 
 // The pair's inputs besides the state and the rows, deposited one pair ahead (two buffers).
 struct Aux {
     alignas(16) bf16 v[kMaxT][kHeadDim];
+    alignas(16) bf16 z[kMaxT][kHeadDim];  // with the fused norm
     float g[kMaxT], beta[kMaxT];
 };
 
@@ -87,7 +97,7 @@ struct Shared {
 // (lt < T: g_lt; T <= lt < 2T: beta_{lt - T}).
 struct Prefetch {
     uint4 rows[2];
-    uint4 vch;
+    uint4 vch, zch;
     float gb;
 };
 
@@ -105,8 +115,11 @@ __device__ __forceinline__ void prefetch(const Params& p, int pair, int lt, Pref
             f.rows[r] = *reinterpret_cast<const uint4*>(src + 8 * ch);
         }
     }
-    if (lt < T * 16) f.vch = *reinterpret_cast<const uint4*>(p.v + b * p.vsb + (int64_t)(lt >> 4) * p.vst + hv * p.vsh +
-                                                             8 * (lt & 15));
+    if (lt < T * 16) {
+        f.vch = *reinterpret_cast<const uint4*>(p.v + b * p.vsb + (int64_t)(lt >> 4) * p.vst + hv * p.vsh + 8 * (lt & 15));
+        if (p.y)
+            f.zch = *reinterpret_cast<const uint4*>(p.z + ((b * T + (lt >> 4)) * p.HV + hv) * kHeadDim + 8 * (lt & 15));
+    }
     if (lt < 2 * T) {
         const int t = lt < T ? lt : lt - T;
         const int64_t gi = (b * T + t) * p.HV + hv;
@@ -119,13 +132,16 @@ __device__ __forceinline__ void prefetch(const Params& p, int pair, int lt, Pref
 // Puts a prefetched pair into the bf16 K-major row operand (chunk ch of row n at its swizzled
 // place in K-panel ch / 8 of 128 rows) and into an Aux buffer.
 template <int T>
-__device__ __forceinline__ void deposit(const Prefetch& f, uint8_t* vb, Aux& aux, int lt) {
+__device__ __forceinline__ void deposit(const Prefetch& f, uint8_t* vb, Aux& aux, int lt, bool with_z) {
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
         const int it = lt + 128 * r, n = it >> 4, ch = it & 15;
         if (it < 2 * T * 16) *reinterpret_cast<uint4*>(vb + (ch >> 3) * kPanel + sw128(n, ch & 7)) = f.rows[r];
     }
-    if (lt < T * 16) *reinterpret_cast<uint4*>(&aux.v[lt >> 4][8 * (lt & 15)]) = f.vch;
+    if (lt < T * 16) {
+        *reinterpret_cast<uint4*>(&aux.v[lt >> 4][8 * (lt & 15)]) = f.vch;
+        if (with_z) *reinterpret_cast<uint4*>(&aux.z[lt >> 4][8 * (lt & 15)]) = f.zch;
+    }
     if (lt < T) aux.g[lt] = f.gb;
     else if (lt < 2 * T) aux.beta[lt - T] = f.gb;
 }
@@ -173,7 +189,7 @@ __global__ void __launch_bounds__(kThreads, 2) verify_block_kernel(const __grid_
     Prefetch pf;
     if (warp >= 4 && npairs > 0) {
         prefetch<T>(p, pair_of(0), tid - 128, pf);
-        deposit<T>(pf, vb, sh.aux[0], tid - 128);
+        deposit<T>(pf, vb, sh.aux[0], tid - 128, p.y != nullptr);
     }
     __syncthreads();
     const uint32_t tb = sh.tmem_base;
@@ -314,11 +330,37 @@ __global__ void __launch_bounds__(kThreads, 2) verify_block_kernel(const __grid_
                 for (int u = 0; u <= t; ++u) ot = __fmaf_rn(cf.cq[t][u], dl[u], ot);
                 const int64_t gi = (b * T + t) * p.HV + hv;
                 p.deltas[gi * kHeadDim + c] = dl[t];
-                p.o[gi * kHeadDim + c] = __float2bfloat16_rn(ot);
+                if (p.y) cf.xs[t][c] = round_bf16(ot);
+                else p.o[gi * kHeadDim + c] = __float2bfloat16_rn(ot);
+            }
+            if (p.y) {
+                // The output-gated RMSNorm of each token's row of 128 (GatedRMSNorm.forward,
+                // model/model.py:150-158) in the standalone norm kernel's order: lane l of a 16-lane
+                // group sums the squares of elements 8 l .. 8 l + 7, the group adds by xor shuffles.
+                named_sync(kBarDrain, 128);
+                {
+                    const int t = c >> 4 < T ? c >> 4 : 0, l = c & 15;
+                    float xs8[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) xs8[e] = cf.xs[t][8 * l + e];
+                    float sq = sum_squares8(xs8);
+#pragma unroll
+                    for (int off = 8; off > 0; off >>= 1) sq = __fadd_rn(sq, __shfl_xor_sync(0xffffffffu, sq, off));
+                    if (l == 0 && (c >> 4) < T) cf.inv[t] = gated_norm_inv(sq, p.eps);
+                }
+                named_sync(kBarDrain, 128);
+                const float wc = __bfloat162float(p.norm_w[c]);
+#pragma unroll
+                for (int t = 0; t < T; ++t) {
+                    const float normed = round_bf16(cf.xs[t][c] * cf.inv[t]);
+                    const float weighted = round_bf16(wc * normed);
+                    const float yv = weighted * silu_f32(__bfloat162float(aux.z[t][c]));
+                    p.y[((b * T + t) * p.HV + hv) * kHeadDim + c] = __float2bfloat16_rn(yv);
+                }
             }
         } else if (j + 1 < npairs) {
             // ---- warps 4-7: the next pair's prefetched inputs (the products that read the rows are done)
-            deposit<T>(pf, vb, sh.aux[(j + 1) & 1], tid - 128);
+            deposit<T>(pf, vb, sh.aux[(j + 1) & 1], tid - 128, p.y != nullptr);
         }
         tc_fence_before();
         __syncthreads();
@@ -367,6 +409,10 @@ int launch_verify_block(const VerifyBlockArgs& a, cudaStream_t s) {
     p.beta_f32 = a.beta_dtype == GDN_F32;
     p.o = static_cast<bf16*>(a.o);
     p.deltas = a.deltas;
+    p.z = static_cast<const bf16*>(a.z);
+    p.norm_w = static_cast<const bf16*>(a.norm_w);
+    p.y = static_cast<bf16*>(a.y);
+    p.eps = a.eps;
     p.qsb = a.qsb; p.qst = a.qst; p.qsh = a.qsh;
     p.ksb = a.ksb; p.kst = a.kst; p.ksh = a.ksh;
     p.vsb = a.vsb; p.vst = a.vst; p.vsh = a.vsh;

@@ -301,6 +301,44 @@ def gated_delta_rule_verify_deltas(q, k, v, g, beta, state, deltas=None, scale=N
     return o, deltas
 
 
+def gated_delta_rule_verify_deltas_gated_norm(q, k, v, g, beta, state, z, norm_weight, eps=1e-6, deltas=None,
+                                              scale=None):
+    """``gated_delta_rule_verify_deltas`` with the output-gated RMSNorm (``GatedRMSNorm.forward``,
+    ``model/model.py:150-158``; the engine's ``self.norm`` after ``delta_outputs``,
+    ``inference/engine.py:435``) fused into the tensor-core block's drain: returns
+    ``(y, deltas)`` with ``y [B, T, HV, 128]`` bf16 equal to ``gated_rms_norm(o, z, norm_weight)`` of
+    the unfused call bit for bit. Needs bf16 rows and 1 <= T <= 8."""
+    what = "gated_delta_rule_verify_deltas_gated_norm"
+    _require_cuda(what, q, k, v, g, beta, state, z, norm_weight, deltas)
+    B, T, H, HV = _check_qkv(what, q, k, v)
+    if q.dtype != torch.bfloat16 or not 1 <= T <= 8:
+        raise ValueError(f"{what}: expected bfloat16 rows and 1 to 8 tokens, got {q.dtype}, {T}")
+    g, beta = _gates(what, g, beta, B, T, HV)
+    h0 = _state_arg(what, state, B, HV, name="state")
+    if h0 is None:
+        raise ValueError(f"{what}: a state is required")
+    shape = (B, T, HV, HEAD_DIM)
+    z = z.reshape(shape)
+    if z.dtype != torch.bfloat16:
+        raise ValueError(f"z: expected bfloat16, got {z.dtype}")
+    z = z.contiguous()
+    w = norm_weight.reshape(HEAD_DIM).to(torch.bfloat16).contiguous()
+    if deltas is None:
+        deltas = torch.empty(shape, dtype=torch.float32, device=q.device)
+    elif deltas.shape != shape or deltas.dtype != torch.float32 or not deltas.is_contiguous():
+        raise ValueError(f"deltas: expected a contiguous float32 tensor of shape {shape}, got {deltas.dtype} "
+                         f"{tuple(deltas.shape)}")
+    q, k, v = _heads_last_contiguous(q), _heads_last_contiguous(k), _heads_last_contiguous(v)
+    y = torch.empty(shape, dtype=torch.bfloat16, device=q.device)
+    status = _lib.load().gdn_recurrent_deltas_gated_norm(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(), beta.data_ptr(), _DTYPES[beta.dtype], h0.data_ptr(),
+        z.data_ptr(), w.data_ptr(), float(eps), y.data_ptr(), deltas.data_ptr(), B, T, H, HV, HEAD_DIM, HEAD_DIM,
+        q.stride(0), q.stride(1), q.stride(2), k.stride(0), k.stride(1), k.stride(2), v.stride(0), v.stride(1),
+        v.stride(2), float(HEAD_DIM ** -0.5 if scale is None else scale), _stream())
+    _lib.check(status, what)
+    return y, deltas
+
+
 def gated_delta_rule_delta_commit(k, g, deltas, state, accepted) -> None:
     """Advance ``state[b]`` in place by ``clamp(accepted[b], 0, T)`` tokens from the update vectors of
     ``gated_delta_rule_verify_deltas`` (run on the same state, k and g), with one streaming pass over

@@ -16,7 +16,8 @@ from . import _lib
 from .conv import causal_conv1d, conv_state_commit, conv_step
 from .gated_delta import (HEAD_DIM, _require_cuda, _stream, gated_delta_rule_advance_inplace,
                           gated_delta_rule_chunk_gated_norm, gated_delta_rule_delta_commit, gated_delta_rule_rollback,
-                          gated_delta_rule_step, gated_delta_rule_verify, gated_delta_rule_verify_deltas)
+                          gated_delta_rule_step, gated_delta_rule_verify, gated_delta_rule_verify_deltas,
+                          gated_delta_rule_verify_deltas_gated_norm)
 from .norm import gated_rms_norm
 
 
@@ -117,6 +118,12 @@ def verify_layer_step(qkv, conv_state, conv_weight, g, beta, state, z, norm_weig
     if snapshots is not None:
         o, snapshots = gated_delta_rule_verify(q, k, v, g, beta, state, snapshots=snapshots, scale=scale)
     elif deltas is not None:
+        if q.dtype == torch.bfloat16 and 1 <= T <= 8 and B * v.shape[2] < 2048:
+            # few states (a GPU's share of a sharded batch): the gated norm in the block's drain saves a
+            # launch; with many, the block's chain is the limit and the standalone norm is faster
+            y, deltas = gated_delta_rule_verify_deltas_gated_norm(q, k, v, g, beta, state, z, norm_weight, eps,
+                                                                  deltas=deltas, scale=scale)
+            return y, (k, v, g, beta, snapshots, deltas)
         o, deltas = gated_delta_rule_verify_deltas(q, k, v, g, beta, state, deltas=deltas, scale=scale)
     else:
         o, _ = gated_delta_rule_step(q, k, v, g, beta, initial_state=state, output_final_state=False, scale=scale)

@@ -318,3 +318,21 @@ def test_delta_commit_checks_its_arguments():
         gdn.gated_delta_rule_delta_commit(k, g, deltas, h0[:1].clone(), acc)
     with pytest.raises(ValueError):
         gdn.gated_delta_rule_delta_commit(k, g, deltas, h0.clone(), acc.float())
+
+
+@pytest.mark.parametrize("T,B", [(1, 6), (5, 37), (8, 64)])
+def test_block_verify_with_fused_gated_norm_equals_the_two_calls(T, B):
+    """The gated norm in the block verify's drain gives the standalone norm of the block's outputs
+    bit for bit, update vectors included."""
+    H, HV = 4, 8
+    q, k, v, g, beta, h0 = cuda(*gdn_inputs(600 + T, B, T, H, HV, normalise=False))
+    gen = torch.Generator().manual_seed(601)
+    z = (torch.randn(B, T, HV, 128, generator=gen) * 3).to(torch.bfloat16)
+    z.view(-1)[::97] = 0
+    z.view(-1)[5::101] = -120.0
+    z = z.cuda()
+    nw = (torch.rand(128, generator=gen) + 0.5).to(torch.bfloat16).cuda()
+    o, d_ref = gdn.gated_delta_rule_verify_deltas(q, k, v, g, beta, h0)
+    y_ref = gdn.gated_rms_norm(o.view(-1, 128), z.view(-1, 128), nw).view(o.shape)
+    y, d = gdn.gated_delta_rule_verify_deltas_gated_norm(q, k, v, g, beta, h0, z, nw)
+    assert same_bits(y, y_ref) and same_bits(d, d_ref)
