@@ -25,6 +25,8 @@
 // ahead). Every wait is bounded; a wait that gives up raises the device error word, the CTA stops
 // taking pairs, waits for the products it started and frees its TMEM.
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "launch.h"
 #include "norm.cuh"
@@ -73,14 +75,20 @@ struct Coef {
     float ck[kMaxT][kMaxT], cq[kMaxT][kMaxT];
     float dk[kMaxT], dq[kMaxT], dec[kMaxT], beta[kMaxT], rk[kMaxT], rq[kMaxT];
     float gram[2 * kMaxT][2 * kMaxT];  // raw row products: [a][b] = row a . row b (k rows, then q rows)
-    float xs[kMaxT][kHeadDim];         // the fused norm: the outputs as bf16 values
-    float inv[kMaxT];                  // and each token's 1 / sqrt(mean square + eps)
 };
+
+// The fused norm's buffers (only in the kernels that fuse it): z one pair ahead (two buffers), the
+// outputs as bf16 values and each token's 1 / sqrt(mean square + eps).
+struct NormBufs {
+    alignas(16) bf16 z[2][kMaxT][kHeadDim];
+    float xs[kMaxT][kHeadDim];
+    float inv[kMaxT];
+};
+struct NoNorm {};
 
 // The pair's inputs besides the state and the rows, deposited one pair ahead (two buffers).
 struct Aux {
     alignas(16) bf16 v[kMaxT][kHeadDim];
-    alignas(16) bf16 z[kMaxT][kHeadDim];  // with the fused norm
     float g[kMaxT], beta[kMaxT];
 };
 
@@ -101,7 +109,7 @@ struct Prefetch {
     float gb;
 };
 
-template <int T>
+template <int T, bool NORM>
 __device__ __forceinline__ void prefetch(const Params& p, int pair, int lt, Prefetch& f) {
     const int64_t b = pair / p.HV;
     const int hv = pair % p.HV;
@@ -117,7 +125,7 @@ __device__ __forceinline__ void prefetch(const Params& p, int pair, int lt, Pref
     }
     if (lt < T * 16) {
         f.vch = *reinterpret_cast<const uint4*>(p.v + b * p.vsb + (int64_t)(lt >> 4) * p.vst + hv * p.vsh + 8 * (lt & 15));
-        if (p.y)
+        if (NORM)
             f.zch = *reinterpret_cast<const uint4*>(p.z + ((b * T + (lt >> 4)) * p.HV + hv) * kHeadDim + 8 * (lt & 15));
     }
     if (lt < 2 * T) {
@@ -132,7 +140,7 @@ __device__ __forceinline__ void prefetch(const Params& p, int pair, int lt, Pref
 // Puts a prefetched pair into the bf16 K-major row operand (chunk ch of row n at its swizzled
 // place in K-panel ch / 8 of 128 rows) and into an Aux buffer.
 template <int T>
-__device__ __forceinline__ void deposit(const Prefetch& f, uint8_t* vb, Aux& aux, int lt, bool with_z) {
+__device__ __forceinline__ void deposit(const Prefetch& f, uint8_t* vb, Aux& aux, int lt, bf16 (*zdst)[kHeadDim]) {
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
         const int it = lt + 128 * r, n = it >> 4, ch = it & 15;
@@ -140,17 +148,21 @@ __device__ __forceinline__ void deposit(const Prefetch& f, uint8_t* vb, Aux& aux
     }
     if (lt < T * 16) {
         *reinterpret_cast<uint4*>(&aux.v[lt >> 4][8 * (lt & 15)]) = f.vch;
-        if (with_z) *reinterpret_cast<uint4*>(&aux.z[lt >> 4][8 * (lt & 15)]) = f.zch;
+        if (zdst) *reinterpret_cast<uint4*>(&zdst[lt >> 4][8 * (lt & 15)]) = f.zch;
     }
     if (lt < T) aux.g[lt] = f.gb;
     else if (lt < 2 * T) aux.beta[lt - T] = f.gb;
 }
 
-template <int T>
+__device__ __forceinline__ bf16 (*z_buffer(NormBufs& nb, int i))[kHeadDim] { return nb.z[i]; }
+__device__ __forceinline__ bf16 (*z_buffer(NoNorm&, int))[kHeadDim] { return nullptr; }
+
+template <int T, bool NORM>
 __global__ void __launch_bounds__(kThreads, 2) verify_block_kernel(const __grid_constant__ Params p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     __shared__ Shared sh;
+    __shared__ typename std::conditional<NORM, NormBufs, NoNorm>::type nb;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int first = blockIdx.x, stride = gridDim.x;
     const int npairs = first < p.pairs ? (p.pairs - first + stride - 1) / stride : 0;
@@ -188,8 +200,8 @@ __global__ void __launch_bounds__(kThreads, 2) verify_block_kernel(const __grid_
     if (npairs > 0) load_state(0);
     Prefetch pf;
     if (warp >= 4 && npairs > 0) {
-        prefetch<T>(p, pair_of(0), tid - 128, pf);
-        deposit<T>(pf, vb, sh.aux[0], tid - 128, p.y != nullptr);
+        prefetch<T, NORM>(p, pair_of(0), tid - 128, pf);
+        deposit<T>(pf, vb, sh.aux[0], tid - 128, z_buffer(nb, 0));
     }
     __syncthreads();
     const uint32_t tb = sh.tmem_base;
@@ -200,7 +212,7 @@ __global__ void __launch_bounds__(kThreads, 2) verify_block_kernel(const __grid_
         const int pair = pair_of(j);
         const Aux& aux = sh.aux[j & 1];
         // the next pair's rows, v and gates start loading now and land during this pair
-        if (warp >= 4 && j + 1 < npairs) prefetch<T>(p, pair_of(j + 1), tid - 128, pf);
+        if (warp >= 4 && j + 1 < npairs) prefetch<T, NORM>(p, pair_of(j + 1), tid - 128, pf);
         // ---- the split: this thread's 16 x 4 state values into bf16 hi and lo (MN-major operands,
         // hi panels 0-1, lo panels 2-3; 8-byte halves of the swizzled 16-byte chunks)
         {
@@ -330,10 +342,10 @@ __global__ void __launch_bounds__(kThreads, 2) verify_block_kernel(const __grid_
                 for (int u = 0; u <= t; ++u) ot = __fmaf_rn(cf.cq[t][u], dl[u], ot);
                 const int64_t gi = (b * T + t) * p.HV + hv;
                 p.deltas[gi * kHeadDim + c] = dl[t];
-                if (p.y) cf.xs[t][c] = round_bf16(ot);
+                if constexpr (NORM) nb.xs[t][c] = round_bf16(ot);
                 else p.o[gi * kHeadDim + c] = __float2bfloat16_rn(ot);
             }
-            if (p.y) {
+            if constexpr (NORM) {
                 // The output-gated RMSNorm of each token's row of 128 (GatedRMSNorm.forward,
                 // model/model.py:150-158) in the standalone norm kernel's order: lane l of a 16-lane
                 // group sums the squares of elements 8 l .. 8 l + 7, the group adds by xor shuffles.
@@ -342,25 +354,25 @@ __global__ void __launch_bounds__(kThreads, 2) verify_block_kernel(const __grid_
                     const int t = c >> 4 < T ? c >> 4 : 0, l = c & 15;
                     float xs8[8];
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) xs8[e] = cf.xs[t][8 * l + e];
+                    for (int e = 0; e < 8; ++e) xs8[e] = nb.xs[t][8 * l + e];
                     float sq = sum_squares8(xs8);
 #pragma unroll
                     for (int off = 8; off > 0; off >>= 1) sq = __fadd_rn(sq, __shfl_xor_sync(0xffffffffu, sq, off));
-                    if (l == 0 && (c >> 4) < T) cf.inv[t] = gated_norm_inv(sq, p.eps);
+                    if (l == 0 && (c >> 4) < T) nb.inv[t] = gated_norm_inv(sq, p.eps);
                 }
                 named_sync(kBarDrain, 128);
                 const float wc = __bfloat162float(p.norm_w[c]);
 #pragma unroll
                 for (int t = 0; t < T; ++t) {
-                    const float normed = round_bf16(cf.xs[t][c] * cf.inv[t]);
+                    const float normed = round_bf16(nb.xs[t][c] * nb.inv[t]);
                     const float weighted = round_bf16(wc * normed);
-                    const float yv = weighted * silu_f32(__bfloat162float(aux.z[t][c]));
+                    const float yv = weighted * silu_f32(__bfloat162float(nb.z[j & 1][t][c]));
                     p.y[((b * T + t) * p.HV + hv) * kHeadDim + c] = __float2bfloat16_rn(yv);
                 }
             }
         } else if (j + 1 < npairs) {
             // ---- warps 4-7: the next pair's prefetched inputs (the products that read the rows are done)
-            deposit<T>(pf, vb, sh.aux[(j + 1) & 1], tid - 128, p.y != nullptr);
+            deposit<T>(pf, vb, sh.aux[(j + 1) & 1], tid - 128, z_buffer(nb, (j + 1) & 1));
         }
         tc_fence_before();
         __syncthreads();
@@ -388,8 +400,12 @@ int launch_verify_block(const VerifyBlockArgs& a, cudaStream_t s) {
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return GDN_ERR_LAUNCH;
     if (!ready[dev]) {
         bool ok = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && sms[dev] > 0;
-#define GDN_VB_ATTR(TT) \
-        ok = ok && cudaFuncSetAttribute(verify_block_kernel<TT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem) == cudaSuccess;
+#define GDN_VB_ATTR(TT)                                                                                          \
+        ok = ok &&                                                                                               \
+             cudaFuncSetAttribute(verify_block_kernel<TT, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,   \
+                                  (int)kSmem) == cudaSuccess &&                                                  \
+             cudaFuncSetAttribute(verify_block_kernel<TT, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,    \
+                                  (int)kSmem) == cudaSuccess;
         GDN_VB_ATTR(1) GDN_VB_ATTR(2) GDN_VB_ATTR(3) GDN_VB_ATTR(4) GDN_VB_ATTR(5) GDN_VB_ATTR(6) GDN_VB_ATTR(7)
         GDN_VB_ATTR(8)
 #undef GDN_VB_ATTR
@@ -423,8 +439,11 @@ int launch_verify_block(const VerifyBlockArgs& a, cudaStream_t s) {
     const int64_t slots = 2 * (int64_t)sms[dev];  // two CTAs an SM: one's serial phases overlap the other's
     const int grid = (int)(pairs < slots ? pairs : slots);
     switch (a.T) {
-#define GDN_VB_CASE(TT) \
-        case TT: verify_block_kernel<TT><<<grid, kThreads, kSmem, s>>>(p); break;
+#define GDN_VB_CASE(TT)                                                                \
+        case TT:                                                                       \
+            if (a.y) verify_block_kernel<TT, true><<<grid, kThreads, kSmem, s>>>(p);   \
+            else verify_block_kernel<TT, false><<<grid, kThreads, kSmem, s>>>(p);      \
+            break;
         GDN_VB_CASE(1) GDN_VB_CASE(2) GDN_VB_CASE(3) GDN_VB_CASE(4) GDN_VB_CASE(5) GDN_VB_CASE(6) GDN_VB_CASE(7)
         GDN_VB_CASE(8)
 #undef GDN_VB_CASE
