@@ -1052,6 +1052,7 @@ __device__ __forceinline__ void scan_cta(const ScanParams& p, int bx, int by) {
 }
 
 __global__ void __launch_bounds__(kScanThreads, 1) chunk_scan_kernel(const __grid_constant__ ScanParams p) {
+    pdl_launch_dependents();  // a gated norm launched after this kernel may stage its z early
     scan_cta(p, blockIdx.x, blockIdx.y);
 }
 
@@ -1071,6 +1072,7 @@ static_assert(FSmem::END % 1024 == 0, "factor warpgroup regions stay 1024-aligne
 __global__ void __launch_bounds__(kScanThreads, 1) chunk_fused_kernel(const __grid_constant__ FactorParams f,
                                                                        const __grid_constant__ ScanParams sp, int nscan,
                                                                        int scan_gx) {
+    pdl_launch_dependents();  // a gated norm launched after this kernel may stage its z early
     if ((int)blockIdx.x < nscan) {
         scan_cta(sp, (int)blockIdx.x % scan_gx, (int)blockIdx.x / scan_gx);
         return;
@@ -1171,7 +1173,9 @@ static const ChunkDevice& chunk_device() {
 static int finish_chunk(const ChunkArgs& a, cudaStream_t s) {
     const int st = launch_status();
     if (st != GDN_OK || a.y == nullptr) return st;
-    return launch_gated_rmsnorm(a.o, a.z, a.norm_w, a.y, a.B * a.T * a.HV, kHeadDim, a.eps, s);
+    // a programmatic dependent of the chunk kernel: its CTAs load z and the weight (inputs of the call,
+    // which the chunk kernel does not write) while the scan ends, and read o after griddepcontrol.wait
+    return launch_gated_rmsnorm(a.o, a.z, a.norm_w, a.y, a.B * a.T * a.HV, kHeadDim, a.eps, s, true);
 }
 
 int launch_chunk(const ChunkArgs& a, cudaStream_t s) {

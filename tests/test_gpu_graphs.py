@@ -26,6 +26,7 @@ def _inputs(seed):
              dq=dq, dk=dk, dv=dv, dg=dg, db=db, ds=torch.randn(6, HV, 128, 128, generator=gen) * 0.02,
              vq=vq, vk=vk, vv=vv, vg=vg, vb=vb, vs=torch.randn(3, HV, 128, 128, generator=gen) * 0.02,
              acc=torch.tensor([1, 4, 2]),
+             vz=torch.randn(3, 4, HV, 128, generator=gen).to(torch.bfloat16),
              qkv=(torch.randn(1, T, C, generator=gen) * 2).to(torch.bfloat16),
              w=(torch.randn(C, 4, generator=gen) * 0.5).to(torch.bfloat16),
              z=torch.randn(T * HV, 128, generator=gen).to(torch.bfloat16),
@@ -56,6 +57,12 @@ def _step(x, cu):
     out = gdn.gated_rms_norm(o.view(-1, 128), x["z"], x["nw"])
     od = fla_inplace.gated_delta_rule_step_inplace(x["dq"], x["dk"], x["dv"], x["dg"], x["db"], x["ds"])
     ov, snaps = gdn.gated_delta_rule_verify(x["vq"], x["vk"], x["vv"], x["vg"], x["vb"], x["vs"])
+    # the tensor-core block verify, plain and with the gated norm fused, then its delta commit
+    ob, db = gdn.gated_delta_rule_verify_deltas(x["vq"], x["vk"], x["vv"], x["vg"], x["vb"], x["vs"])
+    yb, _ = gdn.gated_delta_rule_verify_deltas_gated_norm(x["vq"], x["vk"], x["vv"], x["vg"], x["vb"], x["vs"],
+                                                          x["vz"], x["nw"])
+    sc = x["vs"].clone()
+    gdn.gated_delta_rule_delta_commit(x["vk"], x["vg"], db, sc, x["acc"])
     gdn.gated_delta_rule_rollback(x["vs"], snaps, x["acc"])
     # the gates inside the prefill and the gated norm fused into the call
     og, hg = gdn.gated_delta_rule_chunk_gates(x["q"], x["k"], x["v"], x["graw"][..., :HV], x["graw"][..., HV:],
@@ -69,7 +76,7 @@ def _step(x, cu):
     qm, km, vm = (x["cm"][..., i * D3:(i + 1) * D3].view(2, 2, HV, 128) for i in range(3))
     qr = gdn.rotate_into_cache(x["ck"], x["ck"], qm, km, vm, x["rcos"][:, :2], x["rsin"][:, :2], x["rcos"][:, 1:],
                                x["rsin"][:, 1:], x["kcache"], x["vcache"], x["rows"], x["positions"], 40)
-    return y, beta_g, g_g, o, ht, out, od, ov, og, hg, on, hn, oa, orot, qr
+    return y, beta_g, g_g, o, ht, out, od, ov, ob, db, yb, sc, og, hg, on, hn, oa, orot, qr
 
 
 def test_captured_layer_step_replays_equal_to_eager():
