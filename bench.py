@@ -642,6 +642,17 @@ def verify_unit_bytes(design, T=5, taps=3):
     return state * (1 + T) + conv + io
 
 
+def verify_launches(design, B, layers):
+    """Kernel launches of one config-4 step: per layer the conv step, the verify and the gated norm
+    (for the kept-update-vector design below 2,048 states the norm runs inside the block verify),
+    then the commits (one launch for all layers' kept update vectors, else one a layer) and the
+    conv states' commit."""
+    if design == "deltas":
+        per_layer = 2 if B * HV < 2048 else 3
+        return per_layer * layers + 1 + 1
+    return 3 * layers + layers + 1
+
+
 def bench_verify(gdn, args, device, rank, world, rank_sync, reduce_max, hbm_peak, layers=24, B_total=128, T=5,
                  taps=3):
     """Config 4: the verify branch of every delta layer (conv step over the conv-state window and
@@ -676,9 +687,7 @@ def bench_verify(gdn, args, device, rank, world, rank_sync, reduce_max, hbm_peak
             pending = [gdn.verify_layer_step(qkv[l], conv_states[l], w[l], g[l], beta[l], states[l], z[l], nw, H,
                                              ext_out=ext[l], snapshots=snaps[l], deltas=deltas[l])[1]
                        for l in range(layers)]
-            for l in range(layers):
-                gdn.verify_layer_commit(pending[l], states[l], accepted)
-            gdn.conv_state_commit(ext, conv_states, accepted)
+            gdn.verify_layers_commit(pending, states, accepted, ext=ext, conv_states=conv_states)
 
         graph = capture(step)
         ms = reduce_max(timed(lambda i: graph.replay(), args.steps, args.warmup, rank_sync)) / args.steps
@@ -702,7 +711,8 @@ def bench_verify(gdn, args, device, rank, world, rank_sync, reduce_max, hbm_peak
             "design": names[head],
             "value": best["value"], "unit": "scored tokens/s", "ms_per_step": best["ms_per_step"],
             "roofline": best["roofline"], other: out[other], "snapshots": out["snapshots"],
-            "gpu_launches": (3 * layers + layers + 1) * args.steps * 3}
+            "gpu_launches": (verify_launches("recompute", B, layers) + verify_launches("deltas", B, layers) +
+                             verify_launches("snapshots", B, layers)) * args.steps}
 
 
 # ------------------------------------------------------------------------------------------
@@ -988,9 +998,7 @@ def profile_case(name, device):
         for _ in range(2):
             pending = [gdn.verify_layer_step(qkv, conv_states[l], w, g, beta, states[l], z, nw, H, ext_out=ext[l],
                                              deltas=deltas[l])[1] for l in range(layers)]
-            for l in range(layers):
-                gdn.verify_layer_commit(pending[l], states[l], acc)
-            gdn.conv_state_commit(ext, conv_states, acc)
+            gdn.verify_layers_commit(pending, states, acc, ext=ext, conv_states=conv_states)
     else:
         raise SystemExit(f"unknown profile case {name}")
     torch.cuda.synchronize()

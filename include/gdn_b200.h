@@ -190,6 +190,40 @@ GDN_API int gdn_delta_commit(float* state, const void* k, int k_dtype, const flo
                              int64_t k_stride_b, int64_t k_stride_t, int64_t k_stride_h, void* stream);
 
 /*
+ * gdn_delta_commit for `layers` layers in one launch: the engine's commit loop over its layers
+ * (inference/engine.py:471-472, delta_commit per layer, :254-258). states[l], k[l], g[l], deltas[l]
+ * (host arrays of device pointers) as gdn_delta_commit takes them, with one accepted [B] and the same
+ * shapes and k strides for every layer. Each layer's state equals gdn_delta_commit's bit for bit.
+ * GDN_ERR_SHAPE if two layers' states overlap.
+ */
+GDN_API int gdn_delta_commit_layers(float* const* states, const void* const* k, int k_dtype,
+                                    const float* const* g, const float* const* deltas, int64_t layers,
+                                    const int64_t* accepted, int64_t batch, int64_t seqlen, int64_t key_heads,
+                                    int64_t value_heads, int64_t head_dim_k, int64_t head_dim_v,
+                                    int64_t k_stride_b, int64_t k_stride_t, int64_t k_stride_h, void* stream);
+
+/*
+ * The verify branch of one delta layer for T <= 8 drafted tokens per row, keeping the update
+ * vectors for gdn_delta_commit(_layers): the engine's conv_step, delta_outputs and norm
+ * (inference/engine.py:427-435; model/model.py:335-339, :297-302, :150-158) in one call.
+ * qkv: [B, T, C] bf16 pre-conv (row strides qkv_stride_b, qkv_stride_t; C = 2*H*Dk + HV*Dv laid out
+ * q | k | v); conv_state: [B, C, taps] bf16 (read); conv_w: [C, K] bf16; ext: [B, C, taps + T] bf16
+ * out (the window, for gdn_conv_state_commit); q, k, v: [B, T, HV, 128] bf16 out (q and k
+ * repeat-interleaved to the value heads; k feeds the commit); g: [B, T, HV] fp32; beta: [B, T, HV];
+ * state: [B, HV, 128, 128] fp32 (read); z: [B, T, HV, 128] bf16; norm_w: [128] bf16; y: [B, T, HV,
+ * 128] bf16 out; deltas: [B, T, HV, 128] fp32 out. The results equal gdn_conv_step followed by
+ * gdn_recurrent_deltas_gated_norm bit for bit. The tensor-core block verify starts as a
+ * programmatic dependent of the conv step (its set-up and state loads overlap the conv).
+ */
+GDN_API int gdn_verify_layer_deltas(const void* qkv, int64_t qkv_stride_b, int64_t qkv_stride_t,
+                                    const void* conv_state, const void* conv_w, void* ext, void* q, void* k,
+                                    void* v, const float* g, const void* beta, int beta_dtype, const float* state,
+                                    const void* z, const void* norm_w, void* y, float* deltas, int64_t batch,
+                                    int64_t seqlen, int64_t key_heads, int64_t value_heads, int64_t head_dim_k,
+                                    int64_t head_dim_v, int64_t taps, int64_t kernel_size, float scale, float eps,
+                                    void* stream);
+
+/*
  * Chunked prefill on tcgen05 tensor cores (chunk 64, WY/UT form) with an fp32 state.
  * Replaces gated_delta_rule_chunk, model/model.py:289-294 (fla chunk_gated_delta_rule
  * on CUDA; fp32 eager torch_chunk_gated_delta_rule :242-286). bf16 q, k: [B, T, H, Dk],

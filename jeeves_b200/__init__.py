@@ -12,6 +12,7 @@ from .gated_delta import (  # noqa: F401
     gated_delta_rule_chunk,
     gated_delta_rule_chunk_gated_norm,
     gated_delta_rule_delta_commit,
+    gated_delta_rule_delta_commit_layers,
     gated_delta_rule_rollback,
     gated_delta_rule_step,
     gated_delta_rule_verify,
@@ -22,7 +23,7 @@ from .conv import causal_conv1d, causal_conv1d_step, conv_state_commit, conv_ste
 from .norm import GatedRMSNorm, gated_rms_norm  # noqa: F401
 from .gates import delta_gates, gated_delta_rule_chunk_gates, gated_delta_rule_step_gates  # noqa: F401
 from .layer import (decode_layer_step, fp8_linear, in_proj_conv, prefill_layer, verify_layer_commit,  # noqa: F401
-                    verify_layer_step)
+                    verify_layer_step, verify_layers_commit)
 from .attention import decode_attention, rotary, rotate_into_cache  # noqa: F401
 from . import fla_inplace  # noqa: F401
 from ._lib import load as load_library  # noqa: F401

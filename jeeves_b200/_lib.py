@@ -50,6 +50,10 @@ SIGNATURES: dict[str, list] = {
                                         _i64, _i64, _i64, _i64, _i64, _i64,
                                         _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _p],
     "gdn_delta_commit": [_p, _p, _i32, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p],
+    "gdn_delta_commit_layers": [_p, _p, _i32, _p, _p, _i64, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
+                                _i64, _p],
+    "gdn_verify_layer_deltas": [_p, _i64, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _i32, _p, _p, _p, _p, _p,
+                                _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _f32, _p],
     "gdn_chunk_prefill": [_p, _p, _p, _p, _p, _i32, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64,
                           _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _f32, _p, _sz, _p],
     "gdn_chunk_prefill_gates": [_p, _p, _p, ctypes.POINTER(GateInputs), _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64,

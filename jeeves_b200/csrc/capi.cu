@@ -209,23 +209,85 @@ int gdn_recurrent_deltas_gated_norm(const void* q, const void* k, const void* v,
     return launch_verify_block(vb, as_stream(stream));
 }
 
+static int delta_commit(float* const* states, const void* const* ks, int k_dtype, const float* const* gs,
+                        const float* const* deltas, int64_t layers, const int64_t* accepted, int64_t batch,
+                        int64_t seqlen, int64_t key_heads, int64_t value_heads, int64_t head_dim_k, int64_t head_dim_v,
+                        int64_t k_stride_b, int64_t k_stride_t, int64_t k_stride_h, void* stream) {
+    if (!known_dtype(k_dtype)) return GDN_ERR_DTYPE;
+    if (layers < 0 || batch < 0 || seqlen < 0 || key_heads <= 0 || value_heads <= 0 || value_heads % key_heads)
+        return GDN_ERR_SHAPE;
+    if (batch > 65535 || value_heads > 65535) return GDN_ERR_SHAPE;
+    if (head_dim_k != kHeadDim || head_dim_v != kHeadDim) return GDN_ERR_UNSUPPORTED;
+    if (batch == 0 || seqlen == 0 || layers == 0) return GDN_OK;
+    if (!states || !ks || !gs || !deltas || !accepted) return GDN_ERR_NULL;
+    const int64_t state_bytes = batch * value_heads * kHeadDim * kHeadDim * (int64_t)sizeof(float);
+    for (int64_t l = 0; l < layers; ++l) {
+        if (!states[l] || !ks[l] || !gs[l] || !deltas[l]) return GDN_ERR_NULL;
+        if (!aligned16(states[l]) || !aligned16(deltas[l]) ||
+            !rows_aligned(ks[l], elem_size(k_dtype), k_stride_b, k_stride_t, k_stride_h))
+            return GDN_ERR_ALIGN;
+        // the layers' states are advanced by one launch: no two may overlap
+        const char* a0 = reinterpret_cast<const char*>(states[l]);
+        for (int64_t m = 0; m < l; ++m) {
+            const char* b0 = reinterpret_cast<const char*>(states[m]);
+            if (a0 < b0 + state_bytes && b0 < a0 + state_bytes) return GDN_ERR_SHAPE;
+        }
+    }
+    DeltaCommitArgs a{};
+    a.states = states; a.ks = ks; a.k_dtype = k_dtype; a.gs = gs; a.deltas = deltas; a.layers = layers;
+    a.accepted = accepted;
+    a.rows = batch; a.T = seqlen; a.H = (int)key_heads; a.HV = (int)value_heads;
+    a.ksb = k_stride_b; a.kst = k_stride_t; a.ksh = k_stride_h;
+    return launch_delta_commit(a, as_stream(stream));
+}
+
 int gdn_delta_commit(float* state, const void* k, int k_dtype, const float* g, const float* deltas,
                      const int64_t* accepted, int64_t batch, int64_t seqlen, int64_t key_heads, int64_t value_heads,
                      int64_t head_dim_k, int64_t head_dim_v, int64_t k_stride_b, int64_t k_stride_t,
                      int64_t k_stride_h, void* stream) {
-    if (!known_dtype(k_dtype)) return GDN_ERR_DTYPE;
+    return delta_commit(&state, &k, k_dtype, &g, &deltas, 1, accepted, batch, seqlen, key_heads, value_heads,
+                        head_dim_k, head_dim_v, k_stride_b, k_stride_t, k_stride_h, stream);
+}
+
+int gdn_delta_commit_layers(float* const* states, const void* const* k, int k_dtype, const float* const* g,
+                            const float* const* deltas, int64_t layers, const int64_t* accepted, int64_t batch,
+                            int64_t seqlen, int64_t key_heads, int64_t value_heads, int64_t head_dim_k,
+                            int64_t head_dim_v, int64_t k_stride_b, int64_t k_stride_t, int64_t k_stride_h,
+                            void* stream) {
+    return delta_commit(states, k, k_dtype, g, deltas, layers, accepted, batch, seqlen, key_heads, value_heads,
+                        head_dim_k, head_dim_v, k_stride_b, k_stride_t, k_stride_h, stream);
+}
+
+int gdn_verify_layer_deltas(const void* qkv, int64_t qkv_stride_b, int64_t qkv_stride_t, const void* conv_state,
+                            const void* conv_w, void* ext, void* q, void* k, void* v, const float* g,
+                            const void* beta, int beta_dtype, const float* state, const void* z, const void* norm_w,
+                            void* y, float* deltas, int64_t batch, int64_t seqlen, int64_t key_heads,
+                            int64_t value_heads, int64_t head_dim_k, int64_t head_dim_v, int64_t taps,
+                            int64_t kernel_size, float scale, float eps, void* stream) {
+    if (!known_dtype(beta_dtype)) return GDN_ERR_DTYPE;
     if (batch < 0 || seqlen < 0 || key_heads <= 0 || value_heads <= 0 || value_heads % key_heads) return GDN_ERR_SHAPE;
+    if (taps < 1 || taps > 8 || kernel_size < 1 || kernel_size > taps + 1 || kernel_size > 8) return GDN_ERR_SHAPE;
     if (batch > 65535 || value_heads > 65535) return GDN_ERR_SHAPE;
     if (head_dim_k != kHeadDim || head_dim_v != kHeadDim) return GDN_ERR_UNSUPPORTED;
+    if (seqlen > 8) return GDN_ERR_UNSUPPORTED;  // the tensor-core block takes up to 8 tokens
     if (batch == 0 || seqlen == 0) return GDN_OK;
-    if (!state || !k || !g || !deltas || !accepted) return GDN_ERR_NULL;
-    if (!aligned16(state) || !aligned16(deltas) || !rows_aligned(k, elem_size(k_dtype), k_stride_b, k_stride_t, k_stride_h))
+    if (!qkv || !conv_state || !conv_w || !ext || !q || !k || !v || !g || !beta || !state || !z || !norm_w || !y ||
+        !deltas)
+        return GDN_ERR_NULL;
+    // qkv may have any row strides (the conv step takes 16-byte accesses only where they are aligned)
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(state) || !aligned16(z) || !aligned16(y) ||
+        !aligned16(deltas) || !aligned16(norm_w))
         return GDN_ERR_ALIGN;
-    DeltaCommitArgs a{};
-    a.state = state; a.k = k; a.k_dtype = k_dtype; a.g = g; a.deltas = deltas; a.accepted = accepted;
-    a.rows = batch; a.T = seqlen; a.H = (int)key_heads; a.HV = (int)value_heads;
-    a.ksb = k_stride_b; a.kst = k_stride_t; a.ksh = k_stride_h;
-    return launch_delta_commit(a, as_stream(stream));
+    VerifyLayerArgs a{};
+    a.qkv = qkv; a.qkv_sb = qkv_stride_b; a.qkv_st = qkv_stride_t;
+    a.conv_state = conv_state; a.conv_w = conv_w; a.ext = ext;
+    a.q = q; a.k = k; a.v = v;
+    a.g = g; a.beta = beta; a.beta_dtype = beta_dtype;
+    a.state = state; a.z = z; a.norm_w = norm_w; a.y = y; a.deltas = deltas;
+    a.B = batch; a.T = seqlen; a.H = (int)key_heads; a.HV = (int)value_heads;
+    a.taps = (int)taps; a.K = (int)kernel_size;
+    a.scale = scale; a.eps = eps;
+    return launch_verify_layer(a, as_stream(stream));
 }
 
 static int chunk_prefill(const void* q, const void* k, const void* v, const float* g, const void* beta, int beta_dtype,

@@ -289,6 +289,7 @@ __global__ void conv_step_kernel(const bf16* __restrict__ state, const bf16* __r
 // channels' ext rows are one contiguous block of 8 L values: the state block and the T token
 // vectors are loaded with 16-byte loads, the block is stored with 16-byte stores, and each token's
 // 8 outputs go out as one 16-byte store (per repeated head for q and k). Same arithmetic as above.
+// (One thread per token as well, the window shared through L2, was slower at 16 to 128 rows.)
 template <int TAPS, int T>
 __global__ void conv_step_vec_kernel(const bf16* __restrict__ state, const bf16* __restrict__ qkv, int64_t sqb,
                                      int64_t sqt, const bf16* __restrict__ w, bf16* __restrict__ ext,
@@ -296,6 +297,8 @@ __global__ void conv_step_vec_kernel(const bf16* __restrict__ state, const bf16*
                                      int64_t C, int64_t key_dim, int64_t value_dim, int dk, int rep) {
     constexpr int K = 4, L = TAPS + T;
     static_assert(TAPS >= K - 1 && TAPS <= 8, "the window covers every tap");
+    // a verify that follows as a programmatic dependent may set up and load its states meanwhile
+    pdl_launch_dependents();
     const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int64_t groups = C / 8;
     if (idx >= B * groups) return;

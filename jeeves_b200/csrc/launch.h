@@ -44,13 +44,15 @@ struct RecurrentArgs {
 };
 int launch_recurrent(const RecurrentArgs& a, cudaStream_t s);
 
+// Per layer l < layers (host arrays of device pointers; the layers' states must not overlap):
 struct DeltaCommitArgs {
-    float* state;             // [rows, HV, 128, 128] fp32, advanced in place
-    const void* k;            // [rows, T, H, 128] with element strides ksb, kst, ksh
+    float* const* states;          // [rows, HV, 128, 128] fp32, advanced in place
+    const void* const* ks;         // [rows, T, H, 128] with element strides ksb, kst, ksh (every layer)
     int k_dtype;
-    const float* g;           // [rows, T, HV]
-    const float* deltas;      // [rows, T, HV, 128] fp32 from the verify
-    const int64_t* accepted;  // [rows]
+    const float* const* gs;        // [rows, T, HV]
+    const float* const* deltas;    // [rows, T, HV, 128] fp32 from the verify
+    int64_t layers;
+    const int64_t* accepted;       // [rows], shared by the layers
     int64_t rows, T;
     int H, HV;
     int64_t ksb, kst, ksh;
@@ -78,8 +80,44 @@ struct VerifyBlockArgs {
     const void* norm_w = nullptr;
     void* y = nullptr;
     float eps = 1e-6f;
+    // programmatic launch: the CTAs set up and load their first states while the previous kernel in
+    // the stream runs, and wait for it before reading anything else. Only for a previous kernel that
+    // does not write the states (the verify layer's conv step).
+    bool dependent = false;
 };
 int launch_verify_block(const VerifyBlockArgs& a, cudaStream_t s);
+
+// The verify branch of one delta layer that keeps its update vectors (verify_block.cu): the conv
+// step over the conv-state window and the T new tokens (ext [B, C, taps + T]; q, k
+// repeat-interleaved to the value heads and v, each [B, T, HV, 128] bf16), then the block verify of
+// `state` (a programmatic dependent of the conv step) with the output-gated RMSNorm: y [B, T, HV,
+// 128] bf16, deltas [B, T, HV, 128] fp32. bf16 throughout, T <= 8, 128-wide heads.
+struct VerifyLayerArgs {
+    const void* qkv;
+    int64_t qkv_sb, qkv_st;
+    const void* conv_state;
+    const void* conv_w;
+    void* ext;
+    void* q;
+    void* k;
+    void* v;
+    const float* g;
+    const void* beta;
+    int beta_dtype;
+    const float* state;
+    const void* z;
+    const void* norm_w;
+    void* y;
+    float* deltas;
+    int64_t B, T;
+    int H, HV, taps, K;
+    float scale, eps;
+};
+int launch_verify_layer(const VerifyLayerArgs& a, cudaStream_t s);
+// Below this many (row, value head) states the verify layer runs the gated norm in the block's drain
+// (a launch saved); from here up the block's per-state chain is the limit and the standalone norm
+// after it is faster.
+constexpr int64_t kVerifyFusedNormStates = 2048;
 
 struct ChunkArgs {
     const void* q;

@@ -198,6 +198,9 @@ __global__ void __launch_bounds__(kThreads, 2) verify_block_kernel(const __grid_
         for (int k = 0; k < kRowsPerThread; ++k) sv[k] = ldg_stream(reinterpret_cast<const float4*>(src + 8 * k * kHeadDim));
     };
     if (npairs > 0) load_state(0);
+    // As a programmatic dependent of the verify layer's conv step, the set-up and the first state
+    // loads above overlap that kernel; the rows, v, gates and z are read only past this point.
+    pdl_wait();
     Prefetch pf;
     if (warp >= 4 && npairs > 0) {
         prefetch<T, NORM>(p, pair_of(0), tid - 128, pf);
@@ -211,6 +214,8 @@ __global__ void __launch_bounds__(kThreads, 2) verify_block_kernel(const __grid_
     for (int j = 0; j < npairs; ++j) {
         const int pair = pair_of(j);
         const Aux& aux = sh.aux[j & 1];
+        // a gated norm launched as this kernel's dependent may stage its z during the last pairs
+        if (j + 1 == npairs) pdl_launch_dependents();
         // the next pair's rows, v and gates start loading now and land during this pair
         if (warp >= 4 && j + 1 < npairs) prefetch<T, NORM>(p, pair_of(j + 1), tid - 128, pf);
         // ---- the split: this thread's 16 x 4 state values into bf16 hi and lo (MN-major operands,
@@ -438,18 +443,66 @@ int launch_verify_block(const VerifyBlockArgs& a, cudaStream_t s) {
     p.scale = a.scale;
     const int64_t slots = 2 * (int64_t)sms[dev];  // two CTAs an SM: one's serial phases overlap the other's
     const int grid = (int)(pairs < slots ? pairs : slots);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = a.dependent ? 1 : 0;
+    cudaError_t err;
     switch (a.T) {
-#define GDN_VB_CASE(TT)                                                                \
-        case TT:                                                                       \
-            if (a.y) verify_block_kernel<TT, true><<<grid, kThreads, kSmem, s>>>(p);   \
-            else verify_block_kernel<TT, false><<<grid, kThreads, kSmem, s>>>(p);      \
+#define GDN_VB_CASE(TT)                                                                                   \
+        case TT:                                                                                          \
+            err = a.y ? cudaLaunchKernelEx(&cfg, verify_block_kernel<TT, true>, p)                        \
+                      : cudaLaunchKernelEx(&cfg, verify_block_kernel<TT, false>, p);                      \
             break;
         GDN_VB_CASE(1) GDN_VB_CASE(2) GDN_VB_CASE(3) GDN_VB_CASE(4) GDN_VB_CASE(5) GDN_VB_CASE(6) GDN_VB_CASE(7)
         GDN_VB_CASE(8)
 #undef GDN_VB_CASE
         default: return GDN_ERR_UNSUPPORTED;
     }
-    return launch_status();
+    return err == cudaSuccess ? launch_status() : GDN_ERR_LAUNCH;
+}
+
+// The engine's verify branch of a delta layer (conv_step, delta_outputs, norm;
+// inference/engine.py:427-435) in one call. The block verify is a programmatic dependent of the
+// conv step: the conv does not write the states, so the block's CTAs set up, allocate TMEM and load
+// their first states while the conv runs. For few states the gated norm runs in the block's drain;
+// otherwise the block writes its outputs into y and the standalone norm normalises y in place, as
+// a programmatic dependent of the block.
+int launch_verify_layer(const VerifyLayerArgs& a, cudaStream_t s) {
+    if (a.B == 0 || a.T == 0) return GDN_OK;  // nothing launched, so nothing may depend on a launch
+    if (a.T > vblock::kMaxT) return GDN_ERR_UNSUPPORTED;
+    const int64_t key_dim = (int64_t)a.H * kHeadDim, value_dim = (int64_t)a.HV * kHeadDim;
+    int st = launch_conv_step(a.conv_state, a.qkv, a.qkv_sb, a.qkv_st, a.conv_w, a.ext, a.q, a.k, a.v, a.B, a.T,
+                              a.taps, a.K, key_dim, value_dim, kHeadDim, kHeadDim, s);
+    if (st != GDN_OK) return st;
+    VerifyBlockArgs b{};
+    b.q = a.q; b.k = a.k; b.v = a.v;
+    b.g = a.g; b.beta = a.beta; b.beta_dtype = a.beta_dtype;
+    b.state_in = a.state;
+    b.deltas = a.deltas;
+    b.rows = a.B; b.T = a.T;
+    b.H = a.HV; b.HV = a.HV;  // q and k come repeat-interleaved to the value heads
+    const int64_t tok = value_dim;
+    b.qsb = b.ksb = b.vsb = a.T * tok;
+    b.qst = b.kst = b.vst = tok;
+    b.qsh = b.ksh = b.vsh = kHeadDim;
+    b.scale = a.scale;
+    b.dependent = true;
+    const bool fused = a.B * a.HV < kVerifyFusedNormStates;
+    if (fused) {
+        b.z = a.z; b.norm_w = a.norm_w; b.y = a.y; b.eps = a.eps;
+    } else {
+        b.o = a.y;
+    }
+    st = launch_verify_block(b, s);
+    if (st != GDN_OK || fused) return st;
+    return launch_gated_rmsnorm(a.y, a.z, a.norm_w, a.y, a.B * a.T * a.HV, kHeadDim, a.eps, s, true);
 }
 
 }  // namespace gdn

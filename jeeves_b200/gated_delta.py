@@ -10,6 +10,8 @@ repeat-interleave mapping of ``model/model.py:487-490``), v ``[B, T, HV, 128]``,
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from . import _lib
@@ -366,6 +368,61 @@ def gated_delta_rule_delta_commit(k, g, deltas, state, accepted) -> None:
     status = _lib.load().gdn_delta_commit(state.data_ptr(), k.data_ptr(), _DTYPES[k.dtype], g.data_ptr(),
                                           deltas.data_ptr(), accepted.to(torch.int64).contiguous().data_ptr(), B, T,
                                           H, HV, HEAD_DIM, HEAD_DIM, k.stride(0), k.stride(1), k.stride(2), _stream())
+    _lib.check(status, what)
+
+
+def gated_delta_rule_delta_commit_layers(ks, gs, deltas, states, accepted) -> None:
+    """``gated_delta_rule_delta_commit`` for every layer of a model in one launch: layer l's
+    ``states[l]`` advances by ``clamp(accepted[b], 0, T)`` tokens from ``ks[l]``, ``gs[l]`` and
+    ``deltas[l]`` (the engine's commit loop over its layers, ``inference/engine.py:471-472``). Every
+    layer has the same shapes and k strides; each state ends as the one-layer commit leaves it, bit
+    for bit."""
+    what = "gated_delta_rule_delta_commit_layers"
+    ks, gs, deltas, states = list(ks), list(gs), list(deltas), list(states)
+    L = len(states)
+    if not (len(ks) == len(gs) == len(deltas) == L):
+        raise ValueError(f"{what}: expected as many k, g and deltas tensors as states, got {len(ks)}, {len(gs)}, "
+                         f"{len(deltas)} and {L}")
+    if L == 0:
+        return
+    _require_cuda(what, *ks, *gs, *deltas, *states, accepted)
+    k0 = ks[0]
+    if k0.dim() != 4 or k0.shape[-1] != HEAD_DIM:
+        raise ValueError(f"k: expected [B, T, H, {HEAD_DIM}], got {tuple(k0.shape)}")
+    B, T, H = k0.shape[:3]
+    HV = deltas[0].shape[2] if deltas[0].dim() == 4 else -1
+    if HV <= 0 or HV % H:
+        raise ValueError(f"deltas: expected [B, T, HV, {HEAD_DIM}] with HV a multiple of {H}, got "
+                         f"{tuple(deltas[0].shape)}")
+    if accepted.shape != (B,) or accepted.dtype not in (torch.int32, torch.int64):
+        raise ValueError(f"accepted: expected {B} integers, got {accepted.dtype} {tuple(accepted.shape)}")
+    k_dtype = k0.dtype
+    strides = None
+    kk, gg = [], []
+    for l in range(L):
+        k = _heads_last_contiguous(ks[l])
+        if k.shape != k0.shape or k.dtype != k_dtype:
+            raise ValueError(f"k[{l}]: expected {k_dtype} {tuple(k0.shape)}, got {k.dtype} {tuple(k.shape)}")
+        if strides is None:
+            strides = k.stride()[:3]
+        elif k.stride()[:3] != strides:
+            k = k.contiguous()
+            if k.stride()[:3] != strides:
+                raise ValueError(f"k[{l}]: the layers' k tensors need the same strides")
+        d = deltas[l]
+        if d.shape != (B, T, HV, HEAD_DIM) or d.dtype != torch.float32 or not d.is_contiguous():
+            raise ValueError(f"deltas[{l}]: expected a contiguous float32 tensor of shape {(B, T, HV, HEAD_DIM)}")
+        _check_state_inplace(what, states[l], B, HV)
+        g = gs[l]
+        if g.shape != (B, T, HV) or g.dtype != torch.float32:
+            raise ValueError(f"g[{l}]: expected float32 {(B, T, HV)}, got {g.dtype} {tuple(g.shape)}")
+        kk.append(k)
+        gg.append(g.contiguous())
+    arr = ctypes.c_void_p * L
+    status = _lib.load().gdn_delta_commit_layers(
+        arr(*[s.data_ptr() for s in states]), arr(*[k.data_ptr() for k in kk]), _DTYPES[k_dtype],
+        arr(*[g.data_ptr() for g in gg]), arr(*[d.data_ptr() for d in deltas]), L,
+        accepted.to(torch.int64).contiguous().data_ptr(), B, T, H, HV, HEAD_DIM, HEAD_DIM, *strides, _stream())
     _lib.check(status, what)
 
 

@@ -14,10 +14,10 @@ import torch
 
 from . import _lib
 from .conv import causal_conv1d, conv_state_commit, conv_step
-from .gated_delta import (HEAD_DIM, _require_cuda, _stream, gated_delta_rule_advance_inplace,
-                          gated_delta_rule_chunk_gated_norm, gated_delta_rule_delta_commit, gated_delta_rule_rollback,
-                          gated_delta_rule_step, gated_delta_rule_verify, gated_delta_rule_verify_deltas,
-                          gated_delta_rule_verify_deltas_gated_norm)
+from .gated_delta import (_DTYPES, HEAD_DIM, _require_cuda, _stream, gated_delta_rule_advance_inplace,
+                          gated_delta_rule_chunk_gated_norm, gated_delta_rule_delta_commit,
+                          gated_delta_rule_delta_commit_layers, gated_delta_rule_rollback, gated_delta_rule_step,
+                          gated_delta_rule_verify, gated_delta_rule_verify_deltas)
 from .norm import gated_rms_norm
 
 
@@ -112,23 +112,74 @@ def verify_layer_step(qkv, conv_state, conv_weight, g, beta, state, z, norm_weig
     if C <= 2 * kd or (C - 2 * kd) % HEAD_DIM:
         raise ValueError(f"qkv: {C} channels do not split into 2 x {kd} key channels and whole value heads")
     vd = C - 2 * kd
-    _, q, k, v = conv_step(conv_state, qkv, conv_weight, kd, vd, HEAD_DIM, HEAD_DIM, ext_out=ext_out)
     if snapshots is not None and deltas is not None:
         raise ValueError(f"{what}: pass snapshots or deltas, not both")
+    if deltas is not None and qkv.dtype == torch.bfloat16 and 1 <= T <= 8:
+        return _verify_layer_deltas(what, qkv, conv_state, conv_weight, g, beta, state, z, norm_weight, key_heads,
+                                    ext_out, eps, scale, deltas)
+    _, q, k, v = conv_step(conv_state, qkv, conv_weight, kd, vd, HEAD_DIM, HEAD_DIM, ext_out=ext_out)
     if snapshots is not None:
         o, snapshots = gated_delta_rule_verify(q, k, v, g, beta, state, snapshots=snapshots, scale=scale)
     elif deltas is not None:
-        if q.dtype == torch.bfloat16 and 1 <= T <= 8 and B * v.shape[2] < 2048:
-            # few states (a GPU's share of a sharded batch): the gated norm in the block's drain saves a
-            # launch; with many, the block's chain is the limit and the standalone norm is faster
-            y, deltas = gated_delta_rule_verify_deltas_gated_norm(q, k, v, g, beta, state, z, norm_weight, eps,
-                                                                  deltas=deltas, scale=scale)
-            return y, (k, v, g, beta, snapshots, deltas)
         o, deltas = gated_delta_rule_verify_deltas(q, k, v, g, beta, state, deltas=deltas, scale=scale)
     else:
         o, _ = gated_delta_rule_step(q, k, v, g, beta, initial_state=state, output_final_state=False, scale=scale)
     y = gated_rms_norm(o.view(-1, HEAD_DIM), z.reshape(-1, HEAD_DIM), norm_weight, eps).view(o.shape)
     return y, (k, v, g, beta, snapshots, deltas)
+
+
+def _verify_layer_deltas(what, qkv, conv_state, conv_weight, g, beta, state, z, norm_weight, key_heads, ext_out, eps,
+                         scale, deltas):
+    """The kept-update-vector verify of bf16 rows and 1 <= T <= 8 tokens as one library call
+    (``gdn_verify_layer_deltas``): the conv step, then the tensor-core block verify as its
+    programmatic dependent, with the gated norm (in the block's drain for few states)."""
+    B, T, C = qkv.shape
+    kd = key_heads * HEAD_DIM
+    HV = (C - 2 * kd) // HEAD_DIM
+    taps = conv_state.shape[-1]
+    w = conv_weight.reshape(C, -1)
+    if qkv.stride(-1) != 1:
+        qkv = qkv.contiguous()
+    if conv_state.shape != (B, C, taps) or conv_state.dtype != torch.bfloat16 or not conv_state.is_contiguous():
+        raise ValueError(f"conv_state: expected a contiguous bfloat16 tensor of shape {(B, C, taps)}, got "
+                         f"{conv_state.dtype} {tuple(conv_state.shape)}")
+    if w.dtype != torch.bfloat16:
+        raise ValueError(f"conv_weight: expected bfloat16, got {w.dtype}")
+    w = w.contiguous()
+    ext = torch.empty(B, C, taps + T, dtype=torch.bfloat16, device=qkv.device) if ext_out is None else ext_out
+    if ext.shape != (B, C, taps + T) or ext.dtype != torch.bfloat16 or not ext.is_contiguous():
+        raise ValueError(f"ext_out: expected a contiguous bfloat16 tensor of shape {(B, C, taps + T)}, got {ext.dtype} "
+                         f"{tuple(ext.shape)}")
+    if state.dtype != torch.float32 or not state.is_contiguous() or state.shape != (B, HV, HEAD_DIM, HEAD_DIM):
+        raise ValueError(f"state: expected a contiguous float32 tensor of shape {(B, HV, HEAD_DIM, HEAD_DIM)}, got "
+                         f"{state.dtype} {tuple(state.shape)}")
+    shape = (B, T, HV, HEAD_DIM)
+    if deltas.shape != shape or deltas.dtype != torch.float32 or not deltas.is_contiguous():
+        raise ValueError(f"deltas: expected a contiguous float32 tensor of shape {shape}, got {deltas.dtype} "
+                         f"{tuple(deltas.shape)}")
+    if g.shape != (B, T, HV) or beta.shape != (B, T, HV):
+        raise ValueError(f"g, beta: expected {(B, T, HV)}, got {tuple(g.shape)} and {tuple(beta.shape)}")
+    g = g.to(torch.float32).contiguous()
+    if beta.dtype not in (torch.bfloat16, torch.float32):
+        beta = beta.to(torch.float32)
+    beta = beta.contiguous()
+    z = z.reshape(shape)
+    if z.dtype != torch.bfloat16:
+        raise ValueError(f"z: expected bfloat16, got {z.dtype}")
+    z = z.contiguous()
+    nw = norm_weight.reshape(HEAD_DIM).to(torch.bfloat16).contiguous()
+    q = torch.empty(shape, dtype=torch.bfloat16, device=qkv.device)
+    k = torch.empty_like(q)
+    v = torch.empty_like(q)
+    y = torch.empty_like(q)
+    status = _lib.load().gdn_verify_layer_deltas(
+        qkv.data_ptr(), qkv.stride(0), qkv.stride(1), conv_state.data_ptr(), w.data_ptr(), ext.data_ptr(),
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr(), beta.data_ptr(), _DTYPES[beta.dtype],
+        state.data_ptr(), z.data_ptr(), nw.data_ptr(), y.data_ptr(), deltas.data_ptr(), B, T, key_heads, HV,
+        HEAD_DIM, HEAD_DIM, taps, w.shape[1], float(HEAD_DIM ** -0.5 if scale is None else scale), float(eps),
+        _stream())
+    _lib.check(status, what)
+    return y, (k, v, g, beta, None, deltas)
 
 
 def verify_layer_commit(pending, state, accepted, ext=None, conv_state=None) -> None:
@@ -147,6 +198,25 @@ def verify_layer_commit(pending, state, accepted, ext=None, conv_state=None) -> 
         gated_delta_rule_advance_inplace(k, v, g, beta, state, accepted)
     if ext is not None:
         conv_state_commit(ext, conv_state, accepted)
+
+
+def verify_layers_commit(pendings, states, accepted, ext=None, conv_states=None) -> None:
+    """``verify_layer_commit`` for every layer of a verify step (the engine's commit loop,
+    ``inference/engine.py:471-474``): the layers whose verify kept update vectors are committed by
+    one launch (``gated_delta_rule_delta_commit_layers``), the others one by one; with ``ext`` and
+    ``conv_states`` (stacked ``[layers, B, C, ..]``) the conv states follow in one more launch."""
+    pendings, states = list(pendings), list(states)
+    if len(pendings) != len(states):
+        raise ValueError(f"verify_layers_commit: {len(pendings)} pending verifies for {len(states)} states")
+    kept = [i for i, p in enumerate(pendings) if p[5] is not None and p[4] is None]
+    if kept:
+        gated_delta_rule_delta_commit_layers([pendings[i][0] for i in kept], [pendings[i][2] for i in kept],
+                                             [pendings[i][5] for i in kept], [states[i] for i in kept], accepted)
+    for i, p in enumerate(pendings):
+        if i not in kept:
+            verify_layer_commit(p, states[i], accepted)
+    if ext is not None:
+        conv_state_commit(ext, conv_states, accepted)
 
 
 def in_proj_conv(x, weight, conv_weight, conv_channels: int, cu_seqlens=None, conv_state: bool = False,

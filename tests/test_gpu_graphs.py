@@ -27,6 +27,8 @@ def _inputs(seed):
              vq=vq, vk=vk, vv=vv, vg=vg, vb=vb, vs=torch.randn(3, HV, 128, 128, generator=gen) * 0.02,
              acc=torch.tensor([1, 4, 2]),
              vz=torch.randn(3, 4, HV, 128, generator=gen).to(torch.bfloat16),
+             vqkv=(torch.randn(3, 4, C, generator=gen) * 2).to(torch.bfloat16),
+             vcs=torch.randn(2, 3, C, 3, generator=gen).to(torch.bfloat16),
              qkv=(torch.randn(1, T, C, generator=gen) * 2).to(torch.bfloat16),
              w=(torch.randn(C, 4, generator=gen) * 0.5).to(torch.bfloat16),
              z=torch.randn(T * HV, 128, generator=gen).to(torch.bfloat16),
@@ -63,6 +65,17 @@ def _step(x, cu):
                                                           x["vz"], x["nw"])
     sc = x["vs"].clone()
     gdn.gated_delta_rule_delta_commit(x["vk"], x["vg"], db, sc, x["acc"])
+    # the verify layer as one call (conv step, then the block verify as its programmatic dependent
+    # with the gated norm) for two layers, then both layers' commits in one launch and the conv states'
+    C = x["w"].shape[0]
+    ext = torch.empty(2, 3, C, 3 + 4, dtype=torch.bfloat16, device="cuda")
+    layer_states, pending, ys = [x["vs"].clone(), sc.clone()], [], []
+    for l in range(2):
+        yl, pl = gdn.verify_layer_step(x["vqkv"], x["vcs"][l], x["w"], x["vg"], x["vb"], layer_states[l], x["vz"],
+                                       x["nw"], H, ext_out=ext[l], deltas=torch.empty(3, 4, HV, 128, device="cuda"))
+        ys.append(yl)
+        pending.append(pl)
+    gdn.verify_layers_commit(pending, layer_states, x["acc"], ext=ext, conv_states=x["vcs"])
     gdn.gated_delta_rule_rollback(x["vs"], snaps, x["acc"])
     # the gates inside the prefill and the gated norm fused into the call
     og, hg = gdn.gated_delta_rule_chunk_gates(x["q"], x["k"], x["v"], x["graw"][..., :HV], x["graw"][..., HV:],
@@ -76,7 +89,8 @@ def _step(x, cu):
     qm, km, vm = (x["cm"][..., i * D3:(i + 1) * D3].view(2, 2, HV, 128) for i in range(3))
     qr = gdn.rotate_into_cache(x["ck"], x["ck"], qm, km, vm, x["rcos"][:, :2], x["rsin"][:, :2], x["rcos"][:, 1:],
                                x["rsin"][:, 1:], x["kcache"], x["vcache"], x["rows"], x["positions"], 40)
-    return y, beta_g, g_g, o, ht, out, od, ov, ob, db, yb, sc, og, hg, on, hn, oa, orot, qr
+    return (y, beta_g, g_g, o, ht, out, od, ov, ob, db, yb, sc, *ys, *layer_states, ext, og, hg, on, hn, oa, orot,
+            qr)
 
 
 def test_captured_layer_step_replays_equal_to_eager():
@@ -101,5 +115,6 @@ def test_captured_layer_step_replays_equal_to_eager():
         for a, b in zip(outs, eager):
             assert same_bits(a, b)
         assert same_bits(static["ds"], fresh["ds"]) and same_bits(static["vs"], fresh["vs"])
+        assert same_bits(static["vcs"], fresh["vcs"])
         assert same_bits(static["kcache"], fresh["kcache"]) and same_bits(static["vcache"], fresh["vcache"])
     del graph

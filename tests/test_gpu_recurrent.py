@@ -320,6 +320,26 @@ def test_delta_commit_checks_its_arguments():
         gdn.gated_delta_rule_delta_commit(k, g, deltas, h0.clone(), acc.float())
 
 
+@pytest.mark.parametrize("L,B", [(3, 5), (70, 1)])
+def test_delta_commit_layers_equals_the_one_layer_commits(L, B):
+    """The commit of many layers in one launch (70 layers: two launches of at most 64) leaves every
+    layer's state as the one-layer commit does, bit for bit; overlapping states are refused."""
+    T, H, HV = 5, 2, 4
+    ks, gs, ds, states, want = [], [], [], [], []
+    accepted = torch.tensor([(0, 1, 3, 5, 9)[i % 5] for i in range(B)], device="cuda")
+    for l in range(L):
+        q, k, v, g, beta, h0 = cuda(*gdn_inputs(700 + l, B, T, H, HV, normalise=False))
+        _, deltas = gdn.gated_delta_rule_verify_deltas(q, k, v, g, beta, h0)
+        one = h0.clone()
+        gdn.gated_delta_rule_delta_commit(k, g, deltas, one, accepted)
+        ks.append(k); gs.append(g); ds.append(deltas); states.append(h0); want.append(one)
+    gdn.gated_delta_rule_delta_commit_layers(ks, gs, ds, states, accepted)
+    for st, one in zip(states, want):
+        assert same_bits(st, one)
+    with pytest.raises(ValueError):
+        gdn.gated_delta_rule_delta_commit_layers(ks[:2], gs[:2], ds[:2], [states[0], states[0]], accepted)
+
+
 @pytest.mark.parametrize("T,B", [(1, 6), (5, 37), (8, 64)])
 def test_block_verify_with_fused_gated_norm_equals_the_two_calls(T, B):
     """The gated norm in the block verify's drain gives the standalone norm of the block's outputs

@@ -81,6 +81,55 @@ def test_commit_designs_agree():
     assert rel(results[2], results[0]) < 2e-6 and maxabs(ys[2], ys[0]) < 2e-2
 
 
+@pytest.mark.parametrize("B,T,taps,qkv_pad", [(16, 5, 3, 0), (72, 5, 3, 0), (5, 8, 4, 0), (3, 1, 3, 0), (4, 5, 3, 1)])
+def test_verify_layer_one_call_equals_the_separate_calls(B, T, taps, qkv_pad):
+    """The kept-update-vector verify layer as one library call (the conv step with the block verify
+    as its programmatic dependent; the gated norm in the block's drain below 2,048 states, after it
+    from there: B = 72 with 32 value heads) gives the conv step followed by the block verify and the
+    standalone norm bit for bit. qkv_pad = 1 gives the rows an odd stride, so the conv runs its
+    per-channel form, which does not release the block early."""
+    H, HV = 16, 32
+    qkv, cs, w, g, beta, state, z, nw, _ = verify_inputs(800 + B + T, B, T, H, HV, taps)
+    C = qkv.shape[-1]
+    padded = torch.zeros(B, T, C + qkv_pad, dtype=torch.bfloat16)
+    padded[..., :C] = qkv
+    d = dict(qkv=padded.cuda()[..., :C], cs=cs.cuda(), w=w.cuda(), g=g.cuda(), beta=beta.cuda(), state=state.cuda(),
+             z=z.cuda(), nw=nw.cuda())
+    ext_ref, q, k, v = gdn.conv_step(d["cs"], d["qkv"], d["w"], H * 128, HV * 128, 128, 128)
+    o, d_ref = gdn.gated_delta_rule_verify_deltas(q, k, v, d["g"], d["beta"], d["state"])
+    y_ref = gdn.gated_rms_norm(o.view(-1, 128), d["z"].view(-1, 128), d["nw"]).view(o.shape)
+    ext = torch.empty_like(ext_ref)
+    deltas = torch.empty(B, T, HV, 128, device="cuda")
+    y, pending = gdn.verify_layer_step(d["qkv"], d["cs"], d["w"], d["g"], d["beta"], d["state"], d["z"], d["nw"], H,
+                                       ext_out=ext, deltas=deltas)
+    assert same_bits(ext, ext_ref) and same_bits(y, y_ref) and same_bits(deltas, d_ref)
+    assert same_bits(pending[0], k) and same_bits(pending[1], v) and pending[5] is deltas
+    assert same_bits(d["state"], state)  # read, not written
+
+
+def test_verify_layers_commit_equals_the_layer_commits():
+    """One launch committing every layer's kept update vectors leaves each state as the one-layer
+    commit does, bit for bit; layers of other designs in the same list are committed one by one."""
+    B, T, H, HV, taps, L = 6, 5, 2, 4, 3, 3
+    accepted = torch.tensor([1, 2, 3, 4, 5, 0]).cuda()
+    pendings, states, want = [], [], []
+    for l in range(L):
+        qkv, cs, w, g, beta, state, z, nw, _ = verify_inputs(900 + l, B, T, H, HV, taps)
+        extra = {"snapshots": torch.empty(B, T, HV, 128, 128, device="cuda")} if l == 1 else \
+            {"deltas": torch.empty(B, T, HV, 128, device="cuda")}
+        st = state.cuda()
+        _, p = gdn.verify_layer_step(qkv.cuda(), cs.cuda(), w.cuda(), g.cuda(), beta.cuda(), st, z.cuda(), nw.cuda(),
+                                     H, **extra)
+        one = st.clone()
+        gdn.verify_layer_commit(p, one, accepted)
+        pendings.append(p)
+        states.append(st)
+        want.append(one)
+    gdn.verify_layers_commit(pendings, states, accepted)
+    for st, one in zip(states, want):
+        assert same_bits(st, one)
+
+
 def test_conv_state_commit_over_stacked_layers_matches_gather():
     """One launch over the engine's stacked [layers, max_rows, C, taps] conv states, on the
     leading B rows (strided slices), equals torch.gather of the ext windows."""
