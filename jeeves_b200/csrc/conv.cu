@@ -456,10 +456,57 @@ __global__ void conv_state_commit_kernel(const bf16* __restrict__ ext, bf16* __r
     for (int i = 0; i < taps; ++i) dst[i] = src[i];
 }
 
+// The same for the engine's shape, taps + T = 8 values a channel (one 16-byte vector): one thread
+// per (layer, row, channel) reads its channel's vector (a warp reads 512 contiguous bytes), takes
+// the taps values at j (two 64-bit halves, a shift by a run-time multiple of 16 bits) into shared
+// memory, and the CTA's 128 channels' taps x 2 bytes go out as contiguous 16-byte stores.
+template <int TAPS>
+__global__ void __launch_bounds__(128) conv_state_commit_vec_kernel(const bf16* __restrict__ ext,
+                                                                    bf16* __restrict__ state,
+                                                                    const int64_t* __restrict__ accepted, int64_t C,
+                                                                    int64_t T, int64_t esl, int64_t esb, int64_t ssl,
+                                                                    int64_t ssb) {
+    constexpr int L = 8, CH = 128;
+    __shared__ alignas(16) uint16_t out[CH * TAPS];
+    const int64_t c0 = (int64_t)blockIdx.x * CH;
+    const int64_t b = blockIdx.y, l = blockIdx.z;
+    const int n = (int)(C - c0 < CH ? C - c0 : CH);  // channels of this CTA, a multiple of 8
+    int64_t j = accepted[b];
+    j = j < 0 ? 0 : (j > T ? T : j);
+    if ((int)threadIdx.x < n) {
+        const uint4 v = reinterpret_cast<const uint4*>(ext + l * esl + b * esb + c0 * L)[threadIdx.x];
+        const uint64_t lo = ((uint64_t)v.y << 32) | v.x, hi = ((uint64_t)v.w << 32) | v.z;
+#pragma unroll
+        for (int i = 0; i < TAPS; ++i) {
+            const int k = (int)j + i;  // < L: j <= T = L - TAPS
+            out[threadIdx.x * TAPS + i] = (uint16_t)(k < 4 ? lo >> (16 * k) : hi >> (16 * (k - 4)));
+        }
+    }
+    __syncthreads();
+    const int vecs = n * TAPS / 8;  // 16-byte vectors of the CTA's outputs
+    uint4* dst = reinterpret_cast<uint4*>(state + l * ssl + b * ssb + c0 * TAPS);
+    for (int i = threadIdx.x; i < vecs; i += CH) dst[i] = reinterpret_cast<const uint4*>(out)[i];
+}
+
 int launch_conv_state_commit(const void* ext, void* state, const int64_t* accepted, int64_t layers, int64_t B,
                              int64_t C, int taps, int64_t T, int64_t esl, int64_t esb, int64_t ssl, int64_t ssb,
                              cudaStream_t s) {
     if (layers == 0 || B == 0 || C == 0) return GDN_OK;
+    const bool vec = taps + T == 8 && (taps == 3 || taps == 4) && C % 8 == 0 && aligned16(ext) && aligned16(state) &&
+                     (esl * 2) % 16 == 0 && (esb * 2) % 16 == 0 && (ssl * 2) % 16 == 0 && (ssb * 2) % 16 == 0;
+    if (vec) {
+        constexpr int threads = 128;
+        dim3 grid((unsigned)((C + threads - 1) / threads), (unsigned)B, (unsigned)layers);
+        if (taps == 3)
+            conv_state_commit_vec_kernel<3><<<grid, threads, 0, s>>>(static_cast<const bf16*>(ext),
+                                                                     static_cast<bf16*>(state), accepted, C, T, esl,
+                                                                     esb, ssl, ssb);
+        else
+            conv_state_commit_vec_kernel<4><<<grid, threads, 0, s>>>(static_cast<const bf16*>(ext),
+                                                                     static_cast<bf16*>(state), accepted, C, T, esl,
+                                                                     esb, ssl, ssb);
+        return launch_status();
+    }
     constexpr int threads = 256;
     dim3 grid((unsigned)((C + threads - 1) / threads), (unsigned)B, (unsigned)layers);
     conv_state_commit_kernel<<<grid, threads, 0, s>>>(static_cast<const bf16*>(ext), static_cast<bf16*>(state),

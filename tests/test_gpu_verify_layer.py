@@ -146,6 +146,23 @@ def test_conv_state_commit_over_stacked_layers_matches_gather():
     assert same_bits(states[:, B:], before[:, B:])  # rows past B untouched
 
 
+@pytest.mark.parametrize("taps,T", [(3, 5), (4, 4)])
+def test_conv_state_commit_16_byte_form_matches_gather(taps, T):
+    """The engine's shape (taps + T = 8 values a channel, one 16-byte vector): every clamped
+    acceptance, over strided layer and row slices of the stacked states, equals torch.gather."""
+    layers, R, B, C = 3, 9, 7, 8192
+    gen = torch.Generator().manual_seed(12 + taps)
+    ext = torch.randn(layers, R, C, taps + T, generator=gen).to(torch.bfloat16).cuda()
+    states = torch.randn(layers + 1, R, C, taps, generator=gen).to(torch.bfloat16).cuda()
+    accepted = torch.tensor([-2, 0, 1, 2, 3, T, T + 7])
+    before = states.clone()
+    gdn.conv_state_commit(ext[:, :B], states[1:, :B], accepted.cuda())
+    cols = (accepted.clamp(0, T)[:, None] + torch.arange(taps)[None])[None, :, None, :].expand(layers, B, C, taps)
+    want = torch.gather(ext[:, :B].cpu(), 3, cols)
+    assert same_bits(states[1:, :B], want)
+    assert same_bits(states[0], before[0]) and same_bits(states[1:, B:], before[1:, B:])
+
+
 def test_conv_state_commit_rejects_mismatched_shapes():
     ext = torch.zeros(2, 64, 7, dtype=torch.bfloat16, device="cuda")
     st = torch.zeros(2, 64, 3, dtype=torch.bfloat16, device="cuda")
