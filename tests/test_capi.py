@@ -69,6 +69,46 @@ def test_argument_checks_run_before_any_launch():
     assert lib.gdn_snapshot_commit(16, 16, None, 2, 5, 4, 128, 128, None) == _lib.ERR_NULL
 
 
+def _verify_layer(lib, **over):
+    a = dict(qkv=16, sb=8192 * 5, st=8192, cs=16, cw=16, ext=16, q=16, k=16, v=16, g=16, beta=16, bd=_lib.BF16,
+             state=16, z=16, nw=16, y=16, deltas=16, B=2, T=5, H=16, HV=32, Dk=128, Dv=128, taps=3, K=4)
+    a.update(over)
+    return lib.gdn_verify_layer_deltas(a["qkv"], a["sb"], a["st"], a["cs"], a["cw"], a["ext"], a["q"], a["k"], a["v"],
+                                       a["g"], a["beta"], a["bd"], a["state"], a["z"], a["nw"], a["y"], a["deltas"],
+                                       a["B"], a["T"], a["H"], a["HV"], a["Dk"], a["Dv"], a["taps"], a["K"], 0.0884,
+                                       1e-6, None)
+
+
+def test_verify_layer_call_checks_its_arguments_before_any_launch():
+    lib = _lib.load()
+    assert _verify_layer(lib, bd=9) == _lib.ERR_DTYPE
+    assert _verify_layer(lib, HV=24, H=16) == _lib.ERR_SHAPE
+    assert _verify_layer(lib, taps=3, K=5) == _lib.ERR_SHAPE
+    assert _verify_layer(lib, Dv=64) == _lib.ERR_UNSUPPORTED
+    assert _verify_layer(lib, T=9) == _lib.ERR_UNSUPPORTED  # the tensor-core block takes up to 8 tokens
+    assert _verify_layer(lib, state=None) == _lib.ERR_NULL
+    assert _verify_layer(lib, deltas=24) == _lib.ERR_ALIGN
+    assert _verify_layer(lib, B=0) == _lib.OK and _verify_layer(lib, T=0) == _lib.OK  # nothing to launch
+
+
+def test_layer_commit_checks_its_arguments_before_any_launch():
+    lib = _lib.load()
+    arr = ctypes.c_void_p * 2
+    state_bytes = 2 * 32 * 128 * 128 * 4
+
+    def commit(states, layers=2, B=2, **over):
+        a = dict(kd=_lib.BF16, H=16, HV=32, Dk=128)
+        a.update(over)
+        return lib.gdn_delta_commit_layers(arr(*states), arr(16, 16), a["kd"], arr(16, 16), arr(16, 16), layers, 16, B,
+                                           5, a["H"], a["HV"], a["Dk"], 128, 5 * 16 * 128, 16 * 128, 128, None)
+    assert commit([16, 16 + state_bytes], kd=9) == _lib.ERR_DTYPE
+    assert commit([16, 16 + state_bytes], Dk=64) == _lib.ERR_UNSUPPORTED
+    assert commit([16, None]) == _lib.ERR_NULL
+    assert commit([16, 16 + state_bytes - 16]) == _lib.ERR_SHAPE  # the two layers' states overlap
+    assert commit([16, 24 + state_bytes]) == _lib.ERR_ALIGN
+    assert commit([16, 16], layers=0) == _lib.OK and commit([16, 16], B=0) == _lib.OK
+
+
 def test_status_mapping_to_exceptions():
     with pytest.raises(ValueError):
         _lib.check(_lib.ERR_SHAPE, "x")
