@@ -165,13 +165,35 @@ int launch_conv1d_silu(const void* x, int64_t sxb, int64_t sxt, const void* w, v
     return launch_status();
 }
 
+// Launches `kernel` on `s`; with `dependent` as a programmatic dependent of the previous kernel in
+// the stream (the kernels launched so wait for it before their first memory access).
+template <typename... Params, typename... Args>
+static int launch_conv_kernel(void (*kernel)(Params...), dim3 grid, int threads, bool dependent, cudaStream_t s,
+                              Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(threads);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = dependent ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<Params>(args)...) == cudaSuccess ? launch_status()
+                                                                                        : GDN_ERR_LAUNCH;
+}
+
 // Decode step: y = silu(bf16(sum_i bf16(w_i * window_i))); the state keeps the last `taps`
 // inputs. One thread owns 8 consecutive channels, so every access is a 16-byte vector: the
 // channels' conv states are 8 * taps contiguous bf16 values, and x, y are 8 contiguous bf16.
 template <int TAPS, int K>
 __global__ void conv1d_silu_step_kernel(const bf16* __restrict__ x, int64_t sxb, bf16* __restrict__ state,
                                         const bf16* __restrict__ w, bf16* __restrict__ y, int64_t B, int64_t C) {
-    pdl_launch_dependents();  // the decode layer's recurrent step may start loading its state
+    // Launched as a programmatic dependent of the previous layer's last kernel: wait for it before
+    // any memory access, and only then let the recurrent step start loading its state (so that no
+    // kernel before this one can still be writing that state).
+    pdl_wait();
+    pdl_launch_dependents();
     const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // group of 8 channels
     const int64_t groups = C / 8;
     if (idx >= B * groups) return;
@@ -216,21 +238,24 @@ __global__ void conv1d_silu_step_kernel(const bf16* __restrict__ x, int64_t sxb,
 
 template <int TAPS>
 static int conv_step_taps(const bf16* x, int64_t sxb, bf16* st, const bf16* w, bf16* y, int64_t B, int64_t C, int K,
-                          unsigned blocks, int threads, cudaStream_t s) {
+                          unsigned blocks, int threads, cudaStream_t s, bool dependent) {
     switch (K) {
-        case 2: conv1d_silu_step_kernel<TAPS, 2><<<blocks, threads, 0, s>>>(x, sxb, st, w, y, B, C); break;
-        case 3: conv1d_silu_step_kernel<TAPS, 3><<<blocks, threads, 0, s>>>(x, sxb, st, w, y, B, C); break;
+        case 2:
+            return launch_conv_kernel(conv1d_silu_step_kernel<TAPS, 2>, blocks, threads, dependent, s, x, sxb, st, w, y,
+                                      B, C);
+        case 3:
+            return launch_conv_kernel(conv1d_silu_step_kernel<TAPS, 3>, blocks, threads, dependent, s, x, sxb, st, w, y,
+                                      B, C);
         case 4:
-            if (TAPS >= 3) conv1d_silu_step_kernel<TAPS, (TAPS >= 3 ? 4 : 3)><<<blocks, threads, 0, s>>>(x, sxb, st, w, y, B, C);
-            else return GDN_ERR_SHAPE;
-            break;
+            if (TAPS < 3) return GDN_ERR_SHAPE;
+            return launch_conv_kernel(conv1d_silu_step_kernel<TAPS, (TAPS >= 3 ? 4 : 3)>, blocks, threads, dependent, s,
+                                      x, sxb, st, w, y, B, C);
         default: return GDN_ERR_UNSUPPORTED;
     }
-    return launch_status();
 }
 
 int launch_conv1d_silu_step(const void* x, int64_t sxb, void* state, const void* w, void* y, int64_t B, int64_t C,
-                            int taps, int K, cudaStream_t s) {
+                            int taps, int K, cudaStream_t s, bool dependent) {
     if (B * C == 0) return GDN_OK;
     if (C % 8 || K > taps + 1 || K < 2) return GDN_ERR_SHAPE;
     constexpr int threads = 256;
@@ -240,9 +265,9 @@ int launch_conv1d_silu_step(const void* x, int64_t sxb, void* state, const void*
     auto wp = static_cast<const bf16*>(w);
     auto yp = static_cast<bf16*>(y);
     switch (taps) {
-        case 2: return conv_step_taps<2>(xp, sxb, sp, wp, yp, B, C, K, blocks, threads, s);
-        case 3: return conv_step_taps<3>(xp, sxb, sp, wp, yp, B, C, K, blocks, threads, s);
-        case 4: return conv_step_taps<4>(xp, sxb, sp, wp, yp, B, C, K, blocks, threads, s);
+        case 2: return conv_step_taps<2>(xp, sxb, sp, wp, yp, B, C, K, blocks, threads, s, dependent);
+        case 3: return conv_step_taps<3>(xp, sxb, sp, wp, yp, B, C, K, blocks, threads, s, dependent);
+        case 4: return conv_step_taps<4>(xp, sxb, sp, wp, yp, B, C, K, blocks, threads, s, dependent);
         default: return GDN_ERR_UNSUPPORTED;
     }
 }
@@ -297,7 +322,10 @@ __global__ void conv_step_vec_kernel(const bf16* __restrict__ state, const bf16*
                                      int64_t C, int64_t key_dim, int64_t value_dim, int dk, int rep) {
     constexpr int K = 4, L = TAPS + T;
     static_assert(TAPS >= K - 1 && TAPS <= 8, "the window covers every tap");
-    // a verify that follows as a programmatic dependent may set up and load its states meanwhile
+    // When launched as a programmatic dependent, wait for the previous kernel before any memory
+    // access; then a block verify that follows as this kernel's dependent may set up and load its
+    // states (which no kernel before this one can still be writing).
+    pdl_wait();
     pdl_launch_dependents();
     const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int64_t groups = C / 8;
@@ -383,32 +411,33 @@ __global__ void conv_step_vec_kernel(const bf16* __restrict__ state, const bf16*
 }
 
 template <int TAPS, int T>
-static void conv_step_vec(const bf16* state, const bf16* qkv, int64_t sqb, int64_t sqt, const bf16* w, bf16* ext,
-                          bf16* q, bf16* k, bf16* v, int64_t B, int64_t C, int64_t key_dim, int64_t value_dim, int dk,
-                          int rep, cudaStream_t s) {
+static int conv_step_vec(const bf16* state, const bf16* qkv, int64_t sqb, int64_t sqt, const bf16* w, bf16* ext,
+                         bf16* q, bf16* k, bf16* v, int64_t B, int64_t C, int64_t key_dim, int64_t value_dim, int dk,
+                         int rep, cudaStream_t s, bool dependent) {
     constexpr int threads = 128;
     const unsigned blocks = (unsigned)((B * (C / 8) + threads - 1) / threads);
-    conv_step_vec_kernel<TAPS, T><<<blocks, threads, 0, s>>>(state, qkv, sqb, sqt, w, ext, q, k, v, B, C, key_dim,
-                                                             value_dim, dk, rep);
+    return launch_conv_kernel(conv_step_vec_kernel<TAPS, T>, blocks, threads, dependent, s, state, qkv, sqb, sqt, w,
+                              ext, q, k, v, B, C, key_dim, value_dim, dk, rep);
 }
 
 template <int TAPS>
-static bool conv_step_vec_t(int64_t T, const bf16* sp, const bf16* xp, int64_t sqb, int64_t sqt, const bf16* wp,
-                            bf16* ep, bf16* qp, bf16* kp, bf16* vp, int64_t B, int64_t C, int64_t key_dim,
-                            int64_t value_dim, int dk, int rep, cudaStream_t s) {
+static int conv_step_vec_t(int64_t T, const bf16* sp, const bf16* xp, int64_t sqb, int64_t sqt, const bf16* wp,
+                           bf16* ep, bf16* qp, bf16* kp, bf16* vp, int64_t B, int64_t C, int64_t key_dim,
+                           int64_t value_dim, int dk, int rep, cudaStream_t s, bool dependent) {
     switch (T) {
 #define GDN_CONV_STEP_T(n) \
-    case n: conv_step_vec<TAPS, n>(sp, xp, sqb, sqt, wp, ep, qp, kp, vp, B, C, key_dim, value_dim, dk, rep, s); return true;
+    case n: return conv_step_vec<TAPS, n>(sp, xp, sqb, sqt, wp, ep, qp, kp, vp, B, C, key_dim, value_dim, dk, rep, s, \
+                                          dependent);
         GDN_CONV_STEP_T(1) GDN_CONV_STEP_T(2) GDN_CONV_STEP_T(3) GDN_CONV_STEP_T(4)
         GDN_CONV_STEP_T(5) GDN_CONV_STEP_T(6) GDN_CONV_STEP_T(7) GDN_CONV_STEP_T(8)
 #undef GDN_CONV_STEP_T
-        default: return false;
+        default: return GDN_ERR_UNSUPPORTED;
     }
 }
 
 int launch_conv_step(const void* state, const void* qkv, int64_t sqb, int64_t sqt, const void* w, void* ext, void* q,
                      void* k, void* v, int64_t B, int64_t T, int taps, int K, int64_t key_dim, int64_t value_dim, int dk,
-                     int dv, cudaStream_t s) {
+                     int dv, cudaStream_t s, bool dependent) {
     const int64_t C = 2 * key_dim + value_dim;
     if (B == 0 || C == 0) return GDN_OK;
     const int rep = (int)((value_dim / dv) / (key_dim / dk));
@@ -426,9 +455,11 @@ int launch_conv_step(const void* state, const void* qkv, int64_t sqb, int64_t sq
                      aligned16(state) && aligned16(qkv) && aligned16(w) && aligned16(ext) && aligned16(q) &&
                      aligned16(k) && aligned16(v);
     if (vec) {
-        if (taps == 3) conv_step_vec_t<3>(T, sp, xp, sqb, sqt, wp, ep, qp, kp, vp, B, C, key_dim, value_dim, dk, rep, s);
-        else conv_step_vec_t<4>(T, sp, xp, sqb, sqt, wp, ep, qp, kp, vp, B, C, key_dim, value_dim, dk, rep, s);
-        return launch_status();
+        if (taps == 3)
+            return conv_step_vec_t<3>(T, sp, xp, sqb, sqt, wp, ep, qp, kp, vp, B, C, key_dim, value_dim, dk, rep, s,
+                                      dependent);
+        return conv_step_vec_t<4>(T, sp, xp, sqb, sqt, wp, ep, qp, kp, vp, B, C, key_dim, value_dim, dk, rep, s,
+                                  dependent);
     }
     constexpr int threads = 128;
     dim3 grid((unsigned)((C + threads - 1) / threads), (unsigned)B);

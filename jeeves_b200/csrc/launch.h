@@ -169,11 +169,13 @@ int launch_decode_layer(const DecodeLayerArgs& a, cudaStream_t s);
 
 int launch_conv1d_silu(const void* x, int64_t sxb, int64_t sxt, const void* w, void* y, const int32_t* cu, int64_t B,
                        int64_t T, int64_t C, int K, cudaStream_t s);
+// dependent: launched as a programmatic dependent of the previous kernel in the stream (the kernel
+// waits for it before its first memory access).
 int launch_conv1d_silu_step(const void* x, int64_t sxb, void* state, const void* w, void* y, int64_t B, int64_t C,
-                            int taps, int K, cudaStream_t s);
+                            int taps, int K, cudaStream_t s, bool dependent = false);
 int launch_conv_step(const void* state, const void* qkv, int64_t sqb, int64_t sqt, const void* w, void* ext, void* q,
                      void* k, void* v, int64_t B, int64_t T, int taps, int K, int64_t key_dim, int64_t value_dim, int dk,
-                     int dv, cudaStream_t s);
+                     int dv, cudaStream_t s, bool dependent = false);
 int launch_conv_state_commit(const void* ext, void* state, const int64_t* accepted, int64_t layers, int64_t B,
                              int64_t C, int taps, int64_t T, int64_t esl, int64_t esb, int64_t ssl, int64_t ssb,
                              cudaStream_t s);

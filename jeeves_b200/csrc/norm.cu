@@ -27,6 +27,7 @@ __global__ void gated_rmsnorm_kernel(const bf16* x, const bf16* __restrict__ z, 
     }
     float ws[8];
     load8f(w + 8 * sub, ws);
+    pdl_launch_dependents();  // the next layer's conv, a dependent that waits for this kernel, may launch
     pdl_wait();  // x comes from the previous kernel when launched as its dependent
 #pragma unroll
     for (int k = 0; k < R; ++k) xr[k] = *reinterpret_cast<const uint4*>(x + off[k]);

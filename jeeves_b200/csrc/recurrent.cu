@@ -461,7 +461,10 @@ int launch_decode_layer(const DecodeLayerArgs& a, cudaStream_t s) {
     if (a.B == 0) return GDN_OK;
     const int64_t key_dim = (int64_t)a.H * kHeadDim;
     const int64_t C = 2 * key_dim + (int64_t)a.HV * kHeadDim;
-    int st = launch_conv1d_silu_step(a.qkv, a.qkv_sb, a.conv_state, a.conv_w, a.workspace, a.B, C, a.taps, a.K, s);
+    // the conv launches as a programmatic dependent of whatever ran before (it waits for it before
+    // touching memory), so that its launch overlaps the previous layer's last kernel
+    int st = launch_conv1d_silu_step(a.qkv, a.qkv_sb, a.conv_state, a.conv_w, a.workspace, a.B, C, a.taps, a.K, s,
+                                     true);
     if (st != GDN_OK) return st;
     const bf16* y = static_cast<const bf16*>(a.workspace);
     RecurrentArgs r{};
