@@ -698,9 +698,11 @@ def bench_verify(gdn, args, device, rank, world, rank_sync, reduce_max, hbm_peak
                        "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm_peak, "unit": "GB/s",
                                     "frac": round(ach / hbm_peak, 4), "algorithmic_bytes_per_unit": unit}}
     names = {"recompute": "recompute (the reference's: the commit advances the state by the accepted tokens)",
-             "deltas": "kept update vectors (the verify as one tensor-core block per state: one product of the "
-                       "state with the 10 k/q rows and their Gram, the 5-token recurrence unrolled per column, each "
-                       "token's delta kept; the commit applies the accepted ones in one streaming pass)"}
+             "deltas": "kept update vectors (per layer one library call: the conv step, then the verify as one "
+                       "tensor-core block per state as its programmatic dependent - one product of the state with the "
+                       "10 k/q rows and their Gram, the 5-token recurrence unrolled per column, each token's delta "
+                       "kept - and the gated norm; the commit applies the accepted ones to all 24 layers' states in "
+                       "one streaming launch)"}
     head = min(("recompute", "deltas"), key=lambda d: out[d]["ms_per_step"])
     other = "deltas" if head == "recompute" else "recompute"
     best = out[head]
