@@ -588,20 +588,26 @@ def bench_in_proj(gdn, args, device, rank_sync, reduce_max, world, tc_peak, T=40
 def bench_fp8(gdn, args, device, rank_sync, reduce_max, world, hbm_peak, tc_peak, K=4096, N=C_QKV):
     """The qkv projection with fp8 weights (the reference's FP8Linear: e4m3 codes, fp32 row
     scales; in fp8 the engine runs in_proj_qkv on its own, inference/engine.py:155-166): at a
-    decode batch (256 rows, bound by the codes' bytes) and at prefill (4096 tokens with the conv
-    in the epilogue, bound by the tensor pipe); beside them the same shapes with bf16 weights
-    through the library and through cuBLAS."""
+    decode batch (256 rows, and 32 rows, a GPU's share of 256 on 8 GPUs; bound by the weights'
+    bytes) and at prefill (4096 tokens with the conv in the epilogue, bound by the tensor pipe);
+    beside them the same shapes with bf16 weights through the library and through cuBLAS. Every
+    arm rotates over three weight sets (201 MB of bf16 weights, more than L2), as a decode step
+    reads each layer's weights once: no call finds its weights in L2."""
     gen = torch.Generator().manual_seed(8)
-    w = (torch.randn(N, K, generator=gen) * K ** -0.5).to(torch.bfloat16).to(device)
-    scale = (w.float().abs().amax(1).clamp(min=1e-12) / torch.finfo(torch.float8_e4m3fn).max).contiguous()
-    codes = (w.float() / scale[:, None]).to(torch.float8_e4m3fn).contiguous()
+    ws, scales, codes = [], [], []
+    for _ in range(3):
+        w = (torch.randn(N, K, generator=gen) * K ** -0.5).to(torch.bfloat16).to(device)
+        scale = (w.float().abs().amax(1).clamp(min=1e-12) / torch.finfo(torch.float8_e4m3fn).max).contiguous()
+        ws.append(w)
+        scales.append(scale)
+        codes.append((w.float() / scale[:, None]).to(torch.float8_e4m3fn).contiguous())
     cw = (torch.randn(N, 4, generator=gen) * 0.5).to(torch.bfloat16).to(device)
     res = {}
-    for name, M, conv in (("decode", 256, 0), ("prefill", 4096, N)):
+    for name, M, conv in (("decode", 256, 0), ("decode_32", 32, 0), ("prefill", 4096, N)):
         x = torch.randn(M, K, generator=gen).to(torch.bfloat16).to(device)
-        arms = {"fp8": lambda i: gdn.in_proj_conv(x, codes, cw, conv, weight_scale=scale),
-                "bf16": lambda i: gdn.in_proj_conv(x, w, cw, conv),
-                "cublas_bf16": lambda i: x @ w.T}
+        arms = {"fp8": lambda i: gdn.in_proj_conv(x, codes[i % 3], cw, conv, weight_scale=scales[i % 3]),
+                "bf16": lambda i: gdn.in_proj_conv(x, ws[i % 3], cw, conv),
+                "cublas_bf16": lambda i: x @ ws[i % 3].T}
         ms = {k: reduce_max(timed(f, args.steps, args.warmup, rank_sync)) / args.steps for k, f in arms.items()}
         entry = {k + "_ms": round(v, 4) for k, v in ms.items()}
         if conv == 0:
@@ -616,10 +622,11 @@ def bench_fp8(gdn, args, device, rank_sync, reduce_max, world, hbm_peak, tc_peak
         entry["rows"] = M
         entry["conv"] = bool(conv)
         res[name] = entry
-    return {"workload": f"qkv projection {K} -> {N} with fp8 (e4m3, per-row scale) weights; decode: 256 rows, no conv; "
-                        f"prefill: 4096 tokens with the causal conv + SiLU in the epilogue; one replica per GPU",
+    return {"workload": f"qkv projection {K} -> {N} with fp8 (e4m3, per-row scale) weights; decode: 256 and 32 rows, "
+                        f"no conv (K split over clusters of CTAs); prefill: 4096 tokens with the causal conv + SiLU in "
+                        f"the epilogue; three weight sets rotated (> L2); one replica per GPU",
             "value": round(world * 256 / (res["decode"]["fp8_ms"] / 1e3), 1), "unit": "rows/s (decode)",
-            **res, "gpu_launches": 6 * args.steps}  # per step of each arm: fp8 2 (row kernel, GEMM), bf16 1; two shapes
+            **res, "gpu_launches": 9 * args.steps}  # per step of each arm: fp8 2 (row kernel, GEMM), bf16 1; three shapes
 
 
 def verify_unit_bytes(design, T=5, taps=3):
@@ -982,6 +989,16 @@ def profile_case(name, device):
         x, w, cw = in_proj_case(device)
         for _ in range(2):
             gdn.in_proj_conv(x, w, cw, C_QKV)
+    elif name == "in_proj_decode":  # extra.fp8's decode shape: 256 rows, qkv 4096 -> 8192, bf16 then fp8 weights
+        gen = torch.Generator().manual_seed(8)
+        w = (torch.randn(C_QKV, 4096, generator=gen) * 4096 ** -0.5).to(torch.bfloat16).to(device)
+        scale = (w.float().abs().amax(1).clamp(min=1e-12) / torch.finfo(torch.float8_e4m3fn).max).contiguous()
+        codes = (w.float() / scale[:, None]).to(torch.float8_e4m3fn).contiguous()
+        cw = (torch.randn(C_QKV, 4, generator=gen) * 0.5).to(torch.bfloat16).to(device)
+        x = torch.randn(256, 4096, generator=gen).to(torch.bfloat16).to(device)
+        for _ in range(2):
+            gdn.in_proj_conv(x, w, cw, 0)
+            gdn.in_proj_conv(x, codes, cw, 0, weight_scale=scale)
     elif name in ("verify", "verify_layer"):  # the config-4 step of bench_verify (kept update vectors):
         # 24 layers, or one layer (B = 128 rows; 268 MB of state) for captures that replay kernels
         B, T, taps = 128, 5, 3
@@ -1015,7 +1032,8 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-extras", dest="extras", action="store_false")
     ap.add_argument("--no-cpu-baseline", dest="cpu", action="store_false")
-    ap.add_argument("--profile", choices=("prefill", "varlen", "decode", "verify", "verify_layer", "attention", "in_proj"),
+    ap.add_argument("--profile", choices=("prefill", "varlen", "decode", "verify", "verify_layer", "attention", "in_proj",
+                                           "in_proj_decode"),
                     help="run one workload twice, untimed, for an ncu capture")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)

@@ -64,6 +64,7 @@ constexpr int kChunk = 16;               // accumulator columns per TMEM load
 struct Params {
     CUtensorMap tm_w;  // 2-D (K, N), box (64, 128); fp8: the codes, uint8, no swizzle
     CUtensorMap tm_x;  // 2-D (K, T), box (64, bn)
+    CUtensorMap tm_out;  // split K with out_tma: 2-D (N, T) bf16 over out, box (32, 16)
     const bf16* conv_w;  // [C, 4]
     const int32_t* cu_seqlens;  // [nseq + 1] or null (one sequence of T tokens)
     bf16* out;           // [T, N], row stride ldo
@@ -74,6 +75,8 @@ struct Params {
     int halo;            // leading columns recomputed for the conv window: kHalo with a conv, else 0
     int tiles_t, tiles;  // token tiles, all tiles
     int stages;          // single-CTA kernel: pipeline stages (as many as fit, at most 8)
+    int ksplit;          // single-CTA kernel: CTAs of a cluster that split K (1: no split)
+    int out_tma;         // split K: the owners store their outputs with tm_out
     uint32_t stage_bytes;  // single-CTA kernel: W (16 KB) + X (bn x 128 B) [+ raw codes (8 KB)]
     // fp8 weights (the single-CTA kernel with FP8 = true): e4m3 codes [N, K] (row stride ldc
     // bytes) with one fp32 scale per row, and the activations as fp16 rows with a power-of-two
@@ -234,6 +237,115 @@ __device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t codes) {
     return r;
 }
 
+// ---- split K (decode-sized batches without conv channels): the ks CTAs of a cluster compute one
+// tile's partial products over consecutive K ranges, then sum them through distributed shared
+// memory. The tile's token columns, in chunks of 16 (nch = bn / 16 of them), are dealt out in
+// contiguous blocks to 2 ks workers: worker j = 2 x CTA + warp half (warps 4-7 are half 1) owns
+// chunks [ceil(j nch / 2ks), ceil((j + 1) nch / 2ks)), so that every warp of every CTA sends and
+// sums about the same share (warp w reads TMEM lane quadrant w % 4, i.e. 32 channels). A sender writes its partial of a chunk into a
+// 2 KB slot of the owner's freed stage memory (32 lanes x 16 columns fp32, four columns per lane
+// per 16-byte store, 512 contiguous bytes a warp store); the owner adds the ks partials in rank
+// order (the same bits whichever CTA owns the chunk), rounds to bf16 into a [16 tokens][32
+// channels] box and stores it with one TMA copy (or, when the output's layout does not allow a
+// tensor map, with 2-byte stores per channel).
+struct SplitLayout {
+    int nch, maxown;  // chunks of 16 columns in the tile; chunks a CTA owns at most
+    __device__ __forceinline__ SplitLayout(const Params& p)
+        : nch(p.bn >> 4), maxown((nch + p.ksplit - 1) / p.ksplit) {}
+    // first chunk of worker j = 2 x CTA + warp half (worker j covers [begin(j), begin(j + 1)))
+    __device__ __forceinline__ int begin(const Params& p, int j) const { return (j * nch + 2 * p.ksplit - 1) / (2 * p.ksplit); }
+    // slot of the owner's local chunk li of lane quadrant q from sender s, in the owner's memory
+    __device__ __forceinline__ uint32_t slot(const Params& p, int q, int li, int s) const {
+        return (uint32_t)(((q * maxown + li) * p.ksplit + s) * 2048);
+    }
+    __device__ __forceinline__ uint32_t box(const Params& p, int q, int li) const {
+        return (uint32_t)(4 * maxown * p.ksplit * 2048 + (q * maxown + li) * 1024);
+    }
+};
+
+__device__ __forceinline__ void split_send(const Params& p, uint8_t* sm, uint32_t tb, int w, int lane, int kr) {
+    const SplitLayout L(p);
+    const int q = w & 3, h = w >> 2;
+    const uint32_t acc = tb + ((uint32_t)(32 * q) << 16);
+    for (int o = 0; o < p.ksplit; ++o) {
+        if (o == kr) continue;
+        const int first = L.begin(p, 2 * o), u0 = L.begin(p, 2 * o + h), u1 = L.begin(p, 2 * o + h + 1);
+        const uint32_t dst = mapa_shared(sm + L.slot(p, q, u0 - first, kr), (uint32_t)o);
+        for (int u = u0; u < u1; ++u) {
+            float v[kChunk];
+            tmem_ld16_wait(acc + 16 * u, v);
+            const uint32_t d = dst + (uint32_t)((u - u0) * p.ksplit * 2048);
+#pragma unroll
+            for (int i = 0; i < kChunk / 4; ++i)
+                asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(d + (uint32_t)((i * 32 + lane) * 16)),
+                             "f"(v[4 * i]), "f"(v[4 * i + 1]), "f"(v[4 * i + 2]), "f"(v[4 * i + 3])
+                             : "memory");
+        }
+    }
+}
+
+template <bool SCALED>
+__device__ __forceinline__ void split_finish(const Params& p, uint8_t* sm, uint32_t tb, int tile, int w, int lane, int kr) {
+    if (tile >= p.tiles) return;
+    const SplitLayout L(p);
+    const int ks = p.ksplit, q = w & 3, h = w >> 2;
+    const int first = L.begin(p, 2 * kr), u0 = L.begin(p, 2 * kr + h), u1 = L.begin(p, 2 * kr + h + 1);
+    const int n0 = (tile / p.tiles_t) * kBM, t0 = (tile % p.tiles_t) * p.bn;
+    const uint32_t acc = tb + ((uint32_t)(32 * q) << 16);
+    const int c = n0 + 32 * q + lane;
+    const float ws = SCALED && c < p.N ? __ldg(p.w_scale + c) : 1.f;
+    for (int u = u0; u < u1; ++u) {
+        const int li = u - first;
+        float sum[kChunk];
+        tmem_ld16_wait(acc + 16 * u, sum);  // this CTA's own partial
+        float own[kChunk];
+#pragma unroll
+        for (int e = 0; e < kChunk; ++e) own[e] = sum[e];
+        const uint8_t* slot = sm + L.slot(p, q, li, 0) + lane * 16;
+        for (int s = 0; s < ks; ++s, slot += 2048) {  // rank order p_0 + p_1 + ..., whichever CTA owns the chunk
+#pragma unroll
+            for (int i = 0; i < kChunk / 4; ++i) {
+                float4 f = make_float4(own[4 * i], own[4 * i + 1], own[4 * i + 2], own[4 * i + 3]);
+                if (s != kr) f = *reinterpret_cast<const float4*>(slot + i * 512);
+                if (s == 0) {
+                    sum[4 * i] = f.x;
+                    sum[4 * i + 1] = f.y;
+                    sum[4 * i + 2] = f.z;
+                    sum[4 * i + 3] = f.w;
+                } else {
+                    sum[4 * i] += f.x;
+                    sum[4 * i + 1] += f.y;
+                    sum[4 * i + 2] += f.z;
+                    sum[4 * i + 3] += f.w;
+                }
+            }
+        }
+        const int tu = t0 + 16 * u;  // token of the chunk's first column
+#pragma unroll
+        for (int e = 0; e < kChunk; ++e) {
+            if (SCALED) sum[e] = sum[e] * __ldg(p.row_scale + min(tu + e, p.T - 1)) * ws;
+            sum[e] = round_bf16(sum[e]);
+        }
+        if (p.out_tma) {
+            uint8_t* box = sm + L.box(p, q, li) + lane * 2;
+#pragma unroll
+            for (int e = 0; e < kChunk; ++e) *reinterpret_cast<bf16*>(box + e * 64) = __float2bfloat16_rn(sum[e]);
+        } else if (c < p.N) {
+            store_chunk(p.out + c, p.ldo, tu, 0, p.T, 0, tu + kChunk <= p.T, sum);
+        }
+    }
+    if (p.out_tma && u1 > u0) {
+        fence_async_smem();  // the boxes' generic-proxy stores become visible to the copy engine
+        __syncwarp();
+        if (lane == 0) {
+            for (int u = u0; u < u1; ++u) tma_store_2d(&p.tm_out, sm + L.box(p, q, u - first), n0 + 32 * q, t0 + 16 * u);
+            bulk_commit();
+            bulk_wait_all();  // the boxes are read (and written out) before the CTA's memory goes away
+        }
+        __syncwarp();
+    }
+}
+
 // The single-CTA kernel. FP8: the weight operand comes from e4m3 codes, which TMA brings into a
 // raw area of each stage (128 rows x 64 codes) and warps 10-13 convert to fp16 in the 128-byte
 // swizzled layout that TMA would have produced for bf16; the products are fp16 x fp16 (kind::f16)
@@ -247,6 +359,13 @@ __global__ void __launch_bounds__(FP8 ? kFp8Threads : kThreads, 1) in_proj_conv_
     __shared__ Shared sh;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int kblocks = p.K / kBK;
+    // split K: the CTAs of a cluster share one tile, CTA kr taking K blocks [kb0, kb1); otherwise
+    // the CTA walks the tiles with stride gridDim.x over all K blocks
+    const int ks = p.ksplit;
+    const int kr = ks > 1 ? (int)cluster_rank() : 0;
+    const int kb0 = kblocks * kr / ks, kb1 = kblocks * (kr + 1) / ks;
+    const int tfirst = ks > 1 ? (int)blockIdx.x / ks : (int)blockIdx.x;
+    const int tstep = ks > 1 ? (int)gridDim.x / ks : (int)gridDim.x;
 
     if (tid == 0) {
         for (int s = 0; s < S; ++s) {
@@ -281,10 +400,10 @@ __global__ void __launch_bounds__(FP8 ? kFp8Threads : kThreads, 1) in_proj_conv_
             uint32_t ph = 0;  // parity of stage s's current use (the index and parity advance by steps:
                               // no division by the run-time stage count on these threads)
             bool ok = true;
-            for (int tile = blockIdx.x; ok && tile < p.tiles; tile += gridDim.x) {
+            for (int tile = tfirst; ok && tile < p.tiles; tile += tstep) {
                 const int n0 = (tile / p.tiles_t) * kBM;
                 const int row0 = (tile % p.tiles_t) * (p.bn - p.halo) - p.halo;
-                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                for (int kb = kb0; kb < kb1; ++kb, ++it) {
                     if (it >= S && !mbar_wait_or_abort(&sh.empty[s], ph ^ 1u, kSiteTmaLoad, &sh.abort, false)) {
                         atomicExch(&sh.abort, 1);
                         ok = false;
@@ -318,7 +437,7 @@ __global__ void __launch_bounds__(FP8 ? kFp8Threads : kThreads, 1) in_proj_conv_
             int lt = 0, s = 0;
             uint32_t ph = 0;
             bool ok = true;
-            for (int tile = blockIdx.x; ok && tile < p.tiles; tile += gridDim.x, ++lt) {
+            for (int tile = tfirst; ok && tile < p.tiles; tile += tstep, ++lt) {
                 const int b = lt & 1;
                 const uint32_t acc = tb + b * kAccCols;
                 if (lt >= 2 && !mbar_wait_or_abort(&sh.acc_empty[b], (uint32_t)((lt >> 1) - 1) & 1, kSiteReady,
@@ -327,7 +446,7 @@ __global__ void __launch_bounds__(FP8 ? kFp8Threads : kThreads, 1) in_proj_conv_
                     break;
                 }
                 tc_fence_after();
-                for (int kb = 0; kb < kblocks; ++kb) {
+                for (int kb = kb0; kb < kb1; ++kb) {
                     if (!mbar_wait_or_abort(&sh.full[s], ph, kSiteTmaLoad, &sh.abort, false)) {
                         atomicExch(&sh.abort, 1);
                         ok = false;
@@ -338,7 +457,8 @@ __global__ void __launch_bounds__(FP8 ? kFp8Threads : kThreads, 1) in_proj_conv_
                     const uint64_t da = sdesc_kmajor(st, 0), db = sdesc_kmajor(st + kAStage, 0);
 #pragma unroll
                     for (int kk = 0; kk < kBK / 16; ++kk)
-                        mma_f16(acc, sdesc_add(da, kk * 32), sdesc_add(db, kk * 32), idesc, (kb | kk) != 0 ? 1u : 0u);
+                        mma_f16(acc, sdesc_add(da, kk * 32), sdesc_add(db, kk * 32), idesc,
+                                (kb != kb0 || kk != 0) ? 1u : 0u);
                     mma_commit(&sh.empty[s]);  // the stage is free once these products have read it
                     if (++s == S) {
                         s = 0;
@@ -350,6 +470,9 @@ __global__ void __launch_bounds__(FP8 ? kFp8Threads : kThreads, 1) in_proj_conv_
             mma_commit(&sh.mma_done);
             mbar_wait(&sh.mma_done, 0, kSiteMma);  // every product issued is done before TMEM goes away
         }
+    } else if (warp < kEpilogueWarps && ks > 1) {
+        // split K: the one accumulator is complete; the sums across the cluster follow below
+        if (!mbar_wait_or_abort(&sh.acc_full[0], 0, kSiteMma, &sh.abort)) atomicExch(&sh.abort, 1);
     } else if (warp < kEpilogueWarps) {
         // ================================ epilogue ================================
         const int q = warp & 3, half = p.bn >> 1, col0 = (warp >> 2) * half;
@@ -376,8 +499,8 @@ __global__ void __launch_bounds__(FP8 ? kFp8Threads : kThreads, 1) in_proj_conv_
         // ============================ e4m3 -> fp16 converters ============================
         constexpr int kPer = kBM * kBK / 16 / (32 * kConvertWarps);  // 16-code pieces per thread: 4
         const int ct = tid - 32 * (kEpilogueWarps + 2);              // 0 .. 127
-        const int my_tiles = blockIdx.x < p.tiles ? (p.tiles - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
-        const int total = my_tiles * kblocks;
+        const int my_tiles = tfirst < p.tiles ? (p.tiles - tfirst + tstep - 1) / tstep : 0;
+        const int total = my_tiles * (kb1 - kb0);
         int s = 0;
         uint32_t ph = 0;
         for (int it = 0; it < total; ++it) {
@@ -406,6 +529,15 @@ __global__ void __launch_bounds__(FP8 ? kFp8Threads : kThreads, 1) in_proj_conv_
                 ph ^= 1u;
             }
         }
+    }
+    if (ks > 1) {
+        __syncwarp();
+        tc_fence_before();
+        cluster_sync();  // every CTA of the cluster is done with its products: its stages are free
+        tc_fence_after();
+        if (warp < kEpilogueWarps) split_send(p, sm, tb, warp, lane, kr);
+        cluster_sync();  // the partial sums have landed
+        if (warp < kEpilogueWarps) split_finish<FP8>(p, sm, tb, tfirst, warp, lane, kr);
     }
     tc_fence_before();
     __syncthreads();
@@ -634,6 +766,20 @@ static bool make_map2(CUtensorMap* map, const void* base, int64_t rows, int64_t 
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 2-D map over the bf16 output [T, N] (row stride ld elements) for the split-K owners' stores:
+// box (32 channels, box_rows tokens), no swizzle; the copies clip at T and N.
+static bool make_out_map(CUtensorMap* map, void* base, int64_t T, int64_t N, int64_t ld, uint32_t box_rows) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)T};
+    cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+    cuuint32_t box[2] = {32, box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // 2-D map over the e4m3 codes [rows, K] (row stride ld bytes), box (64, 128), rows kept as they are.
 static bool make_codes_map(CUtensorMap* map, const void* base, int64_t rows, int64_t K, int64_t ld) {
     EncodeTiledFn enc = encode_fn();
@@ -669,6 +815,35 @@ static int choose_bn(int64_t T, int64_t N, int ctas, int tile_channels, int halo
     return best;
 }
 
+// Clusters of `ks` single CTAs (one per SM at the largest stage ring) that can be resident at once.
+static int max_split_clusters(int dev, bool fp8, int ks) {
+    static int cache[64][2][4];  // [device][fp8][log2 ks - 1], 0 = not asked yet, -1 = none
+    const int li = ks == 2 ? 0 : ks == 4 ? 1 : 2;
+    int& slot = cache[dev][fp8 ? 1 : 0][li];
+    if (slot == 0) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)ks);
+        cfg.blockDim = dim3((unsigned)(fp8 ? kFp8Threads : kThreads));
+        cfg.dynamicSmemBytes = kSmemLimit;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = (unsigned)ks;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        const cudaError_t e = fp8 ? cudaOccupancyMaxActiveClusters(&n, in_proj_conv_kernel<true>, &cfg)
+                                  : cudaOccupancyMaxActiveClusters(&n, in_proj_conv_kernel<false>, &cfg);
+        if (e != cudaSuccess) {
+            (void)cudaGetLastError();
+            n = 0;
+        }
+        slot = n > 0 ? n : -1;
+    }
+    return slot;
+}
+
 }  // namespace inproj
 
 size_t in_proj_fp8_workspace_bytes(int64_t T, int64_t K) {
@@ -701,10 +876,25 @@ int launch_in_proj_conv(const InProjArgs& a, cudaStream_t s) {
     const int halo = a.C > 0 ? kHalo : 0;
     const int bn_pair = choose_bn(a.T, a.N, pairs, kPairBM, halo);
     const int64_t pair_tiles = (a.T + bn_pair - halo - 1) / (bn_pair - halo) * ((a.N + kPairBM - 1) / kPairBM);
-    const bool use_pair = !fp8 && pairs >= 1 && pair_tiles >= pairs;
+    // Decode-sized batches without conv channels: all tokens in one tile, and K split over a
+    // cluster of ks CTAs so that the tiles (one per 128 weight rows) cover the SMs; each CTA then
+    // streams 1 / ks of its weight rows (the stage ring's copies, not the products, bound these
+    // shapes). A split needs at least 4 K blocks a CTA and every cluster resident at once.
+    int ks = 1;
+    if (a.C == 0 && a.T <= kMaxBN && a.K % kBK == 0) {
+        const int64_t tiles_n = (a.N + kBM - 1) / kBM;
+        for (int cand = 8; cand >= 2; cand >>= 1)
+            if (tiles_n * cand <= sms[dev] && a.K / kBK >= 4 * cand &&
+                max_split_clusters(dev, fp8, cand) >= tiles_n) {
+                ks = cand;
+                break;
+            }
+    }
+    const bool use_pair = ks == 1 && !fp8 && pairs >= 1 && pair_tiles >= pairs;
     Params p;
     memset(&p, 0, sizeof(p));
-    p.bn = use_pair ? bn_pair : choose_bn(a.T, a.N, sms[dev], kBM, halo);
+    p.ksplit = ks;
+    p.bn = ks > 1 ? (int)((a.T + 31) / 32 * 32) : use_pair ? bn_pair : choose_bn(a.T, a.N, sms[dev], kBM, halo);
     p.halo = halo;
     __half* xh = nullptr;
     if (fp8) {
@@ -745,9 +935,35 @@ int launch_in_proj_conv(const InProjArgs& a, cudaStream_t s) {
     p.stages = (int)((kSmemLimit - 1024) / p.stage_bytes);
     if (p.stages > kMaxStages) p.stages = kMaxStages;
     const uint32_t single_smem = (uint32_t)p.stages * p.stage_bytes + 1024;
-    if (fp8) {
+    if (fp8)
         fp16_rows_kernel<<<(unsigned)a.T, 256, 0, s>>>(static_cast<const bf16*>(a.x), a.ldx, (int)a.K, xh,
                                                          const_cast<float*>(p.row_scale));
+    if (ks > 1) {
+        // the partial sums' slots (4 lane quadrants x the chunks a CTA owns at most x ks senders x
+        // 2 KB) and the owners' output boxes (1 KB a chunk) reuse the stage ring after the products
+        const uint32_t maxown = (uint32_t)((p.bn / 16 + ks - 1) / ks);
+        if (4u * maxown * ((uint32_t)ks * 2048u + 1024u) > (uint32_t)p.stages * p.stage_bytes) return GDN_ERR_LAUNCH;
+        p.out_tma = (reinterpret_cast<uintptr_t>(a.out) % 16 == 0 && (a.ldo * 2) % 16 == 0 &&
+                     make_out_map(&p.tm_out, a.out, a.T, a.N, a.ldo, 16u))
+                        ? 1
+                        : 0;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)(tiles * ks));
+        cfg.blockDim = dim3((unsigned)(fp8 ? kFp8Threads : kThreads));
+        cfg.dynamicSmemBytes = single_smem;
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = (unsigned)ks;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        const cudaError_t e = fp8 ? cudaLaunchKernelEx(&cfg, in_proj_conv_kernel<true>, p)
+                                  : cudaLaunchKernelEx(&cfg, in_proj_conv_kernel<false>, p);
+        return e == cudaSuccess ? launch_status() : GDN_ERR_LAUNCH;
+    }
+    if (fp8) {
         const int grid = (int)(tiles < sms[dev] ? tiles : sms[dev]);
         in_proj_conv_kernel<true><<<grid, kFp8Threads, single_smem, s>>>(p);
     } else if (use_pair) {

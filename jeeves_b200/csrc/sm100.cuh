@@ -217,6 +217,15 @@ __device__ __forceinline__ void bulk_store(void* dst, const void* src, uint32_t 
                  : "memory");
 }
 
+// Tiled TMA store of the 2-D box at (c0, c1) from shared memory (a bulk group; the tensor map
+// clips the box at the tensor's edges).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(smem_u32(src)), "r"(c0), "r"(c1)
+                 : "memory");
+}
+
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 
 // Waits until every committed bulk store of this thread has been performed.

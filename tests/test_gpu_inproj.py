@@ -60,6 +60,19 @@ def test_in_proj_without_conv_channels_matches_matmul(T):
     _close(out, x @ w.T)
 
 
+@pytest.mark.parametrize("T,K,N", [(1, 4096, 8192), (32, 4096, 8192), (256, 4096, 8192), (100, 4096, 4096),
+                                   (17, 4288, 1152), (256, 2048, 640)])
+def test_in_proj_split_k_decode_batches(T, K, N):
+    """Decode-sized batches without conv channels split K over a cluster of 2 to 8 CTAs (so that
+    the tiles, one per 128 weight rows, cover the SMs) and add the partial sums through distributed
+    shared memory in a fixed order: against matmul, and the same bits on a repeated call. K = 4288
+    gives the CTAs K ranges of unequal length."""
+    x, w, cw = _case(T + N, T, K, 0, N)
+    out = gdn.in_proj_conv(x, w, cw, 0)
+    _close(out, x @ w.T)
+    assert torch.equal(out, gdn.in_proj_conv(x, w, cw, 0))
+
+
 @pytest.mark.parametrize("lens,K,C,rest", [([70, 1, 129, 0, 100, 3], 192, 256, 72),        # single CTAs
                                            ([700, 2, 900, 0, 3, 419, 1], 128, 2048, 256),  # pairs, 160 tokens
                                            ([1000, 1, 0, 700, 3, 502], 128, 256, 128),     # pairs, 64 tokens
