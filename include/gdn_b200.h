@@ -464,6 +464,14 @@ GDN_API int gdn_in_proj_conv(const void* x, int64_t x_stride, const void* w, int
  * forward or the output projection). workspace: gdn_in_proj_fp8_workspace_size(tokens, hidden)
  * bytes, 16-byte aligned (the fp16 rows and their scales). The other arguments as gdn_in_proj_conv. */
 GDN_API size_t gdn_in_proj_fp8_workspace_size(int64_t tokens, int64_t hidden);
+/* The workspace for gdn_in_proj_conv_fp8 (same reference lines) that lets the shape take its fastest
+ * path on the current device: for shapes whose token tiles fill the GPU (prefill) the fp16 rows and
+ * scales plus an fp16 copy of the weights, [out_channels, hidden] (the codes are converted once and
+ * the products run on CTA pairs, fp16 x fp16, the same arithmetic); for other shapes the same as
+ * gdn_in_proj_fp8_workspace_size. With gdn_in_proj_fp8_workspace_size bytes every shape runs on
+ * single CTAs that convert the codes tile by tile. */
+GDN_API size_t gdn_in_proj_fp8_prefill_workspace_size(int64_t tokens, int64_t hidden, int64_t out_channels,
+                                                      int64_t conv_channels);
 GDN_API int gdn_in_proj_conv_fp8(const void* x, int64_t x_stride, const void* codes, int64_t codes_stride,
                                  const float* w_scale, const void* conv_w, const int32_t* cu_seqlens, void* out,
                                  int64_t out_stride, void* conv_state, void* workspace, size_t workspace_bytes,

@@ -77,6 +77,7 @@ SIGNATURES: dict[str, list] = {
                               _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _p],
     "gdn_in_proj_conv": [_p, _i64, _p, _i64, _p, _p, _p, _i64, _p, _i64, _i64, _i64, _i64, _i64, _i64, _p],
     "gdn_in_proj_fp8_workspace_size": [_i64, _i64],
+    "gdn_in_proj_fp8_prefill_workspace_size": [_i64, _i64, _i64, _i64],
     "gdn_in_proj_conv_fp8": [_p, _i64, _p, _i64, _p, _p, _p, _p, _i64, _p, _p, _sz, _i64, _i64, _i64, _i64, _i64, _i64, _p],
     "gdn_decode_layer": [_p, _i64, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                          _f32, _f32, _p],
@@ -85,7 +86,8 @@ SIGNATURES: dict[str, list] = {
 }
 
 RESTYPES = {"gdn_status_string": ctypes.c_char_p, "gdn_chunk_prefill_workspace_size": ctypes.c_size_t,
-            "gdn_decode_attention_workspace_size": ctypes.c_size_t, "gdn_in_proj_fp8_workspace_size": ctypes.c_size_t}
+            "gdn_decode_attention_workspace_size": ctypes.c_size_t, "gdn_in_proj_fp8_workspace_size": ctypes.c_size_t,
+            "gdn_in_proj_fp8_prefill_workspace_size": ctypes.c_size_t}
 
 _lock = threading.Lock()
 _lib = None

@@ -575,6 +575,12 @@ size_t gdn_in_proj_fp8_workspace_size(int64_t tokens, int64_t hidden) {
     return in_proj_fp8_workspace_bytes(tokens, hidden);
 }
 
+size_t gdn_in_proj_fp8_prefill_workspace_size(int64_t tokens, int64_t hidden, int64_t out_channels,
+                                              int64_t conv_channels) {
+    if (tokens <= 0 || hidden <= 0 || out_channels <= 0 || conv_channels < 0) return 0;
+    return in_proj_fp8_prefill_workspace_bytes(tokens, hidden, out_channels, conv_channels);
+}
+
 int gdn_in_proj_conv_fp8(const void* x, int64_t x_stride, const void* codes, int64_t codes_stride,
                          const float* w_scale, const void* conv_w, const int32_t* cu_seqlens, void* out,
                          int64_t out_stride, void* conv_state, void* workspace, size_t workspace_bytes,

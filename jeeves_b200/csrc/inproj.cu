@@ -587,6 +587,25 @@ __global__ void __launch_bounds__(256) fp16_rows_kernel(const bf16* __restrict__
     if (threadIdx.x == 0) row_scale[row] = __uint_as_float((uint32_t)(shift + 127) << 23);
 }
 
+// The e4m3 codes [N, K] (row stride ldc bytes) as fp16 [N, K] (exact): the fp8 path's weight
+// operand for the CTA-pair kernel at prefill sizes, where each weight panel is read by many token
+// tiles and converting it once beats converting it in every tile. 16 codes a thread.
+__global__ void __launch_bounds__(256) codes_to_f16_kernel(const uint8_t* __restrict__ codes, int64_t ldc,
+                                                           __half* __restrict__ w16, int64_t N, int K) {
+    const int64_t per_row = K / 16, total = N * per_row;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t row = i / per_row, k = (i % per_row) * 16;
+        const uint4 w = *reinterpret_cast<const uint4*>(codes + row * ldc + k);
+        const uint4 lo = make_uint4(e4m3x2_to_f16x2(w.x), e4m3x2_to_f16x2(w.x >> 16), e4m3x2_to_f16x2(w.y),
+                                    e4m3x2_to_f16x2(w.y >> 16));
+        const uint4 hi = make_uint4(e4m3x2_to_f16x2(w.z), e4m3x2_to_f16x2(w.z >> 16), e4m3x2_to_f16x2(w.w),
+                                    e4m3x2_to_f16x2(w.w >> 16));
+        uint4* dst = reinterpret_cast<uint4*>(w16 + row * K + k);
+        dst[0] = lo;
+        dst[1] = hi;
+    }
+}
+
 // ------------------------------------------------------------------------------------------
 // The CTA-pair form: a cluster of two CTAs computes a 256-channel x bn-token tile with
 // tcgen05.mma.cta_group::2 (M = 256). Each CTA stages its own 128 weight rows and half of the
@@ -612,6 +631,9 @@ __device__ __forceinline__ void pair_abort(int* abort, uint32_t rank) {
                  : "memory");
 }
 
+// F16: fp16 operands (the fp8 path's fp16 activation rows against an fp16 copy of the weights
+// that codes_to_f16_kernel made), and the drain applies the row and weight scales.
+template <bool F16>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     in_proj_conv_pair_kernel(const __grid_constant__ Params p) {
     extern __shared__ uint8_t smem_raw[];
@@ -684,7 +706,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     } else if (warp == kMmaWarp) {
         // ============================== MMA issuer (leader) ==============================
         if (lane == 0 && rank == 0) {
-            const uint32_t idesc = make_idesc(kPairBM, (uint32_t)p.bn, kFmtBF16, false, false);
+            const uint32_t idesc = make_idesc(kPairBM, (uint32_t)p.bn, F16 ? kFmtF16 : kFmtBF16, false, false);
             int it = 0, lt = 0;
             bool ok = true;
             for (int tile = pair; ok && tile < p.tiles; tile += npairs, ++lt) {
@@ -735,8 +757,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const int row0 = tt * (p.bn - p.halo) - p.halo;
             const uint32_t acc = tb + b * kAccCols + ((uint32_t)(32 * q) << 16);
             const int c = nn * kPairBM + kBM * (int)rank + 32 * q + lane;
-            if (p.cu_seqlens) drain<true>(p, acc, col0, half, row0, c, lane);
-            else drain<false>(p, acc, col0, half, row0, c, lane);
+            if (p.cu_seqlens) drain<true, F16>(p, acc, col0, half, row0, c, lane);
+            else drain<false, F16>(p, acc, col0, half, row0, c, lane);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(mapa_shared(&sh.acc_empty[b], 0));  // the leader may overwrite it
@@ -850,51 +872,97 @@ size_t in_proj_fp8_workspace_bytes(int64_t T, int64_t K) {
     return ((size_t)T * K * 2 + 255) / 256 * 256 + (size_t)T * 4;
 }
 
-int launch_in_proj_conv(const InProjArgs& a, cudaStream_t s) {
-    using namespace inproj;
-    if (a.T == 0 || a.N == 0) return GDN_OK;
+// Offset of the fp16 weight copy in an fp8 workspace (after the rows and their scales).
+static size_t fp8_w16_offset(int64_t T, int64_t K) { return (in_proj_fp8_workspace_bytes(T, K) + 255) / 256 * 256; }
+
+size_t in_proj_fp8_pair_workspace_bytes(int64_t T, int64_t K, int64_t N) {
+    return fp8_w16_offset(T, K) + (size_t)N * K * 2;
+}
+
+namespace inproj {
+
+// The kernels' shared-memory limits and the device's SM count, once per device.
+static int device_sms(int& dev) {
     static bool ready[64] = {false};
     static int sms[64] = {0};
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return GDN_ERR_LAUNCH;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
     if (!ready[dev]) {
         if (cudaFuncSetAttribute(in_proj_conv_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)kSmemLimit) != cudaSuccess ||
             cudaFuncSetAttribute(in_proj_conv_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)kSmemLimit) != cudaSuccess ||
-            cudaFuncSetAttribute(in_proj_conv_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            cudaFuncSetAttribute(in_proj_conv_pair_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)kPairSmemBytes) != cudaSuccess ||
+            cudaFuncSetAttribute(in_proj_conv_pair_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)kPairSmemBytes) != cudaSuccess ||
             cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms[dev] < 1)
-            return GDN_ERR_LAUNCH;
+            return 0;
         ready[dev] = true;
     }
-    // bf16 weights: CTA pairs when the pair tiles occupy every pair of SMs, single CTAs for smaller
-    // problems. fp8 weights: single CTAs (the converters feed one CTA's operand).
-    const bool fp8 = a.codes != nullptr;
-    const int pairs = sms[dev] / 2;
+    return sms[dev];
+}
+
+// How a shape runs: K split over clusters of ks CTAs (decode-sized batches without conv
+// channels), CTA pairs with bn_pair-token tiles (when the pair tiles fill every pair of SMs; with
+// fp8 weights only if `fp8_pair`, i.e. the workspace holds an fp16 copy of the weights), or single
+// CTAs.
+struct Plan {
+    int ks = 1, bn_pair = 0, halo = 0;
+    bool use_pair = false;
+    int64_t pair_tiles = 0;
+};
+
+static Plan plan_shape(int64_t T, int64_t N, int64_t K, int64_t C, bool fp8, bool fp8_pair, int dev, int sms) {
+    Plan pl;
+    const int pairs = sms / 2;
     // without conv channels no tile needs the window's leading tokens
-    const int halo = a.C > 0 ? kHalo : 0;
-    const int bn_pair = choose_bn(a.T, a.N, pairs, kPairBM, halo);
-    const int64_t pair_tiles = (a.T + bn_pair - halo - 1) / (bn_pair - halo) * ((a.N + kPairBM - 1) / kPairBM);
+    pl.halo = C > 0 ? kHalo : 0;
+    pl.bn_pair = choose_bn(T, N, pairs, kPairBM, pl.halo);
+    pl.pair_tiles = (T + pl.bn_pair - pl.halo - 1) / (pl.bn_pair - pl.halo) * ((N + kPairBM - 1) / kPairBM);
     // Decode-sized batches without conv channels: all tokens in one tile, and K split over a
     // cluster of ks CTAs so that the tiles (one per 128 weight rows) cover the SMs; each CTA then
     // streams 1 / ks of its weight rows (the stage ring's copies, not the products, bound these
     // shapes). A split needs at least 4 K blocks a CTA and every cluster resident at once.
-    int ks = 1;
-    if (a.C == 0 && a.T <= kMaxBN && a.K % kBK == 0) {
-        const int64_t tiles_n = (a.N + kBM - 1) / kBM;
+    if (C == 0 && T <= kMaxBN && K % kBK == 0) {
+        const int64_t tiles_n = (N + kBM - 1) / kBM;
         for (int cand = 8; cand >= 2; cand >>= 1)
-            if (tiles_n * cand <= sms[dev] && a.K / kBK >= 4 * cand &&
-                max_split_clusters(dev, fp8, cand) >= tiles_n) {
-                ks = cand;
+            if (tiles_n * cand <= sms && K / kBK >= 4 * cand && max_split_clusters(dev, fp8, cand) >= tiles_n) {
+                pl.ks = cand;
                 break;
             }
     }
-    const bool use_pair = ks == 1 && !fp8 && pairs >= 1 && pair_tiles >= pairs;
+    pl.use_pair = pl.ks == 1 && (!fp8 || fp8_pair) && pairs >= 1 && pl.pair_tiles >= pairs;
+    return pl;
+}
+
+}  // namespace inproj
+
+size_t in_proj_fp8_prefill_workspace_bytes(int64_t T, int64_t K, int64_t N, int64_t C) {
+    using namespace inproj;
+    int dev = 0;
+    const int sms = device_sms(dev);
+    const size_t base = in_proj_fp8_workspace_bytes(T, K);
+    if (sms < 1) return base;
+    return plan_shape(T, N, K, C, true, true, dev, sms).use_pair ? in_proj_fp8_pair_workspace_bytes(T, K, N) : base;
+}
+
+int launch_in_proj_conv(const InProjArgs& a, cudaStream_t s) {
+    using namespace inproj;
+    if (a.T == 0 || a.N == 0) return GDN_OK;
+    int dev = 0;
+    const int nsm = device_sms(dev);
+    if (nsm < 1) return GDN_ERR_LAUNCH;
+    const bool fp8 = a.codes != nullptr;
+    // fp8 weights run on CTA pairs too when the workspace also holds an fp16 copy of the weights
+    // (gdn_in_proj_fp8_prefill_workspace_size): one conversion pass, then fp16 x fp16 products
+    const bool fp8_pair = fp8 && a.workspace_bytes >= in_proj_fp8_pair_workspace_bytes(a.T, a.K, a.N);
+    const Plan pl = plan_shape(a.T, a.N, a.K, a.C, fp8, fp8_pair, dev, nsm);
+    const int ks = pl.ks, halo = pl.halo, bn_pair = pl.bn_pair, pairs = nsm / 2;
+    const bool use_pair = pl.use_pair;
     Params p;
     memset(&p, 0, sizeof(p));
     p.ksplit = ks;
-    p.bn = ks > 1 ? (int)((a.T + 31) / 32 * 32) : use_pair ? bn_pair : choose_bn(a.T, a.N, sms[dev], kBM, halo);
+    p.bn = ks > 1 ? (int)((a.T + 31) / 32 * 32) : use_pair ? bn_pair : choose_bn(a.T, a.N, nsm, kBM, halo);
     p.halo = halo;
     __half* xh = nullptr;
     if (fp8) {
@@ -905,9 +973,15 @@ int launch_in_proj_conv(const InProjArgs& a, cudaStream_t s) {
         p.w_scale = a.w_scale;
         p.row_scale = reinterpret_cast<const float*>(static_cast<uint8_t*>(a.workspace) +
                                                      ((size_t)a.T * a.K * 2 + 255) / 256 * 256);
-        if (!make_map2(&p.tm_x, xh, a.T, a.K, a.K, (uint32_t)p.bn, CU_TENSOR_MAP_DATA_TYPE_FLOAT16) ||
-            !make_codes_map(&p.tm_w, a.codes, a.N, a.K, a.ldc))
+        if (use_pair) {
+            __half* w16 = reinterpret_cast<__half*>(static_cast<uint8_t*>(a.workspace) + fp8_w16_offset(a.T, a.K));
+            if (!make_map2(&p.tm_x, xh, a.T, a.K, a.K, (uint32_t)(p.bn / 2), CU_TENSOR_MAP_DATA_TYPE_FLOAT16) ||
+                !make_map2(&p.tm_w, w16, a.N, a.K, a.K, kBM, CU_TENSOR_MAP_DATA_TYPE_FLOAT16))
+                return GDN_ERR_LAUNCH;
+        } else if (!make_map2(&p.tm_x, xh, a.T, a.K, a.K, (uint32_t)p.bn, CU_TENSOR_MAP_DATA_TYPE_FLOAT16) ||
+                   !make_codes_map(&p.tm_w, a.codes, a.N, a.K, a.ldc)) {
             return GDN_ERR_LAUNCH;
+        }
     } else if (!make_map2(&p.tm_w, a.w, a.N, a.K, a.ldw, kBM) ||
                !make_map2(&p.tm_x, a.x, a.T, a.K, a.ldx, (uint32_t)(use_pair ? p.bn / 2 : p.bn))) {
         return GDN_ERR_LAUNCH;
@@ -963,14 +1037,22 @@ int launch_in_proj_conv(const InProjArgs& a, cudaStream_t s) {
                                   : cudaLaunchKernelEx(&cfg, in_proj_conv_kernel<false>, p);
         return e == cudaSuccess ? launch_status() : GDN_ERR_LAUNCH;
     }
-    if (fp8) {
-        const int grid = (int)(tiles < sms[dev] ? tiles : sms[dev]);
-        in_proj_conv_kernel<true><<<grid, kFp8Threads, single_smem, s>>>(p);
-    } else if (use_pair) {
+    if (use_pair) {
         const int grid = 2 * (int)(tiles < pairs ? tiles : pairs);
-        in_proj_conv_pair_kernel<<<grid, kThreads, kPairSmemBytes, s>>>(p);
+        if (fp8) {
+            __half* w16 = reinterpret_cast<__half*>(static_cast<uint8_t*>(a.workspace) + fp8_w16_offset(a.T, a.K));
+            const int64_t pieces = a.N * (a.K / 16);
+            const int cgrid = (int)((pieces + 255) / 256 < 8 * nsm ? (pieces + 255) / 256 : 8 * nsm);
+            codes_to_f16_kernel<<<cgrid, 256, 0, s>>>(static_cast<const uint8_t*>(a.codes), a.ldc, w16, a.N, (int)a.K);
+            in_proj_conv_pair_kernel<true><<<grid, kThreads, kPairSmemBytes, s>>>(p);
+        } else {
+            in_proj_conv_pair_kernel<false><<<grid, kThreads, kPairSmemBytes, s>>>(p);
+        }
+    } else if (fp8) {
+        const int grid = (int)(tiles < nsm ? tiles : nsm);
+        in_proj_conv_kernel<true><<<grid, kFp8Threads, single_smem, s>>>(p);
     } else {
-        const int grid = (int)(tiles < sms[dev] ? tiles : sms[dev]);
+        const int grid = (int)(tiles < nsm ? tiles : nsm);
         in_proj_conv_kernel<false><<<grid, kThreads, single_smem, s>>>(p);
     }
     return launch_status();

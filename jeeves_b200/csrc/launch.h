@@ -253,6 +253,9 @@ struct InProjArgs {
 };
 int launch_in_proj_conv(const InProjArgs& a, cudaStream_t s);
 size_t in_proj_fp8_workspace_bytes(int64_t T, int64_t K);
+size_t in_proj_fp8_pair_workspace_bytes(int64_t T, int64_t K, int64_t N);
+// the pair size when the shape runs on CTA pairs on the current device, else the base size
+size_t in_proj_fp8_prefill_workspace_bytes(int64_t T, int64_t K, int64_t N, int64_t C);
 
 // Runs a bounded device wait that is meant to run out after `limit_cycles` (probe.cu).
 int launch_bounded_wait_probe(int64_t limit_cycles, cudaStream_t s);

@@ -267,7 +267,7 @@ def in_proj_conv(x, weight, conv_weight, conv_channels: int, cu_seqlens=None, co
     common = (None if cw is None else cw.data_ptr(), None if cu is None else cu.data_ptr(), out.data_ptr(), N,
               None if state is None else state.data_ptr())
     if fp8:
-        ws_bytes = lib.gdn_in_proj_fp8_workspace_size(T, K)
+        ws_bytes = lib.gdn_in_proj_fp8_prefill_workspace_size(T, K, N, conv_channels)
         ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=x.device)
         scale = weight_scale.contiguous()
         status = lib.gdn_in_proj_conv_fp8(x2.data_ptr(), x2.stride(0), w.data_ptr(), w.stride(0), scale.data_ptr(),

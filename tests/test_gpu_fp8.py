@@ -101,6 +101,51 @@ def test_fp8_in_proj_conv_packed_sequences_and_state():
         assert torch.equal(state[n], want), n
 
 
+def _fp8_call(lib, x, codes, scale, cw, C, ws_bytes):
+    T, K = x.shape
+    N = codes.shape[0]
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+    out = torch.empty(T, N, dtype=torch.bfloat16, device="cuda")
+    st = lib.gdn_in_proj_conv_fp8(x.data_ptr(), K, codes.data_ptr(), K, scale.data_ptr(),
+                                  cw.data_ptr() if C else None, None, out.data_ptr(), N, None, ws.data_ptr(),
+                                  ws_bytes, T, K, N, C, 1, 4, torch.cuda.current_stream().cuda_stream)
+    assert st == 0, st
+    return out
+
+
+def test_fp8_prefill_on_cta_pairs_and_on_single_ctas():
+    """With the prefill workspace (gdn_in_proj_fp8_prefill_workspace_size) a shape whose token
+    tiles fill the GPU converts the codes to fp16 once and runs its products on CTA pairs; with
+    the base workspace the same call runs on single CTAs that convert tile by tile. Both meet the
+    reference's bar; with the conv in the epilogue, the conv columns against the conv kernel on the
+    plain output and the rest bit-identical to it."""
+    from jeeves_b200 import _lib
+    lib = _lib.load()
+    T, K, C, rest = 2048, 1024, 8192, 256
+    N = C + rest
+    codes, scale = _weights(N, K, 21)
+    x = _rows(T, K, 22)
+    x[1::2, 0] = 3.0
+    cw = (torch.randn(C, 4, generator=torch.Generator(device="cuda").manual_seed(5), device="cuda") * 0.5).to(
+        torch.bfloat16)
+    exact = ((x.double() @ codes.double().t()) * scale.double()).to(torch.bfloat16)
+    small = lib.gdn_in_proj_fp8_workspace_size(T, K)
+    for conv in (0, C):
+        big = lib.gdn_in_proj_fp8_prefill_workspace_size(T, K, N, conv)
+        assert big == small + (256 - small % 256) % 256 + N * K * 2  # this shape runs on CTA pairs
+        plain_pair = _fp8_call(lib, x, codes, scale, cw, 0, big)
+        plain_single = _fp8_call(lib, x, codes, scale, cw, 0, small)
+        for out in (plain_pair, plain_single):
+            assert out.isfinite().all()
+            assert (out == exact).double().mean().item() >= 0.995
+        if conv:
+            for ws_bytes, plain in ((big, plain_pair), (small, plain_single)):
+                out = _fp8_call(lib, x, codes, scale, cw, C, ws_bytes)
+                assert torch.equal(out[:, C:], plain[:, C:])
+                _close(out[:, :C], gdn.causal_conv1d(plain[None, :, :C].contiguous(), cw)[0])
+    assert torch.equal(plain_pair, _fp8_call(lib, x, codes, scale, cw, 0, big))
+
+
 def test_fp8_rejects_bad_arguments():
     codes, scale = _weights(256, 128, 1)
     x = _rows(8, 128, 2)
