@@ -391,6 +391,10 @@ __global__ void __launch_bounds__(FP8 ? kFp8Threads : kThreads, 1) in_proj_conv_
     __syncthreads();
     tc_fence_after();
     const uint32_t tb = sh.tmem_base;
+    // Split-K launches are programmatic dependents of the previous kernel in the stream: the set-up
+    // above (barriers, TMEM, tensor-map prefetch) overlaps that kernel's end; nothing in global
+    // memory is read before this wait (a no-op for an ordinary launch).
+    pdl_wait();
 
     if (warp == kProducerWarp) {
         // ============================== producer ==============================
@@ -1026,13 +1030,15 @@ int launch_in_proj_conv(const InProjArgs& a, cudaStream_t s) {
         cfg.blockDim = dim3((unsigned)(fp8 ? kFp8Threads : kThreads));
         cfg.dynamicSmemBytes = single_smem;
         cfg.stream = s;
-        cudaLaunchAttribute attr[1];
+        cudaLaunchAttribute attr[2];
         attr[0].id = cudaLaunchAttributeClusterDimension;
         attr[0].val.clusterDim.x = (unsigned)ks;
         attr[0].val.clusterDim.y = 1;
         attr[0].val.clusterDim.z = 1;
+        attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[1].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
-        cfg.numAttrs = 1;
+        cfg.numAttrs = 2;
         const cudaError_t e = fp8 ? cudaLaunchKernelEx(&cfg, in_proj_conv_kernel<true>, p)
                                   : cudaLaunchKernelEx(&cfg, in_proj_conv_kernel<false>, p);
         return e == cudaSuccess ? launch_status() : GDN_ERR_LAUNCH;
