@@ -557,6 +557,9 @@ __global__ void __launch_bounds__(FP8 ? kFp8Threads : kThreads, 1) in_proj_conv_
 // (the activation conversion of inference/fp8.py:30-52, FP16_TOP_EXPONENT = 13).
 __global__ void __launch_bounds__(256) fp16_rows_kernel(const bf16* __restrict__ x, int64_t ldx, int K,
                                                         __half* __restrict__ xh, float* __restrict__ row_scale) {
+    // the GEMM behind this kernel (a programmatic dependent when K is split) may start its set-up
+    // now; it reads these rows only after its griddepcontrol.wait, i.e. after this grid completes
+    pdl_launch_dependents();
     __shared__ float red[8];
     const int64_t row = blockIdx.x;
     const bf16* xr = x + row * ldx;
