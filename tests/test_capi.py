@@ -203,3 +203,24 @@ def test_in_proj_conv_checks_its_inputs():
     assert lib.gdn_in_proj_conv(*args(taps=3)) == _lib.ERR_UNSUPPORTED
     assert lib.gdn_in_proj_conv(*args(ldx=60)) == _lib.ERR_ALIGN
     assert lib.gdn_in_proj_conv(*args(T=0)) == _lib.OK
+
+
+def test_fp8_workspace_sizes_and_checks():
+    """The fp8 projection's workspaces: the base size holds the fp16 rows and their scales; the
+    prefill size is never smaller (on a machine without a GPU no shape is planned onto CTA pairs,
+    so the two agree); a workspace below the base size is rejected before any launch."""
+    lib = _lib.load()
+    T, K, N = 300, 256, 512
+    base = lib.gdn_in_proj_fp8_workspace_size(T, K)
+    assert base == (T * K * 2 + 255) // 256 * 256 + T * 4
+    big = lib.gdn_in_proj_fp8_prefill_workspace_size(T, K, N, 0)
+    assert big >= base
+    assert big in (base, (base + 255) // 256 * 256 + N * K * 2)
+    assert lib.gdn_in_proj_fp8_prefill_workspace_size(0, K, N, 0) == 0
+    assert lib.gdn_in_proj_fp8_prefill_workspace_size(T, K, N, -1) == 0
+
+    def call(ws_bytes, codes_stride=K):
+        return lib.gdn_in_proj_conv_fp8(16, K, 16, codes_stride, 16, None, None, 16, N, None, 16, ws_bytes,
+                                        T, K, N, 0, 1, 4, None)
+    assert call(base - 1) == _lib.ERR_WORKSPACE
+    assert call(base, codes_stride=K + 8) == _lib.ERR_ALIGN  # code rows must be 16-byte multiples
