@@ -1,7 +1,8 @@
 """GPU parity of the merged input projection with the causal conv in the GEMM epilogue: the
 projection against PyTorch's bf16 matmul (the reference's nn.Linear on CUDA, fp32 accumulation),
 and the conv part against the library's conv kernel on that matmul's output (same rounding), so
-that only a different summation order of the GEMM can move a bf16 value, by one ulp."""
+that only a different summation order of the GEMM can move a bf16 value, by one ulp; and both
+against a float64 product and conv computed on the CPU, within the reference's bf16 roundings."""
 
 import pytest
 import torch
@@ -102,6 +103,49 @@ def test_in_proj_conv_dense_conv_state(T, C, rest):
     want[0, :, 4 - min(4, T):] = y[-min(4, T):, :C].T
     _close(state, want)
     _close(out[:, C:], y[:, C:])
+
+
+def _bf16_ulp(v):
+    """One bf16 unit in the last place of each value (2^(e-8) for |v| = m 2^e, 0.5 <= m < 1)."""
+    return torch.ldexp(torch.ones_like(v), torch.frexp(v)[1] - 8)
+
+
+def _conv64(y, cw):
+    """The causal depthwise conv + SiLU of model/model.py:199-204 in float64, zeros before the
+    first token, on a [T, C] float64 projection: (SiLU output, conv sum)."""
+    T, C = y.shape
+    taps = cw.shape[-1]
+    yp = torch.cat([torch.zeros(taps - 1, C, dtype=torch.float64), y])
+    acc = sum(cw[:, i].double()[None, :] * yp[i:i + T] for i in range(taps))
+    return acc * torch.sigmoid(acc), acc
+
+
+@pytest.mark.parametrize("T,K,C,rest", [(700, 4096, 2048, 512),     # single CTAs
+                                        (4096, 4096, 8192, 4160),   # the 9B-shaped projection, CTA pairs
+                                        (256, 4096, 0, 8192),       # decode batch, K split over clusters
+                                        (32, 4096, 0, 8192)])
+def test_in_proj_conv_matches_float64_cpu_product(T, K, C, rest):
+    """The projection and its conv against a float64 product and conv computed on the CPU (no
+    intermediate rounding): each projected channel within one bf16 ulp (or 1e-3) of the exactly
+    rounded product, under 1 % of them off at all; each conv channel within the bound that the
+    reference's roundings allow (the projection, the conv sum and the SiLU output are each rounded
+    to bf16, model/model.py:199-204): one ulp of the output, plus 1.1 (the largest slope of SiLU)
+    times one ulp of the conv sum and the sum over the window of |w| times one ulp of the
+    projected value, plus 1e-5. Each ulp term is twice the half-ulp rounding error it covers."""
+    x, w, cw = _case(T * 3 + K + C, T, K, C, rest)
+    out = gdn.in_proj_conv(x, w, cw, C).cpu()
+    y64 = x.cpu().double() @ w.cpu().double().T
+    _close(out[:, C:], y64[:, C:].to(torch.bfloat16))
+    if C:
+        got = out[:, :C].double()
+        want, acc = _conv64(y64[:, :C], cw.cpu())
+        taps = cw.shape[-1]
+        uy = _bf16_ulp(y64[:, :C].abs())
+        uyp = torch.cat([torch.zeros(taps - 1, C, dtype=torch.float64), uy])
+        spread = sum(cw[:, i].cpu().double().abs()[None, :] * uyp[i:i + T] for i in range(taps))
+        bound = _bf16_ulp(torch.maximum(got.abs(), want.abs())) + 1.1 * (_bf16_ulp(acc.abs()) + spread) + 1e-5
+        excess = (got - want).abs() - bound
+        assert bool((excess <= 0).all()), float(excess.max())
 
 
 def test_in_proj_conv_leaves_no_device_error():

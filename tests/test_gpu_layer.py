@@ -76,10 +76,10 @@ def layer_inputs(seed, B, T, H, HV):
     return qkv, w, g, beta, z, nw, h0
 
 
-@pytest.mark.parametrize("B,T,H,HV", [(1, 700, 16, 32), (2, 130, 2, 4)])
+@pytest.mark.parametrize("B,T,H,HV", [(1, 700, 16, 32), (2, 130, 2, 4), (1, 4096, 16, 32)])
 def test_prefill_layer_matches_oracle_composition(B, T, H, HV):
     """conv + SiLU, chunked gated delta rule and gated norm (the prefill branch of the layer)
-    against the oracle's ops. The norm divides each row by its rms (about 0.01 with these inputs),
+    against the oracle's ops, up to config 1's full shape (B=1, T=4096, 16 / 32 heads). The norm divides each row by its rms (about 0.01 with these inputs),
     which magnifies the chunk output's absolute error about a hundredfold, so the layer is checked
     step by step: the conv bit for bit, the chunk output within the bf16 output bound (max-abs
     2e-2) and the state within 1e-3 relative, the norm of that output within two bf16 ulps of
@@ -105,11 +105,15 @@ def test_prefill_layer_matches_oracle_composition(B, T, H, HV):
                                              g, beta, initial_state=h0)
     assert maxabs(o, o_ref) < 2e-2, maxabs(o, o_ref)
     normed = oracle.gated_rms_norm(o.cpu().reshape(-1, 128), z.reshape(-1, 128), nw).reshape(B, T, HV, 128)
-    ulp = torch.ldexp(torch.ones_like(normed.float()), torch.frexp(normed.float())[1] - 8)  # one bf16 ulp each
-    # the norm kernel's bound (as in test_gpu_conv_norm): its sum of squares and rsqrt can round
-    # the normalised value one ulp away from the CPU's, and the product with the weight (up to
-    # 1.5) rounds again, so an element can land two ulps away
-    assert ((out.cpu().float() - normed.float()).abs() <= 2 * ulp).all()
+    # the norm kernel's bound, as in test_gpu_conv_norm: the reference rounds to bf16 three times
+    # (the normalised value, its product with the weight, the product with silu(z)); the kernel's
+    # rsqrt can move the first rounding by one ulp and the CPU's exp in silu(z) the last, so an
+    # element can land up to 2^-6 relative away (two to four bf16 ulps). A CPU simulation of those
+    # two flips over the 16.8 M elements of config 1 gives 4 elements three ulps away, at most 0.8
+    # of this bound.
+    d = (out.cpu().float() - normed.float()).abs()
+    lim = normed.float().abs() * 2 ** -6 + 1e-30
+    assert (d <= lim).all(), float((d / lim).max())
     assert (out.cpu() != normed).float().mean().item() < 0.01
     assert rel(out, out_ref) < 1e-2, rel(out, out_ref)
 
