@@ -59,6 +59,14 @@ def decode_layer_step(qkv, conv_state, conv_weight, g, beta, state, z, norm_weig
     HV = state.shape[1]
     if C != 2 * key_heads * HEAD_DIM + HV * HEAD_DIM:
         raise ValueError(f"qkv: expected {2 * key_heads * HEAD_DIM + HV * HEAD_DIM} channels, got {C}")
+    for name, t in (("qkv", qkv), ("conv_weight", conv_weight), ("z", z), ("norm_weight", norm_weight)):
+        if t.dtype != torch.bfloat16:
+            raise ValueError(f"{name}: expected bfloat16, got {t.dtype}")
+    if z.numel() != B * HV * HEAD_DIM or norm_weight.numel() != HEAD_DIM:
+        raise ValueError(f"z, norm_weight: expected {(B, HV, HEAD_DIM)} and {(HEAD_DIM,)}, got {tuple(z.shape)} and "
+                         f"{tuple(norm_weight.shape)}")
+    if g.numel() != B * HV or beta.numel() != B * HV:
+        raise ValueError(f"g, beta: expected {(B, HV)}, got {tuple(g.shape)} and {tuple(beta.shape)}")
     taps = conv_state.shape[-1]
     w = conv_weight.reshape(C, -1).contiguous()
     if conv_state.shape != (B, C, taps) or not conv_state.is_contiguous() or conv_state.dtype != torch.bfloat16:

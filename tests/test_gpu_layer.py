@@ -79,11 +79,13 @@ def layer_inputs(seed, B, T, H, HV):
 @pytest.mark.parametrize("B,T,H,HV", [(1, 700, 16, 32), (2, 130, 2, 4), (1, 4096, 16, 32)])
 def test_prefill_layer_matches_oracle_composition(B, T, H, HV):
     """conv + SiLU, chunked gated delta rule and gated norm (the prefill branch of the layer)
-    against the oracle's ops, up to config 1's full shape (B=1, T=4096, 16 / 32 heads). The norm divides each row by its rms (about 0.01 with these inputs),
-    which magnifies the chunk output's absolute error about a hundredfold, so the layer is checked
-    step by step: the conv bit for bit, the chunk output within the bf16 output bound (max-abs
-    2e-2) and the state within 1e-3 relative, the norm of that output within two bf16 ulps of
-    the oracle's norm of the same values (under 1% of the elements differing at all), and the whole output within 1e-2 relative (Frobenius)."""
+    against the oracle's ops, up to config 1's full shape (B=1, T=4096, 16 / 32 heads). The norm
+    divides each row by its rms (about 0.01 with these inputs), which magnifies the chunk output's
+    absolute error about a hundredfold, so the layer is checked step by step: the conv bit for bit,
+    the chunk output within the bf16 output bound (max-abs 2e-2) and the state within 1e-3
+    relative, the norm of that output within 2^-6 relative of the oracle's norm of the same values
+    (under 1% of the elements differing at all), and the whole output within 1e-2 relative
+    (Frobenius)."""
     qkv, w, g, beta, z, nw, h0 = layer_inputs(B * 100 + T, B, T, H, HV)
     out_ref, S_ref = reference_prefill_layer(qkv, w, g, beta, z, nw, H, HV, h0)
     qkv_d, w_d, g_d, b_d, z_d, nw_d, h0_d = (t.cuda() for t in (qkv, w, g, beta, z, nw, h0))
@@ -198,3 +200,28 @@ def test_decode_layer_equals_the_three_separate_calls(B, H, HV, taps):
     assert same_bits(cs_f, cs_sep)
     assert same_bits(st_f, st_sep)
     assert same_bits(out_f, out_sep)
+
+
+def test_decode_layer_rejects_bad_arguments_before_any_launch():
+    """Non-bf16 activations or weights (which the kernels would read as bf16), and z, norm
+    weight, g or beta of the wrong size, raise ValueError; the states are left untouched."""
+    B, H, HV, taps = 4, 2, 4, 3
+    C = 2 * H * 128 + HV * 128
+    dev = "cuda"
+    ok = dict(qkv=torch.randn(B, C, device=dev).to(torch.bfloat16),
+              conv_state=torch.zeros(B, C, taps, device=dev, dtype=torch.bfloat16),
+              conv_weight=torch.randn(C, 4, device=dev).to(torch.bfloat16),
+              g=-torch.rand(B, HV, device=dev), beta=torch.rand(B, HV, device=dev).to(torch.bfloat16),
+              state=torch.zeros(B, HV, 128, 128, device=dev),
+              z=torch.randn(B, HV, 128, device=dev).to(torch.bfloat16),
+              norm_weight=torch.ones(128, device=dev, dtype=torch.bfloat16))
+    bad = [("qkv", ok["qkv"].float()), ("conv_weight", ok["conv_weight"].float()), ("z", ok["z"].float()),
+           ("norm_weight", ok["norm_weight"].float()), ("norm_weight", ok["norm_weight"][:64]),
+           ("z", ok["z"][:, :2]), ("g", ok["g"][:, :2]), ("beta", ok["beta"][:2])]
+    for name, value in bad:
+        args = dict(ok, **{name: value})
+        with pytest.raises(ValueError):
+            gdn.decode_layer_step(args["qkv"], args["conv_state"], args["conv_weight"], args["g"], args["beta"],
+                                  args["state"], args["z"], args["norm_weight"], H)
+    torch.cuda.synchronize()
+    assert not ok["state"].any() and not ok["conv_state"].any()
